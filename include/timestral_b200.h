@@ -1,0 +1,76 @@
+/* timestral-b200: device seam of the B200 forecast path.
+ *
+ * The public surface of the reference stays in timestral_capi.h (unchanged). This header
+ * is the thin internal C ABI that replaces the reference's ggml graph runtime
+ * (GraphRunner, reference src/backend.hpp:40-75) and the graph bodies built by
+ * PredictBlock::predict (reference src/predict_block.cpp:6-56): plain pointers and sizes,
+ * integer status codes, a per-handle error string, no C++ or torch types.
+ *
+ * Handles are not reentrant; one handle per device per host thread. Calls are synchronous
+ * unless stated otherwise (work is stream-ordered inside).
+ */
+#ifndef TIMESTRAL_B200_H
+#define TIMESTRAL_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#include "timestral_capi.h"
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+enum {
+    TSB_OK = 0,
+    TSB_ERR_ARG = 1,       /* invalid argument or shape */
+    TSB_ERR_CUDA = 2,      /* CUDA runtime error */
+    TSB_ERR_DEVICE = 3,    /* a kernel reported an error word (bounded wait expired) */
+    TSB_ERR_MODEL = 4,     /* model not supported by the device path */
+    TSB_ERR_NAN = 5,       /* forecast produced NaN (reference: degenerate input) */
+};
+
+/* ---- device-resident forecast (throughput path) ----------------------------------
+ * Equivalent of timestral_capi_forecast for requests without covariates, with the
+ * context and the output already in device memory of the handle's GPU.
+ * d_context: [B,V,T] f32 (NaN = missing); d_mask: [B,V,T] u8 or NULL;
+ * d_out: [B,V,H,Q] f32. Flags: -1 = model default, 0, 1. Runs on the handle's stream
+ * and returns after enqueueing when `async` is nonzero, else after completion. */
+TIMESTRAL_API int tsb_forecast_device(timestral_ctx* ctx, const float* d_context, const uint8_t* d_mask,
+                                      int32_t B, int32_t V, int32_t T, int32_t H, int32_t symmetric,
+                                      int32_t clip, int32_t max_context, float* d_out, int32_t async);
+
+/* Select the GPU used by handles loaded afterwards on this thread (default: current device). */
+TIMESTRAL_API int tsb_set_device(int32_t device);
+/* cudaStream_t of the handle (as an opaque pointer), for callers that time with events. */
+TIMESTRAL_API void* tsb_stream(timestral_ctx* ctx);
+/* Per-kernel timing: when enabled, launches of the named kernel class are bracketed by
+ * CUDA events on the handle's stream. Classes: "attention", "gemm", "all". */
+TIMESTRAL_API int tsb_timing_enable(timestral_ctx* ctx, int32_t enable);
+/* Total milliseconds and launch count recorded for a kernel class since the last reset. */
+TIMESTRAL_API int tsb_timing_read(timestral_ctx* ctx, const char* cls, double* ms, int64_t* launches);
+TIMESTRAL_API void tsb_timing_reset(timestral_ctx* ctx);
+/* Kernels launched by the last forecast call (all classes). */
+TIMESTRAL_API int64_t tsb_last_launch_count(timestral_ctx* ctx);
+/* Compute path chosen for the loaded model: 1 = tensor cores (F16/Q8_0 weights),
+ * 0 = F32 CUDA-core path. */
+TIMESTRAL_API int tsb_model_path(timestral_ctx* ctx);
+
+/* ---- kernel-level test entries (device pointers) ---------------------------------- */
+typedef struct tsb_gemm_test {
+    int32_t kind;                 /* 0 f32, 1 f16, 2 resid, 3 silu, 4 swiglu, 5 vgate, 6 qkvg */
+    const void* A; int64_t lda;   /* f16 [M][lda] */
+    const void* B; int64_t ldb;   /* f16 [N][ldb] */
+    int32_t M, N, K;
+    void* out; int64_t ldo;
+    const float* bias; const float* resid;
+    int32_t row_group, row_stride, row_offset;
+    void* qkvg[4]; int32_t S, H, D, rope;
+    const float* cos_tab; const float* sin_tab; const int32_t* rope_row; int32_t rope_half;
+} tsb_gemm_test;
+/* Runs one tensor-core GEMM on the current device and synchronizes. Returns a TSB_ code;
+ * on TSB_ERR_DEVICE the kernel's error word is written to *dev_error. */
+TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_error);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

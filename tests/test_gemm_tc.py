@@ -1,0 +1,163 @@
+"""tcgen05 GEMM with fused epilogues vs a torch float64 reference of the same op.
+
+Operands are f16 and products of f16 values are exact in f32, so the only difference from
+the float64 reference is the f32 accumulation order: tolerance 2e-5 * sqrt(K) relative to
+the row scale, plus one f16 rounding (2^-11 relative) for f16 outputs.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import timestral_b200 as tb
+
+
+def dp(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def run(kind, A, B, M, N, K, out=None, ldo=0, bias=None, resid=None, row_group=0, row_stride=0, row_offset=0,
+        qkvg=None, S=0, H=0, D=0, rope=0, cos=None, sin=None, rope_row=None, rope_half=32):
+    t = tb.GemmTest()
+    t.kind, t.A, t.lda, t.B, t.ldb = kind, dp(A), A.shape[1], dp(B), B.shape[1]
+    t.M, t.N, t.K = M, N, K
+    t.out, t.ldo, t.bias, t.resid = dp(out), ldo, dp(bias), dp(resid)
+    t.row_group, t.row_stride, t.row_offset = row_group, row_stride, row_offset
+    if qkvg is not None:
+        for i in range(4):
+            t.qkvg[i] = qkvg[i].data_ptr()
+    t.S, t.H, t.D, t.rope = S, H, D, rope
+    t.cos_tab, t.sin_tab, t.rope_row, t.rope_half = dp(cos), dp(sin), dp(rope_row), rope_half
+    err = C.c_int32(0)
+    rc = tb.lib().tsb_test_gemm(C.byref(t), C.byref(err))
+    assert rc == 0, (rc, err.value)
+
+
+def ref_mm(A, B):
+    return (A.double() @ B.double().T)
+
+
+def close(got, want, K, f16=False):
+    got = got.double()
+    scale = want.abs().max().item() + 1e-30
+    tol = 2e-5 * np.sqrt(K) * scale + (want.abs() * 2.0 ** -10 if f16 else 0)
+    bad = (got - want).abs() > tol
+    assert not bad.any(), f"max err {(got - want).abs().max().item():.3e} scale {scale:.3e}"
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    torch.manual_seed(0)
+    return torch.device("cuda:0")
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 768, 768), (77, 96, 32), (1000, 2304, 768), (513, 672, 3072)])
+def test_f32_store(dev, M, N, K):
+    A = torch.randn(M, K, device=dev).half()
+    B = (torch.randn(N, K, device=dev) * 0.05).half()
+    bias = torch.randn(N, device=dev)
+    out = torch.full((M, N), float("nan"), device=dev)
+    run(0, A, B, M, N, K, out=out, ldo=N, bias=bias)
+    close(out, ref_mm(A, B) + bias.double(), K)
+
+
+def test_f16_store(dev):
+    M, N, K = 700, 512, 256
+    A = torch.randn(M, K, device=dev).half()
+    B = (torch.randn(N, K, device=dev) * 0.05).half()
+    out = torch.zeros(M, N, device=dev, dtype=torch.float16)
+    run(1, A, B, M, N, K, out=out, ldo=N)
+    close(out, ref_mm(A, B), K, f16=True)
+
+
+def test_resid_remap(dev):
+    # Patch projection layout: accumulator row m = r*L + p lands on token row r*S + p.
+    R, L, S, N, K = 9, 20, 24, 768, 3072
+    M = R * L
+    A = (torch.randn(M, K, device=dev) * 0.3).half()
+    B = (torch.randn(N, K, device=dev) * 0.02).half()
+    bias = torch.randn(N, device=dev)
+    x = torch.randn(R * S, N, device=dev)
+    x0 = x.clone()
+    run(2, A, B, M, N, K, out=x, ldo=N, bias=bias, resid=x, row_group=L, row_stride=S)
+    want = x0.double().clone()
+    idx = (torch.arange(R, device=dev)[:, None] * S + torch.arange(L, device=dev)[None, :]).reshape(-1)
+    want[idx] = x0.double()[idx] + (ref_mm(A, B) + bias.double())
+    close(x, want, K)
+
+
+def silu(x):
+    return x / (1 + torch.exp(-x))
+
+
+def test_silu(dev):
+    M, N, K = 260, 3072, 768
+    A = torch.randn(M, K, device=dev).half()
+    B = (torch.randn(N, K, device=dev) * 0.05).half()
+    out = torch.zeros(M, N, device=dev, dtype=torch.float16)
+    run(3, A, B, M, N, K, out=out, ldo=N)
+    close(out, silu(ref_mm(A, B)), K, f16=True)
+
+
+def interleave_rows(W1, W2, tile=256):
+    """Rows of two [F,K] matrices interleaved per tile: [W1 tile half | W2 tile half]."""
+    F = W1.shape[0]
+    half = tile // 2
+    parts = []
+    for t in range(F // half):
+        parts += [W1[t * half:(t + 1) * half], W2[t * half:(t + 1) * half]]
+    return torch.cat(parts, 0).contiguous()
+
+
+@pytest.mark.parametrize("kind", [4, 5])
+def test_paired(dev, kind):
+    M, F, K = 333, 2048, 768
+    A = torch.randn(M, K, device=dev).half()
+    W1 = (torch.randn(F, K, device=dev) * 0.05).half()
+    W2 = (torch.randn(F, K, device=dev) * 0.05).half()
+    b1, b2 = torch.randn(F, device=dev), torch.randn(F, device=dev)
+    W = interleave_rows(W1, W2)
+    bias = interleave_rows(b1[:, None], b2[:, None])[:, 0].contiguous()
+    out = torch.zeros(M, F, device=dev, dtype=torch.float16)
+    run(kind, A, W, M, 2 * F, K, out=out, ldo=F, bias=bias)
+    a = ref_mm(A, W1) + b1.double()
+    b = ref_mm(A, W2) + b2.double()
+    want = a * silu(b) if kind == 4 else a * torch.sigmoid(b)
+    close(out, want, K, f16=True)
+
+
+@pytest.mark.parametrize("rope", [0, 1])
+def test_qkvg(dev, rope):
+    Rr, S, H, hd = 5, 72, 12, 64
+    D = H * hd
+    M, N, K = Rr * S, 4 * D, D
+    A = torch.randn(M, K, device=dev).half()
+    B = (torch.randn(N, K, device=dev) * 0.05).half()
+    bias = torch.randn(N, device=dev) * 0.1
+    P = 2113
+    cos = torch.randn(P, 64, device=dev)
+    sin = torch.randn(P, 64, device=dev)
+    rope_row = torch.randint(0, P, (M,), device=dev, dtype=torch.int32)
+    bufs = [torch.zeros(Rr, H, S, 64, device=dev, dtype=torch.float16) for _ in range(4)]
+    run(6, A, B, M, N, K, bias=bias, qkvg=bufs, S=S, H=H, D=D, rope=rope, cos=cos, sin=sin, rope_row=rope_row,
+        rope_half=16)
+    acc = (ref_mm(A, B) + bias.double()).reshape(Rr, S, 4, H, hd).permute(2, 0, 3, 1, 4)  # [4,R,H,S,64]
+    c = cos.double()[rope_row.long()].reshape(Rr, S, 64)[:, None]
+    s = sin.double()[rope_row.long()].reshape(Rr, S, 64)[:, None]
+    for which in range(4):
+        want = acc[which].clone()
+        if which < 2 and rope:
+            x = acc[which]
+            rot = torch.cat([-x[..., 32:], x[..., :32]], -1)
+            active = torch.zeros(64, dtype=torch.bool, device=dev)
+            active[:16] = True
+            active[32:48] = True
+            want = torch.where(active, x * c + rot * s, x)
+        if which == 3:
+            want = torch.sigmoid(want)
+        close(bufs[which], want, K, f16=True)

@@ -1,0 +1,485 @@
+// Attention of the forecast path (reference src/layers.cpp:578-617 sdpa, applied on the time
+// axis per row and on the variate axis per patch slot, src/encoder.cpp:125-139).
+#include "attention.cuh"
+#include "common.cuh"
+
+#include <cstdio>
+
+namespace tsb {
+
+bool make_map_3d_f16(CUtensorMap* map, const void* base, int64_t planes, int64_t rows, int box_rows);
+int device_sm_count();
+
+namespace {
+
+__device__ __forceinline__ bool kv_bit(const MaskMeta& mm, int row, int p) {
+    return (mm.key_valid[int64_t(row) * mm.kv_words + (p >> 5)] >> (p & 31)) & 1u;
+}
+
+__device__ __forceinline__ int anchor_of(const MaskMeta& mm, int p) {
+    return p >= mm.L ? mm.L + mm.block_size * ((p - mm.L) / mm.block_size) : 0;
+}
+
+// Time-axis mask for query q and key k of row r (reference src/masks.cpp:21-26).
+__device__ __forceinline__ bool time_allowed(const MaskMeta& mm, int r, int q, int k) {
+    const int N = mm.N;
+    if (!mm.cov) {
+        if (q < N) return k < N && ((kv_bit(mm, r, k) && k <= q) || q == k);
+        if (k < N) return kv_bit(mm, r, k);
+        return k <= q;
+    }
+    if (q < N) return k < N && ((kv_bit(mm, r, k) && (mm.role[r] == 2 || k <= q)) || q == k);
+    const int qp = q - N;
+    const bool qa = qp >= mm.L;
+    if (k < N) return kv_bit(mm, r, k) && qa && k < anchor_of(mm, qp);
+    const int kp = k - N;
+    return q == k || (k <= q && qa && kp >= mm.L && anchor_of(mm, qp) == anchor_of(mm, kp));
+}
+
+// Keys the reference computes for query t: the encoder split (src/layers.cpp:591).
+__device__ __forceinline__ int time_keys(const MaskMeta& mm, int t) { return t < mm.N ? mm.N : mm.S; }
+
+// Variate-axis mask at slot p for query row q and key row k (reference src/masks.cpp:27).
+__device__ __forceinline__ bool variate_allowed(const MaskMeta& mm, int p, int q, int k) {
+    if (q == k) return true;
+    if (p < mm.N && !kv_bit(mm, k, p)) return false;
+    if (mm.cov) {
+        const int rq = mm.role[q], rk = mm.role[k];
+        if ((rq != 0 && rk == 0) || (rq == 2 && rk != 2)) return false;
+    }
+    return true;  // same group is guaranteed by the caller's key range
+}
+
+// ---------------------------------------------------------------------------------------
+// Tensor-core time attention.
+constexpr int AT_THREADS = 160;  // warps 0-3: softmax + epilogue (one query row each); warp 4: control
+constexpr uint32_t AT_TMEM_COLS = 256;
+
+struct AttnBars {
+    uint64_t full[2];
+    uint64_t s_full, p_ready, o_full;
+    uint32_t tmem;
+    int abort;
+};
+
+template <int NK>
+struct AttnLayout {
+    static constexpr int Q_BYTES = 128 * 128;
+    static constexpr int KV_BYTES = NK * 128;
+    static constexpr int SLOT_BYTES = Q_BYTES + 2 * KV_BYTES;
+    static constexpr int P_BLOCKS = (NK + 63) / 64;
+    static constexpr int P_BYTES = P_BLOCKS * 128 * 128;
+    static constexpr int SMEM = 2 * SLOT_BYTES + P_BYTES + 1024 + 256;
+};
+
+__device__ __forceinline__ bool at_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long start = clock64();
+    while (true) {
+        if (*abort) return false;
+        if (mbar_try_wait(bar, parity)) return true;
+        if (clock64() - start > kWaitCycles) { *abort = 1; record_error(err, kDevTimeoutAttn); return false; }
+    }
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+template <int NK>
+__global__ void __launch_bounds__(AT_THREADS)
+    attn_time_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                        const __grid_constant__ CUtensorMap map_v, const __half* __restrict__ gate,
+                        __half* __restrict__ out, int rows, int H, const MaskMeta mm, int* err) {
+    using Lay = AttnLayout<NK>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* pbuf = base + 2 * Lay::SLOT_BYTES;
+    AttnBars* bars = reinterpret_cast<AttnBars*>(pbuf + Lay::P_BYTES);
+    volatile int* abort = &bars->abort;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int S = mm.S, D = H * 64;
+    const int num = rows * H;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bars->full[0], 1); mbar_init(&bars->full[1], 1);
+        mbar_init(&bars->s_full, 1); mbar_init(&bars->p_ready, 4); mbar_init(&bars->o_full, 1);
+        bars->abort = 0;
+        mbar_fence_init();
+        fence_proxy_async();
+    }
+    if (warp == 4) { tmem_alloc(&bars->tmem, AT_TMEM_COLS); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem;
+    const uint32_t tS = tmem, tO = tmem + 128;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            auto issue = [&](int slot, int prob) {
+                uint8_t* sl = base + slot * Lay::SLOT_BYTES;
+                mbar_arrive_expect_tx(&bars->full[slot], Lay::SLOT_BYTES);
+                tma_load_3d(sl, &map_q, &bars->full[slot], 0, 0, prob);
+                tma_load_3d(sl + Lay::Q_BYTES, &map_k, &bars->full[slot], 0, 0, prob);
+                tma_load_3d(sl + Lay::Q_BYTES + Lay::KV_BYTES, &map_v, &bars->full[slot], 0, 0, prob);
+            };
+            if (int(blockIdx.x) < num) issue(0, blockIdx.x);
+            if (int(blockIdx.x + gridDim.x) < num) issue(1, blockIdx.x + gridDim.x);
+            const uint32_t id1 = idesc_f16(128, NK), id2 = idesc_f16_bmn(128, 64);
+            int i = 0;
+            for (int prob = blockIdx.x; prob < num; prob += gridDim.x, ++i) {
+                const int s = i & 1;
+                if (!at_wait(&bars->full[s], (i >> 1) & 1, abort, err)) break;
+                tc_fence_after();
+                const uint32_t sq = smem_u32(base + s * Lay::SLOT_BYTES);
+                const uint32_t sk = sq + Lay::Q_BYTES, sv = sk + Lay::KV_BYTES;
+                const uint64_t dq = smem_desc_sw128(sq), dk = smem_desc_sw128(sk);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) mma_f16(tS, dq + uint64_t(2 * k), dk + uint64_t(2 * k), id1, k > 0);
+                mma_commit(&bars->s_full);
+                if (!at_wait(&bars->p_ready, i & 1, abort, err)) break;
+                tc_fence_after();
+                const uint32_t sp = smem_u32(pbuf);
+#pragma unroll
+                for (int kk = 0; kk < NK / 16; ++kk) {
+                    const uint64_t da = smem_desc_sw128(sp + (kk / 4) * 16384) + uint64_t(2 * (kk % 4));
+                    const uint64_t dv = smem_desc_sw128(sv + kk * 16 * 128);
+                    mma_f16(tO, da, dv, id2, kk > 0);
+                }
+                mma_commit(&bars->o_full);
+                const int next = prob + 2 * gridDim.x;
+                if (next < num) {
+                    if (!at_wait(&bars->o_full, i & 1, abort, err)) break;
+                    issue(s, next);
+                }
+            }
+        }
+    } else {
+        const int t = threadIdx.x;  // query row == TMEM lane
+        const uint32_t lane_base = uint32_t(warp * 32) << 16;
+        constexpr float kLog2e = 1.4426950408889634f;
+        int i = 0;
+        for (int prob = blockIdx.x; prob < num; prob += gridDim.x, ++i) {
+            const int r = prob / H, h = prob % H;
+            if (!at_wait(&bars->s_full, i & 1, abort, err)) break;
+            tc_fence_after();
+            const bool live = t < S;
+            const int keys = live ? time_keys(mm, t) : 0;
+            // Pass 1: masked maximum of the scaled logits.
+            float mx = -INFINITY;
+            uint32_t rr[16];
+#pragma unroll
+            for (int c = 0; c < NK / 16; ++c) {
+                tmem_ld16(tS + lane_base + c * 16, rr);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int key = c * 16 + j;
+                    if (key < keys && time_allowed(mm, r, t, key)) mx = fmaxf(mx, __uint_as_float(rr[j]) * 0.125f);
+                }
+            }
+            // Pass 2: probabilities (f16), their sum, and the P tile in the 128-byte swizzle.
+            float sum = 0.f;
+            const float off = mx * kLog2e;
+#pragma unroll
+            for (int c = 0; c < NK / 16; ++c) {
+                tmem_ld16(tS + lane_base + c * 16, rr);
+                tmem_ld_wait();
+                float p[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int key = c * 16 + j;
+                    float pj = 0.f;
+                    if (key < keys && time_allowed(mm, r, t, key))
+                        pj = exp2f(__fmaf_rn(__uint_as_float(rr[j]) * 0.125f, kLog2e, -off));
+                    const __half hp = __float2half_rn(pj);
+                    sum += __half2float(hp);
+                    p[j] = pj;
+                }
+#pragma unroll
+                for (int half8 = 0; half8 < 2; ++half8) {
+                    const int k0 = c * 16 + half8 * 8;
+                    const int blk = k0 / 64, chunk = (k0 % 64) / 8;
+                    uint4 u;
+                    u.x = pack_half2(p[half8 * 8 + 0], p[half8 * 8 + 1]);
+                    u.y = pack_half2(p[half8 * 8 + 2], p[half8 * 8 + 3]);
+                    u.z = pack_half2(p[half8 * 8 + 4], p[half8 * 8 + 5]);
+                    u.w = pack_half2(p[half8 * 8 + 6], p[half8 * 8 + 7]);
+                    *reinterpret_cast<uint4*>(pbuf + blk * 16384 + t * 128 + ((chunk ^ (t & 7)) << 4)) = u;
+                }
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->p_ready);
+            if (!at_wait(&bars->o_full, i & 1, abort, err)) break;
+            tc_fence_after();
+            uint32_t o0[32], o1[32];
+            tmem_ld32(tO + lane_base, o0);
+            tmem_ld32(tO + lane_base + 32, o1);
+            tmem_ld_wait();
+            if (live) {
+                const float inv = 1.0f / sum;
+                const int64_t tok = int64_t(r) * S + t;
+                const __half* g = gate ? gate + ((int64_t(r) * H + h) * S + t) * 64 : nullptr;
+                __half* dst = out + tok * D + h * 64;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    float y[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int d = c * 8 + j;
+                        y[j] = __uint_as_float(d < 32 ? o0[d] : o1[d - 32]) * inv;
+                    }
+                    if (g) {
+                        const uint4 gv = *reinterpret_cast<const uint4*>(g + c * 8);
+                        const __half2* gh = reinterpret_cast<const __half2*>(&gv);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float2 f = __half22float2(gh[j]);
+                            y[2 * j] = __fmul_rn(y[2 * j], f.x);
+                            y[2 * j + 1] = __fmul_rn(y[2 * j + 1], f.y);
+                        }
+                    }
+                    uint4 u;
+                    u.x = pack_half2(y[0], y[1]); u.y = pack_half2(y[2], y[3]);
+                    u.z = pack_half2(y[4], y[5]); u.w = pack_half2(y[6], y[7]);
+                    *reinterpret_cast<uint4*>(dst + c * 8) = u;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 4) tmem_dealloc(tmem, AT_TMEM_COLS);
+}
+
+template <int NK>
+cudaError_t launch_attn_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
+                           int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
+    using Lay = AttnLayout<NK>;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_time_tc_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::SMEM);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    CUtensorMap mq, mk, mv;
+    const int64_t planes = int64_t(rows) * H;
+    if (!make_map_3d_f16(&mq, q, planes, mm.S, 128) || !make_map_3d_f16(&mk, k, planes, mm.S, NK) ||
+        !make_map_3d_f16(&mv, v, planes, mm.S, NK))
+        return cudaErrorInvalidValue;
+    const int per_sm = Lay::SMEM * 2 <= 227 * 1024 ? 2 : 1;
+    int grid = device_sm_count() * per_sm;
+    if (int64_t(grid) > planes) grid = int(planes);
+    attn_time_tc_kernel<NK><<<grid, AT_THREADS, Lay::SMEM, stream>>>(mq, mk, mv, gate, out, rows, H, mm, err);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------
+// CUDA-core kernels with the reference's operation order. One warp per query.
+template <class T>
+__device__ __forceinline__ float ld(const T* p) { return float(*p); }
+template <>
+__device__ __forceinline__ float ld<__half>(const __half* p) { return __half2float(*p); }
+template <class T>
+__device__ __forceinline__ void st(T* p, float v) { *p = v; }
+template <>
+__device__ __forceinline__ void st<__half>(__half* p, float v) { *p = __float2half_rn(v); }
+
+// Softmax-weighted value sum of one query over `count` candidate keys given by key(j) with
+// sequence index seq(j) (the index the reference's lane/tail split uses), logits already in
+// `lg` (-inf where masked), as the reference does it (src/layers.cpp:600-614).
+template <class T, class KeyPtr>
+__device__ void softmax_values(float* lg, int count, const int* seqidx, int keys_total, KeyPtr vrow, int hd, float* y_out) {
+    const int lane = threadIdx.x & 31;
+    float mx = -INFINITY;
+    for (int j = lane; j < count; j += 32) mx = fmaxf(mx, lg[j]);
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int end = keys_total / 8 * 8;
+    for (int j = lane; j < count; j += 32) {
+        const float x = __fsub_rn(lg[j], mx);
+        lg[j] = seqidx[j] < end ? attention_exp(x) : float(exp(double(x)));
+    }
+    __syncwarp();
+    // Eight lane sums over full chunks in sequence order, then the fixed tree, then the tail.
+    float part = 0.f;
+    if (lane < 8)
+        for (int j = 0; j < count; ++j)
+            if (seqidx[j] < end && (seqidx[j] & 7) == lane) part = __fadd_rn(part, lg[j]);
+    float s[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) s[l] = __shfl_sync(0xffffffffu, part, l);
+    const float a0 = __fadd_rn(s[0], s[4]), a1 = __fadd_rn(s[1], s[5]), a2 = __fadd_rn(s[2], s[6]), a3 = __fadd_rn(s[3], s[7]);
+    float sum = __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+    for (int j = 0; j < count; ++j)
+        if (seqidx[j] >= end) sum = __fadd_rn(sum, lg[j]);
+    const float reciprocal = __fdiv_rn(1.0f, sum);
+    for (int d = lane; d < hd; d += 32) {
+        float acc = 0.f;
+        for (int j = 0; j < count; ++j) {
+            const float vv = ld(vrow(j) + d);
+            acc = hd < 16 ? __fadd_rn(acc, __fmul_rn(lg[j], vv)) : __fmaf_rn(lg[j], vv, acc);
+        }
+        y_out[d] = __fmul_rn(acc, reciprocal);
+    }
+}
+
+constexpr int SIMT_WARPS = 4;
+constexpr int SIMT_MAX_KEYS = 2176;
+
+// Time axis: block = (row, head, 4 queries). Logits in shared memory.
+template <class T>
+__global__ void __launch_bounds__(SIMT_WARPS * 32)
+    attn_time_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                          const T* __restrict__ gate, T* __restrict__ out, int rows, int H, int hd, const MaskMeta mm) {
+    extern __shared__ float sh[];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int S = mm.S;
+    float* lg = sh + warp * (2 * SIMT_MAX_KEYS);
+    int* seq = reinterpret_cast<int*>(lg + SIMT_MAX_KEYS);
+    float* y = sh + SIMT_WARPS * 2 * SIMT_MAX_KEYS + warp * 256;
+    const int qblocks = (S + SIMT_WARPS - 1) / SIMT_WARPS;
+    const int64_t b = blockIdx.x;
+    const int r = int(b / (int64_t(H) * qblocks)), h = int((b / qblocks) % H), t = int(b % qblocks) * SIMT_WARPS + warp;
+    if (r >= rows || t >= S) return;
+    const int keys = time_keys(mm, t);
+    const T* qp = q + ((int64_t(r) * H + h) * S + t) * hd;
+    const T* kb = k + (int64_t(r) * H + h) * S * hd;
+    for (int j = lane; j < keys; j += 32) {
+        seq[j] = j;
+        if (!time_allowed(mm, r, t, j)) { lg[j] = -INFINITY; continue; }
+        double s = 0;
+        for (int d = 0; d < hd; ++d) s = __fma_rn(double(ld(qp + d)), double(ld(kb + int64_t(j) * hd + d)), s);
+        lg[j] = __fmul_rn(float(s), float(1.0 / sqrt(double(hd))));
+    }
+    __syncwarp();
+    const T* vb = v + (int64_t(r) * H + h) * S * hd;
+    softmax_values<T>(lg, keys, seq, keys, [&](int j) { return vb + int64_t(j) * hd; }, hd, y);
+    __syncwarp();
+    const int D = H * hd;
+    const T* g = gate ? gate + ((int64_t(r) * H + h) * S + t) * hd : nullptr;
+    for (int d = lane; d < hd; d += 32) {
+        float val = y[d];
+        if (g) val = __fmul_rn(val, ld(g + d));
+        st(out + (int64_t(r) * S + t) * D + h * hd + d, val);
+    }
+}
+
+// Variate axis: block = (row, slot, head) with 4 warps over heads; keys are the rows of the
+// query row's series. Sequence index of a key = its row index within the forecast pass.
+template <class T>
+__global__ void __launch_bounds__(SIMT_WARPS * 32)
+    attn_variate_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                             const T* __restrict__ gate, T* __restrict__ out, int rows, int H, int hd, const MaskMeta mm) {
+    extern __shared__ float sh[];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int S = mm.S;
+    float* lg = sh + warp * (2 * SIMT_MAX_KEYS);
+    int* seq = reinterpret_cast<int*>(lg + SIMT_MAX_KEYS);
+    float* y = sh + SIMT_WARPS * 2 * SIMT_MAX_KEYS + warp * 256;
+    const int hblocks = (H + SIMT_WARPS - 1) / SIMT_WARPS;
+    const int64_t b = blockIdx.x;
+    const int r = int(b / (int64_t(S) * hblocks)), p = int((b / hblocks) % S), h = int(b % hblocks) * SIMT_WARPS + warp;
+    if (r >= rows || h >= H) return;
+    const int g0 = mm.group_begin[r], gs = mm.group_size[r];
+    const int pass0 = (r / mm.pass_rows) * mm.pass_rows;
+    const T* qp = q + ((int64_t(r) * H + h) * S + p) * hd;
+    for (int j = lane; j < gs; j += 32) {
+        const int kr = g0 + j;
+        seq[j] = kr - pass0;
+        if (!variate_allowed(mm, p, r, kr)) { lg[j] = -INFINITY; continue; }
+        const T* kp = k + ((int64_t(kr) * H + h) * S + p) * hd;
+        double s = 0;
+        for (int d = 0; d < hd; ++d) s = __fma_rn(double(ld(qp + d)), double(ld(kp + d)), s);
+        lg[j] = __fmul_rn(float(s), float(1.0 / sqrt(double(hd))));
+    }
+    __syncwarp();
+    softmax_values<T>(lg, gs, seq, mm.pass_rows,
+                      [&](int j) { return v + ((int64_t(g0 + j) * H + h) * S + p) * hd; }, hd, y);
+    __syncwarp();
+    const int D = H * hd;
+    const T* g = gate ? gate + ((int64_t(r) * H + h) * S + p) * hd : nullptr;
+    for (int d = lane; d < hd; d += 32) {
+        float val = y[d];
+        if (g) val = __fmul_rn(val, ld(g + d));
+        st(out + (int64_t(r) * S + p) * D + h * hd + d, val);
+    }
+}
+
+constexpr size_t simt_smem() { return (SIMT_WARPS * 2 * SIMT_MAX_KEYS + SIMT_WARPS * 256) * sizeof(float); }
+
+}  // namespace
+
+cudaError_t attention_time_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
+                              int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
+    if (rows <= 0) return cudaSuccess;
+    if (mm.S <= 0 || mm.S > 128) return cudaErrorInvalidValue;
+    const int nk = (mm.S + 15) / 16 * 16;
+    switch (nk) {
+        case 16: return launch_attn_tc<16>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 32: return launch_attn_tc<32>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 48: return launch_attn_tc<48>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 64: return launch_attn_tc<64>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 80: return launch_attn_tc<80>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 96: return launch_attn_tc<96>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 112: return launch_attn_tc<112>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 128: return launch_attn_tc<128>(q, k, v, gate, out, rows, H, mm, stream, err);
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <class T>
+cudaError_t attention_time_simt(const T* q, const T* k, const T* v, const T* gate, T* out, int rows, int H, int hd,
+                                const MaskMeta& mm, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    if (mm.S > SIMT_MAX_KEYS || hd > 256) return cudaErrorInvalidValue;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_time_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(simt_smem()));
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    const int64_t blocks = int64_t(rows) * H * ((mm.S + SIMT_WARPS - 1) / SIMT_WARPS);
+    attn_time_simt_kernel<T><<<unsigned(blocks), SIMT_WARPS * 32, simt_smem(), stream>>>(q, k, v, gate, out, rows, H, hd, mm);
+    return cudaGetLastError();
+}
+
+template <class T>
+cudaError_t attention_variate_simt(const T* q, const T* k, const T* v, const T* gate, T* out, int rows, int H, int hd,
+                                   const MaskMeta& mm, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    if (hd > 256) return cudaErrorInvalidValue;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_variate_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(simt_smem()));
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    const int64_t blocks = int64_t(rows) * mm.S * ((H + SIMT_WARPS - 1) / SIMT_WARPS);
+    attn_variate_simt_kernel<T><<<unsigned(blocks), SIMT_WARPS * 32, simt_smem(), stream>>>(q, k, v, gate, out, rows, H, hd, mm);
+    return cudaGetLastError();
+}
+
+template cudaError_t attention_time_simt<float>(const float*, const float*, const float*, const float*, float*, int, int, int,
+                                                const MaskMeta&, cudaStream_t);
+template cudaError_t attention_time_simt<__half>(const __half*, const __half*, const __half*, const __half*, __half*, int,
+                                                 int, int, const MaskMeta&, cudaStream_t);
+template cudaError_t attention_variate_simt<float>(const float*, const float*, const float*, const float*, float*, int, int,
+                                                   int, const MaskMeta&, cudaStream_t);
+template cudaError_t attention_variate_simt<__half>(const __half*, const __half*, const __half*, const __half*, __half*,
+                                                    int, int, int, const MaskMeta&, cudaStream_t);
+
+}  // namespace tsb

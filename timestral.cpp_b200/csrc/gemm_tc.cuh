@@ -1,0 +1,54 @@
+// Tensor-core GEMM interface: C = A * B^T with A [M,K] f16 activations (K contiguous) and
+// B [N,K] f16 weights (the GGUF row layout), f32 accumulation in tensor memory, and the
+// epilogue fused into the store.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace tsb {
+
+enum EpiKind : int {
+    EPI_F32 = 0,     // out f32 = acc + bias
+    EPI_F16 = 1,     // out f16 = acc + bias
+    EPI_RESID = 2,   // out f32 = resid + (acc + bias)            (resid may alias out)
+    EPI_SILU = 3,    // out f16 = silu(acc + bias)
+    EPI_SWIGLU = 4,  // tile halves (g | u): out f16 = g * silu(u) (weights interleaved per tile)
+    EPI_VGATE = 5,   // tile halves (v | gate): out f16 = v * sigmoid(gate)
+    EPI_QKVG = 6,    // columns q | k | v | gate: RoPE on q,k (optional), sigmoid on gate,
+                     // scattered head-major to [rows][heads][tokens][64] f16
+};
+
+struct GemmEpilogue {
+    void* out = nullptr;
+    int64_t ldo = 0;                  // output row stride (elements)
+    const float* bias = nullptr;      // [N] (in the weight's row order)
+    const float* resid = nullptr;     // EPI_RESID input, same row mapping and stride as out
+    // Output row of accumulator row m: (m / row_group) * row_stride + row_offset + m % row_group.
+    int row_group = 0, row_stride = 0, row_offset = 0;
+    // EPI_QKVG
+    __half* qkvg[4] = {nullptr, nullptr, nullptr, nullptr};
+    int S = 0, H = 0, D = 0;          // tokens per row, heads, model width
+    int rope = 0;                     // apply RoPE to q and k
+    const float* cos_tab = nullptr;   // [P][64]
+    const float* sin_tab = nullptr;
+    const int* rope_row = nullptr;    // [M] table row of each token
+    int rope_half = 32;               // rotated dims per half head (rope_dim / 2)
+};
+
+struct GemmArgs {
+    const __half* A = nullptr;
+    int64_t lda = 0;
+    const __half* B = nullptr;
+    int64_t ldb = 0;
+    int M = 0, N = 0, K = 0;
+    GemmEpilogue epi;
+};
+
+// Launch on `stream`. err: device error word (may be null). Returns a CUDA error code.
+cudaError_t tc_gemm(EpiKind kind, const GemmArgs& args, cudaStream_t stream, int* err);
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count();
+
+}  // namespace tsb

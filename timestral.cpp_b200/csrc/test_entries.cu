@@ -1,0 +1,32 @@
+// Kernel-level test entries of the C ABI (include/timestral_b200.h): run one kernel on
+// caller-owned device buffers so the GPU tests can compare it with a reference op.
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "timestral_b200.h"
+
+extern "C" TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_error) {
+    using namespace tsb;
+    if (!t) return TSB_ERR_ARG;
+    GemmArgs a;
+    a.A = static_cast<const __half*>(t->A); a.lda = t->lda;
+    a.B = static_cast<const __half*>(t->B); a.ldb = t->ldb;
+    a.M = t->M; a.N = t->N; a.K = t->K;
+    GemmEpilogue& e = a.epi;
+    e.out = t->out; e.ldo = t->ldo; e.bias = t->bias; e.resid = t->resid;
+    e.row_group = t->row_group; e.row_stride = t->row_stride; e.row_offset = t->row_offset;
+    for (int i = 0; i < 4; ++i) e.qkvg[i] = static_cast<__half*>(t->qkvg[i]);
+    e.S = t->S; e.H = t->H; e.D = t->D; e.rope = t->rope;
+    e.cos_tab = t->cos_tab; e.sin_tab = t->sin_tab; e.rope_row = t->rope_row; e.rope_half = t->rope_half;
+    int* derr = nullptr;
+    if (cudaMalloc(&derr, sizeof(int)) != cudaSuccess) return TSB_ERR_CUDA;
+    cudaMemset(derr, 0, sizeof(int));
+    cudaError_t ce = tc_gemm(static_cast<EpiKind>(t->kind), a, 0, derr);
+    if (ce == cudaErrorInvalidValue) { cudaFree(derr); return TSB_ERR_ARG; }
+    if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+    int h = 0;
+    cudaMemcpy(&h, derr, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(derr);
+    if (dev_error) *dev_error = h;
+    if (ce != cudaSuccess) return TSB_ERR_CUDA;
+    return h ? TSB_ERR_DEVICE : TSB_OK;
+}
