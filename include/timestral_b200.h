@@ -38,6 +38,9 @@ TIMESTRAL_API int tsb_forecast_device(timestral_ctx* ctx, const float* d_context
                                       int32_t B, int32_t V, int32_t T, int32_t H, int32_t symmetric,
                                       int32_t clip, int32_t max_context, float* d_out, int32_t async);
 
+/* Wait for the handle's stream; returns TSB_ERR_DEVICE (with last_error set) when a kernel
+ * of an asynchronous tsb_forecast_device call reported an error. */
+TIMESTRAL_API int tsb_sync(timestral_ctx* ctx);
 /* Select the GPU used by handles loaded afterwards on this thread (default: current device). */
 TIMESTRAL_API int tsb_set_device(int32_t device);
 /* cudaStream_t of the handle (as an opaque pointer), for callers that time with events. */

@@ -347,3 +347,25 @@ def block_frames(cfg, x, mask, median, rows, length, patches):
 
 def set_per_shot(model, n):
     lib().oracle_model_set_per_shot(model.h, C.c_int32(n))
+
+
+def anchors(context, ps, minimum_scale=1e-6):
+    """First-pass anchor frame of each target row (the causal loc/scale at the last step of
+    the forward-filled, left-padded context), used to normalise forecast comparisons."""
+    B, V, T = context.shape
+    pad = (ps - T % ps) % ps
+    rows = np.zeros((B * V, T + pad), np.float32)
+    mask = np.zeros((B * V, T + pad), np.int8)
+    for r, x in enumerate(np.asarray(context, np.float32).reshape(B * V, T)):
+        obs = np.isfinite(x)
+        idx = np.where(obs, np.arange(T), -1)
+        idx = np.maximum.accumulate(idx)
+        rows[r, pad:] = np.where(idx >= 0, x[np.maximum(idx, 0)], 0.0)
+        mask[r, pad:] = obs
+    cfg = OracleConfig()
+    cfg.patch_size = ps
+    cfg.minimum_scale = minimum_scale
+    cfg.use_asinh = 1
+    _, loc, sc = scale_rows(cfg, rows, mask, B * V, T + pad)
+    L = T + pad
+    return loc.reshape(B * V, L)[:, -1].copy(), sc.reshape(B * V, L)[:, -1].copy()

@@ -27,6 +27,8 @@ COMMON = ["-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibilit
           f"-I{REPO / 'include'}", f"-I{PKG / 'csrc'}", f"-I{PKG / 'host'}"]
 CUDA_FLAGS = ARCH + ["-lineinfo", "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 HOST_CXX = ["-Xcompiler", "-ffp-contract=off"]
+# Sources whose float arithmetic must not be contracted into fused multiply-adds.
+NO_FMAD = {"rows.cu"}
 
 
 def sources():
@@ -52,7 +54,8 @@ def compile_one(src: Path, verbose: bool, newest_header: float):
     obj = OBJ_DIR / (src.name + ".o")
     if obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, newest_header):
         return obj, ""
-    cmd = [NVCC] + ccbin() + COMMON + (CUDA_FLAGS if src.suffix == ".cu" else ["-x", "c++"] + HOST_CXX) + ["-c", str(src), "-o", str(obj)]
+    flags = (CUDA_FLAGS + (["-fmad=false"] if src.name in NO_FMAD else [])) if src.suffix == ".cu" else ["-x", "c++"] + HOST_CXX
+    cmd = [NVCC] + ccbin() + COMMON + flags + ["-c", str(src), "-o", str(obj)]
     if verbose:
         print(" ".join(cmd), flush=True)
     r = subprocess.run(cmd, capture_output=True, text=True)

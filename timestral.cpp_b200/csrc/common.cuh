@@ -19,7 +19,9 @@ enum DeviceError : int {
     kDevTimeoutAccFull = 3,   // epilogue: accumulator never committed
     kDevTimeoutAccEmpty = 4,  // MMA warp: accumulator never drained
     kDevTimeoutAttn = 5,      // attention kernel barrier
-    kDevBadShape = 6,
+    kDevBadShape = 6,         // position outside the RoPE table, or a NaN raw quantile
+    kDevNaN = 7,              // a capped forecast value is NaN (reference: degenerate input)
+    kDevNonFinite = 8,        // a final forecast value is not finite
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {

@@ -1,0 +1,802 @@
+// Device engine: weights in device layouts, workspace, and the forecast pipeline.
+//
+// One forecast runs both symmetric passes as one batch of 2R rows (positive rows, then the
+// exact negation), so every kernel sees twice the rows and the passes cost one launch each.
+// Per decode block (reference src/forecaster.cpp:19-67):
+//   scale_rows -> patch projection -> 24 transformer layers -> out_norm (decoder tokens)
+//   -> head GEMMs -> monotone/denormalise -> refine
+// then cap, symmetric average and clip (src/forecaster.cpp:68-108) in one kernel.
+#include "attention.cuh"
+#include "common.cuh"
+#include "engine.cuh"
+#include "gemm_tc.cuh"
+#include "rows.cuh"
+
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+
+namespace tsb {
+
+namespace {
+
+void check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+float half_bits_to_float(uint16_t h) {
+    __half_raw r;
+    r.x = h;
+    return __half2float(__half(r));
+}
+uint16_t float_to_half_bits(float f) {
+    __half h = __float2half_rn(f);
+    return reinterpret_cast<__half_raw&>(h).x;
+}
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    ~DevBuf() { if (p) cudaFree(p); }
+    void ensure(size_t n) {
+        if (n <= bytes) return;
+        if (p) { cudaFree(p); p = nullptr; bytes = 0; }
+        check(cudaMalloc(&p, std::max<size_t>(n, 256)), "cudaMalloc workspace");
+        bytes = std::max<size_t>(n, 256);
+    }
+    template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+struct AttnW {
+    bool time = true, gate = false;
+    const float* norm = nullptr;
+    // tensor-core path
+    __half* qkvg = nullptr; float* b_qkvg = nullptr; int n_qkvg = 0;   // [3D or 4D][D]
+    __half* vg = nullptr; float* b_vg = nullptr;                        // variate, group size 1: [v|gate] per tile
+    __half* out = nullptr; float* b_out = nullptr;
+    // CUDA-core path
+    float* f_qkv = nullptr; float* fb_qkv = nullptr; float* f_gate = nullptr; float* fb_gate = nullptr;
+    float* f_out = nullptr; float* fb_out = nullptr;
+};
+struct MlpW {
+    const float* norm = nullptr;
+    __half* w12 = nullptr; float* b12 = nullptr;    // tensor cores: [g|u] per tile
+    __half* w3 = nullptr; float* b3 = nullptr;
+    float* f12 = nullptr; float* fb12 = nullptr; float* f3 = nullptr; float* fb3 = nullptr;
+};
+
+constexpr int kTile = 256;  // tensor-core GEMM tile width (gemm_tc.cu BN)
+
+}  // namespace
+
+struct Engine::Impl {
+    ModelView mv;
+    int D = 0, H = 0, hd = 0, F = 0, ps = 0, Q = 0, P = 0;
+    bool tc = false, round_a = false;
+    RowConfig rc;
+    std::vector<void*> allocs;
+    // weights
+    float* query = nullptr;
+    float* cos_tab = nullptr; float* sin_tab = nullptr;
+    int rope_half = 32;
+    float* p_hid = nullptr; float* pb_hid = nullptr; float* p_res = nullptr; float* pb_res = nullptr;
+    __half* p_out = nullptr; float* f_pout = nullptr; float* pb_out = nullptr;
+    std::vector<std::vector<AttnW>> attn;
+    std::vector<MlpW> mlp;
+    const float* out_norm = nullptr;
+    __half* h_hid = nullptr; __half* h_out = nullptr; __half* h_res = nullptr;
+    float* fh_hid = nullptr; float* fh_out = nullptr; float* fh_res = nullptr;
+    // workspace
+    DevBuf rows, mask, win, wmask, role, future, fmask, feat, aloc, ascale, caplo, caphi, capsc, first_obs, kv, rope_row,
+        gbeg, gsize, clip_ok, x, xn, qb, kb, vb, gb, att, hb, zb, fused, gtmp, ph, dec, hh, hraw, qout, refined, scratch,
+        decoded, err, next_rows, next_mask;
+    // timing
+    bool timing = false;
+    struct Ev { cudaEvent_t a, b; std::string cls; };
+    std::vector<Ev> events;
+    size_t ev_used = 0;
+    int64_t launches = 0;
+    cudaStream_t s = nullptr;
+
+    template <class T> T* dalloc(size_t n) {
+        void* p = nullptr;
+        check(cudaMalloc(&p, std::max<size_t>(n * sizeof(T), 16)), "cudaMalloc weights");
+        allocs.push_back(p);
+        return static_cast<T*>(p);
+    }
+    template <class T> T* upload(const T* h, size_t n) {
+        T* d = dalloc<T>(n);
+        check(cudaMemcpy(d, h, n * sizeof(T), cudaMemcpyHostToDevice), "upload");
+        return d;
+    }
+
+    HostTensor t(const std::string& n) const { return mv.tensor(n); }
+
+    // Row values of a weight as float (exact for F32/F16; Q8_0 as f16(d)*q).
+    std::vector<float> rows_f32(const HostTensor& w) const {
+        const size_t K = size_t(w.ne0), N = size_t(w.ne1);
+        std::vector<float> out(K * N);
+        if (w.type == TT_F32) std::memcpy(out.data(), w.data, out.size() * 4);
+        else if (w.type == TT_F16) {
+            const uint16_t* p = static_cast<const uint16_t*>(w.data);
+            for (size_t i = 0; i < out.size(); ++i) out[i] = half_bits_to_float(p[i]);
+        } else {
+            const uint8_t* p = static_cast<const uint8_t*>(w.data);
+            const size_t nb = K / 32;
+            for (size_t n = 0; n < N; ++n)
+                for (size_t b = 0; b < nb; ++b) {
+                    const uint8_t* blk = p + (n * nb + b) * 34;
+                    uint16_t dh;
+                    std::memcpy(&dh, blk, 2);
+                    const float d = half_bits_to_float(dh);
+                    for (size_t j = 0; j < 32; ++j) out[n * K + b * 32 + j] = d * float(int8_t(blk[2 + j]));
+                }
+        }
+        return out;
+    }
+    // Row values as f16 bits (F16 as stored; Q8_0 dequantised then rounded to f16).
+    std::vector<uint16_t> rows_f16(const HostTensor& w) const {
+        const size_t n = size_t(w.ne0) * size_t(w.ne1);
+        std::vector<uint16_t> out(n);
+        if (w.type == TT_F16) std::memcpy(out.data(), w.data, n * 2);
+        else {
+            auto f = rows_f32(w);
+            for (size_t i = 0; i < n; ++i) out[i] = float_to_half_bits(f[i]);
+        }
+        return out;
+    }
+    const float* f32_tensor(const std::string& n) {
+        auto w = t(n);
+        if (w.type != TT_F32) throw std::runtime_error("tensor " + n + " must be F32");
+        return upload(static_cast<const float*>(w.data), size_t(w.ne0) * size_t(w.ne1));
+    }
+    float* bias_or_null(const std::string& n) {
+        if (!mv.has(n)) return nullptr;
+        return const_cast<float*>(f32_tensor(n));
+    }
+    // Two [rows][K] blocks interleaved per tile: [a rows t*128.. | b rows t*128..].
+    static std::vector<uint16_t> interleave(const uint16_t* a, const uint16_t* b, size_t rows, size_t K) {
+        std::vector<uint16_t> out(2 * rows * K);
+        const size_t half = kTile / 2;
+        for (size_t tile = 0; tile < rows / half; ++tile) {
+            std::memcpy(&out[(2 * tile) * half * K], a + tile * half * K, half * K * 2);
+            std::memcpy(&out[(2 * tile + 1) * half * K], b + tile * half * K, half * K * 2);
+        }
+        return out;
+    }
+    static std::vector<float> interleave_bias(const float* a, const float* b, size_t rows) {
+        std::vector<float> out(2 * rows);
+        const size_t half = kTile / 2;
+        for (size_t tile = 0; tile < rows / half; ++tile)
+            for (size_t i = 0; i < half; ++i) {
+                out[2 * tile * half + i] = a ? a[tile * half + i] : 0.f;
+                out[(2 * tile + 1) * half + i] = b ? b[tile * half + i] : 0.f;
+            }
+        return out;
+    }
+
+    void load() {
+        const auto& m = mv;
+        D = m.D; H = m.H; hd = D / H; F = m.F; ps = m.ps; Q = int(m.knots.size());
+        // Tensor cores when every projection weight is reduced (F16/Q8_0) and the shapes
+        // tile (head_dim 64, widths multiple of the 128-row pairing half tile).
+        bool reduced = true;
+        auto is_reduced = [&](const std::string& n) { return t(n).type != TT_F32; };
+        reduced &= is_reduced("patch.out.weight") && is_reduced("head.hidden.weight") && is_reduced("head.out.weight") &&
+                   is_reduced("head.res.weight");
+        for (size_t i = 0; i < m.schedule.size(); ++i) {
+            const std::string b = "blk." + std::to_string(i) + ".";
+            reduced &= is_reduced(b + "ffn_w12.weight") && is_reduced(b + "ffn_w3.weight");
+        }
+        tc = reduced && hd == 64 && D % 128 == 0 && F % 128 == 0 && (ps * Q) % 16 == 0;
+        round_a = reduced && !tc;
+        // row config
+        rc.ps = ps; rc.minimum_scale = m.minimum_scale; rc.use_asinh = m.use_asinh; rc.attend_missing = m.attend_missing;
+        rc.Q = Q; rc.median = m.median; rc.pos_min = m.pos_min; rc.cap_k = m.cap_k; rc.extreme = m.extreme;
+        if (Q > 64) throw std::runtime_error("more than 64 quantile levels are not supported");
+        for (int q = 0; q < Q; ++q) {
+            const double w = q < m.median ? m.knots[q + 1] - m.knots[q] : q > m.median ? m.knots[q] - m.knots[q - 1] : 0;
+            rc.widths[q] = float(m.width_factor) * float(w);
+        }
+        // tables
+        auto tc_ = t("rope.cos");
+        P = int(tc_.ne1);
+        rc.rope_len = P;
+        cos_tab = upload(static_cast<const float*>(tc_.data), size_t(tc_.ne0) * P);
+        sin_tab = upload(static_cast<const float*>(t("rope.sin").data), size_t(tc_.ne0) * P);
+        {   // dims whose table entries are exactly cos 1, sin 0 at every position
+            const float* c = static_cast<const float*>(tc_.data);
+            const float* s = static_cast<const float*>(t("rope.sin").data);
+            const int half = hd / 2;
+            auto identity = [&](int d) {
+                for (int p = 0; p < P; ++p)
+                    if (c[size_t(p) * hd + d] != 1.f || s[size_t(p) * hd + d] != 0.f) return false;
+                return true;
+            };
+            int active = half;
+            while (active > 0 && identity(active - 1) && identity(active - 1 + half)) --active;
+            for (int d = 0; d < active; ++d) if (identity(d) && identity(d + half)) { active = half; break; }
+            rope_half = active;
+        }
+        query = const_cast<float*>(f32_tensor("patch.forecast_query"));
+        p_hid = const_cast<float*>(f32_tensor("patch.hidden.weight")); pb_hid = bias_or_null("patch.hidden.bias");
+        p_res = const_cast<float*>(f32_tensor("patch.res.weight")); pb_res = bias_or_null("patch.res.bias");
+        pb_out = bias_or_null("patch.out.bias");
+        if (tc) { auto v = rows_f16(t("patch.out.weight")); p_out = reinterpret_cast<__half*>(upload(v.data(), v.size())); }
+        else { auto v = rows_f32(t("patch.out.weight")); f_pout = upload(v.data(), v.size()); }
+        attn.resize(m.schedule.size());
+        mlp.resize(m.schedule.size());
+        for (size_t i = 0; i < m.schedule.size(); ++i) {
+            const std::string b = "blk." + std::to_string(i) + ".";
+            const int kind = m.schedule[i];
+            std::vector<bool> axes = kind == 0 ? std::vector<bool>{true} : kind == 1 ? std::vector<bool>{false}
+                                   : kind == 2 ? std::vector<bool>{true, false} : std::vector<bool>{false, true};
+            for (size_t j = 0; j < axes.size(); ++j) {
+                AttnW a;
+                a.time = axes[j];
+                a.gate = axes[j] ? m.time_gate : m.variate_gate;
+                const std::string p = b + "attn." + std::to_string(j) + ".";
+                a.norm = f32_tensor(b + "attn_norm." + std::to_string(j) + ".weight");
+                std::vector<float> bq, bg;
+                if (mv.has(p + "qkv.bias")) { auto w = t(p + "qkv.bias"); bq.assign(static_cast<const float*>(w.data), static_cast<const float*>(w.data) + 3 * D); }
+                if (a.gate && mv.has(p + "gate.bias")) { auto w = t(p + "gate.bias"); bg.assign(static_cast<const float*>(w.data), static_cast<const float*>(w.data) + D); }
+                if (tc) {
+                    auto q = rows_f16(t(p + "qkv.weight"));
+                    std::vector<uint16_t> g;
+                    if (a.gate) g = rows_f16(t(p + "gate.weight"));
+                    std::vector<uint16_t> cat(q);
+                    cat.insert(cat.end(), g.begin(), g.end());
+                    a.qkvg = reinterpret_cast<__half*>(upload(cat.data(), cat.size()));
+                    a.n_qkvg = a.gate ? 4 * D : 3 * D;
+                    if (!bq.empty() || !bg.empty()) {
+                        std::vector<float> bc(size_t(a.n_qkvg), 0.f);
+                        if (!bq.empty()) std::copy(bq.begin(), bq.end(), bc.begin());
+                        if (!bg.empty()) std::copy(bg.begin(), bg.end(), bc.begin() + 3 * D);
+                        a.b_qkvg = upload(bc.data(), bc.size());
+                    }
+                    if (!a.time && a.gate) {
+                        auto vg = interleave(q.data() + size_t(2) * D * D, g.data(), size_t(D), size_t(D));
+                        a.vg = reinterpret_cast<__half*>(upload(vg.data(), vg.size()));
+                        if (!bq.empty() || !bg.empty()) {
+                            auto bvg = interleave_bias(bq.empty() ? nullptr : bq.data() + 2 * D, bg.empty() ? nullptr : bg.data(), size_t(D));
+                            a.b_vg = upload(bvg.data(), bvg.size());
+                        }
+                    }
+                    auto o = rows_f16(t(p + "out.weight"));
+                    a.out = reinterpret_cast<__half*>(upload(o.data(), o.size()));
+                } else {
+                    auto q = rows_f32(t(p + "qkv.weight"));
+                    a.f_qkv = upload(q.data(), q.size());
+                    if (!bq.empty()) a.fb_qkv = upload(bq.data(), bq.size());
+                    if (a.gate) {
+                        auto g = rows_f32(t(p + "gate.weight"));
+                        a.f_gate = upload(g.data(), g.size());
+                        if (!bg.empty()) a.fb_gate = upload(bg.data(), bg.size());
+                    }
+                    auto o = rows_f32(t(p + "out.weight"));
+                    a.f_out = upload(o.data(), o.size());
+                }
+                a.b_out = bias_or_null(p + "out.bias");
+                a.fb_out = a.b_out;
+                attn[i].push_back(a);
+            }
+            MlpW w;
+            w.norm = f32_tensor(b + "ffn_norm.weight");
+            w.b3 = bias_or_null(b + "ffn_w3.bias");
+            w.fb3 = w.b3;
+            if (tc) {
+                auto z = rows_f16(t(b + "ffn_w12.weight"));
+                auto zi = interleave(z.data(), z.data() + size_t(F) * D, size_t(F), size_t(D));
+                w.w12 = reinterpret_cast<__half*>(upload(zi.data(), zi.size()));
+                if (mv.has(b + "ffn_w12.bias")) {
+                    const float* bb = static_cast<const float*>(t(b + "ffn_w12.bias").data);
+                    auto bi = interleave_bias(bb, bb + F, size_t(F));
+                    w.b12 = upload(bi.data(), bi.size());
+                }
+                auto w3 = rows_f16(t(b + "ffn_w3.weight"));
+                w.w3 = reinterpret_cast<__half*>(upload(w3.data(), w3.size()));
+            } else {
+                auto z = rows_f32(t(b + "ffn_w12.weight"));
+                w.f12 = upload(z.data(), z.size());
+                w.fb12 = bias_or_null(b + "ffn_w12.bias");
+                auto w3 = rows_f32(t(b + "ffn_w3.weight"));
+                w.f3 = upload(w3.data(), w3.size());
+            }
+            mlp[i] = w;
+        }
+        out_norm = f32_tensor("out_norm.weight");
+        if (tc) {
+            auto a = rows_f16(t("head.hidden.weight")); h_hid = reinterpret_cast<__half*>(upload(a.data(), a.size()));
+            auto b = rows_f16(t("head.out.weight")); h_out = reinterpret_cast<__half*>(upload(b.data(), b.size()));
+            auto c = rows_f16(t("head.res.weight")); h_res = reinterpret_cast<__half*>(upload(c.data(), c.size()));
+        } else {
+            auto a = rows_f32(t("head.hidden.weight")); fh_hid = upload(a.data(), a.size());
+            auto b = rows_f32(t("head.out.weight")); fh_out = upload(b.data(), b.size());
+            auto c = rows_f32(t("head.res.weight")); fh_res = upload(c.data(), c.size());
+        }
+        err.ensure(sizeof(int));
+        check(cudaMemset(err.p, 0, sizeof(int)), "memset");
+    }
+
+    ~Impl() {
+        for (auto p : allocs) cudaFree(p);
+        for (auto& e : events) { cudaEventDestroy(e.a); cudaEventDestroy(e.b); }
+    }
+
+    // --- launch bookkeeping -------------------------------------------------------------
+    template <class Fn> void run(const char* cls, Fn fn) {
+        Ev* ev = nullptr;
+        if (timing) {
+            if (ev_used == events.size()) {
+                Ev e;
+                check(cudaEventCreate(&e.a), "event");
+                check(cudaEventCreate(&e.b), "event");
+                events.push_back(e);
+            }
+            ev = &events[ev_used++];
+            ev->cls = cls;
+            cudaEventRecord(ev->a, s);
+        }
+        cudaError_t e = fn();
+        if (e != cudaSuccess) throw std::runtime_error(std::string("launch ") + cls + ": " + cudaGetErrorString(e));
+        if (ev) cudaEventRecord(ev->b, s);
+        ++launches;
+    }
+
+    void gemm(EpiKind k, const GemmArgs& a, const char* cls = "gemm") {
+        run(cls, [&] { return tc_gemm(k, a, s, err.as<int>()); });
+    }
+    void sgemm(const SimtGemm& g, const char* cls = "gemm_simt") {
+        run(cls, [&] { return simt_gemm(g, s); });
+    }
+
+    // --- one decode block ---------------------------------------------------------------
+    // Inputs: win/wmask [R2][W] (W = T on the context path, T + h*ps with covariates),
+    // role [R2] (covariate path). Output: refined [R2][h*ps][Q]. first: compute cap stats.
+    void predict_block(int R2, int T, int h, bool cov, int group_rows, int pass_rows, bool first, int cap_ctx) {
+        const int W = cov ? T + h * ps : T;
+        const int N = W / ps, L = T / ps;
+        const int S = cov ? 2 * N : N + h;
+        const int P_all = cov ? N : h;
+        const int kvw = (N + 31) / 32;
+        const int64_t M = int64_t(R2) * S;
+        if (M > INT32_MAX / 4) throw std::runtime_error("batch too large");
+        const float* rows_p = win.as<float>();
+        const int8_t* mask_p = wmask.as<int8_t>();
+        feat.ensure(size_t(R2) * N * 2 * ps * 4);
+        aloc.ensure(R2 * 4); ascale.ensure(R2 * 4); first_obs.ensure(R2 * 4);
+        kv.ensure(size_t(R2) * kvw * 4);
+        rope_row.ensure(size_t(M) * 4); gbeg.ensure(R2 * 4); gsize.ensure(R2 * 4);
+        if (first) { caplo.ensure(R2 * 4); caphi.ensure(R2 * 4); capsc.ensure(R2 * 4); }
+        run("rows", [&] {
+            return scale_rows(rc, rows_p, mask_p, R2, W, cov ? (L - 1) * ps : T - 1, N, kvw, feat.as<float>(),
+                              aloc.as<float>(), ascale.as<float>(), kv.as<uint32_t>(), first_obs.as<int>(),
+                              first ? cap_ctx : 0, first ? caplo.as<float>() : nullptr,
+                              first ? caphi.as<float>() : nullptr, first ? capsc.as<float>() : nullptr, s);
+        });
+        if (cov)
+            run("rows", [&] {
+                return known_rows(rc, rows_p, mask_p, role.as<int8_t>(), R2, W, (L - 1) * ps, feat.as<float>(),
+                                  aloc.as<float>(), ascale.as<float>(), s);
+            });
+        run("rows", [&] {
+            return positions(rc, first_obs.as<int>(), R2, group_rows, N, S, cov, rope_row.as<int>(), gbeg.as<int>(),
+                             gsize.as<int>(), err.as<int>(), s);
+        });
+        // Patch projection (reference src/head.cpp:329-340) into token rows r*S + p, p < N.
+        x.ensure(size_t(M) * D * 4);
+        const int64_t PR = int64_t(R2) * N;
+        ph.ensure(size_t(PR) * 4 * D * (tc ? 2 : 4));
+        {
+            SimtGemm g;
+            g.A = feat.as<float>(); g.lda = 2 * ps; g.W = p_hid; g.M = int(PR); g.N = 4 * D; g.K = 2 * ps;
+            g.order = ORDER_CHAIN; g.epi = tc ? SEPI_SILU_F16 : SEPI_SILU_F32; g.bias = pb_hid; g.out = ph.p; g.ldo = 4 * D;
+            sgemm(g);
+            SimtGemm r;
+            r.A = feat.as<float>(); r.lda = 2 * ps; r.W = p_res; r.M = int(PR); r.N = D; r.K = 2 * ps;
+            r.order = ORDER_CHAIN; r.epi = SEPI_F32; r.bias = pb_res; r.out = x.p; r.ldo = D;
+            r.row_group = N; r.row_stride = S;
+            sgemm(r);
+        }
+        if (tc) {
+            GemmArgs a;
+            a.A = ph.as<__half>(); a.lda = 4 * D; a.B = p_out; a.ldb = 4 * D; a.M = int(PR); a.N = D; a.K = 4 * D;
+            a.epi.out = x.p; a.epi.ldo = D; a.epi.bias = pb_out; a.epi.resid = x.as<float>();
+            a.epi.row_group = N; a.epi.row_stride = S;
+            gemm(EPI_RESID, a);
+        } else {
+            SimtGemm g;
+            g.A = ph.as<float>(); g.lda = 4 * D; g.W = f_pout; g.M = int(PR); g.N = D; g.K = 4 * D;
+            g.order = ORDER_PANEL192; g.round_a_f16 = round_a; g.epi = SEPI_RESID; g.bias = pb_out; g.out = x.p; g.ldo = D;
+            g.row_group = N; g.row_stride = S;
+            sgemm(g);
+        }
+        run("rows", [&] { return fill_query(query, x.as<float>(), R2, S, N, D, s); });
+
+        MaskMeta mm;
+        mm.key_valid = kv.as<uint32_t>(); mm.kv_words = kvw; mm.N = N; mm.L = L; mm.S = S; mm.cov = cov;
+        mm.block_size = mv.block_size; mm.role = cov ? role.as<int8_t>() : nullptr;
+        mm.group_begin = gbeg.as<int>(); mm.group_size = gsize.as<int>(); mm.pass_rows = pass_rows;
+
+        const size_t eb = tc ? 2 : 4;
+        xn.ensure(size_t(M) * D * eb);
+        qb.ensure(size_t(M) * D * eb); kb.ensure(size_t(M) * D * eb); vb.ensure(size_t(M) * D * eb);
+        gb.ensure(size_t(M) * D * eb); att.ensure(size_t(M) * D * eb);
+        hb.ensure(size_t(M) * F * eb);
+        if (!tc) { fused.ensure(size_t(M) * 3 * D * 4); gtmp.ensure(size_t(M) * D * 4); zb.ensure(size_t(M) * 2 * F * 4); }
+
+        for (size_t li = 0; li < attn.size(); ++li) {
+            for (const AttnW& a : attn[li]) {
+                run("rows", [&] { return rms_norm(x.as<float>(), a.norm, int(M), D, mv.eps, xn.p, tc, 0, 0, 0, s); });
+                if (tc) attention_sublayer_tc(a, int(M), R2, S, group_rows, mm);
+                else attention_sublayer_simt(a, int(M), R2, S, mm);
+            }
+            const MlpW& w = mlp[li];
+            run("rows", [&] { return rms_norm(x.as<float>(), w.norm, int(M), D, mv.eps, xn.p, tc, 0, 0, 0, s); });
+            if (tc) {
+                GemmArgs a;
+                a.A = xn.as<__half>(); a.lda = D; a.B = w.w12; a.ldb = D; a.M = int(M); a.N = 2 * F; a.K = D;
+                a.epi.out = hb.p; a.epi.ldo = F; a.epi.bias = w.b12;
+                gemm(EPI_SWIGLU, a);
+                GemmArgs o;
+                o.A = hb.as<__half>(); o.lda = F; o.B = w.w3; o.ldb = F; o.M = int(M); o.N = D; o.K = F;
+                o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = w.b3; o.epi.resid = x.as<float>();
+                gemm(EPI_RESID, o);
+            } else {
+                SimtGemm g;
+                g.A = xn.as<float>(); g.lda = D; g.W = w.f12; g.M = int(M); g.N = 2 * F; g.K = D;
+                g.order = round_a ? ORDER_CHAIN : ORDER_PANEL192; g.round_a_f16 = round_a; g.epi = SEPI_F32;
+                g.bias = w.fb12; g.out = zb.p; g.ldo = 2 * F;
+                sgemm(g);
+                run("rows", [&] { return swiglu(zb.as<float>(), int(M), F, hb.as<float>(), s); });
+                SimtGemm o;
+                o.A = hb.as<float>(); o.lda = F; o.W = w.f3; o.M = int(M); o.N = D; o.K = F;
+                o.order = round_a ? ORDER_CHAIN : ORDER_PANEL192; o.round_a_f16 = round_a; o.epi = SEPI_RESID;
+                o.bias = w.fb3; o.out = x.p; o.ldo = D;
+                sgemm(o);
+            }
+        }
+        // out_norm on the decoder tokens only (per-token op; reference src/encoder.cpp:146 +
+        // src/predict_block.cpp:15-16 slice).
+        const int DR = R2 * P_all;
+        dec.ensure(size_t(DR) * D * eb);
+        run("rows", [&] { return rms_norm(x.as<float>(), out_norm, DR, D, mv.eps, dec.p, tc, P_all, S, N, s); });
+        const int NQ = ps * Q;
+        hh.ensure(size_t(DR) * 4 * D * eb);
+        hraw.ensure(size_t(DR) * NQ * 4);
+        if (tc) {
+            GemmArgs a;
+            a.A = dec.as<__half>(); a.lda = D; a.B = h_hid; a.ldb = D; a.M = DR; a.N = 4 * D; a.K = D;
+            a.epi.out = hh.p; a.epi.ldo = 4 * D;
+            gemm(EPI_SILU, a);
+            GemmArgs b;
+            b.A = hh.as<__half>(); b.lda = 4 * D; b.B = h_out; b.ldb = 4 * D; b.M = DR; b.N = NQ; b.K = 4 * D;
+            b.epi.out = hraw.p; b.epi.ldo = NQ;
+            gemm(EPI_F32, b);
+            GemmArgs c;
+            c.A = dec.as<__half>(); c.lda = D; c.B = h_res; c.ldb = D; c.M = DR; c.N = NQ; c.K = D;
+            c.epi.out = hraw.p; c.epi.ldo = NQ; c.epi.resid = hraw.as<float>();
+            gemm(EPI_RESID, c);
+        } else {
+            const int order = round_a ? ORDER_CHAIN : ORDER_F64;
+            SimtGemm a;
+            a.A = dec.as<float>(); a.lda = D; a.W = fh_hid; a.M = DR; a.N = 4 * D; a.K = D; a.order = order;
+            a.round_a_f16 = round_a; a.epi = SEPI_SILU_F32; a.out = hh.p; a.ldo = 4 * D;
+            sgemm(a);
+            SimtGemm b;
+            b.A = hh.as<float>(); b.lda = 4 * D; b.W = fh_out; b.M = DR; b.N = NQ; b.K = 4 * D; b.order = order;
+            b.round_a_f16 = round_a; b.epi = SEPI_F32; b.out = hraw.p; b.ldo = NQ;
+            sgemm(b);
+            SimtGemm c;
+            c.A = dec.as<float>(); c.lda = D; c.W = fh_res; c.M = DR; c.N = NQ; c.K = D; c.order = order;
+            c.round_a_f16 = round_a; c.epi = SEPI_RESID; c.out = hraw.p; c.ldo = NQ;
+            sgemm(c);
+        }
+        const int steps = h * ps;
+        qout.ensure(size_t(R2) * steps * Q * 4);
+        run("rows", [&] {
+            return quantile_head(rc, hraw.as<float>(), R2, P_all, cov ? L : 0, h, aloc.as<float>(), ascale.as<float>(),
+                                 qout.as<float>(), nullptr, err.as<int>(), s);
+        });
+        refined.ensure(size_t(R2) * steps * Q * 4);
+        if (h > 1) {
+            const int n = T / ps + h;
+            scratch.ensure(size_t(R2) * (3 * size_t(n) + 2 * ps + 2 * h) * 8);
+            const double clip = std::pow(double(FLT_MAX), 0.5) / 1e3;
+            run("rows", [&] {
+                return refine(rc, qout.as<float>(), rows_p, mask_p, W, cov ? role.as<int8_t>() : nullptr, aloc.as<float>(),
+                              ascale.as<float>(), R2, T, h, clip, scratch.as<double>(), refined.as<float>(), s);
+            });
+        } else {
+            check(cudaMemcpyAsync(refined.p, qout.p, size_t(R2) * steps * Q * 4, cudaMemcpyDeviceToDevice, s), "copy");
+        }
+    }
+
+    void attention_sublayer_tc(const AttnW& a, int M, int R2, int S, int group_rows, const MaskMeta& mm) {
+        __half* att16 = att.as<__half>();
+        if (!a.time && group_rows == 1) {
+            // One row per series: attention over a single key returns v exactly
+            // (reference tests/layer_kind_test.hpp:31-33), so the sublayer is
+            // out(v * sigmoid(gate)) and only the v and gate projections are computed.
+            GemmArgs g;
+            g.A = xn.as<__half>(); g.lda = D; g.M = M; g.K = D; g.epi.out = att16; g.epi.ldo = D;
+            if (a.gate) { g.B = a.vg; g.ldb = D; g.N = 2 * D; g.epi.bias = a.b_vg; gemm(EPI_VGATE, g); }
+            else {
+                g.B = a.qkvg + size_t(2) * D * D; g.ldb = D; g.N = D;
+                g.epi.bias = a.b_qkvg ? a.b_qkvg + 2 * D : nullptr;
+                gemm(EPI_F16, g);
+            }
+        } else {
+            GemmArgs g;
+            g.A = xn.as<__half>(); g.lda = D; g.B = a.qkvg; g.ldb = D; g.M = M; g.N = a.n_qkvg; g.K = D;
+            g.epi.bias = a.b_qkvg;
+            g.epi.qkvg[0] = qb.as<__half>(); g.epi.qkvg[1] = kb.as<__half>(); g.epi.qkvg[2] = vb.as<__half>();
+            g.epi.qkvg[3] = gb.as<__half>();
+            g.epi.S = S; g.epi.H = H; g.epi.D = D; g.epi.rope = a.time;
+            g.epi.cos_tab = cos_tab; g.epi.sin_tab = sin_tab; g.epi.rope_row = rope_row.as<int>(); g.epi.rope_half = rope_half;
+            gemm(EPI_QKVG, g);
+            const __half* gate = a.gate ? gb.as<__half>() : nullptr;
+            if (a.time) {
+                if (S <= 128)
+                    run("attention", [&] { return attention_time_tc(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, mm, s, err.as<int>()); });
+                else
+                    run("attention", [&] { return attention_time_simt<__half>(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, hd, mm, s); });
+            } else {
+                run("attention_variate", [&] { return attention_variate_simt<__half>(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, hd, mm, s); });
+            }
+        }
+        GemmArgs o;
+        o.A = att16; o.lda = D; o.B = a.out; o.ldb = D; o.M = M; o.N = D; o.K = D;
+        o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = a.b_out; o.epi.resid = x.as<float>();
+        gemm(EPI_RESID, o);
+    }
+
+    void attention_sublayer_simt(const AttnW& a, int M, int R2, int S, const MaskMeta& mm) {
+        const int order = round_a ? ORDER_CHAIN : ORDER_PANEL192;
+        SimtGemm g;
+        g.A = xn.as<float>(); g.lda = D; g.W = a.f_qkv; g.M = M; g.N = 3 * D; g.K = D; g.order = order;
+        g.round_a_f16 = round_a; g.epi = SEPI_F32; g.bias = a.fb_qkv; g.out = fused.p; g.ldo = 3 * D;
+        sgemm(g);
+        if (a.gate) {
+            SimtGemm q;
+            q.A = xn.as<float>(); q.lda = D; q.W = a.f_gate; q.M = M; q.N = D; q.K = D; q.order = order;
+            q.round_a_f16 = round_a; q.epi = SEPI_F32; q.bias = a.fb_gate; q.out = gtmp.p; q.ldo = D;
+            sgemm(q);
+        }
+        run("rows", [&] {
+            return qkv_scatter(fused.as<float>(), a.gate ? gtmp.as<float>() : nullptr, M, S, H, hd, a.time, cos_tab,
+                               sin_tab, rope_row.as<int>(), qb.as<float>(), kb.as<float>(), vb.as<float>(),
+                               a.gate ? gb.as<float>() : nullptr, s);
+        });
+        const float* gate = a.gate ? gb.as<float>() : nullptr;
+        if (a.time)
+            run("attention", [&] { return attention_time_simt<float>(qb.as<float>(), kb.as<float>(), vb.as<float>(), gate, att.as<float>(), R2, H, hd, mm, s); });
+        else
+            run("attention_variate", [&] { return attention_variate_simt<float>(qb.as<float>(), kb.as<float>(), vb.as<float>(), gate, att.as<float>(), R2, H, hd, mm, s); });
+        SimtGemm o;
+        o.A = att.as<float>(); o.lda = D; o.W = a.f_out; o.M = M; o.N = D; o.K = D; o.order = order;
+        o.round_a_f16 = round_a; o.epi = SEPI_RESID; o.bias = a.fb_out; o.out = x.p; o.ldo = D;
+        sgemm(o);
+    }
+
+    void check_device_error(const char* where) {
+        const int e = read_error(err.as<int>(), s);
+        if (!e) return;
+        if (e == kDevBadShape) throw std::runtime_error("NaN raw quantile or position outside the stored RoPE table");
+        if (e == kDevNaN) throw std::runtime_error("forecast produced NaN values; the input is degenerate");
+        if (e == kDevNonFinite) throw std::runtime_error("C ABI nonfinite forecast output");
+        throw std::runtime_error(std::string(where) + ": device wait expired (error word " + std::to_string(e) + ")");
+    }
+};
+
+Engine::Engine(const ModelView& mv, int device) : impl_(new Impl), device_(device) {
+    check(cudaSetDevice(device), "cudaSetDevice");
+    check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "stream");
+    impl_->s = stream_;
+    impl_->mv = mv;
+    impl_->load();
+    tc_ = impl_->tc;
+}
+
+Engine::~Engine() {
+    cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    impl_.reset();
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Engine::check_errors() {
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    check(cudaStreamSynchronize(stream_), "forecast");
+    impl_->check_device_error("forecast");
+}
+
+void Engine::timing_enable(bool on) { impl_->timing = on; }
+void Engine::timing_reset() { impl_->ev_used = 0; }
+bool Engine::timing_read(const std::string& cls, double* ms, int64_t* launches) {
+    cudaStreamSynchronize(stream_);
+    double total = 0;
+    int64_t n = 0;
+    for (size_t i = 0; i < impl_->ev_used; ++i) {
+        const auto& e = impl_->events[i];
+        if (cls != "all" && e.cls != cls) continue;
+        float t = 0;
+        if (cudaEventElapsedTime(&t, e.a, e.b) == cudaSuccess) { total += t; ++n; }
+    }
+    *ms = total;
+    *launches = n;
+    return true;
+}
+
+void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B, int V, int T, int H, bool symmetric,
+                              bool clip, int max_context, float* d_out, bool sync) {
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    Impl& im = *impl_;
+    im.launches = 0;
+    const ModelView& mv = im.mv;
+    const int ps = im.ps, Q = im.Q;
+    if (B <= 0 || V <= 0 || T <= 0 || H <= 0) throw std::runtime_error("invalid forecast dimensions");
+    const int cap = max_context ? max_context : mv.context_length;
+    if (cap > mv.context_length) throw std::runtime_error("max_context exceeds stored position range");
+    const int kept = std::min(T, cap), pad = (ps - kept % ps) % ps, len = kept + pad;
+    const int patches = (H + ps - 1) / ps;
+    const int shot = std::min(mv.per_shot ? mv.per_shot : 32, mv.block_size);
+    const int R = B * V, R2 = symmetric ? 2 * R : R;
+    const cudaStream_t s = stream_;
+    if (clip) {
+        im.clip_ok.ensure(size_t(R));
+        im.run("rows", [&] { return clip_eligibility(d_ctx, d_umask, R, T, im.clip_ok.as<int8_t>(), s); });
+    }
+    im.win.ensure(size_t(R2) * len * 4);
+    im.wmask.ensure(size_t(R2) * len);
+    im.run("rows", [&] { return assemble_targets(d_ctx, d_umask, R, T, kept, len, symmetric, im.win.as<float>(), im.wmask.as<int8_t>(), s); });
+    int Tc = len, done = 0;
+    const bool single = patches <= shot;
+    if (!single) im.decoded.ensure(size_t(R2) * H * Q * 4);
+    while (done < patches) {
+        const int block = std::min(shot, patches - done), n = block * ps, offset = done * ps;
+        // The V target rows of one series form one group (reference src/covariates.cpp:63).
+        im.predict_block(R2, Tc, block, false, V, R, done == 0, len);
+        if (single) break;
+        const int used = std::min(n, H - offset);
+        check(cudaMemcpy2DAsync(im.decoded.as<float>() + size_t(offset) * Q, size_t(H) * Q * 4, im.refined.p,
+                                size_t(n) * Q * 4, size_t(used) * Q * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
+        done += block;
+        if (done >= patches) break;
+        const int joined = Tc + n, keep = joined > mv.context_length ? std::max(ps, (mv.context_length / ps) * ps) : joined;
+        im.next_rows.ensure(size_t(R2) * keep * 4);
+        im.next_mask.ensure(size_t(R2) * keep);
+        im.run("rows", [&] {
+            return feedback(im.rc, im.win.as<float>(), im.wmask.as<int8_t>(), R2, Tc, im.refined.as<float>(), n, nullptr,
+                            nullptr, nullptr, keep, im.next_rows.as<float>(), im.next_mask.as<int8_t>(), s);
+        });
+        std::swap(im.win.p, im.next_rows.p); std::swap(im.win.bytes, im.next_rows.bytes);
+        std::swap(im.wmask.p, im.next_mask.p); std::swap(im.wmask.bytes, im.next_mask.bytes);
+        Tc = keep;
+    }
+    const float* dec = single ? im.refined.as<float>() : im.decoded.as<float>();
+    const int Hfull = single ? patches * ps : H;
+    im.run("rows", [&] {
+        return finalize(im.rc, dec, R, symmetric, B, V, V, H, Hfull, im.caplo.as<float>(), im.caphi.as<float>(),
+                        im.capsc.as<float>(), mv.cap_k > 0, clip ? im.clip_ok.as<int8_t>() : nullptr, d_out,
+                        im.err.as<int>(), s);
+    });
+    last_launches_ = im.launches;
+    if (sync) im.check_device_error("forecast");
+}
+
+void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetric, bool clip, const float* ctx,
+                           const uint8_t* umask, int T_req, float* h_out) {
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    Impl& im = *impl_;
+    im.launches = 0;
+    const ModelView& mv = im.mv;
+    const int ps = im.ps, Q = im.Q;
+    const int R = a.R, T = a.T, R2 = symmetric ? 2 * R : R;
+    const int patches = (H + ps - 1) / ps;
+    const int shot = std::min(mv.per_shot ? mv.per_shot : 32, mv.block_size);
+    const bool cov = a.roles != nullptr && mv.covariate_enabled;
+    const cudaStream_t s = stream_;
+    // Upload context rows (+ negation), roles, known future (+ negation).
+    std::vector<float> rows2(size_t(R2) * T);
+    std::vector<int8_t> mask2(size_t(R2) * T);
+    for (size_t i = 0; i < size_t(R) * T; ++i) {
+        rows2[i] = a.rows[i]; mask2[i] = a.mask[i];
+        if (symmetric) { rows2[size_t(R) * T + i] = -a.rows[i]; mask2[size_t(R) * T + i] = a.mask[i]; }
+    }
+    std::vector<int8_t> role2;
+    if (cov) {
+        role2.resize(R2);
+        for (int r = 0; r < R2; ++r) role2[r] = int8_t(a.roles[r % R]);
+        im.role.ensure(R2);
+        check(cudaMemcpyAsync(im.role.p, role2.data(), R2, cudaMemcpyHostToDevice, s), "upload roles");
+    }
+    const int Hh = a.Hh;
+    std::vector<float> fut2;
+    std::vector<int8_t> fm2;
+    if (a.future) {
+        fut2.resize(size_t(R2) * Hh);
+        fm2.resize(size_t(R2) * Hh);
+        for (size_t i = 0; i < size_t(R) * Hh; ++i) {
+            fut2[i] = a.future[i]; fm2[i] = a.future_mask[i];
+            if (symmetric) { fut2[size_t(R) * Hh + i] = -a.future[i]; fm2[size_t(R) * Hh + i] = a.future_mask[i]; }
+        }
+        im.future.ensure(fut2.size() * 4); im.fmask.ensure(fm2.size());
+        check(cudaMemcpyAsync(im.future.p, fut2.data(), fut2.size() * 4, cudaMemcpyHostToDevice, s), "upload");
+        check(cudaMemcpyAsync(im.fmask.p, fm2.data(), fm2.size(), cudaMemcpyHostToDevice, s), "upload");
+    }
+    im.rows.ensure(rows2.size() * 4); im.mask.ensure(mask2.size());
+    check(cudaMemcpyAsync(im.rows.p, rows2.data(), rows2.size() * 4, cudaMemcpyHostToDevice, s), "upload");
+    check(cudaMemcpyAsync(im.mask.p, mask2.data(), mask2.size(), cudaMemcpyHostToDevice, s), "upload");
+    // clip eligibility from the request context
+    if (clip) {
+        DevBuf dctx, dum;
+        dctx.ensure(size_t(B) * V * T_req * 4);
+        check(cudaMemcpyAsync(dctx.p, ctx, size_t(B) * V * T_req * 4, cudaMemcpyHostToDevice, s), "upload");
+        if (umask) { dum.ensure(size_t(B) * V * T_req); check(cudaMemcpyAsync(dum.p, umask, size_t(B) * V * T_req, cudaMemcpyHostToDevice, s), "upload"); }
+        im.clip_ok.ensure(size_t(B) * V);
+        im.run("rows", [&] { return clip_eligibility(dctx.as<float>(), umask ? dum.as<uint8_t>() : nullptr, B * V, T_req, im.clip_ok.as<int8_t>(), s); });
+        check(cudaStreamSynchronize(s), "sync");
+    }
+    im.decoded.ensure(size_t(R2) * H * Q * 4);
+    int Tc = T, done = 0;
+    while (done < patches) {
+        const int block = std::min(shot, patches - done), n = block * ps, offset = done * ps;
+        const int W = cov ? Tc + n : Tc;
+        im.win.ensure(size_t(R2) * W * 4);
+        im.wmask.ensure(size_t(R2) * W);
+        check(cudaMemsetAsync(im.win.p, 0, size_t(R2) * W * 4, s), "memset");
+        check(cudaMemsetAsync(im.wmask.p, 0, size_t(R2) * W, s), "memset");
+        check(cudaMemcpy2DAsync(im.win.p, size_t(W) * 4, im.rows.p, size_t(Tc) * 4, size_t(Tc) * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
+        check(cudaMemcpy2DAsync(im.wmask.p, W, im.mask.p, Tc, Tc, R2, cudaMemcpyDeviceToDevice, s), "copy");
+        if (cov && a.future) {
+            check(cudaMemcpy2DAsync(im.win.as<float>() + Tc, size_t(W) * 4, im.future.as<float>() + offset, size_t(Hh) * 4, size_t(n) * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
+            check(cudaMemcpy2DAsync(im.wmask.as<int8_t>() + Tc, W, im.fmask.as<int8_t>() + offset, Hh, n, R2, cudaMemcpyDeviceToDevice, s), "copy");
+        }
+        im.predict_block(R2, Tc, block, cov, a.group_rows, R, done == 0, Tc);
+        const int used = std::min(n, H - offset);
+        check(cudaMemcpy2DAsync(im.decoded.as<float>() + size_t(offset) * Q, size_t(H) * Q * 4, im.refined.p,
+                                size_t(n) * Q * 4, size_t(used) * Q * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
+        done += block;
+        if (done >= patches) break;
+        const int joined = Tc + n, keep = joined > mv.context_length ? std::max(ps, (mv.context_length / ps) * ps) : joined;
+        im.next_rows.ensure(size_t(R2) * keep * 4);
+        im.next_mask.ensure(size_t(R2) * keep);
+        // future slice of this block, row stride n
+        DevBuf fs, fms;
+        if (a.future) {
+            fs.ensure(size_t(R2) * n * 4); fms.ensure(size_t(R2) * n);
+            check(cudaMemcpy2DAsync(fs.p, size_t(n) * 4, im.future.as<float>() + offset, size_t(Hh) * 4, size_t(n) * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
+            check(cudaMemcpy2DAsync(fms.p, n, im.fmask.as<int8_t>() + offset, Hh, n, R2, cudaMemcpyDeviceToDevice, s), "copy");
+        }
+        im.run("rows", [&] {
+            return feedback(im.rc, im.rows.as<float>(), im.mask.as<int8_t>(), R2, Tc, im.refined.as<float>(), n,
+                            cov ? im.role.as<int8_t>() : nullptr, a.future ? fs.as<float>() : nullptr,
+                            a.future ? fms.as<int8_t>() : nullptr, keep, im.next_rows.as<float>(), im.next_mask.as<int8_t>(), s);
+        });
+        check(cudaStreamSynchronize(s), "sync");
+        std::swap(im.rows.p, im.next_rows.p); std::swap(im.rows.bytes, im.next_rows.bytes);
+        std::swap(im.mask.p, im.next_mask.p); std::swap(im.mask.bytes, im.next_mask.bytes);
+        Tc = keep;
+    }
+    DevBuf dout;
+    dout.ensure(size_t(B) * V * H * Q * 4);
+    const int all = R / B;
+    // Cap statistics come from the first block's scale pass over the assembled context.
+    im.run("rows", [&] {
+        return finalize(im.rc, im.decoded.as<float>(), R, symmetric, B, V, all, H, H, im.caplo.as<float>(),
+                        im.caphi.as<float>(), im.capsc.as<float>(), mv.cap_k > 0, clip ? im.clip_ok.as<int8_t>() : nullptr,
+                        dout.as<float>(), im.err.as<int>(), s);
+    });
+    check(cudaMemcpyAsync(h_out, dout.p, size_t(B) * V * H * Q * 4, cudaMemcpyDeviceToHost, s), "download");
+    check(cudaStreamSynchronize(s), "sync");
+    last_launches_ = im.launches;
+    im.check_device_error("forecast");
+}
+
+}  // namespace tsb

@@ -1,0 +1,94 @@
+// Device engine: one model resident on one GPU and the forecast pipeline that replaces the
+// reference's per-block ggml graphs (reference src/predict_block.cpp:6-56 via
+// src/backend.cpp GraphRunner) and its host decode loop (src/forecaster.cpp:19-108).
+#pragma once
+#include <cstdint>
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+namespace tsb {
+
+enum TensorType : int { TT_F32 = 0, TT_F16 = 1, TT_Q8_0 = 8 };
+
+struct HostTensor {
+    int type = TT_F32;
+    int64_t ne0 = 0, ne1 = 1;   // ne0 = contiguous (input) dimension
+    const void* data = nullptr;
+};
+
+// Everything the device needs from a loaded model (config KVs + tensors by GGUF name).
+struct ModelView {
+    int ps = 0, D = 0, H = 0, F = 0;
+    std::vector<int> schedule;        // 0 time, 1 variate, 2 time_variate, 3 variate_time
+    std::vector<double> knots;
+    int median = 0;
+    int block_size = 0, context_length = 0;
+    int rope_dim = 0, pos_min = 0;
+    float eps = 0;
+    bool attn_bias = false, mlp_bias = false, time_gate = false, variate_gate = false;
+    double minimum_scale = 0;
+    bool use_asinh = false, covariate_enabled = false, attend_missing = false;
+    double width_factor = 0;
+    int per_shot = 0;
+    double cap_k = 0, extreme = 0;
+    bool symmetric = false, clip = false;
+    std::function<HostTensor(const std::string&)> tensor;
+    std::function<bool(const std::string&)> has;
+};
+
+// Rows prepared on the host (covariate requests), reference AssembledRows
+// (src/covariates.hpp:12-17).
+struct HostRows {
+    int R = 0, T = 0, Hh = 0;                 // rows, context length, padded horizon
+    const float* rows = nullptr;              // [R][T]
+    const int8_t* mask = nullptr;             // [R][T]
+    const int64_t* roles = nullptr;           // [R] or null
+    const float* future = nullptr;            // [R][Hh] or null
+    const int8_t* future_mask = nullptr;
+    int group_rows = 1;                       // rows per series (contiguous)
+};
+
+class Engine {
+public:
+    Engine(const ModelView& mv, int device);
+    ~Engine();
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
+
+    int device() const { return device_; }
+    cudaStream_t stream() const { return stream_; }
+    bool tensor_cores() const { return tc_; }
+
+    // Requests without covariates, context and output in device memory.
+    // Throws std::runtime_error (message) on invalid input or device failure.
+    void forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B, int V, int T, int H, bool symmetric,
+                          bool clip, int max_context, float* d_out, bool sync);
+    // Requests with covariates: rows assembled on the host (one pass; the mirrored pass is
+    // formed on the device). ctx/umask: the original request context (clip eligibility).
+    void forecast_rows(const HostRows& a, int B, int V, int H, bool symmetric, bool clip, const float* ctx,
+                       const uint8_t* umask, int T_req, float* h_out);
+
+    // Synchronise the stream and turn a device error word into an exception.
+    void check_errors();
+
+    // Per-kernel-class timing (CUDA events on the engine stream).
+    void timing_enable(bool on);
+    void timing_reset();
+    bool timing_read(const std::string& cls, double* ms, int64_t* launches);
+    int64_t last_launches() const { return last_launches_; }
+
+private:
+    struct Impl;
+    std::unique_ptr<Impl> impl_;
+    int device_ = 0;
+    bool tc_ = false;
+    cudaStream_t stream_ = nullptr;
+    int64_t last_launches_ = 0;
+};
+
+}  // namespace tsb

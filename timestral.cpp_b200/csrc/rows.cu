@@ -1,0 +1,723 @@
+// Per-row / per-token kernels of the forecast path. Built with -fmad=false: like the
+// reference's F32 path (built with -ffp-contract=off), no multiply-add is fused unless an
+// explicit fma appears in the source.
+#include "common.cuh"
+#include "rows.cuh"
+
+#include <cfloat>
+#include <cmath>
+
+namespace tsb {
+
+namespace {
+
+constexpr int TPB = 256;
+
+inline unsigned blocks_for(int64_t n, int tpb = TPB) { return unsigned((n + tpb - 1) / tpb); }
+
+// ---------------------------------------------------------------------------------------
+// Assembly of target rows (reference src/covariates.cpp:48-50,69-70).
+__global__ void assemble_kernel(const float* __restrict__ ctx, const uint8_t* __restrict__ umask, int BV, int T,
+                                int kept, int len, int mirrored, float* __restrict__ rows, int8_t* __restrict__ mask) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x & 31;
+    if (warp >= BV) return;
+    const int r = warp, pad = len - kept, start = T - kept;
+    const float* x = ctx + int64_t(r) * T;
+    const uint8_t* um = umask ? umask + int64_t(r) * T : nullptr;
+    float* out = rows + int64_t(r) * len;
+    int8_t* om = mask + int64_t(r) * len;
+    float* out2 = mirrored ? rows + (int64_t(BV) + r) * len : nullptr;
+    int8_t* om2 = mirrored ? mask + (int64_t(BV) + r) * len : nullptr;
+    for (int t = lane; t < pad; t += 32) {
+        out[t] = 0.f; om[t] = 0;
+        if (out2) { out2[t] = -0.f; om2[t] = 0; }
+    }
+    float carry = 0.f;  // value of the last observed step before the chunk
+    for (int c0 = 0; c0 < T; c0 += 32) {
+        const int t = c0 + lane;
+        float v = 0.f;
+        bool obs = false;
+        if (t < T) { v = x[t]; obs = isfinite(v) && (!um || um[t]); }
+        int idx = obs ? lane : -1;
+        // inclusive max-scan of the last observed lane
+        for (int o = 1; o < 32; o <<= 1) {
+            const int other = __shfl_up_sync(0xffffffffu, idx, o);
+            if (lane >= o) idx = max(idx, other);
+        }
+        const float src = __shfl_sync(0xffffffffu, v, idx < 0 ? 0 : idx);
+        const float filled = idx < 0 ? carry : src;
+        const int last = __shfl_sync(0xffffffffu, idx, 31);
+        const float last_val = __shfl_sync(0xffffffffu, v, last < 0 ? 0 : last);
+        if (last >= 0) carry = last_val;
+        if (t < T && t >= start) {
+            const int o = pad + t - start;
+            out[o] = filled; om[o] = obs;
+            if (out2) { out2[o] = -filled; om2[o] = obs; }
+        }
+    }
+}
+
+__global__ void clip_ok_kernel(const float* __restrict__ ctx, const uint8_t* __restrict__ umask, int BV, int T,
+                               int8_t* __restrict__ ok) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x & 31;
+    if (warp >= BV) return;
+    bool any = false, eligible = true;
+    for (int t = lane; t < T; t += 32) {
+        const int64_t i = int64_t(warp) * T + t;
+        const float v = ctx[i];
+        const bool observed = isfinite(v) && (!umask || umask[i]);
+        if (observed) { any = true; eligible &= v >= 0.f; }
+    }
+    any = __any_sync(0xffffffffu, any);
+    eligible = __all_sync(0xffffffffu, eligible);
+    if (lane == 0) ok[warp] = any && eligible;
+}
+
+// ---------------------------------------------------------------------------------------
+// Causal scaler (reference src/scaler.cpp:27-58) and patch features (src/encoder.cpp:12-23).
+__device__ __forceinline__ float affine_value(float x, float loc, float scale, bool observed, bool squash) {
+    const float y = __fdiv_rn(__fsub_rn(x, loc), fmaxf(scale, FLT_EPSILON));
+    if (!observed) return 0.0f;
+    return squash ? asinhf(y) : y;
+}
+
+__global__ void scale_kernel(const RowConfig c, const float* __restrict__ rows, const int8_t* __restrict__ mask, int R,
+                             int W, int anchor_step, int enc_patches, int kv_words, float* __restrict__ features,
+                             float* __restrict__ aloc, float* __restrict__ ascale, uint32_t* __restrict__ key_valid,
+                             int* __restrict__ first_obs, int ctx_len, float* __restrict__ cap_lo,
+                             float* __restrict__ cap_hi, float* __restrict__ cap_scale) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    const int ps = c.ps;
+    const float* x = rows + int64_t(r) * W;
+    const int8_t* m = mask + int64_t(r) * W;
+    float* feat = features + int64_t(r) * (W / ps) * 2 * ps;
+    double cum_w = 0, cum_x = 0, prev_mean = 0, m2 = 0;
+    bool started = false;
+    int first = -1;
+    uint32_t word = 0;
+    float lo = INFINITY, hi = -INFINITY;
+    for (int t = 0; t < W; ++t) {
+        const double v = x[t], w = m[t];
+        cum_w = __dadd_rn(cum_w, w);
+        cum_x = __dadd_rn(cum_x, __dmul_rn(w, v));
+        const double den = fmax(cum_w, 1.0);
+        const double mean = __ddiv_rn(cum_x, den);
+        const double inc = __dmul_rn(__dmul_rn(__dsub_rn(v, prev_mean), __dsub_rn(v, mean)), w);
+        m2 = __dadd_rn(m2, inc);
+        prev_mean = mean;
+        if (t < ctx_len && m[t]) { lo = fminf(lo, x[t]); hi = fmaxf(hi, x[t]); }
+        if ((t + 1) % ps == 0) {
+            const int p = t / ps;
+            const float loc = float(mean);
+            const float scale = float(fmax(sqrt(__ddiv_rn(m2, fmax(__dsub_rn(den, 1.0), 1.0))), c.minimum_scale));
+            bool obs = false;
+            float* f = feat + int64_t(p) * 2 * ps;
+            for (int j = 0; j < ps; ++j) {
+                const int tj = t + 1 - ps + j;
+                const bool o = m[tj] != 0;
+                obs |= o;
+                f[j] = affine_value(x[tj], loc, scale, o, c.use_asinh);
+                f[ps + j] = o ? 0.f : 1.f;
+            }
+            if (p < enc_patches) {
+                started |= obs;
+                if (obs && first < 0) first = p;
+                if (obs || (c.attend_missing && started)) word |= 1u << (p & 31);
+                if ((p & 31) == 31 || p == enc_patches - 1) {
+                    key_valid[int64_t(r) * kv_words + (p >> 5)] = word;
+                    word = 0;
+                }
+            }
+            if (anchor_step >= t + 1 - ps && anchor_step <= t) { aloc[r] = loc; ascale[r] = scale; }
+            if (cap_scale && ctx_len - 1 >= t + 1 - ps && ctx_len - 1 <= t) cap_scale[r] = scale;
+        }
+    }
+    first_obs[r] = first;
+    if (cap_lo) {
+        cap_lo[r] = isfinite(lo) ? lo : 0.f;
+        cap_hi[r] = isfinite(hi) ? hi : 0.f;
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Float sum cascade of ATen's contiguous reduction, one warp per sequence: lane j holds the
+// accumulators of lane slot (k, l) = (j / 8, j % 8) (reference src/torch_sum.hpp:9-23,
+// src/layers.cpp:262-278). `sq` squares each element; `small` enables the four-partial
+// path for length < 8 of the plain sum.
+template <class F>
+__device__ float warp_cascade(F val, int length, bool small_path) {
+    const int lane = threadIdx.x & 31;
+    if (small_path && length < 8) {
+        float total = 0.f;
+        if (lane == 0) {
+            float partial[4] = {0.f, 0.f, 0.f, 0.f};
+            int i = 0;
+            for (; i + 4 <= length; i += 4) for (int j = 0; j < 4; ++j) partial[j] = __fadd_rn(partial[j], val(i + j));
+            for (; i < length; ++i) partial[0] = __fadd_rn(partial[0], val(i));
+            for (int j = 1; j < 4; ++j) partial[0] = __fadd_rn(partial[0], partial[j]);
+            total = partial[0];
+        }
+        return __shfl_sync(0xffffffffu, total, 0);
+    }
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    const int groups = length / 32;
+    int log = 0;
+    for (int n = groups ? groups - 1 : 0; n; n >>= 1) ++log;
+    const int power = max(4, log / 4);
+    const int step = 1 << power, msk = step - 1;
+    int i = 0;
+    for (; i + step <= groups;) {
+        for (int j = 0; j < step; ++j, ++i) acc0 = __fadd_rn(acc0, val(i * 32 + lane));
+        // level 1..3 promotions, with the early break of the reference
+        acc1 = __fadd_rn(acc1, acc0); acc0 = 0.f;
+        if (i & (msk << power)) continue;
+        acc2 = __fadd_rn(acc2, acc1); acc1 = 0.f;
+        if (i & (msk << (2 * power))) continue;
+        acc3 = __fadd_rn(acc3, acc2); acc2 = 0.f;
+    }
+    for (; i < groups; ++i) acc0 = __fadd_rn(acc0, val(i * 32 + lane));
+    acc0 = __fadd_rn(acc0, acc1);
+    acc0 = __fadd_rn(acc0, acc2);
+    acc0 = __fadd_rn(acc0, acc3);
+    int v = groups * 4;
+    if (lane < 8) for (int vv = v; vv < length / 8; ++vv) acc0 = __fadd_rn(acc0, val(vv * 8 + lane));
+    v = max(v, length / 8);
+    // acc[0][0][l] += acc[0][k][l] for k = 1, 2, 3
+    const float k1 = __shfl_sync(0xffffffffu, acc0, (lane & 7) + 8);
+    const float k2 = __shfl_sync(0xffffffffu, acc0, (lane & 7) + 16);
+    const float k3 = __shfl_sync(0xffffffffu, acc0, (lane & 7) + 24);
+    float a = __fadd_rn(__fadd_rn(__fadd_rn(acc0, k1), k2), k3);
+    float sum = 0.f;
+    float lanes[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) lanes[l] = __shfl_sync(0xffffffffu, a, l);
+    if (lane == 0) {
+        for (int d = v * 8; d < length; ++d) sum = __fadd_rn(sum, val(d));
+        for (int l = 0; l < 8; ++l) sum = __fadd_rn(sum, lanes[l]);
+    }
+    return __shfl_sync(0xffffffffu, sum, 0);
+}
+
+__global__ void rms_kernel(const float* __restrict__ x, const float* __restrict__ w, int tokens, int D, float eps,
+                           void* __restrict__ out, int out_f16, int sub, int S, int off) {
+    const int i = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x & 31;
+    if (i >= tokens) return;
+    const int64_t tok = sub ? int64_t(i / sub) * S + off + i % sub : i;
+    const float* xr = x + tok * D;
+    const float ssq = warp_cascade([&](int d) { const float a = xr[d]; return __fmul_rn(a, a); }, D, false);
+    const float mean = __fdiv_rn(ssq, float(D));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    if (out_f16) {
+        __half* o = static_cast<__half*>(out) + int64_t(i) * D;
+        for (int d = lane; d < D; d += 32) o[d] = __float2half_rn(__fmul_rn(__fmul_rn(xr[d], inv), w[d]));
+    } else {
+        float* o = static_cast<float*>(out) + int64_t(i) * D;
+        for (int d = lane; d < D; d += 32) o[d] = __fmul_rn(__fmul_rn(xr[d], inv), w[d]);
+    }
+}
+
+// Known covariate rows: non-causal float statistics (reference src/scaler.cpp:60-107).
+__global__ void known_kernel(const RowConfig c, const float* __restrict__ rows, const int8_t* __restrict__ mask,
+                             const int8_t* __restrict__ role, int R, int W, int anchor_step, float* __restrict__ features,
+                             float* __restrict__ aloc, float* __restrict__ ascale) {
+    const int r = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x & 31;
+    if (r >= R || role[r] != 2) return;
+    const float* x = rows + int64_t(r) * W;
+    const int8_t* m = mask + int64_t(r) * W;
+    bool binary = true, any = false;
+    for (int t = lane; t < W; t += 32) {
+        any |= m[t] != 0;
+        binary &= !m[t] || x[t] == 0.f || x[t] == 1.f;
+    }
+    any = __any_sync(0xffffffffu, any);
+    binary = __all_sync(0xffffffffu, binary);
+    const float n = fmaxf(warp_cascade([&](int t) { return float(m[t]); }, W, true), 1.0f);
+    const float loc = __fdiv_rn(warp_cascade([&](int t) { return __fmul_rn(x[t], float(m[t])); }, W, true), n);
+    const float var = __fdiv_rn(warp_cascade([&](int t) {
+                                    const float cen = __fmul_rn(__fsub_rn(x[t], loc), float(m[t]));
+                                    return __fmul_rn(cen, cen);
+                                }, W, true), n);
+    const float scale = fmaxf(__fsqrt_rn(var), float(c.minimum_scale));
+    const bool is_bin = binary && any;
+    const float L = is_bin ? 0.0f : loc, Sc = is_bin ? 1.0f : scale;
+    const int ps = c.ps;
+    float* feat = features + int64_t(r) * (W / ps) * 2 * ps;
+    for (int t = lane; t < W; t += 32) {
+        const int p = t / ps, j = t % ps;
+        feat[int64_t(p) * 2 * ps + j] = affine_value(x[t], L, Sc, m[t] != 0, c.use_asinh && !is_bin);
+    }
+    if (lane == 0) { aloc[r] = L; ascale[r] = Sc; }
+    (void)anchor_step;
+}
+
+// Positions and groups (reference src/masks.cpp:13-18).
+__global__ void positions_kernel(const RowConfig c, const int* __restrict__ first_obs, int R, int group_rows, int N,
+                                 int S, int cov, int* __restrict__ rope_row, int* __restrict__ gbegin,
+                                 int* __restrict__ gsize, int* err) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    const int g0 = (r / group_rows) * group_rows;
+    int first = N;
+    for (int j = 0; j < group_rows; ++j) {
+        const int f = first_obs[g0 + j];
+        if (f >= 0 && f < first) first = f;
+    }
+    if (first == N) first = 0;
+    for (int p = 0; p < S; ++p) {
+        const int pos = (cov ? p % N : p) - first;
+        const int idx = pos - c.pos_min;
+        if (idx < 0 || idx >= c.rope_len) { record_error(err, kDevBadShape); rope_row[int64_t(r) * S + p] = 0; }
+        else rope_row[int64_t(r) * S + p] = idx;
+    }
+    gbegin[r] = g0;
+    gsize[r] = group_rows;
+}
+
+__global__ void fill_query_kernel(const float* __restrict__ q, float* __restrict__ x, int R, int S, int first, int D) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int per = (S - first) * D;
+    if (i >= int64_t(R) * per) return;
+    const int r = int(i / per), rem = int(i % per), p = first + rem / D, d = rem % D;
+    x[(int64_t(r) * S + p) * D + d] = q[d];
+}
+
+// ---------------------------------------------------------------------------------------
+// F32-path element kernels.
+__global__ void qkv_scatter_kernel(const float* __restrict__ fused, const float* __restrict__ gate, int M, int S, int H,
+                                   int hd, int rope, const float* __restrict__ ct, const float* __restrict__ st,
+                                   const int* __restrict__ rope_row, float* __restrict__ q, float* __restrict__ k,
+                                   float* __restrict__ v, float* __restrict__ g) {
+    const int D = H * hd;
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= int64_t(M) * D) return;
+    const int m = int(i / D), col = int(i % D), h = col / hd, d = col % hd, half = hd / 2;
+    const float* z = fused + int64_t(m) * 3 * D;
+    const int r = m / S, s = m % S;
+    const int64_t o = ((int64_t(r) * H + h) * S + s) * hd + d;
+    float qv = z[col], kv = z[D + col];
+    if (rope) {
+        const float* c = ct + int64_t(rope_row[m]) * hd;
+        const float* sn = st + int64_t(rope_row[m]) * hd;
+        const int base = h * hd;
+        const float qr = d < half ? -z[base + d + half] : z[base + d - half];
+        const float kr = d < half ? -z[D + base + d + half] : z[D + base + d - half];
+        qv = __fadd_rn(__fmul_rn(qv, c[d]), __fmul_rn(qr, sn[d]));
+        kv = __fadd_rn(__fmul_rn(kv, c[d]), __fmul_rn(kr, sn[d]));
+    }
+    q[o] = qv; k[o] = kv; v[o] = z[2 * D + col];
+    if (g) g[o] = ref_sigmoid(gate[int64_t(m) * D + col]);
+}
+
+__global__ void swiglu_kernel(const float* __restrict__ z, int M, int F, float* __restrict__ h) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= int64_t(M) * F) return;
+    const int m = int(i / F), j = int(i % F);
+    const float u = z[int64_t(m) * 2 * F + F + j];
+    h[i] = __fmul_rn(z[int64_t(m) * 2 * F + j], ref_silu(u));
+}
+
+__global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, int64_t n) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = __fadd_rn(x[i], y[i]);
+}
+
+// ---------------------------------------------------------------------------------------
+// Quantile head tail (reference src/head.cpp:61-80, src/scaler.cpp:109-137).
+__global__ void quantile_kernel(const RowConfig c, const float* __restrict__ raw, int R, int P_all, int p0, int h,
+                                const float* __restrict__ loc, const float* __restrict__ scale, float* __restrict__ out,
+                                float* __restrict__ normalized, int* err) {
+    const int ps = c.ps, Q = c.Q, mi = c.median;
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= int64_t(R) * h * ps) return;
+    const int r = int(i / (int64_t(h) * ps)), j = int((i / ps) % h), kstep = int(i % ps);
+    const float* x = raw + (int64_t(r) * P_all + p0 + j) * ps * Q + kstep * Q;
+    const int64_t o = (int64_t(r) * h * ps + int64_t(j) * ps + kstep) * Q;
+    float q[64];
+    for (int t = 0; t < Q; ++t) if (isnan(x[t])) { record_error(err, kDevBadShape); }
+    const float limit = FLT_MAX;
+    auto clampv = [&](float v) { return fmaxf(-limit, fminf(limit, v)); };
+    auto inc = [&](int t) {
+        const float v = x[t];
+        return __fmul_rn(c.widths[t], v > 20.f ? v : log1pf(activation_exp(v)));
+    };
+    const float median = x[mi];
+    q[mi] = clampv(median);
+    double sum = 0;
+    for (int t = mi + 1; t < Q; ++t) { sum = __dadd_rn(sum, double(inc(t))); q[t] = clampv(__fadd_rn(median, float(sum))); }
+    sum = 0;
+    for (int t = mi - 1; t >= 0; --t) { sum = __dadd_rn(sum, double(inc(t))); q[t] = clampv(__fsub_rn(median, float(sum))); }
+    const float L = loc[r], Sc = scale[r];
+    float lo = INFINITY, hi = -INFINITY;
+    for (int t = 0; t < Q; ++t) {
+        if (normalized) normalized[o + t] = q[t];
+        const float v = c.use_asinh ? sinhf(q[t]) : q[t];
+        q[t] = __fadd_rn(__fmul_rn(v, Sc), L);
+        if (isfinite(q[t])) { lo = fminf(lo, q[t]); hi = fmaxf(hi, q[t]); }
+    }
+    for (int t = 0; t < Q; ++t) {
+        float v = q[t];
+        if (v == INFINITY) v = isfinite(hi) ? hi : 0.f;
+        else if (v == -INFINITY) v = isfinite(lo) ? lo : 0.f;
+        out[o + t] = v;
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Refine (reference src/refine.cpp).
+__device__ double numpy_sum_dev(const double* x, int n) {
+    // NumPy pairwise float64 sum (reference src/numpy_sum.hpp:6-14), iterative over the
+    // recursion's leaves for n > 128.
+    if (n < 8) { double r = -0.0; for (int i = 0; i < n; ++i) r = __dadd_rn(r, x[i]); return r; }
+    if (n <= 128) {
+        double r[8];
+        for (int j = 0; j < 8; ++j) r[j] = x[j];
+        int i = 8;
+        for (; i < n - (n % 8); i += 8) for (int j = 0; j < 8; ++j) r[j] = __dadd_rn(r[j], x[i + j]);
+        double out = __dadd_rn(__dadd_rn(__dadd_rn(r[0], r[1]), __dadd_rn(r[2], r[3])),
+                               __dadd_rn(__dadd_rn(r[4], r[5]), __dadd_rn(r[6], r[7])));
+        for (; i < n; ++i) out = __dadd_rn(out, x[i]);
+        return out;
+    }
+    int half = n / 2;
+    half -= half % 8;
+    return __dadd_rn(numpy_sum_dev(x, half), numpy_sum_dev(x + half, n - half));
+}
+
+struct WS { double w, mean, m2; };
+__device__ __forceinline__ WS combine(WS a, WS b) {
+    const double w = __dadd_rn(a.w, b.w), safe = fmax(w, DBL_MIN);
+    const double delta = __dsub_rn(b.mean, a.mean);
+    const double mean = __dadd_rn(a.mean, __ddiv_rn(__dmul_rn(delta, b.w), safe));
+    const double m2 = __dadd_rn(__dadd_rn(a.m2, b.m2), __ddiv_rn(__dmul_rn(__dmul_rn(__dmul_rn(delta, delta), a.w), b.w), safe));
+    return {w, w == 0 ? 0.0 : mean, w == 0 ? 0.0 : m2};
+}
+
+__global__ void refine_kernel(const RowConfig c, const float* __restrict__ q, const float* __restrict__ rows,
+                              const int8_t* __restrict__ mask, int stride, const int8_t* __restrict__ role,
+                              const float* __restrict__ loc0a, const float* __restrict__ scale0a, int R, int T, int h,
+                              double clip, double* __restrict__ scratch, float* __restrict__ out) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    const int ps = c.ps, Q = c.Q, mi = c.median, cp = T / ps, n = cp + h, steps = h * ps;
+    const float* qr = q + int64_t(r) * steps * Q;
+    float* outr = out + int64_t(r) * steps * Q;
+    if (role && role[r] != 0) {
+        for (int i = 0; i < steps * Q; ++i) outr[i] = qr[i];
+        return;
+    }
+    double* st = scratch + int64_t(r) * (3 * int64_t(n) + 2 * ps + 2 * h);
+    double* terms = st + 3 * int64_t(n);
+    double* folded = terms + ps;
+    double* floc = folded + ps;
+    double* fscale = floc + h;
+    const float* x = rows + int64_t(r) * stride;
+    const int8_t* m = mask + int64_t(r) * stride;
+    for (int p = 0; p < cp; ++p) {
+        const int s0 = p * ps;
+        for (int k = 0; k < ps; ++k) terms[k] = m[s0 + k];
+        const double w = numpy_sum_dev(terms, ps);
+        for (int k = 0; k < ps; ++k) terms[k] = __dmul_rn(double(x[s0 + k]), double(m[s0 + k]));
+        const double mean = __ddiv_rn(numpy_sum_dev(terms, ps), fmax(w, 1.0));
+        for (int k = 0; k < ps; ++k) { const double d = __dsub_rn(double(x[s0 + k]), mean); terms[k] = __dmul_rn(double(m[s0 + k]), __dmul_rn(d, d)); }
+        const double m2 = numpy_sum_dev(terms, ps);
+        st[3 * p] = w; st[3 * p + 1] = w == 0 ? 0.0 : mean; st[3 * p + 2] = w == 0 ? 0.0 : m2;
+    }
+    for (int p = cp; p < n; ++p) { st[3 * p] = 0; st[3 * p + 1] = 0; st[3 * p + 2] = 0; }
+    // Inclusive Hillis-Steele rounds, in place from the top so each round reads the previous one.
+    for (int d = 1; d < n;) {
+        for (int i = n - 1; i >= 0; --i) {
+            const WS prev = i >= d ? WS{st[3 * (i - d)], st[3 * (i - d) + 1], st[3 * (i - d) + 2]} : WS{0, 0, 0};
+            const WS cur{st[3 * i], st[3 * i + 1], st[3 * i + 2]};
+            const WS nw = combine(prev, cur);
+            st[3 * i] = nw.w; st[3 * i + 1] = nw.mean; st[3 * i + 2] = nw.m2;
+        }
+        if (d > n / 2) break;
+        d *= 2;
+    }
+    const float loc0 = loc0a[r], scale0 = scale0a[r];
+    WS state{st[3 * (cp - 1)], st[3 * (cp - 1) + 1], st[3 * (cp - 1) + 2]};
+    const double offset = state.mean;
+    for (int j = 0; j < h; ++j) {
+        const double var = fmax(__ddiv_rn(state.m2, fmax(__dsub_rn(state.w, 1.0), 1.0)), 0.0);
+        const double sc = fmax(sqrt(var), c.minimum_scale);
+        floc[j] = state.mean; fscale[j] = sc;
+        for (int k = 0; k < ps; ++k) {
+            const double med = __ddiv_rn(__dsub_rn(double(qr[(j * ps + k) * Q + mi]), double(loc0)), double(scale0));
+            const double v = __dsub_rn(__dadd_rn(__dmul_rn(med, sc), state.mean), offset);
+            folded[k] = __dadd_rn(fmin(fmax(v, -clip), clip), offset);
+        }
+        const double mean = __ddiv_rn(numpy_sum_dev(folded, ps), double(ps));
+        for (int k = 0; k < ps; ++k) { const double d = __dsub_rn(folded[k], mean); terms[k] = __dmul_rn(d, d); }
+        state = combine(state, WS{double(ps), mean, numpy_sum_dev(terms, ps)});
+    }
+    for (int t = 0; t < steps; ++t) {
+        const int j = t / ps;
+        const float loc = j ? float(floc[j]) : loc0, sc = j ? float(fscale[j]) : scale0;
+        float lo = INFINITY, hi = -INFINITY;
+        float vals[64];
+        for (int k = 0; k < Q; ++k) {
+            const float nrm = __fdiv_rn(__fsub_rn(qr[t * Q + k], loc0), scale0);
+            const float v = __fadd_rn(__fmul_rn(nrm, sc), loc);
+            vals[k] = v;
+            if (isfinite(v)) { lo = fminf(lo, v); hi = fmaxf(hi, v); }
+        }
+        for (int k = 0; k < Q; ++k) {
+            float v = vals[k];
+            if (v == INFINITY) v = isfinite(hi) ? hi : 0.f;
+            else if (v == -INFINITY) v = isfinite(lo) ? lo : 0.f;
+            outr[t * Q + k] = v;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Final combine (reference src/forecaster.cpp:72-104).
+__global__ void finalize_kernel(const RowConfig c, const float* __restrict__ dec, int Rp, int mirrored, int B, int V,
+                                int all, int H, int Hfull, const float* __restrict__ lo_a, const float* __restrict__ hi_a,
+                                const float* __restrict__ sc_a, int cap_on, const int8_t* __restrict__ clip_ok,
+                                float* __restrict__ out, int* err) {
+    const int Q = c.Q;
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= int64_t(B) * V * H * Q) return;
+    const int q = int(i % Q), t = int((i / Q) % H), bv = int(i / (int64_t(H) * Q));
+    const int b = bv / V, v = bv % V, row = b * all + v;
+    auto capped = [&](int rr, int qq) {
+        float val = dec[(int64_t(rr) * Hfull + t) * Q + qq];
+        if (cap_on) {
+            // std::min(std::max(v, lo), hi): a NaN value stays NaN
+            const float width = __fmul_rn(sc_a[rr], float(c.cap_k));
+            const float lo = __fsub_rn(lo_a[rr], width), hi = __fadd_rn(hi_a[rr], width);
+            val = (val < lo) ? lo : val;
+            val = (hi < val) ? hi : val;
+        }
+        if (isnan(val)) record_error(err, kDevNaN);
+        return val;
+    };
+    float val = capped(row, q);
+    if (mirrored) {
+        const float mv = capped(Rp + row, Q - 1 - q);
+        val = __fmul_rn(0.5f, __fadd_rn(val, -mv));
+    }
+    if (clip_ok && clip_ok[bv]) val = fmaxf(val, 0.f);
+    if (!isfinite(val)) record_error(err, kDevNonFinite);
+    out[i] = val;
+}
+
+// Next decode block (reference src/forecaster.cpp:52-64).
+__global__ void feedback_kernel(const RowConfig c, const float* __restrict__ rows, const int8_t* __restrict__ mask, int R,
+                                int T, const float* __restrict__ q, int n, const int8_t* __restrict__ role,
+                                const float* __restrict__ future, const int8_t* __restrict__ fmask, int keep,
+                                float* __restrict__ nrows, int8_t* __restrict__ nmask) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= int64_t(R) * keep) return;
+    const int r = int(i / keep), j = int(i % keep);
+    const int start = T + n - keep, t = start + j;
+    float value;
+    int8_t observed;
+    if (t < T) { value = rows[int64_t(r) * T + t]; observed = mask[int64_t(r) * T + t]; }
+    else {
+        const int k = t - T;
+        value = q[(int64_t(r) * n + k) * c.Q + c.median];
+        observed = 1;
+        if (!isfinite(value) || fabsf(value) >= c.extreme) value = 0.f;
+        if (role) {
+            if (role[r] == 2 && future) { value = future[int64_t(r) * n + k]; observed = fmask[int64_t(r) * n + k]; }
+            if (role[r] == 1) { value = 0.f; observed = 0; }
+        }
+    }
+    nrows[i] = value;
+    nmask[i] = observed;
+}
+
+// ---------------------------------------------------------------------------------------
+// CUDA-core GEMM with per-output reference order. Block tile 64x64, 256 threads, 4x4 each.
+constexpr int SB = 64, SK = 16;
+
+template <int ORDER>
+__global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtGemm g) {
+    using Acc = typename std::conditional<ORDER == ORDER_F64, double, float>::type;
+    __shared__ float As[SK][SB + 1];
+    __shared__ float Ws[SK][SB + 1];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const int m0 = blockIdx.y * SB, n0 = blockIdx.x * SB;
+    Acc sum[4][4], pan[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { sum[i][j] = 0; pan[i][j] = 0; }
+    const int K = g.K;
+    const bool panels = ORDER == ORDER_PANEL192 && K >= 192;
+    for (int k0 = 0; k0 < K; k0 += SK) {
+        for (int e = threadIdx.x; e < SK * SB; e += 256) {
+            const int kk = e % SK, rr = e / SK;
+            const int m = m0 + rr, n = n0 + rr, k = k0 + kk;
+            float a = (m < g.M && k < K) ? g.A[int64_t(m) * g.lda + k] : 0.f;
+            if (g.round_a_f16) a = __half2float(__float2half_rn(a));
+            As[kk][rr] = a;
+            Ws[kk][rr] = (n < g.N && k < K) ? g.W[int64_t(n) * K + k] : 0.f;
+        }
+        __syncthreads();
+        const int kend = min(SK, K - k0);
+        for (int kk = 0; kk < kend; ++kk) {
+            float a[4], w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) { a[i] = As[kk][ty * 4 + i]; w[i] = Ws[kk][tx * 4 + i]; }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if constexpr (ORDER == ORDER_F64) pan[i][j] = __dadd_rn(pan[i][j], __dmul_rn(double(w[j]), double(a[i])));
+                    else pan[i][j] = __fmaf_rn(w[j], a[i], pan[i][j]);
+                }
+            const int k = k0 + kk + 1;
+            if (panels && (k % 192 == 0 || k == K)) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) { sum[i][j] = sum[i][j] + pan[i][j]; pan[i][j] = 0; }
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + ty * 4 + i;
+        if (m >= g.M) continue;
+        const int64_t orow = g.row_group > 0 ? int64_t(m / g.row_group) * g.row_stride + g.row_offset + m % g.row_group : m;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = n0 + tx * 4 + j;
+            if (n >= g.N) continue;
+            float v = panels ? float(sum[i][j]) : float(pan[i][j]);
+            if (g.bias) v = __fadd_rn(v, g.bias[n]);
+            const int64_t o = orow * g.ldo + n;
+            switch (g.epi) {
+                case SEPI_F32: static_cast<float*>(g.out)[o] = v; break;
+                case SEPI_F16: static_cast<__half*>(g.out)[o] = __float2half_rn(v); break;
+                case SEPI_RESID: static_cast<float*>(g.out)[o] = __fadd_rn(static_cast<float*>(g.out)[o], v); break;
+                case SEPI_SILU_F32: static_cast<float*>(g.out)[o] = ref_silu(v); break;
+                case SEPI_SILU_F16: static_cast<__half*>(g.out)[o] = __float2half_rn(ref_silu(v)); break;
+            }
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t assemble_targets(const float* ctx, const uint8_t* umask, int BV, int T, int kept, int len, int mirrored,
+                             float* rows, int8_t* mask, cudaStream_t s) {
+    assemble_kernel<<<blocks_for(int64_t(BV) * 32), TPB, 0, s>>>(ctx, umask, BV, T, kept, len, mirrored, rows, mask);
+    return cudaGetLastError();
+}
+
+cudaError_t clip_eligibility(const float* ctx, const uint8_t* umask, int BV, int T, int8_t* ok, cudaStream_t s) {
+    clip_ok_kernel<<<blocks_for(int64_t(BV) * 32), TPB, 0, s>>>(ctx, umask, BV, T, ok);
+    return cudaGetLastError();
+}
+
+cudaError_t scale_rows(const RowConfig& c, const float* rows, const int8_t* mask, int R, int W, int anchor_step,
+                       int enc_patches, int kv_words, float* features, float* loc, float* scale, uint32_t* key_valid,
+                       int* first_obs, int ctx_len, float* cap_lo, float* cap_hi, float* cap_scale, cudaStream_t s) {
+    if (R <= 0) return cudaSuccess;
+    scale_kernel<<<blocks_for(R, 64), 64, 0, s>>>(c, rows, mask, R, W, anchor_step, enc_patches, kv_words, features, loc,
+                                                 scale, key_valid, first_obs, ctx_len, cap_lo, cap_hi, cap_scale);
+    return cudaGetLastError();
+}
+
+cudaError_t known_rows(const RowConfig& c, const float* rows, const int8_t* mask, const int8_t* role, int R, int W,
+                       int anchor_step, float* features, float* loc, float* scale, cudaStream_t s) {
+    known_kernel<<<blocks_for(int64_t(R) * 32), TPB, 0, s>>>(c, rows, mask, role, R, W, anchor_step, features, loc, scale);
+    return cudaGetLastError();
+}
+
+cudaError_t positions(const RowConfig& c, const int* first_obs, int R, int group_rows, int N, int S, int cov,
+                      int* rope_row, int* group_begin, int* group_size, int* err, cudaStream_t s) {
+    positions_kernel<<<blocks_for(R), TPB, 0, s>>>(c, first_obs, R, group_rows, N, S, cov, rope_row, group_begin, group_size, err);
+    return cudaGetLastError();
+}
+
+cudaError_t fill_query(const float* query, float* x, int R, int S, int first, int D, cudaStream_t s) {
+    const int64_t n = int64_t(R) * (S - first) * D;
+    if (n <= 0) return cudaSuccess;
+    fill_query_kernel<<<blocks_for(n), TPB, 0, s>>>(query, x, R, S, first, D);
+    return cudaGetLastError();
+}
+
+cudaError_t rms_norm(const float* x, const float* w, int tokens, int D, float eps, void* out, int out_f16, int sub,
+                     int S, int off, cudaStream_t s) {
+    if (tokens <= 0) return cudaSuccess;
+    rms_kernel<<<blocks_for(int64_t(tokens) * 32), TPB, 0, s>>>(x, w, tokens, D, eps, out, out_f16, sub, S, off);
+    return cudaGetLastError();
+}
+
+cudaError_t qkv_scatter(const float* fused, const float* gate, int M, int S, int H, int hd, int rope, const float* cos_tab,
+                        const float* sin_tab, const int* rope_row, float* q, float* k, float* v, float* g, cudaStream_t s) {
+    const int64_t n = int64_t(M) * H * hd;
+    qkv_scatter_kernel<<<blocks_for(n), TPB, 0, s>>>(fused, gate, M, S, H, hd, rope, cos_tab, sin_tab, rope_row, q, k, v, g);
+    return cudaGetLastError();
+}
+
+cudaError_t swiglu(const float* z, int M, int F, float* h, cudaStream_t s) {
+    swiglu_kernel<<<blocks_for(int64_t(M) * F), TPB, 0, s>>>(z, M, F, h);
+    return cudaGetLastError();
+}
+
+cudaError_t add_inplace(float* x, const float* y, int64_t n, cudaStream_t s) {
+    add_kernel<<<blocks_for(n), TPB, 0, s>>>(x, y, n);
+    return cudaGetLastError();
+}
+
+cudaError_t quantile_head(const RowConfig& c, const float* raw, int R, int P_all, int p0, int h, const float* loc,
+                          const float* scale, float* out, float* normalized, int* err, cudaStream_t s) {
+    if (c.Q > 64) return cudaErrorInvalidValue;
+    quantile_kernel<<<blocks_for(int64_t(R) * h * c.ps, 128), 128, 0, s>>>(c, raw, R, P_all, p0, h, loc, scale, out, normalized, err);
+    return cudaGetLastError();
+}
+
+cudaError_t refine(const RowConfig& c, const float* q, const float* rows, const int8_t* mask, int stride, const int8_t* role,
+                   const float* loc0, const float* scale0, int R, int T, int h, double clip, double* scratch, float* out,
+                   cudaStream_t s) {
+    if (c.Q > 64) return cudaErrorInvalidValue;
+    refine_kernel<<<blocks_for(R, 64), 64, 0, s>>>(c, q, rows, mask, stride, role, loc0, scale0, R, T, h, clip, scratch, out);
+    return cudaGetLastError();
+}
+
+cudaError_t finalize(const RowConfig& c, const float* decoded, int Rp, int mirrored, int B, int V, int all, int H,
+                     int Hfull, const float* cap_lo, const float* cap_hi, const float* cap_scale, int cap_on,
+                     const int8_t* clip_ok, float* out, int* err, cudaStream_t s) {
+    const int64_t n = int64_t(B) * V * H * c.Q;
+    finalize_kernel<<<blocks_for(n), TPB, 0, s>>>(c, decoded, Rp, mirrored, B, V, all, H, Hfull, cap_lo, cap_hi, cap_scale,
+                                                 cap_on, clip_ok, out, err);
+    return cudaGetLastError();
+}
+
+cudaError_t feedback(const RowConfig& c, const float* rows, const int8_t* mask, int R, int T, const float* q, int n,
+                     const int8_t* role, const float* future, const int8_t* fmask, int keep, float* next_rows,
+                     int8_t* next_mask, cudaStream_t s) {
+    feedback_kernel<<<blocks_for(int64_t(R) * keep), TPB, 0, s>>>(c, rows, mask, R, T, q, n, role, future, fmask, keep,
+                                                                 next_rows, next_mask);
+    return cudaGetLastError();
+}
+
+cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s) {
+    if (g.M <= 0 || g.N <= 0) return cudaSuccess;
+    dim3 grid((g.N + SB - 1) / SB, (g.M + SB - 1) / SB);
+    if (grid.y > 65535) return cudaErrorInvalidValue;
+    switch (g.order) {
+        case ORDER_PANEL192: simt_gemm_kernel<ORDER_PANEL192><<<grid, 256, 0, s>>>(g); break;
+        case ORDER_CHAIN: simt_gemm_kernel<ORDER_CHAIN><<<grid, 256, 0, s>>>(g); break;
+        default: simt_gemm_kernel<ORDER_F64><<<grid, 256, 0, s>>>(g); break;
+    }
+    return cudaGetLastError();
+}
+
+int read_error(int* d_err, cudaStream_t s) {
+    int h = 0;
+    cudaMemcpyAsync(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost, s);
+    cudaStreamSynchronize(s);
+    if (h) cudaMemsetAsync(d_err, 0, sizeof(int), s);
+    return h;
+}
+
+}  // namespace tsb

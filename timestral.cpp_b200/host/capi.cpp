@@ -1,0 +1,278 @@
+// Flat C ABI (include/timestral_capi.h) and the device-seam entries (include/timestral_b200.h).
+// Error behaviour follows the reference (src/timestral_capi.cpp:8-92): no exception crosses
+// the ABI, load and NULL-handle errors go to a thread-local string, every other error to
+// the handle, and a successful call clears the handle's error. All sizes are validated
+// before any caller buffer is read.
+#include "timestral_capi.h"
+#include "timestral_b200.h"
+
+#include "engine.cuh"
+#include "forecaster.hpp"
+#include "model.hpp"
+
+#include <climits>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <limits>
+#include <memory>
+#include <new>
+#include <string>
+
+#include <cuda_runtime.h>
+
+namespace {
+
+struct ErrorText {
+    std::string text;
+    bool fallback = false;
+    void clear() noexcept { text.clear(); fallback = false; }
+    void set(const char* m) noexcept {
+        try { text = m ? m : "unknown C ABI error"; fallback = false; }
+        catch (...) { fallback = true; }
+    }
+    const char* get() const noexcept { return fallback ? "C ABI error (diagnostic allocation failed)" : text.c_str(); }
+};
+thread_local ErrorText tls_error;
+thread_local int tls_device = -1;
+
+void require(bool ok, const char* msg) { if (!ok) throw ts::Error(msg); }
+void pointer_count(const void* p, int32_t n) {
+    require(n >= 0, "negative covariate count");
+    require((n != 0) == (p != nullptr), "covariate pointer/count mismatch");
+}
+size_t mul(size_t a, size_t b) {
+    if (b && a > std::numeric_limits<size_t>::max() / b) throw ts::Error("C ABI dimensions overflow");
+    return a * b;
+}
+template <class T> size_t count(size_t a, size_t b, size_t c) {
+    const size_t n = mul(mul(a, b), c);
+    mul(n, sizeof(T));
+    return n;
+}
+
+}  // namespace
+
+struct timestral_ctx {
+    ts::Model model;
+    ts::Forecaster forecaster;
+    int threads;
+    ErrorText error;
+    timestral_ctx(ts::Model&& m, int n, int device) : model(std::move(m)), forecaster(model, device), threads(n) {}
+};
+
+namespace {
+ErrorText& error(timestral_ctx* c) noexcept { return c ? c->error : tls_error; }
+void caught(timestral_ctx* c) noexcept {
+    try { throw; }
+    catch (const std::exception& e) { error(c).set(e.what()); }
+    catch (...) { error(c).set("unknown C ABI exception"); }
+}
+}  // namespace
+
+extern "C" {
+
+TIMESTRAL_API int timestral_capi_abi_version(void) { return 1; }
+
+TIMESTRAL_API timestral_ctx* timestral_capi_load(const char* path, int threads) {
+    try {
+        require(path && *path, "model path is required");
+        require(threads >= 1 && threads <= 1024, "invalid CPU thread count");
+        ts::Model model = ts::Model::load(path);
+        int dev = tls_device;
+        if (dev < 0) {
+            int n = 0;
+            if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0 || cudaGetDevice(&dev) != cudaSuccess)
+                throw ts::Error("no CUDA device available");
+        }
+        auto p = std::make_unique<timestral_ctx>(std::move(model), threads, dev);
+        tls_error.clear();
+        return p.release();
+    } catch (...) {
+        caught(nullptr);
+        return nullptr;
+    }
+}
+
+TIMESTRAL_API void timestral_capi_free(timestral_ctx* c) {
+    try { delete c; } catch (...) { caught(nullptr); }
+}
+
+TIMESTRAL_API const char* timestral_capi_last_error(timestral_ctx* c) { return error(c).get(); }
+
+TIMESTRAL_API int timestral_capi_num_quantiles(timestral_ctx* c) {
+    try {
+        require(c, "null handle");
+        const auto n = c->model.config().num_quantiles();
+        require(n <= INT_MAX, "quantile count overflow");
+        c->error.clear();
+        return int(n);
+    } catch (...) {
+        caught(c);
+        return 0;
+    }
+}
+
+TIMESTRAL_API double timestral_capi_quantile_level(timestral_ctx* c, int i) {
+    try {
+        require(c, "null handle");
+        const auto& q = c->model.config().quantile_knots;
+        require(i >= 0 && size_t(i) < q.size(), "quantile index out of range");
+        const double v = q[size_t(i)];
+        c->error.clear();
+        return v;
+    } catch (...) {
+        caught(c);
+        return std::numeric_limits<double>::quiet_NaN();
+    }
+}
+
+TIMESTRAL_API float* timestral_capi_forecast(timestral_ctx* c, const timestral_forecast_request* a, int32_t* out_q) {
+    if (out_q) *out_q = 0;
+    float* result = nullptr;
+    try {
+        require(c, "null handle");
+        require(a, "null request");
+        require(out_q, "out_q is required");
+        require(a->context, "context is required");
+        require(a->B > 0 && a->V > 0 && a->T > 0 && a->prediction_length > 0, "invalid forecast dimensions");
+        require(a->max_context >= 0, "negative max_context");
+        require(a->symmetric_averaging >= -1 && a->symmetric_averaging <= 1 && a->clip_nonnegative >= -1 &&
+                    a->clip_nonnegative <= 1,
+                "invalid forecast flag");
+        pointer_count(a->past_cov, a->c_past);
+        pointer_count(a->known_cov, a->c_known);
+        pointer_count(a->cat_past, a->cc_past);
+        pointer_count(a->cat_known, a->cc_known);
+        const size_t B = size_t(a->B), V = size_t(a->V), T = size_t(a->T), H = size_t(a->prediction_length);
+        require(T <= std::numeric_limits<size_t>::max() - H, "forecast length overflow");
+        const size_t TH = T + H;
+        const size_t nx = count<float>(B, V, T), np = count<float>(B, size_t(a->c_past), T);
+        const size_t nk = count<float>(B, size_t(a->c_known), TH), ncp = count<double>(B, size_t(a->cc_past), T);
+        const size_t nck = count<double>(B, size_t(a->cc_known), TH);
+        const ts::Config& cfg = c->model.config();
+        const size_t Q = cfg.num_quantiles();
+        require(Q <= INT32_MAX, "quantile count overflow");
+        const size_t no = mul(count<float>(B, V, H), Q);
+        mul(no, sizeof(float));
+        const bool any = a->c_past || a->c_known || a->cc_past || a->cc_known;
+        if (any && !cfg.covariate_enabled) throw ts::Error("this checkpoint was not trained with covariates");
+        if ((a->c_known || a->cc_known) && !ts::supports_known_covariates(cfg))
+            throw ts::Error("this checkpoint cannot condition on known-future covariates");
+        if (size_t(a->max_context) > size_t(cfg.context_length)) throw ts::Error("max_context exceeds stored position range");
+        if (a->observation_mask)
+            for (size_t i = 0; i < nx; ++i) require(a->observation_mask[i] <= 1, "observation mask must be boolean");
+        const bool sym = a->symmetric_averaging == -1 ? cfg.symmetric_averaging : a->symmetric_averaging != 0;
+        const bool clip = a->clip_nonnegative == -1 ? cfg.clip_nonnegative : a->clip_nonnegative != 0;
+        result = static_cast<float*>(std::malloc(no * sizeof(float)));
+        if (!result) throw std::bad_alloc();
+        if (!any) {
+            if (sym)
+                for (size_t i = 0; i < Q; ++i)
+                    if (std::abs(cfg.quantile_knots[i] + cfg.quantile_knots[Q - 1 - i] - 1) >= 1e-9)
+                        throw ts::Error("symmetric averaging needs quantile levels symmetric about 0.5");
+            c->forecaster.forecast_targets(a->context, a->observation_mask, B, V, T, H, sym, clip, size_t(a->max_context),
+                                           result);
+        } else {
+            ts::ForecastRequest r;
+            r.batch = B; r.targets = V; r.length = T; r.horizon = H; r.max_context = size_t(a->max_context);
+            r.past_count = size_t(a->c_past); r.known_count = size_t(a->c_known);
+            r.categorical_past_count = size_t(a->cc_past); r.categorical_known_count = size_t(a->cc_known);
+            if (a->observation_mask) r.observation_mask.assign(a->observation_mask, a->observation_mask + nx);
+            r.context.assign(a->context, a->context + nx);
+            if (np) r.past.assign(a->past_cov, a->past_cov + np);
+            if (nk) r.known.assign(a->known_cov, a->known_cov + nk);
+            if (ncp) r.categorical_past.assign(a->cat_past, a->cat_past + ncp);
+            if (nck) r.categorical_known.assign(a->cat_known, a->cat_known + nck);
+            r.symmetric_averaging = sym;
+            r.clip_nonnegative = clip;
+            c->forecaster.forecast_into(r, result);
+        }
+        *out_q = int32_t(Q);
+        c->error.clear();
+        return result;
+    } catch (...) {
+        std::free(result);
+        caught(c);
+        return nullptr;
+    }
+}
+
+TIMESTRAL_API void timestral_capi_free_buffer(void* p) { std::free(p); }
+
+// ---- device seam --------------------------------------------------------------------
+
+TIMESTRAL_API int tsb_set_device(int32_t device) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        tls_error.set("invalid CUDA device");
+        return TSB_ERR_ARG;
+    }
+    tls_device = device;
+    return TSB_OK;
+}
+
+TIMESTRAL_API int tsb_forecast_device(timestral_ctx* c, const float* d_context, const uint8_t* d_mask, int32_t B,
+                                      int32_t V, int32_t T, int32_t H, int32_t symmetric, int32_t clip,
+                                      int32_t max_context, float* d_out, int32_t async) {
+    try {
+        require(c, "null handle");
+        require(d_context && d_out, "device buffers are required");
+        require(B > 0 && V > 0 && T > 0 && H > 0, "invalid forecast dimensions");
+        require(symmetric >= -1 && symmetric <= 1 && clip >= -1 && clip <= 1, "invalid forecast flag");
+        require(max_context >= 0, "negative max_context");
+        const ts::Config& cfg = c->model.config();
+        const bool sym = symmetric == -1 ? cfg.symmetric_averaging : symmetric != 0;
+        const bool cl = clip == -1 ? cfg.clip_nonnegative : clip != 0;
+        const size_t Q = cfg.num_quantiles();
+        if (sym)
+            for (size_t i = 0; i < Q; ++i)
+                if (std::abs(cfg.quantile_knots[i] + cfg.quantile_knots[Q - 1 - i] - 1) >= 1e-9)
+                    throw ts::Error("symmetric averaging needs quantile levels symmetric about 0.5");
+        c->forecaster.engine().forecast_targets(d_context, d_mask, B, V, T, H, sym, cl, max_context, d_out, !async);
+        c->error.clear();
+        return TSB_OK;
+    } catch (const std::exception& e) {
+        error(c).set(e.what());
+        return TSB_ERR_DEVICE;
+    } catch (...) {
+        caught(c);
+        return TSB_ERR_DEVICE;
+    }
+}
+
+TIMESTRAL_API int tsb_sync(timestral_ctx* c) {
+    try {
+        require(c, "null handle");
+        c->forecaster.engine().check_errors();
+        c->error.clear();
+        return TSB_OK;
+    } catch (...) {
+        caught(c);
+        return TSB_ERR_DEVICE;
+    }
+}
+
+TIMESTRAL_API void* tsb_stream(timestral_ctx* c) { return c ? static_cast<void*>(c->forecaster.engine().stream()) : nullptr; }
+
+TIMESTRAL_API int tsb_timing_enable(timestral_ctx* c, int32_t enable) {
+    if (!c) return TSB_ERR_ARG;
+    c->forecaster.engine().timing_enable(enable != 0);
+    return TSB_OK;
+}
+
+TIMESTRAL_API int tsb_timing_read(timestral_ctx* c, const char* cls, double* ms, int64_t* launches) {
+    if (!c || !cls || !ms || !launches) return TSB_ERR_ARG;
+    c->forecaster.engine().timing_read(cls, ms, launches);
+    return TSB_OK;
+}
+
+TIMESTRAL_API void tsb_timing_reset(timestral_ctx* c) {
+    if (c) c->forecaster.engine().timing_reset();
+}
+
+TIMESTRAL_API int64_t tsb_last_launch_count(timestral_ctx* c) { return c ? c->forecaster.engine().last_launches() : 0; }
+
+TIMESTRAL_API int tsb_model_path(timestral_ctx* c) { return c && c->forecaster.engine().tensor_cores() ? 1 : 0; }
+
+}  // extern "C"

@@ -1,0 +1,356 @@
+#include "forecaster.hpp"
+
+#include "engine.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <limits>
+
+#include <cuda_runtime.h>
+
+namespace ts {
+
+namespace {
+
+size_t mul(size_t a, size_t b) {
+    if (b && a > SIZE_MAX / b) throw Error("row dimensions overflow");
+    return a * b;
+}
+size_t add(size_t a, size_t b) {
+    if (a > SIZE_MAX - b) throw Error("row dimensions overflow");
+    return a + b;
+}
+float finite_value(float v) {
+    return std::isnan(v) ? 0.f : std::isinf(v) ? std::copysign(std::numeric_limits<float>::max(), v) : v;
+}
+void codes_valid(const std::vector<double>& x) {
+    for (double v : x)
+        if (std::isinf(v)) throw Error("categorical covariates must hold finite codes or NaN; got an infinite value");
+}
+
+// NumPy pairwise float64 sum (reference src/numpy_sum.hpp:6-14).
+double pairwise_sum(const double* x, size_t n) {
+    if (n < 8) {
+        double r = -0.0;
+        for (size_t i = 0; i < n; ++i) r += x[i];
+        return r;
+    }
+    if (n <= 128) {
+        double r[8];
+        for (size_t j = 0; j < 8; ++j) r[j] = x[j];
+        size_t i = 8;
+        for (; i < n - (n % 8); i += 8)
+            for (size_t j = 0; j < 8; ++j) r[j] += x[i + j];
+        double out = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+        for (; i < n; ++i) out += x[i];
+        return out;
+    }
+    size_t half = n / 2;
+    half -= half % 8;
+    return pairwise_sum(x, half) + pairwise_sum(x + half, n - half);
+}
+
+// Smoothed mean target encoding of one categorical row, float64
+// (reference src/covariates.cpp:14-25).
+void target_encode(const std::vector<double>& target, const std::vector<double>& past, const std::vector<double>& future,
+                   double smooth, std::vector<float>& out_past, std::vector<float>& out_future) {
+    codes_valid(past);
+    codes_valid(future);
+    std::vector<double> cats;
+    for (double x : past) if (std::isfinite(x)) cats.push_back(x);
+    std::sort(cats.begin(), cats.end());
+    cats.erase(std::unique(cats.begin(), cats.end()), cats.end());
+    const size_t nan_slot = cats.size();
+    auto slot = [&](double code) -> size_t {
+        if (std::isnan(code)) return nan_slot;
+        auto it = std::lower_bound(cats.begin(), cats.end(), code);
+        return it != cats.end() && *it == code ? size_t(it - cats.begin()) : nan_slot + 1;
+    };
+    std::vector<double> values(target.size(), 0.0), sums(nan_slot + 1, 0.0), counts(nan_slot + 1, 0.0);
+    double count = 0;
+    for (size_t i = 0; i < target.size(); ++i)
+        if (std::isfinite(target[i])) { values[i] = target[i]; ++count; }
+    const double mean = count ? pairwise_sum(values.data(), values.size()) / count : 0;
+    for (size_t i = 0; i < past.size(); ++i) {
+        const size_t sl = slot(past[i]);
+        sums[sl] += values[i];
+        counts[sl] += std::isfinite(target[i]) ? 1 : 0;
+    }
+    std::vector<double> lookup(nan_slot + 2, mean);
+    for (size_t i = 0; i <= nan_slot; ++i) lookup[i] = (smooth * mean + sums[i]) / (smooth + counts[i]);
+    out_past.clear();
+    out_future.clear();
+    for (double v : past) out_past.push_back(float(lookup[slot(v)]));
+    for (double v : future) out_future.push_back(float(lookup[slot(v)]));
+}
+
+tsb::ModelView make_view(const Model& m) {
+    const Config& c = m.config();
+    tsb::ModelView v;
+    v.ps = int(c.patch_size); v.D = int(c.d_model); v.H = int(c.num_heads); v.F = int(c.mlp_hidden_dim);
+    for (auto k : c.block_schedule)
+        v.schedule.push_back(k == LayerKind::Time ? 0 : k == LayerKind::Variate ? 1 : k == LayerKind::TimeVariate ? 2 : 3);
+    v.knots = c.quantile_knots;
+    v.median = int(c.median_index());
+    v.block_size = int(c.block_size); v.context_length = int(c.context_length);
+    v.rope_dim = int(c.rope_dim); v.pos_min = c.rope_table_pos_min;
+    v.eps = c.norm_eps;
+    v.attn_bias = c.attn_bias; v.mlp_bias = c.mlp_bias;
+    v.time_gate = c.time_gate == Gate::SdpaSigmoid; v.variate_gate = c.variate_gate == Gate::SdpaSigmoid;
+    v.minimum_scale = c.minimum_scale; v.use_asinh = c.use_asinh;
+    v.covariate_enabled = c.covariate_enabled; v.attend_missing = c.attend_missing_patches;
+    v.width_factor = c.quantile_width_factor;
+    v.per_shot = int(c.per_shot_horizon_patches);
+    v.cap_k = c.quantile_real_cap_k; v.extreme = c.extreme_value_threshold;
+    v.symmetric = c.symmetric_averaging; v.clip = c.clip_nonnegative;
+    const Model* mp = &m;
+    v.tensor = [mp](const std::string& n) {
+        const TensorRef& t = mp->tensor(n);
+        tsb::HostTensor h;
+        h.type = int(t.type);
+        h.ne0 = t.ne[0];
+        h.ne1 = t.ne[1] * t.ne[2] * t.ne[3];
+        h.data = t.data;
+        return h;
+    };
+    v.has = [mp](const std::string& n) { return mp->has(n); };
+    return v;
+}
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw Error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+}  // namespace
+
+bool supports_known_covariates(const Config& c) {  // reference src/covariates.cpp:27-31
+    if (!c.covariate_enabled) return false;
+    std::vector<bool> ops;
+    for (auto k : c.block_schedule) for (bool t : layer_axes(k)) ops.push_back(t);
+    for (size_t i = 0; i < ops.size(); ++i) {
+        if (!ops[i]) continue;
+        bool time = false, var = false;
+        for (size_t j = i + 1; j < ops.size(); ++j) { time |= ops[j]; var |= !ops[j]; }
+        if (time && var) return true;
+    }
+    return false;
+}
+
+AssembledRows assemble_rows(const Config& c, const std::vector<float>& context, const std::vector<int8_t>& user,
+                            size_t B, size_t V, size_t T, size_t H, const std::vector<float>& past, size_t P,
+                            const std::vector<float>& known, size_t K, size_t cap, const std::vector<double>& cp, size_t CP,
+                            const std::vector<double>& ck, size_t CK) {
+    if (!B || !V || !T || !H || !c.patch_size || !c.context_length) throw Error("invalid row dimensions");
+    const size_t TH = add(T, H), BV = mul(B, V);
+    if (context.size() != mul(BV, T) || (!user.empty() && user.size() != context.size()) || past.size() != mul(mul(B, P), T) ||
+        known.size() != mul(mul(B, K), TH) || cp.size() != mul(mul(B, CP), T) || ck.size() != mul(mul(B, CK), TH))
+        throw Error("row input shape mismatch");
+    for (auto v : user) if (v != 0 && v != 1) throw Error("observation mask must be boolean");
+    if ((P || K || CP || CK) && !c.covariate_enabled) throw Error("this checkpoint was not trained with covariates");
+    if ((K || CK) && !supports_known_covariates(c)) throw Error("this checkpoint cannot condition on known-future covariates");
+    codes_valid(cp);
+    codes_valid(ck);
+    cap = cap ? cap : c.context_length;
+    if (cap > c.context_length) throw Error("max_context exceeds stored position range");
+    const size_t kept = std::min(T, cap), ps = c.patch_size, pad = (ps - kept % ps) % ps, len = add(kept, pad);
+    const size_t hor = mul(add(H, ps - 1) / ps, ps);
+    const size_t all = add(add(V, add(P, CP)), add(K, CK)), R = mul(B, all);
+    AssembledRows a;
+    a.rows_count = R; a.length = len; a.horizon = hor;
+    a.rows.assign(mul(R, len), 0.f);
+    a.mask.assign(a.rows.size(), 0);
+    a.groups.resize(R);
+    if (P || CP || K || CK) a.roles.resize(R);
+    if (K || CK) { a.future.assign(mul(R, hor), 0.f); a.future_mask.assign(a.future.size(), 0); }
+    // Targets: observed = finite and not masked out; forward fill from the first observation.
+    std::vector<float> filled(context.size());
+    std::vector<int8_t> obs(context.size());
+    for (size_t r = 0; r < BV; ++r) {
+        float prev = 0;
+        for (size_t t = 0; t < T; ++t) {
+            const size_t i = r * T + t;
+            obs[i] = std::isfinite(context[i]) && (user.empty() || user[i]);
+            if (obs[i]) prev = context[i];
+            filled[i] = prev;
+        }
+    }
+    auto encode = [&](const std::vector<double>& codes, size_t C, size_t width) {
+        std::vector<float> out(codes.size());
+        std::vector<float> ep, ef;
+        for (size_t b = 0; b < B; ++b)
+            for (size_t j = 0; j < C; ++j) {
+                const size_t off = (b * C + j) * width;
+                if (V != 1) {
+                    for (size_t t = 0; t < width; ++t) out[off + t] = float(codes[off + t]);
+                    continue;
+                }
+                std::vector<double> target(T);
+                bool started = false;
+                for (size_t t = 0; t < T; ++t) {
+                    started |= obs[b * T + t] != 0;
+                    target[t] = started && t >= T - kept ? double(filled[b * T + t]) : std::nan("");
+                }
+                std::vector<double> p(codes.begin() + off, codes.begin() + off + T);
+                std::vector<double> f(codes.begin() + off + T, codes.begin() + off + width);
+                target_encode(target, p, f, c.target_encoding_smooth, ep, ef);
+                for (size_t t = 0; t < T; ++t) out[off + t] = std::isnan(target[t]) && std::isnan(p[t]) ? NAN : ep[t];
+                std::copy(ef.begin(), ef.end(), out.begin() + off + T);
+            }
+        return out;
+    };
+    const auto enc_p = encode(cp, CP, T), enc_k = encode(ck, CK, TH);
+    for (size_t b = 0; b < B; ++b)
+        for (size_t j = 0; j < all; ++j) {
+            const size_t r = b * all + j;
+            const int role = j < V ? 0 : j < V + P + CP ? 1 : 2;
+            a.groups[r] = int64_t(b);
+            if (!a.roles.empty()) a.roles[r] = role;
+            const std::vector<float>* src;
+            size_t off;
+            if (j < V) { src = &filled; off = (b * V + j) * T; }
+            else if (j < V + P) { src = &past; off = (b * P + j - V) * T; }
+            else if (j < V + P + CP) { src = &enc_p; off = (b * CP + j - V - P) * T; }
+            else if (j < V + P + CP + K) { src = &known; off = (b * K + j - V - P - CP) * TH; }
+            else { src = &enc_k; off = (b * CK + j - V - P - CP - K) * TH; }
+            for (size_t t = 0; t < kept; ++t) {
+                const size_t from = off + T - kept + t, to = r * len + pad + t;
+                const float v = (*src)[from];
+                a.rows[to] = role ? finite_value(v) : v;
+                a.mask[to] = role ? !std::isnan(v) : obs[(b * V + j) * T + T - kept + t];
+            }
+            if (role == 2)
+                for (size_t t = 0; t < H; ++t) {
+                    const float v = (*src)[off + T + t];
+                    a.future[r * hor + t] = finite_value(v);
+                    a.future_mask[r * hor + t] = !std::isnan(v);
+                }
+        }
+    return a;
+}
+
+struct Forecaster::Staging {
+    void* ctx = nullptr; size_t ctx_bytes = 0;
+    void* mask = nullptr; size_t mask_bytes = 0;
+    void* out = nullptr; size_t out_bytes = 0;
+    static void grow(void*& p, size_t& have, size_t need) {
+        if (need <= have) return;
+        if (p) cudaFree(p);
+        p = nullptr;
+        have = 0;
+        cuda_check(cudaMalloc(&p, need), "cudaMalloc staging");
+        have = need;
+    }
+    ~Staging() {
+        if (ctx) cudaFree(ctx);
+        if (mask) cudaFree(mask);
+        if (out) cudaFree(out);
+    }
+};
+
+Forecaster::Forecaster(const Model& model, int device) : model_(model), staging_(new Staging) {
+    int dev = device;
+    if (dev < 0) cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+    try {
+        engine_ = std::make_unique<tsb::Engine>(make_view(model), dev);
+    } catch (const std::exception& e) {
+        throw Error(e.what());
+    }
+}
+
+Forecaster::~Forecaster() {
+    if (engine_) cudaSetDevice(engine_->device());
+    staging_.reset();
+}
+
+void Forecaster::forecast_targets(const float* context, const uint8_t* mask, size_t B, size_t V, size_t T, size_t H,
+                                  bool sym, bool clip, size_t max_context, float* out) {
+    const Config& c = model_.config();
+    const size_t Q = c.num_quantiles();
+    const size_t cap = max_context ? max_context : c.context_length;
+    if (cap > c.context_length) throw Error("max_context exceeds stored position range");
+    if (T > size_t(INT32_MAX) || H > size_t(INT32_MAX) || mul(B, V) > size_t(INT32_MAX))
+        throw Error("forecast dimensions exceed the device path limits");
+    tsb::Engine& eng = *engine_;
+    cuda_check(cudaSetDevice(eng.device()), "cudaSetDevice");
+    const size_t BV = mul(B, V), n = mul(BV, T), no = mul(mul(BV, H), Q);
+    Staging& st = *staging_;
+    Staging::grow(st.ctx, st.ctx_bytes, n * 4);
+    if (mask) Staging::grow(st.mask, st.mask_bytes, n);
+    Staging::grow(st.out, st.out_bytes, no * 4);
+    cudaStream_t s = eng.stream();
+    cuda_check(cudaMemcpyAsync(st.ctx, context, n * 4, cudaMemcpyHostToDevice, s), "upload context");
+    if (mask) cuda_check(cudaMemcpyAsync(st.mask, mask, n, cudaMemcpyHostToDevice, s), "upload mask");
+    try {
+        eng.forecast_targets(static_cast<float*>(st.ctx), mask ? static_cast<uint8_t*>(st.mask) : nullptr, int(B), int(V),
+                             int(T), int(H), sym, clip, int(max_context), static_cast<float*>(st.out), false);
+        cuda_check(cudaMemcpyAsync(out, st.out, no * 4, cudaMemcpyDeviceToHost, s), "download forecast");
+        eng.check_errors();
+    } catch (const Error&) {
+        throw;
+    } catch (const std::exception& e) {
+        throw Error(e.what());
+    }
+}
+
+Forecast Forecaster::forecast(const ForecastRequest& r) {
+    const Config& c = model_.config();
+    Forecast f;
+    f.batch = r.batch; f.targets = r.targets; f.horizon = r.horizon;
+    f.quantile_levels = c.quantile_knots;
+    f.quantiles.resize(mul(mul(mul(r.batch, r.targets), r.horizon), c.num_quantiles()));
+    forecast_into(r, f.quantiles.data());
+    return f;
+}
+
+void Forecaster::forecast_into(const ForecastRequest& r, float* out) {
+    const Config& c = model_.config();
+    const size_t Q = c.num_quantiles();
+    const bool sym = r.symmetric_averaging.value_or(c.symmetric_averaging);
+    const bool clip = r.clip_nonnegative.value_or(c.clip_nonnegative);
+    if (r.quantile_real_cap_k && *r.quantile_real_cap_k != c.quantile_real_cap_k)
+        throw Error("quantile_real_cap_k overrides are not supported by the device path");
+    if (r.per_shot_horizon_patches && r.per_shot_horizon_patches != c.per_shot_horizon_patches)
+        throw Error("per_shot_horizon_patches overrides are not supported by the device path");
+    if (!r.batch || !r.targets || !r.length || !r.horizon) throw Error("invalid row dimensions");
+    if (sym)
+        for (size_t i = 0; i < Q; ++i)
+            if (std::abs(c.quantile_knots[i] + c.quantile_knots[Q - 1 - i] - 1) >= 1e-9)
+                throw Error("symmetric averaging needs quantile levels symmetric about 0.5");
+    if (r.length > size_t(INT32_MAX) || r.horizon > size_t(INT32_MAX) || r.batch * r.targets > size_t(INT32_MAX))
+        throw Error("forecast dimensions exceed the device path limits");
+    const bool any_cov = r.past_count || r.known_count || r.categorical_past_count || r.categorical_known_count;
+    tsb::Engine& eng = *engine_;
+    cuda_check(cudaSetDevice(eng.device()), "cudaSetDevice");
+    if (!any_cov) {
+        const size_t n = mul(mul(r.batch, r.targets), r.length);
+        if (r.context.size() != n || (!r.observation_mask.empty() && r.observation_mask.size() != n))
+            throw Error("row input shape mismatch");
+        for (auto v : r.observation_mask) if (v != 0 && v != 1) throw Error("observation mask must be boolean");
+        forecast_targets(r.context.data(),
+                         r.observation_mask.empty() ? nullptr : reinterpret_cast<const uint8_t*>(r.observation_mask.data()),
+                         r.batch, r.targets, r.length, r.horizon, sym, clip, r.max_context, out);
+        return;
+    }
+    const AssembledRows a = assemble_rows(c, r.context, r.observation_mask, r.batch, r.targets, r.length, r.horizon, r.past,
+                                          r.past_count, r.known, r.known_count, r.max_context, r.categorical_past,
+                                          r.categorical_past_count, r.categorical_known, r.categorical_known_count);
+    tsb::HostRows h;
+    h.R = int(a.rows_count); h.T = int(a.length); h.Hh = int(a.horizon);
+    h.rows = a.rows.data(); h.mask = a.mask.data();
+    h.roles = a.roles.empty() ? nullptr : a.roles.data();
+    h.future = a.future.empty() ? nullptr : a.future.data();
+    h.future_mask = a.future_mask.empty() ? nullptr : a.future_mask.data();
+    h.group_rows = int(a.rows_count / r.batch);
+    std::vector<uint8_t> um(r.observation_mask.begin(), r.observation_mask.end());
+    try {
+        eng.forecast_rows(h, int(r.batch), int(r.targets), int(r.horizon), sym, clip, r.context.data(),
+                          um.empty() ? nullptr : um.data(), int(r.length), out);
+    } catch (const Error&) {
+        throw;
+    } catch (const std::exception& e) {
+        throw Error(e.what());
+    }
+}
+
+}  // namespace ts

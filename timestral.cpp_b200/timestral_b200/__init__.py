@@ -49,6 +49,7 @@ SIGNATURES = {
     "timestral_capi_free_buffer": (None, [C.c_void_p]),
     "tsb_forecast_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                       C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32]),
+    "tsb_sync": (C.c_int, [C.c_void_p]),
     "tsb_set_device": (C.c_int, [C.c_int32]),
     "tsb_stream": (C.c_void_p, [C.c_void_p]),
     "tsb_timing_enable": (C.c_int, [C.c_void_p, C.c_int32]),
