@@ -1159,6 +1159,29 @@ int oracle_block_frames(const oracle_config* c, const float* x, const int8_t* ma
     return guarded([&] { block_frames(*c, x, mask, median, rows, length, patches, loc, scale); });
 }
 
+int oracle_head_linear_f64(const float* w, const float* x, int64_t K, int64_t N, int64_t rows, float* y) {
+    return guarded([&] { g_threads = 1; head_linear_f64(w, x, K, N, rows, y); });
+}
+
+int oracle_sigmoid(const float* x, int64_t n, float* out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = 1.0f / (1.0f + activation_exp(-x[i]));
+    return 0;
+}
+
+int oracle_assemble_rows(const oracle_config* c, const oracle_request* r, int64_t* R, int64_t* len, int64_t* hor,
+                         float* rows, int8_t* mask, int64_t* groups, int64_t* roles, float* future, int8_t* future_mask) {
+    return guarded([&] {
+        auto a = assemble_rows(*c, *r);
+        *R = int64_t(a.rows_count); *len = int64_t(a.length); *hor = int64_t(a.horizon);
+        if (rows) std::memcpy(rows, a.rows.data(), a.rows.size() * 4);
+        if (mask) std::memcpy(mask, a.mask.data(), a.mask.size());
+        if (groups) std::memcpy(groups, a.groups.data(), a.groups.size() * 8);
+        if (roles && !a.roles.empty()) std::memcpy(roles, a.roles.data(), a.roles.size() * 8);
+        if (future && !a.future.empty()) std::memcpy(future, a.future.data(), a.future.size() * 4);
+        if (future_mask && !a.future_mask.empty()) std::memcpy(future_mask, a.future_mask.data(), a.future_mask.size());
+    });
+}
+
 float oracle_activation_exp(float x) { return activation_exp(x); }
 float oracle_attention_exp(float x) { return attention_exp(x); }
 double oracle_numpy_sum(const double* x, int64_t n) { return numpy_sum(x, n); }

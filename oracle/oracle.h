@@ -97,6 +97,11 @@ int oracle_refine_block(const oracle_config* c, const float* q, const float* x, 
 int oracle_block_frames(const oracle_config* c, const float* x, const int8_t* mask,
                         const double* median, int64_t rows, int64_t length, int64_t patches,
                         double* loc, double* scale);
+int oracle_head_linear_f64(const float* w, const float* x, int64_t K, int64_t N, int64_t rows, float* y);
+int oracle_sigmoid(const float* x, int64_t n, float* out);
+/* Row assembly (reference src/covariates.cpp:32-72); outputs sized by the caller. */
+int oracle_assemble_rows(const oracle_config* c, const oracle_request* r, int64_t* R, int64_t* len, int64_t* hor,
+                         float* rows, int8_t* mask, int64_t* groups, int64_t* roles, float* future, int8_t* future_mask);
 float oracle_activation_exp(float x);
 float oracle_attention_exp(float x);
 double oracle_numpy_sum(const double* x, int64_t n);
