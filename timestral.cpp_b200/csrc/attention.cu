@@ -36,6 +36,49 @@ __device__ __forceinline__ bool time_allowed(const MaskMeta& mm, int r, int q, i
     return q == k || (k <= q && qa && kp >= mm.L && anchor_of(mm, qp) == anchor_of(mm, kp));
 }
 
+// Bits [lo, hi] of a 128-bit set that fall in 32-bit word w.
+__device__ __forceinline__ uint32_t bits_in(int w, int lo, int hi) {
+    const int a = max(lo, w * 32), b = min(hi, w * 32 + 31);
+    if (a > b) return 0u;
+    const int la = a - w * 32, lb = b - w * 32;
+    const uint32_t upper = lb == 31 ? 0xffffffffu : ((1u << (lb + 1)) - 1u);
+    return upper & ~((1u << la) - 1u);
+}
+
+// The set of keys (bit k) that query q of row r attends on the time axis, for S <= 128:
+// time_allowed() restricted to the keys the reference computes (the encoder split),
+// built with word operations from the row's key-valid bits.
+__device__ __forceinline__ void key_set(const MaskMeta& mm, int r, int q, bool live, uint32_t (&m)[4]) {
+    uint32_t kv[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        kv[w] = w < mm.kv_words ? mm.key_valid[int64_t(r) * mm.kv_words + w] : 0u;
+        m[w] = 0u;
+    }
+    if (!live) return;
+    const int N = mm.N;
+    if (q < N) {
+        const bool full = mm.cov && mm.role[r] == 2;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) m[w] = (full ? kv[w] : (kv[w] & bits_in(w, 0, q))) | bits_in(w, q, q);
+        return;
+    }
+    if (!mm.cov) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) m[w] = kv[w] | bits_in(w, N, q);
+        return;
+    }
+    const int qp = q - N;
+    if (qp < mm.L) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) m[w] = bits_in(w, q, q);
+        return;
+    }
+    const int a = anchor_of(mm, qp);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) m[w] = (kv[w] & bits_in(w, 0, a - 1)) | bits_in(w, N + a, q);
+}
+
 // Keys the reference computes for query t: the encoder split (src/layers.cpp:591).
 __device__ __forceinline__ int time_keys(const MaskMeta& mm, int t) { return t < mm.N ? mm.N : mm.S; }
 
@@ -91,7 +134,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 
 template <int NK>
-__global__ void __launch_bounds__(AT_THREADS)
+__global__ void __launch_bounds__(AT_THREADS, 2)
     attn_time_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const __half* __restrict__ gate,
                         __half* __restrict__ out, int rows, int H, const MaskMeta mm, int* err) {
@@ -162,56 +205,52 @@ __global__ void __launch_bounds__(AT_THREADS)
     } else {
         const int t = threadIdx.x;  // query row == TMEM lane
         const uint32_t lane_base = uint32_t(warp * 32) << 16;
-        constexpr float kLog2e = 1.4426950408889634f;
+        // logit scale 1/sqrt(64) folded with log2(e) for exp2
+        constexpr float kScaleLog2e = 0.125f * 1.4426950408889634f;
         int i = 0;
         for (int prob = blockIdx.x; prob < num; prob += gridDim.x, ++i) {
             const int r = prob / H, h = prob % H;
+            const bool live = t < S;
+            uint32_t allowed[4];
+            key_set(mm, r, t, live, allowed);
+            // gate row of this query, fetched while the score MMA runs
+            uint4 gv[8];
+            const __half* g = (gate && live) ? gate + ((int64_t(r) * H + h) * S + t) * 64 : nullptr;
+            if (g) {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) gv[c] = *reinterpret_cast<const uint4*>(g + c * 8);
+            }
             if (!at_wait(&bars->s_full, i & 1, abort, err)) break;
             tc_fence_after();
-            const bool live = t < S;
-            const int keys = live ? time_keys(mm, t) : 0;
-            // Pass 1: masked maximum of the scaled logits.
+            uint32_t sc[NK];
+#pragma unroll
+            for (int c = 0; c < NK / 16; ++c)
+                tmem_ld16(tS + lane_base + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&sc[c * 16]));
+            tmem_ld_wait();
             float mx = -INFINITY;
-            uint32_t rr[16];
 #pragma unroll
-            for (int c = 0; c < NK / 16; ++c) {
-                tmem_ld16(tS + lane_base + c * 16, rr);
-                tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int key = c * 16 + j;
-                    if (key < keys && time_allowed(mm, r, t, key)) mx = fmaxf(mx, __uint_as_float(rr[j]) * 0.125f);
-                }
-            }
-            // Pass 2: probabilities (f16), their sum, and the P tile in the 128-byte swizzle.
+            for (int k = 0; k < NK; ++k)
+                if ((allowed[k >> 5] >> (k & 31)) & 1u) mx = fmaxf(mx, __uint_as_float(sc[k]));
+            // probabilities in f16, their sum, and the P tile in the 128-byte swizzle
+            const float off = mx * kScaleLog2e;
             float sum = 0.f;
-            const float off = mx * kLog2e;
 #pragma unroll
-            for (int c = 0; c < NK / 16; ++c) {
-                tmem_ld16(tS + lane_base + c * 16, rr);
-                tmem_ld_wait();
-                float p[16];
+            for (int k0 = 0; k0 < NK; k0 += 8) {
+                float p[8];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int key = c * 16 + j;
-                    float pj = 0.f;
-                    if (key < keys && time_allowed(mm, r, t, key))
-                        pj = exp2f(__fmaf_rn(__uint_as_float(rr[j]) * 0.125f, kLog2e, -off));
-                    const __half hp = __float2half_rn(pj);
-                    sum += __half2float(hp);
-                    p[j] = pj;
+                for (int j = 0; j < 8; ++j) {
+                    const int k = k0 + j;
+                    const bool on = (allowed[k >> 5] >> (k & 31)) & 1u;
+                    p[j] = on ? exp2f(__fmaf_rn(__uint_as_float(sc[k]), kScaleLog2e, -off)) : 0.f;
                 }
+                uint4 u;
+                u.x = pack_half2(p[0], p[1]); u.y = pack_half2(p[2], p[3]);
+                u.z = pack_half2(p[4], p[5]); u.w = pack_half2(p[6], p[7]);
+                const __half2* hp = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-                for (int half8 = 0; half8 < 2; ++half8) {
-                    const int k0 = c * 16 + half8 * 8;
-                    const int blk = k0 / 64, chunk = (k0 % 64) / 8;
-                    uint4 u;
-                    u.x = pack_half2(p[half8 * 8 + 0], p[half8 * 8 + 1]);
-                    u.y = pack_half2(p[half8 * 8 + 2], p[half8 * 8 + 3]);
-                    u.z = pack_half2(p[half8 * 8 + 4], p[half8 * 8 + 5]);
-                    u.w = pack_half2(p[half8 * 8 + 6], p[half8 * 8 + 7]);
-                    *reinterpret_cast<uint4*>(pbuf + blk * 16384 + t * 128 + ((chunk ^ (t & 7)) << 4)) = u;
-                }
+                for (int j = 0; j < 4; ++j) { const float2 f = __half22float2(hp[j]); sum += f.x + f.y; }
+                const int blk = k0 / 64, chunk = (k0 % 64) / 8;
+                *reinterpret_cast<uint4*>(pbuf + blk * 16384 + t * 128 + ((chunk ^ (t & 7)) << 4)) = u;
             }
             fence_proxy_async();
             tc_fence_before();
@@ -219,26 +258,21 @@ __global__ void __launch_bounds__(AT_THREADS)
             if (lane == 0) mbar_arrive(&bars->p_ready);
             if (!at_wait(&bars->o_full, i & 1, abort, err)) break;
             tc_fence_after();
-            uint32_t o0[32], o1[32];
-            tmem_ld32(tO + lane_base, o0);
-            tmem_ld32(tO + lane_base + 32, o1);
-            tmem_ld_wait();
-            if (live) {
-                const float inv = 1.0f / sum;
-                const int64_t tok = int64_t(r) * S + t;
-                const __half* g = gate ? gate + ((int64_t(r) * H + h) * S + t) * 64 : nullptr;
-                __half* dst = out + tok * D + h * 64;
+            const float inv = live ? 1.0f / sum : 0.f;
+            __half* dst = out + (int64_t(r) * S + t) * D + h * 64;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+            for (int half32 = 0; half32 < 2; ++half32) {
+                uint32_t o[32];
+                tmem_ld32(tO + lane_base + half32 * 32, o);
+                tmem_ld_wait();
+                if (!live) continue;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
                     float y[8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int d = c * 8 + j;
-                        y[j] = __uint_as_float(d < 32 ? o0[d] : o1[d - 32]) * inv;
-                    }
+                    for (int j = 0; j < 8; ++j) y[j] = __uint_as_float(o[c * 8 + j]) * inv;
                     if (g) {
-                        const uint4 gv = *reinterpret_cast<const uint4*>(g + c * 8);
-                        const __half2* gh = reinterpret_cast<const __half2*>(&gv);
+                        const __half2* gh = reinterpret_cast<const __half2*>(&gv[half32 * 4 + c]);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
                             const float2 f = __half22float2(gh[j]);
@@ -249,7 +283,7 @@ __global__ void __launch_bounds__(AT_THREADS)
                     uint4 u;
                     u.x = pack_half2(y[0], y[1]); u.y = pack_half2(y[2], y[3]);
                     u.z = pack_half2(y[4], y[5]); u.w = pack_half2(y[6], y[7]);
-                    *reinterpret_cast<uint4*>(dst + c * 8) = u;
+                    *reinterpret_cast<uint4*>(dst + half32 * 32 + c * 8) = u;
                 }
             }
         }

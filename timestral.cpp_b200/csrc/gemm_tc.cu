@@ -6,9 +6,10 @@
 // accumulate F16 products in F32 — the same arithmetic as kind::f16 with f32 accumulators.
 //
 // Tile 128 x BN x 64 (f16, 128-byte swizzle), STAGES-deep TMA ring, two TMEM accumulators
-// so the epilogue of tile i overlaps the MMAs of tile i+1. Warp roles (192 threads):
+// so the epilogue of tile i overlaps the MMAs of tile i+1. Warp roles (320 threads):
 //   warp 0: TMA producer (one lane)      warp 1: TMEM owner + MMA issuer (one lane)
-//   warps 2..5: epilogue, one accumulator row per thread (TMEM lane quarter = warp % 4).
+//   warps 2..9: epilogue, one accumulator row per thread (TMEM lane quarter = warp % 4),
+//   warps 2..5 take the first half of the tile's columns and warps 6..9 the second.
 // Every mbarrier wait is bounded; a timeout records a device error and unwinds.
 #include "common.cuh"
 #include "gemm_tc.cuh"
@@ -28,7 +29,8 @@ constexpr int A_BYTES = BM * BK * 2;          // 16 KB
 constexpr int B_BYTES = BN * BK * 2;          // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;             // 512: two accumulators
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;                 // two warps per TMEM lane quarter, one per column half
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
 struct Smem {
@@ -81,40 +83,57 @@ __device__ __forceinline__ void store_f16x32(__half* dst, const float* v, int va
     }
 }
 
-// Epilogue of one 128 x BN accumulator: thread owns row `m` and reads its columns.
+// Activations of the tensor-core path. Their results are rounded to f16 for the next
+// GEMM, so they use the hardware exp2 and approximate divide (a few ulp in f32, far below
+// the f16 rounding) instead of the reference's exact float sequence used on the F32 path.
+__device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float fast_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// Epilogue of columns [half*BN/2, (half+1)*BN/2) of one 128 x BN accumulator: the thread owns
+// accumulator row `row_in_tile` (its TMEM lane).
 template <int KIND>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, int m0, int n0, int row_in_tile) {
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, int m0, int n0, int row_in_tile, int half) {
     const GemmEpilogue& e = g.epi;
     const int m = m0 + row_in_tile;
     const bool row_ok = m < g.M;
-    float v[64];
     uint32_t r[32];
     if constexpr (KIND == EPI_SWIGLU || KIND == EPI_VGATE) {
-        // First half of the tile holds the first operand, second half the second.
-        for (int c = 0; c < BN / 64; ++c) {
+        // The first half of the tile holds the first operand, the second half the second.
+        float a[32];
+        for (int c = half * (BN / 128); c < (half + 1) * (BN / 128); ++c) {
             tmem_ld32(tacc + c * 32, r);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            for (int i = 0; i < 32; ++i) a[i] = __uint_as_float(r[i]);
             tmem_ld32(tacc + BN / 2 + c * 32, r);
             tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
             if (!row_ok) continue;
             const int wn = n0 + c * 32;             // weight row of the first operand column 0
             const int on = n0 / 2 + c * 32;         // output column
             float o[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-                float a = v[i], b = v[32 + i];
-                if (e.bias) { a = __fadd_rn(a, e.bias[wn + i]); b = __fadd_rn(b, e.bias[wn + BN / 2 + i]); }
-                o[i] = KIND == EPI_SWIGLU ? __fmul_rn(a, ref_silu(b)) : __fmul_rn(a, ref_sigmoid(b));
+                float x = a[i], y = __uint_as_float(r[i]);
+                if (e.bias) { x = __fadd_rn(x, e.bias[wn + i]); y = __fadd_rn(y, e.bias[wn + BN / 2 + i]); }
+                o[i] = KIND == EPI_SWIGLU ? __fmul_rn(x, fast_silu(y)) : __fmul_rn(x, fast_sigmoid(y));
             }
-            __half* dst = static_cast<__half*>(e.out) + out_row(e, m) * e.ldo + on;
-            store_f16x32(dst, o, 32);
+            store_f16x32(static_cast<__half*>(e.out) + out_row(e, m) * e.ldo + on, o, 32);
         }
     } else if constexpr (KIND == EPI_QKVG) {
-        for (int c = 0; c < BN / 64; ++c) {
+        float v[64];
+        for (int c = half * (BN / 128); c < (half + 1) * (BN / 128); ++c) {
+            const int col = n0 + c * 64;
+            const int which = col / e.D, h = (col % e.D) >> 6;
+            const bool rope = row_ok && col < g.N && which < 2 && e.rope;
+            // RoPE table entries of this token's position, requested before the TMEM reads.
+            float4 tc[8], ts[8];
+            const bool rope16 = rope && e.rope_half <= 16;
+            if (rope16) {
+                const float4* ct = reinterpret_cast<const float4*>(e.cos_tab + int64_t(e.rope_row[m]) * 64);
+                const float4* st = reinterpret_cast<const float4*>(e.sin_tab + int64_t(e.rope_row[m]) * 64);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) { tc[j] = ct[j]; tc[4 + j] = ct[8 + j]; ts[j] = st[j]; ts[4 + j] = st[8 + j]; }
+            }
             tmem_ld32(tacc + c * 64, r);
             tmem_ld_wait();
 #pragma unroll
@@ -123,32 +142,39 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
-            const int col = n0 + c * 64;
             if (!row_ok || col >= g.N) continue;
             if (e.bias) {
 #pragma unroll
                 for (int i = 0; i < 64; ++i) v[i] = __fadd_rn(v[i], e.bias[col + i]);
             }
-            const int which = col / e.D, h = (col % e.D) >> 6;
-            if (which < 2 && e.rope) {
+            if (rope) {
                 // x*cos + rotate_half(x)*sin with separately rounded products and sum
                 // (reference src/layers.cpp:238-246). Dims whose inverse frequency is zero
                 // have cos 1 and sin 0 in every table row and are left unchanged.
-                const float* ct = e.cos_tab + int64_t(e.rope_row[m]) * 64;
-                const float* st = e.sin_tab + int64_t(e.rope_row[m]) * 64;
-                float o[64];
+                if (rope16) {
+                    const float* c0 = reinterpret_cast<const float*>(tc);       // dims 0..15
+                    const float* c1 = reinterpret_cast<const float*>(tc + 4);   // dims 32..47
+                    const float* s0 = reinterpret_cast<const float*>(ts);
+                    const float* s1 = reinterpret_cast<const float*>(ts + 4);
 #pragma unroll
-                for (int i = 0; i < 64; ++i) o[i] = v[i];
-                for (int i = 0; i < e.rope_half; ++i) {
-                    const float x0 = v[i], x1 = v[i + 32];
-                    o[i] = __fadd_rn(__fmul_rn(x0, ct[i]), __fmul_rn(-x1, st[i]));
-                    o[i + 32] = __fadd_rn(__fmul_rn(x1, ct[i + 32]), __fmul_rn(x0, st[i + 32]));
+                    for (int i = 0; i < 16; ++i) {
+                        if (i >= e.rope_half) break;
+                        const float x0 = v[i], x1 = v[i + 32];
+                        v[i] = __fadd_rn(__fmul_rn(x0, c0[i]), __fmul_rn(-x1, s0[i]));
+                        v[i + 32] = __fadd_rn(__fmul_rn(x1, c1[i]), __fmul_rn(x0, s1[i]));
+                    }
+                } else {
+                    const float* ct = e.cos_tab + int64_t(e.rope_row[m]) * 64;
+                    const float* st = e.sin_tab + int64_t(e.rope_row[m]) * 64;
+                    for (int i = 0; i < e.rope_half; ++i) {
+                        const float x0 = v[i], x1 = v[i + 32];
+                        v[i] = __fadd_rn(__fmul_rn(x0, ct[i]), __fmul_rn(-x1, st[i]));
+                        v[i + 32] = __fadd_rn(__fmul_rn(x1, ct[i + 32]), __fmul_rn(x0, st[i + 32]));
+                    }
                 }
-#pragma unroll
-                for (int i = 0; i < 64; ++i) v[i] = o[i];
             } else if (which == 3) {
 #pragma unroll
-                for (int i = 0; i < 64; ++i) v[i] = ref_sigmoid(v[i]);
+                for (int i = 0; i < 64; ++i) v[i] = fast_sigmoid(v[i]);
             }
             const int rr = m / e.S, s = m % e.S;
             __half* dst = e.qkvg[which] + ((int64_t(rr) * e.H + h) * e.S + s) * 64;
@@ -156,7 +182,27 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
             store_f16x32(dst + 32, v + 32, 32);
         }
     } else {
-        for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        const int c0 = half * (BN / 64), c1 = (half + 1) * (BN / 64);
+        const int64_t orow = row_ok ? out_row(e, m) : 0;
+        // Residual rows of the next chunk are requested while the current chunk is stored.
+        float4 rnext[8];
+        auto load_resid = [&](int c, float4 (&dst)[8]) {
+            const int col = n0 + c * 32;
+            if (KIND == EPI_RESID && row_ok && col + 32 <= g.N) {
+                const float4* rs = reinterpret_cast<const float4*>(e.resid + orow * e.ldo + col);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) dst[j] = rs[j];
+            }
+        };
+        if (KIND == EPI_RESID) load_resid(c0, rnext);
+        for (int c = c0; c < c1; ++c) {
+            float4 rcur[8];
+            if (KIND == EPI_RESID) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) rcur[j] = rnext[j];
+                if (c + 1 < c1) load_resid(c + 1, rnext);
+            }
             tmem_ld32(tacc + c * 32, r);
             tmem_ld_wait();
             const int col = n0 + c * 32;
@@ -167,25 +213,22 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
             if (e.bias) {
                 for (int i = 0; i < valid; ++i) v[i] = __fadd_rn(v[i], e.bias[col + i]);
             }
-            const int64_t orow = out_row(e, m);
             if constexpr (KIND == EPI_F32) {
                 store_f32x32(static_cast<float*>(e.out) + orow * e.ldo + col, v, valid);
             } else if constexpr (KIND == EPI_F16) {
                 store_f16x32(static_cast<__half*>(e.out) + orow * e.ldo + col, v, valid);
             } else if constexpr (KIND == EPI_SILU) {
-                for (int i = 0; i < 32; ++i) v[i] = ref_silu(v[i]);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = fast_silu(v[i]);
                 store_f16x32(static_cast<__half*>(e.out) + orow * e.ldo + col, v, valid);
             } else if constexpr (KIND == EPI_RESID) {
-                const float* rs = e.resid + orow * e.ldo + col;
                 float o[32];
                 if (valid >= 32) {
+                    const float* rc = reinterpret_cast<const float*>(rcur);
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        float4 t = *reinterpret_cast<const float4*>(rs + i);
-                        o[i] = __fadd_rn(t.x, v[i]); o[i + 1] = __fadd_rn(t.y, v[i + 1]);
-                        o[i + 2] = __fadd_rn(t.z, v[i + 2]); o[i + 3] = __fadd_rn(t.w, v[i + 3]);
-                    }
+                    for (int i = 0; i < 32; ++i) o[i] = __fadd_rn(rc[i], v[i]);
                 } else {
+                    const float* rs = e.resid + orow * e.ldo + col;
                     for (int i = 0; i < valid; ++i) o[i] = __fadd_rn(rs[i], v[i]);
                 }
                 store_f32x32(static_cast<float*>(e.out) + orow * e.ldo + col, o, valid);
@@ -210,7 +253,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&sm->full[s], 1); mbar_init(&sm->empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(&sm->acc_full[b], 1); mbar_init(&sm->acc_empty[b], 4); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&sm->acc_full[b], 1); mbar_init(&sm->acc_empty[b], EPI_WARPS); }
         sm->abort = 0;
         mbar_fence_init();
         fence_proxy_async();
@@ -266,7 +309,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     } else {
-        const int quarter = warp & 3;
+        const int quarter = warp & 3;         // TMEM lanes this warp may read
+        const int half = (warp - 2) / 4;      // column half of the tile
         uint32_t acc = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++acc) {
             const int b = acc & 1;
@@ -279,7 +323,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
             const uint32_t tacc = tmem + (uint32_t(quarter * 32) << 16) + b * BN;
-            epilogue_tile<KIND>(g, tacc, m0, n0, quarter * 32 + lane);
+            epilogue_tile<KIND>(g, tacc, m0, n0, quarter * 32 + lane, half);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm->acc_empty[b]);
