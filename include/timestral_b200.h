@@ -57,6 +57,29 @@ TIMESTRAL_API int64_t tsb_last_launch_count(timestral_ctx* ctx);
  * 0 = F32 CUDA-core path. */
 TIMESTRAL_API int tsb_model_path(timestral_ctx* ctx);
 
+/* ---- refine without device allocation --------------------------------------------
+ * No counterpart in the reference. The refine step of one decode block (re-normalising a
+ * block's quantiles into advancing per-patch frames) on caller device buffers, for callers
+ * that may not allocate GPU memory: an application that owns every allocation on the
+ * device and hands this library fixed buffers, or a loop that must never enter the CUDA
+ * allocator. The float64 scan scratch comes from a 4 MiB array compiled into the library
+ * (held by every GPU that loads it until the process exits) instead of cudaMalloc; the
+ * call allocates nothing.
+ * d_q/d_out: [rows][patches*patch_size][num_quantiles] f32; d_rows: [rows][length] f32
+ * context; d_mask: [rows][length] bytes 0/1; d_role: [rows] (0 = target row; others keep
+ * their quantiles) or NULL for all targets; d_loc0/d_scale0: [rows] frame of the last
+ * context step. Requests needing more than the reserved scratch, rows * (3 * (length /
+ * patch_size + patches) + 2 * patch_size + 2 * patches) float64 values above 524,288, are
+ * rejected with TSB_ERR_ARG (split the rows across calls). The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture. All calls share the one array: calls that overlap on the GPU (other
+ * streams, other threads) race on it. Enqueued on `stream` (cudaStream_t, NULL = legacy
+ * default stream); errors go to timestral_capi_last_error(NULL). */
+TIMESTRAL_API int tsb_refine_static(const float* d_q, const float* d_rows, const int8_t* d_mask, const int8_t* d_role,
+                                    const float* d_loc0, const float* d_scale0, int32_t rows, int32_t length,
+                                    int32_t patches, int32_t patch_size, int32_t num_quantiles, int32_t median_index,
+                                    double minimum_scale, float* d_out, void* stream);
+
 /* ---- kernel-level test entries (device pointers) ---------------------------------- */
 typedef struct tsb_gemm_test {
     int32_t kind;                 /* 0 f32, 1 f16, 2 resid, 3 silu, 4 swiglu, 5 vgate, 6 qkvg */

@@ -200,6 +200,16 @@ TIMESTRAL_API float* timestral_capi_forecast(timestral_ctx* c, const timestral_f
 
 TIMESTRAL_API void timestral_capi_free_buffer(void* p) { std::free(p); }
 
+}  // extern "C"
+
+namespace tsb {
+// Thread-local error text of entry points that take no handle (read with
+// timestral_capi_last_error(NULL)).
+void set_thread_error(const char* message) { tls_error.set(message); }
+}  // namespace tsb
+
+extern "C" {
+
 // ---- device seam --------------------------------------------------------------------
 
 TIMESTRAL_API int tsb_set_device(int32_t device) {
