@@ -91,6 +91,7 @@ typedef struct tsb_gemm_test {
     int32_t row_group, row_stride, row_offset;
     void* qkvg[4]; int32_t S, H, D, rope;
     const float* cos_tab; const float* sin_tab; const int32_t* rope_row; int32_t rope_half;
+    int32_t rope_dup;             /* tables have equal halves (cos[d] == cos[d + 32]) */
 } tsb_gemm_test;
 /* Runs one tensor-core GEMM on the current device and synchronizes. Returns a TSB_ code;
  * on TSB_ERR_DEVICE the kernel's error word is written to *dev_error. */

@@ -20,7 +20,7 @@ def dp(t):
 
 
 def run(kind, A, B, M, N, K, out=None, ldo=0, bias=None, resid=None, row_group=0, row_stride=0, row_offset=0,
-        qkvg=None, S=0, H=0, D=0, rope=0, cos=None, sin=None, rope_row=None, rope_half=32):
+        qkvg=None, S=0, H=0, D=0, rope=0, cos=None, sin=None, rope_row=None, rope_half=32, rope_dup=0):
     t = tb.GemmTest()
     t.kind, t.A, t.lda, t.B, t.ldb = kind, dp(A), A.shape[1], dp(B), B.shape[1]
     t.M, t.N, t.K = M, N, K
@@ -31,6 +31,7 @@ def run(kind, A, B, M, N, K, out=None, ldo=0, bias=None, resid=None, row_group=0
             t.qkvg[i] = qkvg[i].data_ptr()
     t.S, t.H, t.D, t.rope = S, H, D, rope
     t.cos_tab, t.sin_tab, t.rope_row, t.rope_half = dp(cos), dp(sin), dp(rope_row), rope_half
+    t.rope_dup = rope_dup
     err = C.c_int32(0)
     rc = tb.lib().tsb_test_gemm(C.byref(t), C.byref(err))
     assert rc == 0, (rc, err.value)
@@ -131,8 +132,10 @@ def test_paired(dev, kind):
     close(out, want, K, f16=True)
 
 
-@pytest.mark.parametrize("rope", [0, 1])
+@pytest.mark.parametrize("rope", [0, 1, 2])
 def test_qkvg(dev, rope):
+    """rope 1: arbitrary tables (general path); rope 2: tables with equal halves, as
+    emb = [freqs, freqs] gives, through the path that reads dims 0..15 only."""
     Rr, S, H, hd = 5, 72, 12, 64
     D = H * hd
     M, N, K = Rr * S, 4 * D, D
@@ -142,10 +145,13 @@ def test_qkvg(dev, rope):
     P = 2113
     cos = torch.randn(P, 64, device=dev)
     sin = torch.randn(P, 64, device=dev)
+    if rope == 2:
+        cos[:, 32:] = cos[:, :32]
+        sin[:, 32:] = sin[:, :32]
     rope_row = torch.randint(0, P, (M,), device=dev, dtype=torch.int32)
     bufs = [torch.zeros(Rr, H, S, 64, device=dev, dtype=torch.float16) for _ in range(4)]
-    run(6, A, B, M, N, K, bias=bias, qkvg=bufs, S=S, H=H, D=D, rope=rope, cos=cos, sin=sin, rope_row=rope_row,
-        rope_half=16)
+    run(6, A, B, M, N, K, bias=bias, qkvg=bufs, S=S, H=H, D=D, rope=int(rope > 0), cos=cos, sin=sin,
+        rope_row=rope_row, rope_half=16, rope_dup=int(rope == 2))
     acc = (ref_mm(A, B) + bias.double()).reshape(Rr, S, 4, H, hd).permute(2, 0, 3, 1, 4)  # [4,R,H,S,64]
     c = cos.double()[rope_row.long()].reshape(Rr, S, 64)[:, None]
     s = sin.double()[rope_row.long()].reshape(Rr, S, 64)[:, None]

@@ -84,6 +84,7 @@ struct Engine::Impl {
     float* query = nullptr;
     float* cos_tab = nullptr; float* sin_tab = nullptr;
     int rope_half = 32;
+    int rope_dup = 0;
     float* p_hid = nullptr; float* pb_hid = nullptr; float* p_res = nullptr; float* pb_res = nullptr;
     __half* p_out = nullptr; float* f_pout = nullptr; float* pb_out = nullptr;
     std::vector<std::vector<AttnW>> attn;
@@ -222,6 +223,13 @@ struct Engine::Impl {
             while (active > 0 && identity(active - 1) && identity(active - 1 + half)) --active;
             for (int d = 0; d < active; ++d) if (identity(d) && identity(d + half)) { active = half; break; }
             rope_half = active;
+            rope_dup = 1;
+            for (int p = 0; p < P && rope_dup; ++p)
+                for (int d = 0; d < half; ++d)
+                    if (c[size_t(p) * hd + d] != c[size_t(p) * hd + d + half] || s[size_t(p) * hd + d] != s[size_t(p) * hd + d + half]) {
+                        rope_dup = 0;
+                        break;
+                    }
         }
         query = const_cast<float*>(f32_tensor("patch.forecast_query"));
         p_hid = const_cast<float*>(f32_tensor("patch.hidden.weight")); pb_hid = bias_or_null("patch.hidden.bias");
@@ -539,6 +547,7 @@ struct Engine::Impl {
             g.epi.qkvg[3] = gb.as<__half>();
             g.epi.S = S; g.epi.H = H; g.epi.D = D; g.epi.rope = a.time;
             g.epi.cos_tab = cos_tab; g.epi.sin_tab = sin_tab; g.epi.rope_row = rope_row.as<int>(); g.epi.rope_half = rope_half;
+            g.epi.rope_dup = rope_dup;
             gemm(EPI_QKVG, g);
             const __half* gate = a.gate ? gb.as<__half>() : nullptr;
             if (a.time) {

@@ -31,7 +31,8 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;             // 512: two accumulators
 constexpr int EPI_WARPS = 8;                 // two warps per TMEM lane quarter, one per column half
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int EPI_STAGE_BYTES = EPI_WARPS * 32 * 128;   // per-warp transposition blocks
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
 struct Smem {
     uint64_t full[STAGES];
@@ -61,88 +62,203 @@ __device__ __forceinline__ int64_t out_row(const GemmEpilogue& e, int m) {
     return int64_t(m / e.row_group) * e.row_stride + e.row_offset + (m % e.row_group);
 }
 
-__device__ __forceinline__ void store_f32x32(float* dst, const float* v, int valid) {
-    if (valid >= 32) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-    } else {
-        for (int i = 0; i < valid; ++i) dst[i] = v[i];
-    }
-}
-__device__ __forceinline__ void store_f16x32(__half* dst, const float* v, int valid) {
-    if (valid >= 32) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-            uint4 u;
-            u.x = pack_half2(v[i], v[i + 1]); u.y = pack_half2(v[i + 2], v[i + 3]);
-            u.z = pack_half2(v[i + 4], v[i + 5]); u.w = pack_half2(v[i + 6], v[i + 7]);
-            *reinterpret_cast<uint4*>(dst + i) = u;
-        }
-    } else {
-        for (int i = 0; i < valid; ++i) dst[i] = __float2half_rn(v[i]);
-    }
-}
-
 // Activations of the tensor-core path. Their results are rounded to f16 for the next
 // GEMM, so they use the hardware exp2 and approximate divide (a few ulp in f32, far below
 // the f16 rounding) instead of the reference's exact float sequence used on the F32 path.
 __device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float fast_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// Epilogue of columns [half*BN/2, (half+1)*BN/2) of one 128 x BN accumulator: the thread owns
-// accumulator row `row_in_tile` (its TMEM lane).
+// Per-warp staging block of the epilogue: 32 accumulator rows x 128 bytes. A thread writes
+// its own row (the TMEM lane it read) and the warp then reads the block back so that eight
+// threads cover one 128-byte row, four rows per instruction: every global load and store of
+// the epilogue touches 4 full cache lines per instruction instead of 32 partial ones. The
+// 16-byte chunk index is XORed with the row's low three bits, which keeps both the row
+// writes and the transposed reads free of bank conflicts.
+constexpr int STAGE_ROW_BYTES = 128;
+constexpr int STAGE_WARP_BYTES = 32 * STAGE_ROW_BYTES;
+
+__device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t (&w)[32]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<uint4*>(buf + lane * STAGE_ROW_BYTES + ((j ^ (lane & 7)) << 4)) =
+            make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+}
+// Chunk (lane % 8) of staged row i * 4 + lane / 8.
+__device__ __forceinline__ uint4 unstage(const uint8_t* buf, int i, int lane) {
+    const int row = i * 4 + (lane >> 3), chunk = lane & 7;
+    return *reinterpret_cast<const uint4*>(buf + row * STAGE_ROW_BYTES + ((chunk ^ (row & 7)) << 4));
+}
+__device__ __forceinline__ float4 f4(uint4 u) {
+    return make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
+}
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+__device__ __forceinline__ void pack32(const float* v, uint32_t* w) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = pack_half2(v[2 * i], v[2 * i + 1]);
+}
+
+// Epilogue of one 128 x BN accumulator for one warp: accumulator rows [mw, mw + 32) (its
+// TMEM lane quarter) and columns [half * BN/2, (half + 1) * BN/2).
 template <int KIND>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, int m0, int n0, int row_in_tile, int half) {
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, int m0, int n0, int quarter, int lane,
+                                              int half, uint8_t* buf) {
     const GemmEpilogue& e = g.epi;
-    const int m = m0 + row_in_tile;
-    const bool row_ok = m < g.M;
-    uint32_t r[32];
-    if constexpr (KIND == EPI_SWIGLU || KIND == EPI_VGATE) {
-        // The first half of the tile holds the first operand, the second half the second.
-        float a[32];
-        for (int c = half * (BN / 128); c < (half + 1) * (BN / 128); ++c) {
-            tmem_ld32(tacc + c * 32, r);
+    const int mw = m0 + quarter * 32;
+    // Rows this thread stores after the transpose: mw + i * 4 + lane / 8, i = 0..7.
+    int64_t orow[8];
+    bool rok[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int m = mw + i * 4 + (lane >> 3);
+        rok[i] = m < g.M;
+        orow[i] = rok[i] ? out_row(e, m) : 0;
+    }
+    uint32_t w[32];
+    if constexpr (KIND == EPI_F32 || KIND == EPI_RESID) {
+        // 32 f32 columns per staging pass; the thread stores columns col .. col + 3.
+        constexpr int C = BN / 64;
+        float4 rs[2][8];
+        auto load_resid = [&](int c, float4 (&dst)[8]) {
+            const int col = n0 + (half * C + c) * 32 + (lane & 7) * 4;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (rok[i] && col < g.N) dst[i] = *reinterpret_cast<const float4*>(e.resid + orow[i] * e.ldo + col);
+        };
+        if constexpr (KIND == EPI_RESID) load_resid(0, rs[0]);
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            if constexpr (KIND == EPI_RESID) {
+                if (c + 1 < C) load_resid(c + 1, rs[(c + 1) & 1]);
+            }
+            tmem_ld32(tacc + (half * C + c) * 32, w);
+            tmem_ld_wait();
+            stage_row(buf, lane, w);
+            __syncwarp();
+            const int col = n0 + (half * C + c) * 32 + (lane & 7) * 4;
+            if (col < g.N) {
+                const float4 b = e.bias ? *reinterpret_cast<const float4*>(e.bias + col) : make_float4(0, 0, 0, 0);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    if (!rok[i]) continue;
+                    float4 v = f4(unstage(buf, i, lane));
+                    if (e.bias) v = add4(v, b);
+                    if constexpr (KIND == EPI_RESID) v = add4(rs[c & 1][i], v);
+                    *reinterpret_cast<float4*>(static_cast<float*>(e.out) + orow[i] * e.ldo + col) = v;
+                }
+            }
+            __syncwarp();
+        }
+    } else if constexpr (KIND == EPI_F16 || KIND == EPI_SILU) {
+        // 64 columns (two TMEM reads) per staging pass; the thread stores 8 f16 columns.
+        constexpr int C = BN / 128;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int cb = n0 + (half * C + c) * 64;
+            float v[64];
+            tmem_ld32(tacc + (half * C + c) * 64, w);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) a[i] = __uint_as_float(r[i]);
-            tmem_ld32(tacc + BN / 2 + c * 32, r);
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(w[i]);
+            tmem_ld32(tacc + (half * C + c) * 64 + 32, w);
             tmem_ld_wait();
-            if (!row_ok) continue;
-            const int wn = n0 + c * 32;             // weight row of the first operand column 0
-            const int on = n0 / 2 + c * 32;         // output column
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(w[i]);
+            if (e.bias) {
+#pragma unroll
+                for (int i = 0; i < 64; ++i)
+                    if (cb + i < g.N) v[i] = __fadd_rn(v[i], e.bias[cb + i]);
+            }
+            if constexpr (KIND == EPI_SILU) {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) v[i] = fast_silu(v[i]);
+            }
+            pack32(v, w);
+            pack32(v + 32, w + 16);
+            stage_row(buf, lane, w);
+            __syncwarp();
+            const int col = cb + (lane & 7) * 8;
+            if (col < g.N) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    if (rok[i]) *reinterpret_cast<uint4*>(static_cast<__half*>(e.out) + orow[i] * e.ldo + col) = unstage(buf, i, lane);
+            }
+            __syncwarp();
+        }
+    } else if constexpr (KIND == EPI_SWIGLU || KIND == EPI_VGATE) {
+        // The first half of the tile holds the first operand, the second half the second:
+        // each 32-column pair gives 32 outputs, two pairs fill one 64-column staging pass.
+        constexpr int C = BN / 128;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int cc = half * C + c;
+            const int wn = n0 + cc * 32;              // weight row of the first operand's column 0
+            uint32_t y[32];
+            tmem_ld32(tacc + cc * 32, w);
+            tmem_ld32(tacc + BN / 2 + cc * 32, y);
+            tmem_ld_wait();
             float o[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-                float x = a[i], y = __uint_as_float(r[i]);
-                if (e.bias) { x = __fadd_rn(x, e.bias[wn + i]); y = __fadd_rn(y, e.bias[wn + BN / 2 + i]); }
-                o[i] = KIND == EPI_SWIGLU ? __fmul_rn(x, fast_silu(y)) : __fmul_rn(x, fast_sigmoid(y));
+                float a = __uint_as_float(w[i]), b = __uint_as_float(y[i]);
+                if (e.bias) { a = __fadd_rn(a, e.bias[wn + i]); b = __fadd_rn(b, e.bias[wn + BN / 2 + i]); }
+                o[i] = KIND == EPI_SWIGLU ? __fmul_rn(a, fast_silu(b)) : __fmul_rn(a, fast_sigmoid(b));
             }
-            store_f16x32(static_cast<__half*>(e.out) + out_row(e, m) * e.ldo + on, o, 32);
+            // Row chunk c of the staging row: 16-byte chunks 4c .. 4c + 3.
+            uint32_t pk[16];
+            pack32(o, pk);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int jj = 4 * c + j;
+                *reinterpret_cast<uint4*>(buf + lane * STAGE_ROW_BYTES + ((jj ^ (lane & 7)) << 4)) =
+                    make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            }
         }
+        __syncwarp();
+        const int col = n0 / 2 + half * 64 + (lane & 7) * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (rok[i]) *reinterpret_cast<uint4*>(static_cast<__half*>(e.out) + orow[i] * e.ldo + col) = unstage(buf, i, lane);
+        __syncwarp();
     } else if constexpr (KIND == EPI_QKVG) {
-        float v[64];
-        for (int c = half * (BN / 128); c < (half + 1) * (BN / 128); ++c) {
-            const int col = n0 + c * 64;
+        constexpr int C = BN / 128;
+        const int m = mw + lane;                      // the TMEM row of this thread
+        const bool row_ok = m < g.M;
+        // Head-major row (row * H * S + token) of the rows stored after the transpose.
+        int hm[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int mi = mw + i * 4 + (lane >> 3);
+            hm[i] = (mi / e.S) * e.H * e.S + mi % e.S;
+        }
+        // RoPE table entries of this token's position, fetched once for both heads of the
+        // half: with rope_half <= 16 and tables whose two halves are equal (cos[d] == cos[d + 32],
+        // as for emb = [freqs, freqs]) only dims 0..15 of cos and sin are needed.
+        const int first = n0 + half * C * 64;
+        const bool rope16 = e.rope && e.rope_dup && e.rope_half <= 16 && row_ok && first / e.D < 2;
+        float4 tcs[8];
+        if (rope16) {
+            const float4* ct = reinterpret_cast<const float4*>(e.cos_tab + int64_t(e.rope_row[m]) * 64);
+            const float4* st = reinterpret_cast<const float4*>(e.sin_tab + int64_t(e.rope_row[m]) * 64);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) { tcs[j] = ct[j]; tcs[4 + j] = st[j]; }
+        }
+#pragma unroll 1
+        for (int c = 0; c < C; ++c) {
+            const int col = n0 + (half * C + c) * 64;
             const int which = col / e.D, h = (col % e.D) >> 6;
             const bool rope = row_ok && col < g.N && which < 2 && e.rope;
-            // RoPE table entries of this token's position, requested before the TMEM reads.
-            float4 tc[8], ts[8];
-            const bool rope16 = rope && e.rope_half <= 16;
-            if (rope16) {
-                const float4* ct = reinterpret_cast<const float4*>(e.cos_tab + int64_t(e.rope_row[m]) * 64);
-                const float4* st = reinterpret_cast<const float4*>(e.sin_tab + int64_t(e.rope_row[m]) * 64);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) { tc[j] = ct[j]; tc[4 + j] = ct[8 + j]; ts[j] = st[j]; ts[4 + j] = st[8 + j]; }
-            }
-            tmem_ld32(tacc + c * 64, r);
+            float v[64];
+            tmem_ld32(tacc + (half * C + c) * 64, w);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-            tmem_ld32(tacc + c * 64 + 32, r);
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(w[i]);
+            tmem_ld32(tacc + (half * C + c) * 64 + 32, w);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
-            if (!row_ok || col >= g.N) continue;
+            for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(w[i]);
+            if (col >= g.N) continue;                 // uniform across the warp
             if (e.bias) {
 #pragma unroll
                 for (int i = 0; i < 64; ++i) v[i] = __fadd_rn(v[i], e.bias[col + i]);
@@ -152,21 +268,21 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
                 // (reference src/layers.cpp:238-246). Dims whose inverse frequency is zero
                 // have cos 1 and sin 0 in every table row and are left unchanged.
                 if (rope16) {
-                    const float* c0 = reinterpret_cast<const float*>(tc);       // dims 0..15
-                    const float* c1 = reinterpret_cast<const float*>(tc + 4);   // dims 32..47
-                    const float* s0 = reinterpret_cast<const float*>(ts);
-                    const float* s1 = reinterpret_cast<const float*>(ts + 4);
+                    const float* c0 = reinterpret_cast<const float*>(tcs);       // cos, dims 0..15
+                    const float* s0 = reinterpret_cast<const float*>(tcs + 4);   // sin, dims 0..15
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         if (i >= e.rope_half) break;
                         const float x0 = v[i], x1 = v[i + 32];
                         v[i] = __fadd_rn(__fmul_rn(x0, c0[i]), __fmul_rn(-x1, s0[i]));
-                        v[i + 32] = __fadd_rn(__fmul_rn(x1, c1[i]), __fmul_rn(x0, s1[i]));
+                        v[i + 32] = __fadd_rn(__fmul_rn(x1, c0[i]), __fmul_rn(x0, s0[i]));
                     }
                 } else {
                     const float* ct = e.cos_tab + int64_t(e.rope_row[m]) * 64;
                     const float* st = e.sin_tab + int64_t(e.rope_row[m]) * 64;
-                    for (int i = 0; i < e.rope_half; ++i) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        if (i >= e.rope_half) break;
                         const float x0 = v[i], x1 = v[i + 32];
                         v[i] = __fadd_rn(__fmul_rn(x0, ct[i]), __fmul_rn(-x1, st[i]));
                         v[i + 32] = __fadd_rn(__fmul_rn(x1, ct[i + 32]), __fmul_rn(x0, st[i + 32]));
@@ -176,63 +292,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
 #pragma unroll
                 for (int i = 0; i < 64; ++i) v[i] = fast_sigmoid(v[i]);
             }
-            const int rr = m / e.S, s = m % e.S;
-            __half* dst = e.qkvg[which] + ((int64_t(rr) * e.H + h) * e.S + s) * 64;
-            store_f16x32(dst, v, 32);
-            store_f16x32(dst + 32, v + 32, 32);
-        }
-    } else {
-        float v[32];
-        const int c0 = half * (BN / 64), c1 = (half + 1) * (BN / 64);
-        const int64_t orow = row_ok ? out_row(e, m) : 0;
-        // Residual rows of the next chunk are requested while the current chunk is stored.
-        float4 rnext[8];
-        auto load_resid = [&](int c, float4 (&dst)[8]) {
-            const int col = n0 + c * 32;
-            if (KIND == EPI_RESID && row_ok && col + 32 <= g.N) {
-                const float4* rs = reinterpret_cast<const float4*>(e.resid + orow * e.ldo + col);
+            pack32(v, w);
+            pack32(v + 32, w + 16);
+            stage_row(buf, lane, w);
+            __syncwarp();
+            __half* base = e.qkvg[which] + int64_t(h) * e.S * 64 + (lane & 7) * 8;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) dst[j] = rs[j];
-            }
-        };
-        if (KIND == EPI_RESID) load_resid(c0, rnext);
-        for (int c = c0; c < c1; ++c) {
-            float4 rcur[8];
-            if (KIND == EPI_RESID) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) rcur[j] = rnext[j];
-                if (c + 1 < c1) load_resid(c + 1, rnext);
-            }
-            tmem_ld32(tacc + c * 32, r);
-            tmem_ld_wait();
-            const int col = n0 + c * 32;
-            if (!row_ok || col >= g.N) continue;
-            const int valid = min(32, g.N - col);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-            if (e.bias) {
-                for (int i = 0; i < valid; ++i) v[i] = __fadd_rn(v[i], e.bias[col + i]);
-            }
-            if constexpr (KIND == EPI_F32) {
-                store_f32x32(static_cast<float*>(e.out) + orow * e.ldo + col, v, valid);
-            } else if constexpr (KIND == EPI_F16) {
-                store_f16x32(static_cast<__half*>(e.out) + orow * e.ldo + col, v, valid);
-            } else if constexpr (KIND == EPI_SILU) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = fast_silu(v[i]);
-                store_f16x32(static_cast<__half*>(e.out) + orow * e.ldo + col, v, valid);
-            } else if constexpr (KIND == EPI_RESID) {
-                float o[32];
-                if (valid >= 32) {
-                    const float* rc = reinterpret_cast<const float*>(rcur);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __fadd_rn(rc[i], v[i]);
-                } else {
-                    const float* rs = e.resid + orow * e.ldo + col;
-                    for (int i = 0; i < valid; ++i) o[i] = __fadd_rn(rs[i], v[i]);
-                }
-                store_f32x32(static_cast<float*>(e.out) + orow * e.ldo + col, o, valid);
-            }
+            for (int i = 0; i < 8; ++i)
+                if (rok[i]) *reinterpret_cast<uint4*>(base + int64_t(hm[i]) * 64) = unstage(buf, i, lane);
+            __syncwarp();
         }
     }
 }
@@ -243,7 +311,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                    const GemmArgs g, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    Smem* sm = reinterpret_cast<Smem*>(tiles + STAGES * STAGE_BYTES);
+    uint8_t* stage = tiles + STAGES * STAGE_BYTES;
+    Smem* sm = reinterpret_cast<Smem*>(stage + EPI_STAGE_BYTES);
     volatile int* abort = &sm->abort;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -323,7 +392,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
             const uint32_t tacc = tmem + (uint32_t(quarter * 32) << 16) + b * BN;
-            epilogue_tile<KIND>(g, tacc, m0, n0, quarter * 32 + lane, half);
+            epilogue_tile<KIND>(g, tacc, m0, n0, quarter, lane, half, stage + (warp - 2) * 32 * 128);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm->acc_empty[b]);
@@ -422,6 +491,19 @@ cudaError_t tc_gemm(EpiKind kind, const GemmArgs& a, cudaStream_t stream, int* e
         return cudaErrorInvalidValue;
     if ((kind == EPI_SWIGLU || kind == EPI_VGATE) && a.N % BN) return cudaErrorInvalidValue;
     if (kind == EPI_QKVG && (a.epi.D % 64 || a.N % 64 || a.epi.S <= 0)) return cudaErrorInvalidValue;
+    // The epilogue moves 16-byte vectors: outputs, residuals and f32 biases must be 16-byte
+    // aligned with row pitches that keep every row aligned.
+    auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
+    if (kind == EPI_QKVG) {
+        for (int i = 0; i < 4; ++i)
+            if (misaligned(a.epi.qkvg[i])) return cudaErrorInvalidValue;
+    } else {
+        const int64_t elem = (kind == EPI_F32 || kind == EPI_RESID) ? 4 : 2;
+        if (misaligned(a.epi.out) || (a.epi.ldo * elem) % 16 || (a.epi.row_group > 0 && (a.epi.row_offset * elem) % 16))
+            return cudaErrorInvalidValue;
+        if ((kind == EPI_F32 || kind == EPI_RESID) && (misaligned(a.epi.bias) || misaligned(a.epi.resid)))
+            return cudaErrorInvalidValue;
+    }
     switch (kind) {
         case EPI_F32: return launch<EPI_F32>(a, stream, err);
         case EPI_F16: return launch<EPI_F16>(a, stream, err);

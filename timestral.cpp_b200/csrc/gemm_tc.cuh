@@ -34,6 +34,7 @@ struct GemmEpilogue {
     const float* sin_tab = nullptr;
     const int* rope_row = nullptr;    // [M] table row of each token
     int rope_half = 32;               // rotated dims per half head (rope_dim / 2)
+    int rope_dup = 0;                 // tables satisfy cos[p][d] == cos[p][d + 32] (same for sin)
 };
 
 struct GemmArgs {

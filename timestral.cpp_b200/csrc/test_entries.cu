@@ -17,6 +17,7 @@ extern "C" TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_
     for (int i = 0; i < 4; ++i) e.qkvg[i] = static_cast<__half*>(t->qkvg[i]);
     e.S = t->S; e.H = t->H; e.D = t->D; e.rope = t->rope;
     e.cos_tab = t->cos_tab; e.sin_tab = t->sin_tab; e.rope_row = t->rope_row; e.rope_half = t->rope_half;
+    e.rope_dup = t->rope_dup;
     int* derr = nullptr;
     if (cudaMalloc(&derr, sizeof(int)) != cudaSuccess) return TSB_ERR_CUDA;
     cudaMemset(derr, 0, sizeof(int));

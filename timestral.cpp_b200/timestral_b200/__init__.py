@@ -32,7 +32,8 @@ class GemmTest(C.Structure):
                 ("row_group", C.c_int32), ("row_stride", C.c_int32), ("row_offset", C.c_int32),
                 ("qkvg", C.c_void_p * 4), ("S", C.c_int32), ("H", C.c_int32), ("D", C.c_int32),
                 ("rope", C.c_int32), ("cos_tab", C.c_void_p), ("sin_tab", C.c_void_p),
-                ("rope_row", C.c_void_p), ("rope_half", C.c_int32)]
+                ("rope_row", C.c_void_p), ("rope_half", C.c_int32),
+                ("rope_dup", C.c_int32)]
 
 
 _lib = None
