@@ -96,6 +96,10 @@ typedef struct tsb_gemm_test {
 /* Runs one tensor-core GEMM on the current device and synchronizes. Returns a TSB_ code;
  * on TSB_ERR_DEVICE the kernel's error word is written to *dev_error. */
 TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_error);
+/* RMSNorm of `tokens` rows of width D (device pointers) on the current device, synchronized:
+ * out = x * (1 / sqrt(mean(x^2) + eps)) * w, f32 or (out_f16 != 0) f16. */
+TIMESTRAL_API int tsb_test_rms(const float* x, const float* w, int32_t tokens, int32_t D, float eps, void* out,
+                               int32_t out_f16);
 
 #ifdef __cplusplus
 }

@@ -217,6 +217,62 @@ __global__ void rms_kernel(const float* __restrict__ x, const float* __restrict_
     }
 }
 
+// RMSNorm for widths D = 32 * G: the token's row is loaded into registers with all G loads of
+// a lane in flight at once, then summed in exactly warp_cascade's order (no tail terms exist
+// when D is a multiple of 32) and normalised from the registers.
+__host__ __device__ constexpr int bit_length(int n) { return n ? 1 + bit_length(n >> 1) : 0; }
+
+template <int G>
+__global__ void rms_regs_kernel(const float* __restrict__ x, const float* __restrict__ w, int tokens, float eps,
+                                void* __restrict__ out, int out_f16, int sub, int S, int off) {
+    constexpr int D = 32 * G;
+    const int i = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x & 31;
+    if (i >= tokens) return;
+    const int64_t tok = sub ? int64_t(i / sub) * S + off + i % sub : i;
+    const float* xr = x + tok * D;
+    float v[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) v[g] = __ldcs(xr + g * 32 + lane);
+    // warp_cascade with groups = G: blocks of STEP terms promoted through acc1..acc3.
+    constexpr int POWER = bit_length(G - 1) / 4 > 4 ? bit_length(G - 1) / 4 : 4;
+    constexpr int STEP = 1 << POWER, MSK = STEP - 1;
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+#pragma unroll
+    for (int b = 0; b < G / STEP; ++b) {
+#pragma unroll
+        for (int j = 0; j < STEP; ++j) acc0 = __fadd_rn(acc0, __fmul_rn(v[b * STEP + j], v[b * STEP + j]));
+        const int done = (b + 1) * STEP;
+        acc1 = __fadd_rn(acc1, acc0); acc0 = 0.f;
+        if (done & (MSK << POWER)) continue;
+        acc2 = __fadd_rn(acc2, acc1); acc1 = 0.f;
+        if (done & (MSK << (2 * POWER))) continue;
+        acc3 = __fadd_rn(acc3, acc2); acc2 = 0.f;
+    }
+#pragma unroll
+    for (int g = (G / STEP) * STEP; g < G; ++g) acc0 = __fadd_rn(acc0, __fmul_rn(v[g], v[g]));
+    acc0 = __fadd_rn(acc0, acc1);
+    acc0 = __fadd_rn(acc0, acc2);
+    acc0 = __fadd_rn(acc0, acc3);
+    const float k1 = __shfl_sync(0xffffffffu, acc0, (lane & 7) + 8);
+    const float k2 = __shfl_sync(0xffffffffu, acc0, (lane & 7) + 16);
+    const float k3 = __shfl_sync(0xffffffffu, acc0, (lane & 7) + 24);
+    const float a = __fadd_rn(__fadd_rn(__fadd_rn(acc0, k1), k2), k3);
+    float ssq = 0.f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) ssq = __fadd_rn(ssq, __shfl_sync(0xffffffffu, a, l));
+    const float mean = __fdiv_rn(ssq, float(D));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    if (out_f16) {
+        __half* o = static_cast<__half*>(out) + int64_t(i) * D;
+#pragma unroll
+        for (int g = 0; g < G; ++g) o[g * 32 + lane] = __float2half_rn(__fmul_rn(__fmul_rn(v[g], inv), w[g * 32 + lane]));
+    } else {
+        float* o = static_cast<float*>(out) + int64_t(i) * D;
+#pragma unroll
+        for (int g = 0; g < G; ++g) o[g * 32 + lane] = __fmul_rn(__fmul_rn(v[g], inv), w[g * 32 + lane]);
+    }
+}
+
 // Known covariate rows: non-causal float statistics (reference src/scaler.cpp:60-107).
 __global__ void known_kernel(const RowConfig c, const float* __restrict__ rows, const int8_t* __restrict__ mask,
                              const int8_t* __restrict__ role, int R, int W, int anchor_step, float* __restrict__ features,
@@ -647,7 +703,15 @@ cudaError_t fill_query(const float* query, float* x, int R, int S, int first, in
 cudaError_t rms_norm(const float* x, const float* w, int tokens, int D, float eps, void* out, int out_f16, int sub,
                      int S, int off, cudaStream_t s) {
     if (tokens <= 0) return cudaSuccess;
-    rms_kernel<<<blocks_for(int64_t(tokens) * 32), TPB, 0, s>>>(x, w, tokens, D, eps, out, out_f16, sub, S, off);
+    const unsigned grid = blocks_for(int64_t(tokens) * 32);
+    switch (D) {
+        case 128: rms_regs_kernel<4><<<grid, TPB, 0, s>>>(x, w, tokens, eps, out, out_f16, sub, S, off); break;
+        case 256: rms_regs_kernel<8><<<grid, TPB, 0, s>>>(x, w, tokens, eps, out, out_f16, sub, S, off); break;
+        case 512: rms_regs_kernel<16><<<grid, TPB, 0, s>>>(x, w, tokens, eps, out, out_f16, sub, S, off); break;
+        case 768: rms_regs_kernel<24><<<grid, TPB, 0, s>>>(x, w, tokens, eps, out, out_f16, sub, S, off); break;
+        case 1024: rms_regs_kernel<32><<<grid, TPB, 0, s>>>(x, w, tokens, eps, out, out_f16, sub, S, off); break;
+        default: rms_kernel<<<grid, TPB, 0, s>>>(x, w, tokens, D, eps, out, out_f16, sub, S, off); break;
+    }
     return cudaGetLastError();
 }
 

@@ -2,6 +2,7 @@
 // caller-owned device buffers so the GPU tests can compare it with a reference op.
 #include "common.cuh"
 #include "gemm_tc.cuh"
+#include "rows.cuh"
 #include "timestral_b200.h"
 
 extern "C" TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_error) {
@@ -30,4 +31,12 @@ extern "C" TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_
     if (dev_error) *dev_error = h;
     if (ce != cudaSuccess) return TSB_ERR_CUDA;
     return h ? TSB_ERR_DEVICE : TSB_OK;
+}
+
+extern "C" TIMESTRAL_API int tsb_test_rms(const float* x, const float* w, int32_t tokens, int32_t D, float eps, void* out,
+                                          int32_t out_f16) {
+    if (!x || !w || !out || tokens < 0 || D <= 0) return TSB_ERR_ARG;
+    cudaError_t e = tsb::rms_norm(x, w, tokens, D, eps, out, out_f16, 0, 0, 0, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
 }
