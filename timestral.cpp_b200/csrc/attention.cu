@@ -94,25 +94,33 @@ __device__ __forceinline__ bool variate_allowed(const MaskMeta& mm, int p, int q
 }
 
 // ---------------------------------------------------------------------------------------
-// Tensor-core time attention.
-constexpr int AT_THREADS = 160;  // warps 0-3: softmax + epilogue (one query row each); warp 4: control
-constexpr uint32_t AT_TMEM_COLS = 256;
+// Tensor-core time attention: one (row, head) problem at a time per CTA, several CTAs per SM.
+//
+// 128 threads, one query row per thread (TMEM lane = query). Thread 0 also issues the TMA
+// loads and the two MMAs, so every warp computes. Shared memory holds one problem:
+//   Q  [QR = S rounded to 8 rows][64] f16, K and V [NK = S rounded to 16 rows][64] f16 (rows
+//   past S zero-filled by TMA), P [128][NK] f16 in 64-key blocks (128-byte swizzle).
+// The score MMA reads 128 rows of A starting at Q; rows past QR fall in the K region and only
+// produce scores of query rows that do not exist. O = P V reuses the TMEM columns of S, so a
+// CTA holds 128 columns and up to four CTAs share an SM's TMEM.
+// Per problem: S = Q K^T -> Q/K of the next problem load -> softmax -> O = P V -> V of the
+// next problem loads -> epilogue (the TMEM of O is released before the stores).
+constexpr int AT_THREADS = 128;
+constexpr uint32_t AT_TMEM_COLS = 128;
 
 struct AttnBars {
-    uint64_t full[2];
-    uint64_t s_full, p_ready, o_full;
+    uint64_t full_qk, full_v, s_full, p_ready, o_full, tm_free;
     uint32_t tmem;
     int abort;
 };
 
 template <int NK>
 struct AttnLayout {
-    static constexpr int Q_BYTES = 128 * 128;
     static constexpr int KV_BYTES = NK * 128;
-    static constexpr int SLOT_BYTES = Q_BYTES + 2 * KV_BYTES;
     static constexpr int P_BLOCKS = (NK + 63) / 64;
     static constexpr int P_BYTES = P_BLOCKS * 128 * 128;
-    static constexpr int SMEM = 2 * SLOT_BYTES + P_BYTES + 1024 + 256;
+    __host__ __device__ static constexpr int q_rows(int S) { return (S + 7) / 8 * 8; }
+    __host__ __device__ static constexpr int smem(int S) { return q_rows(S) * 128 + 2 * KV_BYTES + P_BYTES + 1024 + 256; }
 };
 
 __device__ __forceinline__ bool at_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
@@ -124,6 +132,12 @@ __device__ __forceinline__ bool at_wait(uint64_t* bar, uint32_t parity, volatile
         if (clock64() - start > kWaitCycles) { *abort = 1; record_error(err, kDevTimeoutAttn); return false; }
     }
 }
+// Lane 0 waits and the warp follows its verdict, so a warp never splits on an abort.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = at_wait(bar, parity, abort, err);
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
@@ -133,188 +147,250 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 
+// 2^x with subnormal results flushed to zero (probabilities are relative to the row maximum
+// and rounded to f16, whose smallest subnormal is 2^-24).
+__device__ __forceinline__ float exp2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 template <int NK>
-__global__ void __launch_bounds__(AT_THREADS, 2)
+__global__ void __launch_bounds__(AT_THREADS, 3)
     attn_time_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const __half* __restrict__ gate,
                         __half* __restrict__ out, int rows, int H, const MaskMeta mm, int* err) {
     using Lay = AttnLayout<NK>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* pbuf = base + 2 * Lay::SLOT_BYTES;
+    const int S = mm.S, D = H * 64;
+    const int QR = Lay::q_rows(S);
+    uint8_t* qbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* kbuf = qbuf + QR * 128;
+    uint8_t* vbuf = kbuf + Lay::KV_BYTES;
+    uint8_t* pbuf = vbuf + Lay::KV_BYTES;
     AttnBars* bars = reinterpret_cast<AttnBars*>(pbuf + Lay::P_BYTES);
     volatile int* abort = &bars->abort;
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int S = mm.S, D = H * 64;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, t = threadIdx.x;
     const int num = rows * H;
+    const bool ctl = threadIdx.x == 0;
 
-    if (threadIdx.x == 0) {
-        mbar_init(&bars->full[0], 1); mbar_init(&bars->full[1], 1);
-        mbar_init(&bars->s_full, 1); mbar_init(&bars->p_ready, 4); mbar_init(&bars->o_full, 1);
+    if (ctl) {
+        mbar_init(&bars->full_qk, 1); mbar_init(&bars->full_v, 1); mbar_init(&bars->s_full, 1);
+        mbar_init(&bars->p_ready, 4); mbar_init(&bars->o_full, 1); mbar_init(&bars->tm_free, 4);
         bars->abort = 0;
         mbar_fence_init();
         fence_proxy_async();
     }
-    if (warp == 4) { tmem_alloc(&bars->tmem, AT_TMEM_COLS); tmem_relinquish(); }
+    if (warp == 0) { tmem_alloc(&bars->tmem, AT_TMEM_COLS); tmem_relinquish(); }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = bars->tmem;
-    const uint32_t tS = tmem, tO = tmem + 128;
+    const uint32_t tS = bars->tmem;              // S and, after the softmax, O
+    const uint32_t lane_base = uint32_t(warp * 32) << 16;
 
-    if (warp == 4) {
-        if (lane == 0) {
-            auto issue = [&](int slot, int prob) {
-                uint8_t* sl = base + slot * Lay::SLOT_BYTES;
-                mbar_arrive_expect_tx(&bars->full[slot], Lay::SLOT_BYTES);
-                tma_load_3d(sl, &map_q, &bars->full[slot], 0, 0, prob);
-                tma_load_3d(sl + Lay::Q_BYTES, &map_k, &bars->full[slot], 0, 0, prob);
-                tma_load_3d(sl + Lay::Q_BYTES + Lay::KV_BYTES, &map_v, &bars->full[slot], 0, 0, prob);
-            };
-            if (int(blockIdx.x) < num) issue(0, blockIdx.x);
-            if (int(blockIdx.x + gridDim.x) < num) issue(1, blockIdx.x + gridDim.x);
-            const uint32_t id1 = idesc_f16(128, NK), id2 = idesc_f16_bmn(128, 64);
-            int i = 0;
-            for (int prob = blockIdx.x; prob < num; prob += gridDim.x, ++i) {
-                const int s = i & 1;
-                if (!at_wait(&bars->full[s], (i >> 1) & 1, abort, err)) break;
-                tc_fence_after();
-                const uint32_t sq = smem_u32(base + s * Lay::SLOT_BYTES);
-                const uint32_t sk = sq + Lay::Q_BYTES, sv = sk + Lay::KV_BYTES;
-                const uint64_t dq = smem_desc_sw128(sq), dk = smem_desc_sw128(sk);
+    auto issue_qk = [&](int prob) {
+        mbar_arrive_expect_tx(&bars->full_qk, QR * 128 + Lay::KV_BYTES);
+        tma_load_3d(qbuf, &map_q, &bars->full_qk, 0, 0, prob);
+        tma_load_3d(kbuf, &map_k, &bars->full_qk, 0, 0, prob);
+    };
+    auto issue_v = [&](int prob) {
+        mbar_arrive_expect_tx(&bars->full_v, Lay::KV_BYTES);
+        tma_load_3d(vbuf, &map_v, &bars->full_v, 0, 0, prob);
+    };
+    if (ctl && int(blockIdx.x) < num) { issue_qk(blockIdx.x); issue_v(blockIdx.x); }
+
+    // logit scale 1/sqrt(64) folded with log2(e) for exp2
+    constexpr float kScaleLog2e = 0.125f * 1.4426950408889634f;
+    int i = 0;
+    for (int prob = blockIdx.x; prob < num; prob += gridDim.x, ++i) {
+        const uint32_t ph = i & 1;
+        const int next = prob + gridDim.x;
+        const int r = prob / H, h = prob % H;
+        if (warp == 0) {
+            // S = Q K^T once Q and K are resident and every warp has read the previous O.
+            int ok = 1;
+            if (lane == 0) {
+                ok = at_wait(&bars->full_qk, ph, abort, err);
+                if (ok && i > 0) ok = at_wait(&bars->tm_free, ph ^ 1, abort, err);
+                if (ok) {
+                    tc_fence_after();
+                    const uint64_t dq = smem_desc_sw128(smem_u32(qbuf)), dk = smem_desc_sw128(smem_u32(kbuf));
+                    const uint32_t id1 = idesc_f16(128, NK);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) mma_f16(tS, dq + uint64_t(2 * k), dk + uint64_t(2 * k), id1, k > 0);
-                mma_commit(&bars->s_full);
-                if (!at_wait(&bars->p_ready, i & 1, abort, err)) break;
-                tc_fence_after();
-                const uint32_t sp = smem_u32(pbuf);
-#pragma unroll
-                for (int kk = 0; kk < NK / 16; ++kk) {
-                    const uint64_t da = smem_desc_sw128(sp + (kk / 4) * 16384) + uint64_t(2 * (kk % 4));
-                    const uint64_t dv = smem_desc_sw128(sv + kk * 16 * 128);
-                    mma_f16(tO, da, dv, id2, kk > 0);
-                }
-                mma_commit(&bars->o_full);
-                const int next = prob + 2 * gridDim.x;
-                if (next < num) {
-                    if (!at_wait(&bars->o_full, i & 1, abort, err)) break;
-                    issue(s, next);
+                    for (int k = 0; k < 4; ++k) mma_f16(tS, dq + uint64_t(2 * k), dk + uint64_t(2 * k), id1, k > 0);
+                    mma_commit(&bars->s_full);
                 }
             }
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         }
-    } else {
-        const int t = threadIdx.x;  // query row == TMEM lane
-        const uint32_t lane_base = uint32_t(warp * 32) << 16;
-        // logit scale 1/sqrt(64) folded with log2(e) for exp2
-        constexpr float kScaleLog2e = 0.125f * 1.4426950408889634f;
-        int i = 0;
-        for (int prob = blockIdx.x; prob < num; prob += gridDim.x, ++i) {
-            const int r = prob / H, h = prob % H;
-            const bool live = t < S;
-            uint32_t allowed[4];
-            key_set(mm, r, t, live, allowed);
-            // gate row of this query, fetched while the score MMA runs
-            uint4 gv[8];
-            const __half* g = (gate && live) ? gate + ((int64_t(r) * H + h) * S + t) * 64 : nullptr;
-            if (g) {
+        const bool live = t < S;
+        uint32_t allowed[4];
+        key_set(mm, r, t, live, allowed);
+        // Highest key any query of this warp attends: key chunks above it are skipped
+        // (written as zero probabilities), which halves the work of causal rows.
+        int hi = -1;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) gv[c] = *reinterpret_cast<const uint4*>(g + c * 8);
-            }
-            if (!at_wait(&bars->s_full, i & 1, abort, err)) break;
-            tc_fence_after();
-            uint32_t sc[NK];
+        for (int w = 3; w >= 0; --w)
+            if (hi < 0 && allowed[w]) hi = w * 32 + 31 - __clz(allowed[w]);
+        const int kmax = __reduce_max_sync(0xffffffffu, hi + 1) - 1;   // -1: no live query in this warp
+        if (!warp_wait(&bars->s_full, ph, abort, err)) break;
+        tc_fence_after();
+        if (ctl && next < num) issue_qk(next);         // Q and K are free once S is complete
+        float sum = 0.f;
+        if (kmax >= 0) {
+            float sc[NK];
 #pragma unroll
             for (int c = 0; c < NK / 16; ++c)
-                tmem_ld16(tS + lane_base + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&sc[c * 16]));
+                if (c * 16 <= kmax) tmem_ld16(tS + lane_base + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&sc[c * 16]));
             tmem_ld_wait();
+            // Keys outside the query's set score -inf; the row maximum is over its own keys.
             float mx = -INFINITY;
 #pragma unroll
-            for (int k = 0; k < NK; ++k)
-                if ((allowed[k >> 5] >> (k & 31)) & 1u) mx = fmaxf(mx, __uint_as_float(sc[k]));
-            // probabilities in f16, their sum, and the P tile in the 128-byte swizzle
-            const float off = mx * kScaleLog2e;
-            float sum = 0.f;
+            for (int k0 = 0; k0 < NK; k0 += 8) {
+                if (k0 <= kmax) {
+                    const uint32_t bits = allowed[k0 >> 5] >> (k0 & 31);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        sc[k0 + j] = (bits >> j) & 1u ? sc[k0 + j] : -INFINITY;
+                        mx = fmaxf(mx, sc[k0 + j]);
+                    }
+                }
+            }
+            const float off = live ? mx * kScaleLog2e : 0.f;
+            // probabilities in f16 in the 128-byte swizzle, and their sum
 #pragma unroll
             for (int k0 = 0; k0 < NK; k0 += 8) {
-                float p[8];
+                uint4 u = make_uint4(0u, 0u, 0u, 0u);
+                if (k0 <= kmax) {
+                    float p[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int k = k0 + j;
-                    const bool on = (allowed[k >> 5] >> (k & 31)) & 1u;
-                    p[j] = on ? exp2f(__fmaf_rn(__uint_as_float(sc[k]), kScaleLog2e, -off)) : 0.f;
+                    for (int j = 0; j < 8; ++j) {
+                        p[j] = exp2_ftz(__fmaf_rn(sc[k0 + j], kScaleLog2e, -off));
+                        sum += p[j];
+                    }
+                    u.x = pack_half2(p[0], p[1]); u.y = pack_half2(p[2], p[3]);
+                    u.z = pack_half2(p[4], p[5]); u.w = pack_half2(p[6], p[7]);
                 }
-                uint4 u;
-                u.x = pack_half2(p[0], p[1]); u.y = pack_half2(p[2], p[3]);
-                u.z = pack_half2(p[4], p[5]); u.w = pack_half2(p[6], p[7]);
-                const __half2* hp = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) { const float2 f = __half22float2(hp[j]); sum += f.x + f.y; }
                 const int blk = k0 / 64, chunk = (k0 % 64) / 8;
                 *reinterpret_cast<uint4*>(pbuf + blk * 16384 + t * 128 + ((chunk ^ (t & 7)) << 4)) = u;
             }
-            fence_proxy_async();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->p_ready);
-            if (!at_wait(&bars->o_full, i & 1, abort, err)) break;
-            tc_fence_after();
-            const float inv = live ? 1.0f / sum : 0.f;
-            __half* dst = out + (int64_t(r) * S + t) * D + h * 64;
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_ready);
+        if (warp == 0) {
+            // O = P V once every warp's P rows and this problem's V are in shared memory.
+            int ok = 1;
+            if (lane == 0) {
+                ok = at_wait(&bars->p_ready, ph, abort, err) && at_wait(&bars->full_v, ph, abort, err);
+                if (ok) {
+                    tc_fence_after();
+                    const uint32_t sp = smem_u32(pbuf), sv = smem_u32(vbuf);
+                    const uint32_t id2 = idesc_f16_bmn(128, 64);
 #pragma unroll
-            for (int half32 = 0; half32 < 2; ++half32) {
-                uint32_t o[32];
-                tmem_ld32(tO + lane_base + half32 * 32, o);
-                tmem_ld_wait();
-                if (!live) continue;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float y[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) y[j] = __uint_as_float(o[c * 8 + j]) * inv;
-                    if (g) {
-                        const __half2* gh = reinterpret_cast<const __half2*>(&gv[half32 * 4 + c]);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const float2 f = __half22float2(gh[j]);
-                            y[2 * j] = __fmul_rn(y[2 * j], f.x);
-                            y[2 * j + 1] = __fmul_rn(y[2 * j + 1], f.y);
-                        }
+                    for (int kk = 0; kk < NK / 16; ++kk) {
+                        const uint64_t da = smem_desc_sw128(sp + (kk / 4) * 16384) + uint64_t(2 * (kk % 4));
+                        const uint64_t dv = smem_desc_sw128(sv + kk * 16 * 128);
+                        mma_f16(tS, da, dv, id2, kk > 0);
                     }
-                    uint4 u;
-                    u.x = pack_half2(y[0], y[1]); u.y = pack_half2(y[2], y[3]);
-                    u.z = pack_half2(y[4], y[5]); u.w = pack_half2(y[6], y[7]);
-                    *reinterpret_cast<uint4*>(dst + half32 * 32 + c * 8) = u;
+                    mma_commit(&bars->o_full);
                 }
             }
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         }
+        // gate row of this query, fetched while O = P V runs
+        uint4 gv[8];
+        const __half* g = (gate && live) ? gate + ((int64_t(r) * H + h) * S + t) * 64 : nullptr;
+        if (g) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) gv[c] = *reinterpret_cast<const uint4*>(g + c * 8);
+        }
+        if (!warp_wait(&bars->o_full, ph, abort, err)) break;
+        tc_fence_after();
+        if (ctl && next < num) issue_v(next);          // V is free once O is complete
+        // O * (1/sum) * gate in f16, staged row-wise in P block 0 (free once O is complete)
+        // and stored eight threads per 128-byte output row. The TMEM of O is released as soon
+        // as its second half is in registers.
+        const float inv = live ? 1.0f / sum : 0.f;
+        auto stage = [&](const uint32_t (&o)[32], int half32) {
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+                const int c = half32 * 4 + c4;
+                float y[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) y[j] = __uint_as_float(o[c4 * 8 + j]) * inv;
+                if (g) {
+                    const __half2* gh = reinterpret_cast<const __half2*>(&gv[c]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __half22float2(gh[j]);
+                        y[2 * j] = __fmul_rn(y[2 * j], f.x);
+                        y[2 * j + 1] = __fmul_rn(y[2 * j + 1], f.y);
+                    }
+                }
+                uint4 u;
+                u.x = pack_half2(y[0], y[1]); u.y = pack_half2(y[2], y[3]);
+                u.z = pack_half2(y[4], y[5]); u.w = pack_half2(y[6], y[7]);
+                *reinterpret_cast<uint4*>(pbuf + t * 128 + ((c ^ (t & 7)) << 4)) = u;
+            }
+        };
+        uint32_t o[32];
+        if (kmax >= 0) {
+            tmem_ld32(tS + lane_base, o);
+            tmem_ld_wait();
+            stage(o, 0);
+            tmem_ld32(tS + lane_base + 32, o);
+            tmem_ld_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->tm_free);    // the next S may overwrite O
+        if (kmax < 0) continue;
+        stage(o, 1);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int row = warp * 32 + j * 4 + (lane >> 3), chunk = lane & 7;
+            if (row < S)
+                *reinterpret_cast<uint4*>(out + (int64_t(r) * S + row) * D + h * 64 + chunk * 8) =
+                    *reinterpret_cast<const uint4*>(pbuf + row * 128 + ((chunk ^ (row & 7)) << 4));
+        }
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 4) tmem_dealloc(tmem, AT_TMEM_COLS);
+    if (warp == 0) tmem_dealloc(bars->tmem, AT_TMEM_COLS);
 }
 
 template <int NK>
 cudaError_t launch_attn_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
                            int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
     using Lay = AttnLayout<NK>;
+    const int smem = Lay::smem(mm.S);
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(attn_time_tc_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::SMEM);
+        // The largest request of this key count (S = NK) so later calls need no update.
+        cudaError_t e = cudaFuncSetAttribute(attn_time_tc_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Lay::smem(NK));
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
     CUtensorMap mq, mk, mv;
     const int64_t planes = int64_t(rows) * H;
-    if (!make_map_3d_f16(&mq, q, planes, mm.S, 128) || !make_map_3d_f16(&mk, k, planes, mm.S, NK) ||
+    if (!make_map_3d_f16(&mq, q, planes, mm.S, Lay::q_rows(mm.S)) || !make_map_3d_f16(&mk, k, planes, mm.S, NK) ||
         !make_map_3d_f16(&mv, v, planes, mm.S, NK))
         return cudaErrorInvalidValue;
-    const int per_sm = Lay::SMEM * 2 <= 227 * 1024 ? 2 : 1;
+    // CTAs per SM: shared memory (227 KB), TMEM (512 columns) and the launch bounds (3).
+    int per_sm = (227 * 1024) / smem;
+    if (per_sm > 3) per_sm = 3;
+    if (per_sm < 1) per_sm = 1;
     int grid = device_sm_count() * per_sm;
     if (int64_t(grid) > planes) grid = int(planes);
-    attn_time_tc_kernel<NK><<<grid, AT_THREADS, Lay::SMEM, stream>>>(mq, mk, mv, gate, out, rows, H, mm, err);
+    attn_time_tc_kernel<NK><<<grid, AT_THREADS, smem, stream>>>(mq, mk, mv, gate, out, rows, H, mm, err);
     return cudaGetLastError();
 }
 
