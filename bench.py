@@ -41,7 +41,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--weights", default="f16", choices=["f16", "q8_0"])
     ap.add_argument("--batch", type=int, default=B_TOTAL)
-    ap.add_argument("--cpu-sample", type=int, default=16, help="series timed on the CPU baseline")
+    ap.add_argument("--cpu-sample", type=int, default=48, help="series timed on the CPU baseline (about 15-20 s)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
@@ -139,6 +139,12 @@ def cpu_baseline(sample: int, weights: str):
                       f"one forecast call, {dt:.2f} s"}
 
 
+# DRAM bytes (read + write) of one time-attention (row, head) problem at S = 72, from the
+# ncu capture summarised in profiles/attention_time_tc_cfg5.md (B = 1024, dram__bytes_read.sum
+# + dram__bytes_write.sum over 24,576 problems); traffic per launch scales with the problems.
+ATTN_DRAM_BYTES_PER_PROBLEM = 45384
+
+
 def attention_algorithmic(rows: int, S: int, L: int, heads: int = 12, hd: int = 64):
     """FLOPs and bytes of one time-attention launch over `rows` rows: 4*hd*sum_q keys(q) per
     (row, head) with keys = L for encoder queries and S for decoder queries; bytes = q, k, v,
@@ -208,6 +214,10 @@ def main():
         dist.barrier()
     torch.cuda.synchronize(dev)
     clocks.start()
+    # Attention launches are bracketed by CUDA events on the engine stream inside the timed
+    # region (two events per launch, 24 launches per step).
+    model.timing_reset()
+    model.timing(True, attention_only=True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(a.steps):
@@ -218,12 +228,13 @@ def main():
     if tb.lib().tsb_sync(model.h) != 0:
         raise RuntimeError(model.last_error)
     ms = e0.elapsed_time(e1) / a.steps
-    # Attention roofline: one extra instrumented step, events around each attention launch.
+    att_ms, att_n = model.timing_read("attention")
+    model.timing(False)
+    # GEMM share of a step: one extra step with every launch bracketed by events.
     model.timing_reset()
     model.timing(True)
     step()
     tb.lib().tsb_sync(model.h)
-    att_ms, att_n = model.timing_read("attention")
     gemm_ms, gemm_n = model.timing_read("gemm")
     all_ms, all_n = model.timing_read("all")
     model.timing(False)
@@ -271,7 +282,9 @@ def main():
                        "global_batch": a.batch, "seq_len": S, "parallelism": f"series-sharded x{world}",
                        "l2": "per-step working set (~13 GB at B=4096) far above the 126 MB L2"},
             "roofline": {"kernel": "attention_time_tc", "bound": "hbm", "achieved": achieved_gbs, "peak": hbm,
-                         "unit": "GB/s", "frac": achieved_gbs / hbm, "traffic": None,
+                         "unit": "GB/s", "frac": achieved_gbs / hbm,
+                         "traffic": (ATTN_DRAM_BYTES_PER_PROBLEM * rows * 12 if ATTN_DRAM_BYTES_PER_PROBLEM else None),
+                         "traffic_unit": "bytes per launch", "algorithmic_bytes": by,
                          "achieved_tflops": achieved_tf, "roofline_tflops": roof_tf,
                          "frac_of_dense_contraction_roofline": achieved_tf / roof_tf,
                          "launch_ms": att_avg, "launches_per_step": att_n, "peak_kind": kind},

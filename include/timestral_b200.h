@@ -45,8 +45,9 @@ TIMESTRAL_API int tsb_sync(timestral_ctx* ctx);
 TIMESTRAL_API int tsb_set_device(int32_t device);
 /* cudaStream_t of the handle (as an opaque pointer), for callers that time with events. */
 TIMESTRAL_API void* tsb_stream(timestral_ctx* ctx);
-/* Per-kernel timing: when enabled, launches of the named kernel class are bracketed by
- * CUDA events on the handle's stream. Classes: "attention", "gemm", "all". */
+/* Per-kernel timing: when enabled, kernel launches are bracketed by CUDA events on the
+ * handle's stream and read back per class ("attention", "gemm", "rows", "all").
+ * enable: 0 off, 1 every launch, 2 attention launches alone. */
 TIMESTRAL_API int tsb_timing_enable(timestral_ctx* ctx, int32_t enable);
 /* Total milliseconds and launch count recorded for a kernel class since the last reset. */
 TIMESTRAL_API int tsb_timing_read(timestral_ctx* ctx, const char* cls, double* ms, int64_t* launches);

@@ -98,6 +98,7 @@ struct Engine::Impl {
         decoded, err, next_rows, next_mask;
     // timing
     bool timing = false;
+    std::string timing_only;   // empty: every class
     struct Ev { cudaEvent_t a, b; std::string cls; };
     std::vector<Ev> events;
     size_t ev_used = 0;
@@ -339,7 +340,7 @@ struct Engine::Impl {
     // --- launch bookkeeping -------------------------------------------------------------
     template <class Fn> void run(const char* cls, Fn fn) {
         Ev* ev = nullptr;
-        if (timing) {
+        if (timing && (timing_only.empty() || timing_only == cls)) {
             if (ev_used == events.size()) {
                 Ev e;
                 check(cudaEventCreate(&e.a), "event");
@@ -625,7 +626,10 @@ void Engine::check_errors() {
     impl_->check_device_error("forecast");
 }
 
-void Engine::timing_enable(bool on) { impl_->timing = on; }
+void Engine::timing_enable(bool on, const char* only) {
+    impl_->timing = on;
+    impl_->timing_only = only ? only : "";
+}
 void Engine::timing_reset() { impl_->ev_used = 0; }
 bool Engine::timing_read(const std::string& cls, double* ms, int64_t* launches) {
     cudaStreamSynchronize(stream_);

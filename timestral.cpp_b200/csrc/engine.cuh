@@ -77,7 +77,8 @@ public:
     void check_errors();
 
     // Per-kernel-class timing (CUDA events on the engine stream).
-    void timing_enable(bool on);
+    // `only`: time launches of that class alone (nullptr: every class).
+    void timing_enable(bool on, const char* only = nullptr);
     void timing_reset();
     bool timing_read(const std::string& cls, double* ms, int64_t* launches);
     int64_t last_launches() const { return last_launches_; }

@@ -267,7 +267,8 @@ TIMESTRAL_API void* tsb_stream(timestral_ctx* c) { return c ? static_cast<void*>
 
 TIMESTRAL_API int tsb_timing_enable(timestral_ctx* c, int32_t enable) {
     if (!c) return TSB_ERR_ARG;
-    c->forecaster.engine().timing_enable(enable != 0);
+    // 1: every kernel class; 2: attention launches alone (two events per launch).
+    c->forecaster.engine().timing_enable(enable != 0, enable == 2 ? "attention" : nullptr);
     return TSB_OK;
 }
 

@@ -165,8 +165,8 @@ class Model:
     def stream(self) -> int:
         return lib().tsb_stream(self.h) or 0
 
-    def timing(self, enable: bool):
-        lib().tsb_timing_enable(self.h, int(enable))
+    def timing(self, enable: bool, attention_only: bool = False):
+        lib().tsb_timing_enable(self.h, 2 if (enable and attention_only) else int(enable))
 
     def timing_read(self, cls: str):
         ms = C.c_double(0)
