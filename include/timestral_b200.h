@@ -99,6 +99,12 @@ typedef struct tsb_gemm_test {
 TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_error);
 /* RMSNorm of `tokens` rows of width D (device pointers) on the current device, synchronized:
  * out = x * (1 / sqrt(mean(x^2) + eps)) * w, f32 or (out_f16 != 0) f16. */
+/* Tensor-core time attention of `rows` rows without covariates (S <= 128, head_dim 64):
+ * q/k/v/gate f16 head-major [rows][H][S][64] (gate may be NULL), key_valid [rows][ceil(N/32)]
+ * bit p = patch p observed, out f16 token-major [rows * S][H * 64]; synchronized. */
+TIMESTRAL_API int tsb_test_attention_time(const void* q, const void* k, const void* v, const void* gate, void* out,
+                                          const uint32_t* key_valid, int32_t rows, int32_t H, int32_t S, int32_t N,
+                                          int32_t* dev_error);
 TIMESTRAL_API int tsb_test_rms(const float* x, const float* w, int32_t tokens, int32_t D, float eps, void* out,
                                int32_t out_f16);
 

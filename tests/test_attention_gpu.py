@@ -1,0 +1,75 @@
+"""Tensor-core time attention against a float64 torch restatement of the reference's masked,
+sigmoid-gated sdpa on the time axis (reference src/layers.cpp:578-617, src/masks.cpp:21-26,
+src/encoder.cpp:87), through the kernel-level C-ABI test entry.
+
+The kernel rounds probabilities to f16 for the P V product and writes f16 outputs, so the
+tolerance is 4e-3 relative to each row's largest |value| plus 2^-10 of the value."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import timestral_b200 as tb
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return torch.device("cuda:0")
+
+
+def allowed_mask(valid, N, S):
+    """[rows, S, S] bool: query q may attend key k (no covariates)."""
+    rows = valid.shape[0]
+    q = torch.arange(S)[:, None]
+    k = torch.arange(S)[None, :]
+    kv = torch.zeros(rows, S, dtype=torch.bool)
+    kv[:, :N] = valid
+    kvk = kv[:, None, :].expand(rows, S, S)
+    enc = (q < N) & (k < N) & ((kvk & (k <= q)) | (q == k))
+    dec = (q >= N) & (((k < N) & kvk) | ((k >= N) & (k <= q)))
+    return enc | dec
+
+
+@pytest.mark.parametrize("S,N,gated", [(1, 1, True), (9, 8, True), (33, 30, False), (72, 64, True), (100, 97, True),
+                                       (128, 120, True), (70, 70, True)])
+def test_attention_time_tc(dev, S, N, gated):
+    rows, H = 37, 3
+    g = torch.Generator().manual_seed(S * 1000 + N)
+    q = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
+    k = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
+    v = torch.randn(rows, H, S, 64, generator=g).half()
+    gate = torch.rand(rows, H, S, 64, generator=g).half() if gated else None
+    valid = torch.rand(rows, N, generator=g) > 0.2
+    valid[:, 0] = True
+    words = (N + 31) // 32
+    bits = np.zeros((rows, words), np.uint32)
+    vn = valid.numpy()
+    for p in range(N):
+        bits[:, p // 32] |= vn[:, p].astype(np.uint32) << np.uint32(p % 32)
+    allowed = allowed_mask(valid, N, S)
+    s = torch.einsum("rhqd,rhkd->rhqk", q.double(), k.double()) / 8.0
+    s = s.masked_fill(~allowed[:, None], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    want = torch.einsum("rhqk,rhkd->rhqd", p, v.double())
+    if gated:
+        want = want * gate.double()
+    want = want.permute(0, 2, 1, 3).reshape(rows * S, H * 64)
+    dq, dk, dv = q.to(dev), k.to(dev), v.to(dev)
+    dg = gate.to(dev) if gated else None
+    dbits = torch.from_numpy(bits.view(np.int32)).to(dev)
+    out = torch.full((rows * S, H * 64), float("nan"), device=dev, dtype=torch.float16)
+    err = C.c_int32(0)
+    rc = tb.lib().tsb_test_attention_time(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr() if gated else None,
+                                          out.data_ptr(), dbits.data_ptr(), rows, H, S, N, C.byref(err))
+    assert rc == 0, (rc, err.value)
+    got = out.cpu().double()
+    assert torch.isfinite(got).all()
+    scale = want.abs().reshape(rows, S, H, 64).amax(dim=(1, 3), keepdim=True).expand(rows, S, H, 64).reshape(rows * S, H * 64)
+    tol = 4e-3 * scale + want.abs() * 2.0 ** -10
+    bad = (got - want).abs() > tol
+    assert not bad.any(), f"max err {(got - want).abs().max().item():.3e}"

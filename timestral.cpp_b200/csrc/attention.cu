@@ -96,13 +96,15 @@ __device__ __forceinline__ bool variate_allowed(const MaskMeta& mm, int p, int q
 // ---------------------------------------------------------------------------------------
 // Tensor-core time attention: one (row, head) problem at a time per CTA, several CTAs per SM.
 //
-// 128 threads, one query row per thread (TMEM lane = query). Thread 0 also issues the TMA
-// loads and the two MMAs, so every warp computes. Shared memory holds one problem:
-//   Q  [QR = S rounded to 8 rows][64] f16, K and V [NK = S rounded to 16 rows][64] f16 (rows
-//   past S zero-filled by TMA), P [128][NK] f16 in 64-key blocks (128-byte swizzle).
-// The score MMA reads 128 rows of A starting at Q; rows past QR fall in the K region and only
-// produce scores of query rows that do not exist. O = P V reuses the TMEM columns of S, so a
-// CTA holds 128 columns and up to four CTAs share an SM's TMEM.
+// 128 threads, one query per thread. A warp can only read its own quarter of the TMEM lanes,
+// so the S queries are split into four runs of RQ = ceil(S / 4), one per lane quarter: query
+// q * RQ + l sits in lane 32 q + l, and all four warps (on all four SM sub-partitions) have
+// live queries. Thread 0 also issues the TMA loads and the two MMAs. Shared memory holds one
+// problem: Q [128 lanes][64] f16 (four TMA boxes of RQ rounded to 8 rows), K and V
+// [NK = S rounded to 16 rows][64] f16 (rows past S zero-filled by TMA), P [128][NK] f16 in
+// 64-key blocks (128-byte swizzle). Lanes without a query compute scores that are never used.
+// O = P V reuses the TMEM columns of S, so a CTA holds 128 columns and up to four CTAs share
+// an SM's TMEM.
 // Per problem: S = Q K^T -> Q/K of the next problem load -> softmax -> O = P V -> V of the
 // next problem loads -> epilogue (the TMEM of O is released before the stores).
 constexpr int AT_THREADS = 128;
@@ -119,8 +121,9 @@ struct AttnLayout {
     static constexpr int KV_BYTES = NK * 128;
     static constexpr int P_BLOCKS = (NK + 63) / 64;
     static constexpr int P_BYTES = P_BLOCKS * 128 * 128;
-    __host__ __device__ static constexpr int q_rows(int S) { return (S + 7) / 8 * 8; }
-    __host__ __device__ static constexpr int smem(int S) { return q_rows(S) * 128 + 2 * KV_BYTES + P_BYTES + 1024 + 256; }
+    __host__ __device__ static constexpr int run(int S) { return (S + 3) / 4; }                 // queries per lane quarter
+    __host__ __device__ static constexpr int q_box(int S) { return (run(S) + 7) / 8 * 8; }      // TMA box rows
+    static constexpr int SMEM = 128 * 128 + 2 * KV_BYTES + P_BYTES + 1024 + 256;
 };
 
 __device__ __forceinline__ bool at_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
@@ -163,9 +166,9 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
     using Lay = AttnLayout<NK>;
     extern __shared__ uint8_t smem_raw[];
     const int S = mm.S, D = H * 64;
-    const int QR = Lay::q_rows(S);
+    const int RQ = Lay::run(S), QB = Lay::q_box(S);
     uint8_t* qbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* kbuf = qbuf + QR * 128;
+    uint8_t* kbuf = qbuf + 128 * 128;
     uint8_t* vbuf = kbuf + Lay::KV_BYTES;
     uint8_t* pbuf = vbuf + Lay::KV_BYTES;
     AttnBars* bars = reinterpret_cast<AttnBars*>(pbuf + Lay::P_BYTES);
@@ -189,8 +192,9 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
     const uint32_t lane_base = uint32_t(warp * 32) << 16;
 
     auto issue_qk = [&](int prob) {
-        mbar_arrive_expect_tx(&bars->full_qk, QR * 128 + Lay::KV_BYTES);
-        tma_load_3d(qbuf, &map_q, &bars->full_qk, 0, 0, prob);
+        mbar_arrive_expect_tx(&bars->full_qk, 4 * QB * 128 + Lay::KV_BYTES);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tma_load_3d(qbuf + q * 32 * 128, &map_q, &bars->full_qk, 0, q * RQ, prob);
         tma_load_3d(kbuf, &map_k, &bars->full_qk, 0, 0, prob);
     };
     auto issue_v = [&](int prob) {
@@ -223,9 +227,10 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
             }
             if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         }
-        const bool live = t < S;
+        const int qi = warp * RQ + lane;               // this thread's query
+        const bool live = lane < RQ && qi < S;
         uint32_t allowed[4];
-        key_set(mm, r, t, live, allowed);
+        key_set(mm, r, qi, live, allowed);
         // Highest key any query of this warp attends: key chunks above it are skipped
         // (written as zero probabilities), which halves the work of causal rows.
         int hi = -1;
@@ -301,7 +306,7 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
         }
         // gate row of this query, fetched while O = P V runs
         uint4 gv[8];
-        const __half* g = (gate && live) ? gate + ((int64_t(r) * H + h) * S + t) * 64 : nullptr;
+        const __half* g = (gate && live) ? gate + ((int64_t(r) * H + h) * S + qi) * 64 : nullptr;
         if (g) {
 #pragma unroll
             for (int c = 0; c < 8; ++c) gv[c] = *reinterpret_cast<const uint4*>(g + c * 8);
@@ -351,9 +356,9 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
         __syncwarp();
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int row = warp * 32 + j * 4 + (lane >> 3), chunk = lane & 7;
-            if (row < S)
-                *reinterpret_cast<uint4*>(out + (int64_t(r) * S + row) * D + h * 64 + chunk * 8) =
+            const int li = j * 4 + (lane >> 3), chunk = lane & 7, row = warp * 32 + li, q = warp * RQ + li;
+            if (li < RQ && q < S)
+                *reinterpret_cast<uint4*>(out + (int64_t(r) * S + q) * D + h * 64 + chunk * 8) =
                     *reinterpret_cast<const uint4*>(pbuf + row * 128 + ((chunk ^ (row & 7)) << 4));
         }
         __syncwarp();
@@ -368,20 +373,18 @@ template <int NK>
 cudaError_t launch_attn_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
                            int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
     using Lay = AttnLayout<NK>;
-    const int smem = Lay::smem(mm.S);
+    const int smem = Lay::SMEM;
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        // The largest request of this key count (S = NK) so later calls need no update.
-        cudaError_t e = cudaFuncSetAttribute(attn_time_tc_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Lay::smem(NK));
+        cudaError_t e = cudaFuncSetAttribute(attn_time_tc_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
     CUtensorMap mq, mk, mv;
     const int64_t planes = int64_t(rows) * H;
-    if (!make_map_3d_f16(&mq, q, planes, mm.S, Lay::q_rows(mm.S)) || !make_map_3d_f16(&mk, k, planes, mm.S, NK) ||
+    if (!make_map_3d_f16(&mq, q, planes, mm.S, Lay::q_box(mm.S)) || !make_map_3d_f16(&mk, k, planes, mm.S, NK) ||
         !make_map_3d_f16(&mv, v, planes, mm.S, NK))
         return cudaErrorInvalidValue;
     // CTAs per SM: shared memory (227 KB), TMEM (512 columns) and the launch bounds (3).

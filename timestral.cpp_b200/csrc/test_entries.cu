@@ -1,6 +1,7 @@
 // Kernel-level test entries of the C ABI (include/timestral_b200.h): run one kernel on
 // caller-owned device buffers so the GPU tests can compare it with a reference op.
 #include "common.cuh"
+#include "attention.cuh"
 #include "gemm_tc.cuh"
 #include "rows.cuh"
 #include "timestral_b200.h"
@@ -39,4 +40,27 @@ extern "C" TIMESTRAL_API int tsb_test_rms(const float* x, const float* w, int32_
     cudaError_t e = tsb::rms_norm(x, w, tokens, D, eps, out, out_f16, 0, 0, 0, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     return e == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
+}
+
+extern "C" TIMESTRAL_API int tsb_test_attention_time(const void* q, const void* k, const void* v, const void* gate, void* out,
+                                                     const uint32_t* key_valid, int32_t rows, int32_t H, int32_t S,
+                                                     int32_t N, int32_t* dev_error) {
+    using namespace tsb;
+    if (!q || !k || !v || !out || !key_valid || rows <= 0 || H <= 0 || S <= 0 || S > 128 || N <= 0 || N > S)
+        return TSB_ERR_ARG;
+    MaskMeta mm;
+    mm.key_valid = key_valid; mm.kv_words = (N + 31) / 32; mm.N = N; mm.L = N; mm.S = S;
+    int* derr = nullptr;
+    if (cudaMalloc(&derr, sizeof(int)) != cudaSuccess) return TSB_ERR_CUDA;
+    cudaMemset(derr, 0, sizeof(int));
+    cudaError_t ce = attention_time_tc(static_cast<const __half*>(q), static_cast<const __half*>(k),
+                                       static_cast<const __half*>(v), static_cast<const __half*>(gate),
+                                       static_cast<__half*>(out), rows, H, mm, 0, derr);
+    if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+    int h = 0;
+    cudaMemcpy(&h, derr, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(derr);
+    if (dev_error) *dev_error = h;
+    if (ce != cudaSuccess) return ce == cudaErrorInvalidValue ? TSB_ERR_ARG : TSB_ERR_CUDA;
+    return h ? TSB_ERR_DEVICE : TSB_OK;
 }
