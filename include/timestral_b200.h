@@ -105,6 +105,9 @@ TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_error);
 TIMESTRAL_API int tsb_test_attention_time(const void* q, const void* k, const void* v, const void* gate, void* out,
                                           const uint32_t* key_valid, int32_t rows, int32_t H, int32_t S, int32_t N,
                                           int32_t* dev_error);
+/* f16 hi/lo split used by the tensor-core patch projections: out [rows][3K] f16 =
+ * [hi | hi | lo] of each f32 row of a; sets *d_overflow (device int) when any |a| > 30000. */
+TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, void* out, int32_t* d_overflow);
 TIMESTRAL_API int tsb_test_rms(const float* x, const float* w, int32_t tokens, int32_t D, float eps, void* out,
                                int32_t out_f16);
 

@@ -34,3 +34,27 @@ def test_rms_bitwise(dev, tokens, D):
     out16 = torch.empty(tokens, D, device=dev, dtype=torch.float16)
     assert tb.lib().tsb_test_rms(dx.data_ptr(), dw.data_ptr(), tokens, D, C.c_float(1e-6), out16.data_ptr(), 1) == 0
     assert np.array_equal(out16.cpu().numpy(), want.astype(np.float16))
+
+
+@pytest.mark.parametrize("big", [False, True])
+def test_split_f16(dev, big):
+    """hi + lo reproduces each f32 value to ~2^-22 relative (the tensor-core patch projections
+    sum hi*hi + hi*lo + lo*hi), and values beyond 30000 raise the flag that makes the
+    CUDA-core kernels recompute the projections."""
+    rng = np.random.default_rng(7)
+    rows, K = 300, 64
+    a = (rng.standard_normal((rows, K)) * rng.uniform(0.01, 100, (rows, 1))).astype(np.float32)
+    if big:
+        a[123, 5] = 40000.0
+    da = torch.from_numpy(a).to(dev)
+    out = torch.empty(rows, 3 * K, device=dev, dtype=torch.float16)
+    flag = torch.zeros(1, device=dev, dtype=torch.int32)
+    assert tb.lib().tsb_test_split_f16(da.data_ptr(), rows, K, out.data_ptr(), flag.data_ptr()) == 0
+    o = out.cpu().numpy().astype(np.float64)
+    hi, hi2, lo = o[:, :K], o[:, K:2 * K], o[:, 2 * K:]
+    assert np.array_equal(hi, hi2)
+    assert np.array_equal(hi, a.astype(np.float16).astype(np.float64))
+    ok = np.abs(a) <= 30000
+    err = np.abs(hi + lo - a.astype(np.float64))[ok]
+    assert np.all(err <= 2.0 ** -21 * np.abs(a[ok]) + 2.0 ** -24), float(err.max())
+    assert int(flag.item()) == int(big)

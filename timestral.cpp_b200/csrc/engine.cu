@@ -87,6 +87,8 @@ struct Engine::Impl {
     int rope_dup = 0;
     float* p_hid = nullptr; float* pb_hid = nullptr; float* p_res = nullptr; float* pb_res = nullptr;
     __half* p_out = nullptr; float* f_pout = nullptr; float* pb_out = nullptr;
+    __half* p_hid_split = nullptr; __half* p_res_split = nullptr;   // [N][3K] = [hi | lo | hi]
+    bool patch_tc = false;
     std::vector<std::vector<AttnW>> attn;
     std::vector<MlpW> mlp;
     const float* out_norm = nullptr;
@@ -95,7 +97,7 @@ struct Engine::Impl {
     // workspace
     DevBuf rows, mask, win, wmask, role, future, fmask, feat, aloc, ascale, caplo, caphi, capsc, first_obs, kv, rope_row,
         gbeg, gsize, clip_ok, x, xn, qb, kb, vb, gb, att, hb, zb, fused, gtmp, ph, dec, hh, hraw, qout, refined, scratch,
-        decoded, err, next_rows, next_mask;
+        decoded, err, next_rows, next_mask, feat16, pflag;
     // timing
     bool timing = false;
     std::string timing_only;   // empty: every class
@@ -238,6 +240,29 @@ struct Engine::Impl {
         pb_out = bias_or_null("patch.out.bias");
         if (tc) { auto v = rows_f16(t("patch.out.weight")); p_out = reinterpret_cast<__half*>(upload(v.data(), v.size())); }
         else { auto v = rows_f32(t("patch.out.weight")); f_pout = upload(v.data(), v.size()); }
+        // Tensor-core patch projections (K = 2 * patch_size, F32 weights): the weights split into
+        // f16 hi/lo terms, rows of 3K f16 that stay 16-byte aligned.
+        patch_tc = tc && (3 * 2 * ps * 2) % 16 == 0;
+        if (patch_tc) {
+            auto split = [&](const std::string& name) {
+                auto w = t(name);
+                const size_t n = size_t(w.ne1), k = size_t(w.ne0);
+                const float* f = static_cast<const float*>(w.data);
+                std::vector<uint16_t> out(n * 3 * k);
+                for (size_t r = 0; r < n; ++r)
+                    for (size_t c = 0; c < k; ++c) {
+                        const float v = f[r * k + c];
+                        const uint16_t hi = float_to_half_bits(v);
+                        const uint16_t lo = float_to_half_bits(v - half_bits_to_float(hi));
+                        out[r * 3 * k + c] = hi;
+                        out[r * 3 * k + k + c] = lo;
+                        out[r * 3 * k + 2 * k + c] = hi;
+                    }
+                return reinterpret_cast<__half*>(upload(out.data(), out.size()));
+            };
+            p_hid_split = split("patch.hidden.weight");
+            p_res_split = split("patch.res.weight");
+        }
         attn.resize(m.schedule.size());
         mlp.resize(m.schedule.size());
         for (size_t i = 0; i < m.schedule.size(); ++i) {
@@ -405,11 +430,30 @@ struct Engine::Impl {
             SimtGemm g;
             g.A = feat.as<float>(); g.lda = 2 * ps; g.W = p_hid; g.M = int(PR); g.N = 4 * D; g.K = 2 * ps;
             g.order = ORDER_CHAIN; g.epi = tc ? SEPI_SILU_F16 : SEPI_SILU_F32; g.bias = pb_hid; g.out = ph.p; g.ldo = 4 * D;
-            sgemm(g);
             SimtGemm r;
             r.A = feat.as<float>(); r.lda = 2 * ps; r.W = p_res; r.M = int(PR); r.N = D; r.K = 2 * ps;
             r.order = ORDER_CHAIN; r.epi = SEPI_F32; r.bias = pb_res; r.out = x.p; r.ldo = D;
             r.row_group = N; r.row_stride = S;
+            if (patch_tc) {
+                // Tensor cores on the f16 hi/lo split of the features; when a feature falls
+                // outside the split's range the CUDA-core kernels recompute both projections.
+                const int K3 = 3 * 2 * ps;
+                feat16.ensure(size_t(PR) * K3 * 2);
+                pflag.ensure(sizeof(int));
+                check(cudaMemsetAsync(pflag.p, 0, sizeof(int), s), "memset");
+                run("rows", [&] { return split_f16(feat.as<float>(), PR, 2 * ps, feat16.as<__half>(), pflag.as<int>(), s); });
+                GemmArgs h;
+                h.A = feat16.as<__half>(); h.lda = K3; h.B = p_hid_split; h.ldb = K3; h.M = int(PR); h.N = 4 * D; h.K = K3;
+                h.epi.out = ph.p; h.epi.ldo = 4 * D; h.epi.bias = pb_hid;
+                gemm(EPI_SILU, h);
+                GemmArgs o;
+                o.A = feat16.as<__half>(); o.lda = K3; o.B = p_res_split; o.ldb = K3; o.M = int(PR); o.N = D; o.K = K3;
+                o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = pb_res; o.epi.row_group = N; o.epi.row_stride = S;
+                gemm(EPI_F32, o);
+                g.only_if = pflag.as<int>();
+                r.only_if = pflag.as<int>();
+            }
+            sgemm(g);
             sgemm(r);
         }
         if (tc) {

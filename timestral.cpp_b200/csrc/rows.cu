@@ -592,6 +592,7 @@ constexpr int SB = 64, SK = 16;
 
 template <int ORDER>
 __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtGemm g) {
+    if (g.only_if && *g.only_if == 0) return;
     using Acc = typename std::conditional<ORDER == ORDER_F64, double, float>::type;
     __shared__ float As[SK][SB + 1];
     __shared__ float Ws[SK][SB + 1];
@@ -773,6 +774,29 @@ cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s) {
         case ORDER_CHAIN: simt_gemm_kernel<ORDER_CHAIN><<<grid, 256, 0, s>>>(g); break;
         default: simt_gemm_kernel<ORDER_F64><<<grid, 256, 0, s>>>(g); break;
     }
+    return cudaGetLastError();
+}
+
+__global__ void split_f16_kernel(const float* __restrict__ a, int64_t n, int K, __half* __restrict__ out,
+                                 int* __restrict__ overflow) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int64_t m = i / K;
+    const int k = int(i % K);
+    const float v = a[i];
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+    __half* o = out + m * 3 * K;
+    o[k] = hi;
+    o[K + k] = hi;
+    o[2 * K + k] = lo;
+    if (!(fabsf(v) <= 30000.f)) *overflow = 1;
+}
+
+cudaError_t split_f16(const float* a, int64_t rows, int K, __half* out, int* overflow, cudaStream_t s) {
+    const int64_t n = rows * K;
+    if (n <= 0) return cudaSuccess;
+    split_f16_kernel<<<blocks_for(n), TPB, 0, s>>>(a, n, K, out, overflow);
     return cudaGetLastError();
 }
 

@@ -100,8 +100,16 @@ struct SimtGemm {
     const float* bias = nullptr;
     void* out = nullptr; int64_t ldo = 0;
     int row_group = 0, row_stride = 0, row_offset = 0;  // output row remap (as in GemmEpilogue)
+    const int* only_if = nullptr;       // when set, the launch does nothing unless *only_if != 0
 };
 cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s);
+
+// Two-term f16 split of an f32 matrix for tensor-core products at near-f32 accuracy:
+// out[m] = [hi(a[m]) | hi(a[m]) | lo(a[m])] (3K f16 per row), hi = f16(a), lo = f16(a - hi).
+// With weights split as [hi(w) | lo(w) | hi(w)], a K = 3K f16 product sums
+// hi*hi + hi*lo + lo*hi (relative error ~2^-22). Any |a| > 30000 (outside the range where
+// the split is exact enough in f16) sets *overflow.
+cudaError_t split_f16(const float* a, int64_t rows, int K, __half* out, int* overflow, cudaStream_t s);
 
 // Read a device error word and reset it.
 int read_error(int* d_err, cudaStream_t s);

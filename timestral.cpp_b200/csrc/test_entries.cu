@@ -64,3 +64,10 @@ extern "C" TIMESTRAL_API int tsb_test_attention_time(const void* q, const void* 
     if (ce != cudaSuccess) return ce == cudaErrorInvalidValue ? TSB_ERR_ARG : TSB_ERR_CUDA;
     return h ? TSB_ERR_DEVICE : TSB_OK;
 }
+
+extern "C" TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, void* out, int32_t* d_overflow) {
+    if (!a || !out || !d_overflow || rows < 0 || K <= 0) return TSB_ERR_ARG;
+    cudaError_t e = tsb::split_f16(a, rows, K, static_cast<__half*>(out), d_overflow, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
+}
