@@ -191,8 +191,9 @@ def main():
         torch.cuda.set_device(local)
     import timestral_b200 as tb
     dev = torch.device("cuda", local)
-    per = a.batch // world
-    lo, hi = rank * per, (rank + 1) * per
+    from timestral_b200.shard import shard_range
+    lo, hi = shard_range(a.batch, world, rank)
+    per = hi - lo
     path = model_path(a.weights, rank, dist)
     model = tb.Model(path, device=local)
     Q = model.num_quantiles

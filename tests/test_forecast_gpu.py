@@ -155,6 +155,18 @@ def test_sign_symmetry_bitwise_and_batch_invariance():
     assert np.array_equal(one, a[2:3]), "a series' forecast does not depend on the batch it is in"
 
 
+def test_shards_bitwise_equal_to_one_gpu():
+    """A batch forecast in 1, 2, 4 or 8 shards (the per-GPU slices of the series-sharded
+    path) gives the same bits as the whole batch: no row depends on the shard size."""
+    from timestral_b200.shard import forecast_sharded
+    m, _ = models(sy.spec_209m(), "f16")
+    x = sy.series_random_walk(8, 2048, nan_frac=0.01)
+    whole = m.forecast(x, 256)
+    for world in (2, 4, 8):
+        parts = [forecast_sharded(m.forecast, x, 256, r, world) for r in range(world)]
+        assert np.array_equal(np.concatenate(parts).view(np.uint32), whole.view(np.uint32)), world
+
+
 def test_errors_surface_through_the_abi():
     m, _ = models(sy.spec_tiny(), "f32")
     x = random_context(1, 1, 40, seed=1)

@@ -435,13 +435,16 @@ struct Engine::Impl {
             r.order = ORDER_CHAIN; r.epi = SEPI_F32; r.bias = pb_res; r.out = x.p; r.ldo = D;
             r.row_group = N; r.row_stride = S;
             if (patch_tc) {
-                // Tensor cores on the f16 hi/lo split of the features; when a feature falls
-                // outside the split's range the CUDA-core kernels recompute both projections.
+                // Tensor cores on the f16 hi/lo split of the features; rows with a feature
+                // outside the split's range are recomputed by the CUDA-core kernels.
                 const int K3 = 3 * 2 * ps;
                 feat16.ensure(size_t(PR) * K3 * 2);
-                pflag.ensure(sizeof(int));
-                check(cudaMemsetAsync(pflag.p, 0, sizeof(int), s), "memset");
-                run("rows", [&] { return split_f16(feat.as<float>(), PR, 2 * ps, feat16.as<__half>(), pflag.as<int>(), s); });
+                pflag.ensure(sizeof(int) + size_t(PR));
+                check(cudaMemsetAsync(pflag.p, 0, sizeof(int) + size_t(PR), s), "memset");
+                int8_t* row_flags = pflag.as<int8_t>() + sizeof(int);
+                run("rows", [&] {
+                    return split_f16(feat.as<float>(), PR, 2 * ps, feat16.as<__half>(), pflag.as<int>(), row_flags, s);
+                });
                 GemmArgs h;
                 h.A = feat16.as<__half>(); h.lda = K3; h.B = p_hid_split; h.ldb = K3; h.M = int(PR); h.N = 4 * D; h.K = K3;
                 h.epi.out = ph.p; h.epi.ldo = 4 * D; h.epi.bias = pb_hid;
@@ -450,8 +453,10 @@ struct Engine::Impl {
                 o.A = feat16.as<__half>(); o.lda = K3; o.B = p_res_split; o.ldb = K3; o.M = int(PR); o.N = D; o.K = K3;
                 o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = pb_res; o.epi.row_group = N; o.epi.row_stride = S;
                 gemm(EPI_F32, o);
-                g.only_if = pflag.as<int>();
-                r.only_if = pflag.as<int>();
+                // Only the rows with such a feature are rewritten, so every row's result is
+                // the same whatever else is in the batch.
+                g.only_if = pflag.as<int>(); g.row_mask = row_flags;
+                r.only_if = pflag.as<int>(); r.row_mask = row_flags;
             }
             sgemm(g);
             sgemm(r);

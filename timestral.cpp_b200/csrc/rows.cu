@@ -597,64 +597,73 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtGemm g) {
     __shared__ float As[SK][SB + 1];
     __shared__ float Ws[SK][SB + 1];
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-    const int m0 = blockIdx.y * SB, n0 = blockIdx.x * SB;
-    Acc sum[4][4], pan[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) { sum[i][j] = 0; pan[i][j] = 0; }
+    const int tiles_n = (g.N + SB - 1) / SB;
+    const int64_t tiles = int64_t((g.M + SB - 1) / SB) * tiles_n;
     const int K = g.K;
     const bool panels = ORDER == ORDER_PANEL192 && K >= 192;
-    for (int k0 = 0; k0 < K; k0 += SK) {
-        for (int e = threadIdx.x; e < SK * SB; e += 256) {
-            const int kk = e % SK, rr = e / SK;
-            const int m = m0 + rr, n = n0 + rr, k = k0 + kk;
-            float a = (m < g.M && k < K) ? g.A[int64_t(m) * g.lda + k] : 0.f;
-            if (g.round_a_f16) a = __half2float(__float2half_rn(a));
-            As[kk][rr] = a;
-            Ws[kk][rr] = (n < g.N && k < K) ? g.W[int64_t(n) * K + k] : 0.f;
+    for (int64_t tile = blockIdx.x + int64_t(blockIdx.y) * gridDim.x; tile < tiles; tile += int64_t(gridDim.x) * gridDim.y) {
+        const int m0 = int(tile / tiles_n) * SB, n0 = int(tile % tiles_n) * SB;
+        if (g.row_mask) {
+            const int m = m0 + int(threadIdx.x);
+            const bool mine = threadIdx.x < SB && m < g.M && g.row_mask[m] != 0;
+            if (!__syncthreads_or(mine)) continue;
         }
-        __syncthreads();
-        const int kend = min(SK, K - k0);
-        for (int kk = 0; kk < kend; ++kk) {
-            float a[4], w[4];
+        Acc sum[4][4], pan[4][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) { a[i] = As[kk][ty * 4 + i]; w[i] = Ws[kk][tx * 4 + i]; }
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int j = 0; j < 4; ++j) { sum[i][j] = 0; pan[i][j] = 0; }
+        for (int k0 = 0; k0 < K; k0 += SK) {
+            for (int e = threadIdx.x; e < SK * SB; e += 256) {
+                const int kk = e % SK, rr = e / SK;
+                const int m = m0 + rr, n = n0 + rr, k = k0 + kk;
+                float a = (m < g.M && k < K) ? g.A[int64_t(m) * g.lda + k] : 0.f;
+                if (g.round_a_f16) a = __half2float(__float2half_rn(a));
+                As[kk][rr] = a;
+                Ws[kk][rr] = (n < g.N && k < K) ? g.W[int64_t(n) * K + k] : 0.f;
+            }
+            __syncthreads();
+            const int kend = min(SK, K - k0);
+            for (int kk = 0; kk < kend; ++kk) {
+                float a[4], w[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if constexpr (ORDER == ORDER_F64) pan[i][j] = __dadd_rn(pan[i][j], __dmul_rn(double(w[j]), double(a[i])));
-                    else pan[i][j] = __fmaf_rn(w[j], a[i], pan[i][j]);
-                }
-            const int k = k0 + kk + 1;
-            if (panels && (k % 192 == 0 || k == K)) {
+                for (int i = 0; i < 4; ++i) { a[i] = As[kk][ty * 4 + i]; w[i] = Ws[kk][tx * 4 + i]; }
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) { sum[i][j] = sum[i][j] + pan[i][j]; pan[i][j] = 0; }
+                    for (int j = 0; j < 4; ++j) {
+                        if constexpr (ORDER == ORDER_F64) pan[i][j] = __dadd_rn(pan[i][j], __dmul_rn(double(w[j]), double(a[i])));
+                        else pan[i][j] = __fmaf_rn(w[j], a[i], pan[i][j]);
+                    }
+                const int k = k0 + kk + 1;
+                if (panels && (k % 192 == 0 || k == K)) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) { sum[i][j] = sum[i][j] + pan[i][j]; pan[i][j] = 0; }
+                }
             }
+            __syncthreads();
         }
-        __syncthreads();
-    }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int m = m0 + ty * 4 + i;
-        if (m >= g.M) continue;
-        const int64_t orow = g.row_group > 0 ? int64_t(m / g.row_group) * g.row_stride + g.row_offset + m % g.row_group : m;
+        for (int i = 0; i < 4; ++i) {
+            const int m = m0 + ty * 4 + i;
+            if (m >= g.M || (g.row_mask && g.row_mask[m] == 0)) continue;
+            const int64_t orow = g.row_group > 0 ? int64_t(m / g.row_group) * g.row_stride + g.row_offset + m % g.row_group : m;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int n = n0 + tx * 4 + j;
-            if (n >= g.N) continue;
-            float v = panels ? float(sum[i][j]) : float(pan[i][j]);
-            if (g.bias) v = __fadd_rn(v, g.bias[n]);
-            const int64_t o = orow * g.ldo + n;
-            switch (g.epi) {
-                case SEPI_F32: static_cast<float*>(g.out)[o] = v; break;
-                case SEPI_F16: static_cast<__half*>(g.out)[o] = __float2half_rn(v); break;
-                case SEPI_RESID: static_cast<float*>(g.out)[o] = __fadd_rn(static_cast<float*>(g.out)[o], v); break;
-                case SEPI_SILU_F32: static_cast<float*>(g.out)[o] = ref_silu(v); break;
-                case SEPI_SILU_F16: static_cast<__half*>(g.out)[o] = __float2half_rn(ref_silu(v)); break;
+            for (int j = 0; j < 4; ++j) {
+                const int n = n0 + tx * 4 + j;
+                if (n >= g.N) continue;
+                float v = panels ? float(sum[i][j]) : float(pan[i][j]);
+                if (g.bias) v = __fadd_rn(v, g.bias[n]);
+                const int64_t o = orow * g.ldo + n;
+                switch (g.epi) {
+                    case SEPI_F32: static_cast<float*>(g.out)[o] = v; break;
+                    case SEPI_F16: static_cast<__half*>(g.out)[o] = __float2half_rn(v); break;
+                    case SEPI_RESID: static_cast<float*>(g.out)[o] = __fadd_rn(static_cast<float*>(g.out)[o], v); break;
+                    case SEPI_SILU_F32: static_cast<float*>(g.out)[o] = ref_silu(v); break;
+                    case SEPI_SILU_F16: static_cast<__half*>(g.out)[o] = __float2half_rn(ref_silu(v)); break;
+                }
             }
         }
     }
@@ -767,8 +776,14 @@ cudaError_t feedback(const RowConfig& c, const float* rows, const int8_t* mask, 
 
 cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s) {
     if (g.M <= 0 || g.N <= 0) return cudaSuccess;
-    dim3 grid((g.N + SB - 1) / SB, (g.M + SB - 1) / SB);
-    if (grid.y > 65535) return cudaErrorInvalidValue;
+    // One tile per block; launches that are conditional on a device flag (only_if) or whose
+    // tile rows exceed the grid's y limit use a bounded grid that strides over the tiles.
+    const int64_t tm = (g.M + SB - 1) / SB;
+    dim3 grid((g.N + SB - 1) / SB, unsigned(tm));
+    if (g.only_if || tm > 65535) {
+        grid.x = 148 * 8;
+        grid.y = 1;
+    }
     switch (g.order) {
         case ORDER_PANEL192: simt_gemm_kernel<ORDER_PANEL192><<<grid, 256, 0, s>>>(g); break;
         case ORDER_CHAIN: simt_gemm_kernel<ORDER_CHAIN><<<grid, 256, 0, s>>>(g); break;
@@ -778,7 +793,7 @@ cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s) {
 }
 
 __global__ void split_f16_kernel(const float* __restrict__ a, int64_t n, int K, __half* __restrict__ out,
-                                 int* __restrict__ overflow) {
+                                 int* __restrict__ overflow, int8_t* __restrict__ row_overflow) {
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int64_t m = i / K;
@@ -790,13 +805,17 @@ __global__ void split_f16_kernel(const float* __restrict__ a, int64_t n, int K, 
     o[k] = hi;
     o[K + k] = hi;
     o[2 * K + k] = lo;
-    if (!(fabsf(v) <= 30000.f)) *overflow = 1;
+    if (!(fabsf(v) <= 30000.f)) {
+        *overflow = 1;
+        if (row_overflow) row_overflow[m] = 1;
+    }
 }
 
-cudaError_t split_f16(const float* a, int64_t rows, int K, __half* out, int* overflow, cudaStream_t s) {
+cudaError_t split_f16(const float* a, int64_t rows, int K, __half* out, int* overflow, int8_t* row_overflow,
+                      cudaStream_t s) {
     const int64_t n = rows * K;
     if (n <= 0) return cudaSuccess;
-    split_f16_kernel<<<blocks_for(n), TPB, 0, s>>>(a, n, K, out, overflow);
+    split_f16_kernel<<<blocks_for(n), TPB, 0, s>>>(a, n, K, out, overflow, row_overflow);
     return cudaGetLastError();
 }
 

@@ -101,6 +101,7 @@ struct SimtGemm {
     void* out = nullptr; int64_t ldo = 0;
     int row_group = 0, row_stride = 0, row_offset = 0;  // output row remap (as in GemmEpilogue)
     const int* only_if = nullptr;       // when set, the launch does nothing unless *only_if != 0
+    const int8_t* row_mask = nullptr;   // when set, only rows m with row_mask[m] != 0 are written
 };
 cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s);
 
@@ -108,8 +109,9 @@ cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s);
 // out[m] = [hi(a[m]) | hi(a[m]) | lo(a[m])] (3K f16 per row), hi = f16(a), lo = f16(a - hi).
 // With weights split as [hi(w) | lo(w) | hi(w)], a K = 3K f16 product sums
 // hi*hi + hi*lo + lo*hi (relative error ~2^-22). Any |a| > 30000 (outside the range where
-// the split is exact enough in f16) sets *overflow.
-cudaError_t split_f16(const float* a, int64_t rows, int K, __half* out, int* overflow, cudaStream_t s);
+// the split is exact enough in f16) sets *overflow and, when given, row_overflow[row].
+cudaError_t split_f16(const float* a, int64_t rows, int K, __half* out, int* overflow, int8_t* row_overflow,
+                      cudaStream_t s);
 
 // Read a device error word and reset it.
 int read_error(int* d_err, cudaStream_t s);

@@ -67,7 +67,7 @@ extern "C" TIMESTRAL_API int tsb_test_attention_time(const void* q, const void* 
 
 extern "C" TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, void* out, int32_t* d_overflow) {
     if (!a || !out || !d_overflow || rows < 0 || K <= 0) return TSB_ERR_ARG;
-    cudaError_t e = tsb::split_f16(a, rows, K, static_cast<__half*>(out), d_overflow, 0);
+    cudaError_t e = tsb::split_f16(a, rows, K, static_cast<__half*>(out), d_overflow, nullptr, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     return e == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
 }
