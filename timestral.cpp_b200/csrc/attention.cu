@@ -94,21 +94,21 @@ __device__ __forceinline__ bool variate_allowed(const MaskMeta& mm, int p, int q
 }
 
 // ---------------------------------------------------------------------------------------
-// Tensor-core time attention: one (row, head) problem at a time per CTA, several CTAs per SM.
+// Tensor-core time attention: one (row, head) problem at a time per CTA, four CTAs per SM.
 //
-// 128 threads, one query per thread. A warp can only read its own quarter of the TMEM lanes,
-// so the S queries are split into four runs of RQ = ceil(S / 4), one per lane quarter: query
-// q * RQ + l sits in lane 32 q + l, and all four warps (on all four SM sub-partitions) have
-// live queries. Thread 0 also issues the TMA loads and the two MMAs. Shared memory holds one
-// problem: Q [128 lanes][64] f16 (four TMA boxes of RQ rounded to 8 rows), K and V
-// [NK = S rounded to 16 rows][64] f16 (rows past S zero-filled by TMA), P [128][NK] f16 in
-// 64-key blocks (128-byte swizzle). Lanes without a query compute scores that are never used.
-// O = P V reuses the TMEM columns of S, so a CTA holds 128 columns and up to four CTAs share
-// an SM's TMEM.
+// 128 threads, one query row per thread (TMEM lane = query). Thread 0 also issues the TMA
+// loads and the two MMAs, so every warp computes. TMEM (128 columns per CTA):
+//   S = Q K^T in columns [0, NK); the softmax writes P (f16, two keys per column) over
+//   columns [0, NK/2) behind its reads of S; O = P V (P read from TMEM) in columns [64, 128).
+// Shared memory: Q [S rounded to 8 rows][64] f16 (the score MMA reads 128 rows from Q; rows
+// past S fall in the K region and only give scores of queries that do not exist), K and V
+// [NK = S rounded to 16 rows][64] f16 (rows past S zero-filled by TMA), and a 16 KB block in
+// which the epilogue turns its rows into full 128-byte stores.
 // Per problem: S = Q K^T -> Q/K of the next problem load -> softmax -> O = P V -> V of the
-// next problem loads -> epilogue (the TMEM of O is released before the stores).
+// next problem loads -> epilogue (the TMEM is released before the stores).
 constexpr int AT_THREADS = 128;
 constexpr uint32_t AT_TMEM_COLS = 128;
+constexpr uint32_t AT_O_COL = 64;
 
 struct AttnBars {
     uint64_t full_qk, full_v, s_full, p_ready, o_full, tm_free;
@@ -119,11 +119,9 @@ struct AttnBars {
 template <int NK>
 struct AttnLayout {
     static constexpr int KV_BYTES = NK * 128;
-    static constexpr int P_BLOCKS = (NK + 63) / 64;
-    static constexpr int P_BYTES = P_BLOCKS * 128 * 128;
-    __host__ __device__ static constexpr int run(int S) { return (S + 3) / 4; }                 // queries per lane quarter
-    __host__ __device__ static constexpr int q_box(int S) { return (run(S) + 7) / 8 * 8; }      // TMA box rows
-    static constexpr int SMEM = 128 * 128 + 2 * KV_BYTES + P_BYTES + 1024 + 256;
+    static constexpr int STAGE_BYTES = 128 * 128;
+    __host__ __device__ static constexpr int q_rows(int S) { return (S + 7) / 8 * 8; }
+    __host__ __device__ static constexpr int smem(int S) { return q_rows(S) * 128 + 2 * KV_BYTES + STAGE_BYTES + 1024 + 256; }
 };
 
 __device__ __forceinline__ bool at_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
@@ -149,6 +147,21 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
+// Eight consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// D (TMEM) (+)= A (TMEM, K-major f16) * B (shared memory descriptor).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, bool accumulate) {
+    const uint32_t z = 0;
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(uint32_t(accumulate)), "r"(z), "r"(z), "r"(z), "r"(z));
+}
 
 // 2^x with subnormal results flushed to zero (probabilities are relative to the row maximum
 // and rounded to f16, whose smallest subnormal is 2^-24).
@@ -159,19 +172,19 @@ __device__ __forceinline__ float exp2_ftz(float x) {
 }
 
 template <int NK>
-__global__ void __launch_bounds__(AT_THREADS, 3)
+__global__ void __launch_bounds__(AT_THREADS, 4)
     attn_time_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const __half* __restrict__ gate,
                         __half* __restrict__ out, int rows, int H, const MaskMeta mm, int* err) {
     using Lay = AttnLayout<NK>;
     extern __shared__ uint8_t smem_raw[];
     const int S = mm.S, D = H * 64;
-    const int RQ = Lay::run(S), QB = Lay::q_box(S);
+    const int QR = Lay::q_rows(S);
     uint8_t* qbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* kbuf = qbuf + 128 * 128;
+    uint8_t* kbuf = qbuf + QR * 128;
     uint8_t* vbuf = kbuf + Lay::KV_BYTES;
-    uint8_t* pbuf = vbuf + Lay::KV_BYTES;
-    AttnBars* bars = reinterpret_cast<AttnBars*>(pbuf + Lay::P_BYTES);
+    uint8_t* obuf = vbuf + Lay::KV_BYTES;
+    AttnBars* bars = reinterpret_cast<AttnBars*>(obuf + Lay::STAGE_BYTES);
     volatile int* abort = &bars->abort;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, t = threadIdx.x;
     const int num = rows * H;
@@ -188,13 +201,13 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tS = bars->tmem;              // S and, after the softmax, O
+    const uint32_t tS = bars->tmem;                       // S, then P over its first NK/2 columns
+    const uint32_t tO = tS + AT_O_COL;
     const uint32_t lane_base = uint32_t(warp * 32) << 16;
 
     auto issue_qk = [&](int prob) {
-        mbar_arrive_expect_tx(&bars->full_qk, 4 * QB * 128 + Lay::KV_BYTES);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) tma_load_3d(qbuf + q * 32 * 128, &map_q, &bars->full_qk, 0, q * RQ, prob);
+        mbar_arrive_expect_tx(&bars->full_qk, QR * 128 + Lay::KV_BYTES);
+        tma_load_3d(qbuf, &map_q, &bars->full_qk, 0, 0, prob);
         tma_load_3d(kbuf, &map_k, &bars->full_qk, 0, 0, prob);
     };
     auto issue_v = [&](int prob) {
@@ -227,10 +240,9 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
             }
             if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         }
-        const int qi = warp * RQ + lane;               // this thread's query
-        const bool live = lane < RQ && qi < S;
+        const bool live = t < S;
         uint32_t allowed[4];
-        key_set(mm, r, qi, live, allowed);
+        key_set(mm, r, t, live, allowed);
         // Highest key any query of this warp attends: key chunks above it are skipped
         // (written as zero probabilities), which halves the work of causal rows.
         int hi = -1;
@@ -243,62 +255,69 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
         if (ctl && next < num) issue_qk(next);         // Q and K are free once S is complete
         float sum = 0.f;
         if (kmax >= 0) {
-            float sc[NK];
+            // Pass 1: the row maximum over the query's keys (eight partial maxima).
+            float mxj[8];
 #pragma unroll
-            for (int c = 0; c < NK / 16; ++c)
-                if (c * 16 <= kmax) tmem_ld16(tS + lane_base + c * 16, *reinterpret_cast<uint32_t(*)[16]>(&sc[c * 16]));
-            tmem_ld_wait();
-            // Keys outside the query's set score -inf; the row maximum is over its own keys.
-            float mx = -INFINITY;
+            for (int j = 0; j < 8; ++j) mxj[j] = -INFINITY;
 #pragma unroll
-            for (int k0 = 0; k0 < NK; k0 += 8) {
-                if (k0 <= kmax) {
-                    const uint32_t bits = allowed[k0 >> 5] >> (k0 & 31);
+            for (int c = 0; c < NK / 16; ++c) {
+                if (c * 16 > kmax) break;
+                uint32_t sc[16];
+                tmem_ld16(tS + lane_base + c * 16, sc);
+                tmem_ld_wait();
+                const uint32_t bits = allowed[(c * 16) >> 5] >> ((c * 16) & 31);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        sc[k0 + j] = (bits >> j) & 1u ? sc[k0 + j] : -INFINITY;
-                        mx = fmaxf(mx, sc[k0 + j]);
-                    }
-                }
+                for (int j = 0; j < 16; ++j)
+                    if ((bits >> j) & 1u) mxj[j & 7] = fmaxf(mxj[j & 7], __uint_as_float(sc[j]));
             }
+            const float mx = fmaxf(fmaxf(fmaxf(mxj[0], mxj[1]), fmaxf(mxj[2], mxj[3])),
+                                   fmaxf(fmaxf(mxj[4], mxj[5]), fmaxf(mxj[6], mxj[7])));
             const float off = live ? mx * kScaleLog2e : 0.f;
-            // probabilities in f16 in the 128-byte swizzle, and their sum
+            // Pass 2: probabilities in f16, two keys per TMEM column over the columns of S
+            // already read (P columns [8c, 8c + 8) <= S columns [16c, 16c + 16)), and their sum.
+            float sj[8];
 #pragma unroll
-            for (int k0 = 0; k0 < NK; k0 += 8) {
-                uint4 u = make_uint4(0u, 0u, 0u, 0u);
-                if (k0 <= kmax) {
-                    float p[8];
+            for (int j = 0; j < 8; ++j) sj[j] = 0.f;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        p[j] = exp2_ftz(__fmaf_rn(sc[k0 + j], kScaleLog2e, -off));
-                        sum += p[j];
+            for (int c = 0; c < NK / 16; ++c) {
+                uint32_t pk[8];
+                if (c * 16 <= kmax) {
+                    uint32_t sc[16];
+                    tmem_ld16(tS + lane_base + c * 16, sc);
+                    tmem_ld_wait();
+                    const uint32_t bits = allowed[(c * 16) >> 5] >> ((c * 16) & 31);
+                    float p[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        p[j] = (bits >> j) & 1u ? exp2_ftz(__fmaf_rn(__uint_as_float(sc[j]), kScaleLog2e, -off)) : 0.f;
+                        sj[j & 7] += p[j];
                     }
-                    u.x = pack_half2(p[0], p[1]); u.y = pack_half2(p[2], p[3]);
-                    u.z = pack_half2(p[4], p[5]); u.w = pack_half2(p[6], p[7]);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) pk[j] = pack_half2(p[2 * j], p[2 * j + 1]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) pk[j] = 0u;
                 }
-                const int blk = k0 / 64, chunk = (k0 % 64) / 8;
-                *reinterpret_cast<uint4*>(pbuf + blk * 16384 + t * 128 + ((chunk ^ (t & 7)) << 4)) = u;
+                tmem_st8(tS + lane_base + c * 8, pk);
             }
+            tmem_st_wait();
+            sum = ((sj[0] + sj[1]) + (sj[2] + sj[3])) + ((sj[4] + sj[5]) + (sj[6] + sj[7]));
         }
-        fence_proxy_async();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->p_ready);
         if (warp == 0) {
-            // O = P V once every warp's P rows and this problem's V are in shared memory.
+            // O = P V once every warp's P rows are in TMEM and this problem's V is resident.
             int ok = 1;
             if (lane == 0) {
                 ok = at_wait(&bars->p_ready, ph, abort, err) && at_wait(&bars->full_v, ph, abort, err);
                 if (ok) {
                     tc_fence_after();
-                    const uint32_t sp = smem_u32(pbuf), sv = smem_u32(vbuf);
+                    const uint32_t sv = smem_u32(vbuf);
                     const uint32_t id2 = idesc_f16_bmn(128, 64);
 #pragma unroll
-                    for (int kk = 0; kk < NK / 16; ++kk) {
-                        const uint64_t da = smem_desc_sw128(sp + (kk / 4) * 16384) + uint64_t(2 * (kk % 4));
-                        const uint64_t dv = smem_desc_sw128(sv + kk * 16 * 128);
-                        mma_f16(tS, da, dv, id2, kk > 0);
-                    }
+                    for (int kk = 0; kk < NK / 16; ++kk)
+                        mma_f16_ts(tO, tS + kk * 8, smem_desc_sw128(sv + kk * 16 * 128), id2, kk > 0);
                     mma_commit(&bars->o_full);
                 }
             }
@@ -306,7 +325,7 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
         }
         // gate row of this query, fetched while O = P V runs
         uint4 gv[8];
-        const __half* g = (gate && live) ? gate + ((int64_t(r) * H + h) * S + qi) * 64 : nullptr;
+        const __half* g = (gate && live) ? gate + ((int64_t(r) * H + h) * S + t) * 64 : nullptr;
         if (g) {
 #pragma unroll
             for (int c = 0; c < 8; ++c) gv[c] = *reinterpret_cast<const uint4*>(g + c * 8);
@@ -314,9 +333,8 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
         if (!warp_wait(&bars->o_full, ph, abort, err)) break;
         tc_fence_after();
         if (ctl && next < num) issue_v(next);          // V is free once O is complete
-        // O * (1/sum) * gate in f16, staged row-wise in P block 0 (free once O is complete)
-        // and stored eight threads per 128-byte output row. The TMEM of O is released as soon
-        // as its second half is in registers.
+        // O * (1/sum) * gate in f16, staged row-wise and stored eight threads per 128-byte
+        // output row. The TMEM is released as soon as O's second half is in registers.
         const float inv = live ? 1.0f / sum : 0.f;
         auto stage = [&](const uint32_t (&o)[32], int half32) {
 #pragma unroll
@@ -337,29 +355,29 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
                 uint4 u;
                 u.x = pack_half2(y[0], y[1]); u.y = pack_half2(y[2], y[3]);
                 u.z = pack_half2(y[4], y[5]); u.w = pack_half2(y[6], y[7]);
-                *reinterpret_cast<uint4*>(pbuf + t * 128 + ((c ^ (t & 7)) << 4)) = u;
+                *reinterpret_cast<uint4*>(obuf + t * 128 + ((c ^ (t & 7)) << 4)) = u;
             }
         };
         uint32_t o[32];
         if (kmax >= 0) {
-            tmem_ld32(tS + lane_base, o);
+            tmem_ld32(tO + lane_base, o);
             tmem_ld_wait();
             stage(o, 0);
-            tmem_ld32(tS + lane_base + 32, o);
+            tmem_ld32(tO + lane_base + 32, o);
             tmem_ld_wait();
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->tm_free);    // the next S may overwrite O
+        if (lane == 0) mbar_arrive(&bars->tm_free);    // the next S may overwrite P and O
         if (kmax < 0) continue;
         stage(o, 1);
         __syncwarp();
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int li = j * 4 + (lane >> 3), chunk = lane & 7, row = warp * 32 + li, q = warp * RQ + li;
-            if (li < RQ && q < S)
-                *reinterpret_cast<uint4*>(out + (int64_t(r) * S + q) * D + h * 64 + chunk * 8) =
-                    *reinterpret_cast<const uint4*>(pbuf + row * 128 + ((chunk ^ (row & 7)) << 4));
+            const int row = warp * 32 + j * 4 + (lane >> 3), chunk = lane & 7;
+            if (row < S)
+                *reinterpret_cast<uint4*>(out + (int64_t(r) * S + row) * D + h * 64 + chunk * 8) =
+                    *reinterpret_cast<const uint4*>(obuf + row * 128 + ((chunk ^ (row & 7)) << 4));
         }
         __syncwarp();
     }
@@ -373,23 +391,25 @@ template <int NK>
 cudaError_t launch_attn_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
                            int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
     using Lay = AttnLayout<NK>;
-    const int smem = Lay::SMEM;
+    const int smem = Lay::smem(mm.S);
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(attn_time_tc_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        // The largest request of this key count (S = NK) so later calls need no update.
+        cudaError_t e = cudaFuncSetAttribute(attn_time_tc_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Lay::smem(NK));
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
     CUtensorMap mq, mk, mv;
     const int64_t planes = int64_t(rows) * H;
-    if (!make_map_3d_f16(&mq, q, planes, mm.S, Lay::q_box(mm.S)) || !make_map_3d_f16(&mk, k, planes, mm.S, NK) ||
+    if (!make_map_3d_f16(&mq, q, planes, mm.S, Lay::q_rows(mm.S)) || !make_map_3d_f16(&mk, k, planes, mm.S, NK) ||
         !make_map_3d_f16(&mv, v, planes, mm.S, NK))
         return cudaErrorInvalidValue;
-    // CTAs per SM: shared memory (227 KB), TMEM (512 columns) and the launch bounds (3).
+    // CTAs per SM: shared memory (227 KB), TMEM (512 columns, 128 per CTA) and the launch bounds.
     int per_sm = (227 * 1024) / smem;
-    if (per_sm > 3) per_sm = 3;
+    if (per_sm > 4) per_sm = 4;
     if (per_sm < 1) per_sm = 1;
     int grid = device_sm_count() * per_sm;
     if (int64_t(grid) > planes) grid = int(planes);
