@@ -1,15 +1,22 @@
-// Persistent tcgen05 GEMM for sm_100a with fused epilogues.
+// Persistent tcgen05 GEMM for sm_100a with fused epilogues, on CTA pairs.
 //
 // Replaces the reference's projection nodes (src/layers.cpp:250-256 affine, 682-687 swiglu,
 // src/head.cpp:275-286 head/patch projections, src/weight_policy.hpp:23-30 reduced
 // projection), which on the reference's F16/Q8_0 path round activations to F16 and
 // accumulate F16 products in F32 — the same arithmetic as kind::f16 with f32 accumulators.
 //
-// Tile 128 x BN x 64 (f16, 128-byte swizzle), STAGES-deep TMA ring, two TMEM accumulators
-// so the epilogue of tile i overlaps the MMAs of tile i+1. Warp roles (320 threads):
-//   warp 0: TMA producer (one lane)      warp 1: TMEM owner + MMA issuer (one lane)
-//   warps 2..9: epilogue, one accumulator row per thread (TMEM lane quarter = warp % 4),
-//   warps 2..5 take the first half of the tile's columns and warps 6..9 the second.
+// Two CTAs of a cluster compute one 256 x 256 tile with tcgen05.mma.cta_group::2: CTA r holds
+// rows [128 r, 128 r + 128) of the A tile and rows [128 r, 128 r + 128) of the B tile (the
+// tile's columns) in its shared memory, and its TMEM receives the accumulator rows of its A
+// half over all 256 columns. Each SM thus streams 32 KB per 64-deep K step instead of the
+// 48 KB a single-CTA 128 x 256 tile needs, which is what lets the tensor pipe run near its
+// peak on shared-memory bandwidth. No load uses multicast.
+//
+// Per CTA (320 threads): warp 0 lane 0 loads both operand halves (CTA 0 also expects the
+// pair's transaction bytes on its full barrier); warp 1 owns the TMEM (two 256-column
+// accumulators) and, in CTA 0, issues the MMAs and commits to both CTAs' barriers; warps 2..9
+// are the epilogue (TMEM lane quarter = warp % 4, column half = (warp - 2) / 4), and release
+// an accumulator by arriving on CTA 0's accumulator-empty barrier.
 // Every mbarrier wait is bounded; a timeout records a device error and unwinds.
 #include "common.cuh"
 #include "gemm_tc.cuh"
@@ -21,12 +28,13 @@ namespace tsb {
 
 namespace {
 
-constexpr int BM = 128;
+constexpr int BM = 128;                       // accumulator rows per CTA (256 per pair)
 constexpr int BK = 64;
-constexpr int BN = 256;
-constexpr int STAGES = 4;
+constexpr int BN = 256;                       // tile columns
+constexpr int BN_HALF = BN / 2;               // B rows held by each CTA
+constexpr int STAGES = 6;
 constexpr int A_BYTES = BM * BK * 2;          // 16 KB
-constexpr int B_BYTES = BN * BK * 2;          // 32 KB
+constexpr int B_BYTES = BN_HALF * BK * 2;     // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;             // 512: two accumulators
 constexpr int EPI_WARPS = 8;                 // two warps per TMEM lane quarter, one per column half
@@ -316,45 +324,49 @@ __global__ void __launch_bounds__(THREADS, 1)
     volatile int* abort = &sm->abort;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int m_tiles = (g.M + BM - 1) / BM, n_tiles = (g.N + BN - 1) / BN;
+    const uint32_t rank = cluster_ctarank();          // 0: issues the MMAs
+    const int pair = blockIdx.x / 2, pairs = gridDim.x / 2;
+    const int m_tiles = (g.M + 2 * BM - 1) / (2 * BM), n_tiles = (g.N + BN - 1) / BN;
     const int num_tiles = m_tiles * n_tiles;
     const int k_blocks = (g.K + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&sm->full[s], 1); mbar_init(&sm->empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(&sm->acc_full[b], 1); mbar_init(&sm->acc_empty[b], EPI_WARPS); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&sm->acc_full[b], 1); mbar_init(&sm->acc_empty[b], 2 * EPI_WARPS); }
         sm->abort = 0;
         mbar_fence_init();
         fence_proxy_async();
     }
     if (warp == 0 && lane == 0) { tma_prefetch_desc(&map_a); tma_prefetch_desc(&map_b); }
-    if (warp == 1) { tmem_alloc(&sm->tmem_base, TMEM_COLS); tmem_relinquish(); }
+    if (warp == 1) { tmem_alloc_pair(&sm->tmem_base, TMEM_COLS); tmem_relinquish_pair(); }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();                                   // barriers of both CTAs initialised
     tc_fence_after();
     const uint32_t tmem = sm->tmem_base;
 
     if (warp == 0) {
         if (lane == 0) {
             uint32_t it = 0;
-            for (int tile = blockIdx.x; tile < num_tiles && !*abort; tile += gridDim.x) {
-                const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+            for (int tile = pair; tile < num_tiles && !*abort; tile += pairs) {
+                const int m0 = (tile / n_tiles) * 2 * BM + int(rank) * BM;
+                const int n0 = (tile % n_tiles) * BN + int(rank) * BN_HALF;
                 for (int kb = 0; kb < k_blocks; ++kb, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
                     if (!wait_or_abort(&sm->empty[s], ph ^ 1, abort, err, kDevTimeoutEmpty)) break;
                     uint8_t* a = tiles + s * STAGE_BYTES;
-                    mbar_arrive_expect_tx(&sm->full[s], STAGE_BYTES);
-                    tma_load_2d(a, &map_a, &sm->full[s], kb * BK, m0);
-                    tma_load_2d(a + A_BYTES, &map_b, &sm->full[s], kb * BK, n0);
+                    if (rank == 0) mbar_arrive_expect_tx(&sm->full[s], 2 * STAGE_BYTES);
+                    const uint32_t full0 = mapa_shared(smem_u32(&sm->full[s]), 0);
+                    tma_load_2d_pair(a, &map_a, full0, kb * BK, m0);
+                    tma_load_2d_pair(a + A_BYTES, &map_b, full0, kb * BK, n0);
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && rank == 0) {
             uint32_t it = 0, acc = 0;
-            const uint32_t idesc = idesc_f16(BM, BN);
-            for (int tile = blockIdx.x; tile < num_tiles && !*abort; tile += gridDim.x, ++acc) {
+            const uint32_t idesc = idesc_f16(2 * BM, BN);
+            for (int tile = pair; tile < num_tiles && !*abort; tile += pairs, ++acc) {
                 const int b = acc & 1;
                 const uint32_t aph = (acc >> 1) & 1;
                 if (!wait_or_abort(&sm->acc_empty[b], aph ^ 1, abort, err, kDevTimeoutAccEmpty)) break;
@@ -370,18 +382,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint64_t adesc = smem_desc_sw128(a_addr), bdesc = smem_desc_sw128(a_addr + A_BYTES);
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
-                        mma_f16(d, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), idesc, (kb | k) != 0);
-                    mma_commit(&sm->empty[s]);
+                        mma_f16_pair(d, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), idesc, (kb | k) != 0);
+                    mma_commit_pair(&sm->empty[s]);
                 }
                 if (!ok) break;
-                mma_commit(&sm->acc_full[b]);
+                mma_commit_pair(&sm->acc_full[b]);
             }
         }
     } else {
         const int quarter = warp & 3;         // TMEM lanes this warp may read
         const int half = (warp - 2) / 4;      // column half of the tile
+        const uint32_t acc_empty0 = mapa_shared(smem_u32(&sm->acc_empty[0]), 0);
+        const uint32_t acc_empty1 = mapa_shared(smem_u32(&sm->acc_empty[1]), 0);
         uint32_t acc = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++acc) {
+        for (int tile = pair; tile < num_tiles; tile += pairs, ++acc) {
             const int b = acc & 1;
             const uint32_t aph = (acc >> 1) & 1;
             bool ok = true;
@@ -390,18 +404,18 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!ok) break;
             __syncwarp();
             tc_fence_after();
-            const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+            const int m0 = (tile / n_tiles) * 2 * BM + int(rank) * BM, n0 = (tile % n_tiles) * BN;
             const uint32_t tacc = tmem + (uint32_t(quarter * 32) << 16) + b * BN;
             epilogue_tile<KIND>(g, tacc, m0, n0, quarter, lane, half, stage + (warp - 2) * 32 * 128);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm->acc_empty[b]);
+            if (lane == 0) mbar_arrive_cluster(b ? acc_empty1 : acc_empty0);
         }
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();                                   // no CTA leaves while its pair may touch it
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+    if (warp == 1) tmem_dealloc_pair(tmem, TMEM_COLS);
 }
 
 // --- host side ---------------------------------------------------------------------------
@@ -475,12 +489,25 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
         configured[dev] = true;
     }
     CUtensorMap ma, mb;
-    if (!make_map_2d_f16(&ma, a.A, a.M, a.K, a.lda, BM) || !make_map_2d_f16(&mb, a.B, a.N, a.K, a.ldb, BN))
+    if (!make_map_2d_f16(&ma, a.A, a.M, a.K, a.lda, BM) || !make_map_2d_f16(&mb, a.B, a.N, a.K, a.ldb, BN_HALF))
         return cudaErrorInvalidValue;
-    const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-    const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
-    tc_gemm_kernel<KIND><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, a, err);
-    return cudaGetLastError();
+    // One CTA pair (cluster of two) per two SMs, persistent over the 256 x 256 tiles.
+    const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN);
+    const int max_pairs = device_sm_count() / 2;
+    const int pairs = tiles < max_pairs ? tiles : max_pairs;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<KIND>, ma, mb, a, err);
 }
 
 cudaError_t tc_gemm(EpiKind kind, const GemmArgs& a, cudaStream_t stream, int* err) {

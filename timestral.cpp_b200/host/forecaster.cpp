@@ -4,10 +4,17 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstring>
 #include <limits>
+#include <thread>
+#include <vector>
 
 #include <cuda_runtime.h>
+#ifdef __linux__
+#include <sys/mman.h>
+#include <unistd.h>
+#endif
 
 namespace ts {
 
@@ -233,6 +240,7 @@ struct Forecaster::Staging {
     void* ctx = nullptr; size_t ctx_bytes = 0;
     void* mask = nullptr; size_t mask_bytes = 0;
     void* out = nullptr; size_t out_bytes = 0;
+    void* host_out = nullptr; size_t host_out_bytes = 0;   // pinned: the download lands here
     static void grow(void*& p, size_t& have, size_t need) {
         if (need <= have) return;
         if (p) cudaFree(p);
@@ -241,12 +249,54 @@ struct Forecaster::Staging {
         cuda_check(cudaMalloc(&p, need), "cudaMalloc staging");
         have = need;
     }
+    static void grow_host(void*& p, size_t& have, size_t need) {
+        if (need <= have) return;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        have = 0;
+        cuda_check(cudaMallocHost(&p, need), "cudaMallocHost staging");
+        have = need;
+    }
     ~Staging() {
         if (ctx) cudaFree(ctx);
         if (mask) cudaFree(mask);
         if (out) cudaFree(out);
+        if (host_out) cudaFreeHost(host_out);
     }
 };
+
+namespace {
+// Copy a large result from pinned staging into the caller's (typically freshly allocated,
+// not yet faulted-in) buffer: large buffers are asked for transparent huge pages and are
+// written by several threads, so first-touch page faults run in parallel.
+void copy_out(float* dst, const float* src, size_t n) {
+    const size_t bytes = n * sizeof(float);
+    constexpr size_t kParallelBytes = size_t(8) << 20;
+    if (bytes < kParallelBytes) {
+        std::memcpy(dst, src, bytes);
+        return;
+    }
+#ifdef __linux__
+    {
+        const uintptr_t page = uintptr_t(sysconf(_SC_PAGESIZE));
+        const uintptr_t lo = (reinterpret_cast<uintptr_t>(dst) + page - 1) & ~(page - 1);
+        const uintptr_t hi = (reinterpret_cast<uintptr_t>(dst) + bytes) & ~(page - 1);
+        if (hi > lo) madvise(reinterpret_cast<void*>(lo), hi - lo, MADV_HUGEPAGE);
+    }
+#endif
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const size_t threads = std::min<size_t>(std::min<size_t>(hw, 16), bytes / (size_t(4) << 20));
+    const size_t per = (n + threads - 1) / threads;
+    std::vector<std::thread> pool;
+    pool.reserve(threads);
+    for (size_t t = 0; t < threads; ++t) {
+        const size_t b = t * per, e = std::min(n, b + per);
+        if (b >= e) break;
+        pool.emplace_back([=] { std::memcpy(dst + b, src + b, (e - b) * sizeof(float)); });
+    }
+    for (auto& th : pool) th.join();
+}
+}  // namespace
 
 Forecaster::Forecaster(const Model& model, int device) : model_(model), staging_(new Staging) {
     int dev = device;
@@ -284,8 +334,10 @@ void Forecaster::forecast_targets(const float* context, const uint8_t* mask, siz
     try {
         eng.forecast_targets(static_cast<float*>(st.ctx), mask ? static_cast<uint8_t*>(st.mask) : nullptr, int(B), int(V),
                              int(T), int(H), sym, clip, int(max_context), static_cast<float*>(st.out), false);
-        cuda_check(cudaMemcpyAsync(out, st.out, no * 4, cudaMemcpyDeviceToHost, s), "download forecast");
+        Staging::grow_host(st.host_out, st.host_out_bytes, no * 4);
+        cuda_check(cudaMemcpyAsync(st.host_out, st.out, no * 4, cudaMemcpyDeviceToHost, s), "download forecast");
         eng.check_errors();
+        copy_out(out, static_cast<const float*>(st.host_out), no);
     } catch (const Error&) {
         throw;
     } catch (const std::exception& e) {

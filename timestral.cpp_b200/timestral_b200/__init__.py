@@ -5,6 +5,7 @@ when the CUDA library has not been built.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 from pathlib import Path
 
 import numpy as np
@@ -151,11 +152,11 @@ class Model:
         ptr = L.timestral_capi_forecast(self.h, C.byref(r), C.byref(q))
         if not ptr:
             raise TimestralError(self.last_error)
-        try:
-            out = np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_float)), shape=(B, V, H, q.value)).copy()
-        finally:
-            L.timestral_capi_free_buffer(ptr)
-        return out
+        # The array views the library's buffer (no copy); the buffer is released with
+        # timestral_capi_free_buffer when the last view of it goes away.
+        buf = (C.c_float * (B * V * H * q.value)).from_address(ptr)
+        weakref.finalize(buf, L.timestral_capi_free_buffer, C.c_void_p(ptr))
+        return np.ctypeslib.as_array(buf).reshape(B, V, H, q.value)
 
     def forecast_device(self, d_context: int, d_mask: int | None, B, V, T, H, d_out: int,
                         symmetric=-1, clip=-1, max_context=0, asynchronous=False):
