@@ -135,9 +135,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t ran
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
     return r;
 }
-// Arrive on an mbarrier given by its shared::cluster address (possibly in the peer CTA).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+// Arrive on an mbarrier given by its shared::cluster address (possibly in the peer CTA),
+// without release semantics: the arrival orders no memory writes of the caller, so it does
+// not wait for the caller's outstanding global stores (used to hand back TMEM whose reads
+// have completed, tcgen05.wait::ld).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // Every thread of both CTAs of the cluster.
 __device__ __forceinline__ void cluster_sync() {

@@ -409,7 +409,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             epilogue_tile<KIND>(g, tacc, m0, n0, quarter, lane, half, stage + (warp - 2) * 32 * 128);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(b ? acc_empty1 : acc_empty0);
+            if (lane == 0) mbar_arrive_cluster_relaxed(b ? acc_empty1 : acc_empty0);
         }
     }
     tc_fence_before();
