@@ -12,11 +12,11 @@
 // 48 KB a single-CTA 128 x 256 tile needs, which is what lets the tensor pipe run near its
 // peak on shared-memory bandwidth. No load uses multicast.
 //
-// Per CTA (320 threads): warp 0 lane 0 loads both operand halves (CTA 0 also expects the
-// pair's transaction bytes on its full barrier); warp 1 owns the TMEM (two 256-column
-// accumulators) and, in CTA 0, issues the MMAs and commits to both CTAs' barriers; warps 2..9
-// are the epilogue (TMEM lane quarter = warp % 4, column half = (warp - 2) / 4), and release
-// an accumulator by arriving on CTA 0's accumulator-empty barrier.
+// Per CTA: warp 0 lane 0 loads both operand halves (CTA 0 also expects the pair's
+// transaction bytes on its full barrier); warp 1 owns the TMEM (two 256-column accumulators)
+// and, in CTA 0, issues the MMAs and commits to both CTAs' barriers; warps 2.. are the
+// epilogue (TMEM lane quarter = warp % 4, column group = (warp - 2) / 4), and release an
+// accumulator by arriving on CTA 0's accumulator-empty barrier.
 // Every mbarrier wait is bounded; a timeout records a device error and unwinds.
 #include "common.cuh"
 #include "gemm_tc.cuh"
@@ -32,16 +32,29 @@ constexpr int BM = 128;                       // accumulator rows per CTA (256 p
 constexpr int BK = 64;
 constexpr int BN = 256;                       // tile columns
 constexpr int BN_HALF = BN / 2;               // B rows held by each CTA
-constexpr int STAGES = 6;
 constexpr int A_BYTES = BM * BK * 2;          // 16 KB
 constexpr int B_BYTES = BN_HALF * BK * 2;     // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;             // 512: two accumulators
-constexpr int EPI_WARPS = 8;                 // two warps per TMEM lane quarter, one per column half
-constexpr int THREADS = 64 + 32 * EPI_WARPS;
-constexpr int EPI_STAGE_BYTES = EPI_WARPS * 32 * 128;   // per-warp transposition blocks
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
+// Per epilogue kind: PARTS column groups per TMEM lane quarter (epilogue warps = 4 * PARTS).
+// The q/k/v/gate epilogue (RoPE tables in registers) and the residual add (residual rows in
+// registers; bound by its residual traffic or by a long K) run two groups of 128 columns;
+// the activation and plain-store epilogues run four groups of 64, which doubles the warps
+// that hide the epilogue's latency at 96 registers a thread; their staging blocks leave room
+// for five operand stages instead of six.
+template <int KIND>
+struct Cfg {
+    static constexpr int PARTS = (KIND == EPI_QKVG || KIND == EPI_RESID) ? 2 : 4;
+    static constexpr int EPI_WARPS = 4 * PARTS;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int STAGES = PARTS == 2 ? 6 : 5;
+    static constexpr int EPI_STAGE_BYTES = EPI_WARPS * 32 * 128;   // per-warp transposition blocks
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+};
+
+template <int STAGES>
 struct Smem {
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
@@ -108,37 +121,46 @@ __device__ __forceinline__ void pack32(const float* v, uint32_t* w) {
 }
 
 // Epilogue of one 128 x BN accumulator for one warp: accumulator rows [mw, mw + 32) (its
-// TMEM lane quarter) and columns [half * BN/2, (half + 1) * BN/2).
-template <int KIND>
+// TMEM lane quarter) and column group `part` of PARTS.
+template <int KIND, int PARTS>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, int m0, int n0, int quarter, int lane,
-                                              int half, uint8_t* buf) {
+                                              int part, uint8_t* buf) {
+    const int half = part;
     const GemmEpilogue& e = g.epi;
     const int mw = m0 + quarter * 32;
     // Rows this thread stores after the transpose: mw + i * 4 + lane / 8, i = 0..7.
-    int64_t orow[8];
+    int orow[8];
     bool rok[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int m = mw + i * 4 + (lane >> 3);
         rok[i] = m < g.M;
-        orow[i] = rok[i] ? out_row(e, m) : 0;
+        orow[i] = rok[i] ? int(out_row(e, m)) : 0;
     }
     uint32_t w[32];
     if constexpr (KIND == EPI_F32 || KIND == EPI_RESID) {
         // 32 f32 columns per staging pass; the thread stores columns col .. col + 3.
-        constexpr int C = BN / 64;
-        float4 rs[2][8];
+        constexpr int C = BN / PARTS / 32;
+        // Residual rows: with two column groups the next chunk's rows are requested while the
+        // current chunk is stored; with four, each chunk's rows are requested ahead of its
+        // TMEM read (the doubled warp count covers the latency, and registers are fewer).
+        constexpr int RB = PARTS == 2 ? 2 : 1;
+        float4 rs[RB][8];
         auto load_resid = [&](int c, float4 (&dst)[8]) {
             const int col = n0 + (half * C + c) * 32 + (lane & 7) * 4;
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-                if (rok[i] && col < g.N) dst[i] = *reinterpret_cast<const float4*>(e.resid + orow[i] * e.ldo + col);
+                if (rok[i] && col < g.N) dst[i] = *reinterpret_cast<const float4*>(e.resid + int64_t(orow[i]) * e.ldo + col);
         };
-        if constexpr (KIND == EPI_RESID) load_resid(0, rs[0]);
+        if constexpr (KIND == EPI_RESID && RB == 2) load_resid(0, rs[0]);
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             if constexpr (KIND == EPI_RESID) {
-                if (c + 1 < C) load_resid(c + 1, rs[(c + 1) & 1]);
+                if constexpr (RB == 2) {
+                    if (c + 1 < C) load_resid(c + 1, rs[(c + 1) & 1]);
+                } else {
+                    load_resid(c, rs[0]);
+                }
             }
             tmem_ld32(tacc + (half * C + c) * 32, w);
             tmem_ld_wait();
@@ -152,15 +174,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
                     if (!rok[i]) continue;
                     float4 v = f4(unstage(buf, i, lane));
                     if (e.bias) v = add4(v, b);
-                    if constexpr (KIND == EPI_RESID) v = add4(rs[c & 1][i], v);
-                    *reinterpret_cast<float4*>(static_cast<float*>(e.out) + orow[i] * e.ldo + col) = v;
+                    if constexpr (KIND == EPI_RESID) v = add4(rs[c % RB][i], v);
+                    *reinterpret_cast<float4*>(static_cast<float*>(e.out) + int64_t(orow[i]) * e.ldo + col) = v;
                 }
             }
             __syncwarp();
         }
     } else if constexpr (KIND == EPI_F16 || KIND == EPI_SILU) {
         // 64 columns (two TMEM reads) per staging pass; the thread stores 8 f16 columns.
-        constexpr int C = BN / 128;
+        constexpr int C = BN / PARTS / 64;
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             const int cb = n0 + (half * C + c) * 64;
@@ -190,14 +212,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
             if (col < g.N) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
-                    if (rok[i]) *reinterpret_cast<uint4*>(static_cast<__half*>(e.out) + orow[i] * e.ldo + col) = unstage(buf, i, lane);
+                    if (rok[i]) *reinterpret_cast<uint4*>(static_cast<__half*>(e.out) + int64_t(orow[i]) * e.ldo + col) = unstage(buf, i, lane);
             }
             __syncwarp();
         }
     } else if constexpr (KIND == EPI_SWIGLU || KIND == EPI_VGATE) {
         // The first half of the tile holds the first operand, the second half the second:
-        // each 32-column pair gives 32 outputs, two pairs fill one 64-column staging pass.
-        constexpr int C = BN / 128;
+        // each 32-column pair gives 32 outputs (64 bytes of a staging row); a group holds C pairs.
+        constexpr int C = BN / 2 / PARTS / 32;
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             const int cc = half * C + c;
@@ -224,12 +246,25 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
             }
         }
         __syncwarp();
-        const int col = n0 / 2 + half * 64 + (lane & 7) * 8;
+        if constexpr (C == 2) {
+            const int col = n0 / 2 + half * 64 + (lane & 7) * 8;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            if (rok[i]) *reinterpret_cast<uint4*>(static_cast<__half*>(e.out) + orow[i] * e.ldo + col) = unstage(buf, i, lane);
+            for (int i = 0; i < 8; ++i)
+                if (rok[i]) *reinterpret_cast<uint4*>(static_cast<__half*>(e.out) + int64_t(orow[i]) * e.ldo + col) = unstage(buf, i, lane);
+        } else {
+            // 64-byte rows: four threads per row, eight rows per instruction.
+            const int col = n0 / 2 + half * 32 + (lane & 3) * 8;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int row = i * 8 + (lane >> 2), chunk = lane & 3, m = mw + row;
+                if (m < g.M)
+                    *reinterpret_cast<uint4*>(static_cast<__half*>(e.out) + out_row(e, m) * e.ldo + col) =
+                        *reinterpret_cast<const uint4*>(buf + row * STAGE_ROW_BYTES + ((chunk ^ (row & 7)) << 4));
+            }
+        }
         __syncwarp();
     } else if constexpr (KIND == EPI_QKVG) {
+        static_assert(PARTS == 2, "q/k/v/gate groups are 128 columns");
         constexpr int C = BN / 128;
         const int m = mw + lane;                      // the TMEM row of this thread
         const bool row_ok = m < g.M;
@@ -314,13 +349,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
 }
 
 template <int KIND>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Cfg<KIND>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const GemmArgs g, int* err) {
+    constexpr int STAGES = Cfg<KIND>::STAGES, EPI_WARPS = Cfg<KIND>::EPI_WARPS, PARTS = Cfg<KIND>::PARTS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stage = tiles + STAGES * STAGE_BYTES;
-    Smem* sm = reinterpret_cast<Smem*>(stage + EPI_STAGE_BYTES);
+    Smem<STAGES>* sm = reinterpret_cast<Smem<STAGES>*>(stage + Cfg<KIND>::EPI_STAGE_BYTES);
     volatile int* abort = &sm->abort;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -391,7 +427,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else {
         const int quarter = warp & 3;         // TMEM lanes this warp may read
-        const int half = (warp - 2) / 4;      // column half of the tile
+        const int part = (warp - 2) / 4;      // column group of the tile
         const uint32_t acc_empty0 = mapa_shared(smem_u32(&sm->acc_empty[0]), 0);
         const uint32_t acc_empty1 = mapa_shared(smem_u32(&sm->acc_empty[1]), 0);
         uint32_t acc = 0;
@@ -406,7 +442,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             const int m0 = (tile / n_tiles) * 2 * BM + int(rank) * BM, n0 = (tile % n_tiles) * BN;
             const uint32_t tacc = tmem + (uint32_t(quarter * 32) << 16) + b * BN;
-            epilogue_tile<KIND>(g, tacc, m0, n0, quarter, lane, half, stage + (warp - 2) * 32 * 128);
+            epilogue_tile<KIND, PARTS>(g, tacc, m0, n0, quarter, lane, part, stage + (warp - 2) * 32 * 128);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster_relaxed(b ? acc_empty1 : acc_empty0);
@@ -484,7 +520,8 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg<KIND>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
@@ -497,8 +534,8 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
     const int pairs = tiles < max_pairs ? tiles : max_pairs;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.blockDim = dim3(Cfg<KIND>::THREADS);
+    cfg.dynamicSmemBytes = Cfg<KIND>::SMEM_BYTES;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
