@@ -1,18 +1,26 @@
-"""Forecast throughput benchmark (series/sec at T=2048, H=256) on 1..8 B200s.
+"""Forecast throughput benchmark (series/sec) on 1..8 B200s.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--weights f16|q8_0] [--batch B]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg5] [--weights f16|q8_0] [--batch B]
     python bench.py --impl reference ...   # the CPU reference arm (rank 0 only)
 
-Workload: the 209M-architecture forecaster (random init, seed 0) on B=4096 synthetic series
-(seasonal sine with period U[12,200], trend, 1% NaN, seeded per series), V=1, T=2048,
-H=256, symmetric averaging and clipping on. The batch is sharded B/N series per GPU with
-no collective on the forecast path; each rank runs its shard through its own engine.
+Workloads (209M architecture, random init seed 0, synthetic series of each config's shape;
+symmetric averaging and clipping on):
+  cfg1  f32  B=1    V=1   T=512   H=64   sin(2 pi t / 24) + 0.1 N(0,1)
+  cfg2  f16  B=64   V=1   T=2048  H=256  random walks + U(-100,100) offset, 5% NaN
+  cfg3  f16  B=16   V=32  T=1024  H=128  VAR(1), Sigma_ij = 0.5^|i-j|
+  cfg4  f16  B=32   V=4   T=1024  H=96   + 8 past, 4 known, 2 categorical known covariates
+  cfg5  f16 (or --weights q8_0)  B=4096  V=1  T=2048  H=256  seasonal sine + trend, 1% NaN
+The default is cfg5, the throughput configuration the headline metric is quoted on. The
+batch is sharded across GPUs with no collective on the forecast path; each rank runs its
+slice through its own handle.
 
 Printed JSON (rank 0): `value` is whole-job series/sec with the context already in device
-memory (tsb_forecast_device, CUDA events on the engine stream, max over ranks); `e2e` is the
-same metric through timestral_capi_forecast with host buffers (upload and download inside
-the timed region); `roofline` is the attention kernel measured live; `cpu_baseline` is the
-CPU oracle on a bounded sample of the same workload.
+memory (tsb_forecast_device, CUDA events on the engine stream, max over ranks; cfg4's
+covariates have no device-resident entry, so its `value` goes through the C ABI); `e2e` is
+the same metric through timestral_capi_forecast with host buffers (upload and download
+inside the timed region); `roofline` is the time-attention kernel timed with events inside
+the timed region; `roofline_gemm` the tensor-core GEMMs of one extra evented step;
+`cpu_baseline` the CPU oracle on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -30,7 +38,26 @@ import numpy as np
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "timestral.cpp_b200"))
 
-T_CTX, H_OUT, B_TOTAL = 2048, 256, 4096
+D_MODEL, D_FF, HEADS, HEAD_DIM, PATCH, N_Q = 768, 2048, 12, 64, 32, 21
+TIME_SUBLAYERS, VARIATE_SUBLAYERS, MLPS = 24, 6, 24
+
+CONFIGS = {
+    "cfg1": dict(weights="f32", B=1, V=1, T=512, H=64, cpu_sample=1,
+                 desc="cfg1: 209M f32 random-init, B=1, V=1, T=512, H=64, sine + noise"),
+    "cfg2": dict(weights="f16", B=64, V=1, T=2048, H=256, cpu_sample=8,
+                 desc="cfg2: 209M f16 random-init, B=64, V=1, T=2048, H=256, random walks, 5% NaN"),
+    "cfg3": dict(weights="f16", B=16, V=32, T=1024, H=128, cpu_sample=1,
+                 desc="cfg3: 209M f16 random-init, B=16, V=32, T=1024, H=128, VAR(1)"),
+    "cfg4": dict(weights="f16", B=32, V=4, T=1024, H=96, cpu_sample=1,
+                 desc="cfg4: 209M f16 random-init, B=32, V=4, T=1024, H=96, 8 past + 4 known + 2 categorical covariates"),
+    "cfg5": dict(weights=None, B=4096, V=1, T=2048, H=256, cpu_sample=48,
+                 desc="cfg5 throughput: 209M {w} random-init, B={B} series ({per} per GPU), V=1, T=2048, H=256, symmetric+clip"),
+}
+
+# DRAM bytes (read + write) of one time-attention (row, head) problem at S = 72, from the
+# ncu capture summarised in profiles/attention_time_tc_cfg5.md (B = 1024, dram__bytes_read.sum
+# + dram__bytes_write.sum over 24,576 problems); traffic per launch scales with the problems.
+ATTN_DRAM_BYTES_PER_PROBLEM = 45384
 
 
 def parse():
@@ -39,12 +66,21 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--weights", default="f16", choices=["f16", "q8_0"])
-    ap.add_argument("--batch", type=int, default=B_TOTAL)
-    ap.add_argument("--cpu-sample", type=int, default=48, help="series timed on the CPU baseline (about 15-20 s)")
+    ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS))
+    ap.add_argument("--weights", default="f16", choices=["f16", "q8_0"], help="cfg5 weight type")
+    ap.add_argument("--batch", type=int, default=0, help="override the config's batch")
+    ap.add_argument("--cpu-sample", type=int, default=0, help="series timed on the CPU baseline")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    return ap.parse_args()
+    a = ap.parse_args()
+    c = dict(CONFIGS[a.config])
+    if c["weights"] is None:
+        c["weights"] = a.weights
+    if a.batch:
+        c["B"] = a.batch
+    if a.cpu_sample:
+        c["cpu_sample"] = a.cpu_sample
+    return a, c
 
 
 def peaks():
@@ -105,75 +141,86 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def workload(lo: int, hi: int):
+def workload(cfg: str, c: dict, lo: int, hi: int):
+    """Inputs of series [lo, hi) of the config: (context [b,V,T], covariate kwargs)."""
     from timestral_b200 import synthetic as sy
-    out = np.empty((hi - lo, 1, T_CTX), np.float32)
+    T, H, V = c["T"], c["H"], c["V"]
+    if cfg == "cfg1":
+        return np.repeat(sy.series_sine(T, seed=0), hi - lo, axis=0), {}
+    if cfg == "cfg2":
+        return sy.series_random_walk(hi - lo, T, nan_frac=0.05, seed0=lo), {}
+    if cfg == "cfg3":
+        return sy.series_var1(c["B"], V, T, seed=0)[lo:hi], {}
+    if cfg == "cfg4":
+        target, past, known, cat = sy.series_covariates(c["B"], V, T, H, seed=0)
+        return target[lo:hi], {"past": past[lo:hi], "known": known[lo:hi], "cat_known": cat[lo:hi]}
+    out = np.empty((hi - lo, 1, T), np.float32)
     for k, i in enumerate(range(lo, hi)):
-        out[k] = sy.series_seasonal(1, T_CTX, nan_frac=0.01, seed0=i)[0]
-    return out
+        out[k] = sy.series_seasonal(1, T, nan_frac=0.01, seed0=i)[0]
+    return out, {}
 
 
 def model_path(weights: str, rank: int, dist):
     from timestral_b200 import synthetic as sy
     if rank == 0:
-        p = sy.cached_model(sy.spec_209m(), weights)
+        sy.cached_model(sy.spec_209m(), weights)
     if dist is not None:
         dist.barrier()
     return sy.cached_model(sy.spec_209m(), weights)
 
 
-def cpu_baseline(sample: int, weights: str):
-    """The CPU oracle on `sample` series of the same workload, all host threads."""
+def cpu_baseline(cfg: str, c: dict):
+    """The CPU oracle on `cpu_sample` series of the same workload, all host threads."""
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle_py as op
     from timestral_b200 import synthetic as sy
-    m = op.OracleModel(sy.cached_model(sy.spec_209m(), weights))
-    x = workload(0, sample)
+    m = op.OracleModel(sy.cached_model(sy.spec_209m(), c["weights"]))
+    sample = c["cpu_sample"]
+    x, kw = workload(cfg, c, 0, sample)
     threads = os.cpu_count() or 1
-    m.forecast(x[:1], H_OUT, threads=threads)   # warm caches
+    m.forecast(x[:1], c["H"], threads=threads, **{k: v[:1] for k, v in kw.items()})   # warm caches
     t0 = time.perf_counter()
-    m.forecast(x, H_OUT, threads=threads)
+    m.forecast(x, c["H"], threads=threads, **kw)
     dt = time.perf_counter() - t0
     return {"value": sample / dt, "unit": "series/s", "cores": threads, "kind": "port",
-            "sample": f"{sample} series of the same workload (T={T_CTX}, H={H_OUT}, {weights} 209M), "
-                      f"one forecast call, {dt:.2f} s"}
+            "sample": f"{sample} series of the same workload ({c['weights']} 209M, V={c['V']}, T={c['T']}, "
+                      f"H={c['H']}), one forecast call, {dt:.2f} s"}
 
 
-# DRAM bytes (read + write) of one time-attention (row, head) problem at S = 72, from the
-# ncu capture summarised in profiles/attention_time_tc_cfg5.md (B = 1024, dram__bytes_read.sum
-# + dram__bytes_write.sum over 24,576 problems); traffic per launch scales with the problems.
-ATTN_DRAM_BYTES_PER_PROBLEM = 45384
-
-
-def attention_algorithmic(rows: int, S: int, L: int, heads: int = 12, hd: int = 64):
-    """FLOPs and bytes of one time-attention launch over `rows` rows: 4*hd*sum_q keys(q) per
-    (row, head) with keys = L for encoder queries and S for decoder queries; bytes = q, k, v,
-    sigmoid-gate read and output written, f16."""
-    flops = 4 * hd * (L * L + (S - L) * S)
-    nbytes = 5 * S * hd * 2
-    return flops * rows * heads, nbytes * rows * heads
+def gemm_flops(rows: int, S: int, L: int, V_rows: int, decoder_tokens: int) -> int:
+    """Tensor-core GEMM FLOPs of one decode block: per token 24 time sublayers
+    (q|k|v|gate + out: 5 D^2 MACs), 6 variate sublayers (3 D^2 when a series has one row:
+    v|gate + out; else 5 D^2), 24 MLPs (3 D F); the context-patch projections (K = 64:
+    4 D + D outputs, then 4 D -> D); the head per decoder token (D -> 4D -> 21*32, plus
+    the D -> 21*32 residual)."""
+    D, F = D_MODEL, D_FF
+    var = 3 * D * D if V_rows == 1 else 5 * D * D
+    per_token = TIME_SUBLAYERS * 5 * D * D + VARIATE_SUBLAYERS * var + MLPS * 3 * D * F
+    patch = 2 * PATCH * 5 * D + 4 * D * D
+    head = D * 4 * D + 4 * D * N_Q * PATCH + D * N_Q * PATCH
+    return 2 * rows * (S * per_token + L * patch + decoder_tokens * head)
 
 
 def main():
-    a = parse()
+    a, c = parse()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != a.gpus:
         a.gpus = world
+    metric = f"forecast series/sec at T={c['T']},H={c['H']}"
     if a.impl == "reference":
         if rank != 0:
             return 0
-        b = cpu_baseline(a.cpu_sample, a.weights)
-        vals = [b["value"]]
-        for _ in range(max(a.steps, 1) - 1):
-            vals.append(cpu_baseline(a.cpu_sample, a.weights)["value"])
-        v = float(np.median(vals))
+        vals = [cpu_baseline(a.config, c) for _ in range(max(a.steps, 1))]
+        b = vals[0]
+        v = float(np.median([x["value"] for x in vals]))
         b["value"] = v
-        print(json.dumps({"impl": "reference", "metric": "forecast series/sec at T=2048,H=256", "value": v,
-                          "unit": "series/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
-                          "higher_is_better": True, "scaling": "strong", "dtype": "f32", "data": "synthetic",
-                          "config": {"workload": f"209M {a.weights} B={a.batch} V=1 T={T_CTX} H={H_OUT} (CPU sample)"},
+        print(json.dumps({"impl": "reference", "metric": metric, "value": v, "unit": "series/s", "n_gpus": a.gpus,
+                          "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "strong",
+                          "dtype": "f32", "data": "synthetic",
+                          "config": {"workload": f"{a.config} 209M {c['weights']} B={c['B']} V={c['V']} T={c['T']} "
+                                                 f"H={c['H']} (CPU sample)"},
                           "cpu_baseline": b,
                           "e2e": {"value": v, "unit": "series/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
               flush=True)
@@ -190,33 +237,42 @@ def main():
     else:
         torch.cuda.set_device(local)
     import timestral_b200 as tb
-    dev = torch.device("cuda", local)
     from timestral_b200.shard import shard_range
-    lo, hi = shard_range(a.batch, world, rank)
+    dev = torch.device("cuda", local)
+    B, V, T, H = c["B"], c["V"], c["T"], c["H"]
+    lo, hi = shard_range(B, world, rank)
     per = hi - lo
-    path = model_path(a.weights, rank, dist)
+    path = model_path(c["weights"], rank, dist)
     model = tb.Model(path, device=local)
     Q = model.num_quantiles
-    x = workload(lo, hi)
-    d_ctx = torch.from_numpy(x).to(dev)
-    d_out = torch.empty((per, 1, H_OUT, Q), device=dev, dtype=torch.float32)
+    x, kw = workload(a.config, c, lo, hi)
+    covariates = bool(kw)
     stream = torch.cuda.ExternalStream(model.stream(), device=dev)
+    hx = torch.from_numpy(np.ascontiguousarray(x)).pin_memory().numpy()
 
-    def step():
-        model.forecast_device(d_ctx.data_ptr(), None, per, 1, T_CTX, H_OUT, d_out.data_ptr(), asynchronous=True)
+    if covariates:
+        def step():
+            model.forecast(hx, H, **kw)
+    else:
+        d_ctx = torch.from_numpy(x).to(dev)
+        d_out = torch.empty((per, V, H, Q), device=dev, dtype=torch.float32)
+
+        def step():
+            model.forecast_device(d_ctx.data_ptr(), None, per, V, T, H, d_out.data_ptr(), asynchronous=True)
 
     for _ in range(a.warmup):
         step()
     if tb.lib().tsb_sync(model.h) != 0:
         raise RuntimeError(model.last_error)
     launches_per_step = model.last_launch_count()
+    rows, S, L, blocks = model.last_geometry()
     clocks = ClockSampler(local)
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)
     clocks.start()
     # Attention launches are bracketed by CUDA events on the engine stream inside the timed
-    # region (two events per launch, 24 launches per step).
+    # region (two events per launch).
     model.timing_reset()
     model.timing(True, attention_only=True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -242,66 +298,69 @@ def main():
     # End to end through the public C ABI with host buffers.
     e2e = None
     if not a.no_e2e:
-        hx = torch.from_numpy(x).pin_memory().numpy()
-        model.forecast(hx[:1], H_OUT)
+        model.forecast(hx[:1], H, **{k: v[:1] for k, v in kw.items()})
         if dist:
             dist.barrier()
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
         for _ in range(a.steps):
-            model.forecast(hx, H_OUT)
-        e2e_s = (time.perf_counter() - t0) / a.steps
-        e2e = e2e_s
+            model.forecast(hx, H, **kw)
+        e2e = (time.perf_counter() - t0) / a.steps
     stats = torch.tensor([ms, e2e or 0.0], device=dev, dtype=torch.float64)
     if dist:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     ms_max, e2e_max = stats[0].item(), stats[1].item()
     if rank == 0:
         hbm, tf, tf_sus, kind = peaks()
-        L = T_CTX // 32
-        S = L + H_OUT // 32
-        rows = 2 * per
-        fl, by = attention_algorithmic(rows, S, L)
+        # Attention: per (row, head) problem q, k, v, sigmoid(gate) read and the output
+        # written (5 S hd f16 values); FLOPs 4 hd sum_q keys(q), keys = L for encoder queries
+        # and S for decoder queries (the reference's computed set); one launch per time
+        # sublayer and block.
+        problems = rows * HEADS
+        att_bytes = 5 * S * HEAD_DIM * 2 * problems
+        att_flops = 4 * HEAD_DIM * (L * L + (S - L) * S) * problems
         att_avg = att_ms / max(att_n, 1)
-        achieved_gbs = by / (att_avg / 1e3) / 1e9
-        achieved_tf = fl / (att_avg / 1e3) / 1e12
-        roof_tf = min(tf, (fl / by) * hbm / 1e3)
-        # Tensor-core GEMM work per step on this rank, as the kernels compute it: patch
-        # output projection per context patch, per token 24 time sublayers (q|k|v|gate and
-        # out: 5*D^2), 6 variate sublayers of one-row series (v|gate and out: 3*D^2), 24 MLPs
-        # (3*D*F), and the head per decoder token.
-        D, F = 768, 2048
-        per_token = 24 * 5 * D * D + 6 * 3 * D * D + 24 * 3 * D * F
-        gemm_flops = 2 * rows * (L * 4 * D * D + S * per_token + (S - L) * (D * 4 * D + 4 * D * 672 + D * 672))
-        value = a.batch / (ms_max / 1e3)
+        achieved_gbs = att_bytes / (att_avg / 1e3) / 1e9
+        achieved_tf = att_flops / (att_avg / 1e3) / 1e12
+        roof_tf = min(tf, (att_flops / att_bytes) * hbm / 1e3)
+        tc_path = model.tensor_core_path
+        gflops = gemm_flops(rows, S, L, V, S - L) * blocks
+        value = B / (ms_max / 1e3)
+        cdesc = c["desc"].format(w=c["weights"], B=B, per=per) if a.config == "cfg5" else c["desc"]
         out = {
-            "metric": "forecast series/sec at T=2048,H=256", "value": value, "unit": "series/s", "n_gpus": world,
+            "metric": metric, "value": value, "unit": "series/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": f"cfg5 throughput: 209M {a.weights} random-init, B={a.batch} series "
-                                   f"({per} per GPU), V=1, T={T_CTX}, H={H_OUT}, symmetric+clip",
-                       "global_batch": a.batch, "seq_len": S, "parallelism": f"series-sharded x{world}",
-                       "l2": "per-step working set (~13 GB at B=4096) far above the 126 MB L2"},
-            "roofline": {"kernel": "attention_time_tc", "bound": "hbm", "achieved": achieved_gbs, "peak": hbm,
+            "vs_baseline": None, "dtype": "f16" if c["weights"] != "f32" else "f32", "data": "synthetic",
+            "config": {"workload": cdesc, "global_batch": B, "seq_len": S,
+                       "parallelism": f"series-sharded x{world}",
+                       "l2": "per-step working set far above the 126 MB L2" if a.config == "cfg5"
+                             else "steps run back to back without an L2 flush (small working set)",
+                       "path": "device-resident context" if not covariates else "C ABI with host buffers (covariates)"},
+            "roofline": {"kernel": "attention_time_tc" if tc_path and S <= 128 else "attention_time_simt",
+                         "bound": "hbm", "achieved": achieved_gbs, "peak": hbm,
                          "unit": "GB/s", "frac": achieved_gbs / hbm,
-                         "traffic": (ATTN_DRAM_BYTES_PER_PROBLEM * rows * 12 if ATTN_DRAM_BYTES_PER_PROBLEM else None),
-                         "traffic_unit": "bytes per launch", "algorithmic_bytes": by,
+                         "traffic": (ATTN_DRAM_BYTES_PER_PROBLEM * problems
+                                     if (a.config == "cfg5" and ATTN_DRAM_BYTES_PER_PROBLEM) else None),
+                         "traffic_unit": "bytes per launch", "algorithmic_bytes": att_bytes,
                          "achieved_tflops": achieved_tf, "roofline_tflops": roof_tf,
                          "frac_of_dense_contraction_roofline": achieved_tf / roof_tf,
-                         "launch_ms": att_avg, "launches_per_step": att_n, "peak_kind": kind},
-            "roofline_gemm": {"bound": "tensor", "achieved": gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else None,
-                              "peak": tf_sus, "unit": "TFLOP/s",
-                              "frac": (gemm_flops / (gemm_ms / 1e3) / 1e12) / tf_sus if gemm_ms else None,
-                              "gemm_ms_per_step": gemm_ms, "share_of_step": gemm_ms / all_ms if all_ms else None,
-                              "peak_kind": kind + " sustained"},
+                         "launch_ms": att_avg, "launches_per_step": att_n / max(a.steps, 1), "peak_kind": kind},
             "clocks": clk,
             "gpu_launches": launches_per_step * a.steps,
         }
+        if tc_path:
+            out["roofline_gemm"] = {"bound": "tensor",
+                                    "achieved": gflops / (gemm_ms / 1e3) / 1e12 if gemm_ms else None,
+                                    "peak": tf_sus, "unit": "TFLOP/s",
+                                    "frac": (gflops / (gemm_ms / 1e3) / 1e12) / tf_sus if gemm_ms else None,
+                                    "gemm_ms_per_step": gemm_ms, "share_of_step": gemm_ms / all_ms if all_ms else None,
+                                    "peak_kind": kind + " sustained"}
         if e2e:
-            out["e2e"] = {"value": a.batch / e2e_max, "unit": "series/s",
-                          "h2d_bytes_per_step": a.batch * T_CTX * 4, "d2h_bytes_per_step": a.batch * H_OUT * Q * 4}
+            cov_bytes = sum(int(v.nbytes) for v in kw.values()) * B // max(per, 1)
+            out["e2e"] = {"value": B / e2e_max, "unit": "series/s",
+                          "h2d_bytes_per_step": B * V * T * 4 + cov_bytes, "d2h_bytes_per_step": B * V * H * Q * 4}
         if world == 1 and not a.no_cpu:
-            out["cpu_baseline"] = cpu_baseline(a.cpu_sample, a.weights)
+            out["cpu_baseline"] = cpu_baseline(a.config, c)
         print(json.dumps(out), flush=True)
     model.close()
     if dist:

@@ -57,6 +57,9 @@ TIMESTRAL_API int64_t tsb_last_launch_count(timestral_ctx* ctx);
 /* Compute path chosen for the loaded model: 1 = tensor cores (F16/Q8_0 weights),
  * 0 = F32 CUDA-core path. */
 TIMESTRAL_API int tsb_model_path(timestral_ctx* ctx);
+/* Geometry of the last decode block of the handle's last forecast: model rows (both
+ * symmetric passes, every row role), tokens per row, context patches, decode blocks. */
+TIMESTRAL_API int tsb_last_geometry(timestral_ctx* ctx, int64_t* rows, int32_t* S, int32_t* L, int32_t* blocks);
 
 /* ---- refine without device allocation --------------------------------------------
  * No counterpart in the reference. The refine step of one decode block (re-normalising a

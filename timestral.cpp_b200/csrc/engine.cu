@@ -392,10 +392,12 @@ struct Engine::Impl {
     // --- one decode block ---------------------------------------------------------------
     // Inputs: win/wmask [R2][W] (W = T on the context path, T + h*ps with covariates),
     // role [R2] (covariate path). Output: refined [R2][h*ps][Q]. first: compute cap stats.
+    Engine::Geometry geo;
     void predict_block(int R2, int T, int h, bool cov, int group_rows, int pass_rows, bool first, int cap_ctx) {
         const int W = cov ? T + h * ps : T;
         const int N = W / ps, L = T / ps;
         const int S = cov ? 2 * N : N + h;
+        geo.rows = R2; geo.S = S; geo.L = L; geo.blocks = first ? 1 : geo.blocks + 1;
         const int P_all = cov ? N : h;
         const int kvw = (N + 31) / 32;
         const int64_t M = int64_t(R2) * S;
@@ -680,6 +682,7 @@ void Engine::timing_enable(bool on, const char* only) {
     impl_->timing_only = only ? only : "";
 }
 void Engine::timing_reset() { impl_->ev_used = 0; }
+Engine::Geometry Engine::last_geometry() const { return impl_->geo; }
 bool Engine::timing_read(const std::string& cls, double* ms, int64_t* launches) {
     cudaStreamSynchronize(stream_);
     double total = 0;

@@ -82,6 +82,10 @@ public:
     void timing_reset();
     bool timing_read(const std::string& cls, double* ms, int64_t* launches);
     int64_t last_launches() const { return last_launches_; }
+    // Geometry of the last decode block of the last forecast: rows (both passes, every row
+    // role), tokens per row S, context patches L, decode blocks.
+    struct Geometry { int64_t rows = 0; int S = 0, L = 0, blocks = 0; };
+    Geometry last_geometry() const;
 
 private:
     struct Impl;

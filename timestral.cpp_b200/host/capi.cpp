@@ -284,6 +284,13 @@ TIMESTRAL_API void tsb_timing_reset(timestral_ctx* c) {
 
 TIMESTRAL_API int64_t tsb_last_launch_count(timestral_ctx* c) { return c ? c->forecaster.engine().last_launches() : 0; }
 
+TIMESTRAL_API int tsb_last_geometry(timestral_ctx* c, int64_t* rows, int32_t* S, int32_t* L, int32_t* blocks) {
+    if (!c || !rows || !S || !L || !blocks) return TSB_ERR_ARG;
+    const auto g = c->forecaster.engine().last_geometry();
+    *rows = g.rows; *S = g.S; *L = g.L; *blocks = g.blocks;
+    return TSB_OK;
+}
+
 TIMESTRAL_API int tsb_model_path(timestral_ctx* c) { return c && c->forecaster.engine().tensor_cores() ? 1 : 0; }
 
 }  // extern "C"

@@ -59,6 +59,7 @@ SIGNATURES = {
     "tsb_timing_reset": (None, [C.c_void_p]),
     "tsb_last_launch_count": (C.c_int64, [C.c_void_p]),
     "tsb_model_path": (C.c_int, [C.c_void_p]),
+    "tsb_last_geometry": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64)] + [C.POINTER(C.c_int32)] * 3),
     "tsb_test_gemm": (C.c_int, [C.POINTER(GemmTest), C.POINTER(C.c_int32)]),
     "tsb_test_attention_time": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 4 + [C.POINTER(C.c_int32)]),
     "tsb_test_split_f16": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p]),
@@ -182,6 +183,12 @@ class Model:
 
     def last_launch_count(self) -> int:
         return lib().tsb_last_launch_count(self.h)
+
+    def last_geometry(self):
+        """(rows, S, L, blocks) of the last decode block of the last forecast."""
+        rows, S, L, blocks = C.c_int64(0), C.c_int32(0), C.c_int32(0), C.c_int32(0)
+        lib().tsb_last_geometry(self.h, C.byref(rows), C.byref(S), C.byref(L), C.byref(blocks))
+        return rows.value, S.value, L.value, blocks.value
 
     @property
     def tensor_core_path(self) -> bool:
