@@ -111,6 +111,13 @@ TIMESTRAL_API int tsb_test_attention_time(const void* q, const void* k, const vo
 /* f16 hi/lo split used by the tensor-core patch projections: out [rows][3K] f16 =
  * [hi | hi | lo] of each f32 row of a; sets *d_overflow (device int) when any |a| > 30000. */
 TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, void* out, int32_t* d_overflow);
+/* Variate-axis attention of the tensor-core path over groups of G consecutive rows (one
+ * series each): q/k/v/gate f16 head-major [rows][H][S][64] (gate may be NULL), key_valid
+ * [rows][ceil(N/32)] bits, role [rows] (0 target, 1 past, 2 known) or NULL without
+ * covariates, out f16 token-major [rows * S][H * 64]; synchronized. */
+TIMESTRAL_API int tsb_test_attention_variate(const void* q, const void* k, const void* v, const void* gate, void* out,
+                                             const uint32_t* key_valid, const int8_t* role, int32_t rows, int32_t H,
+                                             int32_t S, int32_t N, int32_t G);
 TIMESTRAL_API int tsb_test_rms(const float* x, const float* w, int32_t tokens, int32_t D, float eps, void* out,
                                int32_t out_f16);
 

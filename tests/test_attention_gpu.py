@@ -73,3 +73,58 @@ def test_attention_time_tc(dev, S, N, gated):
     tol = 4e-3 * scale + want.abs() * 2.0 ** -10
     bad = (got - want).abs() > tol
     assert not bad.any(), f"max err {(got - want).abs().max().item():.3e}"
+
+
+@pytest.mark.parametrize("G,S,N,cov", [(32, 36, 32, False), (3, 10, 8, False), (18, 70, 35, True), (64, 20, 16, False),
+                                       (45, 12, 12, True)])
+def test_attention_variate_fast(dev, G, S, N, cov):
+    """Variate axis: at each patch slot p a row attends the rows of its series whose patch p is
+    observed (every row at decoder slots p >= N), under the covariate role firewall, and
+    always itself (reference src/masks.cpp:27)."""
+    groups, H = 5, 2
+    rows = groups * G
+    g = torch.Generator().manual_seed(G * 100 + S)
+    q = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
+    k = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
+    v = torch.randn(rows, H, S, 64, generator=g).half()
+    gate = torch.rand(rows, H, S, 64, generator=g).half()
+    valid = torch.rand(rows, N, generator=g) > 0.3
+    role = torch.randint(0, 3, (rows,), generator=g, dtype=torch.int8) if cov else None
+    words = (N + 31) // 32
+    bits = np.zeros((rows, words), np.uint32)
+    vn = valid.numpy()
+    for pp in range(N):
+        bits[:, pp // 32] |= vn[:, pp].astype(np.uint32) << np.uint32(pp % 32)
+    # allowed[p, i, j] within each group
+    usable = torch.ones(rows, S, dtype=torch.bool)
+    usable[:, :N] = valid
+    want = torch.empty(rows, S, H, 64, dtype=torch.float64)
+    for gi in range(groups):
+        r = slice(gi * G, (gi + 1) * G)
+        qd, kd, vd = q[r].double(), k[r].double(), v[r].double()     # [G,H,S,64]
+        s_ = torch.einsum("ihpd,jhpd->hpij", qd, kd) / 8.0
+        allow = usable[r].T[None, :, None, :].expand(H, S, G, G).clone()   # key j usable at p
+        if cov:
+            rq = role[r].long()[:, None]
+            rk = role[r].long()[None, :]
+            fw = ~(((rq != 0) & (rk == 0)) | ((rq == 2) & (rk != 2)))
+            allow &= fw[None, None]
+        eye = torch.eye(G, dtype=torch.bool)
+        allow |= eye[None, None]
+        s_ = s_.masked_fill(~allow, float("-inf"))
+        pr = torch.softmax(s_, dim=-1)
+        o = torch.einsum("hpij,jhpd->ihpd", pr, vd) * gate[r].double()
+        want[r] = o.permute(0, 2, 1, 3)
+    want = want.reshape(rows * S, H * 64)
+    dq, dk, dv, dg = q.to(dev), k.to(dev), v.to(dev), gate.to(dev)
+    dbits = torch.from_numpy(bits.view(np.int32)).to(dev)
+    drole = role.to(dev) if cov else None
+    out = torch.full((rows * S, H * 64), float("nan"), device=dev, dtype=torch.float16)
+    rc = tb.lib().tsb_test_attention_variate(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), out.data_ptr(),
+                                             dbits.data_ptr(), drole.data_ptr() if cov else None, rows, H, S, N, G)
+    assert rc == 0, rc
+    got = out.cpu().double()
+    assert torch.isfinite(got).all()
+    scale = want.abs().max().item()
+    err = (got - want).abs()
+    assert (err <= 2e-3 * scale + want.abs() * 2.0 ** -10).all(), float(err.max())

@@ -548,6 +548,141 @@ __global__ void __launch_bounds__(SIMT_WARPS * 32)
     }
 }
 
+// Variate-axis attention on the tensor-core path (f16 q/k/v/gate, head_dim 64): one warp per
+// (series group, patch slot, head) problem, the group's K and V rows converted to f32 in
+// shared memory once and read as broadcasts, QPL query rows per lane (group size <= 32 QPL).
+// Scores, softmax and the weighted sum in f32; the keys and mask are the reference's
+// (src/masks.cpp:27: same series, key patch observed or a decoder slot, role firewall, or the
+// query itself); the operation order is not the reference's float order (f16 path).
+constexpr int VF_WARPS = 4;
+
+template <int QPL>
+__global__ void __launch_bounds__(VF_WARPS * 32)
+    attn_variate_fast_kernel(const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
+                             const __half* __restrict__ gate, __half* __restrict__ out, int rows, int H, int G,
+                             const MaskMeta mm) {
+    constexpr int GM = 32 * QPL;
+    extern __shared__ float vf_sh[];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    float* Ks = vf_sh + warp * (2 * GM * 64 + GM);
+    float* Vs = Ks + GM * 64;
+    uint32_t* meta = reinterpret_cast<uint32_t*>(Vs + GM * 64);   // bit 0: key usable, bits 1..: role
+    const int S = mm.S, D = H * 64;
+    const int64_t pid = int64_t(blockIdx.x) * VF_WARPS + warp;
+    const int64_t total = int64_t(rows / G) * H * S;
+    if (pid >= total) return;                                     // uniform across the warp
+    const int p = int(pid % S), h = int((pid / S) % H);
+    const int r0 = int(pid / (int64_t(S) * H)) * G;
+    // K and V rows of the group at (head, slot): eight lanes per 128-byte row.
+    for (int j = lane >> 3; j < G; j += 4) {
+        const int64_t off = ((int64_t(r0 + j) * H + h) * S + p) * 64 + (lane & 7) * 8;
+        const uint4 kk = *reinterpret_cast<const uint4*>(k + off);
+        const uint4 vv = *reinterpret_cast<const uint4*>(v + off);
+        const __half2* kh = reinterpret_cast<const __half2*>(&kk);
+        const __half2* vh = reinterpret_cast<const __half2*>(&vv);
+        float* kd = Ks + j * 64 + (lane & 7) * 8;
+        float* vd = Vs + j * 64 + (lane & 7) * 8;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float2 a = __half22float2(kh[t]), b = __half22float2(vh[t]);
+            kd[2 * t] = a.x; kd[2 * t + 1] = a.y;
+            vd[2 * t] = b.x; vd[2 * t + 1] = b.y;
+        }
+    }
+    for (int j = lane; j < G; j += 32) {
+        const int kr = r0 + j;
+        const bool usable = p >= mm.N || kv_bit(mm, kr, p);
+        meta[j] = (usable ? 1u : 0u) | (uint32_t(mm.cov ? mm.role[kr] : 0) << 1);
+    }
+    __syncwarp();
+#pragma unroll 1
+    for (int qi = 0; qi < QPL; ++qi) {
+        const int i = lane + 32 * qi;
+        const bool live = i < G;
+        const int r = r0 + (live ? i : 0);
+        const int64_t qoff = ((int64_t(r) * H + h) * S + p) * 64;
+        float qv[64];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 u = *reinterpret_cast<const uint4*>(q + qoff + c * 8);
+            const __half2* hh = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float2 f = __half22float2(hh[t]);
+                qv[c * 8 + 2 * t] = f.x; qv[c * 8 + 2 * t + 1] = f.y;
+            }
+        }
+        const int rq = mm.cov ? mm.role[r] : 0;
+        float sc[GM];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < GM; ++j) {
+            sc[j] = -INFINITY;
+            if (j < G) {
+                const uint32_t mj = meta[j];
+                const int rk = int(mj >> 1);
+                const bool allowed = j == i || ((mj & 1u) && !(mm.cov && ((rq != 0 && rk == 0) || (rq == 2 && rk != 2))));
+                if (allowed) {
+                    const float4* kr4 = reinterpret_cast<const float4*>(Ks + j * 64);
+                    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                    for (int d = 0; d < 16; d += 2) {
+                        const float4 x = kr4[d], y = kr4[d + 1];
+                        a0 = fmaf(qv[4 * d], x.x, a0); a0 = fmaf(qv[4 * d + 1], x.y, a0);
+                        a0 = fmaf(qv[4 * d + 2], x.z, a0); a0 = fmaf(qv[4 * d + 3], x.w, a0);
+                        a1 = fmaf(qv[4 * d + 4], y.x, a1); a1 = fmaf(qv[4 * d + 5], y.y, a1);
+                        a1 = fmaf(qv[4 * d + 6], y.z, a1); a1 = fmaf(qv[4 * d + 7], y.w, a1);
+                    }
+                    sc[j] = (a0 + a1) * 0.125f;
+                    mx = fmaxf(mx, sc[j]);
+                }
+            }
+        }
+        float acc[64];
+#pragma unroll
+        for (int d = 0; d < 64; ++d) acc[d] = 0.f;
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < GM; ++j) {
+            if (j < G && sc[j] != -INFINITY) {
+                const float pj = __expf(sc[j] - mx);
+                sum += pj;
+                const float4* vr4 = reinterpret_cast<const float4*>(Vs + j * 64);
+#pragma unroll
+                for (int d = 0; d < 16; ++d) {
+                    const float4 x = vr4[d];
+                    acc[4 * d] = fmaf(pj, x.x, acc[4 * d]); acc[4 * d + 1] = fmaf(pj, x.y, acc[4 * d + 1]);
+                    acc[4 * d + 2] = fmaf(pj, x.z, acc[4 * d + 2]); acc[4 * d + 3] = fmaf(pj, x.w, acc[4 * d + 3]);
+                }
+            }
+        }
+        if (!live) continue;
+        const float inv = 1.0f / sum;
+        const __half* gp = gate ? gate + qoff : nullptr;
+        __half* dst = out + (int64_t(r) * S + p) * D + h * 64;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            float y[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) y[t] = acc[c * 8 + t] * inv;
+            if (gp) {
+                const uint4 gu = *reinterpret_cast<const uint4*>(gp + c * 8);
+                const __half2* gh = reinterpret_cast<const __half2*>(&gu);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float2 f = __half22float2(gh[t]);
+                    y[2 * t] = __fmul_rn(y[2 * t], f.x);
+                    y[2 * t + 1] = __fmul_rn(y[2 * t + 1], f.y);
+                }
+            }
+            uint4 u;
+            u.x = pack_half2(y[0], y[1]); u.y = pack_half2(y[2], y[3]);
+            u.z = pack_half2(y[4], y[5]); u.w = pack_half2(y[6], y[7]);
+            *reinterpret_cast<uint4*>(dst + c * 8) = u;
+        }
+    }
+}
+
 constexpr size_t simt_smem() { return (SIMT_WARPS * 2 * SIMT_MAX_KEYS + SIMT_WARPS * 256) * sizeof(float); }
 
 }  // namespace
@@ -603,6 +738,32 @@ cudaError_t attention_variate_simt(const T* q, const T* k, const T* v, const T* 
     }
     const int64_t blocks = int64_t(rows) * mm.S * ((H + SIMT_WARPS - 1) / SIMT_WARPS);
     attn_variate_simt_kernel<T><<<unsigned(blocks), SIMT_WARPS * 32, simt_smem(), stream>>>(q, k, v, gate, out, rows, H, hd, mm);
+    return cudaGetLastError();
+}
+
+cudaError_t attention_variate_fast(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
+                                   int rows, int H, int G, const MaskMeta& mm, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    if (G <= 0 || G > 64 || rows % G || mm.S <= 0) return cudaErrorInvalidValue;
+    const int64_t problems = int64_t(rows / G) * H * mm.S;
+    const unsigned blocks = unsigned((problems + VF_WARPS - 1) / VF_WARPS);
+    // Both variants use more than the default 48 KB of dynamic shared memory.
+    static bool configured[64] = {false};
+    const size_t smem1 = VF_WARPS * (2 * 32 * 64 + 32) * sizeof(float);
+    const size_t smem2 = VF_WARPS * (2 * 64 * 64 + 64) * sizeof(float);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_variate_fast_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem1));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(attn_variate_fast_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem2));
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    if (G <= 32)
+        attn_variate_fast_kernel<1><<<blocks, VF_WARPS * 32, smem1, stream>>>(q, k, v, gate, out, rows, H, G, mm);
+    else
+        attn_variate_fast_kernel<2><<<blocks, VF_WARPS * 32, smem2, stream>>>(q, k, v, gate, out, rows, H, G, mm);
     return cudaGetLastError();
 }
 

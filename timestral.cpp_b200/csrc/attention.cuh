@@ -35,6 +35,10 @@ cudaError_t attention_time_tc(const __half* q, const __half* k, const __half* v,
 template <class T>
 cudaError_t attention_time_simt(const T* q, const T* k, const T* v, const T* gate, T* out, int rows, int H, int hd,
                                 const MaskMeta& mm, cudaStream_t stream);
+// Variate-axis attention of the tensor-core path: groups of G <= 64 consecutive rows (one
+// series), f16 head-major q/k/v/gate, head_dim 64, out token-major f16.
+cudaError_t attention_variate_fast(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
+                                   int rows, int H, int G, const MaskMeta& mm, cudaStream_t stream);
 template <class T>
 cudaError_t attention_variate_simt(const T* q, const T* k, const T* v, const T* gate, T* out, int rows, int H,
                                    int hd, const MaskMeta& mm, cudaStream_t stream);

@@ -608,7 +608,10 @@ struct Engine::Impl {
                 else
                     run("attention", [&] { return attention_time_simt<__half>(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, hd, mm, s); });
             } else {
-                run("attention_variate", [&] { return attention_variate_simt<__half>(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, hd, mm, s); });
+                if (group_rows <= 64)
+                    run("attention_variate", [&] { return attention_variate_fast(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, group_rows, mm, s); });
+                else
+                    run("attention_variate", [&] { return attention_variate_simt<__half>(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, hd, mm, s); });
             }
         }
         GemmArgs o;

@@ -71,3 +71,21 @@ extern "C" TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, in
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     return e == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
 }
+
+extern "C" TIMESTRAL_API int tsb_test_attention_variate(const void* q, const void* k, const void* v, const void* gate,
+                                                        void* out, const uint32_t* key_valid, const int8_t* role,
+                                                        int32_t rows, int32_t H, int32_t S, int32_t N, int32_t G) {
+    using namespace tsb;
+    if (!q || !k || !v || !out || !key_valid || rows <= 0 || H <= 0 || S <= 0 || N <= 0 || N > S || G <= 0 ||
+        rows % G)
+        return TSB_ERR_ARG;
+    MaskMeta mm;
+    mm.key_valid = key_valid; mm.kv_words = (N + 31) / 32; mm.N = N; mm.L = N; mm.S = S;
+    mm.cov = role != nullptr; mm.role = role;
+    cudaError_t ce = attention_variate_fast(static_cast<const __half*>(q), static_cast<const __half*>(k),
+                                            static_cast<const __half*>(v), static_cast<const __half*>(gate),
+                                            static_cast<__half*>(out), rows, H, G, mm, 0);
+    if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+    if (ce != cudaSuccess) return ce == cudaErrorInvalidValue ? TSB_ERR_ARG : TSB_ERR_CUDA;
+    return TSB_OK;
+}
