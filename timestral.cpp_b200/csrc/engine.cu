@@ -97,7 +97,7 @@ struct Engine::Impl {
     // workspace
     DevBuf rows, mask, win, wmask, role, future, fmask, feat, aloc, ascale, caplo, caphi, capsc, first_obs, kv, rope_row,
         gbeg, gsize, clip_ok, x, xn, qb, kb, vb, gb, att, hb, zb, fused, gtmp, ph, dec, hh, hraw, qout, refined, scratch,
-        decoded, err, next_rows, next_mask, feat16, pflag;
+        decoded, err, next_rows, next_mask, feat16, pflag, panel_scratch;
     // timing
     bool timing = false;
     std::string timing_only;   // empty: every class
@@ -385,7 +385,13 @@ struct Engine::Impl {
     void gemm(EpiKind k, const GemmArgs& a, const char* cls = "gemm") {
         run(cls, [&] { return tc_gemm(k, a, s, err.as<int>()); });
     }
-    void sgemm(const SimtGemm& g, const char* cls = "gemm_simt") {
+    void sgemm(SimtGemm g, const char* cls = "gemm_simt") {
+        const size_t need = simt_panel_scratch_bytes(g);
+        if (need) {
+            panel_scratch.ensure(need);
+            g.panel_scratch = panel_scratch.as<float>();
+            g.panel_scratch_bytes = panel_scratch.bytes;
+        }
         run(cls, [&] { return simt_gemm(g, s); });
     }
 

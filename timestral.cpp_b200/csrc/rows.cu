@@ -774,8 +774,85 @@ cudaError_t feedback(const RowConfig& c, const float* rows, const int8_t* mask, 
     return cudaGetLastError();
 }
 
+// Split-panel form of ORDER_PANEL192 for few rows: block (x, y, p) computes the 32 x 32 tile's
+// FMA chain over panel p's 192 K values (ascending k, as the one-pass kernel), and the combine
+// kernel adds the panels to 0 in order and applies the epilogue: the same operations on every
+// output as simt_gemm_kernel<ORDER_PANEL192>.
+constexpr int PT = 32, PK = 32, PANEL = 192;
+__global__ void __launch_bounds__(256) simt_panel_kernel(const SimtGemm g) {
+    __shared__ float As[PK][PT + 1];
+    __shared__ float Ws[PK][PT + 1];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const int m0 = blockIdx.y * PT, n0 = blockIdx.x * PT, p = blockIdx.z;
+    const int k_lo = p * PANEL, k_hi = min(g.K, k_lo + PANEL);
+    float pan[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    for (int k0 = k_lo; k0 < k_hi; k0 += PK) {
+        for (int e = threadIdx.x; e < PK * PT; e += 256) {
+            const int kk = e % PK, rr = e / PK;
+            const int m = m0 + rr, n = n0 + rr, k = k0 + kk;
+            float a = (m < g.M && k < k_hi) ? g.A[int64_t(m) * g.lda + k] : 0.f;
+            if (g.round_a_f16) a = __half2float(__float2half_rn(a));
+            As[kk][rr] = a;
+            Ws[kk][rr] = (n < g.N && k < k_hi) ? g.W[int64_t(n) * g.K + k] : 0.f;
+        }
+        __syncthreads();
+        const int kend = min(PK, k_hi - k0);
+        for (int kk = 0; kk < kend; ++kk) {
+            const float a0 = As[kk][ty * 2], a1 = As[kk][ty * 2 + 1];
+            const float w0 = Ws[kk][tx * 2], w1 = Ws[kk][tx * 2 + 1];
+            pan[0][0] = __fmaf_rn(w0, a0, pan[0][0]); pan[0][1] = __fmaf_rn(w1, a0, pan[0][1]);
+            pan[1][0] = __fmaf_rn(w0, a1, pan[1][0]); pan[1][1] = __fmaf_rn(w1, a1, pan[1][1]);
+        }
+        __syncthreads();
+    }
+    float* part = g.panel_scratch + int64_t(p) * g.M * g.N;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int m = m0 + ty * 2 + i;
+        if (m >= g.M) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int n = n0 + tx * 2 + j;
+            if (n < g.N) part[int64_t(m) * g.N + n] = pan[i][j];
+        }
+    }
+}
+
+__global__ void simt_panel_combine_kernel(const SimtGemm g, int panels) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= int64_t(g.M) * g.N) return;
+    const int m = int(i / g.N), n = int(i % g.N);
+    float v = 0.f;
+    for (int p = 0; p < panels; ++p) v = v + g.panel_scratch[int64_t(p) * g.M * g.N + i];
+    if (g.bias) v = __fadd_rn(v, g.bias[n]);
+    const int64_t orow = g.row_group > 0 ? int64_t(m / g.row_group) * g.row_stride + g.row_offset + m % g.row_group : m;
+    const int64_t o = orow * g.ldo + n;
+    switch (g.epi) {
+        case SEPI_F32: static_cast<float*>(g.out)[o] = v; break;
+        case SEPI_F16: static_cast<__half*>(g.out)[o] = __float2half_rn(v); break;
+        case SEPI_RESID: static_cast<float*>(g.out)[o] = __fadd_rn(static_cast<float*>(g.out)[o], v); break;
+        case SEPI_SILU_F32: static_cast<float*>(g.out)[o] = ref_silu(v); break;
+        case SEPI_SILU_F16: static_cast<__half*>(g.out)[o] = __float2half_rn(ref_silu(v)); break;
+    }
+}
+
+size_t simt_panel_scratch_bytes(const SimtGemm& g) {
+    if (g.order != ORDER_PANEL192 || g.K < 2 * PANEL || g.M > 512 || g.only_if || g.row_mask) return 0;
+    const int panels = (g.K + PANEL - 1) / PANEL;
+    return size_t(panels) * size_t(g.M) * size_t(g.N) * sizeof(float);
+}
+
 cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s) {
     if (g.M <= 0 || g.N <= 0) return cudaSuccess;
+    const size_t need = simt_panel_scratch_bytes(g);
+    if (need && g.panel_scratch && g.panel_scratch_bytes >= need) {
+        const int panels = (g.K + PANEL - 1) / PANEL;
+        const dim3 grid((g.N + PT - 1) / PT, (g.M + PT - 1) / PT, panels);
+        simt_panel_kernel<<<grid, 256, 0, s>>>(g);
+        const int64_t n = int64_t(g.M) * g.N;
+        simt_panel_combine_kernel<<<blocks_for(n), TPB, 0, s>>>(g, panels);
+        return cudaGetLastError();
+    }
     // One tile per block; launches that are conditional on a device flag (only_if) or whose
     // tile rows exceed the grid's y limit use a bounded grid that strides over the tiles.
     const int64_t tm = (g.M + SB - 1) / SB;

@@ -102,7 +102,13 @@ struct SimtGemm {
     int row_group = 0, row_stride = 0, row_offset = 0;  // output row remap (as in GemmEpilogue)
     const int* only_if = nullptr;       // when set, the launch does nothing unless *only_if != 0
     const int8_t* row_mask = nullptr;   // when set, only rows m with row_mask[m] != 0 are written
+    // ORDER_PANEL192 with few rows: the 192-wide K panels run as separate blocks into this
+    // scratch ([panels][M][N] f32) and are summed in order by a second kernel (same result).
+    float* panel_scratch = nullptr;
+    size_t panel_scratch_bytes = 0;
 };
+// Bytes of panel scratch that simt_gemm uses for `g` (0: one pass, no scratch).
+size_t simt_panel_scratch_bytes(const SimtGemm& g);
 cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s);
 
 // Two-term f16 split of an f32 matrix for tensor-core products at near-f32 accuracy:
