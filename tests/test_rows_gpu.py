@@ -58,3 +58,33 @@ def test_split_f16(dev, big):
     err = np.abs(hi + lo - a.astype(np.float64))[ok]
     assert np.all(err <= 2.0 ** -21 * np.abs(a[ok]) + 2.0 ** -24), float(err.max())
     assert int(flag.item()) == int(big)
+
+
+@pytest.mark.parametrize("R,T,patches,ps", [(64, 2048, 8, 32), (37, 512, 3, 32), (5, 96, 2, 8), (9, 4096, 33, 32)])
+def test_refine_bitwise(dev, R, T, patches, ps):
+    """Refine of one decode block (reference src/refine.cpp:32-106) equals the oracle's float64
+    restatement bit for bit: the warp-parallel kernel keeps every operation and its order."""
+    from helpers import unit_config
+    Q, mi = 21, 10
+    rng = np.random.default_rng(R * 7 + T)
+    x = (np.cumsum(rng.standard_normal((R, T)), axis=1) + rng.uniform(-50, 50, (R, 1))).astype(np.float32)
+    m = (rng.random((R, T)) > 0.1).astype(np.int8)
+    x[m == 0] = 0
+    c = unit_config(patch_size=ps, minimum_scale=1e-6)
+    _, loc, sc = op.scale_rows(c, x, m, R, T)
+    loc0 = np.ascontiguousarray(loc.reshape(R, T)[:, -1])
+    sc0 = np.ascontiguousarray(sc.reshape(R, T)[:, -1])
+    q = np.sort(rng.standard_normal((R, patches * ps, Q)).astype(np.float32) * sc0[:, None, None] + loc0[:, None, None],
+                axis=-1).astype(np.float32)
+    role = np.zeros(R, np.int8)
+    role[-1] = 2
+    want = op.refine_block(c, q, x.reshape(-1), m.reshape(-1), R, T, patches, (role == 0).astype(np.int8))
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    dq, dx, dm, dr, dl, ds = t(q), t(x), t(m), t(role), t(loc0), t(sc0)
+    out = torch.full_like(dq, float("nan"))
+    rc = tb.lib().tsb_refine_static(dq.data_ptr(), dx.data_ptr(), dm.data_ptr(), dr.data_ptr(), dl.data_ptr(),
+                                    ds.data_ptr(), R, T, patches, ps, Q, mi, C.c_double(1e-6), out.data_ptr(), None)
+    assert rc == 0, tb.lib().timestral_capi_last_error(None)
+    got = out.cpu().numpy()
+    want = want.reshape(got.shape)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), float(np.abs(got - want).max())

@@ -749,11 +749,129 @@ cudaError_t quantile_head(const RowConfig& c, const float* raw, int R, int P_all
     return cudaGetLastError();
 }
 
+// NumPy pairwise float64 sum of val(0) .. val(n - 1) for n <= 128 (the same leaves and order
+// as numpy_sum_dev on an array of those values).
+template <class F>
+__device__ __forceinline__ double numpy_sum_small(F val, int n) {
+    if (n < 8) { double r = -0.0; for (int i = 0; i < n; ++i) r = __dadd_rn(r, val(i)); return r; }
+    double r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = val(j);
+    int i = 8;
+    for (; i < n - (n % 8); i += 8)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] = __dadd_rn(r[j], val(i + j));
+    double out = __dadd_rn(__dadd_rn(__dadd_rn(r[0], r[1]), __dadd_rn(r[2], r[3])),
+                           __dadd_rn(__dadd_rn(r[4], r[5]), __dadd_rn(r[6], r[7])));
+    for (; i < n; ++i) out = __dadd_rn(out, val(i));
+    return out;
+}
+
+// refine_kernel with one warp per row (patch_size <= 128): the per-patch statistics one patch
+// per lane, the Hillis-Steele rounds over chunks of 32 elements from the top (each chunk read
+// before it is written, as the in-place top-down loop), the block frames with one step per
+// lane, the output one step per lane. Every value is computed by the same operations in the
+// same order as refine_kernel; the scratch layout is the same.
+__global__ void __launch_bounds__(128) refine_warp_kernel(const RowConfig c, const float* __restrict__ q,
+                                                          const float* __restrict__ rows, const int8_t* __restrict__ mask,
+                                                          int stride, const int8_t* __restrict__ role,
+                                                          const float* __restrict__ loc0a, const float* __restrict__ scale0a,
+                                                          int R, int T, int h, double clip, double* __restrict__ scratch,
+                                                          float* __restrict__ out) {
+    const int r = blockIdx.x * 4 + threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (r >= R) return;                                       // uniform across the warp
+    const int ps = c.ps, Q = c.Q, mi = c.median, cp = T / ps, n = cp + h, steps = h * ps;
+    const float* qr = q + int64_t(r) * steps * Q;
+    float* outr = out + int64_t(r) * steps * Q;
+    if (role && role[r] != 0) {
+        for (int i = lane; i < steps * Q; i += 32) outr[i] = qr[i];
+        return;
+    }
+    double* st = scratch + int64_t(r) * (3 * int64_t(n) + 2 * ps + 2 * h);
+    double* terms = st + 3 * int64_t(n);
+    double* folded = terms + ps;
+    double* floc = folded + ps;
+    double* fscale = floc + h;
+    const float* x = rows + int64_t(r) * stride;
+    const int8_t* m = mask + int64_t(r) * stride;
+    for (int p = lane; p < cp; p += 32) {
+        const int s0 = p * ps;
+        const double w = numpy_sum_small([&](int k) { return double(m[s0 + k]); }, ps);
+        const double mean = __ddiv_rn(numpy_sum_small([&](int k) { return __dmul_rn(double(x[s0 + k]), double(m[s0 + k])); }, ps),
+                                      fmax(w, 1.0));
+        const double m2 = numpy_sum_small([&](int k) {
+            const double d = __dsub_rn(double(x[s0 + k]), mean);
+            return __dmul_rn(double(m[s0 + k]), __dmul_rn(d, d));
+        }, ps);
+        st[3 * p] = w; st[3 * p + 1] = w == 0 ? 0.0 : mean; st[3 * p + 2] = w == 0 ? 0.0 : m2;
+    }
+    for (int p = cp + lane; p < n; p += 32) { st[3 * p] = 0; st[3 * p + 1] = 0; st[3 * p + 2] = 0; }
+    __syncwarp();
+    for (int d = 1; d < n;) {
+        for (int c0 = ((n - 1) / 32) * 32; c0 >= 0; c0 -= 32) {
+            const int i = c0 + lane;
+            WS nw{0, 0, 0};
+            if (i < n) {
+                const WS prev = i >= d ? WS{st[3 * (i - d)], st[3 * (i - d) + 1], st[3 * (i - d) + 2]} : WS{0, 0, 0};
+                const WS cur{st[3 * i], st[3 * i + 1], st[3 * i + 2]};
+                nw = combine(prev, cur);
+            }
+            __syncwarp();
+            if (i < n) { st[3 * i] = nw.w; st[3 * i + 1] = nw.mean; st[3 * i + 2] = nw.m2; }
+            __syncwarp();
+        }
+        if (d > n / 2) break;
+        d *= 2;
+    }
+    const float loc0 = loc0a[r], scale0 = scale0a[r];
+    WS state{st[3 * (cp - 1)], st[3 * (cp - 1) + 1], st[3 * (cp - 1) + 2]};
+    const double offset = state.mean;
+    for (int j = 0; j < h; ++j) {
+        const double var = fmax(__ddiv_rn(state.m2, fmax(__dsub_rn(state.w, 1.0), 1.0)), 0.0);
+        const double sc = fmax(sqrt(var), c.minimum_scale);
+        if (lane == 0) { floc[j] = state.mean; fscale[j] = sc; }
+        for (int k = lane; k < ps; k += 32) {
+            const double med = __ddiv_rn(__dsub_rn(double(qr[(j * ps + k) * Q + mi]), double(loc0)), double(scale0));
+            const double v = __dsub_rn(__dadd_rn(__dmul_rn(med, sc), state.mean), offset);
+            folded[k] = __dadd_rn(fmin(fmax(v, -clip), clip), offset);
+        }
+        __syncwarp();
+        const double mean = __ddiv_rn(numpy_sum_small([&](int k) { return folded[k]; }, ps), double(ps));
+        for (int k = lane; k < ps; k += 32) { const double dd = __dsub_rn(folded[k], mean); terms[k] = __dmul_rn(dd, dd); }
+        __syncwarp();
+        state = combine(state, WS{double(ps), mean, numpy_sum_small([&](int k) { return terms[k]; }, ps)});
+        __syncwarp();
+    }
+    for (int t = lane; t < steps; t += 32) {
+        const int j = t / ps;
+        const float loc = j ? float(floc[j]) : loc0, sc = j ? float(fscale[j]) : scale0;
+        float lo = INFINITY, hi = -INFINITY;
+        float vals[64];
+        for (int k = 0; k < Q; ++k) {
+            const float nrm = __fdiv_rn(__fsub_rn(qr[t * Q + k], loc0), scale0);
+            const float v = __fadd_rn(__fmul_rn(nrm, sc), loc);
+            vals[k] = v;
+            if (isfinite(v)) { lo = fminf(lo, v); hi = fmaxf(hi, v); }
+        }
+        for (int k = 0; k < Q; ++k) {
+            float v = vals[k];
+            if (v == INFINITY) v = isfinite(hi) ? hi : 0.f;
+            else if (v == -INFINITY) v = isfinite(lo) ? lo : 0.f;
+            outr[t * Q + k] = v;
+        }
+    }
+}
+
 cudaError_t refine(const RowConfig& c, const float* q, const float* rows, const int8_t* mask, int stride, const int8_t* role,
                    const float* loc0, const float* scale0, int R, int T, int h, double clip, double* scratch, float* out,
                    cudaStream_t s) {
     if (c.Q > 64) return cudaErrorInvalidValue;
-    refine_kernel<<<blocks_for(R, 64), 64, 0, s>>>(c, q, rows, mask, stride, role, loc0, scale0, R, T, h, clip, scratch, out);
+    if (c.ps <= 128)
+        refine_warp_kernel<<<unsigned((R + 3) / 4), 128, 0, s>>>(c, q, rows, mask, stride, role, loc0, scale0, R, T, h, clip,
+                                                                 scratch, out);
+    else
+        refine_kernel<<<blocks_for(R, 64), 64, 0, s>>>(c, q, rows, mask, stride, role, loc0, scale0, R, T, h, clip, scratch,
+                                                       out);
     return cudaGetLastError();
 }
 
