@@ -92,8 +92,14 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons of one GPU, sampled every 200 ms."""
+    """SM clock and clock-event (throttle) reasons of one GPU during the timed region, read
+    through NVML every 20 ms from a thread (reading only; nothing is set). Falls back to
+    `nvidia-smi -lms 200` when NVML is not importable."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
@@ -102,8 +108,33 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines = []
+        self.samples = []         # (sm_mhz, reasons bitmask)
+        self.max_mhz = None
+        self.stop_flag = threading.Event()
+        self.thread = None
+        self.nvml = None
 
     def start(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nvml = nv
+            handle = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM))
+
+            def poll():
+                while not self.stop_flag.is_set():
+                    try:
+                        self.samples.append((float(nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)),
+                                             int(nv.nvmlDeviceGetCurrentClocksEventReasons(handle))))
+                    except Exception:
+                        pass
+                    self.stop_flag.wait(0.02)
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -117,6 +148,17 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            reasons = set()
+            for _, mask in self.samples:
+                for name, attr in self.REASONS:
+                    if mask & getattr(self.nvml, attr, 0):
+                        reasons.add(name)
+            sm = [mhz for mhz, _ in self.samples]
+            return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml, 20 ms"}
         if self.proc:
             self.proc.terminate()
             try:
@@ -124,7 +166,7 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        names = [n for n, _ in self.REASONS]
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 8:
@@ -138,7 +180,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
 def workload(cfg: str, c: dict, lo: int, hi: int):
