@@ -57,6 +57,10 @@ TIMESTRAL_API int64_t tsb_last_launch_count(timestral_ctx* ctx);
 /* Compute path chosen for the loaded model: 1 = tensor cores (F16/Q8_0 weights),
  * 0 = F32 CUDA-core path. */
 TIMESTRAL_API int tsb_model_path(timestral_ctx* ctx);
+/* Host-side dequantisation of `rows` rows of ne0 elements of a block-quantised GGUF type
+ * (8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K) into float, as the loader expands such weights.
+ * No GPU is used. */
+TIMESTRAL_API int tsb_dequantize_rows(uint32_t type, const void* src, int64_t rows, int64_t ne0, float* dst);
 /* Geometry of the last decode block of the handle's last forecast: model rows (both
  * symmetric passes, every row role), tokens per row, context patches, decode blocks. */
 TIMESTRAL_API int tsb_last_geometry(timestral_ctx* ctx, int64_t* rows, int32_t* S, int32_t* L, int32_t* blocks);

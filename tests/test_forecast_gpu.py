@@ -107,8 +107,10 @@ def test_209m_f32_cfg1():
 
 
 # ---- F16 weights: tensor-core path --------------------------------------------------------
-@pytest.mark.parametrize("B,V,T,H", [(3, 1, 256, 64), (2, 3, 200, 40)])
+@pytest.mark.parametrize("B,V,T,H", [(3, 1, 256, 64), (2, 3, 200, 40), (2, 1, 256, 1100), (1, 2, 128, 1060)])
 def test_small_f16(B, V, T, H):
+    """H > 1024 steps takes two decode blocks (32 patches each): the second block re-encodes the
+    context extended by the first block's median forecast (reference src/forecaster.cpp:19-67)."""
     m, o = models(sy.spec_small(), "f16")
     assert m.tensor_core_path
     x = random_context(B, V, T, seed=T + H)
@@ -140,6 +142,23 @@ def test_209m_q8_reported():
     x = sy.series_seasonal(1, 512)
     mean, mx = check_nd(m.forecast(x, 64), o.forecast(x, 64), x, 32, 0.05)
     print(f"Q8_0 device (f16 dequant) vs oracle Q8_0 restatement: mean {mean:.3e} max {mx:.3e}")
+
+
+@pytest.mark.parametrize("kind,bound", [("q6_k", 0.05), ("q5_k", 0.1), ("q4_k", 0.2)])
+def test_kquant_reported(kind, bound):
+    """K-quant weights are dequantised to F16 at load and run on the tensor-core path; reported
+    against the oracle's F32 forecast of the unquantised weights (the reference multiplies
+    K-quant weights with Q8_K activations inside ggml, which is not restated)."""
+    spec = sy.spec_k256()
+    m = tb.Model(sy.cached_model(spec, kind))
+    assert m.tensor_core_path
+    o = op.OracleModel(sy.cached_model(spec, "f32"))
+    x = random_context(2, 2, 256, seed=9)
+    g, r = m.forecast(x, 64), o.forecast(x, 64)
+    assert np.all(np.isfinite(g)) and np.all(np.diff(g, axis=-1) >= 0)
+    mean, mx = check_nd(g, r, x, 32, bound)
+    print(f"{kind} device (f16 dequant) vs oracle F32 of the unquantised weights: mean {mean:.3e} max {mx:.3e}")
+    m.close()
 
 
 # ---- invariants of the reference (tests/test_forecast.cpp:39-53) on the device -----------

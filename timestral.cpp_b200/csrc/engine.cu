@@ -9,6 +9,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "engine.cuh"
+#include "gguf.hpp"
 #include "gemm_tc.cuh"
 #include "rows.cuh"
 
@@ -121,7 +122,7 @@ struct Engine::Impl {
 
     HostTensor t(const std::string& n) const { return mv.tensor(n); }
 
-    // Row values of a weight as float (exact for F32/F16; Q8_0 as f16(d)*q).
+    // Row values of a weight as float (exact for F32/F16; block-quantised types dequantised).
     std::vector<float> rows_f32(const HostTensor& w) const {
         const size_t K = size_t(w.ne0), N = size_t(w.ne1);
         std::vector<float> out(K * N);
@@ -130,16 +131,13 @@ struct Engine::Impl {
             const uint16_t* p = static_cast<const uint16_t*>(w.data);
             for (size_t i = 0; i < out.size(); ++i) out[i] = half_bits_to_float(p[i]);
         } else {
+            // Block-quantised rows (Q8_0, Q4_K, Q5_K, Q6_K), dequantised as ggml publishes.
             const uint8_t* p = static_cast<const uint8_t*>(w.data);
-            const size_t nb = K / 32;
+            const size_t row = ts::ggml_row_bytes(uint32_t(w.type), int64_t(K));
+            if (!row) throw std::runtime_error("unsupported weight type " + std::to_string(w.type));
             for (size_t n = 0; n < N; ++n)
-                for (size_t b = 0; b < nb; ++b) {
-                    const uint8_t* blk = p + (n * nb + b) * 34;
-                    uint16_t dh;
-                    std::memcpy(&dh, blk, 2);
-                    const float d = half_bits_to_float(dh);
-                    for (size_t j = 0; j < 32; ++j) out[n * K + b * 32 + j] = d * float(int8_t(blk[2 + j]));
-                }
+                if (!ts::dequantize_row(uint32_t(w.type), p + n * row, int64_t(K), out.data() + n * K))
+                    throw std::runtime_error("unsupported weight type " + std::to_string(w.type));
         }
         return out;
     }

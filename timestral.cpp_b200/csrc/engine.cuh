@@ -13,7 +13,7 @@
 
 namespace tsb {
 
-enum TensorType : int { TT_F32 = 0, TT_F16 = 1, TT_Q8_0 = 8 };
+enum TensorType : int { TT_F32 = 0, TT_F16 = 1, TT_Q8_0 = 8, TT_Q4_K = 12, TT_Q5_K = 13, TT_Q6_K = 14 };
 
 struct HostTensor {
     int type = TT_F32;

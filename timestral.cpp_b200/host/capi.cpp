@@ -8,6 +8,7 @@
 
 #include "engine.cuh"
 #include "forecaster.hpp"
+#include "gguf.hpp"
 #include "model.hpp"
 
 #include <climits>
@@ -288,6 +289,16 @@ TIMESTRAL_API int tsb_last_geometry(timestral_ctx* c, int64_t* rows, int32_t* S,
     if (!c || !rows || !S || !L || !blocks) return TSB_ERR_ARG;
     const auto g = c->forecaster.engine().last_geometry();
     *rows = g.rows; *S = g.S; *L = g.L; *blocks = g.blocks;
+    return TSB_OK;
+}
+
+TIMESTRAL_API int tsb_dequantize_rows(uint32_t type, const void* src, int64_t rows, int64_t ne0, float* dst) {
+    if (!src || !dst || rows < 0 || ne0 <= 0) return TSB_ERR_ARG;
+    const size_t row = ts::ggml_row_bytes(type, ne0);
+    if (!row) return TSB_ERR_ARG;
+    for (int64_t r = 0; r < rows; ++r)
+        if (!ts::dequantize_row(type, static_cast<const uint8_t*>(src) + size_t(r) * row, ne0, dst + r * ne0))
+            return TSB_ERR_ARG;
     return TSB_OK;
 }
 

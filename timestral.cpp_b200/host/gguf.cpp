@@ -36,8 +36,135 @@ size_t ggml_row_bytes(uint32_t type, int64_t ne0) {
         case 0: return size_t(ne0) * 4;
         case 1: return size_t(ne0) * 2;
         case 8: return ne0 % 32 ? 0 : size_t(ne0 / 32) * 34;
+        case 12: return ne0 % 256 ? 0 : size_t(ne0 / 256) * 144;   // Q4_K
+        case 13: return ne0 % 256 ? 0 : size_t(ne0 / 256) * 176;   // Q5_K
+        case 14: return ne0 % 256 ? 0 : size_t(ne0 / 256) * 210;   // Q6_K
     }
     return 0;
+}
+
+namespace {
+float half_to_float(const uint8_t* p) {
+    uint16_t h;
+    std::memcpy(&h, p, 2);
+    const uint32_t sign = uint32_t(h >> 15) << 31, exp = (h >> 10) & 31, man = h & 1023;
+    uint32_t bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {   // subnormal: normalise
+            int e = -1;
+            uint32_t m = man;
+            do { m <<= 1; ++e; } while (!(m & 1024));
+            bits = sign | uint32_t(127 - 15 - e) << 23 | (m & 1023) << 13;
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7f800000u | man << 13;
+    } else {
+        bits = sign | (exp + 112) << 23 | man << 13;
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+// Six-bit scale and min of sub-block j (0..7) of a Q4_K/Q5_K super-block: bytes 0-3 hold the
+// low six bits of scales 0-3, bytes 4-7 those of mins 0-3, bytes 8-11 the low four bits of
+// scales/mins 4-7 whose top two bits sit in the top bits of bytes 0-7.
+void scale_min_k4(int j, const uint8_t* q, int* sc, int* m) {
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+}  // namespace
+
+bool dequantize_row(uint32_t type, const uint8_t* src, int64_t ne0, float* dst) {
+    if (ggml_row_bytes(type, ne0) == 0 && ne0 != 0) return false;
+    switch (type) {
+        case 12:   // Q4_K: d, dmin (f16), scales[12], qs[128]; value = (d*sc) * q - dmin*m
+            for (int64_t b = 0; b < ne0 / 256; ++b, src += 144) {
+                const float d = half_to_float(src), dmin = half_to_float(src + 2);
+                const uint8_t* scales = src + 4;
+                const uint8_t* qs = src + 16;
+                for (int g = 0; g < 4; ++g) {
+                    int sc0, m0, sc1, m1;
+                    scale_min_k4(2 * g, scales, &sc0, &m0);
+                    scale_min_k4(2 * g + 1, scales, &sc1, &m1);
+                    const float d0 = d * float(sc0), mm0 = dmin * float(m0);
+                    const float d1 = d * float(sc1), mm1 = dmin * float(m1);
+                    for (int l = 0; l < 32; ++l) {
+                        const float p0 = d0 * float(qs[32 * g + l] & 0xF);
+                        dst[b * 256 + 64 * g + l] = p0 - mm0;
+                    }
+                    for (int l = 0; l < 32; ++l) {
+                        const float p1 = d1 * float(qs[32 * g + l] >> 4);
+                        dst[b * 256 + 64 * g + 32 + l] = p1 - mm1;
+                    }
+                }
+            }
+            return true;
+        case 13:   // Q5_K: d, dmin, scales[12], qh[32], qs[128]; bit j of qh[l] is the fifth bit
+                   // of value l of sub-block j
+            for (int64_t b = 0; b < ne0 / 256; ++b, src += 176) {
+                const float d = half_to_float(src), dmin = half_to_float(src + 2);
+                const uint8_t* scales = src + 4;
+                const uint8_t* qh = src + 16;
+                const uint8_t* qs = src + 48;
+                for (int g = 0; g < 4; ++g) {
+                    int sc0, m0, sc1, m1;
+                    scale_min_k4(2 * g, scales, &sc0, &m0);
+                    scale_min_k4(2 * g + 1, scales, &sc1, &m1);
+                    const float d0 = d * float(sc0), mm0 = dmin * float(m0);
+                    const float d1 = d * float(sc1), mm1 = dmin * float(m1);
+                    for (int l = 0; l < 32; ++l) {
+                        const int q = (qs[32 * g + l] & 0xF) | (((qh[l] >> (2 * g)) & 1) << 4);
+                        const float p0 = d0 * float(q);
+                        dst[b * 256 + 64 * g + l] = p0 - mm0;
+                    }
+                    for (int l = 0; l < 32; ++l) {
+                        const int q = (qs[32 * g + l] >> 4) | (((qh[l] >> (2 * g + 1)) & 1) << 4);
+                        const float p1 = d1 * float(q);
+                        dst[b * 256 + 64 * g + 32 + l] = p1 - mm1;
+                    }
+                }
+            }
+            return true;
+        case 14:   // Q6_K: ql[128], qh[64], scales[16] (int8), d (f16); value = (d*scale) * (q - 32)
+            for (int64_t b = 0; b < ne0 / 256; ++b, src += 210) {
+                const uint8_t* ql = src;
+                const uint8_t* qh = src + 128;
+                const int8_t* sc = reinterpret_cast<const int8_t*>(src + 192);
+                const float d = half_to_float(src + 208);
+                for (int h = 0; h < 2; ++h) {
+                    const uint8_t* l0 = ql + 64 * h;
+                    const uint8_t* h0 = qh + 32 * h;
+                    const int8_t* s0 = sc + 8 * h;
+                    float* y = dst + b * 256 + 128 * h;
+                    for (int l = 0; l < 32; ++l) {
+                        const int is = l / 16;
+                        const int q1 = int((l0[l] & 0xF) | (((h0[l] >> 0) & 3) << 4)) - 32;
+                        const int q2 = int((l0[l + 32] & 0xF) | (((h0[l] >> 2) & 3) << 4)) - 32;
+                        const int q3 = int((l0[l] >> 4) | (((h0[l] >> 4) & 3) << 4)) - 32;
+                        const int q4 = int((l0[l + 32] >> 4) | (((h0[l] >> 6) & 3) << 4)) - 32;
+                        y[l] = (d * float(s0[is])) * float(q1);
+                        y[l + 32] = (d * float(s0[is + 2])) * float(q2);
+                        y[l + 64] = (d * float(s0[is + 4])) * float(q3);
+                        y[l + 96] = (d * float(s0[is + 6])) * float(q4);
+                    }
+                }
+            }
+            return true;
+        case 8:    // Q8_0: d (f16), q[32] (int8); value = d * q
+            for (int64_t b = 0; b < ne0 / 32; ++b, src += 34) {
+                const float d = half_to_float(src);
+                for (int j = 0; j < 32; ++j) dst[b * 32 + j] = d * float(int8_t(src[2 + j]));
+            }
+            return true;
+    }
+    return false;
 }
 
 MappedFile::MappedFile(const std::string& path) {

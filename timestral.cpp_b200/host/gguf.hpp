@@ -71,9 +71,13 @@ private:
     size_t data_offset_ = 0, alignment_ = 32;
 };
 
-// Bytes of a tensor of ggml type `type` with ne0 x rows elements (F32, F16, Q8_0;
-// 0 for any other type).
+// Bytes of one row of ne0 elements of ggml type `type` (F32, F16, Q8_0, Q4_K, Q5_K, Q6_K;
+// 0 for any other type or a row that is not a whole number of blocks).
 size_t ggml_row_bytes(uint32_t type, int64_t ne0);
+// Values of one row of a block-quantised ggml type (Q8_0, Q4_K, Q5_K, Q6_K) as float,
+// with ggml's published dequantisation (per-block f16 scales and mins; single-precision
+// products in the same order). Returns false for other types.
+bool dequantize_row(uint32_t type, const uint8_t* src, int64_t ne0, float* dst);
 const char* ggml_type_name(uint32_t type);
 
 }  // namespace ts

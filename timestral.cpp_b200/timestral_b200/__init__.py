@@ -59,6 +59,7 @@ SIGNATURES = {
     "tsb_timing_reset": (None, [C.c_void_p]),
     "tsb_last_launch_count": (C.c_int64, [C.c_void_p]),
     "tsb_model_path": (C.c_int, [C.c_void_p]),
+    "tsb_dequantize_rows": (C.c_int, [C.c_uint32, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]),
     "tsb_last_geometry": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64)] + [C.POINTER(C.c_int32)] * 3),
     "tsb_test_gemm": (C.c_int, [C.POINTER(GemmTest), C.POINTER(C.c_int32)]),
     "tsb_test_attention_time": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 4 + [C.POINTER(C.c_int32)]),

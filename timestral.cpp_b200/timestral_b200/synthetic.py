@@ -91,6 +91,14 @@ def spec_tiny(bias: bool = False) -> ModelSpec:
                      block_size=4, context_length=2048, attn_bias=bias, mlp_bias=bias)
 
 
+def spec_k256() -> ModelSpec:
+    """spec_small with 256-wide rows (D = 256, four heads, F = 512), so that every reduced
+    weight row is a whole number of 256-value K-quant super-blocks."""
+    return ModelSpec(name="timestral-k256", patch_size=32, d_model=256, num_heads=4, mlp_hidden_dim=512,
+                     block_schedule=("time", "variate", "time_variate", "variate_time"),
+                     quantile_knots=KNOTS_21, block_size=32, context_length=4096)
+
+
 def spec_small(bias: bool = False) -> ModelSpec:
     """A model with the 209M head and patch geometry (head_dim 64, patch 32, 21 knots) but
     two heads and four layers, one of each kind, so that tensor-core shapes are exercised
@@ -184,11 +192,82 @@ def init_weights(s: ModelSpec, seed: int = 0):
     return w
 
 
+# ---------------------------------------------------------------------------------------
+# K-quant encoders for test models. They write valid ggml Q4_K / Q5_K / Q6_K super-blocks of
+# 256 values (layouts as ggml publishes them) with simple min/max scales; they are not ggml's
+# quantiser (which searches the scales), only a way to produce K-quant GGUFs to load.
+
+def _f16(x):
+    return np.asarray(x, np.float32).astype(np.float16)
+
+
+def quantize_k(a, kind: str) -> np.ndarray:
+    """a: [N][K] float32 with K % 256 == 0 -> uint8 [N][K/256 * block bytes]."""
+    a = np.ascontiguousarray(a, np.float32)
+    N, K = a.shape
+    assert K % 256 == 0, K
+    x = a.reshape(-1, 256)
+    nb = x.shape[0]
+    if kind in ("q4_k", "q5_k"):
+        levels = 15 if kind == "q4_k" else 31
+        sub = x.reshape(nb, 8, 32)
+        mn = np.minimum(sub.min(axis=2), 0.0)
+        mx = sub.max(axis=2)
+        scale = (mx - mn) / levels
+        mins = -mn
+        d16 = _f16(scale.max(axis=1) / 63.0)
+        m16 = _f16(mins.max(axis=1) / 63.0)
+        d = d16.astype(np.float32)[:, None]
+        dm = m16.astype(np.float32)[:, None]
+        sc = np.where(d > 0, np.clip(np.rint(scale / np.where(d > 0, d, 1)), 0, 63), 0).astype(np.int32)
+        mq = np.where(dm > 0, np.clip(np.rint(mins / np.where(dm > 0, dm, 1)), 0, 63), 0).astype(np.int32)
+        step = (d * sc)[:, :, None]
+        off = (dm * mq)[:, :, None]
+        q = np.where(step > 0, np.clip(np.rint((sub + off) / np.where(step > 0, step, 1)), 0, levels), 0).astype(np.int32)
+        scales = np.zeros((nb, 12), np.uint8)
+        scales[:, 0:4] = (sc[:, 0:4] & 63) | ((sc[:, 4:8] >> 4) << 6)
+        scales[:, 4:8] = (mq[:, 0:4] & 63) | ((mq[:, 4:8] >> 4) << 6)
+        scales[:, 8:12] = (sc[:, 4:8] & 0xF) | ((mq[:, 4:8] & 0xF) << 4)
+        lo = (q & 0xF).astype(np.uint8).reshape(nb, 4, 2, 32)
+        qs = (lo[:, :, 0, :] | (lo[:, :, 1, :] << 4)).reshape(nb, 128)
+        parts = [d16.reshape(nb, 1).view(np.uint8), m16.reshape(nb, 1).view(np.uint8), scales]
+        if kind == "q5_k":
+            hi = ((q >> 4) & 1).astype(np.uint8)                       # [nb, 8, 32]
+            qh = np.zeros((nb, 32), np.uint8)
+            for j in range(8):
+                qh |= hi[:, j, :] << j
+            parts.append(qh)
+        parts.append(qs)
+        out = np.concatenate(parts, axis=1)
+    elif kind == "q6_k":
+        sub = x.reshape(nb, 16, 16)
+        scale = np.abs(sub).max(axis=2) / 31.0
+        d16 = _f16(scale.max(axis=1) / 127.0)
+        d = d16.astype(np.float32)[:, None]
+        sc = np.where(d > 0, np.clip(np.rint(scale / np.where(d > 0, d, 1)), 0, 127), 0).astype(np.int32)
+        step = (d * sc)[:, :, None]
+        q = np.where(step > 0, np.clip(np.rint(sub / np.where(step > 0, step, 1)), -32, 31), 0).astype(np.int32) + 32
+        q = q.reshape(nb, 2, 4, 32)                                    # [half][t][l]: value l + 32 t
+        ql = np.zeros((nb, 2, 64), np.uint8)
+        ql[:, :, 0:32] = (q[:, :, 0, :] & 0xF) | ((q[:, :, 2, :] & 0xF) << 4)
+        ql[:, :, 32:64] = (q[:, :, 1, :] & 0xF) | ((q[:, :, 3, :] & 0xF) << 4)
+        qh = ((q[:, :, 0, :] >> 4) | ((q[:, :, 1, :] >> 4) << 2) | ((q[:, :, 2, :] >> 4) << 4) |
+              ((q[:, :, 3, :] >> 4) << 6)).astype(np.uint8)
+        out = np.concatenate([ql.reshape(nb, 128), qh.reshape(nb, 64), sc.astype(np.int8).view(np.uint8),
+                              d16.reshape(nb, 1).view(np.uint8)], axis=1)
+    else:
+        raise ValueError(kind)
+    return np.ascontiguousarray(out.reshape(N, -1))
+
+
+K_QUANT_TYPES = {"q4_k": 12, "q5_k": 13, "q6_k": 14}
+
+
 def write_gguf(path, s: ModelSpec, outtype: str = "f32", seed: int = 0, weights=None) -> Path:
-    """Write one model file. outtype: f32, f16 or q8_0 (reduced weights only)."""
+    """Write one model file. outtype: f32, f16, q8_0, q4_k, q5_k or q6_k (reduced weights only)."""
     import gguf
     from gguf import GGUFValueType as VT
-    if outtype not in ("f32", "f16", "q8_0"):
+    if outtype not in ("f32", "f16", "q8_0", "q4_k", "q5_k", "q6_k"):
         raise ValueError(outtype)
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)
@@ -251,6 +330,9 @@ def write_gguf(path, s: ModelSpec, outtype: str = "f32", seed: int = 0, weights=
             from gguf.quants import quantize
             q = quantize(a, gguf.GGMLQuantizationType.Q8_0)
             wr.add_tensor(name, np.ascontiguousarray(q), raw_dtype=gguf.GGMLQuantizationType.Q8_0)
+        elif outtype in K_QUANT_TYPES and reduced_weight_name(name):
+            q = quantize_k(a.reshape(a.shape[0], -1), outtype)
+            wr.add_tensor(name, q, raw_dtype=gguf.GGMLQuantizationType(K_QUANT_TYPES[outtype]))
         else:
             wr.add_tensor(name, a, raw_dtype=gguf.GGMLQuantizationType.F32)
     wr.write_header_to_file()
