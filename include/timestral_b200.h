@@ -112,6 +112,16 @@ TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_error);
 TIMESTRAL_API int tsb_test_attention_time(const void* q, const void* k, const void* v, const void* gate, void* out,
                                           const uint32_t* key_valid, int32_t rows, int32_t H, int32_t S, int32_t N,
                                           int32_t* dev_error);
+/* Time attention with the full mask description: N encoder tokens, L context patches,
+ * covariate layout (cov != 0: S = 2N, role [rows] 0 target / 1 past / 2 known, decode blocks
+ * of block_size patches). kernel: 0 the engine's choice, 1 the S <= 128 tensor-core kernel,
+ * 2 the tiled tensor-core kernel (any S), 3 the CUDA-core kernel. Same layouts as above.
+ * repeat > 0 with ms non-NULL: after the checked launch, *ms = the average device time of
+ * `repeat` more launches. */
+TIMESTRAL_API int tsb_test_attention_time_ex(const void* q, const void* k, const void* v, const void* gate, void* out,
+                                             const uint32_t* key_valid, const int8_t* role, int32_t rows, int32_t H,
+                                             int32_t S, int32_t N, int32_t L, int32_t cov, int32_t block_size,
+                                             int32_t kernel, int32_t repeat, float* ms, int32_t* dev_error);
 /* f16 hi/lo split used by the tensor-core patch projections: out [rows][3K] f16 =
  * [hi | hi | lo] of each f32 row of a; sets *d_overflow (device int) when any |a| > 30000. */
 TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, void* out, int32_t* d_overflow);

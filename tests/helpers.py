@@ -28,3 +28,33 @@ def i8(x):
 
 def bits(a):
     return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def time_mask_torch(valid, role, N, L, S, cov, bs):
+    """[rows, S, S] bool torch mask: query q may attend key k on the time axis (reference
+    src/masks.cpp:21-26), restricted to the keys the reference computes (keys < N for encoder
+    queries, src/layers.cpp:591). valid: [rows, N] bool key-valid patches; role: [rows] int8
+    (0 target, 1 past, 2 known; used on the covariate layout, S = 2N, L context patches,
+    decode blocks of bs patches)."""
+    import torch
+    rows = valid.shape[0]
+    q = torch.arange(S)[:, None]
+    k = torch.arange(S)[None, :]
+    kv = torch.zeros(rows, S, dtype=torch.bool)
+    kv[:, :N] = valid
+    kvk = kv[:, None, :].expand(rows, S, S)
+    if not cov:
+        enc = (q < N) & (k < N) & ((kvk & (k <= q)) | (q == k))
+        dec = (q >= N) & (((k < N) & kvk) | ((k >= N) & (k <= q)))
+        return enc | dec
+    known = (role.long() == 2)[:, None, None]
+
+    def anchor(p):
+        return torch.where(p >= L, L + bs * torch.div(p - L, bs, rounding_mode="floor"), torch.zeros_like(p))
+
+    enc = (q < N) & (k < N) & ((kvk & (known | (k <= q))) | (q == k))
+    qp, kp = q - N, k - N
+    qa = qp >= L
+    dec_ctx = (q >= N) & (k < N) & kvk & qa & (k < anchor(qp))
+    dec_dec = (q >= N) & (k >= N) & ((q == k) | ((k <= q) & qa & (kp >= L) & (anchor(qp) == anchor(kp))))
+    return enc | dec_ctx | dec_dec

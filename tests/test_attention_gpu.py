@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 
 import timestral_b200 as tb
+from helpers import time_mask_torch
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
@@ -128,3 +129,54 @@ def test_attention_variate_fast(dev, G, S, N, cov):
     scale = want.abs().max().item()
     err = (got - want).abs()
     assert (err <= 2e-3 * scale + want.abs() * 2.0 ** -10).all(), float(err.max())
+
+
+@pytest.mark.parametrize("S,N,L,cov,kernel,dense", [(1056, 1024, 1024, 0, 2, False), (300, 280, 280, 0, 2, False),
+                                                    (129, 128, 128, 0, 2, False), (72, 64, 64, 0, 2, False),
+                                                    (1, 1, 1, 0, 2, False), (200, 190, 190, 0, 0, False),
+                                                    (140, 70, 64, 1, 2, False), (1200, 600, 560, 1, 2, False),
+                                                    (2112, 1056, 1024, 1, 0, False), (72, 36, 32, 1, 2, False),
+                                                    (1056, 1024, 1024, 0, 2, True), (1200, 600, 560, 1, 2, True),
+                                                    (520, 512, 512, 0, 2, True)])
+def test_attention_time_long(dev, S, N, L, cov, kernel, dense):
+    """Tiled tensor-core time attention (key tiles of 64, query tiles of 128, lazy rescaling
+    of O) against the float64 restatement, with and without the covariate layout."""
+    rows, H, bs = 5, 2, 32
+    g = torch.Generator().manual_seed(S * 7 + N + cov)
+    q = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
+    k = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
+    # a few large logits late in the row force the reference maximum to move (rescaling)
+    k[:, :, S // 2 :: 97] *= 3
+    v = torch.randn(rows, H, S, 64, generator=g).half()
+    gate = torch.rand(rows, H, S, 64, generator=g).half()
+    valid = torch.rand(rows, N, generator=g) > (0.0 if dense else 0.2)   # dense: unmasked key tiles
+    if dense:
+        valid[:] = True
+    role = torch.tensor([0, 1, 2, 2, 0][:rows], dtype=torch.int8)
+    words = (N + 31) // 32
+    bits = np.zeros((rows, words), np.uint32)
+    vn = valid.numpy()
+    for p in range(N):
+        bits[:, p // 32] |= vn[:, p].astype(np.uint32) << np.uint32(p % 32)
+    allowed = time_mask_torch(valid, role, N, L, S, cov, bs).to(dev)
+    qd, kd, vd, gd = (t.to(dev).double() for t in (q, k, v, gate))
+    s = torch.einsum("rhqd,rhkd->rhqk", qd, kd) / 8.0
+    s = s.masked_fill(~allowed[:, None], float("-inf"))
+    want = torch.einsum("rhqk,rhkd->rhqd", torch.softmax(s, dim=-1), vd) * gd
+    del s
+    want = want.permute(0, 2, 1, 3).reshape(rows * S, H * 64).cpu()
+    dbits = torch.from_numpy(bits.view(np.int32)).to(dev)
+    drole = role.to(dev)
+    out = torch.full((rows * S, H * 64), float("nan"), device=dev, dtype=torch.float16)
+    err = C.c_int32(0)
+    dq, dk, dv, dg = q.to(dev), k.to(dev), v.to(dev), gate.to(dev)
+    rc = tb.lib().tsb_test_attention_time_ex(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), out.data_ptr(),
+                                             dbits.data_ptr(), drole.data_ptr(), rows, H, S, N, L, cov, bs, kernel, 0, None,
+                                             C.byref(err))
+    assert rc == 0, (rc, err.value)
+    got = out.cpu().double()
+    assert torch.isfinite(got).all()
+    scale = want.abs().reshape(rows, S, H, 64).amax(dim=(1, 3), keepdim=True).expand(rows, S, H, 64).reshape(rows * S, H * 64)
+    tol = 4e-3 * scale + want.abs() * 2.0 ** -10
+    bad = (got - want).abs() > tol
+    assert not bad.any(), f"max err {(got - want).abs().max().item():.3e} at {bad.nonzero()[:4].tolist()}"

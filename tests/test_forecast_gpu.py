@@ -118,6 +118,30 @@ def test_small_f16(B, V, T, H):
     check_nd(g, r, x, 32, F16_MEAN_ND)
 
 
+@pytest.mark.parametrize("B,V,T,H", [(1, 1, 4096, 64), (1, 2, 32768, 1024), (2, 1, 9000, 300)])
+def test_small_f16_long_rows(B, V, T, H):
+    """Rows longer than 128 tokens (S = 130, 1056, 291) run the tiled tensor-core attention."""
+    spec = sy.spec_small() if T <= 4096 else sy.spec_small_long()
+    m, o = models(spec, "f16")
+    x = random_context(B, V, T, seed=T + H)
+    g, r = m.forecast(x, H), o.forecast(x, H)
+    assert m.last_geometry()[1] > 128
+    check_nd(g, r, x, 32, F16_MEAN_ND)
+
+
+def test_small_f16_long_covariates():
+    """Covariate layout with long rows (S = 2N = 584): both streams on the tiled kernel."""
+    m, o = models(sy.spec_small_long(), "f16")
+    rng = np.random.default_rng(31)
+    B, V, T, H = 1, 1, 9000, 300
+    x = random_context(B, V, T, seed=32)
+    kw = dict(past=rng.standard_normal((B, 1, T)).astype(np.float32),
+              known=rng.standard_normal((B, 2, T + H)).astype(np.float32))
+    g, r = m.forecast(x, H, **kw), o.forecast(x, H, **kw)
+    assert m.last_geometry()[1] > 128
+    check_nd(g, r, x, 32, F16_MEAN_ND)
+
+
 def test_small_f16_covariates():
     m, o = models(sy.spec_small(True), "f16")
     rng = np.random.default_rng(21)

@@ -418,6 +418,468 @@ cudaError_t launch_attn_tc(const __half* q, const __half* k, const __half* v, co
 }
 
 // ---------------------------------------------------------------------------------------
+// Tensor-core time attention for long rows (S > 128: context_length / patch_size up to
+// 1024 context patches plus a decode block, twice that on the covariate layout).
+//
+// One problem = (tile of 128 query tokens, row, head). Query tiles are aligned to the end of
+// the row, so the partial tile is the first one, whose causal keys fit in one key tile;
+// problems with the most key tiles run first. Keys and values stream through separate
+// four-stage shared-memory rings in tiles of 64 tokens: a key stage is free once its score
+// product completes, a value stage once its P V product does.
+// Warps 0-3 own the queries (TMEM lane = query token of the tile), warp 4 issues the TMA
+// loads (polling the query, key and value rings so that none waits behind another), warp 5
+// issues the MMAs. TMEM (256 columns, two CTAs per SM): two score buffers of 64 columns,
+// each overwritten by its f16 probabilities (two keys per column), and O in columns
+// [128, 192). Per key tile g: S[g&1] = Q K_g^T, softmax, O += P V_g; the score product of
+// tile g+1 runs while the softmax of tile g does. The epilogue stages its output rows in
+// the problem's own query buffer, which the next-but-one problem reloads afterwards.
+// Each query keeps a reference maximum m: a tile whose maximum exceeds m by more than
+// 2^8 (in exp2 units) moves m and rescales the query's O row and running sum first, so
+// every probability exp2(s - m) lies in (0, 256] and rescaling is rare.
+constexpr int AL_THREADS = 192;
+constexpr int AL_KT = 64;                 // keys per tile
+constexpr int AL_QT = 128;                // queries per problem
+constexpr int AL_NST = 4;                 // key stages, and value stages
+constexpr uint32_t AL_TMEM_COLS = 256;
+constexpr uint32_t AL_O_COL = 128;
+constexpr float AL_RESCALE = 8.f;         // log2 of the largest probability kept unscaled
+constexpr int AL_Q_BYTES = AL_QT * 128;   // 128 query rows of 64 f16
+constexpr int AL_KV_BYTES = AL_KT * 128;  // 64 key (or value) rows of 64 f16
+
+struct AlBars {
+    uint64_t q_full[2], q_empty[2], k_full[AL_NST], k_empty[AL_NST], v_full[AL_NST], v_empty[AL_NST];
+    uint64_t s_full[2], p_ready[2], pv_done, o_full, tm_free;
+    uint32_t tmem;
+    int abort;
+};
+constexpr int AL_SMEM = 1024 + 2 * AL_Q_BYTES + 2 * AL_NST * AL_KV_BYTES + int(sizeof(AlBars));
+
+// Keys of query q as two parts: key-valid patches k <= A, and the contiguous range [lo, q]
+// (empty for a query outside the row: lo > q). Equal to time_allowed() restricted to the
+// keys the reference computes (src/masks.cpp:21-26, the encoder split of src/layers.cpp:591).
+struct QKeys { int A, lo, q; };
+__device__ __forceinline__ QKeys query_keys(const MaskMeta& mm, int r, int q, bool live) {
+    QKeys m{-1, 1, 0};
+    if (!live) return m;
+    const int N = mm.N;
+    m.q = q;
+    if (q < N) {
+        m.A = (mm.cov && mm.role[r] == 2) ? N - 1 : q;   // known covariates see the whole context
+        m.lo = q;
+    } else if (!mm.cov) {
+        m.A = N - 1; m.lo = N;
+    } else if (q - N < mm.L) {
+        m.lo = q;                                         // second-stream context: itself only
+    } else {
+        const int a = anchor_of(mm, q - N);
+        m.A = min(a - 1, N - 1); m.lo = N + a;
+    }
+    return m;
+}
+// Bits [lo, hi] of a 64-bit set, clipped to [0, 63].
+__device__ __forceinline__ uint64_t range64(int lo, int hi) {
+    lo = max(lo, 0); hi = min(hi, 63);
+    if (lo > hi) return 0ull;
+    const uint64_t upper = hi == 63 ? ~0ull : ((1ull << (hi + 1)) - 1ull);
+    return upper & ~((1ull << lo) - 1ull);
+}
+// The keys [k0, k0 + 64) of query m, k0 a multiple of 64.
+__device__ __forceinline__ uint64_t tile_keys(const MaskMeta& mm, int r, const QKeys& m, int k0) {
+    uint64_t kv = 0;
+    if (m.A >= k0) {
+        const int w = k0 >> 5;
+        const uint32_t* row = mm.key_valid + int64_t(r) * mm.kv_words;
+        const uint64_t lo = w < mm.kv_words ? row[w] : 0u, hi = w + 1 < mm.kv_words ? row[w + 1] : 0u;
+        kv = (hi << 32 | lo) & range64(0, m.A - k0);
+    }
+    return kv | range64(m.lo - k0, m.q - k0);
+}
+// Problem p: query tile qt (of QT, heaviest first) of plane rh = row * H + head. The tile's
+// first query token q0 = S - (QT - qt) * 128 is negative for the partial first tile.
+struct AlProblem { int q0, rh, r, n; };
+__device__ __forceinline__ AlProblem al_problem(const MaskMeta& mm, int p, int RH, int QT, int H) {
+    AlProblem a;
+    const int qt = QT - 1 - p / RH;
+    a.rh = p % RH;
+    a.r = a.rh / H;
+    a.q0 = mm.S - (QT - qt) * AL_QT;
+    // key tiles: up to the tile's last query, or the whole context for the context queries
+    // of a known-covariate row
+    int kb = a.q0 + AL_QT - 1;
+    if (mm.cov && a.q0 < mm.N && mm.role[a.r] == 2) kb = max(kb, mm.N - 1);
+    a.n = kb / AL_KT + 1;
+    return a;
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// Walks the key (or value) tiles of this CTA's problems in order.
+struct TileCursor {
+    int p = 0, i = 0, j = 0, n = 0, g = 0, rh = 0;
+};
+
+__global__ void __launch_bounds__(AL_THREADS, 2)
+    attn_time_long_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                          const __grid_constant__ CUtensorMap map_v, const __half* __restrict__ gate,
+                          __half* __restrict__ out, int rows, int H, const MaskMeta mm, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* qbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* kbuf = qbuf + 2 * AL_Q_BYTES;
+    uint8_t* vbuf = kbuf + AL_NST * AL_KV_BYTES;
+    AlBars* bars = reinterpret_cast<AlBars*>(vbuf + AL_NST * AL_KV_BYTES);
+    volatile int* abort = &bars->abort;
+    const int S = mm.S, D = H * 64, RH = rows * H, QT = (S + AL_QT - 1) / AL_QT;
+    const int num = RH * QT;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->q_full[b], 1); mbar_init(&bars->q_empty[b], 4);
+            mbar_init(&bars->s_full[b], 1); mbar_init(&bars->p_ready[b], 4);
+        }
+        for (int s = 0; s < AL_NST; ++s) {
+            mbar_init(&bars->k_full[s], 1); mbar_init(&bars->k_empty[s], 1);
+            mbar_init(&bars->v_full[s], 1); mbar_init(&bars->v_empty[s], 1);
+        }
+        mbar_init(&bars->pv_done, 1); mbar_init(&bars->o_full, 1); mbar_init(&bars->tm_free, 4);
+        bars->abort = 0;
+        mbar_fence_init();
+        fence_proxy_async();
+    }
+    if (warp == 0) { tmem_alloc(&bars->tmem, AL_TMEM_COLS); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = bars->tmem;
+    const uint32_t tO = tbase + AL_O_COL;
+
+    if (warp == 4) {
+        // TMA producer: three independent streams (query tiles per problem, key tiles and
+        // value tiles), each issued as soon as its ring slot is free.
+        if (lane == 0) {
+            int qp = blockIdx.x, qi = 0;                  // next query tile: problem, local index
+            TileCursor kc, vc;
+            kc.p = vc.p = blockIdx.x;
+            auto enter = [&](TileCursor& c) {
+                if (c.p < num) { const AlProblem a = al_problem(mm, c.p, RH, QT, H); c.n = a.n; c.rh = a.rh; c.j = 0; }
+            };
+            auto advance = [&](TileCursor& c) {
+                ++c.g;
+                if (++c.j == c.n) { c.p += gridDim.x; ++c.i; enter(c); }
+            };
+            enter(kc);
+            enter(vc);
+            long long idle_since = clock64();
+            while (qp < num || kc.p < num || vc.p < num) {
+                bool moved = false;
+                if (qp < num && (qi < 2 || mbar_test(&bars->q_empty[qi & 1], ((qi >> 1) - 1) & 1))) {
+                    const AlProblem a = al_problem(mm, qp, RH, QT, H);
+                    mbar_arrive_expect_tx(&bars->q_full[qi & 1], AL_Q_BYTES);
+                    tma_load_3d(qbuf + (qi & 1) * AL_Q_BYTES, &map_q, &bars->q_full[qi & 1], 0, a.q0, a.rh);
+                    qp += gridDim.x; ++qi;
+                    moved = true;
+                }
+                if (kc.p < num) {
+                    const int st = kc.g % AL_NST;
+                    if (kc.g < AL_NST || mbar_test(&bars->k_empty[st], ((kc.g / AL_NST) - 1) & 1)) {
+                        mbar_arrive_expect_tx(&bars->k_full[st], AL_KV_BYTES);
+                        tma_load_3d(kbuf + st * AL_KV_BYTES, &map_k, &bars->k_full[st], 0, kc.j * AL_KT, kc.rh);
+                        advance(kc);
+                        moved = true;
+                    }
+                }
+                if (vc.p < num) {
+                    const int st = vc.g % AL_NST;
+                    if (vc.g < AL_NST || mbar_test(&bars->v_empty[st], ((vc.g / AL_NST) - 1) & 1)) {
+                        mbar_arrive_expect_tx(&bars->v_full[st], AL_KV_BYTES);
+                        tma_load_3d(vbuf + st * AL_KV_BYTES, &map_v, &bars->v_full[st], 0, vc.j * AL_KT, vc.rh);
+                        advance(vc);
+                        moved = true;
+                    }
+                }
+                if (moved) {
+                    idle_since = clock64();
+                } else {
+                    if (*abort) break;
+                    if (clock64() - idle_since > kWaitCycles) { *abort = 1; record_error(err, kDevTimeoutAttn); break; }
+                    __nanosleep(64);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        // MMA issuer. Order per key tile g: S[g&1] = Q K_g^T, then O += P_{g-1} V_{g-1}, so the
+        // score product of the next tile overlaps the softmax of the current one.
+        if (lane == 0) {
+            const uint32_t id_qk = idesc_f16(128, AL_KT), id_pv = idesc_f16_bmn(128, 64);
+            int pg = -1, pi = 0;            // pending P V: global tile and problem index
+            bool pfirst = false, plast = false;
+            auto issue_pv = [&]() -> bool {
+                const int st = pg % AL_NST;
+                if (!at_wait(&bars->p_ready[pg & 1], (pg >> 1) & 1, abort, err) ||
+                    !at_wait(&bars->v_full[st], (pg / AL_NST) & 1, abort, err))
+                    return false;
+                // the first tile of a problem overwrites O: the previous problem's O must be read
+                if (pfirst && pi >= 1 && !at_wait(&bars->tm_free, (pi - 1) & 1, abort, err)) return false;
+                tc_fence_after();
+                const uint32_t tp = tbase + uint32_t(pg & 1) * AL_KT;
+                const uint32_t sv = smem_u32(vbuf + st * AL_KV_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < AL_KT / 16; ++kk)
+                    mma_f16_ts(tO, tp + kk * 8, smem_desc_sw128(sv + kk * 16 * 128), id_pv, kk > 0 || !pfirst);
+                mma_commit(&bars->pv_done);
+                mma_commit(&bars->v_empty[st]);
+                if (plast) mma_commit(&bars->o_full);
+                return true;
+            };
+            int i = 0, g = 0;
+            bool ok = true;
+            for (int p = blockIdx.x; p < num && ok; p += gridDim.x, ++i) {
+                const int n = al_problem(mm, p, RH, QT, H).n;
+                const int qb = i & 1;
+                if (!at_wait(&bars->q_full[qb], (i >> 1) & 1, abort, err)) { ok = false; break; }
+                const uint64_t dq = smem_desc_sw128(smem_u32(qbuf + qb * AL_Q_BYTES));
+                for (int j = 0; j < n; ++j, ++g) {
+                    const int st = g % AL_NST;
+                    // S[g&1] is free once P_{g-2}, written over it, has been multiplied.
+                    if (!at_wait(&bars->k_full[st], (g / AL_NST) & 1, abort, err) ||
+                        (g >= 2 && !at_wait(&bars->pv_done, (g - 2) & 1, abort, err))) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t dk = smem_desc_sw128(smem_u32(kbuf + st * AL_KV_BYTES));
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        mma_f16(tbase + uint32_t(g & 1) * AL_KT, dq + uint64_t(2 * k), dk + uint64_t(2 * k), id_qk, k > 0);
+                    mma_commit(&bars->s_full[g & 1]);
+                    mma_commit(&bars->k_empty[st]);
+                    if (pg >= 0 && !issue_pv()) { ok = false; break; }
+                    pg = g; pi = i; pfirst = j == 0; plast = j == n - 1;
+                }
+            }
+            if (ok && pg >= 0) issue_pv();
+        }
+        __syncwarp();
+    } else {
+        // Softmax and epilogue: thread t = query token q0 + t, TMEM lane t.
+        constexpr float kScaleLog2e = 0.125f * 1.4426950408889634f;
+        const int t = threadIdx.x;
+        const uint32_t lane_base = uint32_t(warp * 32) << 16;
+        int i = 0, g = 0;
+        for (int p = blockIdx.x; p < num; p += gridDim.x, ++i) {
+            const AlProblem a = al_problem(mm, p, RH, QT, H);
+            const int r = a.r, h = a.rh % H, n = a.n;
+            const int q = a.q0 + t;
+            const bool live = q >= 0;
+            const QKeys qk = query_keys(mm, r, q, live);
+            float mref = -INFINITY, sum = 0.f;
+            bool ok = true;
+            for (int j = 0; j < n; ++j, ++g) {
+                const int b = g & 1;
+                const uint64_t bits = tile_keys(mm, r, qk, j * AL_KT);
+                if (!warp_wait(&bars->s_full[b], (g >> 1) & 1, abort, err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t ts = tbase + lane_base + uint32_t(b) * AL_KT;
+                uint32_t pk[32];
+                if (__any_sync(0xffffffffu, bits != 0ull)) {
+                    uint32_t s0[32], s1[32];
+                    tmem_ld32(ts, s0);
+                    tmem_ld32(ts + 32, s1);
+                    tmem_ld_wait();
+                    const uint32_t b0 = uint32_t(bits), b1 = uint32_t(bits >> 32);
+                    // every lane of the warp attends every key of the tile: no per-key masking
+                    const bool full = __all_sync(0xffffffffu, bits == ~0ull);
+                    float mxj[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) mxj[c] = -INFINITY;
+                    if (full) {
+#pragma unroll
+                        for (int c = 0; c < 32; ++c)
+                            mxj[c & 7] = fmaxf(mxj[c & 7], fmaxf(__uint_as_float(s0[c]), __uint_as_float(s1[c])));
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 32; ++c) {
+                            if ((b0 >> c) & 1u) mxj[c & 7] = fmaxf(mxj[c & 7], __uint_as_float(s0[c]));
+                            if ((b1 >> c) & 1u) mxj[c & 7] = fmaxf(mxj[c & 7], __uint_as_float(s1[c]));
+                        }
+                    }
+                    const float mt = fmaxf(fmaxf(fmaxf(mxj[0], mxj[1]), fmaxf(mxj[2], mxj[3])),
+                                           fmaxf(fmaxf(mxj[4], mxj[5]), fmaxf(mxj[6], mxj[7]))) * kScaleLog2e;
+                    // Move the reference maximum; with earlier keys, rescale O and the sum.
+                    const bool first = mref == -INFINITY && bits != 0ull;
+                    const bool need = mref != -INFINITY && mt > mref + AL_RESCALE;
+                    float factor = 1.f;
+                    if (need) { factor = exp2_ftz(mref - mt); sum *= factor; }
+                    if (first || need) mref = mt;
+                    if (__any_sync(0xffffffffu, need)) {
+                        // O holds the tiles before this one once the last P V completed.
+                        if (!warp_wait(&bars->pv_done, (g - 1) & 1, abort, err)) { ok = false; break; }
+                        tc_fence_after();
+#pragma unroll 1
+                        for (int c0 = 0; c0 < 64; c0 += 16) {
+                            uint32_t o[16];
+                            tmem_ld16(tO + lane_base + c0, o);
+                            tmem_ld_wait();
+                            uint32_t w[8];
+#pragma unroll
+                            for (int c = 0; c < 8; ++c) w[c] = __float_as_uint(__uint_as_float(o[c]) * factor);
+                            tmem_st8(tO + lane_base + c0, w);
+#pragma unroll
+                            for (int c = 0; c < 8; ++c) w[c] = __float_as_uint(__uint_as_float(o[8 + c]) * factor);
+                            tmem_st8(tO + lane_base + c0 + 8, w);
+                        }
+                        tmem_st_wait();
+                    }
+                    const float off = bits ? mref : 0.f;
+                    float sj[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) sj[c] = 0.f;
+                    if (full) {
+#pragma unroll
+                        for (int c = 0; c < 16; ++c) {
+                            const float e0 = exp2_ftz(__fmaf_rn(__uint_as_float(s0[2 * c]), kScaleLog2e, -off));
+                            const float e1 = exp2_ftz(__fmaf_rn(__uint_as_float(s0[2 * c + 1]), kScaleLog2e, -off));
+                            const float e2 = exp2_ftz(__fmaf_rn(__uint_as_float(s1[2 * c]), kScaleLog2e, -off));
+                            const float e3 = exp2_ftz(__fmaf_rn(__uint_as_float(s1[2 * c + 1]), kScaleLog2e, -off));
+                            sj[(2 * c) & 7] += e0; sj[(2 * c + 1) & 7] += e1;
+                            sj[(2 * c) & 7] += e2; sj[(2 * c + 1) & 7] += e3;
+                            pk[c] = pack_half2(e0, e1);
+                            pk[16 + c] = pack_half2(e2, e3);
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 16; ++c) {
+                            const float e0 = (b0 >> (2 * c)) & 1u ? exp2_ftz(__fmaf_rn(__uint_as_float(s0[2 * c]), kScaleLog2e, -off)) : 0.f;
+                            const float e1 = (b0 >> (2 * c + 1)) & 1u ? exp2_ftz(__fmaf_rn(__uint_as_float(s0[2 * c + 1]), kScaleLog2e, -off)) : 0.f;
+                            const float e2 = (b1 >> (2 * c)) & 1u ? exp2_ftz(__fmaf_rn(__uint_as_float(s1[2 * c]), kScaleLog2e, -off)) : 0.f;
+                            const float e3 = (b1 >> (2 * c + 1)) & 1u ? exp2_ftz(__fmaf_rn(__uint_as_float(s1[2 * c + 1]), kScaleLog2e, -off)) : 0.f;
+                            sj[(2 * c) & 7] += e0; sj[(2 * c + 1) & 7] += e1;
+                            sj[(2 * c) & 7] += e2; sj[(2 * c + 1) & 7] += e3;
+                            pk[c] = pack_half2(e0, e1);
+                            pk[16 + c] = pack_half2(e2, e3);
+                        }
+                    }
+                    sum += ((sj[0] + sj[1]) + (sj[2] + sj[3])) + ((sj[4] + sj[5]) + (sj[6] + sj[7]));
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) pk[c] = 0u;
+                }
+                tmem_st32(ts, pk);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->p_ready[b]);
+            }
+            if (!ok) break;
+            // Epilogue: O * (1/sum) * gate in f16, staged per warp in this problem's query
+            // buffer (every score product of the problem has completed) and stored as full rows.
+            uint8_t* obuf = qbuf + (i & 1) * AL_Q_BYTES;
+            uint4 gv[8];
+            const __half* gp = (gate && live) ? gate + ((int64_t(r) * H + h) * S + q) * 64 : nullptr;
+            if (gp) {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) gv[c] = *reinterpret_cast<const uint4*>(gp + c * 8);
+            }
+            if (!warp_wait(&bars->o_full, i & 1, abort, err)) break;
+            tc_fence_after();
+            const float inv = live ? 1.0f / sum : 0.f;
+            uint32_t o[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                if ((c & 3) == 0) {
+                    tmem_ld32(tO + lane_base + c * 8, o);
+                    tmem_ld_wait();
+                    if (c == 4) {                   // O is in registers: the next problem may overwrite it
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bars->tm_free);
+                    }
+                }
+                float y[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[e] = __uint_as_float(o[(c & 3) * 8 + e]) * inv;
+                if (gp) {
+                    const __half2* gh = reinterpret_cast<const __half2*>(&gv[c]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(gh[e]);
+                        y[2 * e] = __fmul_rn(y[2 * e], f.x);
+                        y[2 * e + 1] = __fmul_rn(y[2 * e + 1], f.y);
+                    }
+                }
+                uint4 u;
+                u.x = pack_half2(y[0], y[1]); u.y = pack_half2(y[2], y[3]);
+                u.z = pack_half2(y[4], y[5]); u.w = pack_half2(y[6], y[7]);
+                *reinterpret_cast<uint4*>(obuf + t * 128 + ((c ^ (t & 7)) << 4)) = u;
+            }
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int row = warp * 32 + j * 4 + (lane >> 3), chunk = lane & 7;
+                const int tok = a.q0 + row;
+                if (tok >= 0)
+                    *reinterpret_cast<uint4*>(out + (int64_t(r) * S + tok) * D + h * 64 + chunk * 8) =
+                        *reinterpret_cast<const uint4*>(obuf + row * 128 + ((chunk ^ (row & 7)) << 4));
+            }
+            // the query buffer may be reloaded (async proxy) once every warp's rows are out
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->q_empty[i & 1]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tbase, AL_TMEM_COLS);
+}
+
+}  // namespace
+
+cudaError_t attention_time_tc_long(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
+                                   int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
+    if (rows <= 0) return cudaSuccess;
+    if (mm.S <= 0 || H <= 0) return cudaErrorInvalidValue;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_time_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AL_SMEM);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    CUtensorMap mq, mk, mv;
+    const int64_t planes = int64_t(rows) * H;
+    if (!make_map_3d_f16(&mq, q, planes, mm.S, AL_QT) || !make_map_3d_f16(&mk, k, planes, mm.S, AL_KT) ||
+        !make_map_3d_f16(&mv, v, planes, mm.S, AL_KT))
+        return cudaErrorInvalidValue;
+    const int64_t problems = planes * ((mm.S + AL_QT - 1) / AL_QT);
+    if (problems > INT32_MAX) return cudaErrorInvalidValue;
+    int grid = device_sm_count() * 2;
+    if (int64_t(grid) > problems) grid = int(problems);
+    attn_time_long_kernel<<<grid, AL_THREADS, AL_SMEM, stream>>>(mq, mk, mv, gate, out, rows, H, mm, err);
+    return cudaGetLastError();
+}
+
+namespace {
+
+// ---------------------------------------------------------------------------------------
 // CUDA-core kernels with the reference's operation order. One warp per query.
 template <class T>
 __device__ __forceinline__ float ld(const T* p) { return float(*p); }

@@ -65,6 +65,55 @@ extern "C" TIMESTRAL_API int tsb_test_attention_time(const void* q, const void* 
     return h ? TSB_ERR_DEVICE : TSB_OK;
 }
 
+extern "C" TIMESTRAL_API int tsb_test_attention_time_ex(const void* q, const void* k, const void* v, const void* gate,
+                                                        void* out, const uint32_t* key_valid, const int8_t* role,
+                                                        int32_t rows, int32_t H, int32_t S, int32_t N, int32_t L,
+                                                        int32_t cov, int32_t block_size, int32_t kernel,
+                                                        int32_t repeat, float* ms, int32_t* dev_error) {
+    using namespace tsb;
+    if (!q || !k || !v || !out || !key_valid || rows <= 0 || H <= 0 || S <= 0 || N <= 0 || N > S || L <= 0 || L > N ||
+        (cov && (!role || block_size <= 0 || S != 2 * N)) || kernel < 0 || kernel > 3 || (kernel == 1 && S > 128))
+        return TSB_ERR_ARG;
+    MaskMeta mm;
+    mm.key_valid = key_valid; mm.kv_words = (N + 31) / 32; mm.N = N; mm.L = L; mm.S = S;
+    mm.cov = cov ? 1 : 0; mm.block_size = block_size; mm.role = role;
+    if (kernel == 0) kernel = S <= 128 ? 1 : 2;
+    int* derr = nullptr;
+    if (cudaMalloc(&derr, sizeof(int)) != cudaSuccess) return TSB_ERR_CUDA;
+    cudaMemset(derr, 0, sizeof(int));
+    const __half *hq = static_cast<const __half*>(q), *hk = static_cast<const __half*>(k), *hv = static_cast<const __half*>(v);
+    const __half* hg = static_cast<const __half*>(gate);
+    __half* ho = static_cast<__half*>(out);
+    auto launch = [&]() {
+        return kernel == 1   ? attention_time_tc(hq, hk, hv, hg, ho, rows, H, mm, 0, derr)
+               : kernel == 2 ? attention_time_tc_long(hq, hk, hv, hg, ho, rows, H, mm, 0, derr)
+                             : attention_time_simt<__half>(hq, hk, hv, hg, ho, rows, H, 64, mm, 0);
+    };
+    cudaError_t ce = launch();
+    if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+    if (ce == cudaSuccess && repeat > 0 && ms) {
+        // average device time of `repeat` further launches (CUDA events on the launch stream)
+        cudaEvent_t e0, e1;
+        cudaEventCreate(&e0);
+        cudaEventCreate(&e1);
+        cudaEventRecord(e0, 0);
+        for (int it = 0; it < repeat && ce == cudaSuccess; ++it) ce = launch();
+        cudaEventRecord(e1, 0);
+        if (ce == cudaSuccess) ce = cudaEventSynchronize(e1);
+        float t = 0.f;
+        cudaEventElapsedTime(&t, e0, e1);
+        *ms = t / float(repeat);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    int h = 0;
+    cudaMemcpy(&h, derr, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(derr);
+    if (dev_error) *dev_error = h;
+    if (ce != cudaSuccess) return ce == cudaErrorInvalidValue ? TSB_ERR_ARG : TSB_ERR_CUDA;
+    return h ? TSB_ERR_DEVICE : TSB_OK;
+}
+
 extern "C" TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, void* out, int32_t* d_overflow) {
     if (!a || !out || !d_overflow || rows < 0 || K <= 0) return TSB_ERR_ARG;
     cudaError_t e = tsb::split_f16(a, rows, K, static_cast<__half*>(out), d_overflow, nullptr, 0);

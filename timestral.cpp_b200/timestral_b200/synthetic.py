@@ -110,6 +110,14 @@ def spec_small(bias: bool = False) -> ModelSpec:
                      attn_bias=bias, mlp_bias=bias)
 
 
+def spec_small_long() -> ModelSpec:
+    """spec_small with the 209M context length (32768 steps, 1024 context patches), so rows
+    reach the long-row attention kernel (S up to 1056, 2112 with covariates)."""
+    return ModelSpec(name="timestral-small-long", patch_size=32, d_model=128, num_heads=2, mlp_hidden_dim=256,
+                     block_schedule=("time", "variate", "time_variate", "variate_time"),
+                     quantile_knots=KNOTS_21, block_size=32, context_length=32768)
+
+
 LAYER_AXES = {"time": (True,), "variate": (False,), "time_variate": (True, False),
               "variate_time": (False, True)}
 
