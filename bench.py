@@ -52,6 +52,9 @@ CONFIGS = {
                  desc="cfg4: 209M f16 random-init, B=32, V=4, T=1024, H=96, 8 past + 4 known + 2 categorical covariates"),
     "cfg5": dict(weights=None, B=4096, V=1, T=2048, H=256, cpu_sample=48,
                  desc="cfg5 throughput: 209M {w} random-init, B={B} series ({per} per GPU), V=1, T=2048, H=256, symmetric+clip"),
+    "cfg6": dict(weights="f16", B=64, V=1, T=32768, H=1024, cpu_sample=1,
+                 desc="cfg6 long context: 209M f16 random-init, B=64, V=1, T=32768 (the full 1024-patch context), "
+                      "H=1024 (one 32-patch decode block, S=1056), seasonal + 1% NaN"),
 }
 
 # DRAM bytes (read + write) of one time-attention (row, head) problem at S = 72, from the
@@ -375,12 +378,15 @@ def main():
             "vs_baseline": None, "dtype": "f16" if c["weights"] != "f32" else "f32", "data": "synthetic",
             "config": {"workload": cdesc, "global_batch": B, "seq_len": S,
                        "parallelism": f"series-sharded x{world}",
-                       "l2": "per-step working set far above the 126 MB L2" if a.config == "cfg5"
+                       "l2": "per-step working set far above the 126 MB L2" if a.config in ("cfg5", "cfg6")
                              else "steps run back to back without an L2 flush (small working set)",
                        "path": "device-resident context" if not covariates else "C ABI with host buffers (covariates)"},
-            "roofline": {"kernel": "attention_time_tc" if tc_path and S <= 128 else "attention_time_simt",
-                         "bound": "hbm", "achieved": achieved_gbs, "peak": hbm,
-                         "unit": "GB/s", "frac": achieved_gbs / hbm,
+            "roofline": {"kernel": ("attention_time_tc" if S <= 128 else "attention_time_tc_long") if tc_path
+                                   else "attention_time_simt",
+                         **({"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
+                             "frac": achieved_gbs / hbm} if roof_tf < tf else
+                            {"bound": "tensor", "achieved": achieved_tf, "peak": tf_sus, "unit": "TFLOP/s",
+                             "frac": achieved_tf / tf_sus}),
                          "traffic": (ATTN_DRAM_BYTES_PER_PROBLEM * problems
                                      if (a.config == "cfg5" and ATTN_DRAM_BYTES_PER_PROBLEM) else None),
                          "traffic_unit": "bytes per launch", "algorithmic_bytes": att_bytes,

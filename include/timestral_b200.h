@@ -122,6 +122,16 @@ TIMESTRAL_API int tsb_test_attention_time_ex(const void* q, const void* k, const
                                              const uint32_t* key_valid, const int8_t* role, int32_t rows, int32_t H,
                                              int32_t S, int32_t N, int32_t L, int32_t cov, int32_t block_size,
                                              int32_t kernel, int32_t repeat, float* ms, int32_t* dev_error);
+/* Causal scaler and patch features of R rows of W steps (device pointers, synchronized):
+ * rows f32 / mask int8 [R][W]; features [R][W/ps][2ps]; loc/scale [R] (frame of step
+ * anchor_step); key_valid [R][ceil(enc_patches/32)]; first_obs [R]; cap_lo/cap_hi/cap_scale
+ * [R] or NULL (statistics over the first ctx_len steps). kernel 0: one thread per row,
+ * 1: one block per row (the two give identical results). */
+TIMESTRAL_API int tsb_test_scale_rows(const float* rows, const int8_t* mask, int32_t R, int32_t W, int32_t ps,
+                                      double minimum_scale, int32_t use_asinh, int32_t attend_missing,
+                                      int32_t anchor_step, int32_t enc_patches, int32_t ctx_len, int32_t kernel,
+                                      float* features, float* loc, float* scale, uint32_t* key_valid, int32_t* first_obs,
+                                      float* cap_lo, float* cap_hi, float* cap_scale);
 /* f16 hi/lo split used by the tensor-core patch projections: out [rows][3K] f16 =
  * [hi | hi | lo] of each f32 row of a; sets *d_overflow (device int) when any |a| > 30000. */
 TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, void* out, int32_t* d_overflow);

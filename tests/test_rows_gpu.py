@@ -8,6 +8,7 @@ import pytest
 
 import oracle_py as op
 import timestral_b200 as tb
+from timestral_b200 import synthetic as sy
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
@@ -88,3 +89,41 @@ def test_refine_bitwise(dev, R, T, patches, ps):
     got = out.cpu().numpy()
     want = want.reshape(got.shape)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), float(np.abs(got - want).max())
+
+
+@pytest.mark.parametrize("R,W,ps,attend", [(5, 3072, 32, 1), (3, 96, 32, 0), (4, 1056, 32, 1), (2, 2400, 48, 1),
+                                           (3, 32768, 32, 1), (70, 2048, 32, 1)])
+def test_scale_rows_block_form(dev, R, W, ps, attend):
+    """The block-per-row scaler (long rows) equals the one-thread-per-row form bit for bit on
+    every output, and its anchor frame equals the oracle's causal scaler (reference
+    src/scaler.cpp:27-58) at the anchor step."""
+    rng = np.random.default_rng(W + R)
+    x = (np.cumsum(rng.standard_normal((R, W)), axis=1) * rng.uniform(0.01, 50, (R, 1))).astype(np.float32)
+    m = (rng.random((R, W)) > 0.1).astype(np.int8)
+    lead = rng.integers(0, W // 2, R)
+    for i in range(R):
+        m[i, : lead[i]] = 0          # left padding: leading unobserved patches
+    x[m == 0] = 0.0
+    enc = W // ps - 1
+    anchor, ctx_len = (enc * ps) - 1, enc * ps
+    dx, dm = torch.from_numpy(x).to(dev), torch.from_numpy(m).to(dev)
+    outs = []
+    for kernel in (0, 1):
+        feat = torch.full((R, W // ps, 2 * ps), float("nan"), device=dev)
+        loc, sc, clo, chi, csc = (torch.full((R,), float("nan"), device=dev) for _ in range(5))
+        kv = torch.zeros((R, (enc + 31) // 32), dtype=torch.int32, device=dev)
+        fo = torch.full((R,), -7, dtype=torch.int32, device=dev)
+        rc = tb.lib().tsb_test_scale_rows(dx.data_ptr(), dm.data_ptr(), R, W, ps, C.c_double(1e-6), 1, attend, anchor, enc,
+                                          ctx_len, kernel, feat.data_ptr(), loc.data_ptr(), sc.data_ptr(), kv.data_ptr(),
+                                          fo.data_ptr(), clo.data_ptr(), chi.data_ptr(), csc.data_ptr())
+        assert rc == 0, rc
+        outs.append([t.cpu().numpy() for t in (feat, loc, sc, kv, fo, clo, chi, csc)])
+    for a, b in zip(*outs):
+        assert np.array_equal(a.view(np.uint8), b.view(np.uint8))
+    c = op.make_config(sy.spec_209m())
+    c.patch_size = ps
+    c.minimum_scale = 1e-6
+    _, oloc, osc = op.scale_rows(c, x, m, R, W)
+    oloc, osc = oloc.reshape(R, W), osc.reshape(R, W)
+    assert np.array_equal(outs[1][1].view(np.uint32), oloc[:, anchor].view(np.uint32))
+    assert np.array_equal(outs[1][2].view(np.uint32), osc[:, anchor].view(np.uint32))

@@ -413,18 +413,18 @@ struct Engine::Impl {
         kv.ensure(size_t(R2) * kvw * 4);
         rope_row.ensure(size_t(M) * 4); gbeg.ensure(R2 * 4); gsize.ensure(R2 * 4);
         if (first) { caplo.ensure(R2 * 4); caphi.ensure(R2 * 4); capsc.ensure(R2 * 4); }
-        run("rows", [&] {
+        run("scale", [&] {
             return scale_rows(rc, rows_p, mask_p, R2, W, cov ? (L - 1) * ps : T - 1, N, kvw, feat.as<float>(),
                               aloc.as<float>(), ascale.as<float>(), kv.as<uint32_t>(), first_obs.as<int>(),
                               first ? cap_ctx : 0, first ? caplo.as<float>() : nullptr,
                               first ? caphi.as<float>() : nullptr, first ? capsc.as<float>() : nullptr, s);
         });
         if (cov)
-            run("rows", [&] {
+            run("scale", [&] {
                 return known_rows(rc, rows_p, mask_p, role.as<int8_t>(), R2, W, (L - 1) * ps, feat.as<float>(),
                                   aloc.as<float>(), ascale.as<float>(), s);
             });
-        run("rows", [&] {
+        run("positions", [&] {
             return positions(rc, first_obs.as<int>(), R2, group_rows, N, S, cov, rope_row.as<int>(), gbeg.as<int>(),
                              gsize.as<int>(), err.as<int>(), s);
         });
@@ -448,7 +448,7 @@ struct Engine::Impl {
                 pflag.ensure(sizeof(int) + size_t(PR));
                 check(cudaMemsetAsync(pflag.p, 0, sizeof(int) + size_t(PR), s), "memset");
                 int8_t* row_flags = pflag.as<int8_t>() + sizeof(int);
-                run("rows", [&] {
+                run("patch_split", [&] {
                     return split_f16(feat.as<float>(), PR, 2 * ps, feat16.as<__half>(), pflag.as<int>(), row_flags, s);
                 });
                 GemmArgs h;
@@ -480,7 +480,7 @@ struct Engine::Impl {
             g.row_group = N; g.row_stride = S;
             sgemm(g);
         }
-        run("rows", [&] { return fill_query(query, x.as<float>(), R2, S, N, D, s); });
+        run("fill", [&] { return fill_query(query, x.as<float>(), R2, S, N, D, s); });
 
         MaskMeta mm;
         mm.key_valid = kv.as<uint32_t>(); mm.kv_words = kvw; mm.N = N; mm.L = L; mm.S = S; mm.cov = cov;
@@ -496,12 +496,12 @@ struct Engine::Impl {
 
         for (size_t li = 0; li < attn.size(); ++li) {
             for (const AttnW& a : attn[li]) {
-                run("rows", [&] { return rms_norm(x.as<float>(), a.norm, int(M), D, mv.eps, xn.p, tc, 0, 0, 0, s); });
+                run("rms", [&] { return rms_norm(x.as<float>(), a.norm, int(M), D, mv.eps, xn.p, tc, 0, 0, 0, s); });
                 if (tc) attention_sublayer_tc(a, int(M), R2, S, group_rows, mm);
                 else attention_sublayer_simt(a, int(M), R2, S, mm);
             }
             const MlpW& w = mlp[li];
-            run("rows", [&] { return rms_norm(x.as<float>(), w.norm, int(M), D, mv.eps, xn.p, tc, 0, 0, 0, s); });
+            run("rms", [&] { return rms_norm(x.as<float>(), w.norm, int(M), D, mv.eps, xn.p, tc, 0, 0, 0, s); });
             if (tc) {
                 GemmArgs a;
                 a.A = xn.as<__half>(); a.lda = D; a.B = w.w12; a.ldb = D; a.M = int(M); a.N = 2 * F; a.K = D;
@@ -517,7 +517,7 @@ struct Engine::Impl {
                 g.order = round_a ? ORDER_CHAIN : ORDER_PANEL192; g.round_a_f16 = round_a; g.epi = SEPI_F32;
                 g.bias = w.fb12; g.out = zb.p; g.ldo = 2 * F;
                 sgemm(g);
-                run("rows", [&] { return swiglu(zb.as<float>(), int(M), F, hb.as<float>(), s); });
+                run("swiglu", [&] { return swiglu(zb.as<float>(), int(M), F, hb.as<float>(), s); });
                 SimtGemm o;
                 o.A = hb.as<float>(); o.lda = F; o.W = w.f3; o.M = int(M); o.N = D; o.K = F;
                 o.order = round_a ? ORDER_CHAIN : ORDER_PANEL192; o.round_a_f16 = round_a; o.epi = SEPI_RESID;
@@ -529,7 +529,7 @@ struct Engine::Impl {
         // src/predict_block.cpp:15-16 slice).
         const int DR = R2 * P_all;
         dec.ensure(size_t(DR) * D * eb);
-        run("rows", [&] { return rms_norm(x.as<float>(), out_norm, DR, D, mv.eps, dec.p, tc, P_all, S, N, s); });
+        run("rms", [&] { return rms_norm(x.as<float>(), out_norm, DR, D, mv.eps, dec.p, tc, P_all, S, N, s); });
         const int NQ = ps * Q;
         hh.ensure(size_t(DR) * 4 * D * eb);
         hraw.ensure(size_t(DR) * NQ * 4);
@@ -563,7 +563,7 @@ struct Engine::Impl {
         }
         const int steps = h * ps;
         qout.ensure(size_t(R2) * steps * Q * 4);
-        run("rows", [&] {
+        run("head", [&] {
             return quantile_head(rc, hraw.as<float>(), R2, P_all, cov ? L : 0, h, aloc.as<float>(), ascale.as<float>(),
                                  qout.as<float>(), nullptr, err.as<int>(), s);
         });
@@ -572,7 +572,7 @@ struct Engine::Impl {
             const int n = T / ps + h;
             scratch.ensure(size_t(R2) * (3 * size_t(n) + 2 * ps + 2 * h) * 8);
             const double clip = std::pow(double(FLT_MAX), 0.5) / 1e3;
-            run("rows", [&] {
+            run("refine", [&] {
                 return refine(rc, qout.as<float>(), rows_p, mask_p, W, cov ? role.as<int8_t>() : nullptr, aloc.as<float>(),
                               ascale.as<float>(), R2, T, h, clip, scratch.as<double>(), refined.as<float>(), s);
             });
@@ -636,7 +636,7 @@ struct Engine::Impl {
             q.round_a_f16 = round_a; q.epi = SEPI_F32; q.bias = a.fb_gate; q.out = gtmp.p; q.ldo = D;
             sgemm(q);
         }
-        run("rows", [&] {
+        run("scatter", [&] {
             return qkv_scatter(fused.as<float>(), a.gate ? gtmp.as<float>() : nullptr, M, S, H, hd, a.time, cos_tab,
                                sin_tab, rope_row.as<int>(), qb.as<float>(), kb.as<float>(), vb.as<float>(),
                                a.gate ? gb.as<float>() : nullptr, s);
@@ -722,11 +722,11 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
     const cudaStream_t s = stream_;
     if (clip) {
         im.clip_ok.ensure(size_t(R));
-        im.run("rows", [&] { return clip_eligibility(d_ctx, d_umask, R, T, im.clip_ok.as<int8_t>(), s); });
+        im.run("clip", [&] { return clip_eligibility(d_ctx, d_umask, R, T, im.clip_ok.as<int8_t>(), s); });
     }
     im.win.ensure(size_t(R2) * len * 4);
     im.wmask.ensure(size_t(R2) * len);
-    im.run("rows", [&] { return assemble_targets(d_ctx, d_umask, R, T, kept, len, symmetric, im.win.as<float>(), im.wmask.as<int8_t>(), s); });
+    im.run("assemble", [&] { return assemble_targets(d_ctx, d_umask, R, T, kept, len, symmetric, im.win.as<float>(), im.wmask.as<int8_t>(), s); });
     int Tc = len, done = 0;
     const bool single = patches <= shot;
     if (!single) im.decoded.ensure(size_t(R2) * H * Q * 4);
@@ -743,7 +743,7 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
         const int joined = Tc + n, keep = joined > mv.context_length ? std::max(ps, (mv.context_length / ps) * ps) : joined;
         im.next_rows.ensure(size_t(R2) * keep * 4);
         im.next_mask.ensure(size_t(R2) * keep);
-        im.run("rows", [&] {
+        im.run("feedback", [&] {
             return feedback(im.rc, im.win.as<float>(), im.wmask.as<int8_t>(), R2, Tc, im.refined.as<float>(), n, nullptr,
                             nullptr, nullptr, keep, im.next_rows.as<float>(), im.next_mask.as<int8_t>(), s);
         });
@@ -753,7 +753,7 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
     }
     const float* dec = single ? im.refined.as<float>() : im.decoded.as<float>();
     const int Hfull = single ? patches * ps : H;
-    im.run("rows", [&] {
+    im.run("finalize", [&] {
         return finalize(im.rc, dec, R, symmetric, B, V, V, H, Hfull, im.caplo.as<float>(), im.caphi.as<float>(),
                         im.capsc.as<float>(), mv.cap_k > 0, clip ? im.clip_ok.as<int8_t>() : nullptr, d_out,
                         im.err.as<int>(), s);
@@ -812,7 +812,7 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
         check(cudaMemcpyAsync(dctx.p, ctx, size_t(B) * V * T_req * 4, cudaMemcpyHostToDevice, s), "upload");
         if (umask) { dum.ensure(size_t(B) * V * T_req); check(cudaMemcpyAsync(dum.p, umask, size_t(B) * V * T_req, cudaMemcpyHostToDevice, s), "upload"); }
         im.clip_ok.ensure(size_t(B) * V);
-        im.run("rows", [&] { return clip_eligibility(dctx.as<float>(), umask ? dum.as<uint8_t>() : nullptr, B * V, T_req, im.clip_ok.as<int8_t>(), s); });
+        im.run("clip", [&] { return clip_eligibility(dctx.as<float>(), umask ? dum.as<uint8_t>() : nullptr, B * V, T_req, im.clip_ok.as<int8_t>(), s); });
         check(cudaStreamSynchronize(s), "sync");
     }
     im.decoded.ensure(size_t(R2) * H * Q * 4);
@@ -846,7 +846,7 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
             check(cudaMemcpy2DAsync(fs.p, size_t(n) * 4, im.future.as<float>() + offset, size_t(Hh) * 4, size_t(n) * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
             check(cudaMemcpy2DAsync(fms.p, n, im.fmask.as<int8_t>() + offset, Hh, n, R2, cudaMemcpyDeviceToDevice, s), "copy");
         }
-        im.run("rows", [&] {
+        im.run("feedback", [&] {
             return feedback(im.rc, im.rows.as<float>(), im.mask.as<int8_t>(), R2, Tc, im.refined.as<float>(), n,
                             cov ? im.role.as<int8_t>() : nullptr, a.future ? fs.as<float>() : nullptr,
                             a.future ? fms.as<int8_t>() : nullptr, keep, im.next_rows.as<float>(), im.next_mask.as<int8_t>(), s);
@@ -860,7 +860,7 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
     dout.ensure(size_t(B) * V * H * Q * 4);
     const int all = R / B;
     // Cap statistics come from the first block's scale pass over the assembled context.
-    im.run("rows", [&] {
+    im.run("finalize", [&] {
         return finalize(im.rc, im.decoded.as<float>(), R, symmetric, B, V, all, H, H, im.caplo.as<float>(),
                         im.caphi.as<float>(), im.capsc.as<float>(), mv.cap_k > 0, clip ? im.clip_ok.as<int8_t>() : nullptr,
                         dout.as<float>(), im.err.as<int>(), s);

@@ -140,6 +140,187 @@ __global__ void scale_kernel(const RowConfig c, const float* __restrict__ rows, 
     }
 }
 
+// The same scaler with one block per row, for long rows: thread 0 runs the reference's two
+// float64 recurrences (the masked running sum, then the running sum of deviation terms) in
+// their order, and nothing else; the products, the running weight (an integer count, so its
+// prefix sums are exact in any order), the divisions, deviation terms, patch statistics,
+// features and key-valid words are computed by all threads, over chunks of the row staged
+// in shared memory. Every value is produced by the same operations as in scale_kernel, so
+// the results are identical (the cap minimum and maximum are order-independent).
+constexpr int SC_THREADS = 128;
+constexpr int SC_CHUNK = 1024;
+constexpr int SC_PER = SC_CHUNK / SC_THREADS;   // consecutive steps per thread in the count scan
+
+__global__ void __launch_bounds__(SC_THREADS)
+    scale_block_kernel(const RowConfig c, const float* __restrict__ rows, const int8_t* __restrict__ mask, int W,
+                       int anchor_step, int enc_patches, int kv_words, float* __restrict__ features,
+                       float* __restrict__ aloc, float* __restrict__ ascale, uint32_t* __restrict__ key_valid,
+                       int* __restrict__ first_obs, int ctx_len, float* __restrict__ cap_lo,
+                       float* __restrict__ cap_hi, float* __restrict__ cap_scale) {
+    __shared__ float xs[SC_CHUNK];
+    __shared__ int8_t mk[SC_CHUNK];
+    __shared__ double cx[SC_CHUNK];      // w * x, then the running sum, then the running mean
+    __shared__ double dn[SC_CHUNK];      // max(running weight, 1)
+    __shared__ double dv[SC_CHUNK];      // deviation terms, then the running m2 at patch ends
+    __shared__ float ploc[SC_CHUNK], pscale[SC_CHUNK];
+    __shared__ int8_t pobs[SC_CHUNK];
+    __shared__ int wsum[SC_THREADS / 32];
+    __shared__ float wlo[SC_THREADS / 32], whi[SC_THREADS / 32];
+    __shared__ double prev_mean_sh;
+    __shared__ long long weight_sh;
+    const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, ps = c.ps;
+    const int chunk = (SC_CHUNK / ps) * ps;
+    const float* x = rows + int64_t(r) * W;
+    const int8_t* m = mask + int64_t(r) * W;
+    float* feat = features + int64_t(r) * (W / ps) * 2 * ps;
+    // thread 0's sequential state
+    double cum_x = 0, m2 = 0;
+    bool started = false;
+    int first = -1;
+    uint32_t word = 0;
+    float lo = INFINITY, hi = -INFINITY;    // this thread's share of the cap statistics
+    if (tid == 0) { prev_mean_sh = 0.0; weight_sh = 0; }
+    for (int c0 = 0; c0 < W; c0 += chunk) {
+        const int n = min(chunk, W - c0);
+        for (int i = tid; i < n; i += SC_THREADS) {
+            const float v = x[c0 + i];
+            const int8_t w = m[c0 + i];
+            xs[i] = v;
+            mk[i] = w;
+            cx[i] = __dmul_rn(double(w), double(v));
+            if (c0 + i < ctx_len && w) { lo = fminf(lo, v); hi = fmaxf(hi, v); }
+        }
+        __syncthreads();
+        // running weight: block-wide inclusive scan of the mask over steps [tid*8, tid*8+8)
+        {
+            int part[SC_PER], run = 0;
+#pragma unroll
+            for (int k = 0; k < SC_PER; ++k) {
+                const int i = tid * SC_PER + k;
+                run += i < n ? int(mk[i]) : 0;
+                part[k] = run;
+            }
+            int incl = run;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (lane == 31) wsum[wid] = incl;
+            __syncthreads();
+            long long base = weight_sh;
+            for (int w = 0; w < wid; ++w) base += wsum[w];
+            base += incl - run;
+#pragma unroll
+            for (int k = 0; k < SC_PER; ++k) {
+                const int i = tid * SC_PER + k;
+                if (i < n) dn[i] = fmax(double(base + part[k]), 1.0);
+            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            long long total = weight_sh;
+            for (int w = 0; w < SC_THREADS / 32; ++w) total += wsum[w];
+            weight_sh = total;
+            // the running sum, eight products loaded ahead
+            int i = 0;
+            for (; i + 8 <= n; i += 8) {
+                double a[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) a[k] = cx[i + k];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) { cum_x = __dadd_rn(cum_x, a[k]); cx[i + k] = cum_x; }
+            }
+            for (; i < n; ++i) { cum_x = __dadd_rn(cum_x, cx[i]); cx[i] = cum_x; }
+        }
+        __syncthreads();
+        for (int i = tid; i < n; i += SC_THREADS) cx[i] = __ddiv_rn(cx[i], dn[i]);
+        __syncthreads();
+        for (int i = tid; i < n; i += SC_THREADS) {
+            const double v = xs[i], w = mk[i];
+            const double pm = i == 0 ? prev_mean_sh : cx[i - 1];
+            dv[i] = __dmul_rn(__dmul_rn(__dsub_rn(v, pm), __dsub_rn(v, cx[i])), w);
+        }
+        __syncthreads();
+        const int np = n / ps;
+        if (tid == 0) {
+            // the m2 chain, eight terms loaded ahead; m2 is kept at each patch end
+            int i = 0;
+            if ((ps & 7) == 0) {
+                for (int pp = 0; pp < np; ++pp) {
+                    for (int j = 0; j < ps; j += 8, i += 8) {
+                        double d[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) d[k] = dv[i + k];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) m2 = __dadd_rn(m2, d[k]);
+                    }
+                    dv[i - 1] = m2;
+                }
+            } else {
+                for (int pp = 0; pp < np; ++pp) {
+                    for (int j = 0; j < ps; ++j, ++i) m2 = __dadd_rn(m2, dv[i]);
+                    dv[i - 1] = m2;
+                }
+            }
+            for (; i < n; ++i) m2 = __dadd_rn(m2, dv[i]);
+            prev_mean_sh = cx[n - 1];
+        }
+        __syncthreads();
+        for (int pp = tid; pp < np; pp += SC_THREADS) {
+            const int te = (pp + 1) * ps - 1, t0 = c0 + pp * ps;
+            const float loc = float(cx[te]);
+            const float scale = float(fmax(sqrt(__ddiv_rn(dv[te], fmax(__dsub_rn(dn[te], 1.0), 1.0))), c.minimum_scale));
+            ploc[pp] = loc;
+            pscale[pp] = scale;
+            bool obs = false;
+            for (int j = 0; j < ps; ++j) obs |= mk[pp * ps + j] != 0;
+            pobs[pp] = obs;
+            if (anchor_step >= t0 && anchor_step <= t0 + ps - 1) { aloc[r] = loc; ascale[r] = scale; }
+            if (cap_scale && ctx_len - 1 >= t0 && ctx_len - 1 <= t0 + ps - 1) cap_scale[r] = scale;
+        }
+        __syncthreads();
+        float* f = feat + int64_t(c0 / ps) * 2 * ps;
+        for (int e = tid; e < np * ps; e += SC_THREADS) {
+            const int pp = e / ps, j = e - pp * ps;
+            const bool o = mk[e] != 0;
+            f[int64_t(pp) * 2 * ps + j] = affine_value(xs[e], ploc[pp], pscale[pp], o, c.use_asinh);
+            f[int64_t(pp) * 2 * ps + ps + j] = o ? 0.f : 1.f;
+        }
+        if (tid == 0) {
+            for (int pp = 0; pp < np; ++pp) {
+                const int p = c0 / ps + pp;
+                if (p >= enc_patches) break;
+                const bool obs = pobs[pp];
+                started |= obs;
+                if (obs && first < 0) first = p;
+                if (obs || (c.attend_missing && started)) word |= 1u << (p & 31);
+                if ((p & 31) == 31 || p == enc_patches - 1) {
+                    key_valid[int64_t(r) * kv_words + (p >> 5)] = word;
+                    word = 0;
+                }
+            }
+        }
+        __syncthreads();
+    }
+    // cap statistics: minimum and maximum over the observed steps of the context
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    if (lane == 0) { wlo[wid] = lo; whi[wid] = hi; }
+    __syncthreads();
+    if (tid == 0) {
+        first_obs[r] = first;
+        if (cap_lo) {
+            for (int w = 1; w < SC_THREADS / 32; ++w) { lo = fminf(lo, wlo[w]); hi = fmaxf(hi, whi[w]); }
+            cap_lo[r] = isfinite(lo) ? lo : 0.f;
+            cap_hi[r] = isfinite(hi) ? hi : 0.f;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------------------
 // Float sum cascade of ATen's contiguous reduction, one warp per sequence: lane j holds the
 // accumulators of lane slot (k, l) = (j / 8, j % 8) (reference src/torch_sum.hpp:9-23,
@@ -684,10 +865,17 @@ cudaError_t clip_eligibility(const float* ctx, const uint8_t* umask, int BV, int
 
 cudaError_t scale_rows(const RowConfig& c, const float* rows, const int8_t* mask, int R, int W, int anchor_step,
                        int enc_patches, int kv_words, float* features, float* loc, float* scale, uint32_t* key_valid,
-                       int* first_obs, int ctx_len, float* cap_lo, float* cap_hi, float* cap_scale, cudaStream_t s) {
+                       int* first_obs, int ctx_len, float* cap_lo, float* cap_hi, float* cap_scale, cudaStream_t s,
+                       int kernel) {
     if (R <= 0) return cudaSuccess;
-    scale_kernel<<<blocks_for(R, 64), 64, 0, s>>>(c, rows, mask, R, W, anchor_step, enc_patches, kv_words, features, loc,
-                                                 scale, key_valid, first_obs, ctx_len, cap_lo, cap_hi, cap_scale);
+    const bool block_ok = c.ps > 0 && c.ps <= SC_CHUNK && (W % c.ps) == 0;
+    if (kernel == 1 && !block_ok) return cudaErrorInvalidValue;
+    if (kernel != 0 && block_ok)
+        scale_block_kernel<<<R, SC_THREADS, 0, s>>>(c, rows, mask, W, anchor_step, enc_patches, kv_words, features, loc,
+                                                    scale, key_valid, first_obs, ctx_len, cap_lo, cap_hi, cap_scale);
+    else
+        scale_kernel<<<blocks_for(R, 64), 64, 0, s>>>(c, rows, mask, R, W, anchor_step, enc_patches, kv_words, features,
+                                                     loc, scale, key_valid, first_obs, ctx_len, cap_lo, cap_hi, cap_scale);
     return cudaGetLastError();
 }
 

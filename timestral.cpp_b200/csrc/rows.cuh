@@ -31,7 +31,10 @@ cudaError_t assemble_targets(const float* ctx, const uint8_t* umask, int BV, int
 // `enc_patches` patches; optional cap statistics over the first `ctx_len` steps.
 cudaError_t scale_rows(const RowConfig& c, const float* rows, const int8_t* mask, int R, int W, int anchor_step,
                        int enc_patches, int kv_words, float* features, float* loc, float* scale, uint32_t* key_valid,
-                       int* first_obs, int ctx_len, float* cap_lo, float* cap_hi, float* cap_scale, cudaStream_t s);
+                       int* first_obs, int ctx_len, float* cap_lo, float* cap_hi, float* cap_scale, cudaStream_t s,
+                       int kernel = -1);
+// kernel: -1 the block-per-row form when the patch size allows it, 0 one thread per row,
+// 1 one block per row (identical results).
 
 // --- instance-norm statistics of known covariate rows, overwriting their features and
 // anchors (reference src/scaler.cpp:60-107).

@@ -114,6 +114,22 @@ extern "C" TIMESTRAL_API int tsb_test_attention_time_ex(const void* q, const voi
     return h ? TSB_ERR_DEVICE : TSB_OK;
 }
 
+extern "C" TIMESTRAL_API int tsb_test_scale_rows(const float* rows, const int8_t* mask, int32_t R, int32_t W, int32_t ps,
+                                                double minimum_scale, int32_t use_asinh, int32_t attend_missing,
+                                                int32_t anchor_step, int32_t enc_patches, int32_t ctx_len, int32_t kernel,
+                                                float* features, float* loc, float* scale, uint32_t* key_valid,
+                                                int32_t* first_obs, float* cap_lo, float* cap_hi, float* cap_scale) {
+    if (!rows || !mask || !features || !loc || !scale || !key_valid || !first_obs || R <= 0 || ps <= 0 || W <= 0 ||
+        W % ps || enc_patches <= 0 || enc_patches > W / ps || kernel < 0 || kernel > 1)
+        return TSB_ERR_ARG;
+    tsb::RowConfig c;
+    c.ps = ps; c.minimum_scale = minimum_scale; c.use_asinh = use_asinh; c.attend_missing = attend_missing;
+    cudaError_t e = tsb::scale_rows(c, rows, mask, R, W, anchor_step, enc_patches, (enc_patches + 31) / 32, features, loc,
+                                    scale, key_valid, first_obs, ctx_len, cap_lo, cap_hi, cap_scale, 0, kernel);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e == cudaSuccess ? TSB_OK : (e == cudaErrorInvalidValue ? TSB_ERR_ARG : TSB_ERR_CUDA);
+}
+
 extern "C" TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, void* out, int32_t* d_overflow) {
     if (!a || !out || !d_overflow || rows < 0 || K <= 0) return TSB_ERR_ARG;
     cudaError_t e = tsb::split_f16(a, rows, K, static_cast<__half*>(out), d_overflow, nullptr, 0);

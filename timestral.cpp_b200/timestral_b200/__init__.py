@@ -63,6 +63,8 @@ SIGNATURES = {
     "tsb_last_geometry": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64)] + [C.POINTER(C.c_int32)] * 3),
     "tsb_test_gemm": (C.c_int, [C.POINTER(GemmTest), C.POINTER(C.c_int32)]),
     "tsb_test_attention_time": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 4 + [C.POINTER(C.c_int32)]),
+    "tsb_test_scale_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_double] + [C.c_int32] * 6
+                            + [C.c_void_p] * 8),
     "tsb_test_attention_time_ex": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 9 + [C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
     "tsb_test_split_f16": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p]),
     "tsb_test_attention_variate": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 5),
