@@ -61,6 +61,9 @@ CONFIGS = {
 # ncu capture summarised in profiles/attention_time_tc_cfg5.md (B = 1024, dram__bytes_read.sum
 # + dram__bytes_write.sum over 24,576 problems); traffic per launch scales with the problems.
 ATTN_DRAM_BYTES_PER_PROBLEM = 45384
+# The same for the long-row kernel at S = 1056 (cfg6), per (row, head) plane, from
+# profiles/attention_time_tc_long_cfg6.md (B = 8: 119.4 MB over 192 planes).
+ATTN_LONG_DRAM_BYTES_PER_PLANE = 621760
 
 
 def parse():
@@ -387,8 +390,8 @@ def main():
                              "frac": achieved_gbs / hbm} if roof_tf < tf else
                             {"bound": "tensor", "achieved": achieved_tf, "peak": tf_sus, "unit": "TFLOP/s",
                              "frac": achieved_tf / tf_sus}),
-                         "traffic": (ATTN_DRAM_BYTES_PER_PROBLEM * problems
-                                     if (a.config == "cfg5" and ATTN_DRAM_BYTES_PER_PROBLEM) else None),
+                         "traffic": (ATTN_DRAM_BYTES_PER_PROBLEM * problems if a.config == "cfg5" else
+                                     ATTN_LONG_DRAM_BYTES_PER_PLANE * problems if a.config == "cfg6" else None),
                          "traffic_unit": "bytes per launch", "algorithmic_bytes": att_bytes,
                          "achieved_tflops": achieved_tf, "roofline_tflops": roof_tf,
                          "frac_of_dense_contraction_roofline": achieved_tf / roof_tf,
