@@ -45,8 +45,13 @@ TIMESTRAL_API int tsb_sync(timestral_ctx* ctx);
 TIMESTRAL_API int tsb_set_device(int32_t device);
 /* cudaStream_t of the handle (as an opaque pointer), for callers that time with events. */
 TIMESTRAL_API void* tsb_stream(timestral_ctx* ctx);
+/* Covariate requests: assemble the rows on the device (on_device != 0, the default) or on
+ * the host (the host path of the reference's assemble_rows, kept for comparison); the two
+ * give identical forecasts. Replaces nothing in the reference (its assembly is host-only,
+ * src/covariates.cpp:32-72). */
+TIMESTRAL_API int tsb_covariate_assembly(timestral_ctx* ctx, int32_t on_device);
 /* Per-kernel timing: when enabled, kernel launches are bracketed by CUDA events on the
- * handle's stream and read back per class ("attention", "gemm", "rows", "all").
+ * handle's stream and read back per class ("attention", "gemm", "rms", "scale", "all", ...).
  * enable: 0 off, 1 every launch, 2 attention launches alone. */
 TIMESTRAL_API int tsb_timing_enable(timestral_ctx* ctx, int32_t enable);
 /* Total milliseconds and launch count recorded for a kernel class since the last reset. */

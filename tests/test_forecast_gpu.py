@@ -142,6 +142,42 @@ def test_small_f16_long_covariates():
     check_nd(g, r, x, 32, F16_MEAN_ND)
 
 
+@pytest.mark.parametrize("V,T,H,cats,mask,nan_codes", [(1, 192, 40, 2, False, False), (1, 300, 70, 1, True, True),
+                                                     (3, 200, 40, 2, False, False), (1, 5000, 64, 2, False, True),
+                                                     (2, 96, 33, 0, True, False)])
+def test_device_covariate_assembly_equals_host(V, T, H, cats, mask, nan_codes):
+    """Covariate rows assembled on the device (forward fill, casts, smoothed-mean target
+    encoding for one-target series, padding, roles, futures, mirrored pass) give the same
+    forecast bit for bit as the host assembly (reference src/covariates.cpp:14-72)."""
+    m, _ = models(sy.spec_small(True), "f16")
+    rng = np.random.default_rng(T + H + V)
+    B = 3
+    x = random_context(B, V, T, seed=T)
+    x[0, :, : T // 3] = np.nan                       # a late first observation
+    kw = dict(past=rng.standard_normal((B, 2, T)).astype(np.float32),
+              known=rng.standard_normal((B, 1, T + H)).astype(np.float32))
+    kw["past"][1, 0, 5:9] = np.nan
+    kw["known"][2, 0, T + 3] = np.inf
+    if cats:
+        ck = rng.integers(0, 7, (B, cats, T + H)).astype(np.float64)
+        cp = rng.integers(-3, 3, (B, 1, T)).astype(np.float64) * 0.5
+        if nan_codes:
+            ck[0, 0, ::11] = np.nan
+            cp[1, 0, ::5] = np.nan
+            ck[2, -1, T:] = 99.0                          # future codes absent from the context
+        ck[1, 0, T // 2] = -0.0
+        kw.update(cat_known=ck, cat_past=cp)
+    if mask:
+        kw["mask"] = (rng.random((B, V, T)) > 0.2)
+    try:
+        m.covariate_assembly(False)
+        host = m.forecast(x, H, **kw)
+    finally:
+        m.covariate_assembly(True)
+    dev = m.forecast(x, H, **kw)
+    assert np.array_equal(dev.view(np.uint32), host.view(np.uint32)), float(np.abs(dev - host).max())
+
+
 def test_small_f16_covariates():
     m, o = models(sy.spec_small(True), "f16")
     rng = np.random.default_rng(21)

@@ -99,6 +99,8 @@ struct Engine::Impl {
     DevBuf rows, mask, win, wmask, role, future, fmask, feat, aloc, ascale, caplo, caphi, capsc, first_obs, kv, rope_row,
         gbeg, gsize, clip_ok, x, xn, qb, kb, vb, gb, att, hb, zb, fused, gtmp, ph, dec, hh, hraw, qout, refined, scratch,
         decoded, err, next_rows, next_mask, feat16, pflag, panel_scratch;
+    // raw covariate request inputs and assembly scratch
+    DevBuf cov_ctx, cov_umask, cov_past, cov_known, cov_cpast, cov_cknown, cov_first, cov_scratch;
     // timing
     bool timing = false;
     std::string timing_only;   // empty: every class
@@ -768,10 +770,7 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
     Impl& im = *impl_;
     im.launches = 0;
     const ModelView& mv = im.mv;
-    const int ps = im.ps, Q = im.Q;
     const int R = a.R, T = a.T, R2 = symmetric ? 2 * R : R;
-    const int patches = (H + ps - 1) / ps;
-    const int shot = std::min(mv.per_shot ? mv.per_shot : 32, mv.block_size);
     const bool cov = a.roles != nullptr && mv.covariate_enabled;
     const cudaStream_t s = stream_;
     // Upload context rows (+ negation), roles, known future (+ negation).
@@ -815,6 +814,73 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
         im.run("clip", [&] { return clip_eligibility(dctx.as<float>(), umask ? dum.as<uint8_t>() : nullptr, B * V, T_req, im.clip_ok.as<int8_t>(), s); });
         check(cudaStreamSynchronize(s), "sync");
     }
+    decode_rows(B, V, H, R, T, Hh, symmetric, clip, cov, a.future != nullptr, a.group_rows, h_out);
+}
+
+void Engine::forecast_covariates(const CovRequest& q, bool symmetric, bool clip, float* h_out) {
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    Impl& im = *impl_;
+    im.launches = 0;
+    const ModelView& mv = im.mv;
+    const int all = q.V + q.P + q.CP + q.K + q.CK;
+    const int64_t R64 = int64_t(q.B) * all;
+    if (q.B <= 0 || q.V <= 0 || q.T <= 0 || q.H <= 0 || R64 * (symmetric ? 2 : 1) > INT32_MAX)
+        throw std::runtime_error("invalid covariate request dimensions");
+    const int R = int(R64), R2 = symmetric ? 2 * R : R;
+    const cudaStream_t s = stream_;
+    const size_t TH = size_t(q.T) + q.H;
+    auto upload = [&](DevBuf& d, const void* src, size_t bytes) {
+        if (!bytes) return;
+        d.ensure(bytes);
+        check(cudaMemcpyAsync(d.p, src, bytes, cudaMemcpyHostToDevice, s), "upload");
+    };
+    upload(im.cov_ctx, q.ctx, size_t(q.B) * q.V * q.T * 4);
+    if (q.umask) upload(im.cov_umask, q.umask, size_t(q.B) * q.V * q.T);
+    upload(im.cov_past, q.past, size_t(q.B) * q.P * q.T * 4);
+    upload(im.cov_known, q.known, size_t(q.B) * q.K * TH * 4);
+    upload(im.cov_cpast, q.cat_past, size_t(q.B) * q.CP * q.T * 8);
+    upload(im.cov_cknown, q.cat_known, size_t(q.B) * q.CK * TH * 8);
+    CovShape c;
+    c.B = q.B; c.V = q.V; c.P = q.P; c.CP = q.CP; c.K = q.K; c.CK = q.CK;
+    c.T = q.T; c.H = q.H; c.kept = q.kept; c.len = q.len; c.hor = q.hor;
+    c.mirrored = symmetric ? 1 : 0;
+    c.smooth = q.smooth;
+    const bool cov = mv.covariate_enabled && (q.P || q.K || q.CP || q.CK);
+    const bool has_future = q.K || q.CK;
+    im.rows.ensure(size_t(R2) * q.len * 4);
+    im.mask.ensure(size_t(R2) * q.len);
+    im.role.ensure(R2);
+    if (has_future) { im.future.ensure(size_t(R2) * q.hor * 4); im.fmask.ensure(size_t(R2) * q.hor); }
+    im.cov_first.ensure(size_t(q.B) * q.V * 4);
+    const size_t scratch = covariate_scratch_bytes(c);
+    if (scratch) im.cov_scratch.ensure(scratch);
+    im.run("assemble", [&] {
+        return assemble_covariates(c, im.cov_ctx.as<float>(), q.umask ? im.cov_umask.as<uint8_t>() : nullptr,
+                                   im.cov_past.as<float>(), im.cov_known.as<float>(), im.cov_cpast.as<double>(),
+                                   im.cov_cknown.as<double>(), im.rows.as<float>(), im.mask.as<int8_t>(),
+                                   cov ? im.role.as<int8_t>() : nullptr, has_future ? im.future.as<float>() : nullptr,
+                                   has_future ? im.fmask.as<int8_t>() : nullptr, im.cov_first.as<int>(),
+                                   scratch ? im.cov_scratch.p : nullptr, s);
+    });
+    if (clip) {
+        im.clip_ok.ensure(size_t(q.B) * q.V);
+        im.run("clip", [&] {
+            return clip_eligibility(im.cov_ctx.as<float>(), q.umask ? im.cov_umask.as<uint8_t>() : nullptr, q.B * q.V,
+                                    q.T, im.clip_ok.as<int8_t>(), s);
+        });
+    }
+    decode_rows(q.B, q.V, q.H, R, q.len, q.hor, symmetric, clip, cov, has_future, all, h_out);
+}
+
+void Engine::decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetric, bool clip, bool cov,
+                         bool has_future, int group_rows, float* h_out) {
+    Impl& im = *impl_;
+    const ModelView& mv = im.mv;
+    const int ps = im.ps, Q = im.Q;
+    const int R2 = symmetric ? 2 * R : R;
+    const int patches = (H + ps - 1) / ps;
+    const int shot = std::min(mv.per_shot ? mv.per_shot : 32, mv.block_size);
+    const cudaStream_t s = stream_;
     im.decoded.ensure(size_t(R2) * H * Q * 4);
     int Tc = T, done = 0;
     while (done < patches) {
@@ -826,11 +892,11 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
         check(cudaMemsetAsync(im.wmask.p, 0, size_t(R2) * W, s), "memset");
         check(cudaMemcpy2DAsync(im.win.p, size_t(W) * 4, im.rows.p, size_t(Tc) * 4, size_t(Tc) * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
         check(cudaMemcpy2DAsync(im.wmask.p, W, im.mask.p, Tc, Tc, R2, cudaMemcpyDeviceToDevice, s), "copy");
-        if (cov && a.future) {
+        if (cov && has_future) {
             check(cudaMemcpy2DAsync(im.win.as<float>() + Tc, size_t(W) * 4, im.future.as<float>() + offset, size_t(Hh) * 4, size_t(n) * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
             check(cudaMemcpy2DAsync(im.wmask.as<int8_t>() + Tc, W, im.fmask.as<int8_t>() + offset, Hh, n, R2, cudaMemcpyDeviceToDevice, s), "copy");
         }
-        im.predict_block(R2, Tc, block, cov, a.group_rows, R, done == 0, Tc);
+        im.predict_block(R2, Tc, block, cov, group_rows, R, done == 0, Tc);
         const int used = std::min(n, H - offset);
         check(cudaMemcpy2DAsync(im.decoded.as<float>() + size_t(offset) * Q, size_t(H) * Q * 4, im.refined.p,
                                 size_t(n) * Q * 4, size_t(used) * Q * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
@@ -841,15 +907,15 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
         im.next_mask.ensure(size_t(R2) * keep);
         // future slice of this block, row stride n
         DevBuf fs, fms;
-        if (a.future) {
+        if (has_future) {
             fs.ensure(size_t(R2) * n * 4); fms.ensure(size_t(R2) * n);
             check(cudaMemcpy2DAsync(fs.p, size_t(n) * 4, im.future.as<float>() + offset, size_t(Hh) * 4, size_t(n) * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
             check(cudaMemcpy2DAsync(fms.p, n, im.fmask.as<int8_t>() + offset, Hh, n, R2, cudaMemcpyDeviceToDevice, s), "copy");
         }
         im.run("feedback", [&] {
             return feedback(im.rc, im.rows.as<float>(), im.mask.as<int8_t>(), R2, Tc, im.refined.as<float>(), n,
-                            cov ? im.role.as<int8_t>() : nullptr, a.future ? fs.as<float>() : nullptr,
-                            a.future ? fms.as<int8_t>() : nullptr, keep, im.next_rows.as<float>(), im.next_mask.as<int8_t>(), s);
+                            cov ? im.role.as<int8_t>() : nullptr, has_future ? fs.as<float>() : nullptr,
+                            has_future ? fms.as<int8_t>() : nullptr, keep, im.next_rows.as<float>(), im.next_mask.as<int8_t>(), s);
         });
         check(cudaStreamSynchronize(s), "sync");
         std::swap(im.rows.p, im.next_rows.p); std::swap(im.rows.bytes, im.next_rows.bytes);

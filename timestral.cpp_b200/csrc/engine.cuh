@@ -53,6 +53,22 @@ struct HostRows {
     int group_rows = 1;                       // rows per series (contiguous)
 };
 
+// A covariate request as the caller holds it (reference ForecastRequest fields), assembled
+// on the device: context [B][V][T] (+ optional 0/1 mask), past [B][P][T], known [B][K][T+H],
+// categorical past [B][CP][T] and known [B][CK][T+H] f64 codes (validated by the caller:
+// finite or NaN). kept/len/hor: kept context steps, padded row length, padded horizon.
+struct CovRequest {
+    int B = 0, V = 0, T = 0, H = 0, P = 0, K = 0, CP = 0, CK = 0;
+    const float* ctx = nullptr;
+    const uint8_t* umask = nullptr;
+    const float* past = nullptr;
+    const float* known = nullptr;
+    const double* cat_past = nullptr;
+    const double* cat_known = nullptr;
+    int kept = 0, len = 0, hor = 0;
+    double smooth = 0;
+};
+
 class Engine {
 public:
     Engine(const ModelView& mv, int device);
@@ -72,6 +88,8 @@ public:
     // formed on the device). ctx/umask: the original request context (clip eligibility).
     void forecast_rows(const HostRows& a, int B, int V, int H, bool symmetric, bool clip, const float* ctx,
                        const uint8_t* umask, int T_req, float* h_out);
+    // Requests with covariates assembled on the device (host buffers in and out).
+    void forecast_covariates(const CovRequest& q, bool symmetric, bool clip, float* h_out);
 
     // Synchronise the stream and turn a device error word into an exception.
     void check_errors();
@@ -88,6 +106,10 @@ public:
     Geometry last_geometry() const;
 
 private:
+    // The decode blocks of an assembled covariate request (rows, masks, roles, futures in
+    // device memory) through the final download.
+    void decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetric, bool clip, bool cov, bool has_future,
+                     int group_rows, float* h_out);
     struct Impl;
     std::unique_ptr<Impl> impl_;
     int device_ = 0;

@@ -17,17 +17,23 @@ inline unsigned blocks_for(int64_t n, int tpb = TPB) { return unsigned((n + tpb 
 
 // ---------------------------------------------------------------------------------------
 // Assembly of target rows (reference src/covariates.cpp:48-50,69-70).
+// Target row i = b * V + v of the request goes to row (i / V) * all + i % V (all = rows per
+// series: V when there are no covariates), its negation to row `mirror_rows` + that row.
+// first_obs (optional): first observed step of each target row, T if none.
 __global__ void assemble_kernel(const float* __restrict__ ctx, const uint8_t* __restrict__ umask, int BV, int T,
-                                int kept, int len, int mirrored, float* __restrict__ rows, int8_t* __restrict__ mask) {
+                                int kept, int len, int mirrored, int V, int all, int64_t mirror_rows,
+                                float* __restrict__ rows, int8_t* __restrict__ mask, int* __restrict__ first_obs) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x & 31;
     if (warp >= BV) return;
     const int r = warp, pad = len - kept, start = T - kept;
+    const int64_t orow = int64_t(r / V) * all + r % V;
     const float* x = ctx + int64_t(r) * T;
     const uint8_t* um = umask ? umask + int64_t(r) * T : nullptr;
-    float* out = rows + int64_t(r) * len;
-    int8_t* om = mask + int64_t(r) * len;
-    float* out2 = mirrored ? rows + (int64_t(BV) + r) * len : nullptr;
-    int8_t* om2 = mirrored ? mask + (int64_t(BV) + r) * len : nullptr;
+    float* out = rows + orow * len;
+    int8_t* om = mask + orow * len;
+    float* out2 = mirrored ? rows + (mirror_rows + orow) * len : nullptr;
+    int8_t* om2 = mirrored ? mask + (mirror_rows + orow) * len : nullptr;
+    int first = T;
     for (int t = lane; t < pad; t += 32) {
         out[t] = 0.f; om[t] = 0;
         if (out2) { out2[t] = -0.f; om2[t] = 0; }
@@ -49,10 +55,205 @@ __global__ void assemble_kernel(const float* __restrict__ ctx, const uint8_t* __
         const int last = __shfl_sync(0xffffffffu, idx, 31);
         const float last_val = __shfl_sync(0xffffffffu, v, last < 0 ? 0 : last);
         if (last >= 0) carry = last_val;
+        const unsigned seen = __ballot_sync(0xffffffffu, obs);
+        if (first == T && seen) first = c0 + __ffs(seen) - 1;
         if (t < T && t >= start) {
             const int o = pad + t - start;
             out[o] = filled; om[o] = obs;
             if (out2) { out2[o] = -filled; om2[o] = obs; }
+        }
+    }
+    if (first_obs && lane == 0) first_obs[r] = first;
+}
+
+// ---------------------------------------------------------------------------------------
+// Covariate rows (reference src/covariates.cpp:32-72): per series b the rows are the V
+// targets, P past, CP categorical past, K known, CK categorical known covariates.
+__device__ __forceinline__ float finite_value(float v) {
+    return isnan(v) ? 0.f : isinf(v) ? copysignf(FLT_MAX, v) : v;
+}
+
+// One warp per covariate row (and per target row for its zero future): the kept context
+// window (left-padded to len) as finite values with the not-NaN mask, the known rows' future
+// steps, roles, and the negated copies of the mirrored pass.
+__global__ void cov_rows_kernel(const CovShape c, const float* __restrict__ past, const float* __restrict__ known,
+                                const double* __restrict__ cat_past, const double* __restrict__ cat_known,
+                                const float* __restrict__ enc_past, const float* __restrict__ enc_known,
+                                float* __restrict__ rows, int8_t* __restrict__ mask, int8_t* __restrict__ role,
+                                float* __restrict__ future, int8_t* __restrict__ fmask) {
+    const int all = c.V + c.P + c.CP + c.K + c.CK;
+    const int64_t R = int64_t(c.B) * all;
+    const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+    const int lane = threadIdx.x & 31;
+    if (warp >= R) return;
+    const int b = int(warp / all), j = int(warp % all);
+    const int TH = c.T + c.H, pad = c.len - c.kept, start = c.T - c.kept;
+    int kind;                 // 0 target, 1 past, 2 categorical past, 3 known, 4 categorical known
+    int64_t off = 0;
+    int jj = j;
+    if (jj < c.V) kind = 0;
+    else if ((jj -= c.V) < c.P) { kind = 1; off = (int64_t(b) * c.P + jj) * c.T; }
+    else if ((jj -= c.P) < c.CP) { kind = 2; off = (int64_t(b) * c.CP + jj) * c.T; }
+    else if ((jj -= c.CP) < c.K) { kind = 3; off = (int64_t(b) * c.K + jj) * TH; }
+    else { jj -= c.K; kind = 4; off = (int64_t(b) * c.CK + jj) * TH; }
+    const int rl = kind == 0 ? 0 : kind <= 2 ? 1 : 2;
+    const bool encoded = c.V == 1;
+    auto value = [&](int t) -> float {        // step t of the row's source (t < T + H)
+        switch (kind) {
+            case 1: return past[off + t];
+            case 2: return encoded ? enc_past[off + t] : float(cat_past[off + t]);
+            case 3: return known[off + t];
+            default: return encoded ? enc_known[off + t] : float(cat_known[off + t]);
+        }
+    };
+    if (lane == 0) {
+        if (role) role[warp] = int8_t(rl);
+        if (role && c.mirrored) role[R + warp] = int8_t(rl);
+    }
+    if (kind != 0) {
+        float* out = rows + warp * c.len;
+        int8_t* om = mask + warp * c.len;
+        for (int t = lane; t < c.len; t += 32) {
+            float y = 0.f;
+            int8_t m = 0;
+            if (t >= pad) {
+                const float v = value(start + t - pad);
+                y = finite_value(v);
+                m = !isnan(v);
+            }
+            out[t] = y; om[t] = m;
+            if (c.mirrored) { rows[(R + warp) * c.len + t] = -y; mask[(R + warp) * c.len + t] = m; }
+        }
+    }
+    if (future) {
+        for (int t = lane; t < c.hor; t += 32) {
+            float y = 0.f;
+            int8_t m = 0;
+            if (rl == 2 && t < c.H) {
+                const float v = value(c.T + t);
+                y = finite_value(v);
+                m = !isnan(v);
+            }
+            future[warp * c.hor + t] = y; fmask[warp * c.hor + t] = m;
+            if (c.mirrored) { future[(R + warp) * c.hor + t] = -y; fmask[(R + warp) * c.hor + t] = m; }
+        }
+    }
+}
+
+// Smoothed mean target encoding of one categorical row of a one-target series (reference
+// src/covariates.cpp:14-25), one block per (series, categorical row). The categories are the
+// distinct non-NaN codes of the context part; each category's sum of target values runs in
+// step order (the codes are sorted with their step as the tie-break), the target mean is the
+// NumPy pairwise sum over the context divided by the count of finite targets. Context steps
+// whose target and code are both NaN stay NaN; future codes absent from the context take the
+// mean. Scratch per block: values [Tp] f64, order [Tp] i32, lookups [T] f32.
+constexpr int ENC_THREADS = 256;
+__device__ double numpy_sum_dev(const double* x, int n);   // NumPy pairwise sum, defined with refine
+
+__device__ __forceinline__ bool code_before(const double* code, int a, int b) {
+    if (a < 0) return false;                  // padding sorts last
+    if (b < 0) return true;
+    const double ca = code[a], cb = code[b];
+    const bool na = isnan(ca), nb = isnan(cb);
+    if (na != nb) return nb;                  // NaN codes after the categories
+    if (!na && ca != cb) return ca < cb;
+    return a < b;
+}
+__device__ __forceinline__ bool same_code(double a, double b) { return (isnan(a) && isnan(b)) || a == b; }
+
+__global__ void __launch_bounds__(ENC_THREADS)
+    target_encode_kernel(const CovShape c, const float* __restrict__ rows, const int* __restrict__ first_obs,
+                         const double* __restrict__ cat_past, const double* __restrict__ cat_known,
+                         float* __restrict__ enc_past, float* __restrict__ enc_known, double* __restrict__ scratch,
+                         int Tp) {
+    const int per = c.CP + c.CK;
+    const int b = blockIdx.x / per, k = blockIdx.x % per, tid = threadIdx.x;
+    const int all = c.V + c.P + c.CP + c.K + c.CK, T = c.T, TH = c.T + c.H;
+    const bool is_known = k >= c.CP;
+    const int width = is_known ? TH : T;
+    const double* code = is_known ? cat_known + (int64_t(b) * c.CK + (k - c.CP)) * TH : cat_past + (int64_t(b) * c.CP + k) * T;
+    float* enc = is_known ? enc_known + (int64_t(b) * c.CK + (k - c.CP)) * TH : enc_past + (int64_t(b) * c.CP + k) * T;
+    double* values = scratch + int64_t(blockIdx.x) * Tp * 2;
+    int* order = reinterpret_cast<int*>(values + Tp);
+    float* lookup = reinterpret_cast<float*>(order + Tp);
+    const float* filled = rows + int64_t(b) * all * c.len + (c.len - c.kept);   // the series' target row
+    const int start = T - c.kept, first = first_obs[b];
+    __shared__ int count_sh;
+    __shared__ double mean_sh, nan_lookup_sh;
+    __shared__ int has_nan_sh;
+    if (tid == 0) { count_sh = 0; has_nan_sh = 0; }
+    __syncthreads();
+    // target values: the forward-filled target from its first observation, inside the kept window
+    int cnt = 0;
+    for (int i = tid; i < Tp; i += ENC_THREADS) {
+        double v = 0.0;
+        if (i < T && i >= start && i >= first) { v = double(filled[i - start]); cnt += isfinite(v) ? 1 : 0; }
+        if (i < T && !isfinite(v)) v = 0.0;
+        values[i] = v;
+        order[i] = i < T ? i : -1;
+    }
+    atomicAdd(&count_sh, cnt);
+    __syncthreads();
+    if (tid == 0) mean_sh = count_sh ? __ddiv_rn(numpy_sum_dev(values, T), double(count_sh)) : 0.0;
+    // bitonic sort of the steps by (code, step)
+    for (int size = 2; size <= Tp; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            __syncthreads();
+            for (int i = tid; i < Tp; i += ENC_THREADS) {
+                const int jx = i ^ stride;
+                if (jx > i) {
+                    const int a = order[i], bb = order[jx];
+                    const bool up = (i & size) == 0;
+                    if (up ? code_before(code, bb, a) : code_before(code, a, bb)) { order[i] = bb; order[jx] = a; }
+                }
+            }
+        }
+    __syncthreads();
+    const double mean = mean_sh, smooth = c.smooth;
+    // one thread per category: its sum in step order, its count, its lookup value
+    for (int kk = tid; kk < T; kk += ENC_THREADS) {
+        const int i0 = order[kk];
+        if (kk > 0 && same_code(code[order[kk - 1]], code[i0])) continue;
+        double sum = 0.0, n = 0.0;
+        int e = kk;
+        for (; e < T && same_code(code[order[e]], code[i0]); ++e) {
+            const int i = order[e];
+            sum = __dadd_rn(sum, values[i]);
+            const bool fin = i >= start && i >= first && isfinite(filled[i - start]);
+            n = __dadd_rn(n, fin ? 1.0 : 0.0);
+        }
+        const double lk = __ddiv_rn(__dadd_rn(__dmul_rn(smooth, mean), sum), __dadd_rn(smooth, n));
+        for (int e2 = kk; e2 < e; ++e2) lookup[order[e2]] = float(lk);
+        if (isnan(code[i0])) { nan_lookup_sh = lk; has_nan_sh = 1; }
+    }
+    __syncthreads();
+    if (tid == 0 && !has_nan_sh)
+        nan_lookup_sh = __ddiv_rn(__dadd_rn(__dmul_rn(smooth, mean), 0.0), __dadd_rn(smooth, 0.0));
+    __syncthreads();
+    // number of non-NaN codes in the context part (they sort first)
+    __shared__ int finite_sh;
+    if (tid == 0) {
+        int lo = 0, hi = T;
+        while (lo < hi) { const int mid = (lo + hi) >> 1; if (isnan(code[order[mid]])) hi = mid; else lo = mid + 1; }
+        finite_sh = lo;
+    }
+    __syncthreads();
+    const int nf = finite_sh;
+    for (int i = tid; i < width; i += ENC_THREADS) {
+        if (i < T) {
+            const bool tgt_nan = !(i >= start && i >= first) || !isfinite(filled[i - start]);
+            enc[i] = (tgt_nan && isnan(code[i])) ? NAN : lookup[i];
+        } else {
+            const double f = code[i];
+            float v;
+            if (isnan(f)) {
+                v = float(nan_lookup_sh);
+            } else {
+                int lo = 0, hi = nf;
+                while (lo < hi) { const int mid = (lo + hi) >> 1; if (code[order[mid]] < f) lo = mid + 1; else hi = mid; }
+                v = (lo < nf && code[order[lo]] == f) ? lookup[order[lo]] : float(mean);
+            }
+            enc[i] = v;
         }
     }
 }
@@ -602,23 +803,49 @@ __global__ void quantile_kernel(const RowConfig c, const float* __restrict__ raw
 
 // ---------------------------------------------------------------------------------------
 // Refine (reference src/refine.cpp).
-__device__ double numpy_sum_dev(const double* x, int n) {
-    // NumPy pairwise float64 sum (reference src/numpy_sum.hpp:6-14), iterative over the
-    // recursion's leaves for n > 128.
+// NumPy pairwise float64 sum (reference src/numpy_sum.hpp:6-14): leaves of at most 128 values
+// summed with eight partial sums, each larger range split at half rounded down to a multiple
+// of 8 and its two halves added. Walked iteratively (post-order over an explicit stack of at
+// most 32 ranges) instead of recursively, so the per-thread stack stays fixed.
+__device__ double numpy_leaf(const double* x, int n) {
     if (n < 8) { double r = -0.0; for (int i = 0; i < n; ++i) r = __dadd_rn(r, x[i]); return r; }
-    if (n <= 128) {
-        double r[8];
-        for (int j = 0; j < 8; ++j) r[j] = x[j];
-        int i = 8;
-        for (; i < n - (n % 8); i += 8) for (int j = 0; j < 8; ++j) r[j] = __dadd_rn(r[j], x[i + j]);
-        double out = __dadd_rn(__dadd_rn(__dadd_rn(r[0], r[1]), __dadd_rn(r[2], r[3])),
-                               __dadd_rn(__dadd_rn(r[4], r[5]), __dadd_rn(r[6], r[7])));
-        for (; i < n; ++i) out = __dadd_rn(out, x[i]);
-        return out;
+    double r[8];
+    for (int j = 0; j < 8; ++j) r[j] = x[j];
+    int i = 8;
+    for (; i < n - (n % 8); i += 8) for (int j = 0; j < 8; ++j) r[j] = __dadd_rn(r[j], x[i + j]);
+    double out = __dadd_rn(__dadd_rn(__dadd_rn(r[0], r[1]), __dadd_rn(r[2], r[3])),
+                           __dadd_rn(__dadd_rn(r[4], r[5]), __dadd_rn(r[6], r[7])));
+    for (; i < n; ++i) out = __dadd_rn(out, x[i]);
+    return out;
+}
+__device__ double numpy_sum_dev(const double* x, int n) {
+    if (n <= 128) return numpy_leaf(x, n);
+    int off[32], len[32], state[32];   // state 0: unvisited, 1: left half pending, 2: right half pending
+    double acc[32];
+    int top = 0;
+    off[0] = 0; len[0] = n; state[0] = 0;
+    for (;;) {
+        if (len[top] > 128 && state[top] == 0) {
+            state[top] = 1;
+            const int half = len[top] / 2 - (len[top] / 2) % 8;
+            off[top + 1] = off[top]; len[top + 1] = half; state[top + 1] = 0;
+            ++top;
+            continue;
+        }
+        double v = numpy_leaf(x + off[top], len[top]);
+        for (;;) {
+            if (top == 0) return v;
+            --top;
+            if (state[top] == 1) {
+                acc[top] = v; state[top] = 2;
+                const int half = len[top] / 2 - (len[top] / 2) % 8;
+                off[top + 1] = off[top] + half; len[top + 1] = len[top] - half; state[top + 1] = 0;
+                ++top;
+                break;
+            }
+            v = __dadd_rn(acc[top], v);
+        }
     }
-    int half = n / 2;
-    half -= half % 8;
-    return __dadd_rn(numpy_sum_dev(x, half), numpy_sum_dev(x + half, n - half));
 }
 
 struct WS { double w, mean, m2; };
@@ -854,7 +1081,47 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtGemm g) {
 
 cudaError_t assemble_targets(const float* ctx, const uint8_t* umask, int BV, int T, int kept, int len, int mirrored,
                              float* rows, int8_t* mask, cudaStream_t s) {
-    assemble_kernel<<<blocks_for(int64_t(BV) * 32), TPB, 0, s>>>(ctx, umask, BV, T, kept, len, mirrored, rows, mask);
+    assemble_kernel<<<blocks_for(int64_t(BV) * 32), TPB, 0, s>>>(ctx, umask, BV, T, kept, len, mirrored, BV, BV, BV,
+                                                                   rows, mask, nullptr);
+    return cudaGetLastError();
+}
+
+static int pow2_at_least(int n) { int p = 1; while (p < n) p <<= 1; return p; }
+
+size_t covariate_scratch_bytes(const CovShape& c) {
+    if (c.V != 1 || c.CP + c.CK == 0) return 0;
+    const int Tp = pow2_at_least(c.T);
+    const int64_t blocks = int64_t(c.B) * (c.CP + c.CK);
+    const int64_t th = int64_t(c.T) + c.H;
+    // per block: values f64 + order i32 + lookups f32 over Tp; encoded rows f32
+    return size_t(blocks) * size_t(Tp) * 16 + size_t(c.B) * (size_t(c.CP) * c.T + size_t(c.CK) * th) * 4 + 256;
+}
+
+cudaError_t assemble_covariates(const CovShape& c, const float* ctx, const uint8_t* umask, const float* past,
+                                const float* known, const double* cat_past, const double* cat_known, float* rows,
+                                int8_t* mask, int8_t* role, float* future, int8_t* fmask, int* first_obs, void* scratch,
+                                cudaStream_t s) {
+    const int all = c.V + c.P + c.CP + c.K + c.CK;
+    const int64_t R = int64_t(c.B) * all, BV = int64_t(c.B) * c.V;
+    if (c.B <= 0 || c.V <= 0 || c.T <= 0 || c.kept <= 0 || c.kept > c.T || c.len < c.kept || R > INT32_MAX)
+        return cudaErrorInvalidValue;
+    assemble_kernel<<<blocks_for(BV * 32), TPB, 0, s>>>(ctx, umask, int(BV), c.T, c.kept, c.len, c.mirrored, c.V, all, R,
+                                                        rows, mask, first_obs);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    float *enc_p = nullptr, *enc_k = nullptr;
+    if (c.V == 1 && c.CP + c.CK > 0) {
+        if (!scratch) return cudaErrorInvalidValue;
+        const int Tp = pow2_at_least(c.T);
+        const int64_t blocks = int64_t(c.B) * (c.CP + c.CK);
+        enc_p = reinterpret_cast<float*>(static_cast<char*>(scratch) + size_t(blocks) * Tp * 16);
+        enc_k = enc_p + size_t(c.B) * c.CP * c.T;
+        target_encode_kernel<<<unsigned(blocks), ENC_THREADS, 0, s>>>(c, rows, first_obs, cat_past, cat_known, enc_p, enc_k,
+                                                                      static_cast<double*>(scratch), Tp);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    cov_rows_kernel<<<blocks_for(R * 32), TPB, 0, s>>>(c, past, known, cat_past, cat_known, enc_p, enc_k, rows, mask,
+                                                       role, future, fmask);
     return cudaGetLastError();
 }
 

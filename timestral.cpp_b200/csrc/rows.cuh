@@ -25,6 +25,28 @@ struct RowConfig {
 cudaError_t assemble_targets(const float* ctx, const uint8_t* umask, int BV, int T, int kept, int len, int mirrored,
                              float* rows, int8_t* mask, cudaStream_t s);
 
+// --- covariate requests assembled on the device (reference src/covariates.cpp:32-72):
+// per series b the rows b * all + j are its V targets (forward filled), P past, CP
+// categorical past, K known and CK categorical known covariates (codes cast to float, or
+// smoothed-mean target encoded when V == 1), the kept context left-padded to len, roles, the
+// known rows' future steps padded to hor, and the negated mirrored pass at rows R..2R-1.
+struct CovShape {
+    int B = 0, V = 0, P = 0, CP = 0, K = 0, CK = 0;
+    int T = 0, H = 0;               // request context length and horizon
+    int kept = 0, len = 0, hor = 0; // kept context steps, padded row length, padded horizon
+    int mirrored = 0;
+    double smooth = 0;              // target-encoding smoothing
+};
+size_t covariate_scratch_bytes(const CovShape& c);
+// ctx/umask [B][V][T] (umask may be null); past [B][P][T]; known [B][K][T+H]; cat_past
+// [B][CP][T] and cat_known [B][CK][T+H] f64 codes (finite or NaN); rows/mask [R2][len],
+// role [R2], future/fmask [R2][hor]; first_obs [B * V] scratch; scratch of
+// covariate_scratch_bytes(c) bytes (null when that is 0).
+cudaError_t assemble_covariates(const CovShape& c, const float* ctx, const uint8_t* umask, const float* past,
+                                const float* known, const double* cat_past, const double* cat_known, float* rows,
+                                int8_t* mask, int8_t* role, float* future, int8_t* fmask, int* first_obs, void* scratch,
+                                cudaStream_t s);
+
 // --- causal scaler + patch features (reference src/scaler.cpp:27-58, src/encoder.cpp:12-23).
 // rows/mask [R][W]; features [R][W/ps][2ps] f32; anchor frame of step `anchor_step`;
 // key-valid bits [R][kv_words]; first observed patch per row (-1 if none) among the first

@@ -273,6 +273,12 @@ TIMESTRAL_API int tsb_timing_enable(timestral_ctx* c, int32_t enable) {
     return TSB_OK;
 }
 
+TIMESTRAL_API int tsb_covariate_assembly(timestral_ctx* c, int32_t on_device) {
+    if (!c) return TSB_ERR_ARG;
+    c->forecaster.set_device_assembly(on_device != 0);
+    return TSB_OK;
+}
+
 TIMESTRAL_API int tsb_timing_read(timestral_ctx* c, const char* cls, double* ms, int64_t* launches) {
     if (!c || !cls || !ms || !launches) return TSB_ERR_ARG;
     c->forecaster.engine().timing_read(cls, ms, launches);

@@ -144,10 +144,15 @@ bool supports_known_covariates(const Config& c) {  // reference src/covariates.c
     return false;
 }
 
-AssembledRows assemble_rows(const Config& c, const std::vector<float>& context, const std::vector<int8_t>& user,
-                            size_t B, size_t V, size_t T, size_t H, const std::vector<float>& past, size_t P,
-                            const std::vector<float>& known, size_t K, size_t cap, const std::vector<double>& cp, size_t CP,
-                            const std::vector<double>& ck, size_t CK) {
+namespace {
+struct RowGeometry { size_t kept, pad, len, hor; };
+
+// The checks and the kept/padded lengths of an assembled covariate request (reference
+// src/covariates.cpp:32-47), shared by the host and the device assembly.
+RowGeometry check_rows(const Config& c, const std::vector<float>& context, const std::vector<int8_t>& user, size_t B,
+                       size_t V, size_t T, size_t H, const std::vector<float>& past, size_t P,
+                       const std::vector<float>& known, size_t K, size_t cap, const std::vector<double>& cp, size_t CP,
+                       const std::vector<double>& ck, size_t CK) {
     if (!B || !V || !T || !H || !c.patch_size || !c.context_length) throw Error("invalid row dimensions");
     const size_t TH = add(T, H), BV = mul(B, V);
     if (context.size() != mul(BV, T) || (!user.empty() && user.size() != context.size()) || past.size() != mul(mul(B, P), T) ||
@@ -160,8 +165,23 @@ AssembledRows assemble_rows(const Config& c, const std::vector<float>& context, 
     codes_valid(ck);
     cap = cap ? cap : c.context_length;
     if (cap > c.context_length) throw Error("max_context exceeds stored position range");
-    const size_t kept = std::min(T, cap), ps = c.patch_size, pad = (ps - kept % ps) % ps, len = add(kept, pad);
-    const size_t hor = mul(add(H, ps - 1) / ps, ps);
+    RowGeometry g;
+    const size_t ps = c.patch_size;
+    g.kept = std::min(T, cap);
+    g.pad = (ps - g.kept % ps) % ps;
+    g.len = add(g.kept, g.pad);
+    g.hor = mul(add(H, ps - 1) / ps, ps);
+    return g;
+}
+}  // namespace
+
+AssembledRows assemble_rows(const Config& c, const std::vector<float>& context, const std::vector<int8_t>& user,
+                            size_t B, size_t V, size_t T, size_t H, const std::vector<float>& past, size_t P,
+                            const std::vector<float>& known, size_t K, size_t cap, const std::vector<double>& cp, size_t CP,
+                            const std::vector<double>& ck, size_t CK) {
+    const RowGeometry geo = check_rows(c, context, user, B, V, T, H, past, P, known, K, cap, cp, CP, ck, CK);
+    const size_t TH = add(T, H), BV = mul(B, V);
+    const size_t kept = geo.kept, pad = geo.pad, len = geo.len, hor = geo.hor;
     const size_t all = add(add(V, add(P, CP)), add(K, CK)), R = mul(B, all);
     AssembledRows a;
     a.rows_count = R; a.length = len; a.horizon = hor;
@@ -382,6 +402,32 @@ void Forecaster::forecast_into(const ForecastRequest& r, float* out) {
         forecast_targets(r.context.data(),
                          r.observation_mask.empty() ? nullptr : reinterpret_cast<const uint8_t*>(r.observation_mask.data()),
                          r.batch, r.targets, r.length, r.horizon, sym, clip, r.max_context, out);
+        return;
+    }
+    if (device_assembly_) {
+        const RowGeometry g = check_rows(c, r.context, r.observation_mask, r.batch, r.targets, r.length, r.horizon, r.past,
+                                         r.past_count, r.known, r.known_count, r.max_context, r.categorical_past,
+                                         r.categorical_past_count, r.categorical_known, r.categorical_known_count);
+        const size_t all = r.targets + r.past_count + r.categorical_past_count + r.known_count + r.categorical_known_count;
+        if (mul(r.batch, all) > size_t(INT32_MAX) / 2 || g.len > size_t(INT32_MAX) || g.hor > size_t(INT32_MAX))
+            throw Error("forecast dimensions exceed the device path limits");
+        tsb::CovRequest q;
+        q.B = int(r.batch); q.V = int(r.targets); q.T = int(r.length); q.H = int(r.horizon);
+        q.P = int(r.past_count); q.K = int(r.known_count);
+        q.CP = int(r.categorical_past_count); q.CK = int(r.categorical_known_count);
+        q.ctx = r.context.data();
+        q.umask = r.observation_mask.empty() ? nullptr : reinterpret_cast<const uint8_t*>(r.observation_mask.data());
+        q.past = r.past.data(); q.known = r.known.data();
+        q.cat_past = r.categorical_past.data(); q.cat_known = r.categorical_known.data();
+        q.kept = int(g.kept); q.len = int(g.len); q.hor = int(g.hor);
+        q.smooth = c.target_encoding_smooth;
+        try {
+            eng.forecast_covariates(q, sym, clip, out);
+        } catch (const Error&) {
+            throw;
+        } catch (const std::exception& e) {
+            throw Error(e.what());
+        }
         return;
     }
     const AssembledRows a = assemble_rows(c, r.context, r.observation_mask, r.batch, r.targets, r.length, r.horizon, r.past,

@@ -64,9 +64,14 @@ public:
                           bool symmetric, bool clip, size_t max_context, float* out);
 
     tsb::Engine& engine() { return *engine_; }
+    // Covariate requests are assembled on the device (default) or, for comparison, on the
+    // host (assemble_rows) and uploaded; both give identical forecasts.
+    void set_device_assembly(bool on) { device_assembly_ = on; }
+    bool device_assembly() const { return device_assembly_; }
 
 private:
     const Model& model_;
+    bool device_assembly_ = true;
     std::unique_ptr<tsb::Engine> engine_;
     struct Staging;
     std::unique_ptr<Staging> staging_;

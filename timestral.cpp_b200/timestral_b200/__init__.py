@@ -63,6 +63,7 @@ SIGNATURES = {
     "tsb_last_geometry": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64)] + [C.POINTER(C.c_int32)] * 3),
     "tsb_test_gemm": (C.c_int, [C.POINTER(GemmTest), C.POINTER(C.c_int32)]),
     "tsb_test_attention_time": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 4 + [C.POINTER(C.c_int32)]),
+    "tsb_covariate_assembly": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_test_scale_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_double] + [C.c_int32] * 6
                             + [C.c_void_p] * 8),
     "tsb_test_attention_time_ex": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 9 + [C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
@@ -173,6 +174,11 @@ class Model:
 
     def stream(self) -> int:
         return lib().tsb_stream(self.h) or 0
+
+    def covariate_assembly(self, on_device: bool):
+        """Assemble covariate requests on the device (default) or on the host."""
+        if lib().tsb_covariate_assembly(self.h, int(on_device)) != 0:
+            raise RuntimeError("tsb_covariate_assembly failed")
 
     def timing(self, enable: bool, attention_only: bool = False):
         lib().tsb_timing_enable(self.h, 2 if (enable and attention_only) else int(enable))
