@@ -101,6 +101,8 @@ struct Engine::Impl {
         decoded, err, next_rows, next_mask, feat16, pflag, panel_scratch;
     // raw covariate request inputs and assembly scratch
     DevBuf cov_ctx, cov_umask, cov_past, cov_known, cov_cpast, cov_cknown, cov_first, cov_scratch;
+    // request-sized buffers kept across calls (no allocation on the forecast path once warm)
+    DevBuf req_ctx, req_umask, fut_slice, fmask_slice, out_rows;
     // timing
     bool timing = false;
     std::string timing_only;   // empty: every class
@@ -806,7 +808,8 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
     check(cudaMemcpyAsync(im.mask.p, mask2.data(), mask2.size(), cudaMemcpyHostToDevice, s), "upload");
     // clip eligibility from the request context
     if (clip) {
-        DevBuf dctx, dum;
+        DevBuf& dctx = im.req_ctx;
+        DevBuf& dum = im.req_umask;
         dctx.ensure(size_t(B) * V * T_req * 4);
         check(cudaMemcpyAsync(dctx.p, ctx, size_t(B) * V * T_req * 4, cudaMemcpyHostToDevice, s), "upload");
         if (umask) { dum.ensure(size_t(B) * V * T_req); check(cudaMemcpyAsync(dum.p, umask, size_t(B) * V * T_req, cudaMemcpyHostToDevice, s), "upload"); }
@@ -906,7 +909,8 @@ void Engine::decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetr
         im.next_rows.ensure(size_t(R2) * keep * 4);
         im.next_mask.ensure(size_t(R2) * keep);
         // future slice of this block, row stride n
-        DevBuf fs, fms;
+        DevBuf& fs = im.fut_slice;
+        DevBuf& fms = im.fmask_slice;
         if (has_future) {
             fs.ensure(size_t(R2) * n * 4); fms.ensure(size_t(R2) * n);
             check(cudaMemcpy2DAsync(fs.p, size_t(n) * 4, im.future.as<float>() + offset, size_t(Hh) * 4, size_t(n) * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
@@ -922,7 +926,7 @@ void Engine::decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetr
         std::swap(im.mask.p, im.next_mask.p); std::swap(im.mask.bytes, im.next_mask.bytes);
         Tc = keep;
     }
-    DevBuf dout;
+    DevBuf& dout = im.out_rows;
     dout.ensure(size_t(B) * V * H * Q * 4);
     const int all = R / B;
     // Cap statistics come from the first block's scale pass over the assembled context.
