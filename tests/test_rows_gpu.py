@@ -127,3 +127,43 @@ def test_scale_rows_block_form(dev, R, W, ps, attend):
     oloc, osc = oloc.reshape(R, W), osc.reshape(R, W)
     assert np.array_equal(outs[1][1].view(np.uint32), oloc[:, anchor].view(np.uint32))
     assert np.array_equal(outs[1][2].view(np.uint32), osc[:, anchor].view(np.uint32))
+
+
+GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden"
+
+
+@pytest.mark.parametrize("D", [128, 768])
+def test_rms_matches_reference_golden(dev, D):
+    """Device RMSNorm against the reference's own output (tests/golden, written by the
+    reference's compiled src/layers.cpp), bit for bit."""
+    d = np.load(GOLDEN / f"rms_norm_D{D}.npz")
+    x, w = d["x"], d["w"]
+    dx, dw = torch.from_numpy(x).to(dev), torch.from_numpy(w).to(dev)
+    out = torch.empty(x.shape, device=dev)
+    assert tb.lib().tsb_test_rms(dx.data_ptr(), dw.data_ptr(), x.shape[0], D, C.c_float(1e-6), out.data_ptr(), 0) == 0
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), d["out"].view(np.uint32))
+
+
+@pytest.mark.parametrize("kernel", [0, 1])
+def test_scaler_matches_reference_golden(dev, kernel):
+    """Both device scaler forms: the frame at every patch end equals the reference's own
+    running loc/scale there (tests/golden, written by the reference's compiled
+    src/scaler.cpp), bit for bit."""
+    d = np.load(GOLDEN / "scale_rows_ps32_T256.npz")
+    x, m = d["x"], d["m"]
+    R, W = x.shape
+    ps = 32
+    ref_loc, ref_scale = d["loc"].reshape(R, W), d["scale"].reshape(R, W)
+    dx, dm = torch.from_numpy(x).to(dev), torch.from_numpy(m).to(dev)
+    enc = W // ps
+    for anchor in range(ps - 1, W, ps):
+        feat = torch.empty((R, W // ps, 2 * ps), device=dev)
+        loc, sc = torch.empty(R, device=dev), torch.empty(R, device=dev)
+        kv = torch.zeros((R, (enc + 31) // 32), dtype=torch.int32, device=dev)
+        fo = torch.empty(R, dtype=torch.int32, device=dev)
+        rc = tb.lib().tsb_test_scale_rows(dx.data_ptr(), dm.data_ptr(), R, W, ps, C.c_double(1e-6), 1, 1, anchor, enc,
+                                          W, kernel, feat.data_ptr(), loc.data_ptr(), sc.data_ptr(), kv.data_ptr(),
+                                          fo.data_ptr(), None, None, None)
+        assert rc == 0
+        assert np.array_equal(loc.cpu().numpy().view(np.uint32), ref_loc[:, anchor].view(np.uint32)), anchor
+        assert np.array_equal(sc.cpu().numpy().view(np.uint32), ref_scale[:, anchor].view(np.uint32)), anchor
