@@ -36,9 +36,11 @@ def allowed_mask(valid, N, S):
     return enc | dec
 
 
-@pytest.mark.parametrize("S,N,gated", [(1, 1, True), (9, 8, True), (33, 30, False), (72, 64, True), (100, 97, True),
-                                       (128, 120, True), (70, 70, True)])
-def test_attention_time_tc(dev, S, N, gated):
+@pytest.mark.parametrize("S,N,gated,dense", [(1, 1, True, False), (9, 8, True, False), (33, 30, False, False),
+                                             (72, 64, True, False), (100, 97, True, False), (128, 120, True, False),
+                                             (70, 70, True, False), (72, 64, True, True), (128, 120, False, True),
+                                             (40, 32, True, True)])
+def test_attention_time_tc(dev, S, N, gated, dense):
     rows, H = 37, 3
     g = torch.Generator().manual_seed(S * 1000 + N)
     q = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
@@ -47,6 +49,8 @@ def test_attention_time_tc(dev, S, N, gated):
     gate = torch.rand(rows, H, S, 64, generator=g).half() if gated else None
     valid = torch.rand(rows, N, generator=g) > 0.2
     valid[:, 0] = True
+    if dense:                        # every key valid: unmasked 16-key chunks below the diagonal
+        valid[:] = True
     words = (N + 31) // 32
     bits = np.zeros((rows, words), np.uint32)
     vn = valid.numpy()
