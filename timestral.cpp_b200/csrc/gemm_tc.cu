@@ -96,7 +96,6 @@ __device__ __forceinline__ float fast_silu(float x) { return __fdividef(x, 1.0f 
 // 16-byte chunk index is XORed with the row's low three bits, which keeps both the row
 // writes and the transposed reads free of bank conflicts.
 constexpr int STAGE_ROW_BYTES = 128;
-constexpr int STAGE_WARP_BYTES = 32 * STAGE_ROW_BYTES;
 
 __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t (&w)[32]) {
 #pragma unroll
