@@ -246,6 +246,29 @@ def test_shards_bitwise_equal_to_one_gpu():
         assert np.array_equal(np.concatenate(parts).view(np.uint32), whole.view(np.uint32)), world
 
 
+def test_result_buffers_are_never_shared():
+    """Forecast results come from a pool of page-locked buffers recycled by
+    timestral_capi_free_buffer: a result the caller still holds is never handed out again,
+    and recycled buffers give the same forecasts."""
+    import gc
+    m, _ = models(sy.spec_small(), "f16")
+    xa = random_context(3, 1, 256, seed=71)
+    xb = random_context(3, 1, 256, seed=72)
+    first = m.forecast(xa, 64)
+    keep = first.copy()
+    for i in range(6):                       # other results come and go meanwhile
+        other = m.forecast(xb if i % 2 else xa, 64)
+        del other
+        gc.collect()
+        assert np.array_equal(first.view(np.uint32), keep.view(np.uint32))
+    again = m.forecast(xa, 64)
+    assert np.array_equal(again.view(np.uint32), keep.view(np.uint32))
+    held = [m.forecast(xb, 64) for _ in range(4)]
+    assert len({h.__array_interface__["data"][0] for h in held} | {first.__array_interface__["data"][0]}) == 5
+    for h in held[1:]:
+        assert np.array_equal(h.view(np.uint32), held[0].view(np.uint32))
+
+
 def test_errors_surface_through_the_abi():
     m, _ = models(sy.spec_tiny(), "f32")
     x = random_context(1, 1, 40, seed=1)

@@ -11,6 +11,7 @@
 #include "gguf.hpp"
 #include "model.hpp"
 
+#include <algorithm>
 #include <climits>
 #include <cmath>
 #include <cstdlib>
@@ -18,7 +19,9 @@
 #include <limits>
 #include <memory>
 #include <new>
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include <cuda_runtime.h>
 
@@ -128,6 +131,86 @@ TIMESTRAL_API double timestral_capi_quantile_level(timestral_ctx* c, int i) {
     }
 }
 
+namespace {
+// Result buffers of timestral_capi_forecast. The reference's contract is that the caller
+// frees them only with timestral_capi_free_buffer (include/timestral_capi.h:42-44), so they
+// come from page-locked host memory recycled through a small pool: the device writes the
+// forecast straight into the caller's buffer, with no staging copy and no first-touch page
+// faults. A 64-byte header before the data records how the block was obtained.
+struct OutHeader {
+    uint64_t magic;
+    uint64_t capacity;     // data bytes
+    uint32_t pinned;
+    uint32_t pad;
+    uint64_t reserved[5];
+};
+static_assert(sizeof(OutHeader) == 64, "header keeps the data 64-byte aligned");
+constexpr uint64_t kOutMagic = 0x74736230'6f757462ull;
+constexpr size_t kPoolMaxBuffers = 16;
+constexpr size_t kPoolMaxBytes = size_t(4) << 30;
+
+std::mutex& pool_mutex() { static std::mutex m; return m; }
+std::vector<OutHeader*>& pool() { static auto* v = new std::vector<OutHeader*>(); return *v; }   // never destroyed
+size_t pool_bytes = 0;
+
+float* out_alloc(size_t bytes, bool* pinned) {
+    {
+        std::lock_guard<std::mutex> lock(pool_mutex());
+        auto& v = pool();
+        size_t best = v.size();
+        for (size_t i = 0; i < v.size(); ++i)
+            if (v[i]->capacity >= bytes && v[i]->capacity <= 2 * bytes + (size_t(1) << 20) &&
+                (best == v.size() || v[i]->capacity < v[best]->capacity))
+                best = i;
+        if (best < v.size()) {
+            OutHeader* h = v[best];
+            v.erase(v.begin() + std::ptrdiff_t(best));
+            pool_bytes -= h->capacity;
+            *pinned = true;
+            return reinterpret_cast<float*>(h + 1);
+        }
+    }
+    void* p = nullptr;
+    OutHeader* h = nullptr;
+    if (cudaHostAlloc(&p, bytes + sizeof(OutHeader), cudaHostAllocPortable) == cudaSuccess) {
+        h = static_cast<OutHeader*>(p);
+        h->pinned = 1;
+    } else {
+        cudaGetLastError();
+        p = std::malloc(bytes + sizeof(OutHeader));
+        if (!p) throw std::bad_alloc();
+        h = static_cast<OutHeader*>(p);
+        h->pinned = 0;
+    }
+    h->magic = kOutMagic;
+    h->capacity = bytes;
+    *pinned = h->pinned != 0;
+    return reinterpret_cast<float*>(h + 1);
+}
+
+void out_free(void* data) {
+    if (!data) return;
+    OutHeader* h = reinterpret_cast<OutHeader*>(data) - 1;
+    if (h->magic != kOutMagic) return;      // not a buffer of this library: leave it alone
+    if (!h->pinned) {
+        h->magic = 0;
+        std::free(h);
+        return;
+    }
+    {
+        std::lock_guard<std::mutex> lock(pool_mutex());
+        auto& v = pool();
+        if (v.size() < kPoolMaxBuffers && pool_bytes + h->capacity <= kPoolMaxBytes) {
+            v.push_back(h);
+            pool_bytes += h->capacity;
+            return;
+        }
+    }
+    h->magic = 0;
+    cudaFreeHost(h);
+}
+}  // namespace
+
 TIMESTRAL_API float* timestral_capi_forecast(timestral_ctx* c, const timestral_forecast_request* a, int32_t* out_q) {
     if (out_q) *out_q = 0;
     float* result = nullptr;
@@ -165,15 +248,15 @@ TIMESTRAL_API float* timestral_capi_forecast(timestral_ctx* c, const timestral_f
             for (size_t i = 0; i < nx; ++i) require(a->observation_mask[i] <= 1, "observation mask must be boolean");
         const bool sym = a->symmetric_averaging == -1 ? cfg.symmetric_averaging : a->symmetric_averaging != 0;
         const bool clip = a->clip_nonnegative == -1 ? cfg.clip_nonnegative : a->clip_nonnegative != 0;
-        result = static_cast<float*>(std::malloc(no * sizeof(float)));
-        if (!result) throw std::bad_alloc();
+        bool pinned = false;
+        result = out_alloc(no * sizeof(float), &pinned);
         if (!any) {
             if (sym)
                 for (size_t i = 0; i < Q; ++i)
                     if (std::abs(cfg.quantile_knots[i] + cfg.quantile_knots[Q - 1 - i] - 1) >= 1e-9)
                         throw ts::Error("symmetric averaging needs quantile levels symmetric about 0.5");
             c->forecaster.forecast_targets(a->context, a->observation_mask, B, V, T, H, sym, clip, size_t(a->max_context),
-                                           result);
+                                           result, pinned);
         } else {
             ts::ForecastRequest r;
             r.batch = B; r.targets = V; r.length = T; r.horizon = H; r.max_context = size_t(a->max_context);
@@ -193,13 +276,13 @@ TIMESTRAL_API float* timestral_capi_forecast(timestral_ctx* c, const timestral_f
         c->error.clear();
         return result;
     } catch (...) {
-        std::free(result);
+        out_free(result);
         caught(c);
         return nullptr;
     }
 }
 
-TIMESTRAL_API void timestral_capi_free_buffer(void* p) { std::free(p); }
+TIMESTRAL_API void timestral_capi_free_buffer(void* p) { out_free(p); }
 
 }  // extern "C"
 

@@ -334,7 +334,7 @@ Forecaster::~Forecaster() {
 }
 
 void Forecaster::forecast_targets(const float* context, const uint8_t* mask, size_t B, size_t V, size_t T, size_t H,
-                                  bool sym, bool clip, size_t max_context, float* out) {
+                                  bool sym, bool clip, size_t max_context, float* out, bool out_pinned) {
     const Config& c = model_.config();
     const size_t Q = c.num_quantiles();
     const size_t cap = max_context ? max_context : c.context_length;
@@ -354,10 +354,15 @@ void Forecaster::forecast_targets(const float* context, const uint8_t* mask, siz
     try {
         eng.forecast_targets(static_cast<float*>(st.ctx), mask ? static_cast<uint8_t*>(st.mask) : nullptr, int(B), int(V),
                              int(T), int(H), sym, clip, int(max_context), static_cast<float*>(st.out), false);
-        Staging::grow_host(st.host_out, st.host_out_bytes, no * 4);
-        cuda_check(cudaMemcpyAsync(st.host_out, st.out, no * 4, cudaMemcpyDeviceToHost, s), "download forecast");
-        eng.check_errors();
-        copy_out(out, static_cast<const float*>(st.host_out), no);
+        if (out_pinned) {
+            cuda_check(cudaMemcpyAsync(out, st.out, no * 4, cudaMemcpyDeviceToHost, s), "download forecast");
+            eng.check_errors();
+        } else {
+            Staging::grow_host(st.host_out, st.host_out_bytes, no * 4);
+            cuda_check(cudaMemcpyAsync(st.host_out, st.out, no * 4, cudaMemcpyDeviceToHost, s), "download forecast");
+            eng.check_errors();
+            copy_out(out, static_cast<const float*>(st.host_out), no);
+        }
     } catch (const Error&) {
         throw;
     } catch (const std::exception& e) {

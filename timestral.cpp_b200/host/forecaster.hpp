@@ -60,8 +60,10 @@ public:
     void forecast_into(const ForecastRequest& r, float* out);
     // Requests without covariates from caller host buffers: context [B,V,T] (NaN = missing),
     // mask [B,V,T] bytes 0/1 or null; out [B,V,H,Q]. Flags already resolved.
+    // out_pinned: `out` is page-locked host memory, so the forecast is downloaded into it
+    // directly instead of through the staging buffer.
     void forecast_targets(const float* context, const uint8_t* mask, size_t B, size_t V, size_t T, size_t H,
-                          bool symmetric, bool clip, size_t max_context, float* out);
+                          bool symmetric, bool clip, size_t max_context, float* out, bool out_pinned = false);
 
     tsb::Engine& engine() { return *engine_; }
     // Covariate requests are assembled on the device (default) or, for comparison, on the
