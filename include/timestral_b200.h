@@ -45,6 +45,14 @@ TIMESTRAL_API int tsb_sync(timestral_ctx* ctx);
 TIMESTRAL_API int tsb_set_device(int32_t device);
 /* cudaStream_t of the handle (as an opaque pointer), for callers that time with events. */
 TIMESTRAL_API void* tsb_stream(timestral_ctx* ctx);
+/* CUDA-graph replay (on by default): a forecast without covariates that fits one decode
+ * block (H <= 32 patches of the 209M geometry) is captured into a CUDA graph on its second
+ * call with the same sizes, flags and device buffers (tsb_forecast_device pointers, or the
+ * handle's staging buffers for timestral_capi_forecast), and later identical calls launch
+ * that graph, which removes the per-kernel launch cost. The graph is dropped when any
+ * workspace of the library is reallocated. on = 0 disables it. Replaces nothing in the
+ * reference (its graphs are ggml's per-block graphs, src/backend.cpp GraphRunner). */
+TIMESTRAL_API int tsb_graph_replay(timestral_ctx* ctx, int32_t on);
 /* Covariate requests: assemble the rows on the device (on_device != 0, the default) or on
  * the host (the host path of the reference's assemble_rows, kept for comparison); the two
  * give identical forecasts. Replaces nothing in the reference (its assembly is host-only,

@@ -246,6 +246,40 @@ def test_shards_bitwise_equal_to_one_gpu():
         assert np.array_equal(np.concatenate(parts).view(np.uint32), whole.view(np.uint32)), world
 
 
+def test_graph_replay_equals_plain_launches():
+    """Repeated single-block forecasts are captured into a CUDA graph on their second call and
+    replayed afterwards; every result equals the plain launches' bit for bit, also when new
+    inputs sit in the same device buffers and through the host-buffer C ABI."""
+    torch = pytest.importorskip("torch")
+    m, _ = models(sy.spec_small(), "f16")
+    B, V, T, H = 3, 1, 256, 64
+    Q = m.num_quantiles
+    xs = [random_context(B, V, T, seed=s) for s in (81, 82, 83)]
+    dev = torch.device("cuda", 0)
+    d_ctx = torch.empty((B, V, T), device=dev)
+    d_out = torch.empty((B, V, H, Q), device=dev)
+
+    def device_forecast(x):
+        d_ctx.copy_(torch.from_numpy(x))
+        m.forecast_device(d_ctx.data_ptr(), None, B, V, T, H, d_out.data_ptr())
+        return d_out.cpu().numpy().copy()
+
+    try:
+        m.graph_replay(False)
+        ref = [device_forecast(x) for x in xs]
+        plain_launches = m.last_launch_count()
+        m.graph_replay(True)
+        for i in (0, 0, 1, 2, 0, 1):
+            got = device_forecast(xs[i])
+            assert np.array_equal(got.view(np.uint32), ref[i].view(np.uint32)), i
+            assert m.last_launch_count() == plain_launches
+        for i in (2, 0, 1, 2):
+            got = m.forecast(xs[i], H)
+            assert np.array_equal(got.view(np.uint32), ref[i].view(np.uint32)), i
+    finally:
+        m.graph_replay(True)
+
+
 def test_result_buffers_are_never_shared():
     """Forecast results come from a pool of page-locked buffers recycled by
     timestral_capi_free_buffer: a result the caller still holds is never handed out again,

@@ -14,6 +14,7 @@
 #include "rows.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 #include <cmath>
 #include <cstring>
@@ -37,6 +38,10 @@ uint16_t float_to_half_bits(float f) {
     return reinterpret_cast<__half_raw&>(h).x;
 }
 
+// Counts workspace reallocations in the process: a captured forecast graph holds the
+// workspace addresses of its capture and is replayed only while this count is unchanged.
+std::atomic<uint64_t> g_workspace_generation{0};
+
 struct DevBuf {
     void* p = nullptr;
     size_t bytes = 0;
@@ -46,6 +51,7 @@ struct DevBuf {
     ~DevBuf() { if (p) cudaFree(p); }
     void ensure(size_t n) {
         if (n <= bytes) return;
+        g_workspace_generation.fetch_add(1);
         if (p) { cudaFree(p); p = nullptr; bytes = 0; }
         check(cudaMalloc(&p, std::max<size_t>(n, 256)), "cudaMalloc workspace");
         bytes = std::max<size_t>(n, 256);
@@ -103,6 +109,27 @@ struct Engine::Impl {
     DevBuf cov_ctx, cov_umask, cov_past, cov_known, cov_cpast, cov_cknown, cov_first, cov_scratch;
     // request-sized buffers kept across calls (no allocation on the forecast path once warm)
     DevBuf req_ctx, req_umask, fut_slice, fmask_slice, out_rows;
+    // CUDA-graph replay of single-block forecasts without covariates: the second call with
+    // the same shapes, flags and device buffers is captured, later ones replay the graph.
+    struct GraphKey {
+        const void* ctx = nullptr; const void* umask = nullptr; void* out = nullptr;
+        int B = 0, V = 0, T = 0, H = 0, max_context = 0;
+        bool sym = false, clip = false;
+        bool operator==(const GraphKey& o) const {
+            return ctx == o.ctx && umask == o.umask && out == o.out && B == o.B && V == o.V && T == o.T && H == o.H &&
+                   max_context == o.max_context && sym == o.sym && clip == o.clip;
+        }
+    };
+    bool graphs = true;
+    bool have_last = false;
+    GraphKey last_key, graph_key;
+    cudaGraphExec_t graph_exec = nullptr;
+    uint64_t graph_generation = 0;
+    int64_t graph_launches = 0;
+    void drop_graph() {
+        if (graph_exec) cudaGraphExecDestroy(graph_exec);
+        graph_exec = nullptr;
+    }
     // timing
     bool timing = false;
     std::string timing_only;   // empty: every class
@@ -678,6 +705,7 @@ Engine::Engine(const ModelView& mv, int device) : impl_(new Impl), device_(devic
 Engine::~Engine() {
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    if (impl_) impl_->drop_graph();
     impl_.reset();
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -715,7 +743,7 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
     Impl& im = *impl_;
     im.launches = 0;
     const ModelView& mv = im.mv;
-    const int ps = im.ps, Q = im.Q;
+    const int ps = im.ps;
     if (B <= 0 || V <= 0 || T <= 0 || H <= 0) throw std::runtime_error("invalid forecast dimensions");
     const int cap = max_context ? max_context : mv.context_length;
     if (cap > mv.context_length) throw std::runtime_error("max_context exceeds stored position range");
@@ -723,6 +751,58 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
     const int patches = (H + ps - 1) / ps;
     const int shot = std::min(mv.per_shot ? mv.per_shot : 32, mv.block_size);
     const int R = B * V, R2 = symmetric ? 2 * R : R;
+    const cudaStream_t s = stream_;
+    const bool single = patches <= shot;
+    Impl::GraphKey key;
+    key.ctx = d_ctx; key.umask = d_umask; key.out = d_out;
+    key.B = B; key.V = V; key.T = T; key.H = H; key.max_context = max_context; key.sym = symmetric; key.clip = clip;
+    const bool graphable = im.graphs && single && !im.timing;
+    if (graphable && im.graph_exec && key == im.graph_key && im.graph_generation == g_workspace_generation.load()) {
+        check(cudaGraphLaunch(im.graph_exec, s), "graph launch");
+        im.launches = im.graph_launches;
+        last_launches_ = im.launches;
+        if (sync) im.check_device_error("forecast");
+        return;
+    }
+    const bool capture = graphable && im.have_last && key == im.last_key;
+    im.last_key = key;
+    im.have_last = true;
+    if (capture) {
+        im.drop_graph();
+        check(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+    }
+    try {
+        targets_body(d_ctx, d_umask, B, V, T, H, symmetric, clip, d_out, kept, len, patches, shot, R, R2);
+    } catch (...) {
+        if (capture) {
+            cudaGraph_t g = nullptr;
+            cudaStreamEndCapture(s, &g);
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            im.have_last = false;          // the next identical call runs uncaptured
+        }
+        throw;
+    }
+    if (capture) {
+        cudaGraph_t g = nullptr;
+        check(cudaStreamEndCapture(s, &g), "end capture");
+        const cudaError_t e = cudaGraphInstantiate(&im.graph_exec, g, 0);
+        cudaGraphDestroy(g);
+        check(e, "graph instantiate");
+        im.graph_key = key;
+        im.graph_generation = g_workspace_generation.load();
+        im.graph_launches = im.launches;
+        check(cudaGraphLaunch(im.graph_exec, s), "graph launch");
+    }
+    last_launches_ = im.launches;
+    if (sync) im.check_device_error("forecast");
+}
+
+void Engine::targets_body(const float* d_ctx, const uint8_t* d_umask, int B, int V, int T, int H, bool symmetric,
+                          bool clip, float* d_out, int kept, int len, int patches, int shot, int R, int R2) {
+    Impl& im = *impl_;
+    const ModelView& mv = im.mv;
+    const int ps = im.ps, Q = im.Q;
     const cudaStream_t s = stream_;
     if (clip) {
         im.clip_ok.ensure(size_t(R));
@@ -734,6 +814,7 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
     int Tc = len, done = 0;
     const bool single = patches <= shot;
     if (!single) im.decoded.ensure(size_t(R2) * H * Q * 4);
+    (void)T;
     while (done < patches) {
         const int block = std::min(shot, patches - done), n = block * ps, offset = done * ps;
         // The V target rows of one series form one group (reference src/covariates.cpp:63).
@@ -762,8 +843,11 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
                         im.capsc.as<float>(), mv.cap_k > 0, clip ? im.clip_ok.as<int8_t>() : nullptr, d_out,
                         im.err.as<int>(), s);
     });
-    last_launches_ = im.launches;
-    if (sync) im.check_device_error("forecast");
+}
+
+void Engine::graph_replay(bool on) {
+    impl_->graphs = on;
+    if (!on) { impl_->drop_graph(); impl_->have_last = false; }
 }
 
 void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetric, bool clip, const float* ctx,

@@ -91,6 +91,11 @@ public:
     // Requests with covariates assembled on the device (host buffers in and out).
     void forecast_covariates(const CovRequest& q, bool symmetric, bool clip, float* h_out);
 
+    // CUDA-graph replay of single-block forecasts without covariates (on by default): the
+    // second call with the same shapes, flags and device buffers is captured into a graph,
+    // later identical calls launch the graph.
+    void graph_replay(bool on);
+
     // Synchronise the stream and turn a device error word into an exception.
     void check_errors();
 
@@ -106,6 +111,8 @@ public:
     Geometry last_geometry() const;
 
 private:
+    void targets_body(const float* d_ctx, const uint8_t* d_umask, int B, int V, int T, int H, bool symmetric, bool clip,
+                      float* d_out, int kept, int len, int patches, int shot, int R, int R2);
     // The decode blocks of an assembled covariate request (rows, masks, roles, futures in
     // device memory) through the final download.
     void decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetric, bool clip, bool cov, bool has_future,

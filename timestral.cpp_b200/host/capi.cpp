@@ -356,6 +356,17 @@ TIMESTRAL_API int tsb_timing_enable(timestral_ctx* c, int32_t enable) {
     return TSB_OK;
 }
 
+TIMESTRAL_API int tsb_graph_replay(timestral_ctx* c, int32_t on) {
+    if (!c) return TSB_ERR_ARG;
+    try {
+        c->forecaster.engine().graph_replay(on != 0);
+    } catch (...) {
+        caught(c);
+        return TSB_ERR_CUDA;
+    }
+    return TSB_OK;
+}
+
 TIMESTRAL_API int tsb_covariate_assembly(timestral_ctx* c, int32_t on_device) {
     if (!c) return TSB_ERR_ARG;
     c->forecaster.set_device_assembly(on_device != 0);
