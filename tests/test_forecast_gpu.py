@@ -280,6 +280,24 @@ def test_graph_replay_equals_plain_launches():
         m.graph_replay(True)
 
 
+def test_graph_replay_f32_path():
+    """The F32 CUDA-core path replays its graph too, bit for bit, and a forecast that needs
+    two decode blocks (not captured) still matches plain launches."""
+    m, _ = models(sy.spec_tiny(), "f32")
+    x = random_context(2, 2, 100, seed=91)
+    y = random_context(2, 2, 100, seed=92)
+    try:
+        m.graph_replay(False)
+        rx, ry, rlong = m.forecast(x, 9).copy(), m.forecast(y, 9).copy(), m.forecast(x, 200).copy()
+        m.graph_replay(True)
+        for z, r in ((x, rx), (x, rx), (y, ry), (x, rx), (y, ry)):
+            assert np.array_equal(m.forecast(z, 9).view(np.uint32), r.view(np.uint32))
+        assert np.array_equal(m.forecast(x, 200).view(np.uint32), rlong.view(np.uint32))
+        assert np.array_equal(m.forecast(y, 9).view(np.uint32), ry.view(np.uint32))
+    finally:
+        m.graph_replay(True)
+
+
 def test_result_buffers_are_never_shared():
     """Forecast results come from a pool of page-locked buffers recycled by
     timestral_capi_free_buffer: a result the caller still holds is never handed out again,
