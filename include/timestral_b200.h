@@ -45,6 +45,16 @@ TIMESTRAL_API int tsb_sync(timestral_ctx* ctx);
 TIMESTRAL_API int tsb_set_device(int32_t device);
 /* cudaStream_t of the handle (as an opaque pointer), for callers that time with events. */
 TIMESTRAL_API void* tsb_stream(timestral_ctx* ctx);
+/* RMSNorm carried by the tensor-core GEMMs (mode 1, the default): each residual-add GEMM
+ * also leaves an f16 copy of the residual (scaled by 1/16) and its row sums of squares, and
+ * the next GEMM, whose weights hold the norm weight, scales each row by 1/rms itself, so the
+ * RMSNorm kernel runs once per decode block instead of once per sublayer. A forecast that
+ * meets a residual value the f16 copy cannot hold (|x| > 2^20) or a row whose RMS is below
+ * 2^-8 is run again with the RMSNorm kernel, so results never depend on that range. Mode 0:
+ * always the RMSNorm kernel. Mode 2: mode 1, and every forecast also takes the fallback run
+ * (tests that path). Replaces the reference's per-sublayer rms_f32 node (src/layers.cpp:262-287)
+ * on the tensor-core path. */
+TIMESTRAL_API int tsb_fused_norm(timestral_ctx* ctx, int32_t mode);
 /* CUDA-graph replay (on by default): a forecast without covariates that fits one decode
  * block (H <= 32 patches of the 209M geometry) is captured into a CUDA graph on its second
  * call with the same sizes, flags and device buffers (tsb_forecast_device pointers, or the

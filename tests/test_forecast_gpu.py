@@ -280,6 +280,44 @@ def test_graph_replay_equals_plain_launches():
         m.graph_replay(True)
 
 
+@pytest.mark.parametrize("V", [1, 3])
+def test_fused_norm_and_its_fallback(V):
+    """RMSNorm carried by the GEMMs (default) stays within the F16 bound of the oracle; the
+    fallback run (forced by mode 2) equals the RMSNorm-kernel path (mode 0) bit for bit through
+    the C ABI, an asynchronous device forecast, and a covariate request."""
+    torch = pytest.importorskip("torch")
+    m, o = models(sy.spec_small(True), "f16")
+    B, T, H = 3, 256, 64
+    x = random_context(B, V, T, seed=95 + V)
+    rng = np.random.default_rng(96)
+    kw = dict(past=rng.standard_normal((B, 1, T)).astype(np.float32),
+              known=rng.standard_normal((B, 1, T + H)).astype(np.float32))
+    Q = m.num_quantiles
+    dev = torch.device("cuda", 0)
+    d_ctx = torch.from_numpy(x).to(dev)
+    d_out = torch.empty((B, V, H, Q), device=dev)
+
+    def device_async():
+        m.forecast_device(d_ctx.data_ptr(), None, B, V, T, H, d_out.data_ptr(), asynchronous=True)
+        assert tb.lib().tsb_sync(m.h) == 0
+        return d_out.cpu().numpy().copy()
+
+    try:
+        m.fused_norm(0)
+        plain, plain_dev, plain_cov = m.forecast(x, H).copy(), device_async(), m.forecast(x, H, **kw).copy()
+        m.fused_norm(2)
+        for _ in range(3):                     # the third call replays a captured graph
+            assert np.array_equal(m.forecast(x, H).view(np.uint32), plain.view(np.uint32))
+            assert np.array_equal(device_async().view(np.uint32), plain_dev.view(np.uint32))
+        assert np.array_equal(m.forecast(x, H, **kw).view(np.uint32), plain_cov.view(np.uint32))
+        m.fused_norm(1)
+        fused = m.forecast(x, H)
+        check_nd(fused, o.forecast(x, H), x, 32, F16_MEAN_ND)
+        check_nd(m.forecast(x, H, **kw), o.forecast(x, H, **kw), x, 32, F16_MEAN_ND)
+    finally:
+        m.fused_norm(1)
+
+
 def test_graph_replay_f32_path():
     """The F32 CUDA-core path replays its graph too, bit for bit, and a forecast that needs
     two decode blocks (not captured) still matches plain launches."""

@@ -37,6 +37,11 @@ uint16_t float_to_half_bits(float f) {
     __half h = __float2half_rn(f);
     return reinterpret_cast<__half_raw&>(h).x;
 }
+// W[n][k] *= norm[k] over f16 rows of width K, rounded to f16: the RMSNorm weight folded into
+// the weights of the GEMM that consumes the normalised rows (tensor-core path).
+void fold_norm(std::vector<uint16_t>& W, size_t K, const float* norm) {
+    for (size_t i = 0; i < W.size(); ++i) W[i] = float_to_half_bits(half_bits_to_float(W[i]) * norm[i % K]);
+}
 
 // Counts workspace reallocations in the process: a captured forecast graph holds the
 // workspace addresses of its capture and is replayed only while this count is unchanged.
@@ -105,6 +110,25 @@ struct Engine::Impl {
     DevBuf rows, mask, win, wmask, role, future, fmask, feat, aloc, ascale, caplo, caphi, capsc, first_obs, kv, rope_row,
         gbeg, gsize, clip_ok, x, xn, qb, kb, vb, gb, att, hb, zb, fused, gtmp, ph, dec, hh, hraw, qout, refined, scratch,
         decoded, err, next_rows, next_mask, feat16, pflag, panel_scratch;
+    // RMSNorm carried by the GEMMs (tensor-core path): x16 = f16(x / 16) and per-row sums of
+    // squares per 128-column slot, written by the residual-add epilogues; unit norm weights for
+    // the sublayers that normalise with the RMSNorm kernel (the norm weights are folded into
+    // the consuming weights); a flag that sends a forecast back through the unfused path.
+    DevBuf x16, ssq, nflag, ones;
+    struct Pending {            // the last forecast without covariates, for its fallback run
+        bool valid = false;
+        const void* ctx = nullptr; const void* umask = nullptr;
+        int B = 0, V = 0, T = 0, H = 0;
+        bool sym = false, clip = false;
+        void* out = nullptr;
+        int kept = 0, len = 0, patches = 0, shot = 0, R = 0, R2 = 0;
+    } pending;
+    bool fuse = true;            // allowed
+    bool fuse_now = true;        // used by the running forecast
+    bool force_fallback = false; // test hook: treat every fused forecast as flagged
+    const __half* a_in = nullptr;
+    const float* ssq_in = nullptr;
+    bool produce16 = false;
     // raw covariate request inputs and assembly scratch
     DevBuf cov_ctx, cov_umask, cov_past, cov_known, cov_cpast, cov_cknown, cov_first, cov_scratch;
     // request-sized buffers kept across calls (no allocation on the forecast path once warm)
@@ -309,9 +333,11 @@ struct Engine::Impl {
                 if (mv.has(p + "qkv.bias")) { auto w = t(p + "qkv.bias"); bq.assign(static_cast<const float*>(w.data), static_cast<const float*>(w.data) + 3 * D); }
                 if (a.gate && mv.has(p + "gate.bias")) { auto w = t(p + "gate.bias"); bg.assign(static_cast<const float*>(w.data), static_cast<const float*>(w.data) + D); }
                 if (tc) {
+                    const float* nw = static_cast<const float*>(t(b + "attn_norm." + std::to_string(j) + ".weight").data);
                     auto q = rows_f16(t(p + "qkv.weight"));
+                    fold_norm(q, size_t(D), nw);
                     std::vector<uint16_t> g;
-                    if (a.gate) g = rows_f16(t(p + "gate.weight"));
+                    if (a.gate) { g = rows_f16(t(p + "gate.weight")); fold_norm(g, size_t(D), nw); }
                     std::vector<uint16_t> cat(q);
                     cat.insert(cat.end(), g.begin(), g.end());
                     a.qkvg = reinterpret_cast<__half*>(upload(cat.data(), cat.size()));
@@ -354,6 +380,7 @@ struct Engine::Impl {
             w.fb3 = w.b3;
             if (tc) {
                 auto z = rows_f16(t(b + "ffn_w12.weight"));
+                fold_norm(z, size_t(D), static_cast<const float*>(t(b + "ffn_norm.weight").data));
                 auto zi = interleave(z.data(), z.data() + size_t(F) * D, size_t(F), size_t(D));
                 w.w12 = reinterpret_cast<__half*>(upload(zi.data(), zi.size()));
                 if (mv.has(b + "ffn_w12.bias")) {
@@ -384,6 +411,36 @@ struct Engine::Impl {
         }
         err.ensure(sizeof(int));
         check(cudaMemset(err.p, 0, sizeof(int)), "memset");
+        nflag.ensure(sizeof(int));
+        check(cudaMemset(nflag.p, 0, sizeof(int)), "memset");
+        if (tc) {
+            std::vector<float> one(size_t(D), 1.0f);
+            ones.ensure(size_t(D) * 4);
+            check(cudaMemcpy(ones.p, one.data(), size_t(D) * 4, cudaMemcpyHostToDevice), "upload");
+        }
+    }
+
+    bool fuse_allowed() const { return fuse && tc && D % 128 == 0; }
+    // Reads and clears the flag of the forecast just run (synchronises the stream).
+    bool take_norm_flag() {
+        const int h = read_error(nflag.as<int>(), s);
+        return h != 0 || force_fallback;
+    }
+    // The normalised input of the next consuming GEMM: x16 and the row sums of squares left by
+    // the last residual-add epilogue, or the RMSNorm kernel (unit weights) into xn.
+    void norm_input(bool have16, int64_t M) {
+        if (fuse_now && have16) { a_in = x16.as<__half>(); ssq_in = ssq.as<float>(); return; }
+        run("rms", [&] { return rms_norm(x.as<float>(), ones.as<float>(), int(M), D, mv.eps, xn.p, 1, 0, 0, 0, s); });
+        a_in = xn.as<__half>();
+        ssq_in = nullptr;
+    }
+    void consume(GemmEpilogue& e) const {
+        e.ssq_in = ssq_in; e.ssq_slots = D / 128; e.rms_D = D; e.rms_eps = mv.eps; e.norm_flag = nflag.as<int>();
+    }
+    void produce(GemmEpilogue& e) const {
+        if (!produce16) return;
+        e.x16 = x16.as<__half>(); e.ldx16 = D; e.ssq = ssq.as<float>(); e.ssq_slots = D / 128;
+        e.norm_flag = nflag.as<int>();
     }
 
     ~Impl() {
@@ -525,24 +582,37 @@ struct Engine::Impl {
         hb.ensure(size_t(M) * F * eb);
         if (!tc) { fused.ensure(size_t(M) * 3 * D * 4); gtmp.ensure(size_t(M) * D * 4); zb.ensure(size_t(M) * 2 * F * 4); }
 
+        if (tc && fuse_now) { x16.ensure(size_t(M) * D * 2); ssq.ensure(size_t(M) * (D / 128) * 4); }
+        bool have16 = false;   // x16 and ssq hold the current x
         for (size_t li = 0; li < attn.size(); ++li) {
             for (const AttnW& a : attn[li]) {
-                run("rms", [&] { return rms_norm(x.as<float>(), a.norm, int(M), D, mv.eps, xn.p, tc, 0, 0, 0, s); });
-                if (tc) attention_sublayer_tc(a, int(M), R2, S, group_rows, mm);
-                else attention_sublayer_simt(a, int(M), R2, S, mm);
+                if (tc) {
+                    norm_input(have16, M);
+                    produce16 = fuse_now;
+                    attention_sublayer_tc(a, int(M), R2, S, group_rows, mm);
+                    have16 = fuse_now;
+                } else {
+                    run("rms", [&] { return rms_norm(x.as<float>(), a.norm, int(M), D, mv.eps, xn.p, 0, 0, 0, 0, s); });
+                    attention_sublayer_simt(a, int(M), R2, S, mm);
+                }
             }
             const MlpW& w = mlp[li];
-            run("rms", [&] { return rms_norm(x.as<float>(), w.norm, int(M), D, mv.eps, xn.p, tc, 0, 0, 0, s); });
             if (tc) {
+                norm_input(have16, M);
+                produce16 = fuse_now;
                 GemmArgs a;
-                a.A = xn.as<__half>(); a.lda = D; a.B = w.w12; a.ldb = D; a.M = int(M); a.N = 2 * F; a.K = D;
+                a.A = a_in; a.lda = D; a.B = w.w12; a.ldb = D; a.M = int(M); a.N = 2 * F; a.K = D;
                 a.epi.out = hb.p; a.epi.ldo = F; a.epi.bias = w.b12;
+                consume(a.epi);
                 gemm(EPI_SWIGLU, a);
                 GemmArgs o;
                 o.A = hb.as<__half>(); o.lda = F; o.B = w.w3; o.ldb = F; o.M = int(M); o.N = D; o.K = F;
                 o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = w.b3; o.epi.resid = x.as<float>();
+                produce(o.epi);
                 gemm(EPI_RESID, o);
+                have16 = fuse_now;
             } else {
+                run("rms", [&] { return rms_norm(x.as<float>(), w.norm, int(M), D, mv.eps, xn.p, 0, 0, 0, 0, s); });
                 SimtGemm g;
                 g.A = xn.as<float>(); g.lda = D; g.W = w.f12; g.M = int(M); g.N = 2 * F; g.K = D;
                 g.order = round_a ? ORDER_CHAIN : ORDER_PANEL192; g.round_a_f16 = round_a; g.epi = SEPI_F32;
@@ -619,7 +689,8 @@ struct Engine::Impl {
             // (reference tests/layer_kind_test.hpp:31-33), so the sublayer is
             // out(v * sigmoid(gate)) and only the v and gate projections are computed.
             GemmArgs g;
-            g.A = xn.as<__half>(); g.lda = D; g.M = M; g.K = D; g.epi.out = att16; g.epi.ldo = D;
+            g.A = a_in; g.lda = D; g.M = M; g.K = D; g.epi.out = att16; g.epi.ldo = D;
+            consume(g.epi);
             if (a.gate) { g.B = a.vg; g.ldb = D; g.N = 2 * D; g.epi.bias = a.b_vg; gemm(EPI_VGATE, g); }
             else {
                 g.B = a.qkvg + size_t(2) * D * D; g.ldb = D; g.N = D;
@@ -628,8 +699,9 @@ struct Engine::Impl {
             }
         } else {
             GemmArgs g;
-            g.A = xn.as<__half>(); g.lda = D; g.B = a.qkvg; g.ldb = D; g.M = M; g.N = a.n_qkvg; g.K = D;
+            g.A = a_in; g.lda = D; g.B = a.qkvg; g.ldb = D; g.M = M; g.N = a.n_qkvg; g.K = D;
             g.epi.bias = a.b_qkvg;
+            consume(g.epi);
             g.epi.qkvg[0] = qb.as<__half>(); g.epi.qkvg[1] = kb.as<__half>(); g.epi.qkvg[2] = vb.as<__half>();
             g.epi.qkvg[3] = gb.as<__half>();
             g.epi.S = S; g.epi.H = H; g.epi.D = D; g.epi.rope = a.time;
@@ -652,6 +724,7 @@ struct Engine::Impl {
         GemmArgs o;
         o.A = att16; o.lda = D; o.B = a.out; o.ldb = D; o.M = M; o.N = D; o.K = D;
         o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = a.b_out; o.epi.resid = x.as<float>();
+        produce(o.epi);
         gemm(EPI_RESID, o);
     }
 
@@ -713,7 +786,7 @@ Engine::~Engine() {
 void Engine::check_errors() {
     check(cudaSetDevice(device_), "cudaSetDevice");
     check(cudaStreamSynchronize(stream_), "forecast");
-    impl_->check_device_error("forecast");
+    finish_targets();
 }
 
 void Engine::timing_enable(bool on, const char* only) {
@@ -757,11 +830,13 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
     key.ctx = d_ctx; key.umask = d_umask; key.out = d_out;
     key.B = B; key.V = V; key.T = T; key.H = H; key.max_context = max_context; key.sym = symmetric; key.clip = clip;
     const bool graphable = im.graphs && single && !im.timing;
+    im.fuse_now = im.fuse_allowed();
+    im.pending = Impl::Pending{true, d_ctx, d_umask, B, V, T, H, symmetric, clip, d_out, kept, len, patches, shot, R, R2};
     if (graphable && im.graph_exec && key == im.graph_key && im.graph_generation == g_workspace_generation.load()) {
         check(cudaGraphLaunch(im.graph_exec, s), "graph launch");
         im.launches = im.graph_launches;
         last_launches_ = im.launches;
-        if (sync) im.check_device_error("forecast");
+        if (sync) finish_targets();
         return;
     }
     const bool capture = graphable && im.have_last && key == im.last_key;
@@ -795,7 +870,29 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
         check(cudaGraphLaunch(im.graph_exec, s), "graph launch");
     }
     last_launches_ = im.launches;
-    if (sync) im.check_device_error("forecast");
+    if (sync) finish_targets();
+}
+
+// Errors of the last forecast without covariates; when the norm carried by the GEMMs flagged a
+// row (an f16 overflow of the residual copy, or a row too small for it), the forecast is run
+// again with the RMSNorm kernel, into the same output.
+void Engine::finish_targets() {
+    Impl& im = *impl_;
+    im.check_device_error("forecast");
+    if (!im.pending.valid || !im.fuse_now) return;
+    im.pending.valid = false;
+    if (!im.take_norm_flag()) return;
+    const Impl::Pending p = im.pending;
+    im.fuse_now = false;
+    try {
+        targets_body(static_cast<const float*>(p.ctx), static_cast<const uint8_t*>(p.umask), p.B, p.V, p.T, p.H, p.sym,
+                     p.clip, static_cast<float*>(p.out), p.kept, p.len, p.patches, p.shot, p.R, p.R2);
+    } catch (...) {
+        im.fuse_now = true;
+        throw;
+    }
+    im.fuse_now = true;
+    im.check_device_error("forecast");
 }
 
 void Engine::targets_body(const float* d_ctx, const uint8_t* d_umask, int B, int V, int T, int H, bool symmetric,
@@ -845,6 +942,13 @@ void Engine::targets_body(const float* d_ctx, const uint8_t* d_umask, int B, int
     });
 }
 
+void Engine::fused_norm(int mode) {
+    impl_->fuse = mode != 0;
+    impl_->force_fallback = mode == 2;
+    impl_->drop_graph();
+    impl_->have_last = false;
+}
+
 void Engine::graph_replay(bool on) {
     impl_->graphs = on;
     if (!on) { impl_->drop_graph(); impl_->have_last = false; }
@@ -855,6 +959,8 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
     check(cudaSetDevice(device_), "cudaSetDevice");
     Impl& im = *impl_;
     im.launches = 0;
+    im.pending.valid = false;
+    im.fuse_now = im.fuse_allowed();
     const ModelView& mv = im.mv;
     const int R = a.R, T = a.T, R2 = symmetric ? 2 * R : R;
     const bool cov = a.roles != nullptr && mv.covariate_enabled;
@@ -902,12 +1008,20 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
         check(cudaStreamSynchronize(s), "sync");
     }
     decode_rows(B, V, H, R, T, Hh, symmetric, clip, cov, a.future != nullptr, a.group_rows, h_out);
+    if (im.fuse_now && im.take_norm_flag()) {
+        const bool saved = im.fuse;
+        im.fuse = false;
+        try { forecast_rows(a, B, V, H, symmetric, clip, ctx, umask, T_req, h_out); } catch (...) { im.fuse = saved; throw; }
+        im.fuse = saved;
+    }
 }
 
 void Engine::forecast_covariates(const CovRequest& q, bool symmetric, bool clip, float* h_out) {
     check(cudaSetDevice(device_), "cudaSetDevice");
     Impl& im = *impl_;
     im.launches = 0;
+    im.pending.valid = false;
+    im.fuse_now = im.fuse_allowed();
     const ModelView& mv = im.mv;
     const int all = q.V + q.P + q.CP + q.K + q.CK;
     const int64_t R64 = int64_t(q.B) * all;
@@ -957,6 +1071,12 @@ void Engine::forecast_covariates(const CovRequest& q, bool symmetric, bool clip,
         });
     }
     decode_rows(q.B, q.V, q.H, R, q.len, q.hor, symmetric, clip, cov, has_future, all, h_out);
+    if (im.fuse_now && im.take_norm_flag()) {      // fallback: the whole request with RMSNorm kernels
+        const bool saved = im.fuse;
+        im.fuse = false;
+        try { forecast_covariates(q, symmetric, clip, h_out); } catch (...) { im.fuse = saved; throw; }
+        im.fuse = saved;
+    }
 }
 
 void Engine::decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetric, bool clip, bool cov,

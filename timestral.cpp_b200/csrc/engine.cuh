@@ -95,6 +95,12 @@ public:
     // second call with the same shapes, flags and device buffers is captured into a graph,
     // later identical calls launch the graph.
     void graph_replay(bool on);
+    // RMSNorm carried by the tensor-core GEMMs (default, mode 1): the residual-add epilogues
+    // leave an f16 copy of the residual and its row sums of squares for the next GEMM, which
+    // applies 1/rms itself; a forecast that meets a row outside the f16 copy's range runs
+    // again with the RMSNorm kernel. Mode 0: always the RMSNorm kernel. Mode 2: carried, and
+    // every forecast also takes the fallback run (a test of that path).
+    void fused_norm(int mode);
 
     // Synchronise the stream and turn a device error word into an exception.
     void check_errors();
@@ -111,6 +117,7 @@ public:
     Geometry last_geometry() const;
 
 private:
+    void finish_targets();
     void targets_body(const float* d_ctx, const uint8_t* d_umask, int B, int V, int T, int H, bool symmetric, bool clip,
                       float* d_out, int kept, int len, int patches, int shot, int R, int R2);
     // The decode blocks of an assembled covariate request (rows, masks, roles, futures in

@@ -89,6 +89,19 @@ __device__ __forceinline__ int64_t out_row(const GemmEpilogue& e, int m) {
 __device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float fast_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+// 1/rms of accumulator row m when the A operand is x / 16 and the norm is carried by the
+// GEMM (see GemmEpilogue::ssq_in); 1 otherwise. The slot sums are added in slot order.
+__device__ __forceinline__ float row_scale(const GemmEpilogue& e, int m, bool row_ok) {
+    if (!e.ssq_in || !row_ok) return 1.0f;
+    const float* p = e.ssq_in + int64_t(m) * e.ssq_slots;
+    float sum = 0.f;
+    for (int j = 0; j < e.ssq_slots; ++j) sum = __fadd_rn(sum, p[j]);
+    const float mean = __fdiv_rn(sum, float(e.rms_D));
+    const float rms = __fsqrt_rn(__fadd_rn(mean, e.rms_eps));
+    if (!(rms >= 0.00390625f) && e.norm_flag) atomicOr(e.norm_flag, 1);
+    return __fdiv_rn(16.0f, rms);
+}
+
 // Per-warp staging block of the epilogue: 32 accumulator rows x 128 bytes. A thread writes
 // its own row (the TMEM lane it read) and the warp then reads the block back so that eight
 // threads cover one 128-byte row, four rows per instruction: every global load and store of
@@ -152,6 +165,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
                 if (rok[i] && col < g.N) dst[i] = *reinterpret_cast<const float4*>(e.resid + int64_t(orow[i]) * e.ldo + col);
         };
         if constexpr (KIND == EPI_RESID && RB == 2) load_resid(0, rs[0]);
+        float sq[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sq[i] = 0.f;
+        bool over = false;
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             if constexpr (KIND == EPI_RESID) {
@@ -175,13 +192,44 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
                     if (e.bias) v = add4(v, b);
                     if constexpr (KIND == EPI_RESID) v = add4(rs[c % RB][i], v);
                     *reinterpret_cast<float4*>(static_cast<float*>(e.out) + int64_t(orow[i]) * e.ldo + col) = v;
+                    if constexpr (KIND == EPI_RESID) {
+                        if (e.x16) {
+                            sq[i] = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, fmaf(v.x, v.x, sq[i]))));
+                            uint2 h;
+                            h.x = pack_half2(v.x * 0.0625f, v.y * 0.0625f);
+                            h.y = pack_half2(v.z * 0.0625f, v.w * 0.0625f);
+                            *reinterpret_cast<uint2*>(e.x16 + int64_t(orow[i]) * e.ldx16 + col) = h;
+                        }
+                    }
                 }
             }
             __syncwarp();
         }
+        if constexpr (KIND == EPI_RESID) {
+            if (e.x16) {
+                // Each row's eight column quads are held by the eight lanes sharing lane / 8.
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+#pragma unroll
+                    for (int o = 1; o < 8; o <<= 1) sq[i] = __fadd_rn(sq[i], __shfl_xor_sync(0xffffffffu, sq[i], o));
+                }
+                const int slot = (n0 + half * C * 32) / 128;
+                // Every |x| <= 2^20 (x / 16 fits f16) whenever a slot's sum of squares is at most
+                // 2^40; a larger sum (rarely a false alarm) sends the forecast to the fallback.
+#pragma unroll
+                for (int i = 0; i < 8; ++i) over |= !(sq[i] <= 1099511627776.0f);
+                if ((lane & 7) == 0) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        if (rok[i]) e.ssq[int64_t(orow[i]) * e.ssq_slots + slot] = sq[i];
+                }
+                if (__any_sync(0xffffffffu, over && (lane & 7) == 0) && lane == 0 && e.norm_flag) atomicOr(e.norm_flag, 1);
+            }
+        }
     } else if constexpr (KIND == EPI_F16 || KIND == EPI_SILU) {
         // 64 columns (two TMEM reads) per staging pass; the thread stores 8 f16 columns.
         constexpr int C = BN / PARTS / 64;
+        const float rsc = row_scale(e, mw + lane, mw + lane < g.M);
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             const int cb = n0 + (half * C + c) * 64;
@@ -194,6 +242,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(w[i]);
+            if (e.ssq_in) {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) v[i] = __fmul_rn(v[i], rsc);
+            }
             if (e.bias) {
 #pragma unroll
                 for (int i = 0; i < 64; ++i)
@@ -219,6 +271,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
         // The first half of the tile holds the first operand, the second half the second:
         // each 32-column pair gives 32 outputs (64 bytes of a staging row); a group holds C pairs.
         constexpr int C = BN / 2 / PARTS / 32;
+        const float rsc = row_scale(e, mw + lane, mw + lane < g.M);
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             const int cc = half * C + c;
@@ -231,6 +284,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 float a = __uint_as_float(w[i]), b = __uint_as_float(y[i]);
+                if (e.ssq_in) { a = __fmul_rn(a, rsc); b = __fmul_rn(b, rsc); }
                 if (e.bias) { a = __fadd_rn(a, e.bias[wn + i]); b = __fadd_rn(b, e.bias[wn + BN / 2 + i]); }
                 o[i] = KIND == EPI_SWIGLU ? __fmul_rn(a, fast_silu(b)) : __fmul_rn(a, fast_sigmoid(b));
             }
@@ -267,6 +321,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
         constexpr int C = BN / 128;
         const int m = mw + lane;                      // the TMEM row of this thread
         const bool row_ok = m < g.M;
+        const float rsc = row_scale(e, m, row_ok);
         // Head-major row (row * H * S + token) of the rows stored after the transpose.
         int hm[8];
 #pragma unroll
@@ -301,6 +356,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(w[i]);
             if (col >= g.N) continue;                 // uniform across the warp
+            if (e.ssq_in) {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) v[i] = __fmul_rn(v[i], rsc);
+            }
             if (e.bias) {
 #pragma unroll
                 for (int i = 0; i < 64; ++i) v[i] = __fadd_rn(v[i], e.bias[col + i]);

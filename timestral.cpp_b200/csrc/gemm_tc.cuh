@@ -35,6 +35,22 @@ struct GemmEpilogue {
     const int* rope_row = nullptr;    // [M] table row of each token
     int rope_half = 32;               // rotated dims per half head (rope_dim / 2)
     int rope_dup = 0;                 // tables satisfy cos[p][d] == cos[p][d + 32] (same for sin)
+    // RMSNorm carried by the GEMMs (the norm weight folded into the consuming weights).
+    // EPI_RESID: also write x16 = f16(x / 16) and, per row, the sum of squares of x over
+    // each 128-column slot into ssq[m * ssq_slots + slot]; a value of x16 that would
+    // overflow sets *norm_flag.
+    __half* x16 = nullptr;
+    int64_t ldx16 = 0;
+    float* ssq = nullptr;
+    int ssq_slots = 0;
+    int* norm_flag = nullptr;
+    // Consumers (EPI_F16, EPI_SWIGLU, EPI_VGATE, EPI_QKVG): with ssq_in set, the accumulator
+    // of row m (A = x16) is scaled by 16 / sqrt(sum_j ssq_in[m * ssq_slots + j] / rms_D + rms_eps)
+    // before the bias; a row whose RMS is below 2^-8 (where x / 16 loses precision in f16)
+    // sets *norm_flag.
+    const float* ssq_in = nullptr;
+    int rms_D = 0;
+    float rms_eps = 0.f;
 };
 
 struct GemmArgs {

@@ -356,6 +356,17 @@ TIMESTRAL_API int tsb_timing_enable(timestral_ctx* c, int32_t enable) {
     return TSB_OK;
 }
 
+TIMESTRAL_API int tsb_fused_norm(timestral_ctx* c, int32_t mode) {
+    if (!c || mode < 0 || mode > 2) return TSB_ERR_ARG;
+    try {
+        c->forecaster.engine().fused_norm(mode);
+    } catch (...) {
+        caught(c);
+        return TSB_ERR_CUDA;
+    }
+    return TSB_OK;
+}
+
 TIMESTRAL_API int tsb_graph_replay(timestral_ctx* c, int32_t on) {
     if (!c) return TSB_ERR_ARG;
     try {

@@ -354,13 +354,16 @@ void Forecaster::forecast_targets(const float* context, const uint8_t* mask, siz
     try {
         eng.forecast_targets(static_cast<float*>(st.ctx), mask ? static_cast<uint8_t*>(st.mask) : nullptr, int(B), int(V),
                              int(T), int(H), sym, clip, int(max_context), static_cast<float*>(st.out), false);
+        // Completes the forecast (including a fallback run, which rewrites st.out) before the
+        // download.
+        eng.check_errors();
         if (out_pinned) {
             cuda_check(cudaMemcpyAsync(out, st.out, no * 4, cudaMemcpyDeviceToHost, s), "download forecast");
-            eng.check_errors();
+            cuda_check(cudaStreamSynchronize(s), "download forecast");
         } else {
             Staging::grow_host(st.host_out, st.host_out_bytes, no * 4);
             cuda_check(cudaMemcpyAsync(st.host_out, st.out, no * 4, cudaMemcpyDeviceToHost, s), "download forecast");
-            eng.check_errors();
+            cuda_check(cudaStreamSynchronize(s), "download forecast");
             copy_out(out, static_cast<const float*>(st.host_out), no);
         }
     } catch (const Error&) {

@@ -65,6 +65,7 @@ SIGNATURES = {
     "tsb_test_attention_time": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 4 + [C.POINTER(C.c_int32)]),
     "tsb_covariate_assembly": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_graph_replay": (C.c_int, [C.c_void_p, C.c_int32]),
+    "tsb_fused_norm": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_test_scale_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_double] + [C.c_int32] * 6
                             + [C.c_void_p] * 8),
     "tsb_test_attention_time_ex": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 9 + [C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
@@ -175,6 +176,11 @@ class Model:
 
     def stream(self) -> int:
         return lib().tsb_stream(self.h) or 0
+
+    def fused_norm(self, mode: int):
+        """RMSNorm carried by the GEMMs: 1 (default), 0 off, 2 on with a forced fallback run."""
+        if lib().tsb_fused_norm(self.h, int(mode)) != 0:
+            raise RuntimeError("tsb_fused_norm failed")
 
     def graph_replay(self, on: bool):
         """CUDA-graph replay of repeated single-block forecasts (on by default)."""
