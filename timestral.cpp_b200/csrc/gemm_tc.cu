@@ -136,7 +136,7 @@ __device__ __forceinline__ void pack32(const float* v, uint32_t* w) {
 // TMEM lane quarter) and column group `part` of PARTS.
 template <int KIND, int PARTS>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, int m0, int n0, int quarter, int lane,
-                                              int part, uint8_t* buf) {
+                                              int part, uint8_t* buf, float rsc) {
     const int half = part;
     const GemmEpilogue& e = g.epi;
     const int mw = m0 + quarter * 32;
@@ -229,7 +229,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
     } else if constexpr (KIND == EPI_F16 || KIND == EPI_SILU) {
         // 64 columns (two TMEM reads) per staging pass; the thread stores 8 f16 columns.
         constexpr int C = BN / PARTS / 64;
-        const float rsc = row_scale(e, mw + lane, mw + lane < g.M);
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             const int cb = n0 + (half * C + c) * 64;
@@ -271,7 +270,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
         // The first half of the tile holds the first operand, the second half the second:
         // each 32-column pair gives 32 outputs (64 bytes of a staging row); a group holds C pairs.
         constexpr int C = BN / 2 / PARTS / 32;
-        const float rsc = row_scale(e, mw + lane, mw + lane < g.M);
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             const int cc = half * C + c;
@@ -321,7 +319,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
         constexpr int C = BN / 128;
         const int m = mw + lane;                      // the TMEM row of this thread
         const bool row_ok = m < g.M;
-        const float rsc = row_scale(e, m, row_ok);
         // Head-major row (row * H * S + token) of the rows stored after the transpose.
         int hm[8];
 #pragma unroll
@@ -492,15 +489,21 @@ __global__ void __launch_bounds__(Cfg<KIND>::THREADS, 1)
         for (int tile = pair; tile < num_tiles; tile += pairs, ++acc) {
             const int b = acc & 1;
             const uint32_t aph = (acc >> 1) & 1;
+            const int m0 = (tile / n_tiles) * 2 * BM + int(rank) * BM, n0 = (tile % n_tiles) * BN;
+            // The row's 1/rms (norm carried by the GEMM) is read before the accumulator is ready.
+            float rsc = 1.0f;
+            if constexpr (KIND != EPI_F32 && KIND != EPI_RESID) {
+                const int m = m0 + quarter * 32 + lane;
+                rsc = row_scale(g.epi, m, m < g.M);
+            }
             bool ok = true;
             if (lane == 0) ok = wait_or_abort(&sm->acc_full[b], aph, abort, err, kDevTimeoutAccFull);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             __syncwarp();
             tc_fence_after();
-            const int m0 = (tile / n_tiles) * 2 * BM + int(rank) * BM, n0 = (tile % n_tiles) * BN;
             const uint32_t tacc = tmem + (uint32_t(quarter * 32) << 16) + b * BN;
-            epilogue_tile<KIND, PARTS>(g, tacc, m0, n0, quarter, lane, part, stage + (warp - 2) * 32 * 128);
+            epilogue_tile<KIND, PARTS>(g, tacc, m0, n0, quarter, lane, part, stage + (warp - 2) * 32 * 128, rsc);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster_relaxed(b ? acc_empty1 : acc_empty0);
