@@ -296,6 +296,8 @@ def test_fused_norm_and_its_fallback(V):
     dev = torch.device("cuda", 0)
     d_ctx = torch.from_numpy(x).to(dev)
     d_out = torch.empty((B, V, H, Q), device=dev)
+    d_ctx2 = torch.from_numpy(random_context(B, V, T, seed=97 + V)).to(dev)
+    d_out2 = torch.empty((B, V, H, Q), device=dev)
 
     def device_async():
         m.forecast_device(d_ctx.data_ptr(), None, B, V, T, H, d_out.data_ptr(), asynchronous=True)
@@ -305,11 +307,19 @@ def test_fused_norm_and_its_fallback(V):
     try:
         m.fused_norm(0)
         plain, plain_dev, plain_cov = m.forecast(x, H).copy(), device_async(), m.forecast(x, H, **kw).copy()
+        m.forecast_device(d_ctx2.data_ptr(), None, B, V, T, H, d_out2.data_ptr())
+        plain_dev2 = d_out2.cpu().numpy().copy()
         m.fused_norm(2)
         for _ in range(3):                     # the third call replays a captured graph
             assert np.array_equal(m.forecast(x, H).view(np.uint32), plain.view(np.uint32))
             assert np.array_equal(device_async().view(np.uint32), plain_dev.view(np.uint32))
         assert np.array_equal(m.forecast(x, H, **kw).view(np.uint32), plain_cov.view(np.uint32))
+        # two asynchronous forecasts into two outputs before one sync: both get their fallback run
+        m.forecast_device(d_ctx.data_ptr(), None, B, V, T, H, d_out.data_ptr(), asynchronous=True)
+        m.forecast_device(d_ctx2.data_ptr(), None, B, V, T, H, d_out2.data_ptr(), asynchronous=True)
+        assert tb.lib().tsb_sync(m.h) == 0
+        assert np.array_equal(d_out.cpu().numpy().view(np.uint32), plain_dev.view(np.uint32))
+        assert np.array_equal(d_out2.cpu().numpy().view(np.uint32), plain_dev2.view(np.uint32))
         m.fused_norm(1)
         fused = m.forecast(x, H)
         check_nd(fused, o.forecast(x, H), x, 32, F16_MEAN_ND)

@@ -830,6 +830,13 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
     key.ctx = d_ctx; key.umask = d_umask; key.out = d_out;
     key.B = B; key.V = V; key.T = T; key.H = H; key.max_context = max_context; key.sym = symmetric; key.clip = clip;
     const bool graphable = im.graphs && single && !im.timing;
+    // An earlier asynchronous forecast that carried the norm in the GEMMs is completed and
+    // checked (and run again if flagged) before this one shares the flag.
+    if (im.pending.valid && im.fuse_now) {
+        check(cudaStreamSynchronize(s), "forecast");
+        finish_targets();
+        im.launches = 0;
+    }
     im.fuse_now = im.fuse_allowed();
     im.pending = Impl::Pending{true, d_ctx, d_umask, B, V, T, H, symmetric, clip, d_out, kept, len, patches, shot, R, R2};
     if (graphable && im.graph_exec && key == im.graph_key && im.graph_generation == g_workspace_generation.load()) {
@@ -958,6 +965,10 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
                            const uint8_t* umask, int T_req, float* h_out) {
     check(cudaSetDevice(device_), "cudaSetDevice");
     Impl& im = *impl_;
+    if (im.pending.valid && im.fuse_now) {       // an earlier asynchronous forecast: complete it
+        check(cudaStreamSynchronize(stream_), "forecast");
+        finish_targets();
+    }
     im.launches = 0;
     im.pending.valid = false;
     im.fuse_now = im.fuse_allowed();
@@ -1019,6 +1030,10 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
 void Engine::forecast_covariates(const CovRequest& q, bool symmetric, bool clip, float* h_out) {
     check(cudaSetDevice(device_), "cudaSetDevice");
     Impl& im = *impl_;
+    if (im.pending.valid && im.fuse_now) {       // an earlier asynchronous forecast: complete it
+        check(cudaStreamSynchronize(stream_), "forecast");
+        finish_targets();
+    }
     im.launches = 0;
     im.pending.valid = false;
     im.fuse_now = im.fuse_allowed();
