@@ -106,3 +106,14 @@ def test_model_loader_rejects_schema_violations(tmp_path):
     w.write_header_to_file(); w.write_kv_data_to_file(); w.write_tensors_to_file(); w.close()
     assert not lib.timestral_capi_load(str(tmp_path / "missing.gguf").encode(), 1)
     assert lib.timestral_capi_last_error(None) == b"missing tensor: out_norm.weight"
+
+
+def test_device_switches_reject_bad_arguments():
+    """The device-seam switches refuse a null handle (and tsb_fused_norm an unknown mode)
+    without touching a GPU."""
+    import timestral_b200 as tb
+    L = tb.lib()
+    err_arg = 1                      # TSB_ERR_ARG
+    assert L.tsb_fused_norm(None, 1) == err_arg
+    assert L.tsb_graph_replay(None, 1) == err_arg
+    assert L.tsb_covariate_assembly(None, 1) == err_arg
