@@ -328,6 +328,19 @@ def test_fused_norm_and_its_fallback(V):
         m.fused_norm(1)
 
 
+@pytest.mark.parametrize("mode", [1, 0])
+def test_non_unit_norm_gains(mode):
+    """With RMSNorm gains other than 1 (folded into the consuming GEMM weights at load), both
+    norm modes stay within the F16 bound of the oracle."""
+    m, o = models(sy.spec_small_gains(), "f16")
+    x = random_context(3, 2, 256, seed=99)
+    try:
+        m.fused_norm(mode)
+        check_nd(m.forecast(x, 64), o.forecast(x, 64), x, 32, F16_MEAN_ND)
+    finally:
+        m.fused_norm(1)
+
+
 def test_graph_replay_f32_path():
     """The F32 CUDA-core path replays its graph too, bit for bit, and a forecast that needs
     two decode blocks (not captured) still matches plain launches."""

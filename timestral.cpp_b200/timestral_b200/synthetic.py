@@ -56,6 +56,7 @@ class ModelSpec:
     symmetric_averaging: bool = True
     clip_nonnegative: bool = True
     target_encoding_smooth: float = 1.0
+    norm_gain_spread: float = 0.0     # > 0: RMSNorm gains drawn from 1 + U(-spread, spread)
 
     @property
     def head_dim(self) -> int:
@@ -116,6 +117,12 @@ def spec_small_long() -> ModelSpec:
     return ModelSpec(name="timestral-small-long", patch_size=32, d_model=128, num_heads=2, mlp_hidden_dim=256,
                      block_schedule=("time", "variate", "time_variate", "variate_time"),
                      quantile_knots=KNOTS_21, block_size=32, context_length=32768)
+
+
+def spec_small_gains() -> ModelSpec:
+    """spec_small with RMSNorm gains in [0.5, 1.5] (the random init of the others is 1), so
+    that the norm weights folded into the consuming GEMM weights are not a no-op."""
+    return dataclasses.replace(spec_small(), name="timestral-small-gains", norm_gain_spread=0.5)
 
 
 LAYER_AXES = {"time": (True,), "variate": (False,), "time_variate": (True, False),
@@ -194,6 +201,8 @@ def init_weights(s: ModelSpec, seed: int = 0):
             w[name] = np.zeros(shape, np.float32)
         elif kind == "norm":
             w[name] = np.ones(shape, np.float32)
+            if s.norm_gain_spread > 0:
+                w[name] += rng.uniform(-s.norm_gain_spread, s.norm_gain_spread, shape).astype(np.float32)
     w["rope.inv_freq"], w["rope.cos"], w["rope.sin"] = inv, cos, sin
     # The converter stores qkv rows head-major (docs/PLAN.md B.3); a random init has no
     # torch order to permute from, so the draw above is already taken as head-major.
