@@ -58,12 +58,13 @@ CONFIGS = {
                       "H=1024 (one 32-patch decode block, S=1056), seasonal + 1% NaN"),
 }
 
-# DRAM bytes (read + write) of one time-attention (row, head) problem at S = 72, from the
-# ncu capture summarised in profiles/attention_time_tc_cfg5.md (B = 1024, dram__bytes_read.sum
-# + dram__bytes_write.sum over 24,576 problems); traffic per launch scales with the problems.
-ATTN_DRAM_BYTES_PER_PROBLEM = 45384
-# The same for the long-row kernel at S = 1056 (cfg6), per (row, head) plane, from
-# profiles/attention_time_tc_long_cfg6.md (B = 8: 119.4 MB over 192 planes).
+# DRAM bytes (read + write) of one time-attention (row, head) problem at S = 72: a constant
+# taken from one ncu capture of the kernel (B = 1024, dram__bytes_read.sum +
+# dram__bytes_write.sum over 24,576 problems), not measured by this script; traffic per
+# launch scales with the problems. The bench line says so in roofline.traffic_source.
+ATTN_DRAM_BYTES_PER_PROBLEM = 45300
+# The same for the long-row kernel at S = 1056 (cfg6), per (row, head) plane (B = 8: 119.4 MB
+# over 192 planes).
 ATTN_LONG_DRAM_BYTES_PER_PLANE = 621760
 
 

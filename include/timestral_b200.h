@@ -55,6 +55,13 @@ TIMESTRAL_API void* tsb_stream(timestral_ctx* ctx);
  * (tests that path). Replaces the reference's per-sublayer rms_f32 node (src/layers.cpp:262-287)
  * on the tensor-core path. */
 TIMESTRAL_API int tsb_fused_norm(timestral_ctx* ctx, int32_t mode);
+/* Attention kernels of the tensor-core path: mode 0 (default) the tensor-core kernels (f16
+ * probabilities, f32 accumulation in tensor memory); mode 1 the CUDA-core kernels that keep
+ * the reference's attention arithmetic (float64 q.k dots, f32 softmax, f32 value sums;
+ * reference src/layers.cpp:578-617) on the same f16 q/k/v, for time rows of up to 2176 tokens
+ * and the variate axis. Mode 1 is slower; it shows how much of a forecast's deviation from the
+ * reference comes from the tensor-core attention. */
+TIMESTRAL_API int tsb_attention_kernels(timestral_ctx* ctx, int32_t mode);
 /* CUDA-graph replay (on by default): a forecast without covariates that fits one decode
  * block (H <= 32 patches of the 209M geometry) is captured into a CUDA graph on its second
  * call with the same sizes, flags and device buffers (tsb_forecast_device pointers, or the
@@ -94,16 +101,20 @@ TIMESTRAL_API int tsb_last_geometry(timestral_ctx* ctx, int64_t* rows, int32_t* 
  * that may not allocate GPU memory: an application that owns every allocation on the
  * device and hands this library fixed buffers, or a loop that must never enter the CUDA
  * allocator. The float64 scan scratch comes from a 4 MiB array compiled into the library
- * (held by every GPU that loads it until the process exits) instead of cudaMalloc; the
- * call allocates nothing.
+ * instead of cudaMalloc. CUDA loads a library's device code lazily, so the array is reserved
+ * on a GPU when the library's code first runs there (this entry point's first call, or any
+ * forecast) and is held until the process exits; make a first call at set-up (a one-row
+ * request is enough) and every later call allocates nothing.
  * d_q/d_out: [rows][patches*patch_size][num_quantiles] f32; d_rows: [rows][length] f32
  * context; d_mask: [rows][length] bytes 0/1; d_role: [rows] (0 = target row; others keep
  * their quantiles) or NULL for all targets; d_loc0/d_scale0: [rows] frame of the last
  * context step. Requests needing more than the reserved scratch, rows * (3 * (length /
  * patch_size + patches) + 2 * patch_size + 2 * patches) float64 values above 524,288, are
- * rejected with TSB_ERR_ARG (split the rows across calls). The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress); make that first call before
- * any stream capture. All calls share the one array: calls that overlap on the GPU (other
+ * rejected with TSB_ERR_ARG before any device work (split the rows across calls). The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress), and so does
+ * the first call after that device's context was reset (cudaDeviceReset); make those calls
+ * before any stream capture. All calls share the one array, which keeps the last call's
+ * values (every value a call reads it first writes): calls that overlap on the GPU (other
  * streams, other threads) race on it. Enqueued on `stream` (cudaStream_t, NULL = legacy
  * default stream); errors go to timestral_capi_last_error(NULL). */
 TIMESTRAL_API int tsb_refine_static(const float* d_q, const float* d_rows, const int8_t* d_mask, const int8_t* d_role,
@@ -165,6 +176,13 @@ TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, vo
 TIMESTRAL_API int tsb_test_attention_variate(const void* q, const void* k, const void* v, const void* gate, void* out,
                                              const uint32_t* key_valid, const int8_t* role, int32_t rows, int32_t H,
                                              int32_t S, int32_t N, int32_t G);
+/* The refine step of one decode block with its float64 scratch from cudaMalloc (as the
+ * forecast's workspace provides it), on the current device, synchronized; arguments as
+ * tsb_refine_static (patches >= 2, d_role may be NULL). */
+TIMESTRAL_API int tsb_test_refine(const float* d_q, const float* d_rows, const int8_t* d_mask, const int8_t* d_role,
+                                  const float* d_loc0, const float* d_scale0, int32_t rows, int32_t length, int32_t patches,
+                                  int32_t patch_size, int32_t num_quantiles, int32_t median_index, double minimum_scale,
+                                  float* d_out);
 TIMESTRAL_API int tsb_test_rms(const float* x, const float* w, int32_t tokens, int32_t D, float eps, void* out,
                                int32_t out_f16);
 

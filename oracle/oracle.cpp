@@ -357,6 +357,7 @@ struct Tensor {
 struct oracle_model {
     oracle_config c;
     int per_shot = 0;   // test override of ForecastRequest::per_shot_horizon_patches
+    bool round_attention = false;   // test knob: f16-rounded q/k/v and sigmoid(gate), as the device stores them
     std::map<std::string, Tensor> t;
     const Tensor& get(const std::string& n) const {
         auto it = t.find(n); if (it == t.end()) throw Error("tensor not found: " + n); return it->second;
@@ -612,6 +613,10 @@ std::vector<float> run_encoder(const oracle_model& m, std::vector<float> x, size
             if (time) {
                 apply_rope(q.data(), cosg.data(), sing.data(), M, H, hd);
                 apply_rope(k.data(), cosg.data(), sing.data(), M, H, hd);
+            }
+            if (m.round_attention)
+                for (size_t i = 0; i < M * D; ++i) { q[i] = round_f16(q[i]); k[i] = round_f16(k[i]); v[i] = round_f16(v[i]); }
+            if (time) {
                 sdpa_generic(q.data(), k.data(), v.data(), att.data(), hd, H, S, R, mk.enc_len,
                              [S](size_t bb, size_t i) { return bb * S + i; },
                              [&](size_t bb, size_t t, size_t jj) { return tadd[(bb * S + t) * S + jj]; });
@@ -624,7 +629,10 @@ std::vector<float> run_encoder(const oracle_model& m, std::vector<float> x, size
             bool gated = (time ? c.time_gate : c.variate_gate) == 1;
             if (gated) {
                 project(m, a + "gate", norm.data(), M, c.attn_bias, false, gate);
-                for (size_t i = 0; i < M * D; ++i) att[i] = att[i] * (1.0f / (1.0f + activation_exp(-gate[i])));
+                for (size_t i = 0; i < M * D; ++i) {
+                    float sg = 1.0f / (1.0f + activation_exp(-gate[i]));
+                    att[i] = att[i] * (m.round_attention ? round_f16(sg) : sg);
+                }
             }
             project(m, a + "out", att.data(), M, c.attn_bias, false, outp);
             for (size_t i = 0; i < M * D; ++i) x[i] = x[i] + outp[i];
@@ -1041,6 +1049,7 @@ const char* oracle_last_error(void) { return g_error.c_str(); }
 
 oracle_model* oracle_model_new(const oracle_config* cfg) { auto* m = new oracle_model; m->c = *cfg; return m; }
 void oracle_model_set_per_shot(oracle_model* m, int32_t n) { m->per_shot = n; }
+void oracle_model_set_round_attention(oracle_model* m, int32_t on) { m->round_attention = on != 0; }
 void oracle_model_free(oracle_model* m) { delete m; }
 
 int oracle_model_set(oracle_model* m, const char* name, const void* data, int32_t type, int64_t ne0, int64_t ne1) {

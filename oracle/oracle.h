@@ -48,6 +48,9 @@ int oracle_model_set(oracle_model* m, const char* name, const void* data, int32_
 const char* oracle_last_error(void);
 /* Test override of the request's per_shot_horizon_patches (0 = model default). */
 void oracle_model_set_per_shot(oracle_model* m, int32_t n);
+/* Test knob: round q/k/v (after RoPE) and sigmoid(gate) to f16 before attention, as the
+ * device's tensor-core path stores them, to separate that rounding from other deviations. */
+void oracle_model_set_round_attention(oracle_model* m, int32_t on);
 
 /* Same fields and meaning as timestral_forecast_request (include/timestral_capi.h). */
 typedef struct oracle_request {

@@ -62,6 +62,8 @@ def lib():
         _lib.oracle_model_free.argtypes = [C.c_void_p]
         _lib.oracle_model_set.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int64]
         _lib.oracle_forecast.argtypes = [C.c_void_p, C.POINTER(OracleRequest), C.c_void_p, C.c_int32]
+        _lib.oracle_model_set_per_shot.argtypes = [C.c_void_p, C.c_int32]
+        _lib.oracle_model_set_round_attention.argtypes = [C.c_void_p, C.c_int32]
         _lib.oracle_activation_exp.restype = C.c_float
         _lib.oracle_activation_exp.argtypes = [C.c_float]
         _lib.oracle_attention_exp.restype = C.c_float
@@ -223,6 +225,13 @@ def normalized_deviation(actual, ref, loc, scale):
     """Per-row normalized deviation of the reference's quantisation quality metric
     (scripts/quant_metrics.py:50-69): z = asinh((ref-loc)/scale), w = scale*cosh(z),
     e = |actual-ref| / (w * rms(z)). Returns (mean, max) over all rows."""
+    means, maxs = normalized_deviation_rows(actual, ref, loc, scale)
+    return float(np.mean(means)), float(np.max(maxs))
+
+
+def normalized_deviation_rows(actual, ref, loc, scale):
+    """The same metric per target row: (mean over the row's values, max over them), each
+    an array of one entry per row."""
     ref = np.asarray(ref, np.float64)
     act = np.asarray(actual, np.float64)
     R = loc.shape[0]
@@ -241,7 +250,7 @@ def normalized_deviation(actual, ref, loc, scale):
         e = np.abs(act[r] - ref[r]) / (w * rms)
         means.append(float(np.mean(e)))
         maxs.append(float(np.max(e)))
-    return float(np.mean(means)), float(np.max(maxs))
+    return np.array(means), np.array(maxs)
 
 
 # ---------------------------------------------------------------------------------------
@@ -347,6 +356,11 @@ def block_frames(cfg, x, mask, median, rows, length, patches):
 
 def set_per_shot(model, n):
     lib().oracle_model_set_per_shot(model.h, C.c_int32(n))
+
+
+def set_round_attention(model, on):
+    """Round q/k/v and sigmoid(gate) to f16 before attention (the device's storage)."""
+    lib().oracle_model_set_round_attention(model.h, C.c_int32(int(on)))
 
 
 def anchors(context, ps, minimum_scale=1e-6):

@@ -1,4 +1,4 @@
-// C entry points into the reference's own sources, compiled from /root/reference/src by
+// C entry points into the reference's own sources, compiled from the reference's src/ by
 // oracle/ref/Makefile into oracle/_ref/libtsref.so — TEST INFRASTRUCTURE ONLY: the tests use
 // it to pin the CPU oracle (oracle/oracle.cpp) against the reference's real code.
 //

@@ -7,9 +7,12 @@ Tolerances:
   * F16 weights (tensor-core path): mean normalized deviation <= 1e-3, the reference's
     documented F16 quality bound (scripts/quant_metrics.py:50-69 metric, bound from
     docs/quantization-209m-result.md:28), measured against the oracle's F16 restatement.
-  * Q8_0 weights: reported against the oracle's Q8_0 restatement (activations quantised
-    per 32-block, as ggml does) with a loose sanity bound; the device path dequantises the
-    weights to F16 and keeps F16 activations.
+    A good mean could hide a few bad series, so every target row's own mean is also held to
+    3x the bound and every single value to 30x it (F16_ROW_FACTOR, F16_VALUE_FACTOR).
+  * Q8_0 weights: against the oracle's F32 forecast of the same model, as the reference
+    reports its Q8_0 quality (docs/quantization-209m-result.md:23: mean 0.005658 against F32),
+    and against the oracle's Q8_0 restatement (activations quantised per 32-block, as ggml
+    does); the device path dequantises the weights to F16 and keeps F16 activations.
 """
 import numpy as np
 import pytest
@@ -22,6 +25,10 @@ pytestmark = pytest.mark.gpu
 
 F32_RTOL, F32_ATOL = 1e-3, 1e-4
 F16_MEAN_ND = 1e-3
+F16_ROW_FACTOR = 3.0      # each target row's mean deviation <= 3 x the mean bound
+F16_VALUE_FACTOR = 30.0   # each value's deviation <= 30 x the mean bound
+Q8_F32_MEAN_ND = 0.011    # device Q8_0 against F32: within 2x the reference's published 0.005658
+REFERENCE_Q8_F32 = 0.005658
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -50,11 +57,21 @@ def check_f32(gpu, ref):
     assert np.all(err <= tol), worst
 
 
-def check_nd(gpu, ref, context, ps, bound):
+def nd_stats(gpu, ref, context, ps=32):
+    """(mean, worst row mean, worst value) of the normalized deviation of gpu from ref."""
     loc, sc = op.anchors(context, ps)
-    mean, mx = op.normalized_deviation(gpu, ref, loc, sc)
-    print(f"normalized deviation mean={mean:.3e} max={mx:.3e} (bound {bound})")
-    assert mean <= bound, (mean, mx)
+    rows_mean, rows_max = op.normalized_deviation_rows(gpu, ref, loc, sc)
+    return float(np.mean(rows_mean)), float(np.max(rows_mean)), float(np.max(rows_max))
+
+
+def check_nd(gpu, ref, context, ps, bound, row_factor=F16_ROW_FACTOR, value_factor=F16_VALUE_FACTOR):
+    """Mean normalized deviation <= bound, every target row's mean <= row_factor * bound and
+    every value <= value_factor * bound. Returns (mean, worst value)."""
+    mean, row, mx = nd_stats(gpu, ref, context, ps)
+    print(f"normalized deviation mean={mean:.3e} worst row={row:.3e} worst value={mx:.3e} (bound {bound})")
+    assert mean <= bound, (mean, row, mx)
+    assert row <= row_factor * bound, (mean, row, mx)
+    assert mx <= value_factor * bound, (mean, row, mx)
     return mean, mx
 
 
@@ -196,12 +213,102 @@ def test_209m_f16_cfg2_shape():
     check_nd(m.forecast(x, 256), o.forecast(x, 256), x, 32, F16_MEAN_ND)
 
 
-def test_209m_q8_reported():
-    m, o = models(sy.spec_209m(), "q8_0")
-    assert m.tensor_core_path
-    x = sy.series_seasonal(1, 512)
-    mean, mx = check_nd(m.forecast(x, 64), o.forecast(x, 64), x, 32, 0.05)
-    print(f"Q8_0 device (f16 dequant) vs oracle Q8_0 restatement: mean {mean:.3e} max {mx:.3e}")
+def test_209m_f16_cfg3_shape():
+    """Multivariate: V=32 targets per series (VAR(1), Sigma_ij = 0.5^|i-j|), T=1024, H=128:
+    32-row series on the variate axis (cfg3 shape, B cut to 2 for the oracle's CPU time)."""
+    m, o = models(sy.spec_209m(), "f16")
+    x = sy.series_var1(2, 32, 1024, seed=0)
+    g, r = m.forecast(x, 128), o.forecast(x, 128)
+    rows, S, L, _ = m.last_geometry()
+    assert (rows, S, L) == (2 * 2 * 32, 36, 32)
+    check_nd(g, r, x, 32, F16_MEAN_ND)
+
+
+def test_209m_f16_cfg4_shape():
+    """Covariates: V=4 targets, 8 past numeric (AR(1)), 4 known numeric (sinusoids), 2
+    categorical known codes in [0, 16), T=1024, H=96 (cfg4 shape, B cut to 2): the two-stream
+    layout S = 2N with 18 rows per series and raw categorical codes (V != 1)."""
+    m, o = models(sy.spec_209m(), "f16")
+    x, past, known, cat = sy.series_covariates(2, 4, 1024, 96, seed=0)
+    kw = dict(past=past, known=known, cat_known=cat)
+    g, r = m.forecast(x, 96, **kw), o.forecast(x, 96, **kw)
+    rows, S, L, _ = m.last_geometry()
+    assert (rows, S, L) == (2 * 2 * 18, 70, 32)
+    check_nd(g, r, x, 32, F16_MEAN_ND)
+
+
+def test_209m_f16_cfg5_scale():
+    """The throughput workload at full size: B=4096 seasonal series, T=2048, H=256 in one call
+    (589,824 token rows, workspace offsets beyond 2^31 bytes). Eight series spread over the
+    batch equal their own B=1 forecasts bit for bit, and the oracle on those eight."""
+    m, o = models(sy.spec_209m(), "f16")
+    x = sy.series_seasonal(4096, 2048, nan_frac=0.01)
+    big = m.forecast(x, 256).copy()
+    assert np.all(np.isfinite(big)) and np.all(np.diff(big, axis=-1) >= 0)
+    idx = [0, 1, 777, 2047, 2048, 3001, 4094, 4095]
+    for i in idx:
+        one = m.forecast(x[i:i + 1], 256)
+        assert np.array_equal(one.view(np.uint32), big[i:i + 1].view(np.uint32)), i
+    sub = np.ascontiguousarray(x[idx])
+    check_nd(big[idx], o.forecast(sub, 256), sub, 32, F16_MEAN_ND)
+
+
+def test_209m_attention_share():
+    """How much of the F16 deviation comes from attention, at the cfg2 shape on the 209M
+    model. Four comparisons: the device with its tensor-core attention and with the CUDA-core
+    attention (the reference's float64 q.k dots and f32 softmax on the same f16 q/k/v), each
+    against the oracle and against the oracle with q/k/v and sigmoid(gate) rounded to f16 as
+    the device stores them. All stay within the F16 bound."""
+    m, o = models(sy.spec_209m(), "f16")
+    x = sy.series_random_walk(2, 2048, nan_frac=0.05)
+    ref = o.forecast(x, 256)
+    try:
+        op.set_round_attention(o, True)
+        ref_r = o.forecast(x, 256)
+    finally:
+        op.set_round_attention(o, False)
+    try:
+        m.attention_kernels(1)
+        simt = m.forecast(x, 256).copy()
+    finally:
+        m.attention_kernels(0)
+    tc = m.forecast(x, 256)
+    out = {}
+    for name, g in (("tensor-core attention", tc), ("CUDA-core attention", simt)):
+        for rname, r in (("oracle", ref), ("oracle, f16 q/k/v", ref_r)):
+            out[(name, rname)] = nd_stats(g, r, x)
+            print(f"{name:>22} vs {rname:<18}: mean {out[(name, rname)][0]:.3e} "
+                  f"worst row {out[(name, rname)][1]:.3e} worst value {out[(name, rname)][2]:.3e}")
+    print(f"oracle f16 q/k/v vs oracle: mean {nd_stats(ref_r, ref, x)[0]:.3e}")
+    for (mean, row, mx) in out.values():
+        assert mean <= F16_MEAN_ND and row <= F16_ROW_FACTOR * F16_MEAN_ND and mx <= F16_VALUE_FACTOR * F16_MEAN_ND
+    assert not np.array_equal(tc, simt)
+
+
+def test_209m_q8_against_f32():
+    """Q8_0 quality as the reference reports it: the Q8_0 forecast against the F32 forecast of
+    the same seed-0 weights (cfg2 shape), beside the reference's published mean 0.005658 for
+    its own Q8_0 path (a trained model on its evaluation data). Also printed: the oracle's
+    restatement of ggml's Q8_0 arithmetic (activations quantised per 32-block) against F32,
+    the device F16 forecast against F32, and the device Q8_0 against the oracle's Q8_0."""
+    q8, o8 = models(sy.spec_209m(), "q8_0")
+    assert q8.tensor_core_path
+    f16, _ = models(sy.spec_209m(), "f16")
+    o32 = op.OracleModel(sy.cached_model(sy.spec_209m(), "f32"))
+    x = sy.series_random_walk(2, 2048, nan_frac=0.05)
+    ref = o32.forecast(x, 256)
+    dev_q8 = q8.forecast(x, 256)
+    orc_q8 = o8.forecast(x, 256)
+    dev_f16 = f16.forecast(x, 256)
+    rows = {"device Q8_0 vs F32": nd_stats(dev_q8, ref, x), "oracle Q8_0 (ggml arithmetic) vs F32": nd_stats(orc_q8, ref, x),
+            "device F16 vs F32": nd_stats(dev_f16, ref, x), "device Q8_0 vs oracle Q8_0": nd_stats(dev_q8, orc_q8, x)}
+    for k, (mean, row, mx) in rows.items():
+        print(f"{k:>38}: mean {mean:.3e} worst row {row:.3e} worst value {mx:.3e}")
+    print(f"{'reference Q8_0 vs F32 (published)':>38}: mean {REFERENCE_Q8_F32:.3e}")
+    mean, row, mx = rows["device Q8_0 vs F32"]
+    assert mean <= Q8_F32_MEAN_ND, mean
+    assert row <= F16_ROW_FACTOR * Q8_F32_MEAN_ND and mx <= F16_VALUE_FACTOR * Q8_F32_MEAN_ND, (row, mx)
+    assert rows["device F16 vs F32"][0] <= F16_MEAN_ND
 
 
 @pytest.mark.parametrize("kind,bound", [("q6_k", 0.05), ("q5_k", 0.1), ("q4_k", 0.2)])

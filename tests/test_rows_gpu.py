@@ -63,8 +63,9 @@ def test_split_f16(dev, big):
 
 @pytest.mark.parametrize("R,T,patches,ps", [(64, 2048, 8, 32), (37, 512, 3, 32), (5, 96, 2, 8), (9, 4096, 33, 32)])
 def test_refine_bitwise(dev, R, T, patches, ps):
-    """Refine of one decode block (reference src/refine.cpp:32-106) equals the oracle's float64
-    restatement bit for bit: the warp-parallel kernel keeps every operation and its order."""
+    """Refine of one decode block (reference src/refine.cpp:32-106), with its scratch from the
+    allocator as inside a forecast, equals the oracle's float64 restatement bit for bit: the
+    warp-parallel kernel keeps every operation and its order."""
     from helpers import unit_config
     Q, mi = 21, 10
     rng = np.random.default_rng(R * 7 + T)
@@ -83,12 +84,36 @@ def test_refine_bitwise(dev, R, T, patches, ps):
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
     dq, dx, dm, dr, dl, ds = t(q), t(x), t(m), t(role), t(loc0), t(sc0)
     out = torch.full_like(dq, float("nan"))
-    rc = tb.lib().tsb_refine_static(dq.data_ptr(), dx.data_ptr(), dm.data_ptr(), dr.data_ptr(), dl.data_ptr(),
-                                    ds.data_ptr(), R, T, patches, ps, Q, mi, C.c_double(1e-6), out.data_ptr(), None)
-    assert rc == 0, tb.lib().timestral_capi_last_error(None)
+    rc = tb.lib().tsb_test_refine(dq.data_ptr(), dx.data_ptr(), dm.data_ptr(), dr.data_ptr(), dl.data_ptr(),
+                                  ds.data_ptr(), R, T, patches, ps, Q, mi, C.c_double(1e-6), out.data_ptr())
+    assert rc == 0, rc
     got = out.cpu().numpy()
     want = want.reshape(got.shape)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), float(np.abs(got - want).max())
+
+
+@pytest.mark.parametrize("name", ["refine_ps32_T256", "refine_ps8_T40"])
+def test_refine_matches_reference_golden(dev, name):
+    """The device refine against the reference's own refine_block output (tests/golden,
+    written by the reference's compiled src/refine.cpp), bit for bit. The anchor frame it
+    takes is the scaler's frame at the last context step (pinned to the same reference)."""
+    import json
+    from helpers import unit_config
+    d = np.load(GOLDEN / f"{name}.npz")
+    cfg = json.loads(str(d["config"]))
+    R, T, patches, ps = cfg["R"], cfg["T"], cfg["patches"], cfg["patch_size"]
+    c = unit_config(patch_size=ps, minimum_scale=cfg["minimum_scale"])
+    _, loc, sc = op.scale_rows(c, d["x"], d["m"], R, T)
+    loc0 = np.ascontiguousarray(loc.reshape(R, T)[:, -1])
+    sc0 = np.ascontiguousarray(sc.reshape(R, T)[:, -1])
+    role = (d["targets"] == 0).astype(np.int8)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    dq, dx, dm, dr, dl, ds = t(d["q"]), t(d["x"]), t(d["m"]), t(role), t(loc0), t(sc0)
+    out = torch.full_like(dq, float("nan"))
+    rc = tb.lib().tsb_test_refine(dq.data_ptr(), dx.data_ptr(), dm.data_ptr(), dr.data_ptr(), dl.data_ptr(),
+                                  ds.data_ptr(), R, T, patches, ps, 21, 10, C.c_double(cfg["minimum_scale"]), out.data_ptr())
+    assert rc == 0, rc
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), d["refined"].view(np.uint32))
 
 
 @pytest.mark.parametrize("R,W,ps,attend", [(5, 3072, 32, 1), (3, 96, 32, 0), (4, 1056, 32, 1), (2, 2400, 48, 1),

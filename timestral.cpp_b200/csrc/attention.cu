@@ -929,7 +929,7 @@ __device__ void softmax_values(float* lg, int count, const int* seqidx, int keys
 }
 
 constexpr int SIMT_WARPS = 4;
-constexpr int SIMT_MAX_KEYS = 2176;
+constexpr int SIMT_MAX_KEYS = kSimtMaxKeys;
 
 // Time axis: block = (row, head, 4 queries). Logits in shared memory.
 template <class T>

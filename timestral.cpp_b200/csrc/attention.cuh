@@ -32,6 +32,9 @@ cudaError_t attention_time_tc(const __half* q, const __half* k, const __half* v,
 cudaError_t attention_time_tc_long(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
                                    int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err);
 
+// Longest time row (tokens) the CUDA-core time-attention kernel takes.
+constexpr int kSimtMaxKeys = 2176;
+
 // CUDA-core kernels with the reference's operation order (float64 q.k dots, ATen exp for
 // full eight-lane chunks, libm exp for the tail, eight-lane sums, value FMA chain, one
 // reciprocal multiply). T = float (F32 path) or __half (tensor-core path inputs).

@@ -126,6 +126,7 @@ struct Engine::Impl {
     bool fuse = true;            // allowed
     bool fuse_now = true;        // used by the running forecast
     bool force_fallback = false; // test hook: treat every fused forecast as flagged
+    bool attn_simt = false;      // tensor-core path: attention on the CUDA-core kernels
     const __half* a_in = nullptr;
     const float* ssq_in = nullptr;
     bool produce16 = false;
@@ -709,7 +710,11 @@ struct Engine::Impl {
             g.epi.rope_dup = rope_dup;
             gemm(EPI_QKVG, g);
             const __half* gate = a.gate ? gb.as<__half>() : nullptr;
-            if (a.time) {
+            if (attn_simt && a.time && S <= kSimtMaxKeys) {
+                run("attention", [&] { return attention_time_simt<__half>(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, hd, mm, s); });
+            } else if (attn_simt && !a.time) {
+                run("attention_variate", [&] { return attention_variate_simt<__half>(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, hd, mm, s); });
+            } else if (a.time) {
                 if (S <= 128)
                     run("attention", [&] { return attention_time_tc(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, mm, s, err.as<int>()); });
                 else
@@ -952,6 +957,12 @@ void Engine::targets_body(const float* d_ctx, const uint8_t* d_umask, int B, int
 void Engine::fused_norm(int mode) {
     impl_->fuse = mode != 0;
     impl_->force_fallback = mode == 2;
+    impl_->drop_graph();
+    impl_->have_last = false;
+}
+
+void Engine::attention_kernels(int mode) {
+    impl_->attn_simt = mode == 1;
     impl_->drop_graph();
     impl_->have_last = false;
 }

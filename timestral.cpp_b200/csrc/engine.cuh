@@ -101,6 +101,12 @@ public:
     // again with the RMSNorm kernel. Mode 0: always the RMSNorm kernel. Mode 2: carried, and
     // every forecast also takes the fallback run (a test of that path).
     void fused_norm(int mode);
+    // Attention kernels of the tensor-core path: 0 (default) the tensor-core kernels; 1 the
+    // CUDA-core kernels with the reference's operation order (float64 q.k dots, f32 softmax
+    // and value sums) on the same f16 q/k/v, for time rows of up to kSimtMaxKeys tokens and
+    // the variate axis. Mode 1 isolates the tensor-core attention's share of the deviation
+    // from the reference's f32 attention.
+    void attention_kernels(int mode);
 
     // Synchronise the stream and turn a device error word into an exception.
     void check_errors();

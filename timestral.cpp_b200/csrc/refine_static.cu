@@ -10,6 +10,8 @@
 #include "rows.cuh"
 #include "timestral_b200.h"
 
+#include <cuda.h>
+
 #include <cfloat>
 #include <cmath>
 #include <cstring>
@@ -22,25 +24,56 @@ void set_thread_error(const char* message);
 
 namespace {
 
-// Fixed scratch: 4 MiB of float64 per GPU that loads the library, held until the process
-// exits. One call needs rows * (3 * (length / patch_size + patches) + 2 * patch_size +
+// Fixed scratch: 4 MiB of float64 on every GPU where the library's device code is loaded
+// (with CUDA's lazy module loading, from the first call of this entry point or of another
+// kernel of the library on that device), held until the process exits. One call needs rows * (3 * (length / patch_size + patches) + 2 * patch_size +
 // 2 * patches) values (e.g. 1,700 rows of a 2048-step context with 8 horizon patches).
 constexpr size_t kScratchDoubles = size_t(1) << 19;
 static __device__ __align__(256) double g_refine_scratch[kScratchDoubles];
 
 constexpr int kMaxDevices = 64;
 double* g_scratch_ptr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};   // context id the address belongs to
 std::mutex g_setup_mutex;
 
-// Device address of the scratch array on the current device, looked up once per device.
-// In host code `g_refine_scratch` names a host-side stand-in, not device memory.
+// Unique id (for the life of the process) of the calling thread's current CUDA context, or
+// false when the driver does not offer it or no context is current yet.
+bool current_context_id(unsigned long long* id) {
+    using GetCurrentFn = CUresult (*)(CUcontext*);
+    using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrentFn get_current = nullptr;
+    static GetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrentFn>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetIdFn>(p);
+    });
+    CUcontext ctx = nullptr;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx) return false;
+    return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Device address of the scratch array on the current device. In host code
+// `g_refine_scratch` names a host-side stand-in, not device memory, so the address is looked
+// up with cudaGetSymbolAddress: on a device's first call (which also loads the library's
+// device code there and reserves the array, CUDA loading modules lazily), and again after
+// the device's context was replaced (cudaDeviceReset), which invalidates the old address.
 cudaError_t scratch_address(int dev, double** out) {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (!g_scratch_ptr[dev]) {
+    unsigned long long id = 0;
+    const bool known = current_context_id(&id);
+    if (!g_scratch_ptr[dev] || !known || id != g_scratch_ctx[dev]) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_refine_scratch);
         if (e != cudaSuccess) return e;
         g_scratch_ptr[dev] = static_cast<double*>(p);
+        g_scratch_ctx[dev] = current_context_id(&id) ? id : 0;
     }
     *out = g_scratch_ptr[dev];
     return cudaSuccess;

@@ -6,6 +6,10 @@
 #include "rows.cuh"
 #include "timestral_b200.h"
 
+#include <cfloat>
+#include <cmath>
+#include <cstring>
+
 extern "C" TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_error) {
     using namespace tsb;
     if (!t) return TSB_ERR_ARG;
@@ -153,4 +157,31 @@ extern "C" TIMESTRAL_API int tsb_test_attention_variate(const void* q, const voi
     if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
     if (ce != cudaSuccess) return ce == cudaErrorInvalidValue ? TSB_ERR_ARG : TSB_ERR_CUDA;
     return TSB_OK;
+}
+
+// The refine kernel as the forecast runs it: float64 scan scratch taken from the allocator
+// (the forecast's workspace), then freed. Same arguments as tsb_refine_static.
+extern "C" TIMESTRAL_API int tsb_test_refine(const float* d_q, const float* d_rows, const int8_t* d_mask, const int8_t* d_role,
+                                             const float* d_loc0, const float* d_scale0, int32_t rows, int32_t length,
+                                             int32_t patches, int32_t patch_size, int32_t num_quantiles,
+                                             int32_t median_index, double minimum_scale, float* d_out) {
+    if (!d_q || !d_out || !d_rows || !d_mask || !d_loc0 || !d_scale0 || rows <= 0 || patches <= 1 || patch_size <= 0 ||
+        length <= 0 || length % patch_size || num_quantiles <= 0 || num_quantiles > 64 || median_index < 0 ||
+        median_index >= num_quantiles || !(minimum_scale > 0))
+        return TSB_ERR_ARG;
+    const size_t per_row = 3 * (size_t(length / patch_size) + size_t(patches)) + 2 * size_t(patch_size) + 2 * size_t(patches);
+    double* scratch = nullptr;
+    if (cudaMalloc(&scratch, per_row * size_t(rows) * sizeof(double)) != cudaSuccess) return TSB_ERR_CUDA;
+    tsb::RowConfig rc;
+    std::memset(&rc, 0, sizeof(rc));
+    rc.ps = patch_size;
+    rc.minimum_scale = minimum_scale;
+    rc.Q = num_quantiles;
+    rc.median = median_index;
+    const double clip = std::pow(double(FLT_MAX), 0.5) / 1e3;
+    cudaError_t e = tsb::refine(rc, d_q, d_rows, d_mask, length, d_role, d_loc0, d_scale0, rows, length, patches, clip,
+                                scratch, d_out, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(scratch);
+    return e == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
 }

@@ -367,6 +367,17 @@ TIMESTRAL_API int tsb_fused_norm(timestral_ctx* c, int32_t mode) {
     return TSB_OK;
 }
 
+TIMESTRAL_API int tsb_attention_kernels(timestral_ctx* c, int32_t mode) {
+    if (!c || mode < 0 || mode > 1) return TSB_ERR_ARG;
+    try {
+        c->forecaster.engine().attention_kernels(mode);
+    } catch (...) {
+        caught(c);
+        return TSB_ERR_CUDA;
+    }
+    return TSB_OK;
+}
+
 TIMESTRAL_API int tsb_graph_replay(timestral_ctx* c, int32_t on) {
     if (!c) return TSB_ERR_ARG;
     try {

@@ -66,12 +66,14 @@ SIGNATURES = {
     "tsb_covariate_assembly": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_graph_replay": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_fused_norm": (C.c_int, [C.c_void_p, C.c_int32]),
+    "tsb_attention_kernels": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_test_scale_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_double] + [C.c_int32] * 6
                             + [C.c_void_p] * 8),
     "tsb_test_attention_time_ex": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 9 + [C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
     "tsb_test_split_f16": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p]),
     "tsb_test_attention_variate": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 5),
     "tsb_test_rms": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_float, C.c_void_p, C.c_int32]),
+    "tsb_test_refine": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 6 + [C.c_double, C.c_void_p]),
     "tsb_refine_static": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 6 + [C.c_double, C.c_void_p, C.c_void_p]),
 }
 
@@ -181,6 +183,12 @@ class Model:
         """RMSNorm carried by the GEMMs: 1 (default), 0 off, 2 on with a forced fallback run."""
         if lib().tsb_fused_norm(self.h, int(mode)) != 0:
             raise RuntimeError("tsb_fused_norm failed")
+
+    def attention_kernels(self, mode: int):
+        """Tensor-core path attention: 0 tensor-core kernels (default), 1 CUDA-core kernels with
+        the reference's float64 q.k dots and f32 softmax on the same f16 q/k/v."""
+        if lib().tsb_attention_kernels(self.h, int(mode)) != 0:
+            raise RuntimeError("tsb_attention_kernels failed")
 
     def graph_replay(self, on: bool):
         """CUDA-graph replay of repeated single-block forecasts (on by default)."""
