@@ -10,9 +10,11 @@ Tolerances:
     A good mean could hide a few bad series, so every target row's own mean is also held to
     3x the bound and every single value to 30x it (F16_ROW_FACTOR, F16_VALUE_FACTOR).
   * Q8_0 weights: against the oracle's F32 forecast of the same model, as the reference
-    reports its Q8_0 quality (docs/quantization-209m-result.md:23: mean 0.005658 against F32),
-    and against the oracle's Q8_0 restatement (activations quantised per 32-block, as ggml
-    does); the device path dequantises the weights to F16 and keeps F16 activations.
+    reports its Q8_0 quality (docs/quantization-209m-result.md:23: mean 0.005658 against F32
+    on the trained model). The bound is the reference's own Q8_0 arithmetic on the same
+    random-init model and inputs: the device forecast is no further from F32 than the
+    oracle's restatement of ggml's Q8_0 path (activations quantised per 32-block). The device
+    path dequantises the weights to F16 and keeps F16 activations.
 """
 import numpy as np
 import pytest
@@ -27,8 +29,7 @@ F32_RTOL, F32_ATOL = 1e-3, 1e-4
 F16_MEAN_ND = 1e-3
 F16_ROW_FACTOR = 3.0      # each target row's mean deviation <= 3 x the mean bound
 F16_VALUE_FACTOR = 30.0   # each value's deviation <= 30 x the mean bound
-Q8_F32_MEAN_ND = 0.011    # device Q8_0 against F32: within 2x the reference's published 0.005658
-REFERENCE_Q8_F32 = 0.005658
+REFERENCE_Q8_F32 = 0.005658   # the reference's published Q8_0 vs F32 mean (trained model)
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -288,9 +289,13 @@ def test_209m_attention_share():
 def test_209m_q8_against_f32():
     """Q8_0 quality as the reference reports it: the Q8_0 forecast against the F32 forecast of
     the same seed-0 weights (cfg2 shape), beside the reference's published mean 0.005658 for
-    its own Q8_0 path (a trained model on its evaluation data). Also printed: the oracle's
-    restatement of ggml's Q8_0 arithmetic (activations quantised per 32-block) against F32,
-    the device F16 forecast against F32, and the device Q8_0 against the oracle's Q8_0."""
+    its own Q8_0 path (a trained model on its evaluation data). The random-init 24-layer model
+    amplifies any perturbation far more than the trained one (rounding only q/k/v to f16 moves
+    the oracle's own F16 forecast by ~7e-4, test_209m_attention_share), so the bound is the
+    reference's Q8_0 arithmetic on this model: the oracle's restatement of ggml's Q8_0 path
+    (activations quantised per 32-block) against F32. The device (F16 activations) must be no
+    further from F32 than that, in the mean, the worst row and the worst value. Also printed:
+    the device F16 forecast against F32 and the device Q8_0 against the oracle's Q8_0."""
     q8, o8 = models(sy.spec_209m(), "q8_0")
     assert q8.tensor_core_path
     f16, _ = models(sy.spec_209m(), "f16")
@@ -305,9 +310,8 @@ def test_209m_q8_against_f32():
     for k, (mean, row, mx) in rows.items():
         print(f"{k:>38}: mean {mean:.3e} worst row {row:.3e} worst value {mx:.3e}")
     print(f"{'reference Q8_0 vs F32 (published)':>38}: mean {REFERENCE_Q8_F32:.3e}")
-    mean, row, mx = rows["device Q8_0 vs F32"]
-    assert mean <= Q8_F32_MEAN_ND, mean
-    assert row <= F16_ROW_FACTOR * Q8_F32_MEAN_ND and mx <= F16_VALUE_FACTOR * Q8_F32_MEAN_ND, (row, mx)
+    dev, ggml = rows["device Q8_0 vs F32"], rows["oracle Q8_0 (ggml arithmetic) vs F32"]
+    assert all(d <= g for d, g in zip(dev, ggml)), (dev, ggml)
     assert rows["device F16 vs F32"][0] <= F16_MEAN_ND
 
 
