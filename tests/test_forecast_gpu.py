@@ -104,6 +104,21 @@ def test_tiny_f32_flags_and_mask():
     check_f32(m.forecast(x, 16, max_context=48), o.forecast(x, 16, max_context=48))
 
 
+def test_tiny_f32_max_context_multi_block():
+    """A context cap below the model's context length, over several decode blocks: each block
+    slides the context back to the cap in whole patches (reference src/forecaster.cpp
+    decode_impl, keep = joined > cap ? ...), with and without covariates."""
+    m, o = models(sy.spec_tiny(), "f32")
+    x = random_context(2, 2, 100, seed=41)
+    check_f32(m.forecast(x, 200, max_context=48), o.forecast(x, 200, max_context=48))
+    rng = np.random.default_rng(42)
+    B, V, T, H = 2, 1, 90, 100
+    x = random_context(B, V, T, seed=43)
+    kw = dict(past=rng.standard_normal((B, 1, T)).astype(np.float32),
+              known=rng.standard_normal((B, 1, T + H)).astype(np.float32))
+    check_f32(m.forecast(x, H, max_context=40, **kw), o.forecast(x, H, max_context=40, **kw))
+
+
 def test_tiny_f32_covariates():
     m, o = models(sy.spec_tiny(), "f32")
     rng = np.random.default_rng(11)

@@ -121,12 +121,30 @@ struct Engine::Impl {
         int B = 0, V = 0, T = 0, H = 0;
         bool sym = false, clip = false;
         void* out = nullptr;
-        int kept = 0, len = 0, patches = 0, shot = 0, R = 0, R2 = 0;
+        int kept = 0, len = 0, patches = 0, shot = 0, R = 0, R2 = 0, cap = 0;
     } pending;
     bool fuse = true;            // allowed
     bool fuse_now = true;        // used by the running forecast
     bool force_fallback = false; // test hook: treat every fused forecast as flagged
     bool attn_simt = false;      // tensor-core path: attention on the CUDA-core kernels
+    const BlockObserver* observer = nullptr;
+    int shot_override = 0;       // patches per decode block (0: the model's)
+    double cap_override = -1;    // cap factor (negative: the model's)
+    int shot() const { return std::min(shot_override ? shot_override : (mv.per_shot ? mv.per_shot : 32), mv.block_size); }
+    double cap_k() const { return cap_override >= 0 ? cap_override : mv.cap_k; }
+    // Hands one finished decode block to the observer (device pointers, stream synchronised).
+    void observe(int offset, int block, int Tc, int R2, int64_t ctx_stride, const float* fut, const int8_t* fmask,
+                 int64_t fut_stride) {
+        if (!observer || !observer->after) return;
+        check(cudaStreamSynchronize(s), "sync");
+        BlockView v;
+        v.offset = offset; v.patches = block; v.length = Tc; v.rows = R2;
+        v.context = win.as<float>(); v.mask = wmask.as<int8_t>(); v.context_stride = ctx_stride;
+        v.future = fut; v.future_mask = fmask; v.future_stride = fut_stride;
+        v.predicted = qout.as<float>(); v.refined = refined.as<float>();
+        v.loc = aloc.as<float>(); v.scale = ascale.as<float>();
+        observer->after(v);
+    }
     const __half* a_in = nullptr;
     const float* ssq_in = nullptr;
     bool produce16 = false;
@@ -138,11 +156,12 @@ struct Engine::Impl {
     // the same shapes, flags and device buffers is captured, later ones replay the graph.
     struct GraphKey {
         const void* ctx = nullptr; const void* umask = nullptr; void* out = nullptr;
-        int B = 0, V = 0, T = 0, H = 0, max_context = 0;
+        int B = 0, V = 0, T = 0, H = 0, max_context = 0, shot = 0;
+        double cap_k = 0;
         bool sym = false, clip = false;
         bool operator==(const GraphKey& o) const {
             return ctx == o.ctx && umask == o.umask && out == o.out && B == o.B && V == o.V && T == o.T && H == o.H &&
-                   max_context == o.max_context && sym == o.sym && clip == o.clip;
+                   max_context == o.max_context && sym == o.sym && clip == o.clip && shot == o.shot && cap_k == o.cap_k;
         }
     };
     bool graphs = true;
@@ -827,14 +846,15 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
     if (cap > mv.context_length) throw std::runtime_error("max_context exceeds stored position range");
     const int kept = std::min(T, cap), pad = (ps - kept % ps) % ps, len = kept + pad;
     const int patches = (H + ps - 1) / ps;
-    const int shot = std::min(mv.per_shot ? mv.per_shot : 32, mv.block_size);
+    const int shot = im.shot();
     const int R = B * V, R2 = symmetric ? 2 * R : R;
     const cudaStream_t s = stream_;
     const bool single = patches <= shot;
     Impl::GraphKey key;
     key.ctx = d_ctx; key.umask = d_umask; key.out = d_out;
     key.B = B; key.V = V; key.T = T; key.H = H; key.max_context = max_context; key.sym = symmetric; key.clip = clip;
-    const bool graphable = im.graphs && single && !im.timing;
+    key.shot = shot; key.cap_k = im.cap_k();
+    const bool graphable = im.graphs && single && !im.timing && !im.observer;
     // An earlier asynchronous forecast that carried the norm in the GEMMs is completed and
     // checked (and run again if flagged) before this one shares the flag.
     if (im.pending.valid && im.fuse_now) {
@@ -843,7 +863,7 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
         im.launches = 0;
     }
     im.fuse_now = im.fuse_allowed();
-    im.pending = Impl::Pending{true, d_ctx, d_umask, B, V, T, H, symmetric, clip, d_out, kept, len, patches, shot, R, R2};
+    im.pending = Impl::Pending{true, d_ctx, d_umask, B, V, T, H, symmetric, clip, d_out, kept, len, patches, shot, R, R2, cap};
     if (graphable && im.graph_exec && key == im.graph_key && im.graph_generation == g_workspace_generation.load()) {
         check(cudaGraphLaunch(im.graph_exec, s), "graph launch");
         im.launches = im.graph_launches;
@@ -859,7 +879,7 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
         check(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
     }
     try {
-        targets_body(d_ctx, d_umask, B, V, T, H, symmetric, clip, d_out, kept, len, patches, shot, R, R2);
+        targets_body(d_ctx, d_umask, B, V, T, H, symmetric, clip, d_out, kept, len, patches, shot, R, R2, cap);
     } catch (...) {
         if (capture) {
             cudaGraph_t g = nullptr;
@@ -898,7 +918,7 @@ void Engine::finish_targets() {
     im.fuse_now = false;
     try {
         targets_body(static_cast<const float*>(p.ctx), static_cast<const uint8_t*>(p.umask), p.B, p.V, p.T, p.H, p.sym,
-                     p.clip, static_cast<float*>(p.out), p.kept, p.len, p.patches, p.shot, p.R, p.R2);
+                     p.clip, static_cast<float*>(p.out), p.kept, p.len, p.patches, p.shot, p.R, p.R2, p.cap);
     } catch (...) {
         im.fuse_now = true;
         throw;
@@ -908,7 +928,7 @@ void Engine::finish_targets() {
 }
 
 void Engine::targets_body(const float* d_ctx, const uint8_t* d_umask, int B, int V, int T, int H, bool symmetric,
-                          bool clip, float* d_out, int kept, int len, int patches, int shot, int R, int R2) {
+                          bool clip, float* d_out, int kept, int len, int patches, int shot, int R, int R2, int cap) {
     Impl& im = *impl_;
     const ModelView& mv = im.mv;
     const int ps = im.ps, Q = im.Q;
@@ -926,15 +946,18 @@ void Engine::targets_body(const float* d_ctx, const uint8_t* d_umask, int B, int
     (void)T;
     while (done < patches) {
         const int block = std::min(shot, patches - done), n = block * ps, offset = done * ps;
+        if (im.observer && im.observer->before) im.observer->before(offset, block, Tc);
         // The V target rows of one series form one group (reference src/covariates.cpp:63).
         im.predict_block(R2, Tc, block, false, V, R, done == 0, len);
+        im.observe(offset, block, Tc, R2, Tc, nullptr, nullptr, 0);
         if (single) break;
         const int used = std::min(n, H - offset);
         check(cudaMemcpy2DAsync(im.decoded.as<float>() + size_t(offset) * Q, size_t(H) * Q * 4, im.refined.p,
                                 size_t(n) * Q * 4, size_t(used) * Q * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
         done += block;
         if (done >= patches) break;
-        const int joined = Tc + n, keep = joined > mv.context_length ? std::max(ps, (mv.context_length / ps) * ps) : joined;
+        // Slide to the request's context cap, whole patches (reference src/forecaster.cpp decode_impl).
+        const int joined = Tc + n, keep = joined > cap ? std::max(ps, (cap / ps) * ps) : joined;
         im.next_rows.ensure(size_t(R2) * keep * 4);
         im.next_mask.ensure(size_t(R2) * keep);
         im.run("feedback", [&] {
@@ -948,8 +971,10 @@ void Engine::targets_body(const float* d_ctx, const uint8_t* d_umask, int B, int
     const float* dec = single ? im.refined.as<float>() : im.decoded.as<float>();
     const int Hfull = single ? patches * ps : H;
     im.run("finalize", [&] {
-        return finalize(im.rc, dec, R, symmetric, B, V, V, H, Hfull, im.caplo.as<float>(), im.caphi.as<float>(),
-                        im.capsc.as<float>(), mv.cap_k > 0, clip ? im.clip_ok.as<int8_t>() : nullptr, d_out,
+        RowConfig rc = im.rc;
+        rc.cap_k = im.cap_k();
+        return finalize(rc, dec, R, symmetric, B, V, V, H, Hfull, im.caplo.as<float>(), im.caphi.as<float>(),
+                        im.capsc.as<float>(), rc.cap_k > 0, clip ? im.clip_ok.as<int8_t>() : nullptr, d_out,
                         im.err.as<int>(), s);
     });
 }
@@ -967,9 +992,58 @@ void Engine::attention_kernels(int mode) {
     impl_->have_last = false;
 }
 
+void Engine::set_observer(const BlockObserver* observer) {
+    impl_->observer = observer;
+    if (observer) impl_->have_last = false;
+}
+
+void Engine::set_overrides(int per_shot, double cap_k) {
+    impl_->shot_override = per_shot > 0 ? per_shot : 0;
+    impl_->cap_override = cap_k;
+}
+
 void Engine::graph_replay(bool on) {
     impl_->graphs = on;
     if (!on) { impl_->drop_graph(); impl_->have_last = false; }
+}
+
+void Engine::decode_host_rows(const HostRows& a, int H, float* h_decoded) {
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    Impl& im = *impl_;
+    if (im.pending.valid && im.fuse_now) {       // an earlier asynchronous forecast: complete it
+        check(cudaStreamSynchronize(stream_), "forecast");
+        finish_targets();
+    }
+    im.launches = 0;
+    im.pending.valid = false;
+    im.fuse_now = im.fuse_allowed();
+    const ModelView& mv = im.mv;
+    const int R = a.R, T = a.T;
+    const bool cov = a.roles != nullptr && mv.covariate_enabled;
+    const cudaStream_t s = stream_;
+    if (cov) {
+        std::vector<int8_t> role(R);
+        for (int r = 0; r < R; ++r) role[r] = int8_t(a.roles[r]);
+        im.role.ensure(R);
+        check(cudaMemcpyAsync(im.role.p, role.data(), R, cudaMemcpyHostToDevice, s), "upload roles");
+        check(cudaStreamSynchronize(s), "sync");
+    }
+    if (a.future) {
+        im.future.ensure(size_t(R) * a.Hh * 4); im.fmask.ensure(size_t(R) * a.Hh);
+        check(cudaMemcpyAsync(im.future.p, a.future, size_t(R) * a.Hh * 4, cudaMemcpyHostToDevice, s), "upload");
+        check(cudaMemcpyAsync(im.fmask.p, a.future_mask, size_t(R) * a.Hh, cudaMemcpyHostToDevice, s), "upload");
+    }
+    im.rows.ensure(size_t(R) * T * 4); im.mask.ensure(size_t(R) * T);
+    check(cudaMemcpyAsync(im.rows.p, a.rows, size_t(R) * T * 4, cudaMemcpyHostToDevice, s), "upload");
+    check(cudaMemcpyAsync(im.mask.p, a.mask, size_t(R) * T, cudaMemcpyHostToDevice, s), "upload");
+    decode_rows(0, 0, H, R, T, a.Hh, false, false, cov, a.future != nullptr, a.group_rows,
+                a.cap ? a.cap : mv.context_length, nullptr, h_decoded);
+    if (im.fuse_now && im.take_norm_flag()) {
+        const bool saved = im.fuse;
+        im.fuse = false;
+        try { decode_host_rows(a, H, h_decoded); } catch (...) { im.fuse = saved; throw; }
+        im.fuse = saved;
+    }
 }
 
 void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetric, bool clip, const float* ctx,
@@ -1029,7 +1103,7 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
         im.run("clip", [&] { return clip_eligibility(dctx.as<float>(), umask ? dum.as<uint8_t>() : nullptr, B * V, T_req, im.clip_ok.as<int8_t>(), s); });
         check(cudaStreamSynchronize(s), "sync");
     }
-    decode_rows(B, V, H, R, T, Hh, symmetric, clip, cov, a.future != nullptr, a.group_rows, h_out);
+    decode_rows(B, V, H, R, T, Hh, symmetric, clip, cov, a.future != nullptr, a.group_rows, a.cap ? a.cap : mv.context_length, h_out, nullptr);
     if (im.fuse_now && im.take_norm_flag()) {
         const bool saved = im.fuse;
         im.fuse = false;
@@ -1096,7 +1170,7 @@ void Engine::forecast_covariates(const CovRequest& q, bool symmetric, bool clip,
                                     q.T, im.clip_ok.as<int8_t>(), s);
         });
     }
-    decode_rows(q.B, q.V, q.H, R, q.len, q.hor, symmetric, clip, cov, has_future, all, h_out);
+    decode_rows(q.B, q.V, q.H, R, q.len, q.hor, symmetric, clip, cov, has_future, all, q.cap ? q.cap : mv.context_length, h_out, nullptr);
     if (im.fuse_now && im.take_norm_flag()) {      // fallback: the whole request with RMSNorm kernels
         const bool saved = im.fuse;
         im.fuse = false;
@@ -1106,13 +1180,13 @@ void Engine::forecast_covariates(const CovRequest& q, bool symmetric, bool clip,
 }
 
 void Engine::decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetric, bool clip, bool cov,
-                         bool has_future, int group_rows, float* h_out) {
+                         bool has_future, int group_rows, int cap, float* h_out, float* h_decoded) {
     Impl& im = *impl_;
     const ModelView& mv = im.mv;
     const int ps = im.ps, Q = im.Q;
     const int R2 = symmetric ? 2 * R : R;
     const int patches = (H + ps - 1) / ps;
-    const int shot = std::min(mv.per_shot ? mv.per_shot : 32, mv.block_size);
+    const int shot = im.shot();
     const cudaStream_t s = stream_;
     im.decoded.ensure(size_t(R2) * H * Q * 4);
     int Tc = T, done = 0;
@@ -1129,13 +1203,16 @@ void Engine::decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetr
             check(cudaMemcpy2DAsync(im.win.as<float>() + Tc, size_t(W) * 4, im.future.as<float>() + offset, size_t(Hh) * 4, size_t(n) * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
             check(cudaMemcpy2DAsync(im.wmask.as<int8_t>() + Tc, W, im.fmask.as<int8_t>() + offset, Hh, n, R2, cudaMemcpyDeviceToDevice, s), "copy");
         }
+        if (im.observer && im.observer->before) im.observer->before(offset, block, Tc);
         im.predict_block(R2, Tc, block, cov, group_rows, R, done == 0, Tc);
+        im.observe(offset, block, Tc, R2, W, has_future ? im.future.as<float>() + offset : nullptr,
+                   has_future ? im.fmask.as<int8_t>() + offset : nullptr, Hh);
         const int used = std::min(n, H - offset);
         check(cudaMemcpy2DAsync(im.decoded.as<float>() + size_t(offset) * Q, size_t(H) * Q * 4, im.refined.p,
                                 size_t(n) * Q * 4, size_t(used) * Q * 4, R2, cudaMemcpyDeviceToDevice, s), "copy");
         done += block;
         if (done >= patches) break;
-        const int joined = Tc + n, keep = joined > mv.context_length ? std::max(ps, (mv.context_length / ps) * ps) : joined;
+        const int joined = Tc + n, keep = joined > cap ? std::max(ps, (cap / ps) * ps) : joined;
         im.next_rows.ensure(size_t(R2) * keep * 4);
         im.next_mask.ensure(size_t(R2) * keep);
         // future slice of this block, row stride n
@@ -1156,13 +1233,22 @@ void Engine::decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetr
         std::swap(im.mask.p, im.next_mask.p); std::swap(im.mask.bytes, im.next_mask.bytes);
         Tc = keep;
     }
+    if (h_decoded) {                             // decode only: [R2][H][Q] before cap and combine
+        check(cudaMemcpyAsync(h_decoded, im.decoded.p, size_t(R2) * H * Q * 4, cudaMemcpyDeviceToHost, s), "download");
+        check(cudaStreamSynchronize(s), "sync");
+        last_launches_ = im.launches;
+        im.check_device_error("decode");
+        return;
+    }
     DevBuf& dout = im.out_rows;
     dout.ensure(size_t(B) * V * H * Q * 4);
     const int all = R / B;
     // Cap statistics come from the first block's scale pass over the assembled context.
     im.run("finalize", [&] {
-        return finalize(im.rc, im.decoded.as<float>(), R, symmetric, B, V, all, H, H, im.caplo.as<float>(),
-                        im.caphi.as<float>(), im.capsc.as<float>(), mv.cap_k > 0, clip ? im.clip_ok.as<int8_t>() : nullptr,
+        RowConfig rc = im.rc;
+        rc.cap_k = im.cap_k();
+        return finalize(rc, im.decoded.as<float>(), R, symmetric, B, V, all, H, H, im.caplo.as<float>(),
+                        im.caphi.as<float>(), im.capsc.as<float>(), rc.cap_k > 0, clip ? im.clip_ok.as<int8_t>() : nullptr,
                         dout.as<float>(), im.err.as<int>(), s);
     });
     check(cudaMemcpyAsync(h_out, dout.p, size_t(B) * V * H * Q * 4, cudaMemcpyDeviceToHost, s), "download");

@@ -51,6 +51,7 @@ struct HostRows {
     const float* future = nullptr;            // [R][Hh] or null
     const int8_t* future_mask = nullptr;
     int group_rows = 1;                       // rows per series (contiguous)
+    int cap = 0;                              // context cap of the decode slide (0: the model's)
 };
 
 // A covariate request as the caller holds it (reference ForecastRequest fields), assembled
@@ -67,6 +68,32 @@ struct CovRequest {
     const double* cat_known = nullptr;
     int kept = 0, len = 0, hor = 0;
     double smooth = 0;
+    int cap = 0;                              // context cap of the decode slide (0: the model's)
+};
+
+// One decode block as the device holds it right after its prediction and refinement, for
+// callers that trace a forecast (reference ForecastTrace / DecodeBlock,
+// src/forecaster.hpp:24-38). Device pointers, valid until the next block starts; rows are
+// both symmetric passes when the forecast is mirrored (positive pass first).
+struct BlockView {
+    int offset = 0, patches = 0, length = 0;     // first step, patches, context steps of the block
+    int rows = 0;
+    const float* context = nullptr;              // [rows][context_stride], first `length` steps used
+    const int8_t* mask = nullptr;                // same layout
+    int64_t context_stride = 0;
+    const float* future = nullptr;               // [rows][future_stride] from the block's first step, or null
+    const int8_t* future_mask = nullptr;
+    int64_t future_stride = 0;
+    const float* predicted = nullptr;            // [rows][patches * patch_size][Q] before refinement
+    const float* refined = nullptr;              // [rows][patches * patch_size][Q]
+    const float* loc = nullptr;                  // [rows] frame of the block's last context step
+    const float* scale = nullptr;
+};
+struct BlockObserver {
+    // Called before each block's prediction with (first step, patches, context steps).
+    std::function<void(int, int, int)> before;
+    // Called after each block's refinement, with the engine stream synchronised.
+    std::function<void(const BlockView&)> after;
 };
 
 class Engine {
@@ -90,6 +117,9 @@ public:
                        const uint8_t* umask, int T_req, float* h_out);
     // Requests with covariates assembled on the device (host buffers in and out).
     void forecast_covariates(const CovRequest& q, bool symmetric, bool clip, float* h_out);
+    // Decode of assembled rows of one pass (reference Forecaster::decode): every block with
+    // median feedback and refinement, no cap, symmetric average or clip; h_decoded [R][H][Q].
+    void decode_host_rows(const HostRows& a, int H, float* h_decoded);
 
     // CUDA-graph replay of single-block forecasts without covariates (on by default): the
     // second call with the same shapes, flags and device buffers is captured into a graph,
@@ -107,6 +137,13 @@ public:
     // the variate axis. Mode 1 isolates the tensor-core attention's share of the deviation
     // from the reference's f32 attention.
     void attention_kernels(int mode);
+    // Observe every decode block of the following forecasts (nullptr: none). While an
+    // observer is set, forecasts are not captured into or replayed from CUDA graphs.
+    void set_observer(const BlockObserver* observer);
+    // Per-request overrides (reference ForecastRequest::per_shot_horizon_patches and
+    // quantile_real_cap_k): patches per decode block (0: the model's) and the cap factor
+    // (negative: the model's; 0 disables the cap).
+    void set_overrides(int per_shot, double cap_k);
 
     // Synchronise the stream and turn a device error word into an exception.
     void check_errors();
@@ -125,11 +162,11 @@ public:
 private:
     void finish_targets();
     void targets_body(const float* d_ctx, const uint8_t* d_umask, int B, int V, int T, int H, bool symmetric, bool clip,
-                      float* d_out, int kept, int len, int patches, int shot, int R, int R2);
+                      float* d_out, int kept, int len, int patches, int shot, int R, int R2, int cap);
     // The decode blocks of an assembled covariate request (rows, masks, roles, futures in
     // device memory) through the final download.
     void decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetric, bool clip, bool cov, bool has_future,
-                     int group_rows, float* h_out);
+                     int group_rows, int cap, float* h_out, float* h_decoded);
     struct Impl;
     std::unique_ptr<Impl> impl_;
     int device_ = 0;

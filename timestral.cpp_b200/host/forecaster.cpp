@@ -373,26 +373,171 @@ void Forecaster::forecast_targets(const float* context, const uint8_t* mask, siz
     }
 }
 
-Forecast Forecaster::forecast(const ForecastRequest& r) {
+namespace {
+
+// Per-call engine settings (request overrides, block observer), undone when the call ends.
+struct CallScope {
+    tsb::Engine& eng;
+    CallScope(tsb::Engine& e, int per_shot, double cap_k, const tsb::BlockObserver* observer) : eng(e) {
+        eng.set_overrides(per_shot, cap_k);
+        eng.set_observer(observer);
+    }
+    ~CallScope() {
+        eng.set_observer(nullptr);
+        eng.set_overrides(0, -1);
+    }
+};
+
+// Rows [r0, r0 + n) of a [rows][stride] device matrix of `width` used columns, to the host.
+template <class T>
+std::vector<T> download_rows(const T* d, int64_t stride, size_t r0, size_t n, size_t width) {
+    std::vector<T> out(n * width);
+    if (!n || !width) return out;
+    cuda_check(cudaMemcpy2D(out.data(), width * sizeof(T), d + int64_t(r0) * stride, size_t(stride) * sizeof(T),
+                            width * sizeof(T), n, cudaMemcpyDeviceToHost),
+               "download trace");
+    return out;
+}
+
+// One pass's rows of an observed block as the reference's DecodeBlock.
+DecodeBlock block_of(const tsb::BlockView& v, size_t r0, size_t rows, size_t ps, size_t Q) {
+    DecodeBlock b;
+    const size_t n = size_t(v.patches) * ps;
+    b.offset = size_t(v.offset); b.patches = size_t(v.patches); b.length = size_t(v.length);
+    b.context = download_rows(v.context, v.context_stride, r0, rows, size_t(v.length));
+    b.mask = download_rows(v.mask, v.context_stride, r0, rows, size_t(v.length));
+    if (v.future) {
+        b.future = download_rows(v.future, v.future_stride, r0, rows, n);
+        b.future_mask = download_rows(v.future_mask, v.future_stride, r0, rows, n);
+    }
+    b.predicted = download_rows(v.predicted, int64_t(n * Q), r0, rows, n * Q);
+    b.refined = download_rows(v.refined, int64_t(n * Q), r0, rows, n * Q);
+    return b;
+}
+
+}  // namespace
+
+Forecast Forecaster::forecast(const ForecastRequest& r, ForecastTrace* trace) {
     const Config& c = model_.config();
     Forecast f;
     f.batch = r.batch; f.targets = r.targets; f.horizon = r.horizon;
     f.quantile_levels = c.quantile_knots;
     f.quantiles.resize(mul(mul(mul(r.batch, r.targets), r.horizon), c.num_quantiles()));
-    forecast_into(r, f.quantiles.data());
+    forecast_into(r, f.quantiles.data(), trace);
     return f;
 }
 
-void Forecaster::forecast_into(const ForecastRequest& r, float* out) {
+std::vector<float> Forecaster::decode(const AssembledRows& a, size_t H, size_t cap, size_t shot,
+                                      std::vector<DecodeBlock>* trace, const DecodeProgress& progress) {
+    const Config& c = model_.config();
+    const size_t ps = c.patch_size, Q = c.num_quantiles(), R = a.rows_count, T = a.length;
+    const size_t cap_eff = cap ? cap : c.context_length;
+    const size_t shot_eff = std::min<size_t>(shot ? shot : c.per_shot_horizon_patches, c.block_size);
+    // The reference's checks (src/forecaster.cpp:21-27).
+    if (!H || !R || !T || T % ps || !shot_eff || !cap_eff || cap_eff > c.context_length || H > SIZE_MAX - (ps - 1))
+        throw Error("invalid decode dimensions");
+    if (a.rows.size() != mul(R, T) || a.mask.size() != a.rows.size() || a.groups.size() != R ||
+        (!a.roles.empty() && a.roles.size() != R))
+        throw Error("invalid decode rows");
+    const size_t patches = (H + ps - 1) / ps, full = mul(patches, ps);
+    if (a.horizon != full || a.future.size() != a.future_mask.size() || (!a.future.empty() && a.future.size() != mul(R, full)))
+        throw Error("invalid decode future");
+    for (int64_t role : a.roles)
+        if (role < 0 || role > 2) throw Error("invalid decode role");
+    // The device keeps the rows of a group contiguous and of one size (as assemble_rows lays
+    // them out: group b holds rows [b * all, (b + 1) * all)).
+    size_t group_rows = 1;
+    while (group_rows < R && a.groups[group_rows] == a.groups[0]) ++group_rows;
+    if (R % group_rows) throw Error("decode rows: groups must be contiguous runs of equal size");
+    for (size_t r = 0; r < R; ++r)
+        if (a.groups[r] != a.groups[(r / group_rows) * group_rows] ||
+            (r % group_rows == 0 && r && a.groups[r] == a.groups[r - 1]))
+            throw Error("decode rows: groups must be contiguous runs of equal size");
+    if (R > size_t(INT32_MAX) / 2 || T > size_t(INT32_MAX) || full > size_t(INT32_MAX) || H > size_t(INT32_MAX))
+        throw Error("forecast dimensions exceed the device path limits");
+    if (trace) trace->clear();
+    tsb::HostRows h;
+    h.R = int(R); h.T = int(T); h.Hh = int(full);
+    h.rows = a.rows.data(); h.mask = a.mask.data();
+    h.roles = a.roles.empty() ? nullptr : a.roles.data();
+    h.future = a.future.empty() ? nullptr : a.future.data();
+    h.future_mask = a.future_mask.empty() ? nullptr : a.future_mask.data();
+    h.group_rows = int(group_rows);
+    h.cap = int(cap_eff);
+    tsb::BlockObserver obs;
+    if (progress) obs.before = [&](int offset, int block, int length) {
+        if (offset == 0 && trace) trace->clear();      // a fallback run starts again
+        progress(size_t(offset), size_t(block), size_t(length));
+    };
+    else if (trace) obs.before = [&](int offset, int, int) { if (offset == 0) trace->clear(); };
+    if (trace) obs.after = [&](const tsb::BlockView& v) { trace->push_back(block_of(v, 0, R, ps, Q)); };
+    std::vector<float> out(mul(mul(R, H), Q));
+    tsb::Engine& eng = *engine_;
+    try {
+        CallScope scope(eng, int(shot_eff), -1, (trace || progress) ? &obs : nullptr);
+        eng.decode_host_rows(h, int(H), out.data());
+    } catch (const Error&) {
+        throw;
+    } catch (const std::exception& e) {
+        throw Error(e.what());
+    }
+    return out;
+}
+
+void Forecaster::forecast_into(const ForecastRequest& r, float* out, ForecastTrace* trace) {
     const Config& c = model_.config();
     const size_t Q = c.num_quantiles();
+    if (trace) { trace->initial_anchors.reset(); trace->positive.clear(); trace->negative.clear(); }
     const bool sym = r.symmetric_averaging.value_or(c.symmetric_averaging);
     const bool clip = r.clip_nonnegative.value_or(c.clip_nonnegative);
-    if (r.quantile_real_cap_k && *r.quantile_real_cap_k != c.quantile_real_cap_k)
-        throw Error("quantile_real_cap_k overrides are not supported by the device path");
-    if (r.per_shot_horizon_patches && r.per_shot_horizon_patches != c.per_shot_horizon_patches)
-        throw Error("per_shot_horizon_patches overrides are not supported by the device path");
+    const double cap_k = r.quantile_real_cap_k.value_or(c.quantile_real_cap_k);
+    if (!std::isfinite(cap_k)) throw Error("invalid quantile cap");
     if (!r.batch || !r.targets || !r.length || !r.horizon) throw Error("invalid row dimensions");
+    const size_t shot = std::min<size_t>(r.per_shot_horizon_patches ? r.per_shot_horizon_patches : c.per_shot_horizon_patches,
+                                 c.block_size);
+    if (!shot) throw Error("invalid decode dimensions");
+    // Trace: the observer splits each block's rows into the two passes (positive first).
+    const size_t all = r.targets + r.past_count + r.categorical_past_count + r.known_count + r.categorical_known_count;
+    std::optional<ForecastAnchors> anchors;
+    tsb::BlockObserver obs;
+    if (trace) {
+        if (trace->capture_initial_anchors) anchors = ForecastAnchors{r.batch, r.targets, {}, {}};
+        obs.before = [&, trace](int offset, int block, int length) {
+            if (offset == 0) { trace->positive.clear(); trace->negative.clear(); }   // a fallback run starts again
+            if (trace->before_block) {
+                trace->before_block(size_t(offset), size_t(block), size_t(length));
+                if (sym) trace->before_block(size_t(offset), size_t(block), size_t(length));
+            }
+        };
+        obs.after = [&, trace](const tsb::BlockView& v) {
+            const size_t rows = size_t(v.rows) / (sym ? 2 : 1), ps = c.patch_size;
+            if (trace->capture_blocks) {
+                trace->positive.push_back(block_of(v, 0, rows, ps, Q));
+                if (sym) trace->negative.push_back(block_of(v, rows, rows, ps, Q));
+            }
+            if (anchors && v.offset == 0) {
+                const std::vector<float> loc = download_rows(v.loc, 1, 0, rows, 1);
+                const std::vector<float> scale = download_rows(v.scale, 1, 0, rows, 1);
+                anchors->loc.resize(mul(r.batch, r.targets));
+                anchors->scale.resize(anchors->loc.size());
+                for (size_t b = 0; b < r.batch; ++b)
+                    for (size_t v2 = 0; v2 < r.targets; ++v2) {
+                        const float l = loc[b * all + v2], sc = scale[b * all + v2];
+                        if (!std::isfinite(l) || !std::isfinite(sc) || sc <= 0) throw Error("invalid initial anchor");
+                        anchors->loc[b * r.targets + v2] = l;
+                        anchors->scale[b * r.targets + v2] = sc;
+                    }
+            }
+        };
+    }
+    CallScope scope(*engine_, int(shot), cap_k, trace ? &obs : nullptr);
+    forecast_request(r, out, sym, clip);
+    if (trace && anchors) trace->initial_anchors = std::move(anchors);
+}
+
+void Forecaster::forecast_request(const ForecastRequest& r, float* out, bool sym, bool clip) {
+    const Config& c = model_.config();
+    const size_t Q = c.num_quantiles();
     if (sym)
         for (size_t i = 0; i < Q; ++i)
             if (std::abs(c.quantile_knots[i] + c.quantile_knots[Q - 1 - i] - 1) >= 1e-9)
@@ -429,6 +574,7 @@ void Forecaster::forecast_into(const ForecastRequest& r, float* out) {
         q.cat_past = r.categorical_past.data(); q.cat_known = r.categorical_known.data();
         q.kept = int(g.kept); q.len = int(g.len); q.hor = int(g.hor);
         q.smooth = c.target_encoding_smooth;
+        q.cap = int(r.max_context ? r.max_context : c.context_length);
         try {
             eng.forecast_covariates(q, sym, clip, out);
         } catch (const Error&) {
@@ -448,6 +594,7 @@ void Forecaster::forecast_into(const ForecastRequest& r, float* out) {
     h.future = a.future.empty() ? nullptr : a.future.data();
     h.future_mask = a.future_mask.empty() ? nullptr : a.future_mask.data();
     h.group_rows = int(a.rows_count / r.batch);
+    h.cap = int(r.max_context ? r.max_context : c.context_length);
     std::vector<uint8_t> um(r.observation_mask.begin(), r.observation_mask.end());
     try {
         eng.forecast_rows(h, int(r.batch), int(r.targets), int(r.horizon), sym, clip, r.context.data(),

@@ -60,10 +60,10 @@ struct TensorSpec {
 };
 
 // The config of a parsed GGUF (reference src/model_loader.cpp:72-160). Throws ts::Error.
-Config read_config(const GgufFile& g);
+TS_API Config read_config(const GgufFile& g);
 // The tensors a file with this config must contain, in file order
 // (reference src/model_loader.cpp:166-207).
-std::vector<TensorSpec> expected_schema(const Config& c);
+TS_API std::vector<TensorSpec> expected_schema(const Config& c);
 // Storage policy (reference src/weight_policy.hpp:8-22): F32 everywhere, F16/Q8_0/K-quants
 // only on the projection weights of the allowlist.
 bool reduced_weight_name(const std::string& name);
@@ -76,7 +76,7 @@ struct TensorRef {
     size_t bytes = 0;
 };
 
-class Model {
+class TS_API Model {
 public:
     // Load `path`; weights stay in the read-only mapping. Throws ts::Error.
     static Model load(const std::string& path);
