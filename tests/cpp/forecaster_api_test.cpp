@@ -133,7 +133,7 @@ void run(const ts::Model& m, ts::Forecaster& fc, timestral_ctx* h, bool covariat
     check(same_bytes(plain.quantiles, light.quantiles), "anchor-only output");
     check(only.positive.empty() && only.negative.empty() && count == progress, "anchor-only blocks and progress");
     check(only.initial_anchors && captured.initial_anchors, "anchor presence");
-    const auto& anchor = *only.initial_anchors;
+    const ts::ForecastAnchors anchor = *only.initial_anchors;   // a copy: `only` is reused below
     check(anchor.batch == r.batch && anchor.targets == r.targets, "anchor dimensions");
     check(same_bytes(anchor.loc, captured.initial_anchors->loc) && same_bytes(anchor.scale, captured.initial_anchors->scale),
           "anchor modes");
