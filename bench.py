@@ -51,7 +51,7 @@ CONFIGS = {
                  desc="cfg3: 209M f16 random-init, B=16, V=32, T=1024, H=128, VAR(1)"),
     "cfg4": dict(weights="f16", B=32, V=4, T=1024, H=96, cpu_sample=1,
                  desc="cfg4: 209M f16 random-init, B=32, V=4, T=1024, H=96, 8 past + 4 known + 2 categorical covariates"),
-    "cfg5": dict(weights=None, B=4096, V=1, T=2048, H=256, cpu_sample=48,
+    "cfg5": dict(weights=None, B=4096, V=1, T=2048, H=256, cpu_sample=16,
                  desc="cfg5 throughput: 209M {w} random-init, B={B} series ({per} per GPU), V=1, T=2048, H=256, symmetric+clip"),
     "cfg6": dict(weights="f16", B=64, V=1, T=32768, H=1024, cpu_sample=1,
                  desc="cfg6 long context: 209M f16 random-init, B=64, V=1, T=32768 (the full 1024-patch context), "
@@ -82,6 +82,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     a = ap.parse_args()
     c = dict(CONFIGS[a.config])
+    c.setdefault("cpu_sample_1t", 1)
     if c["weights"] is None:
         c["weights"] = a.weights
     if a.batch:
@@ -219,22 +220,62 @@ def model_path(weights: str, rank: int, dist):
     return sy.cached_model(sy.spec_209m(), weights)
 
 
-def cpu_baseline(cfg: str, c: dict):
-    """The CPU oracle on `cpu_sample` series of the same workload, all host threads."""
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def oracle_runs(cfg: str, c: dict, sample: int, threads: int, repeats: int):
+    """Seconds of `repeats` timed calls of the CPU oracle (the port of the reference's
+    forecast path) on the first `sample` series of the workload, after one untimed call."""
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle_py as op
     from timestral_b200 import synthetic as sy
     m = op.OracleModel(sy.cached_model(sy.spec_209m(), c["weights"]))
-    sample = c["cpu_sample"]
     x, kw = workload(cfg, c, 0, sample)
-    threads = os.cpu_count() or 1
     m.forecast(x[:1], c["H"], threads=threads, **{k: v[:1] for k, v in kw.items()})   # warm caches
-    t0 = time.perf_counter()
-    m.forecast(x, c["H"], threads=threads, **kw)
-    dt = time.perf_counter() - t0
-    return {"value": sample / dt, "unit": "series/s", "cores": threads, "kind": "port",
-            "sample": f"{sample} series of the same workload ({c['weights']} 209M, V={c['V']}, T={c['T']}, "
-                      f"H={c['H']}), one forecast call, {dt:.2f} s"}
+    out = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        m.forecast(x, c["H"], threads=threads, **kw)
+        out.append(time.perf_counter() - t0)
+    return out
+
+
+def _cpu_child(cfg, c, plan, q):
+    import resource
+    res = []
+    for sample, threads, repeats in plan:
+        res.append((sample, threads, oracle_runs(cfg, c, sample, threads, repeats)))
+    q.put((res, resource.getrusage(resource.RUSAGE_SELF).ru_maxrss * 1024))
+
+
+def cpu_baseline(cfg: str, c: dict, repeats: int = 5):
+    """The CPU oracle on a bounded sample of the same workload, timed in a spawned child
+    process (its own peak RSS, no GPU state): all host threads on `cpu_sample` series and one
+    thread on `cpu_sample_1t` series, each the median of `repeats` calls after one warm-up."""
+    import multiprocessing as mp
+    threads = os.cpu_count() or 1
+    plan = [(c["cpu_sample"], threads, repeats), (c["cpu_sample_1t"], 1, repeats)]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_cpu_child, args=(cfg, c, plan, q))
+    p.start()
+    res, rss = q.get()
+    p.join()
+    (s_all, t_all, d_all), (s_one, _, d_one) = res
+    med_all, med_one = float(np.median(d_all)), float(np.median(d_one))
+    return {"value": s_all / med_all, "unit": "series/s", "cores": t_all, "kind": "port",
+            "sample": f"{s_all} series of the same workload ({c['weights']} 209M, V={c['V']}, T={c['T']}, "
+                      f"H={c['H']}) per call, median of {repeats} calls ({med_all:.2f} s) after one warm-up",
+            "one_thread": {"value": s_one / med_one, "unit": "series/s", "cores": 1,
+                           "sample": f"{s_one} series per call, median of {repeats} calls ({med_one:.2f} s)"},
+            "peak_rss_bytes": int(rss), "cpu_model": cpu_model()}
 
 
 def gemm_flops(rows: int, S: int, L: int, V_rows: int, decoder_tokens: int) -> int:
@@ -262,13 +303,16 @@ def main():
     if a.impl == "reference":
         if rank != 0:
             return 0
-        vals = [cpu_baseline(a.config, c) for _ in range(max(a.steps, 1))]
-        b = vals[0]
-        v = float(np.median([x["value"] for x in vals]))
-        b["value"] = v
+        threads = os.cpu_count() or 1
+        secs = oracle_runs(a.config, c, c["cpu_sample"], threads, max(a.steps, 1))
+        v = c["cpu_sample"] / float(np.median(secs))
+        b = {"value": v, "unit": "series/s", "cores": threads, "kind": "port", "cpu_model": cpu_model(),
+             "sample": f"{c['cpu_sample']} series of the same workload per step, median of {len(secs)} steps"}
+        # The port computes what the reference computes on this GGUF: F16 weights with
+        # activations rounded to F16 and F32 accumulation (ggml's F16 mul_mat), f32 elsewhere.
         print(json.dumps({"impl": "reference", "metric": metric, "value": v, "unit": "series/s", "n_gpus": a.gpus,
                           "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "strong",
-                          "dtype": "f32", "data": "synthetic",
+                          "dtype": c["weights"], "data": "synthetic",
                           "config": {"workload": f"{a.config} 209M {c['weights']} B={c['B']} V={c['V']} T={c['T']} "
                                                  f"H={c['H']} (CPU sample)"},
                           "cpu_baseline": b,
@@ -351,32 +395,59 @@ def main():
     gemm_ms, gemm_n = model.timing_read("gemm")
     all_ms, all_n = model.timing_read("all")
     model.timing(False)
-    # End to end through the public C ABI with host buffers.
-    e2e = None
+    # End to end through the public C ABI with host buffers: the context from page-locked
+    # memory (e2e) and from ordinary pageable memory (e2e_pageable); the result lands in the
+    # buffer the library returns. One GPU: this rank's handle. Several GPUs: rank 0 alone
+    # forecasts the whole batch through one handle over every rank's GPU (tsb_load_devices:
+    # series shards, one host thread and stream per GPU, each shard's result copied into its
+    # slice of the one output), while the other ranks wait on the host.
+    e2e = e2e_pageable = None
+    multi_note = None
     if not a.no_e2e:
-        model.forecast(hx, H, **kw)          # sizes the pinned staging buffers once, untimed
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-        t0 = time.perf_counter()
-        for _ in range(a.steps):
-            model.forecast(hx, H, **kw)
-        e2e = (time.perf_counter() - t0) / a.steps
-    stats = torch.tensor([ms, e2e or 0.0], device=dev, dtype=torch.float64)
+        def timed(fn):
+            fn()                              # sizes the staging buffers once, untimed
+            t0 = time.perf_counter()
+            for _ in range(a.steps):
+                fn()
+            return (time.perf_counter() - t0) / a.steps
+        if world == 1:
+            px = np.ascontiguousarray(x)
+            e2e = timed(lambda: model.forecast(hx, H, **kw))
+            e2e_pageable = timed(lambda: model.forecast(px, H, **kw))
+        else:
+            import datetime
+            host_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
+            dist.barrier(group=host_group)
+            if rank == 0:
+                full_x, full_kw = workload(a.config, c, 0, B)
+                full_hx = torch.from_numpy(np.ascontiguousarray(full_x)).pin_memory().numpy()
+                multi = tb.Model(path, devices=list(range(world)))
+                e2e = timed(lambda: multi.forecast(full_hx, H, **full_kw))
+                e2e_pageable = timed(lambda: multi.forecast(np.ascontiguousarray(full_x), H, **full_kw))
+                multi.close()
+                multi_note = (f"one process, one handle over {world} GPUs (tsb_load_devices), wall clock around "
+                              "timestral_capi_forecast: H2D of every shard, forecasts, D2H into one buffer")
+            dist.barrier(group=host_group)
+    stats = torch.tensor([ms], device=dev, dtype=torch.float64)
     if dist:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    ms_max, e2e_max = stats[0].item(), stats[1].item()
+    ms_max = stats[0].item()
     if rank == 0:
         hbm, tf, tf_sus, kind = peaks()
         # Attention: per (row, head) problem q, k, v, sigmoid(gate) read and the output
         # written (5 S hd f16 values); FLOPs 4 hd sum_q keys(q), keys = L for encoder queries
         # and S for decoder queries (the reference's computed set); one launch per time
         # sublayer and block.
+        # Two byte counts per (row, head) problem: the survey's (q, k, v read and the output
+        # written, 4 S hd f16 values: the bytes any unfused attention must move) and the
+        # kernel's own (also sigmoid(gate), which it reads to apply the gate in its epilogue).
         problems = rows * HEADS
-        att_bytes = 5 * S * HEAD_DIM * 2 * problems
+        att_bytes = 4 * S * HEAD_DIM * 2 * problems
+        att_kernel_bytes = 5 * S * HEAD_DIM * 2 * problems
         att_flops = 4 * HEAD_DIM * (L * L + (S - L) * S) * problems
         att_avg = att_ms / max(att_n, 1)
         achieved_gbs = att_bytes / (att_avg / 1e3) / 1e9
+        achieved_kernel_gbs = att_kernel_bytes / (att_avg / 1e3) / 1e9
         achieved_tf = att_flops / (att_avg / 1e3) / 1e12
         roof_tf = min(tf, (att_flops / att_bytes) * hbm / 1e3)
         tc_path = model.tensor_core_path
@@ -400,7 +471,15 @@ def main():
                              "frac": achieved_tf / tf_sus}),
                          "traffic": (ATTN_DRAM_BYTES_PER_PROBLEM * problems if a.config == "cfg5" else
                                      ATTN_LONG_DRAM_BYTES_PER_PLANE * problems if a.config == "cfg6" else None),
-                         "traffic_unit": "bytes per launch", "algorithmic_bytes": att_bytes,
+                         "traffic_unit": "bytes per launch",
+                         "traffic_source": ("a constant per (row, head) problem from one ncu capture of this kernel "
+                                            "(dram__bytes_read.sum + dram__bytes_write.sum), scaled by the problems "
+                                            "of a launch; not measured in this run"),
+                         "algorithmic_bytes": att_bytes,
+                         "bytes_convention": "q, k, v read + output written (4 x S x 64 f16 per row and head)",
+                         "kernel_bytes": att_kernel_bytes, "kernel_bytes_achieved_gbs": achieved_kernel_gbs,
+                         "kernel_bytes_frac": achieved_kernel_gbs / hbm,
+                         "kernel_bytes_convention": "also sigmoid(gate) read (5 x S x 64 f16 per row and head)",
                          "achieved_tflops": achieved_tf, "roofline_tflops": roof_tf,
                          "frac_of_dense_contraction_roofline": achieved_tf / roof_tf,
                          "launch_ms": att_avg, "launches_per_step": att_n / max(a.steps, 1), "peak_kind": kind},
@@ -416,8 +495,14 @@ def main():
                                     "peak_kind": kind + " sustained"}
         if e2e:
             cov_bytes = sum(int(v.nbytes) for v in kw.values()) * B // max(per, 1)
-            out["e2e"] = {"value": B / e2e_max, "unit": "series/s",
-                          "h2d_bytes_per_step": B * V * T * 4 + cov_bytes, "d2h_bytes_per_step": B * V * H * Q * 4}
+            out["e2e"] = {"value": B / e2e, "unit": "series/s",
+                          "h2d_bytes_per_step": B * V * T * 4 + cov_bytes, "d2h_bytes_per_step": B * V * H * Q * 4,
+                          "input": "page-locked host buffer", "output": "the library's result buffer"}
+            if multi_note:
+                out["e2e"]["how"] = multi_note
+            if e2e_pageable:
+                out["e2e_pageable"] = {"value": B / e2e_pageable, "unit": "series/s",
+                                       "input": "pageable host buffer (numpy)"}
         if world == 1 and not a.no_cpu:
             out["cpu_baseline"] = cpu_baseline(a.config, c)
         print(json.dumps(out), flush=True)

@@ -38,6 +38,23 @@ TIMESTRAL_API int tsb_forecast_device(timestral_ctx* ctx, const float* d_context
                                       int32_t B, int32_t V, int32_t T, int32_t H, int32_t symmetric,
                                       int32_t clip, int32_t max_context, float* d_out, int32_t async);
 
+/* ---- several GPUs per handle ---------------------------------------------------------
+ * A handle that forecasts on several GPUs of this machine through the unchanged
+ * timestral_capi_forecast (reference src/timestral_capi.cpp:60-90): the model is uploaded
+ * to every listed device; each request's series are split into contiguous shards, one per
+ * device (shard k of n holds series [k*B/n, (k+1)*B/n)), forecast concurrently by one host
+ * thread and CUDA stream per device, and each shard's result is copied from its device
+ * straight into its slice of the one result buffer. There is no collective: a series never
+ * leaves its device, and its forecast is the same bits as on one GPU. A device listed more
+ * than once takes that many shards (each with its own stream). Returns NULL (error in
+ * timestral_capi_last_error(NULL)) for an invalid device ordinal.
+ * timestral_capi_load does the same when the environment variable TIMESTRAL_DEVICES holds a
+ * comma-separated list of device ordinals or "all". The device-resident entries below
+ * (tsb_forecast_device, tsb_stream, ...) act on the handle's first device. */
+TIMESTRAL_API timestral_ctx* tsb_load_devices(const char* path, int threads, const int32_t* devices, int32_t n_devices);
+/* Number of GPUs the handle forecasts on. */
+TIMESTRAL_API int32_t tsb_device_count(timestral_ctx* ctx);
+
 /* Wait for the handle's stream; returns TSB_ERR_DEVICE (with last_error set) when a kernel
  * of an asynchronous tsb_forecast_device call reported an error. */
 TIMESTRAL_API int tsb_sync(timestral_ctx* ctx);

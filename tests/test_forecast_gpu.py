@@ -518,3 +518,42 @@ def test_errors_surface_through_the_abi():
     # a successful call clears the handle error
     m.forecast(x, 8)
     assert m.last_error == ""
+
+
+def test_multi_device_handle_equals_one_gpu():
+    """A handle over several GPUs (tsb_load_devices; here device 0 listed three times, so the
+    three series shards run concurrently on three streams of the one GPU of the test box)
+    gives the same bits as a single-device handle, with and without covariates, for batch
+    sizes that do not divide evenly and a batch smaller than the device list."""
+    path = sy.cached_model(sy.spec_small(True), "f16")
+    one, _ = models(sy.spec_small(True), "f16")
+    multi = tb.Model(path, devices=[0, 0, 0])
+    assert multi.device_count == 3
+    rng = np.random.default_rng(61)
+    for B, V in ((7, 1), (2, 2), (5, 3)):
+        x = random_context(B, V, 256, seed=60 + B)
+        assert np.array_equal(multi.forecast(x, 64).view(np.uint32), one.forecast(x, 64).view(np.uint32)), (B, V)
+    B, V, T, H = 5, 1, 192, 40
+    x = random_context(B, V, T, seed=62)
+    kw = dict(past=rng.standard_normal((B, 2, T)).astype(np.float32),
+              known=rng.standard_normal((B, 1, T + H)).astype(np.float32),
+              cat_known=rng.integers(0, 5, (B, 1, T + H)).astype(np.float64))
+    assert np.array_equal(multi.forecast(x, H, **kw).view(np.uint32), one.forecast(x, H, **kw).view(np.uint32))
+    with pytest.raises(tb.TimestralError, match="observation mask must be boolean"):
+        multi.forecast(x, H, mask=np.full(x.shape, 2, np.uint8))
+    multi.close()
+
+
+def test_multi_device_handle_on_every_gpu():
+    """With every GPU of the machine in one handle (TIMESTRAL_DEVICES=all semantics through
+    tsb_load_devices), a batch forecast equals the single-GPU forecast bit for bit."""
+    import torch
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("one GPU")
+    path = sy.cached_model(sy.spec_small(), "f16")
+    one, _ = models(sy.spec_small(), "f16")
+    multi = tb.Model(path, devices=list(range(n)))
+    x = random_context(3 * n + 1, 1, 256, seed=63)
+    assert np.array_equal(multi.forecast(x, 64).view(np.uint32), one.forecast(x, 64).view(np.uint32))
+    multi.close()

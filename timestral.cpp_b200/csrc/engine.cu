@@ -17,12 +17,30 @@
 #include <atomic>
 #include <cfloat>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
+#include <memory>
 #include <stdexcept>
+
+#include <nvtx3/nvToolsExt.h>
 
 namespace tsb {
 
 namespace {
+
+// NVTX range of one forecast stage on the calling host thread (visible in Nsight Systems
+// timelines beside the kernels it enqueues; a no-op when no profiler is attached).
+struct Range {
+    explicit Range(const char* name) { nvtxRangePushA(name); }
+    Range(const char* fmt, int i) {
+        char buf[48];
+        std::snprintf(buf, sizeof(buf), fmt, i);
+        nvtxRangePushA(buf);
+    }
+    ~Range() { nvtxRangePop(); }
+    Range(const Range&) = delete;
+    Range& operator=(const Range&) = delete;
+};
 
 void check(cudaError_t e, const char* what) {
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
@@ -506,6 +524,7 @@ struct Engine::Impl {
     // role [R2] (covariate path). Output: refined [R2][h*ps][Q]. first: compute cap stats.
     Engine::Geometry geo;
     void predict_block(int R2, int T, int h, bool cov, int group_rows, int pass_rows, bool first, int cap_ctx) {
+        Range block_range("predict_block");
         const int W = cov ? T + h * ps : T;
         const int N = W / ps, L = T / ps;
         const int S = cov ? 2 * N : N + h;
@@ -521,6 +540,7 @@ struct Engine::Impl {
         kv.ensure(size_t(R2) * kvw * 4);
         rope_row.ensure(size_t(M) * 4); gbeg.ensure(R2 * 4); gsize.ensure(R2 * 4);
         if (first) { caplo.ensure(R2 * 4); caphi.ensure(R2 * 4); capsc.ensure(R2 * 4); }
+        auto embed_range = std::make_unique<Range>("scale_rows + patch embedding");
         run("scale", [&] {
             return scale_rows(rc, rows_p, mask_p, R2, W, cov ? (L - 1) * ps : T - 1, N, kvw, feat.as<float>(),
                               aloc.as<float>(), ascale.as<float>(), kv.as<uint32_t>(), first_obs.as<int>(),
@@ -604,7 +624,9 @@ struct Engine::Impl {
 
         if (tc && fuse_now) { x16.ensure(size_t(M) * D * 2); ssq.ensure(size_t(M) * (D / 128) * 4); }
         bool have16 = false;   // x16 and ssq hold the current x
+        embed_range.reset();
         for (size_t li = 0; li < attn.size(); ++li) {
+            Range layer_range("layer %d", int(li));
             for (const AttnW& a : attn[li]) {
                 if (tc) {
                     norm_input(have16, M);
@@ -648,6 +670,7 @@ struct Engine::Impl {
         }
         // out_norm on the decoder tokens only (per-token op; reference src/encoder.cpp:146 +
         // src/predict_block.cpp:15-16 slice).
+        Range head_range("out_norm + quantile head + refine");
         const int DR = R2 * P_all;
         dec.ensure(size_t(DR) * D * eb);
         run("rms", [&] { return rms_norm(x.as<float>(), out_norm, DR, D, mv.eps, dec.p, tc, P_all, S, N, s); });
@@ -836,6 +859,7 @@ bool Engine::timing_read(const std::string& cls, double* ms, int64_t* launches) 
 
 void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B, int V, int T, int H, bool symmetric,
                               bool clip, int max_context, float* d_out, bool sync) {
+    Range range("tsb forecast");
     check(cudaSetDevice(device_), "cudaSetDevice");
     Impl& im = *impl_;
     im.launches = 0;
@@ -1008,6 +1032,7 @@ void Engine::graph_replay(bool on) {
 }
 
 void Engine::decode_host_rows(const HostRows& a, int H, float* h_decoded) {
+    Range range("tsb decode");
     check(cudaSetDevice(device_), "cudaSetDevice");
     Impl& im = *impl_;
     if (im.pending.valid && im.fuse_now) {       // an earlier asynchronous forecast: complete it
@@ -1048,6 +1073,7 @@ void Engine::decode_host_rows(const HostRows& a, int H, float* h_decoded) {
 
 void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetric, bool clip, const float* ctx,
                            const uint8_t* umask, int T_req, float* h_out) {
+    Range range("tsb forecast (host rows)");
     check(cudaSetDevice(device_), "cudaSetDevice");
     Impl& im = *impl_;
     if (im.pending.valid && im.fuse_now) {       // an earlier asynchronous forecast: complete it
@@ -1113,6 +1139,7 @@ void Engine::forecast_rows(const HostRows& a, int B, int V, int H, bool symmetri
 }
 
 void Engine::forecast_covariates(const CovRequest& q, bool symmetric, bool clip, float* h_out) {
+    Range range("tsb forecast (covariates)");
     check(cudaSetDevice(device_), "cudaSetDevice");
     Impl& im = *impl_;
     if (im.pending.valid && im.fuse_now) {       // an earlier asynchronous forecast: complete it

@@ -21,6 +21,7 @@
 #include <new>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include <cuda_runtime.h>
@@ -57,12 +58,23 @@ template <class T> size_t count(size_t a, size_t b, size_t c) {
 
 }  // namespace
 
+// A handle: one model mapping and one Forecaster per GPU it forecasts on. With several GPUs
+// (tsb_load_devices, or TIMESTRAL_DEVICES for timestral_capi_load) a request's series are
+// split into contiguous shards, one per GPU, forecast concurrently by one host thread each,
+// and every shard's result lands in its own slice of the one output buffer: no collective,
+// a series never leaves its GPU, and a series' result does not depend on the shard it is in.
 struct timestral_ctx {
     ts::Model model;
-    ts::Forecaster forecaster;
+    ts::Forecaster forecaster;                                   // the first GPU
+    std::vector<std::unique_ptr<ts::Forecaster>> more;           // the other GPUs, in list order
     int threads;
     ErrorText error;
-    timestral_ctx(ts::Model&& m, int n, int device) : model(std::move(m)), forecaster(model, device), threads(n) {}
+    timestral_ctx(ts::Model&& m, int n, const std::vector<int>& devices)
+        : model(std::move(m)), forecaster(model, devices.at(0)), threads(n) {
+        for (size_t i = 1; i < devices.size(); ++i) more.push_back(std::make_unique<ts::Forecaster>(model, devices[i]));
+    }
+    size_t gpus() const { return 1 + more.size(); }
+    ts::Forecaster& gpu(size_t k) { return k ? *more[k - 1] : forecaster; }
 };
 
 namespace {
@@ -78,25 +90,81 @@ extern "C" {
 
 TIMESTRAL_API int timestral_capi_abi_version(void) { return 1; }
 
+namespace {
+int device_count() {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) throw ts::Error("no CUDA device available");
+    return n;
+}
+
+// GPUs of a handle loaded with timestral_capi_load: TIMESTRAL_DEVICES ("all", or a comma-separated
+// list of device ordinals), else the device chosen with tsb_set_device, else the current one.
+std::vector<int> default_devices() {
+    const int n = device_count();
+    if (const char* env = std::getenv("TIMESTRAL_DEVICES")) {
+        std::vector<int> list;
+        const std::string v(env);
+        if (v == "all") {
+            for (int d = 0; d < n; ++d) list.push_back(d);
+            return list;
+        }
+        size_t i = 0;
+        while (i < v.size()) {
+            size_t j = v.find(',', i);
+            if (j == std::string::npos) j = v.size();
+            const std::string item = v.substr(i, j - i);
+            char* end = nullptr;
+            const long d = std::strtol(item.c_str(), &end, 10);
+            require(!item.empty() && end && *end == 0 && d >= 0 && d < n, "TIMESTRAL_DEVICES: invalid device list");
+            list.push_back(int(d));
+            i = j + 1;
+        }
+        require(!list.empty(), "TIMESTRAL_DEVICES: invalid device list");
+        return list;
+    }
+    int dev = tls_device;
+    if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) throw ts::Error("no CUDA device available");
+    return {dev};
+}
+
+// The model file is checked before any GPU is touched (its errors come first, as in the
+// reference); `devices` null: default_devices().
+timestral_ctx* load_on(const char* path, int threads, const std::vector<int>* devices) {
+    require(path && *path, "model path is required");
+    require(threads >= 1 && threads <= 1024, "invalid CPU thread count");
+    ts::Model model = ts::Model::load(path);
+    auto p = std::make_unique<timestral_ctx>(std::move(model), threads, devices ? *devices : default_devices());
+    tls_error.clear();
+    return p.release();
+}
+}  // namespace
+
 TIMESTRAL_API timestral_ctx* timestral_capi_load(const char* path, int threads) {
     try {
         require(path && *path, "model path is required");
         require(threads >= 1 && threads <= 1024, "invalid CPU thread count");
-        ts::Model model = ts::Model::load(path);
-        int dev = tls_device;
-        if (dev < 0) {
-            int n = 0;
-            if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0 || cudaGetDevice(&dev) != cudaSuccess)
-                throw ts::Error("no CUDA device available");
-        }
-        auto p = std::make_unique<timestral_ctx>(std::move(model), threads, dev);
-        tls_error.clear();
-        return p.release();
+        return load_on(path, threads, nullptr);
     } catch (...) {
         caught(nullptr);
         return nullptr;
     }
 }
+
+TIMESTRAL_API timestral_ctx* tsb_load_devices(const char* path, int threads, const int32_t* devices, int32_t n_devices) {
+    try {
+        require(path && *path, "model path is required");
+        require(devices && n_devices >= 1 && n_devices <= 64, "invalid device list");
+        const int n = device_count();
+        std::vector<int> list(devices, devices + n_devices);
+        for (int d : list) require(d >= 0 && d < n, "invalid device ordinal");
+        return load_on(path, threads, &list);
+    } catch (...) {
+        caught(nullptr);
+        return nullptr;
+    }
+}
+
+TIMESTRAL_API int32_t tsb_device_count(timestral_ctx* c) { return c ? int32_t(c->gpus()) : 0; }
 
 TIMESTRAL_API void timestral_capi_free(timestral_ctx* c) {
     try { delete c; } catch (...) { caught(nullptr); }
@@ -234,6 +302,7 @@ TIMESTRAL_API float* timestral_capi_forecast(timestral_ctx* c, const timestral_f
         const size_t nx = count<float>(B, V, T), np = count<float>(B, size_t(a->c_past), T);
         const size_t nk = count<float>(B, size_t(a->c_known), TH), ncp = count<double>(B, size_t(a->cc_past), T);
         const size_t nck = count<double>(B, size_t(a->cc_known), TH);
+        (void)np; (void)nk; (void)ncp; (void)nck;      // overflow checks of the covariate sizes
         const ts::Config& cfg = c->model.config();
         const size_t Q = cfg.num_quantiles();
         require(Q <= INT32_MAX, "quantile count overflow");
@@ -250,27 +319,51 @@ TIMESTRAL_API float* timestral_capi_forecast(timestral_ctx* c, const timestral_f
         const bool clip = a->clip_nonnegative == -1 ? cfg.clip_nonnegative : a->clip_nonnegative != 0;
         bool pinned = false;
         result = out_alloc(no * sizeof(float), &pinned);
-        if (!any) {
-            if (sym)
-                for (size_t i = 0; i < Q; ++i)
-                    if (std::abs(cfg.quantile_knots[i] + cfg.quantile_knots[Q - 1 - i] - 1) >= 1e-9)
-                        throw ts::Error("symmetric averaging needs quantile levels symmetric about 0.5");
-            c->forecaster.forecast_targets(a->context, a->observation_mask, B, V, T, H, sym, clip, size_t(a->max_context),
-                                           result, pinned);
-        } else {
+        if (!any && sym)
+            for (size_t i = 0; i < Q; ++i)
+                if (std::abs(cfg.quantile_knots[i] + cfg.quantile_knots[Q - 1 - i] - 1) >= 1e-9)
+                    throw ts::Error("symmetric averaging needs quantile levels symmetric about 0.5");
+        // Series shard k of n: [k * B / n, (k + 1) * B / n), on the handle's k-th GPU.
+        const size_t shards = std::min(c->gpus(), B);
+        auto run_shard = [&](size_t k) {
+            const size_t b0 = k * B / shards, b1 = (k + 1) * B / shards, Bk = b1 - b0;
+            float* out_k = result + b0 * V * H * Q;
+            ts::Forecaster& f = c->gpu(k);
+            if (!any) {
+                f.forecast_targets(a->context + b0 * V * T, a->observation_mask ? a->observation_mask + b0 * V * T : nullptr,
+                                   Bk, V, T, H, sym, clip, size_t(a->max_context), out_k, pinned);
+                return;
+            }
             ts::ForecastRequest r;
-            r.batch = B; r.targets = V; r.length = T; r.horizon = H; r.max_context = size_t(a->max_context);
+            r.batch = Bk; r.targets = V; r.length = T; r.horizon = H; r.max_context = size_t(a->max_context);
             r.past_count = size_t(a->c_past); r.known_count = size_t(a->c_known);
             r.categorical_past_count = size_t(a->cc_past); r.categorical_known_count = size_t(a->cc_known);
-            if (a->observation_mask) r.observation_mask.assign(a->observation_mask, a->observation_mask + nx);
-            r.context.assign(a->context, a->context + nx);
-            if (np) r.past.assign(a->past_cov, a->past_cov + np);
-            if (nk) r.known.assign(a->known_cov, a->known_cov + nk);
-            if (ncp) r.categorical_past.assign(a->cat_past, a->cat_past + ncp);
-            if (nck) r.categorical_known.assign(a->cat_known, a->cat_known + nck);
+            auto take = [&](auto* src, size_t per_series, auto& dst) {
+                if (src && per_series) dst.assign(src + b0 * per_series, src + b1 * per_series);
+            };
+            if (a->observation_mask) r.observation_mask.assign(a->observation_mask + b0 * V * T, a->observation_mask + b1 * V * T);
+            take(a->context, V * T, r.context);
+            take(a->past_cov, size_t(a->c_past) * T, r.past);
+            take(a->known_cov, size_t(a->c_known) * TH, r.known);
+            take(a->cat_past, size_t(a->cc_past) * T, r.categorical_past);
+            take(a->cat_known, size_t(a->cc_known) * TH, r.categorical_known);
             r.symmetric_averaging = sym;
             r.clip_nonnegative = clip;
-            c->forecaster.forecast_into(r, result);
+            f.forecast_into(r, out_k);
+        };
+        if (shards == 1) {
+            run_shard(0);
+        } else {
+            std::vector<std::exception_ptr> failed(shards);
+            std::vector<std::thread> pool;
+            pool.reserve(shards);
+            for (size_t k = 0; k < shards; ++k)
+                pool.emplace_back([&, k] {
+                    try { run_shard(k); } catch (...) { failed[k] = std::current_exception(); }
+                });
+            for (auto& t : pool) t.join();
+            for (auto& e : failed)
+                if (e) std::rethrow_exception(e);
         }
         *out_q = int32_t(Q);
         c->error.clear();

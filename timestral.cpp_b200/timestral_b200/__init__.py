@@ -52,6 +52,8 @@ SIGNATURES = {
     "tsb_forecast_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                       C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32]),
     "tsb_sync": (C.c_int, [C.c_void_p]),
+    "tsb_load_devices": (C.c_void_p, [C.c_char_p, C.c_int, C.POINTER(C.c_int32), C.c_int32]),
+    "tsb_device_count": (C.c_int32, [C.c_void_p]),
     "tsb_set_device": (C.c_int, [C.c_int32]),
     "tsb_stream": (C.c_void_p, [C.c_void_p]),
     "tsb_timing_enable": (C.c_int, [C.c_void_p, C.c_int32]),
@@ -107,13 +109,23 @@ def _vp(a):
 class Model:
     """A loaded model handle (timestral_capi_load) with the reference's C ABI semantics."""
 
-    def __init__(self, path, n_threads: int = 1, device: int | None = None):
+    def __init__(self, path, n_threads: int = 1, device: int | None = None, devices=None):
+        """devices: a list of GPU ordinals to shard every request's series over (one handle,
+        tsb_load_devices); device: the one GPU of a single-device handle."""
         L = lib()
-        if device is not None:
-            L.tsb_set_device(device)
-        self.h = L.timestral_capi_load(str(path).encode(), n_threads)
+        if devices is not None:
+            arr = (C.c_int32 * len(devices))(*devices)
+            self.h = L.tsb_load_devices(str(path).encode(), n_threads, arr, len(devices))
+        else:
+            if device is not None:
+                L.tsb_set_device(device)
+            self.h = L.timestral_capi_load(str(path).encode(), n_threads)
         if not self.h:
             raise TimestralError(L.timestral_capi_last_error(None).decode())
+
+    @property
+    def device_count(self) -> int:
+        return lib().tsb_device_count(self.h)
 
     def close(self):
         if getattr(self, "h", None):
