@@ -79,6 +79,13 @@ TIMESTRAL_API int tsb_fused_norm(timestral_ctx* ctx, int32_t mode);
  * and the variate axis. Mode 1 is slower; it shows how much of a forecast's deviation from the
  * reference comes from the tensor-core attention. */
 TIMESTRAL_API int tsb_attention_kernels(timestral_ctx* ctx, int32_t mode);
+/* Decoder-token tail (on = 1, the default): the last layer of the 209M schedule starts with a
+ * time sublayer and continues with per-token work (a one-row series' variate sublayer and
+ * the MLP), and the head reads only the decoder tokens, so after that layer's time attention
+ * the remaining GEMMs run on the decoder tokens of every row alone (8 of 72 tokens at T = 2048,
+ * H = 256). The forecast is the same bits either way; on = 0 computes every token as the
+ * reference does (src/encoder.cpp:45-106 then src/predict_block.cpp:15-16 slices). */
+TIMESTRAL_API int tsb_decoder_tail(timestral_ctx* ctx, int32_t on);
 /* CUDA-graph replay (on by default): a forecast without covariates that fits one decode
  * block (H <= 32 patches of the 209M geometry) is captured into a CUDA graph on its second
  * call with the same sizes, flags and device buffers (tsb_forecast_device pointers, or the
@@ -151,6 +158,8 @@ typedef struct tsb_gemm_test {
     void* qkvg[4]; int32_t S, H, D, rope;
     const float* cos_tab; const float* sin_tab; const int32_t* rope_row; int32_t rope_half;
     int32_t rope_dup;             /* tables have equal halves (cos[d] == cos[d + 32]) */
+    int32_t a_group, a_stride, a_offset;  /* A row of accumulator row m: (m / a_group) * a_stride
+                                             + a_offset + m % a_group (a_group 0: m) */
 } tsb_gemm_test;
 /* Runs one tensor-core GEMM on the current device and synchronizes. Returns a TSB_ code;
  * on TSB_ERR_DEVICE the kernel's error word is written to *dev_error. */

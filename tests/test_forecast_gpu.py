@@ -269,6 +269,26 @@ def test_209m_f16_cfg5_scale():
     check_nd(big[idx], o.forecast(sub, 256), sub, 32, F16_MEAN_ND)
 
 
+@pytest.mark.parametrize("norm_mode", [1, 0])
+def test_decoder_tail_same_bits(norm_mode):
+    """The last layer's per-token work on the decoder tokens alone (the default) gives the same
+    forecast bits as computing every token, with the norm carried by the GEMMs and with the
+    RMSNorm kernel, for one and for two decode blocks."""
+    m, _ = models(sy.spec_209m(), "f16")
+    x = sy.series_random_walk(3, 2048, nan_frac=0.02)
+    try:
+        m.fused_norm(norm_mode)
+        for H in (256, 1100):
+            tail = m.forecast(x, H).copy()
+            m.decoder_tail(False)
+            full = m.forecast(x, H).copy()
+            m.decoder_tail(True)
+            assert np.array_equal(tail.view(np.uint32), full.view(np.uint32)), H
+    finally:
+        m.decoder_tail(True)
+        m.fused_norm(1)
+
+
 def test_209m_attention_share():
     """How much of the F16 deviation comes from attention, at the cfg2 shape on the 209M
     model. Four comparisons: the device with its tensor-core attention and with the CUDA-core

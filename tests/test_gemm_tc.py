@@ -20,7 +20,8 @@ def dp(t):
 
 
 def run(kind, A, B, M, N, K, out=None, ldo=0, bias=None, resid=None, row_group=0, row_stride=0, row_offset=0,
-        qkvg=None, S=0, H=0, D=0, rope=0, cos=None, sin=None, rope_row=None, rope_half=32, rope_dup=0):
+        qkvg=None, S=0, H=0, D=0, rope=0, cos=None, sin=None, rope_row=None, rope_half=32, rope_dup=0,
+        a_group=0, a_stride=0, a_offset=0):
     t = tb.GemmTest()
     t.kind, t.A, t.lda, t.B, t.ldb = kind, dp(A), A.shape[1], dp(B), B.shape[1]
     t.M, t.N, t.K = M, N, K
@@ -32,6 +33,7 @@ def run(kind, A, B, M, N, K, out=None, ldo=0, bias=None, resid=None, row_group=0
     t.S, t.H, t.D, t.rope = S, H, D, rope
     t.cos_tab, t.sin_tab, t.rope_row, t.rope_half = dp(cos), dp(sin), dp(rope_row), rope_half
     t.rope_dup = rope_dup
+    t.a_group, t.a_stride, t.a_offset = a_group, a_stride, a_offset
     err = C.c_int32(0)
     rc = tb.lib().tsb_test_gemm(C.byref(t), C.byref(err))
     assert rc == 0, (rc, err.value)
@@ -74,6 +76,28 @@ def test_f16_store(dev):
     out = torch.zeros(M, N, device=dev, dtype=torch.float16)
     run(1, A, B, M, N, K, out=out, ldo=N)
     close(out, ref_mm(A, B), K, f16=True)
+
+
+@pytest.mark.parametrize("group,R", [(8, 300), (1, 517), (32, 9), (4, 1024)])
+def test_row_gather_decoder_tokens(dev, group, R):
+    """The decoder-token tail: accumulator row m reads A row (m / g) * S + N + m % g (a 3D
+    tensor-map gather, g decoder tokens of every S-token row) and writes its residual row at
+    the same position; the other rows of the residual stream are untouched."""
+    S, Nn, K, N = 72 if group <= 8 else 80, 64 if group <= 8 else 48, 768, 768
+    A = torch.randn(R * S, K, device=dev).half()
+    B = (torch.randn(N, K, device=dev) * 0.05).half()
+    x = torch.randn(R * S, N, device=dev)
+    x0 = x.clone()
+    M = R * group
+    run(2, A, B, M, N, K, out=x, ldo=N, resid=x, row_group=group, row_stride=S, row_offset=Nn,
+        a_group=group, a_stride=S, a_offset=Nn)
+    rows = (torch.arange(M, device=dev) // group) * S + Nn + torch.arange(M, device=dev) % group
+    want = x0.clone().double()
+    want[rows] += ref_mm(A[rows], B)
+    close(x, want, K)
+    keep = torch.ones(R * S, dtype=torch.bool, device=dev)
+    keep[rows] = False
+    assert torch.equal(x[keep], x0[keep])
 
 
 def test_resid_remap(dev):

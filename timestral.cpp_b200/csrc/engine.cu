@@ -145,6 +145,7 @@ struct Engine::Impl {
     bool fuse_now = true;        // used by the running forecast
     bool force_fallback = false; // test hook: treat every fused forecast as flagged
     bool attn_simt = false;      // tensor-core path: attention on the CUDA-core kernels
+    bool tail_enabled = true;    // decoder-token tail of the last layer (see RowMap tail)
     const BlockObserver* observer = nullptr;
     int shot_override = 0;       // patches per decode block (0: the model's)
     double cap_override = -1;    // cap factor (negative: the model's)
@@ -166,6 +167,13 @@ struct Engine::Impl {
     const __half* a_in = nullptr;
     const float* ssq_in = nullptr;
     bool produce16 = false;
+    // Decoder-token tail of the last layer: after its time attention every later op of the
+    // layer is per token, and only the decoder tokens reach the head, so the out projection,
+    // the one-row variate sublayer and the MLP run on those tokens alone (rows r * S + N + j,
+    // j < h; the other tokens' results were never used). Same bits for the tokens kept.
+    struct RowMap { int group = 0, stride = 0, offset = 0; };
+    RowMap a_map, tail;
+    int tail_rows = 0;
     // raw covariate request inputs and assembly scratch
     DevBuf cov_ctx, cov_umask, cov_past, cov_known, cov_cpast, cov_cknown, cov_first, cov_scratch;
     // request-sized buffers kept across calls (no allocation on the forecast path once warm)
@@ -467,11 +475,28 @@ struct Engine::Impl {
     // The normalised input of the next consuming GEMM: x16 and the row sums of squares left by
     // the last residual-add epilogue, or the RMSNorm kernel (unit weights) into xn.
     void norm_input(bool have16, int64_t M) {
+        a_map = RowMap{};
         if (fuse_now && have16) { a_in = x16.as<__half>(); ssq_in = ssq.as<float>(); return; }
         run("rms", [&] { return rms_norm(x.as<float>(), ones.as<float>(), int(M), D, mv.eps, xn.p, 1, 0, 0, 0, s); });
         a_in = xn.as<__half>();
         ssq_in = nullptr;
     }
+    // The same for the decoder tokens alone (`tail` rows): the carried x16 read through the
+    // row gather, or the RMSNorm kernel writing those tokens' normalised rows compactly.
+    void norm_input_tail(bool have16) {
+        if (fuse_now && have16) { a_in = x16.as<__half>(); ssq_in = ssq.as<float>(); a_map = tail; return; }
+        run("rms", [&] {
+            return rms_norm(x.as<float>(), ones.as<float>(), tail_rows, D, mv.eps, xn.p, 1, tail.group, tail.stride,
+                            tail.offset, s);
+        });
+        a_in = xn.as<__half>();
+        ssq_in = nullptr;
+        a_map = RowMap{};
+    }
+    // A-operand rows of the next GEMM (see GemmArgs::a_group).
+    void gather_a(GemmArgs& g) const { g.a_group = a_map.group; g.a_stride = a_map.stride; g.a_offset = a_map.offset; }
+    // Output rows of a tail GEMM that writes the residual stream: the decoder tokens' rows.
+    void scatter_out(GemmEpilogue& e) const { e.row_group = tail.group; e.row_stride = tail.stride; e.row_offset = tail.offset; }
     void consume(GemmEpilogue& e) const {
         e.ssq_in = ssq_in; e.ssq_slots = D / 128; e.rms_D = D; e.rms_eps = mv.eps; e.norm_flag = nflag.as<int>();
     }
@@ -625,13 +650,25 @@ struct Engine::Impl {
         if (tc && fuse_now) { x16.ensure(size_t(M) * D * 2); ssq.ensure(size_t(M) * (D / 128) * 4); }
         bool have16 = false;   // x16 and ssq hold the current x
         embed_range.reset();
+        // The decoder-token tail applies when the last layer starts with a time sublayer and
+        // the rest of it is per token (one-row series on the variate axis), on the context
+        // path with h dividing the GEMM's 128-row box.
+        const size_t last = attn.size() - 1;
+        bool tail_ok = tc && tail_enabled && !cov && group_rows == 1 && h > 0 && 128 % h == 0 && !attn[last].empty() &&
+                       attn[last][0].time;
+        for (size_t j = 1; tail_ok && j < attn[last].size(); ++j) tail_ok = !attn[last][j].time;
+        tail = RowMap{h, S, N};
+        tail_rows = R2 * h;
         for (size_t li = 0; li < attn.size(); ++li) {
             Range layer_range("layer %d", int(li));
-            for (const AttnW& a : attn[li]) {
+            const bool in_tail = tail_ok && li == last;
+            for (size_t j = 0; j < attn[li].size(); ++j) {
+                const AttnW& a = attn[li][j];
                 if (tc) {
-                    norm_input(have16, M);
+                    if (in_tail && j > 0) norm_input_tail(have16);
+                    else norm_input(have16, M);
                     produce16 = fuse_now;
-                    attention_sublayer_tc(a, int(M), R2, S, group_rows, mm);
+                    attention_sublayer_tc(a, int(M), R2, S, group_rows, mm, in_tail ? (j == 0 ? 1 : 2) : 0);
                     have16 = fuse_now;
                 } else {
                     run("rms", [&] { return rms_norm(x.as<float>(), a.norm, int(M), D, mv.eps, xn.p, 0, 0, 0, 0, s); });
@@ -640,16 +677,21 @@ struct Engine::Impl {
             }
             const MlpW& w = mlp[li];
             if (tc) {
-                norm_input(have16, M);
+                const bool in_tail = tail_ok && li == last;
+                const int Mm = in_tail ? tail_rows : int(M);
+                if (in_tail) norm_input_tail(have16);
+                else norm_input(have16, M);
                 produce16 = fuse_now;
                 GemmArgs a;
-                a.A = a_in; a.lda = D; a.B = w.w12; a.ldb = D; a.M = int(M); a.N = 2 * F; a.K = D;
+                a.A = a_in; a.lda = D; a.B = w.w12; a.ldb = D; a.M = Mm; a.N = 2 * F; a.K = D;
                 a.epi.out = hb.p; a.epi.ldo = F; a.epi.bias = w.b12;
+                gather_a(a);
                 consume(a.epi);
                 gemm(EPI_SWIGLU, a);
                 GemmArgs o;
-                o.A = hb.as<__half>(); o.lda = F; o.B = w.w3; o.ldb = F; o.M = int(M); o.N = D; o.K = F;
+                o.A = hb.as<__half>(); o.lda = F; o.B = w.w3; o.ldb = F; o.M = Mm; o.N = D; o.K = F;
                 o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = w.b3; o.epi.resid = x.as<float>();
+                if (in_tail) scatter_out(o.epi);
                 produce(o.epi);
                 gemm(EPI_RESID, o);
                 have16 = fuse_now;
@@ -725,14 +767,27 @@ struct Engine::Impl {
         }
     }
 
-    void attention_sublayer_tc(const AttnW& a, int M, int R2, int S, int group_rows, const MaskMeta& mm) {
+    // tail_stage: 0 every token; 1 the last layer's time sublayer, whose out projection runs on
+    // the decoder tokens alone; 2 a later one-row variate sublayer of that layer, wholly on them.
+    void attention_sublayer_tc(const AttnW& a, int M, int R2, int S, int group_rows, const MaskMeta& mm, int tail_stage) {
         __half* att16 = att.as<__half>();
+        GemmArgs o;                                  // the out projection (input: att16 rows)
+        o.M = M;
+        if (tail_stage == 2) {
+            if (a.time || group_rows != 1) throw std::runtime_error("decoder tail: unexpected sublayer");
+            M = tail_rows;
+            o.M = tail_rows;                         // att16 holds the tail rows compactly
+        } else if (tail_stage == 1) {
+            o.M = tail_rows;                         // att16 holds every token: gather the tail rows
+            o.a_group = tail.group; o.a_stride = tail.stride; o.a_offset = tail.offset;
+        }
         if (!a.time && group_rows == 1) {
             // One row per series: attention over a single key returns v exactly
             // (reference tests/layer_kind_test.hpp:31-33), so the sublayer is
             // out(v * sigmoid(gate)) and only the v and gate projections are computed.
             GemmArgs g;
             g.A = a_in; g.lda = D; g.M = M; g.K = D; g.epi.out = att16; g.epi.ldo = D;
+            if (tail_stage == 2) gather_a(g);
             consume(g.epi);
             if (a.gate) { g.B = a.vg; g.ldb = D; g.N = 2 * D; g.epi.bias = a.b_vg; gemm(EPI_VGATE, g); }
             else {
@@ -768,9 +823,9 @@ struct Engine::Impl {
                     run("attention_variate", [&] { return attention_variate_simt<__half>(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, hd, mm, s); });
             }
         }
-        GemmArgs o;
-        o.A = att16; o.lda = D; o.B = a.out; o.ldb = D; o.M = M; o.N = D; o.K = D;
+        o.A = att16; o.lda = D; o.B = a.out; o.ldb = D; o.N = D; o.K = D;
         o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = a.b_out; o.epi.resid = x.as<float>();
+        if (tail_stage) scatter_out(o.epi);
         produce(o.epi);
         gemm(EPI_RESID, o);
     }
@@ -1012,6 +1067,12 @@ void Engine::fused_norm(int mode) {
 
 void Engine::attention_kernels(int mode) {
     impl_->attn_simt = mode == 1;
+    impl_->drop_graph();
+    impl_->have_last = false;
+}
+
+void Engine::decoder_tail(bool on) {
+    impl_->tail_enabled = on;
     impl_->drop_graph();
     impl_->have_last = false;
 }

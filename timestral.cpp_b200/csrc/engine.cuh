@@ -137,6 +137,10 @@ public:
     // the variate axis. Mode 1 isolates the tensor-core attention's share of the deviation
     // from the reference's f32 attention.
     void attention_kernels(int mode);
+    // Decoder-token tail (on by default): when the last layer starts with a time sublayer and
+    // the rest of it is per token, its out projection, one-row variate sublayer and MLP run on
+    // the decoder tokens alone, the only tokens the head reads. Off: every token, same bits.
+    void decoder_tail(bool on);
     // Observe every decode block of the following forecasts (nullptr: none). While an
     // observer is set, forecasts are not captured into or replayed from CUDA graphs.
     void set_observer(const BlockObserver* observer);

@@ -89,11 +89,17 @@ __device__ __forceinline__ int64_t out_row(const GemmEpilogue& e, int m) {
 __device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float fast_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// 1/rms of accumulator row m when the A operand is x / 16 and the norm is carried by the
-// GEMM (see GemmEpilogue::ssq_in); 1 otherwise. The slot sums are added in slot order.
-__device__ __forceinline__ float row_scale(const GemmEpilogue& e, int m, bool row_ok) {
+// A row read by accumulator row m (GemmArgs::a_group).
+__device__ __forceinline__ int64_t a_row(const GemmArgs& g, int m) {
+    if (g.a_group <= 0) return m;
+    return int64_t(m / g.a_group) * g.a_stride + g.a_offset + (m % g.a_group);
+}
+
+// 1/rms of A row `row` when the A operand is x / 16 and the norm is carried by the GEMM (see
+// GemmEpilogue::ssq_in); 1 otherwise. The slot sums are added in slot order.
+__device__ __forceinline__ float row_scale(const GemmEpilogue& e, int64_t row, bool row_ok) {
     if (!e.ssq_in || !row_ok) return 1.0f;
-    const float* p = e.ssq_in + int64_t(m) * e.ssq_slots;
+    const float* p = e.ssq_in + row * e.ssq_slots;
     float sum = 0.f;
     for (int j = 0; j < e.ssq_slots; ++j) sum = __fadd_rn(sum, p[j]);
     const float mean = __fdiv_rn(sum, float(e.rms_D));
@@ -448,7 +454,8 @@ __global__ void __launch_bounds__(Cfg<KIND>::THREADS, 1)
                     uint8_t* a = tiles + s * STAGE_BYTES;
                     if (rank == 0) mbar_arrive_expect_tx(&sm->full[s], 2 * STAGE_BYTES);
                     const uint32_t full0 = mapa_shared(smem_u32(&sm->full[s]), 0);
-                    tma_load_2d_pair(a, &map_a, full0, kb * BK, m0);
+                    if (g.a_group > 0) tma_load_3d_pair(a, &map_a, full0, kb * BK, 0, m0 / g.a_group);
+                    else tma_load_2d_pair(a, &map_a, full0, kb * BK, m0);
                     tma_load_2d_pair(a + A_BYTES, &map_b, full0, kb * BK, n0);
                 }
             }
@@ -494,7 +501,7 @@ __global__ void __launch_bounds__(Cfg<KIND>::THREADS, 1)
             float rsc = 1.0f;
             if constexpr (KIND != EPI_F32 && KIND != EPI_RESID) {
                 const int m = m0 + quarter * 32 + lane;
-                rsc = row_scale(g.epi, m, m < g.M);
+                rsc = row_scale(g.epi, a_row(g, m), m < g.M);
             }
             bool ok = true;
             if (lane == 0) ok = wait_or_abort(&sm->acc_full[b], aph, abort, err, kDevTimeoutAccFull);
@@ -549,6 +556,23 @@ bool make_map_2d_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t c
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3D f16 tensor map of a row gather: groups of `group` consecutive rows, one group every
+// `stride` rows of a row-major matrix with pitch `ld` elements; `groups` groups, `cols`
+// columns; box {64 columns, group rows, box_groups groups}, 128-byte swizzle (the same
+// shared-memory image as the 2D map's box of group * box_groups rows).
+bool make_map_gather_f16(CUtensorMap* map, const void* base, int64_t groups, int group, int64_t stride, int64_t cols,
+                         int64_t ld, int box_groups) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(group), cuuint64_t(groups)};
+    cuuint64_t strides[2] = {cuuint64_t(ld) * 2, cuuint64_t(stride) * cuuint64_t(ld) * 2};
+    cuuint32_t box[3] = {64, cuuint32_t(group), cuuint32_t(box_groups)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 3D f16 tensor map over [planes][rows][64] (head-major q/k/v), box {64, box_rows, 1}.
 bool make_map_3d_f16(CUtensorMap* map, const void* base, int64_t planes, int64_t rows, int box_rows) {
     auto fn = encode_fn();
@@ -587,8 +611,11 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
         configured[dev] = true;
     }
     CUtensorMap ma, mb;
-    if (!make_map_2d_f16(&ma, a.A, a.M, a.K, a.lda, BM) || !make_map_2d_f16(&mb, a.B, a.N, a.K, a.ldb, BN_HALF))
-        return cudaErrorInvalidValue;
+    const bool map_a = a.a_group > 0
+        ? make_map_gather_f16(&ma, a.A + int64_t(a.a_offset) * a.lda, (a.M + a.a_group - 1) / a.a_group, a.a_group,
+                              a.a_stride, a.K, a.lda, BM / a.a_group)
+        : make_map_2d_f16(&ma, a.A, a.M, a.K, a.lda, BM);
+    if (!map_a || !make_map_2d_f16(&mb, a.B, a.N, a.K, a.ldb, BN_HALF)) return cudaErrorInvalidValue;
     // One CTA pair (cluster of two) per two SMs, persistent over the 256 x 256 tiles.
     const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN);
     const int max_pairs = device_sm_count() / 2;
@@ -615,6 +642,11 @@ cudaError_t tc_gemm(EpiKind kind, const GemmArgs& a, cudaStream_t stream, int* e
         (a.ldb * 2) % 16 || a.N % 16)
         return cudaErrorInvalidValue;
     if ((kind == EPI_SWIGLU || kind == EPI_VGATE) && a.N % BN) return cudaErrorInvalidValue;
+    // Row gather: whole groups per 128-row box, groups inside the strided rows, 16-byte base.
+    if (a.a_group < 0 || (a.a_group > 0 && (BM % a.a_group || a.M % a.a_group || a.a_offset < 0 ||
+                                           a.a_offset + a.a_group > a.a_stride ||
+                                           (reinterpret_cast<uintptr_t>(a.A + int64_t(a.a_offset) * a.lda) & 15))))
+        return cudaErrorInvalidValue;
     if (kind == EPI_QKVG && (a.epi.D % 64 || a.N % 64 || a.epi.S <= 0)) return cudaErrorInvalidValue;
     // The epilogue moves 16-byte vectors: outputs, residuals and f32 biases must be 16-byte
     // aligned with row pitches that keep every row aligned.

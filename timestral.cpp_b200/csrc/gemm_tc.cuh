@@ -56,6 +56,11 @@ struct GemmEpilogue {
 struct GemmArgs {
     const __half* A = nullptr;
     int64_t lda = 0;
+    // Row gather of A: with a_group > 0, accumulator row m reads A row
+    // (m / a_group) * a_stride + a_offset + m % a_group (a_group divides 128), and so does its
+    // ssq_in row (norm carried by the GEMM). Used to run a GEMM on the decoder tokens of every
+    // row alone; 0: A rows are the accumulator rows.
+    int a_group = 0, a_stride = 0, a_offset = 0;
     const __half* B = nullptr;
     int64_t ldb = 0;
     int M = 0, N = 0, K = 0;

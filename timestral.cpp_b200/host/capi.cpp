@@ -452,7 +452,7 @@ TIMESTRAL_API int tsb_timing_enable(timestral_ctx* c, int32_t enable) {
 TIMESTRAL_API int tsb_fused_norm(timestral_ctx* c, int32_t mode) {
     if (!c || mode < 0 || mode > 2) return TSB_ERR_ARG;
     try {
-        c->forecaster.engine().fused_norm(mode);
+        for (size_t k = 0; k < c->gpus(); ++k) c->gpu(k).engine().fused_norm(mode);
     } catch (...) {
         caught(c);
         return TSB_ERR_CUDA;
@@ -463,7 +463,18 @@ TIMESTRAL_API int tsb_fused_norm(timestral_ctx* c, int32_t mode) {
 TIMESTRAL_API int tsb_attention_kernels(timestral_ctx* c, int32_t mode) {
     if (!c || mode < 0 || mode > 1) return TSB_ERR_ARG;
     try {
-        c->forecaster.engine().attention_kernels(mode);
+        for (size_t k = 0; k < c->gpus(); ++k) c->gpu(k).engine().attention_kernels(mode);
+    } catch (...) {
+        caught(c);
+        return TSB_ERR_CUDA;
+    }
+    return TSB_OK;
+}
+
+TIMESTRAL_API int tsb_decoder_tail(timestral_ctx* c, int32_t on) {
+    if (!c) return TSB_ERR_ARG;
+    try {
+        for (size_t k = 0; k < c->gpus(); ++k) c->gpu(k).engine().decoder_tail(on != 0);
     } catch (...) {
         caught(c);
         return TSB_ERR_CUDA;
@@ -474,7 +485,7 @@ TIMESTRAL_API int tsb_attention_kernels(timestral_ctx* c, int32_t mode) {
 TIMESTRAL_API int tsb_graph_replay(timestral_ctx* c, int32_t on) {
     if (!c) return TSB_ERR_ARG;
     try {
-        c->forecaster.engine().graph_replay(on != 0);
+        for (size_t k = 0; k < c->gpus(); ++k) c->gpu(k).engine().graph_replay(on != 0);
     } catch (...) {
         caught(c);
         return TSB_ERR_CUDA;
@@ -484,7 +495,7 @@ TIMESTRAL_API int tsb_graph_replay(timestral_ctx* c, int32_t on) {
 
 TIMESTRAL_API int tsb_covariate_assembly(timestral_ctx* c, int32_t on_device) {
     if (!c) return TSB_ERR_ARG;
-    c->forecaster.set_device_assembly(on_device != 0);
+    for (size_t k = 0; k < c->gpus(); ++k) c->gpu(k).set_device_assembly(on_device != 0);
     return TSB_OK;
 }
 

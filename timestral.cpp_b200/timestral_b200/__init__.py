@@ -34,7 +34,8 @@ class GemmTest(C.Structure):
                 ("qkvg", C.c_void_p * 4), ("S", C.c_int32), ("H", C.c_int32), ("D", C.c_int32),
                 ("rope", C.c_int32), ("cos_tab", C.c_void_p), ("sin_tab", C.c_void_p),
                 ("rope_row", C.c_void_p), ("rope_half", C.c_int32),
-                ("rope_dup", C.c_int32)]
+                ("rope_dup", C.c_int32), ("a_group", C.c_int32), ("a_stride", C.c_int32),
+                ("a_offset", C.c_int32)]
 
 
 _lib = None
@@ -69,6 +70,7 @@ SIGNATURES = {
     "tsb_graph_replay": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_fused_norm": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_attention_kernels": (C.c_int, [C.c_void_p, C.c_int32]),
+    "tsb_decoder_tail": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_test_scale_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_double] + [C.c_int32] * 6
                             + [C.c_void_p] * 8),
     "tsb_test_attention_time_ex": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 9 + [C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
@@ -201,6 +203,11 @@ class Model:
         the reference's float64 q.k dots and f32 softmax on the same f16 q/k/v."""
         if lib().tsb_attention_kernels(self.h, int(mode)) != 0:
             raise RuntimeError("tsb_attention_kernels failed")
+
+    def decoder_tail(self, on: bool):
+        """Last layer's per-token work on the decoder tokens alone (default on; same bits)."""
+        if lib().tsb_decoder_tail(self.h, int(on)) != 0:
+            raise RuntimeError("tsb_decoder_tail failed")
 
     def graph_replay(self, on: bool):
         """CUDA-graph replay of repeated single-block forecasts (on by default)."""
