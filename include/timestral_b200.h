@@ -79,6 +79,13 @@ TIMESTRAL_API int tsb_fused_norm(timestral_ctx* ctx, int32_t mode);
  * and the variate axis. Mode 1 is slower; it shows how much of a forecast's deviation from the
  * reference comes from the tensor-core attention. */
 TIMESTRAL_API int tsb_attention_kernels(timestral_ctx* ctx, int32_t mode);
+/* Q8_0 weights dequantised in the GEMM prologue (on = 1) instead of read as the f16 copies
+ * made at load (on = 0, the default): the GEMM streams the int8 weight tiles and their f16
+ * block scales (reference Q8_0 blocks, src/weight_policy.hpp:23-30) and converter warps write
+ * the f16 tiles the tensor cores read, each value q * d rounded once to f16 as at load, so the
+ * forecast is the same bits. Weights that carry a folded RMSNorm gain other than 1 keep their
+ * f16 copy. Returns TSB_ERR_MODEL when the model has no Q8_0 weights. */
+TIMESTRAL_API int tsb_q8_prologue(timestral_ctx* ctx, int32_t on);
 /* Decoder-token tail (on = 1, the default): the last layer of the 209M schedule starts with a
  * time sublayer and continues with per-token work (a one-row series' variate sublayer and
  * the MLP), and the head reads only the decoder tokens, so after that layer's time attention
@@ -160,6 +167,8 @@ typedef struct tsb_gemm_test {
     int32_t rope_dup;             /* tables have equal halves (cos[d] == cos[d + 32]) */
     int32_t a_group, a_stride, a_offset;  /* A row of accumulator row m: (m / a_group) * a_stride
                                              + a_offset + m % a_group (a_group 0: m) */
+    const int8_t* Bq; const void* Bd; int64_t ldd;  /* Q8_0 B: int8 [N][ldb bytes], f16 scales
+                                                       [K/32][ldd]; used instead of B when Bq is set */
 } tsb_gemm_test;
 /* Runs one tensor-core GEMM on the current device and synchronizes. Returns a TSB_ code;
  * on TSB_ERR_DEVICE the kernel's error word is written to *dev_error. */

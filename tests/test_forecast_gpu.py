@@ -321,6 +321,23 @@ def test_209m_attention_share():
     assert not np.array_equal(tc, simt)
 
 
+def test_209m_q8_prologue_same_bits():
+    """Q8_0 weights dequantised in the GEMM prologue (tsb_q8_prologue) give the same forecast
+    bits as the f16 copies made at load: the converter rounds each q * d once to f16."""
+    m, _ = models(sy.spec_209m(), "q8_0")
+    x = sy.series_random_walk(3, 2048, nan_frac=0.02)
+    try:
+        m.q8_prologue(True)
+        pro = m.forecast(x, 256).copy()
+    finally:
+        m.q8_prologue(False)
+    ref = m.forecast(x, 256)
+    assert np.array_equal(pro.view(np.uint32), ref.view(np.uint32))
+    f16, _ = models(sy.spec_209m(), "f16")
+    with pytest.raises(tb.TimestralError, match="no Q8_0 weights"):
+        f16.q8_prologue(True)
+
+
 def test_209m_q8_against_f32():
     """Q8_0 quality as the reference reports it: the Q8_0 forecast against the F32 forecast of
     the same seed-0 weights (cfg2 shape), beside the reference's published mean 0.005658 for

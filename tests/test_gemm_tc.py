@@ -21,7 +21,7 @@ def dp(t):
 
 def run(kind, A, B, M, N, K, out=None, ldo=0, bias=None, resid=None, row_group=0, row_stride=0, row_offset=0,
         qkvg=None, S=0, H=0, D=0, rope=0, cos=None, sin=None, rope_row=None, rope_half=32, rope_dup=0,
-        a_group=0, a_stride=0, a_offset=0):
+        a_group=0, a_stride=0, a_offset=0, Bq=None, Bd=None, ldd=0):
     t = tb.GemmTest()
     t.kind, t.A, t.lda, t.B, t.ldb = kind, dp(A), A.shape[1], dp(B), B.shape[1]
     t.M, t.N, t.K = M, N, K
@@ -34,6 +34,9 @@ def run(kind, A, B, M, N, K, out=None, ldo=0, bias=None, resid=None, row_group=0
     t.cos_tab, t.sin_tab, t.rope_row, t.rope_half = dp(cos), dp(sin), dp(rope_row), rope_half
     t.rope_dup = rope_dup
     t.a_group, t.a_stride, t.a_offset = a_group, a_stride, a_offset
+    t.Bq, t.Bd, t.ldd = dp(Bq), dp(Bd), ldd
+    if Bq is not None:
+        t.B, t.ldb = None, Bq.shape[1]
     err = C.c_int32(0)
     rc = tb.lib().tsb_test_gemm(C.byref(t), C.byref(err))
     assert rc == 0, (rc, err.value)
@@ -98,6 +101,36 @@ def test_row_gather_decoder_tokens(dev, group, R):
     keep = torch.ones(R * S, dtype=torch.bool, device=dev)
     keep[rows] = False
     assert torch.equal(x[keep], x0[keep])
+
+
+def q8_weights(N, K, dev, seed):
+    """Random Q8_0 weights: int8 values [N][K], f16 block scales [N][K/32] (d = amax/127 of
+    N(0, 0.02) rows, as the converter writes them), and the f16 weights q * d rounded once."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+    d = (torch.rand(N, K // 32, generator=g) * 0.0004 + 1e-5).half()
+    w16 = (q.float() * d.float().repeat_interleave(32, dim=1)).half()
+    return q.to(dev), d.t().contiguous().to(dev), w16.to(dev)
+
+
+@pytest.mark.parametrize("kind,M,N,K", [(0, 300, 768, 768), (1, 700, 512, 256), (2, 513, 768, 3072),
+                                        (3, 257, 3072, 768), (4, 1000, 4096, 768), (5, 130, 1536, 768)])
+def test_q8_prologue_equals_f16_weights(dev, kind, M, N, K):
+    """The Q8_0 prologue (int8 tiles and block scales dequantised in shared memory by the
+    converter warps) gives the same bits as the GEMM on the f16 weights q * d."""
+    q, dT, w16 = q8_weights(N, K, dev, seed=kind * 7 + M)
+    A = torch.randn(M, K, device=dev).half()
+    f32 = kind in (0, 2)
+    width = N // 2 if kind in (4, 5) else N
+    outs = []
+    for use_q8 in (False, True):
+        out = torch.full((M, width), 0.5, device=dev, dtype=torch.float32 if f32 else torch.float16)
+        kw = dict(Bq=q, Bd=dT, ldd=N) if use_q8 else {}
+        run(kind, A, w16, M, N, K, out=out, ldo=width, resid=out if kind == 2 else None, **kw)
+        outs.append(out.cpu())
+    assert torch.equal(outs[0].view(torch.int32 if f32 else torch.int16), outs[1].view(torch.int32 if f32 else torch.int16))
+    if kind == 0:
+        close(outs[1].to(dev), ref_mm(A, w16), K)
 
 
 def test_resid_remap(dev):

@@ -22,6 +22,7 @@ enum DeviceError : int {
     kDevBadShape = 6,         // position outside the RoPE table, or a NaN raw quantile
     kDevNaN = 7,              // a capped forecast value is NaN (reference: degenerate input)
     kDevNonFinite = 8,        // a final forecast value is not finite
+    kDevTimeoutConv = 9,      // Q8_0 GEMM: weights never converted / int8 stage never filled
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {
@@ -141,6 +142,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t ran
 // have completed, tcgen05.wait::ld).
 __device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Arrive with release semantics (cluster scope) on an mbarrier given by its shared::cluster
+// address: the caller's earlier shared-memory writes are visible to whoever waits on it.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // Every thread of both CTAs of the cluster.
 __device__ __forceinline__ void cluster_sync() {

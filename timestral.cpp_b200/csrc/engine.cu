@@ -82,8 +82,23 @@ struct DevBuf {
     template <class T> T* as() const { return static_cast<T*>(p); }
 };
 
+// Q8_0 weights in the device format of the GEMM's dequantising prologue: int8 values [N][K]
+// and the f16 scale of every 32-value block, transposed to [K / 32][N] (ldd = N).
+struct Q8W {
+    const int8_t* q = nullptr;
+    const __half* d = nullptr;
+    int64_t ldd = 0;
+};
+// The same on the host while the weights are rearranged: d [N][K / 32] in row order.
+struct Q8Host {
+    std::vector<int8_t> q;
+    std::vector<uint16_t> d;
+    size_t N = 0, K = 0;
+};
+
 struct AttnW {
     bool time = true, gate = false;
+    Q8W qkvg_q8, vg_q8, out_q8;   // Q8_0 twins of qkvg, vg, out (null when not Q8_0)
     const float* norm = nullptr;
     // tensor-core path
     __half* qkvg = nullptr; float* b_qkvg = nullptr; int n_qkvg = 0;   // [3D or 4D][D]
@@ -95,6 +110,7 @@ struct AttnW {
 };
 struct MlpW {
     const float* norm = nullptr;
+    Q8W w12_q8, w3_q8;
     __half* w12 = nullptr; float* b12 = nullptr;    // tensor cores: [g|u] per tile
     __half* w3 = nullptr; float* b3 = nullptr;
     float* f12 = nullptr; float* fb12 = nullptr; float* f3 = nullptr; float* fb3 = nullptr;
@@ -123,6 +139,8 @@ struct Engine::Impl {
     std::vector<MlpW> mlp;
     const float* out_norm = nullptr;
     __half* h_hid = nullptr; __half* h_out = nullptr; __half* h_res = nullptr;
+    Q8W p_out_q8, h_hid_q8, h_out_q8, h_res_q8;
+    bool q8_prologue = false;    // Q8_0 weights dequantised in the GEMM prologue (else the f16 copies)
     float* fh_hid = nullptr; float* fh_out = nullptr; float* fh_res = nullptr;
     // workspace
     DevBuf rows, mask, win, wmask, role, future, fmask, feat, aloc, ascale, caplo, caphi, capsc, first_obs, kv, rope_row,
@@ -262,6 +280,75 @@ struct Engine::Impl {
         if (!mv.has(n)) return nullptr;
         return const_cast<float*>(f32_tensor(n));
     }
+    // --- Q8_0 twins ------------------------------------------------------------------
+    static bool q8_type(const HostTensor& w) { return w.type == TT_Q8_0 && w.ne0 % 32 == 0; }
+    // GGUF Q8_0 rows (blocks of 34 bytes: f16 d, then 32 int8 values) as values and scales.
+    static Q8Host q8_rows(const HostTensor& w) {
+        Q8Host h;
+        h.K = size_t(w.ne0); h.N = size_t(w.ne1);
+        const size_t nb = h.K / 32;
+        h.q.resize(h.N * h.K);
+        h.d.resize(h.N * nb);
+        const uint8_t* p = static_cast<const uint8_t*>(w.data);
+        for (size_t n = 0; n < h.N; ++n)
+            for (size_t b = 0; b < nb; ++b) {
+                const uint8_t* blk = p + (n * nb + b) * 34;
+                std::memcpy(&h.d[n * nb + b], blk, 2);
+                std::memcpy(&h.q[n * h.K + b * 32], blk + 2, 32);
+            }
+        return h;
+    }
+    static void q8_append(Q8Host& a, const Q8Host& b) {
+        a.q.insert(a.q.end(), b.q.begin(), b.q.end());
+        a.d.insert(a.d.end(), b.d.begin(), b.d.end());
+        a.N += b.N;
+    }
+    // Rows [r0, r0 + n) of a twin.
+    static Q8Host q8_slice(const Q8Host& a, size_t r0, size_t n) {
+        Q8Host h;
+        h.K = a.K; h.N = n;
+        const size_t nb = a.K / 32;
+        h.q.assign(a.q.begin() + r0 * a.K, a.q.begin() + (r0 + n) * a.K);
+        h.d.assign(a.d.begin() + r0 * nb, a.d.begin() + (r0 + n) * nb);
+        return h;
+    }
+    // Two twins of `rows` rows each interleaved per tile, as interleave() does for f16 rows.
+    static Q8Host q8_interleave(const Q8Host& a, const Q8Host& b, size_t rows) {
+        Q8Host h;
+        h.K = a.K; h.N = 2 * rows;
+        const size_t nb = a.K / 32, half = kTile / 2;
+        for (size_t tile = 0; tile < rows / half; ++tile)
+            for (const Q8Host* src : {&a, &b}) {
+                h.q.insert(h.q.end(), src->q.begin() + tile * half * a.K, src->q.begin() + (tile + 1) * half * a.K);
+                h.d.insert(h.d.end(), src->d.begin() + tile * half * nb, src->d.begin() + (tile + 1) * half * nb);
+            }
+        return h;
+    }
+    Q8W q8_upload(const Q8Host& h) {
+        const size_t nb = h.K / 32;
+        std::vector<uint16_t> dt(nb * h.N);
+        for (size_t n = 0; n < h.N; ++n)
+            for (size_t b = 0; b < nb; ++b) dt[b * h.N + n] = h.d[n * nb + b];
+        Q8W w;
+        w.q = upload(h.q.data(), h.q.size());
+        w.d = reinterpret_cast<const __half*>(upload(dt.data(), dt.size()));
+        w.ldd = int64_t(h.N);
+        return w;
+    }
+    static bool unit_gains(const float* w, size_t n) {
+        for (size_t i = 0; i < n; ++i)
+            if (w[i] != 1.0f) return false;
+        return true;
+    }
+    // B operand of a GEMM from a twin when the prologue mode is on (row offset into it).
+    void q8(GemmArgs& g, const Q8W& w, int64_t row0 = 0) const {
+        if (!q8_prologue || !w.q) return;
+        g.Bq = w.q + row0 * g.K;
+        g.Bd = w.d + row0;
+        g.ldd = w.ldd;
+        g.ldb = g.K;
+    }
+
     // Two [rows][K] blocks interleaved per tile: [a rows t*128.. | b rows t*128..].
     static std::vector<uint16_t> interleave(const uint16_t* a, const uint16_t* b, size_t rows, size_t K) {
         std::vector<uint16_t> out(2 * rows * K);
@@ -337,7 +424,10 @@ struct Engine::Impl {
         p_hid = const_cast<float*>(f32_tensor("patch.hidden.weight")); pb_hid = bias_or_null("patch.hidden.bias");
         p_res = const_cast<float*>(f32_tensor("patch.res.weight")); pb_res = bias_or_null("patch.res.bias");
         pb_out = bias_or_null("patch.out.bias");
-        if (tc) { auto v = rows_f16(t("patch.out.weight")); p_out = reinterpret_cast<__half*>(upload(v.data(), v.size())); }
+        if (tc) {
+            auto v = rows_f16(t("patch.out.weight")); p_out = reinterpret_cast<__half*>(upload(v.data(), v.size()));
+            if (q8_type(t("patch.out.weight"))) p_out_q8 = q8_upload(q8_rows(t("patch.out.weight")));
+        }
         else { auto v = rows_f32(t("patch.out.weight")); f_pout = upload(v.data(), v.size()); }
         // Tensor-core patch projections (K = 2 * patch_size, F32 weights): the weights split into
         // f16 hi/lo terms, rows of 3K f16 that stay 16-byte aligned.
@@ -404,6 +494,17 @@ struct Engine::Impl {
                     }
                     auto o = rows_f16(t(p + "out.weight"));
                     a.out = reinterpret_cast<__half*>(upload(o.data(), o.size()));
+                    // Q8_0 twins; the norm gain folded into q/k/v/gate must be a no-op for them.
+                    if (q8_type(t(p + "out.weight"))) a.out_q8 = q8_upload(q8_rows(t(p + "out.weight")));
+                    if (q8_type(t(p + "qkv.weight")) && (!a.gate || q8_type(t(p + "gate.weight"))) &&
+                        unit_gains(nw, size_t(D))) {
+                        Q8Host qk = q8_rows(t(p + "qkv.weight"));
+                        Q8Host gt;
+                        if (a.gate) { gt = q8_rows(t(p + "gate.weight")); q8_append(qk, gt); }
+                        a.qkvg_q8 = q8_upload(qk);
+                        if (!a.time && a.gate)
+                            a.vg_q8 = q8_upload(q8_interleave(q8_slice(qk, size_t(2) * D, size_t(D)), gt, size_t(D)));
+                    }
                 } else {
                     auto q = rows_f32(t(p + "qkv.weight"));
                     a.f_qkv = upload(q.data(), q.size());
@@ -436,6 +537,12 @@ struct Engine::Impl {
                 }
                 auto w3 = rows_f16(t(b + "ffn_w3.weight"));
                 w.w3 = reinterpret_cast<__half*>(upload(w3.data(), w3.size()));
+                if (q8_type(t(b + "ffn_w3.weight"))) w.w3_q8 = q8_upload(q8_rows(t(b + "ffn_w3.weight")));
+                if (q8_type(t(b + "ffn_w12.weight")) &&
+                    unit_gains(static_cast<const float*>(t(b + "ffn_norm.weight").data), size_t(D))) {
+                    Q8Host z12 = q8_rows(t(b + "ffn_w12.weight"));
+                    w.w12_q8 = q8_upload(q8_interleave(q8_slice(z12, 0, size_t(F)), q8_slice(z12, size_t(F), size_t(F)), size_t(F)));
+                }
             } else {
                 auto z = rows_f32(t(b + "ffn_w12.weight"));
                 w.f12 = upload(z.data(), z.size());
@@ -450,6 +557,9 @@ struct Engine::Impl {
             auto a = rows_f16(t("head.hidden.weight")); h_hid = reinterpret_cast<__half*>(upload(a.data(), a.size()));
             auto b = rows_f16(t("head.out.weight")); h_out = reinterpret_cast<__half*>(upload(b.data(), b.size()));
             auto c = rows_f16(t("head.res.weight")); h_res = reinterpret_cast<__half*>(upload(c.data(), c.size()));
+            if (q8_type(t("head.hidden.weight"))) h_hid_q8 = q8_upload(q8_rows(t("head.hidden.weight")));
+            if (q8_type(t("head.out.weight"))) h_out_q8 = q8_upload(q8_rows(t("head.out.weight")));
+            if (q8_type(t("head.res.weight"))) h_res_q8 = q8_upload(q8_rows(t("head.res.weight")));
         } else {
             auto a = rows_f32(t("head.hidden.weight")); fh_hid = upload(a.data(), a.size());
             auto b = rows_f32(t("head.out.weight")); fh_out = upload(b.data(), b.size());
@@ -625,6 +735,7 @@ struct Engine::Impl {
             a.A = ph.as<__half>(); a.lda = 4 * D; a.B = p_out; a.ldb = 4 * D; a.M = int(PR); a.N = D; a.K = 4 * D;
             a.epi.out = x.p; a.epi.ldo = D; a.epi.bias = pb_out; a.epi.resid = x.as<float>();
             a.epi.row_group = N; a.epi.row_stride = S;
+            q8(a, p_out_q8);
             gemm(EPI_RESID, a);
         } else {
             SimtGemm g;
@@ -685,12 +796,14 @@ struct Engine::Impl {
                 GemmArgs a;
                 a.A = a_in; a.lda = D; a.B = w.w12; a.ldb = D; a.M = Mm; a.N = 2 * F; a.K = D;
                 a.epi.out = hb.p; a.epi.ldo = F; a.epi.bias = w.b12;
+                q8(a, w.w12_q8);
                 gather_a(a);
                 consume(a.epi);
                 gemm(EPI_SWIGLU, a);
                 GemmArgs o;
                 o.A = hb.as<__half>(); o.lda = F; o.B = w.w3; o.ldb = F; o.M = Mm; o.N = D; o.K = F;
                 o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = w.b3; o.epi.resid = x.as<float>();
+                q8(o, w.w3_q8);
                 if (in_tail) scatter_out(o.epi);
                 produce(o.epi);
                 gemm(EPI_RESID, o);
@@ -723,14 +836,17 @@ struct Engine::Impl {
             GemmArgs a;
             a.A = dec.as<__half>(); a.lda = D; a.B = h_hid; a.ldb = D; a.M = DR; a.N = 4 * D; a.K = D;
             a.epi.out = hh.p; a.epi.ldo = 4 * D;
+            q8(a, h_hid_q8);
             gemm(EPI_SILU, a);
             GemmArgs b;
             b.A = hh.as<__half>(); b.lda = 4 * D; b.B = h_out; b.ldb = 4 * D; b.M = DR; b.N = NQ; b.K = 4 * D;
             b.epi.out = hraw.p; b.epi.ldo = NQ;
+            q8(b, h_out_q8);
             gemm(EPI_F32, b);
             GemmArgs c;
             c.A = dec.as<__half>(); c.lda = D; c.B = h_res; c.ldb = D; c.M = DR; c.N = NQ; c.K = D;
             c.epi.out = hraw.p; c.epi.ldo = NQ; c.epi.resid = hraw.as<float>();
+            q8(c, h_res_q8);
             gemm(EPI_RESID, c);
         } else {
             const int order = round_a ? ORDER_CHAIN : ORDER_F64;
@@ -789,16 +905,18 @@ struct Engine::Impl {
             g.A = a_in; g.lda = D; g.M = M; g.K = D; g.epi.out = att16; g.epi.ldo = D;
             if (tail_stage == 2) gather_a(g);
             consume(g.epi);
-            if (a.gate) { g.B = a.vg; g.ldb = D; g.N = 2 * D; g.epi.bias = a.b_vg; gemm(EPI_VGATE, g); }
+            if (a.gate) { g.B = a.vg; g.ldb = D; g.N = 2 * D; g.epi.bias = a.b_vg; q8(g, a.vg_q8); gemm(EPI_VGATE, g); }
             else {
                 g.B = a.qkvg + size_t(2) * D * D; g.ldb = D; g.N = D;
                 g.epi.bias = a.b_qkvg ? a.b_qkvg + 2 * D : nullptr;
+                q8(g, a.qkvg_q8, int64_t(2) * D);
                 gemm(EPI_F16, g);
             }
         } else {
             GemmArgs g;
             g.A = a_in; g.lda = D; g.B = a.qkvg; g.ldb = D; g.M = M; g.N = a.n_qkvg; g.K = D;
             g.epi.bias = a.b_qkvg;
+            q8(g, a.qkvg_q8);
             consume(g.epi);
             g.epi.qkvg[0] = qb.as<__half>(); g.epi.qkvg[1] = kb.as<__half>(); g.epi.qkvg[2] = vb.as<__half>();
             g.epi.qkvg[3] = gb.as<__half>();
@@ -825,6 +943,7 @@ struct Engine::Impl {
         }
         o.A = att16; o.lda = D; o.B = a.out; o.ldb = D; o.N = D; o.K = D;
         o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = a.b_out; o.epi.resid = x.as<float>();
+        q8(o, a.out_q8);
         if (tail_stage) scatter_out(o.epi);
         produce(o.epi);
         gemm(EPI_RESID, o);
@@ -1069,6 +1188,14 @@ void Engine::attention_kernels(int mode) {
     impl_->attn_simt = mode == 1;
     impl_->drop_graph();
     impl_->have_last = false;
+}
+
+bool Engine::q8_prologue(bool on) {
+    const bool any = impl_->p_out_q8.q || impl_->h_hid_q8.q || (!impl_->mlp.empty() && impl_->mlp[0].w3_q8.q);
+    impl_->q8_prologue = on && any;
+    impl_->drop_graph();
+    impl_->have_last = false;
+    return impl_->q8_prologue == on;
 }
 
 void Engine::decoder_tail(bool on) {

@@ -36,6 +36,13 @@ constexpr int A_BYTES = BM * BK * 2;          // 16 KB
 constexpr int B_BYTES = BN_HALF * BK * 2;     // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;             // 512: two accumulators
+// Q8_0 prologue: each stage also holds the CTA's int8 weight tile (128 rows x 64) and the
+// f16 scales of its two 32-value blocks (2 x 128), which the converter warps turn into the
+// f16 B tile of the same stage.
+constexpr int BQ_BYTES = BN_HALF * BK;        // 8 KB
+constexpr int BD_BYTES = 2 * BN_HALF * 2;     // 512 B
+constexpr int Q8_STAGE_BYTES = STAGE_BYTES + BQ_BYTES + 1024;   // scales padded: stages stay 1 KB aligned
+constexpr int CONV_WARPS = 2;                 // 384 threads with the 8 epilogue warps: no spills
 
 // Per epilogue kind: PARTS column groups per TMEM lane quarter (epilogue warps = 4 * PARTS).
 // The q/k/v/gate epilogue (RoPE tables in registers) and the residual add (residual rows in
@@ -43,14 +50,17 @@ constexpr int TMEM_COLS = 2 * BN;             // 512: two accumulators
 // the activation and plain-store epilogues run four groups of 64, which doubles the warps
 // that hide the epilogue's latency at 96 registers a thread; their staging blocks leave room
 // for five operand stages instead of six.
-template <int KIND>
+// Q8: the Q8_0 prologue variant, which adds CONV_WARPS converter warps after the epilogue
+// warps, uses two column groups for every epilogue kind (register budget) and four stages.
+template <int KIND, bool Q8 = false>
 struct Cfg {
-    static constexpr int PARTS = (KIND == EPI_QKVG || KIND == EPI_RESID) ? 2 : 4;
+    static constexpr int PARTS = (Q8 || KIND == EPI_QKVG || KIND == EPI_RESID) ? 2 : 4;
     static constexpr int EPI_WARPS = 4 * PARTS;
-    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-    static constexpr int STAGES = PARTS == 2 ? 6 : 5;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS + (Q8 ? 32 * CONV_WARPS : 0);
+    static constexpr int STAGE = Q8 ? Q8_STAGE_BYTES : STAGE_BYTES;
+    static constexpr int STAGES = Q8 ? 4 : PARTS == 2 ? 6 : 5;
     static constexpr int EPI_STAGE_BYTES = EPI_WARPS * 32 * 128;   // per-warp transposition blocks
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int SMEM_BYTES = STAGES * STAGE + EPI_STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 };
 
@@ -60,9 +70,27 @@ struct Smem {
     uint64_t empty[STAGES];
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
+    uint64_t bfull[STAGES];   // Q8: this CTA's int8 tile and scales arrived
+    uint64_t conv[STAGES];    // Q8 (CTA 0): both CTAs' f16 tiles written
     uint32_t tmem_base;
     int abort;
 };
+static_assert(sizeof(Smem<6>) <= 512, "barrier block");
+
+// Four signed int8 values (one word, value k in byte k) times the f16 scale pair d2: two
+// half2 words (values 0,1 and 2,3). Each byte b becomes the f16 1024 + (b + 128) by placing it
+// under the exponent 0x64, so subtracting 1152 gives b exactly; one f16 multiply then rounds
+// b * d once, as rounding the exact product at load does.
+__device__ __forceinline__ void dequant4(uint32_t w, __half2 d2, uint32_t& lo, uint32_t& hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint32_t p0 = __byte_perm(u, 0x64646464u, 0x5140);
+    const uint32_t p1 = __byte_perm(u, 0x64646464u, 0x5342);
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));   // 1152
+    __half2 a = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&p0), bias), d2);
+    __half2 b = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&p1), bias), d2);
+    lo = *reinterpret_cast<uint32_t*>(&a);
+    hi = *reinterpret_cast<uint32_t*>(&b);
+}
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -409,15 +437,17 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
     }
 }
 
-template <int KIND>
-__global__ void __launch_bounds__(Cfg<KIND>::THREADS, 1)
+template <int KIND, bool Q8>
+__global__ void __launch_bounds__(Cfg<KIND, Q8>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_bq, const __grid_constant__ CUtensorMap map_bd,
                    const GemmArgs g, int* err) {
-    constexpr int STAGES = Cfg<KIND>::STAGES, EPI_WARPS = Cfg<KIND>::EPI_WARPS, PARTS = Cfg<KIND>::PARTS;
+    using CF = Cfg<KIND, Q8>;
+    constexpr int STAGES = CF::STAGES, EPI_WARPS = CF::EPI_WARPS, PARTS = CF::PARTS, SB = CF::STAGE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stage = tiles + STAGES * STAGE_BYTES;
-    Smem<STAGES>* sm = reinterpret_cast<Smem<STAGES>*>(stage + Cfg<KIND>::EPI_STAGE_BYTES);
+    uint8_t* stage = tiles + STAGES * SB;
+    Smem<STAGES>* sm = reinterpret_cast<Smem<STAGES>*>(stage + CF::EPI_STAGE_BYTES);
     volatile int* abort = &sm->abort;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -428,13 +458,20 @@ __global__ void __launch_bounds__(Cfg<KIND>::THREADS, 1)
     const int k_blocks = (g.K + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) { mbar_init(&sm->full[s], 1); mbar_init(&sm->empty[s], 1); }
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&sm->full[s], 1); mbar_init(&sm->empty[s], 1);
+            mbar_init(&sm->bfull[s], 1); mbar_init(&sm->conv[s], 2 * CONV_WARPS);
+        }
         for (int b = 0; b < 2; ++b) { mbar_init(&sm->acc_full[b], 1); mbar_init(&sm->acc_empty[b], 2 * EPI_WARPS); }
         sm->abort = 0;
         mbar_fence_init();
         fence_proxy_async();
     }
-    if (warp == 0 && lane == 0) { tma_prefetch_desc(&map_a); tma_prefetch_desc(&map_b); }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&map_a);
+        if constexpr (Q8) { tma_prefetch_desc(&map_bq); tma_prefetch_desc(&map_bd); }
+        else tma_prefetch_desc(&map_b);
+    }
     if (warp == 1) { tmem_alloc_pair(&sm->tmem_base, TMEM_COLS); tmem_relinquish_pair(); }
     tc_fence_before();
     cluster_sync();                                   // barriers of both CTAs initialised
@@ -451,12 +488,21 @@ __global__ void __launch_bounds__(Cfg<KIND>::THREADS, 1)
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
                     if (!wait_or_abort(&sm->empty[s], ph ^ 1, abort, err, kDevTimeoutEmpty)) break;
-                    uint8_t* a = tiles + s * STAGE_BYTES;
-                    if (rank == 0) mbar_arrive_expect_tx(&sm->full[s], 2 * STAGE_BYTES);
+                    uint8_t* a = tiles + s * SB;
+                    if (rank == 0) mbar_arrive_expect_tx(&sm->full[s], Q8 ? 2 * A_BYTES : 2 * STAGE_BYTES);
                     const uint32_t full0 = mapa_shared(smem_u32(&sm->full[s]), 0);
                     if (g.a_group > 0) tma_load_3d_pair(a, &map_a, full0, kb * BK, 0, m0 / g.a_group);
                     else tma_load_2d_pair(a, &map_a, full0, kb * BK, m0);
-                    tma_load_2d_pair(a + A_BYTES, &map_b, full0, kb * BK, n0);
+                    if constexpr (Q8) {
+                        // This CTA's int8 rows and their scales, on its own barrier (its converter
+                        // warps wait for them); the f16 tile is written by those warps.
+                        uint8_t* bq = a + STAGE_BYTES;
+                        mbar_arrive_expect_tx(&sm->bfull[s], BQ_BYTES + BD_BYTES);
+                        tma_load_2d(bq, &map_bq, &sm->bfull[s], kb * BK, n0);
+                        tma_load_2d(bq + BQ_BYTES, &map_bd, &sm->bfull[s], n0, kb * (BK / 32));
+                    } else {
+                        tma_load_2d_pair(a + A_BYTES, &map_b, full0, kb * BK, n0);
+                    }
                 }
             }
         }
@@ -475,8 +521,11 @@ __global__ void __launch_bounds__(Cfg<KIND>::THREADS, 1)
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
                     if (!wait_or_abort(&sm->full[s], ph, abort, err, kDevTimeoutFull)) { ok = false; break; }
+                    if constexpr (Q8) {
+                        if (!wait_or_abort(&sm->conv[s], ph, abort, err, kDevTimeoutConv)) { ok = false; break; }
+                    }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(tiles + s * STAGE_BYTES);
+                    const uint32_t a_addr = smem_u32(tiles + s * SB);
                     const uint64_t adesc = smem_desc_sw128(a_addr), bdesc = smem_desc_sw128(a_addr + A_BYTES);
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
@@ -485,6 +534,45 @@ __global__ void __launch_bounds__(Cfg<KIND>::THREADS, 1)
                 }
                 if (!ok) break;
                 mma_commit_pair(&sm->acc_full[b]);
+            }
+        }
+    } else if (Q8 && warp >= 2 + EPI_WARPS) {
+        // Converter warps: warp c writes rows [64 c, 64 c + 64) of this CTA's f16 B tile of each
+        // stage from its int8 tile. A lane takes 16 values (16 bytes) of one row per step, eight
+        // rows per warp step: the int8 reads cover 512 contiguous bytes, and the two 16-byte f16
+        // chunks a lane writes land in distinct banks (128-byte swizzle of the tile).
+        const int cw = warp - 2 - EPI_WARPS;
+        const int c = lane & 3;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = pair; ok && tile < num_tiles; tile += pairs) {
+            for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1;
+                ok = __all_sync(0xffffffffu, wait_or_abort(&sm->bfull[s], ph, abort, err, kDevTimeoutConv));
+                if (!ok) break;
+                uint8_t* base = tiles + s * SB;
+                const uint8_t* bq = base + STAGE_BYTES;
+                const __half* bd = reinterpret_cast<const __half*>(bq + BQ_BYTES);
+                uint8_t* bf = base + A_BYTES;
+                constexpr int ROWS = BN_HALF / CONV_WARPS;
+#pragma unroll 4
+                for (int i = 0; i < ROWS / 8; ++i) {
+                    const int r = cw * ROWS + i * 8 + (lane >> 2);
+                    const uint4 q = *reinterpret_cast<const uint4*>(bq + r * BK + c * 16);
+                    const __half d = bd[(c >> 1) * BN_HALF + r];
+                    const __half2 d2 = __halves2half2(d, d);
+                    uint32_t h[8];
+                    dequant4(q.x, d2, h[0], h[1]);
+                    dequant4(q.y, d2, h[2], h[3]);
+                    dequant4(q.z, d2, h[4], h[5]);
+                    dequant4(q.w, d2, h[6], h[7]);
+                    *reinterpret_cast<uint4*>(bf + r * 128 + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<uint4*>(bf + r * 128 + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+                }
+                fence_proxy_async();                  // generic-proxy writes -> tensor-core reads
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&sm->conv[s]), 0));
             }
         }
     } else {
@@ -573,6 +661,22 @@ bool make_map_gather_f16(CUtensorMap* map, const void* base, int64_t groups, int
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2D tensor map without swizzle over a row-major [rows][cols] matrix of 1- or 2-byte
+// elements (pitch `ld_bytes`), box {box_cols, box_rows}: the Q8_0 int8 weight tiles and their
+// scale blocks.
+bool make_map_2d_plain(CUtensorMap* map, const void* base, CUtensorMapDataType type, int64_t rows, int64_t cols,
+                       int64_t ld_bytes, int box_cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(ld_bytes)};
+    cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
 // 3D f16 tensor map over [planes][rows][64] (head-major q/k/v), box {64, box_rows, 1}.
 bool make_map_3d_f16(CUtensorMap* map, const void* base, int64_t planes, int64_t rows, int box_rows) {
     auto fn = encode_fn();
@@ -599,31 +703,40 @@ int device_sm_count() {
     return counts[dev];
 }
 
-template <int KIND>
+template <int KIND, bool Q8>
 static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg<KIND>::SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<KIND, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg<KIND, Q8>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mq, md;
     const bool map_a = a.a_group > 0
         ? make_map_gather_f16(&ma, a.A + int64_t(a.a_offset) * a.lda, (a.M + a.a_group - 1) / a.a_group, a.a_group,
                               a.a_stride, a.K, a.lda, BM / a.a_group)
         : make_map_2d_f16(&ma, a.A, a.M, a.K, a.lda, BM);
-    if (!map_a || !make_map_2d_f16(&mb, a.B, a.N, a.K, a.ldb, BN_HALF)) return cudaErrorInvalidValue;
+    if (!map_a) return cudaErrorInvalidValue;
+    if constexpr (Q8) {
+        if (!make_map_2d_plain(&mq, a.Bq, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.N, a.K, a.ldb, BK, BN_HALF) ||
+            !make_map_2d_plain(&md, a.Bd, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (a.K + 31) / 32, a.N, a.ldd * 2, BN_HALF, BK / 32))
+            return cudaErrorInvalidValue;
+        mb = mq;                                      // unused by this variant
+    } else {
+        if (!make_map_2d_f16(&mb, a.B, a.N, a.K, a.ldb, BN_HALF)) return cudaErrorInvalidValue;
+        mq = mb; md = mb;                             // unused by this variant
+    }
     // One CTA pair (cluster of two) per two SMs, persistent over the 256 x 256 tiles.
     const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN);
     const int max_pairs = device_sm_count() / 2;
     const int pairs = tiles < max_pairs ? tiles : max_pairs;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(Cfg<KIND>::THREADS);
-    cfg.dynamicSmemBytes = Cfg<KIND>::SMEM_BYTES;
+    cfg.blockDim = dim3(Cfg<KIND, Q8>::THREADS);
+    cfg.dynamicSmemBytes = Cfg<KIND, Q8>::SMEM_BYTES;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -632,15 +745,26 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<KIND>, ma, mb, a, err);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<KIND, Q8>, ma, mb, mq, md, a, err);
+}
+
+template <int KIND>
+static cudaError_t launch_kind(const GemmArgs& a, cudaStream_t stream, int* err) {
+    return a.Bq ? launch<KIND, true>(a, stream, err) : launch<KIND, false>(a, stream, err);
 }
 
 cudaError_t tc_gemm(EpiKind kind, const GemmArgs& a, cudaStream_t stream, int* err) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaSuccess;
-    // TMA: 16-byte aligned base and row pitch.
-    if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15) || (a.lda * 2) % 16 ||
-        (a.ldb * 2) % 16 || a.N % 16)
+    // TMA: 16-byte aligned bases and row pitches (f16 B: ldb elements; int8 Bq: ldb bytes;
+    // scales Bd: ldd f16 per block row, at least N).
+    if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (a.lda * 2) % 16 || a.N % 16) return cudaErrorInvalidValue;
+    if (a.Bq) {
+        if ((reinterpret_cast<uintptr_t>(a.Bq) & 15) || (reinterpret_cast<uintptr_t>(a.Bd) & 15) || a.ldb % 16 ||
+            (a.ldd * 2) % 16 || a.ldd < a.N || a.K % 32)
+            return cudaErrorInvalidValue;
+    } else if ((reinterpret_cast<uintptr_t>(a.B) & 15) || (a.ldb * 2) % 16) {
         return cudaErrorInvalidValue;
+    }
     if ((kind == EPI_SWIGLU || kind == EPI_VGATE) && a.N % BN) return cudaErrorInvalidValue;
     // Row gather: whole groups per 128-row box, groups inside the strided rows, 16-byte base.
     if (a.a_group < 0 || (a.a_group > 0 && (BM % a.a_group || a.M % a.a_group || a.a_offset < 0 ||
@@ -662,13 +786,13 @@ cudaError_t tc_gemm(EpiKind kind, const GemmArgs& a, cudaStream_t stream, int* e
             return cudaErrorInvalidValue;
     }
     switch (kind) {
-        case EPI_F32: return launch<EPI_F32>(a, stream, err);
-        case EPI_F16: return launch<EPI_F16>(a, stream, err);
-        case EPI_RESID: return launch<EPI_RESID>(a, stream, err);
-        case EPI_SILU: return launch<EPI_SILU>(a, stream, err);
-        case EPI_SWIGLU: return launch<EPI_SWIGLU>(a, stream, err);
-        case EPI_VGATE: return launch<EPI_VGATE>(a, stream, err);
-        case EPI_QKVG: return launch<EPI_QKVG>(a, stream, err);
+        case EPI_F32: return launch_kind<EPI_F32>(a, stream, err);
+        case EPI_F16: return launch_kind<EPI_F16>(a, stream, err);
+        case EPI_RESID: return launch_kind<EPI_RESID>(a, stream, err);
+        case EPI_SILU: return launch_kind<EPI_SILU>(a, stream, err);
+        case EPI_SWIGLU: return launch_kind<EPI_SWIGLU>(a, stream, err);
+        case EPI_VGATE: return launch_kind<EPI_VGATE>(a, stream, err);
+        case EPI_QKVG: return launch_kind<EPI_QKVG>(a, stream, err);
     }
     return cudaErrorInvalidValue;
 }

@@ -63,6 +63,14 @@ struct GemmArgs {
     int a_group = 0, a_stride = 0, a_offset = 0;
     const __half* B = nullptr;
     int64_t ldb = 0;
+    // Q8_0 weights dequantised in the GEMM prologue (used instead of B when Bq is set): int8
+    // values Bq [N][K] (row pitch ldb bytes) and the f16 scale of every 32-value block,
+    // Bd [K / 32][ldd] (scale of row n, block j at Bd[j * ldd + n]). In shared memory each
+    // int8 tile becomes the f16 tile the tensor cores read, value q * d rounded once to f16:
+    // the same f16 weights as dequantising at load.
+    const int8_t* Bq = nullptr;
+    const __half* Bd = nullptr;
+    int64_t ldd = 0;
     int M = 0, N = 0, K = 0;
     GemmEpilogue epi;
 };

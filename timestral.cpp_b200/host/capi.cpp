@@ -471,6 +471,22 @@ TIMESTRAL_API int tsb_attention_kernels(timestral_ctx* c, int32_t mode) {
     return TSB_OK;
 }
 
+TIMESTRAL_API int tsb_q8_prologue(timestral_ctx* c, int32_t on) {
+    if (!c) return TSB_ERR_ARG;
+    try {
+        bool ok = true;
+        for (size_t k = 0; k < c->gpus(); ++k) ok &= c->gpu(k).engine().q8_prologue(on != 0);
+        if (!ok) {
+            c->error.set("tsb_q8_prologue: the model has no Q8_0 weights");
+            return TSB_ERR_MODEL;
+        }
+    } catch (...) {
+        caught(c);
+        return TSB_ERR_CUDA;
+    }
+    return TSB_OK;
+}
+
 TIMESTRAL_API int tsb_decoder_tail(timestral_ctx* c, int32_t on) {
     if (!c) return TSB_ERR_ARG;
     try {

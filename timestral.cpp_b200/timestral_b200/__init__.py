@@ -35,7 +35,7 @@ class GemmTest(C.Structure):
                 ("rope", C.c_int32), ("cos_tab", C.c_void_p), ("sin_tab", C.c_void_p),
                 ("rope_row", C.c_void_p), ("rope_half", C.c_int32),
                 ("rope_dup", C.c_int32), ("a_group", C.c_int32), ("a_stride", C.c_int32),
-                ("a_offset", C.c_int32)]
+                ("a_offset", C.c_int32), ("Bq", C.c_void_p), ("Bd", C.c_void_p), ("ldd", C.c_int64)]
 
 
 _lib = None
@@ -71,6 +71,7 @@ SIGNATURES = {
     "tsb_fused_norm": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_attention_kernels": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_decoder_tail": (C.c_int, [C.c_void_p, C.c_int32]),
+    "tsb_q8_prologue": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_test_scale_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_double] + [C.c_int32] * 6
                             + [C.c_void_p] * 8),
     "tsb_test_attention_time_ex": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 9 + [C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
@@ -203,6 +204,12 @@ class Model:
         the reference's float64 q.k dots and f32 softmax on the same f16 q/k/v."""
         if lib().tsb_attention_kernels(self.h, int(mode)) != 0:
             raise RuntimeError("tsb_attention_kernels failed")
+
+    def q8_prologue(self, on: bool):
+        """Q8_0 weights dequantised in the GEMM prologue (on) or read as f16 copies (off)."""
+        rc = lib().tsb_q8_prologue(self.h, int(on))
+        if rc != 0:
+            raise TimestralError(f"tsb_q8_prologue failed ({rc}): {self.last_error}")
 
     def decoder_tail(self, on: bool):
         """Last layer's per-token work on the decoder tokens alone (default on; same bits)."""
