@@ -113,7 +113,7 @@ def q8_weights(N, K, dev, seed):
     return q.to(dev), d.t().contiguous().to(dev), w16.to(dev)
 
 
-@pytest.mark.parametrize("kind,M,N,K", [(0, 300, 768, 768), (1, 700, 512, 256), (2, 513, 768, 3072),
+@pytest.mark.parametrize("kind,M,N,K", [(0, 300, 768, 768), (0, 77, 672, 3072), (1, 700, 512, 256), (2, 513, 768, 3072),
                                         (3, 257, 3072, 768), (4, 1000, 4096, 768), (5, 130, 1536, 768)])
 def test_q8_prologue_equals_f16_weights(dev, kind, M, N, K):
     """The Q8_0 prologue (int8 tiles and block scales dequantised in shared memory by the

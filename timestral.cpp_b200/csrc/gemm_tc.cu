@@ -92,12 +92,18 @@ __device__ __forceinline__ void dequant4(uint32_t w, __half2 d2, uint32_t& lo, u
     hi = *reinterpret_cast<uint32_t*>(&b);
 }
 
+template <bool CLUSTER = false>
+__device__ __forceinline__ bool try_wait_scoped(uint64_t* bar, uint32_t parity) {
+    return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+}
+
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (try_wait_scoped<CLUSTER>(bar, parity)) return true;
     const long long start = clock64();
     while (true) {
         if (*abort) return false;
-        if (mbar_try_wait(bar, parity)) return true;
+        if (try_wait_scoped<CLUSTER>(bar, parity)) return true;
         if (clock64() - start > kWaitCycles) {
             *abort = 1;
             record_error(err, code);
@@ -522,7 +528,7 @@ __global__ void __launch_bounds__(Cfg<KIND, Q8>::THREADS, 1)
                     const uint32_t ph = (it / STAGES) & 1;
                     if (!wait_or_abort(&sm->full[s], ph, abort, err, kDevTimeoutFull)) { ok = false; break; }
                     if constexpr (Q8) {
-                        if (!wait_or_abort(&sm->conv[s], ph, abort, err, kDevTimeoutConv)) { ok = false; break; }
+                        if (!wait_or_abort<true>(&sm->conv[s], ph, abort, err, kDevTimeoutConv)) { ok = false; break; }
                     }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(tiles + s * SB);
