@@ -59,10 +59,11 @@ CONFIGS = {
 }
 
 # DRAM bytes (read + write) of one time-attention (row, head) problem at S = 72: a constant
-# taken from one ncu capture of the kernel (B = 1024, dram__bytes_read.sum +
-# dram__bytes_write.sum over 24,576 problems), not measured by this script; traffic per
-# launch scales with the problems. The bench line says so in roofline.traffic_source.
-ATTN_DRAM_BYTES_PER_PROBLEM = 45300
+# taken from ncu captures of the kernel (B = 1024, dram__bytes_read.sum +
+# dram__bytes_write.sum over 24,576 problems, mean of two launches), not measured by this
+# script; traffic per launch scales with the problems. The bench line says so in
+# roofline.traffic_source.
+ATTN_DRAM_BYTES_PER_PROBLEM = 45220
 # The same for the long-row kernel at S = 1056 (cfg6), per (row, head) plane (B = 8: 119.4 MB
 # over 192 planes).
 ATTN_LONG_DRAM_BYTES_PER_PLANE = 621760
