@@ -79,13 +79,15 @@ TIMESTRAL_API int tsb_fused_norm(timestral_ctx* ctx, int32_t mode);
  * and the variate axis. Mode 1 is slower; it shows how much of a forecast's deviation from the
  * reference comes from the tensor-core attention. */
 TIMESTRAL_API int tsb_attention_kernels(timestral_ctx* ctx, int32_t mode);
-/* Q8_0 weights dequantised in the GEMM prologue (on = 1) instead of read as the f16 copies
- * made at load (on = 0, the default): the GEMM streams the int8 weight tiles and their f16
- * block scales (reference Q8_0 blocks, src/weight_policy.hpp:23-30) and converter warps write
- * the f16 tiles the tensor cores read, each value q * d rounded once to f16 as at load, so the
- * forecast is the same bits. Weights that carry a folded RMSNorm gain other than 1 keep their
- * f16 copy. Returns TSB_ERR_MODEL when the model has no Q8_0 weights. */
-TIMESTRAL_API int tsb_q8_prologue(timestral_ctx* ctx, int32_t on);
+/* Block-quantised weights dequantised in the GEMM prologue (on = 1) instead of read as the
+ * f16 copies made at load (on = 0, the default): the GEMM streams the int8 weight tiles with
+ * their block scales (Q8_0: the f16 scale of every 32 values, reference src/weight_policy.hpp:23-30)
+ * or scales and offsets (Q4_K/Q5_K/Q6_K, src/weight_policy.hpp:13-16: one f32 scale and
+ * offset per 16 values, unpacked from the super-blocks at load), and converter warps write the
+ * f16 tiles the tensor cores read, each value rounded once to f16 as at load, so the forecast
+ * is the same bits. Weights that carry a folded RMSNorm gain other than 1 keep their f16 copy.
+ * Returns TSB_ERR_MODEL when the model has no block-quantised weights. */
+TIMESTRAL_API int tsb_dequant_prologue(timestral_ctx* ctx, int32_t on);
 /* Decoder-token tail (on = 1, the default): the last layer of the 209M schedule starts with a
  * time sublayer and continues with per-token work (a one-row series' variate sublayer and
  * the MLP), and the head reads only the decoder tokens, so after that layer's time attention
@@ -122,6 +124,13 @@ TIMESTRAL_API int tsb_model_path(timestral_ctx* ctx);
  * (8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K) into float, as the loader expands such weights.
  * No GPU is used. */
 TIMESTRAL_API int tsb_dequantize_rows(uint32_t type, const void* src, int64_t rows, int64_t ne0, float* dst);
+/* Host-side unpacking of `rows` rows of ne0 elements of a block-quantised GGUF type (8 Q8_0,
+ * 12 Q4_K, 13 Q5_K, 14 Q6_K) into the form the GEMM's dequantising prologue reads: integer
+ * values q [rows][ne0] and, per 16 consecutive values, a scale a and an offset b
+ * ([rows][ne0 / 16] each), with tsb_dequantize_rows' value = (a * q) - b exactly in single
+ * precision. No GPU is used. */
+TIMESTRAL_API int tsb_scaled_int8_rows(uint32_t type, const void* src, int64_t rows, int64_t ne0, int8_t* q, float* a,
+                                       float* b);
 /* Geometry of the last decode block of the handle's last forecast: model rows (both
  * symmetric passes, every row role), tokens per row, context patches, decode blocks. */
 TIMESTRAL_API int tsb_last_geometry(timestral_ctx* ctx, int64_t* rows, int32_t* S, int32_t* L, int32_t* blocks);
@@ -169,6 +178,8 @@ typedef struct tsb_gemm_test {
                                              + a_offset + m % a_group (a_group 0: m) */
     const int8_t* Bq; const void* Bd; int64_t ldd;  /* Q8_0 B: int8 [N][ldb bytes], f16 scales
                                                        [K/32][ldd]; used instead of B when Bq is set */
+    const float* Bs; int64_t lds;                   /* scaled int8 B: (scale, offset) per 16 values,
+                                                       [K/16][lds][2]; used instead of Bd when set */
 } tsb_gemm_test;
 /* Runs one tensor-core GEMM on the current device and synchronizes. Returns a TSB_ code;
  * on TSB_ERR_DEVICE the kernel's error word is written to *dev_error. */

@@ -321,21 +321,29 @@ def test_209m_attention_share():
     assert not np.array_equal(tc, simt)
 
 
-def test_209m_q8_prologue_same_bits():
-    """Q8_0 weights dequantised in the GEMM prologue (tsb_q8_prologue) give the same forecast
-    bits as the f16 copies made at load: the converter rounds each q * d once to f16."""
-    m, _ = models(sy.spec_209m(), "q8_0")
+@pytest.mark.parametrize("kind", ["q8_0", "q6_k", "q4_k"])
+def test_209m_dequant_prologue_same_bits(kind):
+    """Block-quantised weights dequantised in the GEMM prologue (tsb_dequant_prologue: Q8_0 with
+    its f16 block scales, K-quants as int8 values with an f32 scale and offset per 16 values)
+    give the same forecast bits as the f16 copies made at load."""
+    if kind == "q8_0":
+        m, _ = models(sy.spec_209m(), kind)
+    else:
+        m = tb.Model(sy.cached_model(sy.spec_209m(), kind))
     x = sy.series_random_walk(3, 2048, nan_frac=0.02)
     try:
-        m.q8_prologue(True)
+        m.dequant_prologue(True)
         pro = m.forecast(x, 256).copy()
     finally:
-        m.q8_prologue(False)
+        m.dequant_prologue(False)
     ref = m.forecast(x, 256)
     assert np.array_equal(pro.view(np.uint32), ref.view(np.uint32))
+    if kind != "q8_0":
+        m.close()
+        return
     f16, _ = models(sy.spec_209m(), "f16")
-    with pytest.raises(tb.TimestralError, match="no Q8_0 weights"):
-        f16.q8_prologue(True)
+    with pytest.raises(tb.TimestralError, match="no block-quantised weights"):
+        f16.dequant_prologue(True)
 
 
 def test_209m_q8_against_f32():

@@ -21,7 +21,7 @@ def dp(t):
 
 def run(kind, A, B, M, N, K, out=None, ldo=0, bias=None, resid=None, row_group=0, row_stride=0, row_offset=0,
         qkvg=None, S=0, H=0, D=0, rope=0, cos=None, sin=None, rope_row=None, rope_half=32, rope_dup=0,
-        a_group=0, a_stride=0, a_offset=0, Bq=None, Bd=None, ldd=0):
+        a_group=0, a_stride=0, a_offset=0, Bq=None, Bd=None, ldd=0, Bs=None, lds=0):
     t = tb.GemmTest()
     t.kind, t.A, t.lda, t.B, t.ldb = kind, dp(A), A.shape[1], dp(B), B.shape[1]
     t.M, t.N, t.K = M, N, K
@@ -35,6 +35,7 @@ def run(kind, A, B, M, N, K, out=None, ldo=0, bias=None, resid=None, row_group=0
     t.rope_dup = rope_dup
     t.a_group, t.a_stride, t.a_offset = a_group, a_stride, a_offset
     t.Bq, t.Bd, t.ldd = dp(Bq), dp(Bd), ldd
+    t.Bs, t.lds = dp(Bs), lds
     if Bq is not None:
         t.B, t.ldb = None, Bq.shape[1]
     err = C.c_int32(0)
@@ -131,6 +132,39 @@ def test_q8_prologue_equals_f16_weights(dev, kind, M, N, K):
     assert torch.equal(outs[0].view(torch.int32 if f32 else torch.int16), outs[1].view(torch.int32 if f32 else torch.int16))
     if kind == 0:
         close(outs[1].to(dev), ref_mm(A, w16), K)
+
+
+@pytest.mark.parametrize("kind,M,N,K,lo,hi", [(0, 300, 768, 768, -32, 32), (2, 513, 768, 3072, 0, 16),
+                                              (4, 1000, 4096, 768, 0, 32), (6, 144, 3072, 768, -32, 32)])
+def test_kquant_prologue_equals_f16_weights(dev, kind, M, N, K, lo, hi):
+    """The scaled-int8 prologue (K-quant weights: int8 values with an f32 scale and offset per
+    16 values, dequantised by the converter warps as (scale * q) - offset, each operation
+    rounded in single precision, then once to f16) gives the same bits as the GEMM on those
+    f16 weights. Value ranges of Q6_K (-32..31), Q4_K (0..15) and Q5_K (0..31)."""
+    g = torch.Generator(device="cpu").manual_seed(kind * 13 + M)
+    q = torch.randint(lo, hi, (N, K), generator=g, dtype=torch.int8)
+    a = (torch.rand(N, K // 16, generator=g) * 0.003 + 1e-5)
+    b = torch.rand(N, K // 16, generator=g) * (0.02 if lo == 0 else 0.0)
+    w16 = ((a.repeat_interleave(16, dim=1) * q.float()) - b.repeat_interleave(16, dim=1)).half()
+    ab = torch.stack([a.t(), b.t()], dim=-1).contiguous()          # [K/16][N][2]
+    q, ab, w16 = q.to(dev), ab.to(dev), w16.to(dev)
+    A = torch.randn(M, K, device=dev).half()
+    outs = []
+    for use in (False, True):
+        if kind == 6:
+            S, H, D = 72, 12, 768
+            qkvg = [torch.zeros((M // S) * H * S * 64, device=dev, dtype=torch.float16) for _ in range(4)]
+            kw = dict(Bq=q, Bs=ab, lds=N) if use else {}
+            run(kind, A, w16, M, N, K, qkvg=qkvg, S=S, H=H, D=D, **kw)
+            outs.append(torch.cat([t.cpu() for t in qkvg]).view(torch.int16))
+            continue
+        f32 = kind in (0, 2)
+        width = N // 2 if kind in (4, 5) else N
+        out = torch.full((M, width), 0.5, device=dev, dtype=torch.float32 if f32 else torch.float16)
+        kw = dict(Bq=q, Bs=ab, lds=N) if use else {}
+        run(kind, A, w16, M, N, K, out=out, ldo=width, resid=out if kind == 2 else None, **kw)
+        outs.append(out.cpu().view(torch.int32 if f32 else torch.int16))
+    assert torch.equal(outs[0], outs[1])
 
 
 def test_resid_remap(dev):

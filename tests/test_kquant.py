@@ -56,6 +56,26 @@ def test_dequantize_bitwise_against_gguf_py(kind):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("kind", ["q4_k", "q5_k", "q6_k", "q8_0"])
+def test_scaled_int8_form_equals_dequantisation(kind):
+    """The form the GEMM's dequantising prologue reads (integer values, and per 16 values a
+    single-precision scale and offset) gives every value of the loader's dequantisation bit
+    for bit as (a * q) - b, each operation rounded in single precision."""
+    rng = np.random.default_rng({"q4_k": 5, "q5_k": 6, "q6_k": 7, "q8_0": 8}[kind])
+    rows, ne0 = 5, 768
+    raw = np.ascontiguousarray(random_blocks(kind, rows, ne0, rng))
+    code = TYPES[kind][0]
+    q = np.empty((rows, ne0), np.int8)
+    a = np.empty((rows, ne0 // 16), np.float32)
+    b = np.empty_like(a)
+    assert tb.lib().tsb_scaled_int8_rows(code, raw.ctypes.data, rows, ne0, q.ctypes.data, a.ctypes.data,
+                                         b.ctypes.data) == 0
+    aa, bb = np.repeat(a, 16, axis=1), np.repeat(b, 16, axis=1)
+    got = (aa * q.astype(np.float32)).astype(np.float32) - bb
+    want = ours(code, raw, rows, ne0)
+    assert np.array_equal(got.astype(np.float32).view(np.uint32), want.view(np.uint32))
+
+
 @pytest.mark.parametrize("kind,tol", [("q4_k", 0.08), ("q5_k", 0.04), ("q6_k", 0.03)])
 def test_encoder_round_trip(kind, tol):
     rng = np.random.default_rng(5)

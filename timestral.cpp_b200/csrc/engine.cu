@@ -82,17 +82,22 @@ struct DevBuf {
     template <class T> T* as() const { return static_cast<T*>(p); }
 };
 
-// Q8_0 weights in the device format of the GEMM's dequantising prologue: int8 values [N][K]
-// and the f16 scale of every 32-value block, transposed to [K / 32][N] (ldd = N).
+// Block-quantised weights in the device format of the GEMM's dequantising prologue: int8
+// values [N][K] and either (Q8_0) the f16 scale of every 32-value block, transposed to
+// [K / 32][N], or (K-quants) an f32 scale and offset per 16 values, [K / 16][N][2]; ldd = N.
 struct Q8W {
     const int8_t* q = nullptr;
     const __half* d = nullptr;
+    const float* s = nullptr;
     int64_t ldd = 0;
 };
-// The same on the host while the weights are rearranged: d [N][K / 32] in row order.
+// The same on the host while the weights are rearranged, in row order: d [N][K / 32] (Q8_0)
+// or ab [N][K / 16][2] (scaled: K-quants).
 struct Q8Host {
     std::vector<int8_t> q;
     std::vector<uint16_t> d;
+    std::vector<float> ab;
+    bool scaled = false;
     size_t N = 0, K = 0;
 };
 
@@ -140,7 +145,7 @@ struct Engine::Impl {
     const float* out_norm = nullptr;
     __half* h_hid = nullptr; __half* h_out = nullptr; __half* h_res = nullptr;
     Q8W p_out_q8, h_hid_q8, h_out_q8, h_res_q8;
-    bool q8_prologue = false;    // Q8_0 weights dequantised in the GEMM prologue (else the f16 copies)
+    bool q8_prologue = false;    // block-quantised weights dequantised in the GEMM prologue (else the f16 copies)
     float* fh_hid = nullptr; float* fh_out = nullptr; float* fh_res = nullptr;
     // workspace
     DevBuf rows, mask, win, wmask, role, future, fmask, feat, aloc, ascale, caplo, caphi, capsc, first_obs, kv, rope_row,
@@ -281,11 +286,32 @@ struct Engine::Impl {
         return const_cast<float*>(f32_tensor(n));
     }
     // --- Q8_0 twins ------------------------------------------------------------------
-    static bool q8_type(const HostTensor& w) { return w.type == TT_Q8_0 && w.ne0 % 32 == 0; }
-    // GGUF Q8_0 rows (blocks of 34 bytes: f16 d, then 32 int8 values) as values and scales.
+    static bool q8_type(const HostTensor& w) {
+        return (w.type == TT_Q8_0 && w.ne0 % 32 == 0) ||
+               ((w.type == TT_Q4_K || w.type == TT_Q5_K || w.type == TT_Q6_K) && w.ne0 % 256 == 0);
+    }
+    // GGUF Q8_0 rows (blocks of 34 bytes: f16 d, then 32 int8 values) as values and scales;
+    // K-quant rows as values with a scale and an offset per 16 values (ts::scaled_int8_row).
     static Q8Host q8_rows(const HostTensor& w) {
         Q8Host h;
         h.K = size_t(w.ne0); h.N = size_t(w.ne1);
+        if (w.type != TT_Q8_0) {
+            h.scaled = true;
+            h.q.resize(h.N * h.K);
+            h.ab.resize(h.N * (h.K / 16) * 2);
+            std::vector<float> a(h.K / 16), b(h.K / 16);
+            const size_t row = ts::ggml_row_bytes(uint32_t(w.type), int64_t(h.K));
+            for (size_t n = 0; n < h.N; ++n) {
+                if (!ts::scaled_int8_row(uint32_t(w.type), static_cast<const uint8_t*>(w.data) + n * row, int64_t(h.K),
+                                         h.q.data() + n * h.K, a.data(), b.data()))
+                    throw std::runtime_error("unsupported weight type " + std::to_string(w.type));
+                for (size_t g = 0; g < h.K / 16; ++g) {
+                    h.ab[(n * (h.K / 16) + g) * 2] = a[g];
+                    h.ab[(n * (h.K / 16) + g) * 2 + 1] = b[g];
+                }
+            }
+            return h;
+        }
         const size_t nb = h.K / 32;
         h.q.resize(h.N * h.K);
         h.d.resize(h.N * nb);
@@ -299,40 +325,59 @@ struct Engine::Impl {
         return h;
     }
     static void q8_append(Q8Host& a, const Q8Host& b) {
+        if (a.scaled != b.scaled) throw std::runtime_error("mixed block formats in one projection");
         a.q.insert(a.q.end(), b.q.begin(), b.q.end());
         a.d.insert(a.d.end(), b.d.begin(), b.d.end());
+        a.ab.insert(a.ab.end(), b.ab.begin(), b.ab.end());
         a.N += b.N;
     }
+    // Scale entries per row (f16 scales or f32 scale/offset values).
+    static size_t d_per_row(const Q8Host& h) { return h.scaled ? 0 : h.K / 32; }
+    static size_t ab_per_row(const Q8Host& h) { return h.scaled ? (h.K / 16) * 2 : 0; }
     // Rows [r0, r0 + n) of a twin.
     static Q8Host q8_slice(const Q8Host& a, size_t r0, size_t n) {
         Q8Host h;
-        h.K = a.K; h.N = n;
-        const size_t nb = a.K / 32;
+        h.K = a.K; h.N = n; h.scaled = a.scaled;
+        const size_t nb = d_per_row(a), na = ab_per_row(a);
         h.q.assign(a.q.begin() + r0 * a.K, a.q.begin() + (r0 + n) * a.K);
         h.d.assign(a.d.begin() + r0 * nb, a.d.begin() + (r0 + n) * nb);
+        h.ab.assign(a.ab.begin() + r0 * na, a.ab.begin() + (r0 + n) * na);
         return h;
     }
     // Two twins of `rows` rows each interleaved per tile, as interleave() does for f16 rows.
     static Q8Host q8_interleave(const Q8Host& a, const Q8Host& b, size_t rows) {
+        if (a.scaled != b.scaled) throw std::runtime_error("mixed block formats in one projection");
         Q8Host h;
-        h.K = a.K; h.N = 2 * rows;
-        const size_t nb = a.K / 32, half = kTile / 2;
+        h.K = a.K; h.N = 2 * rows; h.scaled = a.scaled;
+        const size_t nb = d_per_row(a), na = ab_per_row(a), half = kTile / 2;
         for (size_t tile = 0; tile < rows / half; ++tile)
             for (const Q8Host* src : {&a, &b}) {
                 h.q.insert(h.q.end(), src->q.begin() + tile * half * a.K, src->q.begin() + (tile + 1) * half * a.K);
                 h.d.insert(h.d.end(), src->d.begin() + tile * half * nb, src->d.begin() + (tile + 1) * half * nb);
+                h.ab.insert(h.ab.end(), src->ab.begin() + tile * half * na, src->ab.begin() + (tile + 1) * half * na);
             }
         return h;
     }
     Q8W q8_upload(const Q8Host& h) {
+        Q8W w;
+        w.q = upload(h.q.data(), h.q.size());
+        w.ldd = int64_t(h.N);
+        if (h.scaled) {
+            const size_t ng = h.K / 16;
+            std::vector<float> st(ng * h.N * 2);
+            for (size_t n = 0; n < h.N; ++n)
+                for (size_t g = 0; g < ng; ++g) {
+                    st[(g * h.N + n) * 2] = h.ab[(n * ng + g) * 2];
+                    st[(g * h.N + n) * 2 + 1] = h.ab[(n * ng + g) * 2 + 1];
+                }
+            w.s = upload(st.data(), st.size());
+            return w;
+        }
         const size_t nb = h.K / 32;
         std::vector<uint16_t> dt(nb * h.N);
         for (size_t n = 0; n < h.N; ++n)
             for (size_t b = 0; b < nb; ++b) dt[b * h.N + n] = h.d[n * nb + b];
-        Q8W w;
-        w.q = upload(h.q.data(), h.q.size());
         w.d = reinterpret_cast<const __half*>(upload(dt.data(), dt.size()));
-        w.ldd = int64_t(h.N);
         return w;
     }
     static bool unit_gains(const float* w, size_t n) {
@@ -344,9 +389,9 @@ struct Engine::Impl {
     void q8(GemmArgs& g, const Q8W& w, int64_t row0 = 0) const {
         if (!q8_prologue || !w.q) return;
         g.Bq = w.q + row0 * g.K;
-        g.Bd = w.d + row0;
-        g.ldd = w.ldd;
         g.ldb = g.K;
+        if (w.s) { g.Bs = w.s + 2 * row0; g.lds = w.ldd; }
+        else { g.Bd = w.d + row0; g.ldd = w.ldd; }
     }
 
     // Two [rows][K] blocks interleaved per tile: [a rows t*128.. | b rows t*128..].
@@ -1190,7 +1235,7 @@ void Engine::attention_kernels(int mode) {
     impl_->have_last = false;
 }
 
-bool Engine::q8_prologue(bool on) {
+bool Engine::dequant_prologue(bool on) {
     const bool any = impl_->p_out_q8.q || impl_->h_hid_q8.q || (!impl_->mlp.empty() && impl_->mlp[0].w3_q8.q);
     impl_->q8_prologue = on && any;
     impl_->drop_graph();

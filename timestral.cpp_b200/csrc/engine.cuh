@@ -141,12 +141,13 @@ public:
     // the rest of it is per token, its out projection, one-row variate sublayer and MLP run on
     // the decoder tokens alone, the only tokens the head reads. Off: every token, same bits.
     void decoder_tail(bool on);
-    // Q8_0 weights dequantised in the GEMM prologue (on) instead of read as the f16 copies
-    // made at load (off, the default): the int8 tiles and block scales travel to shared memory
-    // and converter warps write the f16 tiles the tensor cores read; the same f16 values, so the
-    // same forecast bits. Weights whose norm gain is folded into them keep the f16 copy unless
-    // the gain is 1. Returns false when the model has no Q8_0 weights (and `on` was asked).
-    bool q8_prologue(bool on);
+    // Block-quantised weights (Q8_0, Q4_K, Q5_K, Q6_K) dequantised in the GEMM prologue (on)
+    // instead of read as the f16 copies made at load (off, the default): the int8 tiles and
+    // their block scales (and offsets) travel to shared memory and converter warps write the
+    // f16 tiles the tensor cores read; the same f16 values, so the same forecast bits. Weights
+    // whose norm gain is folded into them keep the f16 copy unless the gain is 1. Returns
+    // false when the model has no block-quantised weights (and `on` was asked).
+    bool dequant_prologue(bool on);
     // Observe every decode block of the following forecasts (nullptr: none). While an
     // observer is set, forecasts are not captured into or replayed from CUDA graphs.
     void set_observer(const BlockObserver* observer);

@@ -42,6 +42,13 @@ constexpr int TMEM_COLS = 2 * BN;             // 512: two accumulators
 constexpr int BQ_BYTES = BN_HALF * BK;        // 8 KB
 constexpr int BD_BYTES = 2 * BN_HALF * 2;     // 512 B
 constexpr int Q8_STAGE_BYTES = STAGE_BYTES + BQ_BYTES + 1024;   // scales padded: stages stay 1 KB aligned
+// K-quant prologue (scaled int8): the same int8 tile plus, per 16 values, an f32 scale and
+// offset for each of the 128 rows: 4 groups x 128 float2 = 4 KB.
+constexpr int BS_BYTES = (BK / 16) * BN_HALF * 8;
+constexpr int KQ_STAGE_BYTES = STAGE_BYTES + BQ_BYTES + BS_BYTES;
+// Weight formats of the B operand: f16, Q8_0 (int8 + f16 scale per 32 values), scaled int8
+// (int8 + f32 scale and offset per 16 values: the K-quants, and Q8_0 as well).
+enum WeightFmt : int { FMT_F16 = 0, FMT_Q8 = 1, FMT_KQ = 2 };
 constexpr int CONV_WARPS = 2;                 // 384 threads with the 8 epilogue warps: no spills
 
 // Per epilogue kind: PARTS column groups per TMEM lane quarter (epilogue warps = 4 * PARTS).
@@ -50,14 +57,16 @@ constexpr int CONV_WARPS = 2;                 // 384 threads with the 8 epilogue
 // the activation and plain-store epilogues run four groups of 64, which doubles the warps
 // that hide the epilogue's latency at 96 registers a thread; their staging blocks leave room
 // for five operand stages instead of six.
-// Q8: the Q8_0 prologue variant, which adds CONV_WARPS converter warps after the epilogue
-// warps, uses two column groups for every epilogue kind (register budget) and four stages.
-template <int KIND, bool Q8 = false>
+// FMT != FMT_F16: the dequantising-prologue variants, which add CONV_WARPS converter warps
+// after the epilogue warps, use two column groups for every epilogue kind (register budget)
+// and four stages.
+template <int KIND, int FMT = FMT_F16>
 struct Cfg {
+    static constexpr bool Q8 = FMT != FMT_F16;
     static constexpr int PARTS = (Q8 || KIND == EPI_QKVG || KIND == EPI_RESID) ? 2 : 4;
     static constexpr int EPI_WARPS = 4 * PARTS;
     static constexpr int THREADS = 64 + 32 * EPI_WARPS + (Q8 ? 32 * CONV_WARPS : 0);
-    static constexpr int STAGE = Q8 ? Q8_STAGE_BYTES : STAGE_BYTES;
+    static constexpr int STAGE = FMT == FMT_Q8 ? Q8_STAGE_BYTES : FMT == FMT_KQ ? KQ_STAGE_BYTES : STAGE_BYTES;
     static constexpr int STAGES = Q8 ? 4 : PARTS == 2 ? 6 : 5;
     static constexpr int EPI_STAGE_BYTES = EPI_WARPS * 32 * 128;   // per-warp transposition blocks
     static constexpr int SMEM_BYTES = STAGES * STAGE + EPI_STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
@@ -443,12 +452,33 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
     }
 }
 
-template <int KIND, bool Q8>
-__global__ void __launch_bounds__(Cfg<KIND, Q8>::THREADS, 1)
+// Sixteen signed int8 values of one row (q) and their group's scale and offset: the f16
+// values (a * q) - b, each operation rounded in single precision, then once to f16 (the
+// loader's dequantisation). A byte b becomes the float 2^23 + (b + 128) under the exponent
+// 0x4B, so subtracting 2^23 + 128 gives b exactly.
+__device__ __forceinline__ void dequant16_scaled(const uint4 q, float2 ab, uint32_t (&h)[8]) {
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t u = w[i] ^ 0x80808080u;
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float f = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u + uint32_t(k)));
+            v[k] = __fsub_rn(__fmul_rn(ab.x, __fsub_rn(f, 8388736.0f)), ab.y);
+        }
+        h[2 * i] = pack_half2(v[0], v[1]);
+        h[2 * i + 1] = pack_half2(v[2], v[3]);
+    }
+}
+
+template <int KIND, int FMT>
+__global__ void __launch_bounds__(Cfg<KIND, FMT>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_bq, const __grid_constant__ CUtensorMap map_bd,
                    const GemmArgs g, int* err) {
-    using CF = Cfg<KIND, Q8>;
+    using CF = Cfg<KIND, FMT>;
+    constexpr bool Q8 = CF::Q8;
     constexpr int STAGES = CF::STAGES, EPI_WARPS = CF::EPI_WARPS, PARTS = CF::PARTS, SB = CF::STAGE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -503,9 +533,10 @@ __global__ void __launch_bounds__(Cfg<KIND, Q8>::THREADS, 1)
                         // This CTA's int8 rows and their scales, on its own barrier (its converter
                         // warps wait for them); the f16 tile is written by those warps.
                         uint8_t* bq = a + STAGE_BYTES;
-                        mbar_arrive_expect_tx(&sm->bfull[s], BQ_BYTES + BD_BYTES);
+                        mbar_arrive_expect_tx(&sm->bfull[s], BQ_BYTES + (FMT == FMT_Q8 ? BD_BYTES : BS_BYTES));
                         tma_load_2d(bq, &map_bq, &sm->bfull[s], kb * BK, n0);
-                        tma_load_2d(bq + BQ_BYTES, &map_bd, &sm->bfull[s], n0, kb * (BK / 32));
+                        if constexpr (FMT == FMT_Q8) tma_load_2d(bq + BQ_BYTES, &map_bd, &sm->bfull[s], n0, kb * (BK / 32));
+                        else tma_load_2d(bq + BQ_BYTES, &map_bd, &sm->bfull[s], 2 * n0, kb * (BK / 16));
                     } else {
                         tma_load_2d_pair(a + A_BYTES, &map_b, full0, kb * BK, n0);
                     }
@@ -566,13 +597,19 @@ __global__ void __launch_bounds__(Cfg<KIND, Q8>::THREADS, 1)
                 for (int i = 0; i < ROWS / 8; ++i) {
                     const int r = cw * ROWS + i * 8 + (lane >> 2);
                     const uint4 q = *reinterpret_cast<const uint4*>(bq + r * BK + c * 16);
-                    const __half d = bd[(c >> 1) * BN_HALF + r];
-                    const __half2 d2 = __halves2half2(d, d);
                     uint32_t h[8];
-                    dequant4(q.x, d2, h[0], h[1]);
-                    dequant4(q.y, d2, h[2], h[3]);
-                    dequant4(q.z, d2, h[4], h[5]);
-                    dequant4(q.w, d2, h[6], h[7]);
+                    if constexpr (FMT == FMT_Q8) {
+                        const __half d = bd[(c >> 1) * BN_HALF + r];
+                        const __half2 d2 = __halves2half2(d, d);
+                        dequant4(q.x, d2, h[0], h[1]);
+                        dequant4(q.y, d2, h[2], h[3]);
+                        dequant4(q.z, d2, h[4], h[5]);
+                        dequant4(q.w, d2, h[6], h[7]);
+                    } else {
+                        // group c of this K step: row r's scale and offset
+                        const float2 ab = reinterpret_cast<const float2*>(bq + BQ_BYTES)[c * BN_HALF + r];
+                        dequant16_scaled(q, ab, h);
+                    }
                     *reinterpret_cast<uint4*>(bf + r * 128 + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
                     *reinterpret_cast<uint4*>(bf + r * 128 + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
                 }
@@ -709,14 +746,14 @@ int device_sm_count() {
     return counts[dev];
 }
 
-template <int KIND, bool Q8>
+template <int KIND, int FMT>
 static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<KIND, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg<KIND, Q8>::SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<KIND, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg<KIND, FMT>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
@@ -726,11 +763,18 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
                               a.a_stride, a.K, a.lda, BM / a.a_group)
         : make_map_2d_f16(&ma, a.A, a.M, a.K, a.lda, BM);
     if (!map_a) return cudaErrorInvalidValue;
-    if constexpr (Q8) {
+    if constexpr (FMT == FMT_Q8) {
         if (!make_map_2d_plain(&mq, a.Bq, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.N, a.K, a.ldb, BK, BN_HALF) ||
             !make_map_2d_plain(&md, a.Bd, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (a.K + 31) / 32, a.N, a.ldd * 2, BN_HALF, BK / 32))
             return cudaErrorInvalidValue;
         mb = mq;                                      // unused by this variant
+    } else if constexpr (FMT == FMT_KQ) {
+        // scales as f32 [K / 16][2 * lds] (scale, offset of row n at columns 2n, 2n + 1)
+        if (!make_map_2d_plain(&mq, a.Bq, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.N, a.K, a.ldb, BK, BN_HALF) ||
+            !make_map_2d_plain(&md, a.Bs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (a.K + 15) / 16, 2 * a.N, a.lds * 8,
+                               2 * BN_HALF, BK / 16))
+            return cudaErrorInvalidValue;
+        mb = mq;
     } else {
         if (!make_map_2d_f16(&mb, a.B, a.N, a.K, a.ldb, BN_HALF)) return cudaErrorInvalidValue;
         mq = mb; md = mb;                             // unused by this variant
@@ -741,8 +785,8 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
     const int pairs = tiles < max_pairs ? tiles : max_pairs;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(Cfg<KIND, Q8>::THREADS);
-    cfg.dynamicSmemBytes = Cfg<KIND, Q8>::SMEM_BYTES;
+    cfg.blockDim = dim3(Cfg<KIND, FMT>::THREADS);
+    cfg.dynamicSmemBytes = Cfg<KIND, FMT>::SMEM_BYTES;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -751,12 +795,14 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<KIND, Q8>, ma, mb, mq, md, a, err);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<KIND, FMT>, ma, mb, mq, md, a, err);
 }
 
 template <int KIND>
 static cudaError_t launch_kind(const GemmArgs& a, cudaStream_t stream, int* err) {
-    return a.Bq ? launch<KIND, true>(a, stream, err) : launch<KIND, false>(a, stream, err);
+    if (a.Bq && a.Bs) return launch<KIND, FMT_KQ>(a, stream, err);
+    if (a.Bq) return launch<KIND, FMT_Q8>(a, stream, err);
+    return launch<KIND, FMT_F16>(a, stream, err);
 }
 
 cudaError_t tc_gemm(EpiKind kind, const GemmArgs& a, cudaStream_t stream, int* err) {
@@ -764,7 +810,11 @@ cudaError_t tc_gemm(EpiKind kind, const GemmArgs& a, cudaStream_t stream, int* e
     // TMA: 16-byte aligned bases and row pitches (f16 B: ldb elements; int8 Bq: ldb bytes;
     // scales Bd: ldd f16 per block row, at least N).
     if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (a.lda * 2) % 16 || a.N % 16) return cudaErrorInvalidValue;
-    if (a.Bq) {
+    if (a.Bq && a.Bs) {
+        if ((reinterpret_cast<uintptr_t>(a.Bq) & 15) || (reinterpret_cast<uintptr_t>(a.Bs) & 15) || a.ldb % 16 ||
+            (a.lds * 8) % 16 || a.lds < a.N || a.K % 16)
+            return cudaErrorInvalidValue;
+    } else if (a.Bq) {
         if ((reinterpret_cast<uintptr_t>(a.Bq) & 15) || (reinterpret_cast<uintptr_t>(a.Bd) & 15) || a.ldb % 16 ||
             (a.ldd * 2) % 16 || a.ldd < a.N || a.K % 32)
             return cudaErrorInvalidValue;

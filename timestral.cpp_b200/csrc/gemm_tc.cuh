@@ -71,6 +71,11 @@ struct GemmArgs {
     const int8_t* Bq = nullptr;
     const __half* Bd = nullptr;
     int64_t ldd = 0;
+    // K-quant weights (and Q8_0) in scaled-int8 form, used with Bq instead of Bd when set: per
+    // 16 values of row n, block g, a scale and an offset Bs[2 * (g * lds + n)], Bs[... + 1];
+    // value (scale * q) - offset rounded once to f16, the loader's dequantisation.
+    const float* Bs = nullptr;
+    int64_t lds = 0;
     int M = 0, N = 0, K = 0;
     GemmEpilogue epi;
 };

@@ -19,6 +19,7 @@ extern "C" TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_
     a.M = t->M; a.N = t->N; a.K = t->K;
     a.a_group = t->a_group; a.a_stride = t->a_stride; a.a_offset = t->a_offset;
     a.Bq = t->Bq; a.Bd = static_cast<const __half*>(t->Bd); a.ldd = t->ldd;
+    a.Bs = t->Bs; a.lds = t->lds;
     GemmEpilogue& e = a.epi;
     e.out = t->out; e.ldo = t->ldo; e.bias = t->bias; e.resid = t->resid;
     e.row_group = t->row_group; e.row_stride = t->row_stride; e.row_offset = t->row_offset;

@@ -471,13 +471,13 @@ TIMESTRAL_API int tsb_attention_kernels(timestral_ctx* c, int32_t mode) {
     return TSB_OK;
 }
 
-TIMESTRAL_API int tsb_q8_prologue(timestral_ctx* c, int32_t on) {
+TIMESTRAL_API int tsb_dequant_prologue(timestral_ctx* c, int32_t on) {
     if (!c) return TSB_ERR_ARG;
     try {
         bool ok = true;
-        for (size_t k = 0; k < c->gpus(); ++k) ok &= c->gpu(k).engine().q8_prologue(on != 0);
+        for (size_t k = 0; k < c->gpus(); ++k) ok &= c->gpu(k).engine().dequant_prologue(on != 0);
         if (!ok) {
-            c->error.set("tsb_q8_prologue: the model has no Q8_0 weights");
+            c->error.set("tsb_dequant_prologue: the model has no block-quantised weights");
             return TSB_ERR_MODEL;
         }
     } catch (...) {
@@ -540,6 +540,18 @@ TIMESTRAL_API int tsb_dequantize_rows(uint32_t type, const void* src, int64_t ro
     if (!row) return TSB_ERR_ARG;
     for (int64_t r = 0; r < rows; ++r)
         if (!ts::dequantize_row(type, static_cast<const uint8_t*>(src) + size_t(r) * row, ne0, dst + r * ne0))
+            return TSB_ERR_ARG;
+    return TSB_OK;
+}
+
+TIMESTRAL_API int tsb_scaled_int8_rows(uint32_t type, const void* src, int64_t rows, int64_t ne0, int8_t* q, float* a,
+                                       float* b) {
+    if (!src || !q || !a || !b || rows < 0 || ne0 <= 0 || ne0 % 16) return TSB_ERR_ARG;
+    const size_t row = ts::ggml_row_bytes(type, ne0);
+    if (!row) return TSB_ERR_ARG;
+    for (int64_t r = 0; r < rows; ++r)
+        if (!ts::scaled_int8_row(type, static_cast<const uint8_t*>(src) + size_t(r) * row, ne0, q + r * ne0,
+                                 a + r * (ne0 / 16), b + r * (ne0 / 16)))
             return TSB_ERR_ARG;
     return TSB_OK;
 }

@@ -81,6 +81,72 @@ void scale_min_k4(int j, const uint8_t* q, int* sc, int* m) {
 }
 }  // namespace
 
+bool scaled_int8_row(uint32_t type, const uint8_t* src, int64_t ne0, int8_t* q, float* a, float* b) {
+    if (ggml_row_bytes(type, ne0) == 0 && ne0 != 0) return false;
+    switch (type) {
+        case 12:   // Q4_K
+        case 13:   // Q5_K
+            for (int64_t blk = 0; blk < ne0 / 256; ++blk) {
+                const uint8_t* base = src + blk * (type == 12 ? 144 : 176);
+                const float d = half_to_float(base), dmin = half_to_float(base + 2);
+                const uint8_t* scales = base + 4;
+                const uint8_t* qh = base + 16;
+                const uint8_t* qs = base + (type == 12 ? 16 : 48);
+                for (int g = 0; g < 4; ++g)
+                    for (int half = 0; half < 2; ++half) {
+                        int sc, m;
+                        scale_min_k4(2 * g + half, scales, &sc, &m);
+                        const int64_t p0 = blk * 256 + 64 * g + 32 * half;
+                        for (int l = 0; l < 32; ++l) {
+                            int v = half ? (qs[32 * g + l] >> 4) : (qs[32 * g + l] & 0xF);
+                            if (type == 13) v |= ((qh[l] >> (2 * g + half)) & 1) << 4;
+                            q[p0 + l] = int8_t(v);
+                        }
+                        for (int k = 0; k < 2; ++k) {
+                            a[p0 / 16 + k] = d * float(sc);
+                            b[p0 / 16 + k] = dmin * float(m);
+                        }
+                    }
+            }
+            return true;
+        case 14:   // Q6_K
+            for (int64_t blk = 0; blk < ne0 / 256; ++blk) {
+                const uint8_t* ql = src + blk * 210;
+                const uint8_t* qh = ql + 128;
+                const int8_t* sc = reinterpret_cast<const int8_t*>(ql + 192);
+                const float d = half_to_float(ql + 208);
+                for (int h = 0; h < 2; ++h) {
+                    const uint8_t* l0 = ql + 64 * h;
+                    const uint8_t* h0 = qh + 32 * h;
+                    const int64_t p0 = blk * 256 + 128 * h;
+                    for (int l = 0; l < 32; ++l) {
+                        q[p0 + l] = int8_t(int((l0[l] & 0xF) | (((h0[l] >> 0) & 3) << 4)) - 32);
+                        q[p0 + l + 32] = int8_t(int((l0[l + 32] & 0xF) | (((h0[l] >> 2) & 3) << 4)) - 32);
+                        q[p0 + l + 64] = int8_t(int((l0[l] >> 4) | (((h0[l] >> 4) & 3) << 4)) - 32);
+                        q[p0 + l + 96] = int8_t(int((l0[l + 32] >> 4) | (((h0[l] >> 6) & 3) << 4)) - 32);
+                    }
+                    // 16-value group j of this half: quadrant j / 2, scale index is + 2 * quadrant.
+                    for (int j = 0; j < 8; ++j) {
+                        a[p0 / 16 + j] = d * float(sc[8 * h + (j & 1) + 2 * (j >> 1)]);
+                        b[p0 / 16 + j] = 0.f;
+                    }
+                }
+            }
+            return true;
+        case 8:    // Q8_0
+            for (int64_t blk = 0; blk < ne0 / 32; ++blk) {
+                const uint8_t* base = src + blk * 34;
+                const float d = half_to_float(base);
+                for (int j = 0; j < 32; ++j) q[blk * 32 + j] = int8_t(base[2 + j]);
+                a[blk * 2] = a[blk * 2 + 1] = d;
+                b[blk * 2] = b[blk * 2 + 1] = 0.f;
+            }
+            return true;
+        default:
+            return false;
+    }
+}
+
 bool dequantize_row(uint32_t type, const uint8_t* src, int64_t ne0, float* dst) {
     if (ggml_row_bytes(type, ne0) == 0 && ne0 != 0) return false;
     switch (type) {

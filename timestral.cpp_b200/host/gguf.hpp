@@ -78,6 +78,12 @@ size_t ggml_row_bytes(uint32_t type, int64_t ne0);
 // with ggml's published dequantisation (per-block f16 scales and mins; single-precision
 // products in the same order). Returns false for other types.
 bool dequantize_row(uint32_t type, const uint8_t* src, int64_t ne0, float* dst);
+// The same row as integer values q[i] and, per group g of 16 consecutive values, a scale
+// a[g] and an offset b[g] such that dequantize_row gives exactly (a[g] * q[i]) - b[g] in
+// single precision (b = 0 where the format has no minimum): the form the GEMM's dequantising
+// prologue consumes. Q4_K/Q5_K: a = d * scale, b = dmin * min of the 32-value sub-block;
+// Q6_K: a = d * scale of the 16 values, q - 32; Q8_0: a = d. Returns false for other types.
+bool scaled_int8_row(uint32_t type, const uint8_t* src, int64_t ne0, int8_t* q, float* a, float* b);
 const char* ggml_type_name(uint32_t type);
 
 }  // namespace ts

@@ -35,7 +35,8 @@ class GemmTest(C.Structure):
                 ("rope", C.c_int32), ("cos_tab", C.c_void_p), ("sin_tab", C.c_void_p),
                 ("rope_row", C.c_void_p), ("rope_half", C.c_int32),
                 ("rope_dup", C.c_int32), ("a_group", C.c_int32), ("a_stride", C.c_int32),
-                ("a_offset", C.c_int32), ("Bq", C.c_void_p), ("Bd", C.c_void_p), ("ldd", C.c_int64)]
+                ("a_offset", C.c_int32), ("Bq", C.c_void_p), ("Bd", C.c_void_p), ("ldd", C.c_int64),
+                ("Bs", C.c_void_p), ("lds", C.c_int64)]
 
 
 _lib = None
@@ -63,6 +64,7 @@ SIGNATURES = {
     "tsb_last_launch_count": (C.c_int64, [C.c_void_p]),
     "tsb_model_path": (C.c_int, [C.c_void_p]),
     "tsb_dequantize_rows": (C.c_int, [C.c_uint32, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]),
+    "tsb_scaled_int8_rows": (C.c_int, [C.c_uint32, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]),
     "tsb_last_geometry": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64)] + [C.POINTER(C.c_int32)] * 3),
     "tsb_test_gemm": (C.c_int, [C.POINTER(GemmTest), C.POINTER(C.c_int32)]),
     "tsb_test_attention_time": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 4 + [C.POINTER(C.c_int32)]),
@@ -71,7 +73,7 @@ SIGNATURES = {
     "tsb_fused_norm": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_attention_kernels": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_decoder_tail": (C.c_int, [C.c_void_p, C.c_int32]),
-    "tsb_q8_prologue": (C.c_int, [C.c_void_p, C.c_int32]),
+    "tsb_dequant_prologue": (C.c_int, [C.c_void_p, C.c_int32]),
     "tsb_test_scale_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_double] + [C.c_int32] * 6
                             + [C.c_void_p] * 8),
     "tsb_test_attention_time_ex": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 9 + [C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
@@ -205,11 +207,12 @@ class Model:
         if lib().tsb_attention_kernels(self.h, int(mode)) != 0:
             raise RuntimeError("tsb_attention_kernels failed")
 
-    def q8_prologue(self, on: bool):
-        """Q8_0 weights dequantised in the GEMM prologue (on) or read as f16 copies (off)."""
-        rc = lib().tsb_q8_prologue(self.h, int(on))
+    def dequant_prologue(self, on: bool):
+        """Block-quantised weights (Q8_0, K-quants) dequantised in the GEMM prologue (on) or
+        read as the f16 copies made at load (off, the default)."""
+        rc = lib().tsb_dequant_prologue(self.h, int(on))
         if rc != 0:
-            raise TimestralError(f"tsb_q8_prologue failed ({rc}): {self.last_error}")
+            raise TimestralError(f"tsb_dequant_prologue failed ({rc}): {self.last_error}")
 
     def decoder_tail(self, on: bool):
         """Last layer's per-token work on the decoder tokens alone (default on; same bits)."""
