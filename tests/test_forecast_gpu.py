@@ -635,3 +635,41 @@ def test_multi_device_handle_on_every_gpu():
     x = random_context(3 * n + 1, 1, 256, seed=63)
     assert np.array_equal(multi.forecast(x, 64).view(np.uint32), one.forecast(x, 64).view(np.uint32))
     multi.close()
+
+
+_ENV_CHILD = r"""
+import sys, numpy as np
+sys.path[:0] = sys.argv[1:3]
+import timestral_b200 as tb
+from timestral_b200 import synthetic as sy
+path = sy.cached_model(sy.spec_small(), "f16")
+try:
+    m = tb.Model(path)
+except tb.TimestralError as e:
+    print("ERROR", e)
+    sys.exit(0)
+x = np.asarray(np.random.default_rng(5).standard_normal((5, 1, 256)).cumsum(-1), np.float32)
+np.save(sys.argv[3], m.forecast(x, 64))
+print("GPUS", m.device_count)
+"""
+
+
+@pytest.mark.parametrize("devices,expect", [("0,0", "GPUS 2"), ("0", "GPUS 1"), ("99", "ERROR TIMESTRAL_DEVICES: invalid device list")])
+def test_timestral_devices_environment(tmp_path, devices, expect):
+    """An unmodified caller of the reference's C ABI (timestral_capi_load) spreads every request
+    over the GPUs TIMESTRAL_DEVICES lists, with the same forecast bits as one GPU; an invalid
+    list is a load error with its text in timestral_capi_last_error(NULL)."""
+    import os
+    import subprocess
+    import sys
+    repo = __import__("pathlib").Path(__file__).resolve().parents[1]
+    out = tmp_path / "f.npy"
+    env = dict(os.environ, TIMESTRAL_DEVICES=devices)
+    p = subprocess.run([sys.executable, "-c", _ENV_CHILD, str(repo / "timestral.cpp_b200"), str(repo / "oracle"), str(out)],
+                       capture_output=True, text=True, env=env, timeout=600)
+    assert p.returncode == 0, p.stderr[-2000:]
+    assert expect in p.stdout, p.stdout
+    if expect.startswith("GPUS"):
+        one, _ = models(sy.spec_small(), "f16")
+        x = np.asarray(np.random.default_rng(5).standard_normal((5, 1, 256)).cumsum(-1), np.float32)
+        assert np.array_equal(np.load(out).view(np.uint32), one.forecast(x, 64).view(np.uint32))
