@@ -85,7 +85,7 @@ struct DevBuf {
 // Block-quantised weights in the device format of the GEMM's dequantising prologue: int8
 // values [N][K] and either (Q8_0) the f16 scale of every 32-value block, transposed to
 // [K / 32][N], or (K-quants) an f32 scale and offset per 16 values, [K / 16][N][2]; ldd = N.
-struct Q8W {
+struct BlockW {
     const int8_t* q = nullptr;
     const __half* d = nullptr;
     const float* s = nullptr;
@@ -93,7 +93,7 @@ struct Q8W {
 };
 // The same on the host while the weights are rearranged, in row order: d [N][K / 32] (Q8_0)
 // or ab [N][K / 16][2] (scaled: K-quants).
-struct Q8Host {
+struct BlockHost {
     std::vector<int8_t> q;
     std::vector<uint16_t> d;
     std::vector<float> ab;
@@ -103,7 +103,7 @@ struct Q8Host {
 
 struct AttnW {
     bool time = true, gate = false;
-    Q8W qkvg_q8, vg_q8, out_q8;   // Q8_0 twins of qkvg, vg, out (null when not Q8_0)
+    BlockW qkvg_blk, vg_blk, out_blk;   // block-quantised twins of qkvg, vg, out (null when not block-quantised)
     const float* norm = nullptr;
     // tensor-core path
     __half* qkvg = nullptr; float* b_qkvg = nullptr; int n_qkvg = 0;   // [3D or 4D][D]
@@ -115,7 +115,7 @@ struct AttnW {
 };
 struct MlpW {
     const float* norm = nullptr;
-    Q8W w12_q8, w3_q8;
+    BlockW w12_blk, w3_blk;
     __half* w12 = nullptr; float* b12 = nullptr;    // tensor cores: [g|u] per tile
     __half* w3 = nullptr; float* b3 = nullptr;
     float* f12 = nullptr; float* fb12 = nullptr; float* f3 = nullptr; float* fb3 = nullptr;
@@ -144,8 +144,8 @@ struct Engine::Impl {
     std::vector<MlpW> mlp;
     const float* out_norm = nullptr;
     __half* h_hid = nullptr; __half* h_out = nullptr; __half* h_res = nullptr;
-    Q8W p_out_q8, h_hid_q8, h_out_q8, h_res_q8;
-    bool q8_prologue = false;    // block-quantised weights dequantised in the GEMM prologue (else the f16 copies)
+    BlockW p_out_blk, h_hid_blk, h_out_blk, h_res_blk;
+    bool dq_prologue = false;    // block-quantised weights dequantised in the GEMM prologue (else the f16 copies)
     float* fh_hid = nullptr; float* fh_out = nullptr; float* fh_res = nullptr;
     // workspace
     DevBuf rows, mask, win, wmask, role, future, fmask, feat, aloc, ascale, caplo, caphi, capsc, first_obs, kv, rope_row,
@@ -285,15 +285,15 @@ struct Engine::Impl {
         if (!mv.has(n)) return nullptr;
         return const_cast<float*>(f32_tensor(n));
     }
-    // --- Q8_0 twins ------------------------------------------------------------------
-    static bool q8_type(const HostTensor& w) {
+    // --- block-quantised twins (the dequantising GEMM prologue's weight formats) -------
+    static bool block_type(const HostTensor& w) {
         return (w.type == TT_Q8_0 && w.ne0 % 32 == 0) ||
                ((w.type == TT_Q4_K || w.type == TT_Q5_K || w.type == TT_Q6_K) && w.ne0 % 256 == 0);
     }
     // GGUF Q8_0 rows (blocks of 34 bytes: f16 d, then 32 int8 values) as values and scales;
     // K-quant rows as values with a scale and an offset per 16 values (ts::scaled_int8_row).
-    static Q8Host q8_rows(const HostTensor& w) {
-        Q8Host h;
+    static BlockHost block_rows(const HostTensor& w) {
+        BlockHost h;
         h.K = size_t(w.ne0); h.N = size_t(w.ne1);
         if (w.type != TT_Q8_0) {
             h.scaled = true;
@@ -324,7 +324,7 @@ struct Engine::Impl {
             }
         return h;
     }
-    static void q8_append(Q8Host& a, const Q8Host& b) {
+    static void block_append(BlockHost& a, const BlockHost& b) {
         if (a.scaled != b.scaled) throw std::runtime_error("mixed block formats in one projection");
         a.q.insert(a.q.end(), b.q.begin(), b.q.end());
         a.d.insert(a.d.end(), b.d.begin(), b.d.end());
@@ -332,11 +332,11 @@ struct Engine::Impl {
         a.N += b.N;
     }
     // Scale entries per row (f16 scales or f32 scale/offset values).
-    static size_t d_per_row(const Q8Host& h) { return h.scaled ? 0 : h.K / 32; }
-    static size_t ab_per_row(const Q8Host& h) { return h.scaled ? (h.K / 16) * 2 : 0; }
+    static size_t d_per_row(const BlockHost& h) { return h.scaled ? 0 : h.K / 32; }
+    static size_t ab_per_row(const BlockHost& h) { return h.scaled ? (h.K / 16) * 2 : 0; }
     // Rows [r0, r0 + n) of a twin.
-    static Q8Host q8_slice(const Q8Host& a, size_t r0, size_t n) {
-        Q8Host h;
+    static BlockHost block_slice(const BlockHost& a, size_t r0, size_t n) {
+        BlockHost h;
         h.K = a.K; h.N = n; h.scaled = a.scaled;
         const size_t nb = d_per_row(a), na = ab_per_row(a);
         h.q.assign(a.q.begin() + r0 * a.K, a.q.begin() + (r0 + n) * a.K);
@@ -345,21 +345,21 @@ struct Engine::Impl {
         return h;
     }
     // Two twins of `rows` rows each interleaved per tile, as interleave() does for f16 rows.
-    static Q8Host q8_interleave(const Q8Host& a, const Q8Host& b, size_t rows) {
+    static BlockHost block_interleave(const BlockHost& a, const BlockHost& b, size_t rows) {
         if (a.scaled != b.scaled) throw std::runtime_error("mixed block formats in one projection");
-        Q8Host h;
+        BlockHost h;
         h.K = a.K; h.N = 2 * rows; h.scaled = a.scaled;
         const size_t nb = d_per_row(a), na = ab_per_row(a), half = kTile / 2;
         for (size_t tile = 0; tile < rows / half; ++tile)
-            for (const Q8Host* src : {&a, &b}) {
+            for (const BlockHost* src : {&a, &b}) {
                 h.q.insert(h.q.end(), src->q.begin() + tile * half * a.K, src->q.begin() + (tile + 1) * half * a.K);
                 h.d.insert(h.d.end(), src->d.begin() + tile * half * nb, src->d.begin() + (tile + 1) * half * nb);
                 h.ab.insert(h.ab.end(), src->ab.begin() + tile * half * na, src->ab.begin() + (tile + 1) * half * na);
             }
         return h;
     }
-    Q8W q8_upload(const Q8Host& h) {
-        Q8W w;
+    BlockW block_upload(const BlockHost& h) {
+        BlockW w;
         w.q = upload(h.q.data(), h.q.size());
         w.ldd = int64_t(h.N);
         if (h.scaled) {
@@ -386,8 +386,8 @@ struct Engine::Impl {
         return true;
     }
     // B operand of a GEMM from a twin when the prologue mode is on (row offset into it).
-    void q8(GemmArgs& g, const Q8W& w, int64_t row0 = 0) const {
-        if (!q8_prologue || !w.q) return;
+    void block_b(GemmArgs& g, const BlockW& w, int64_t row0 = 0) const {
+        if (!dq_prologue || !w.q) return;
         g.Bq = w.q + row0 * g.K;
         g.ldb = g.K;
         if (w.s) { g.Bs = w.s + 2 * row0; g.lds = w.ldd; }
@@ -471,7 +471,7 @@ struct Engine::Impl {
         pb_out = bias_or_null("patch.out.bias");
         if (tc) {
             auto v = rows_f16(t("patch.out.weight")); p_out = reinterpret_cast<__half*>(upload(v.data(), v.size()));
-            if (q8_type(t("patch.out.weight"))) p_out_q8 = q8_upload(q8_rows(t("patch.out.weight")));
+            if (block_type(t("patch.out.weight"))) p_out_blk = block_upload(block_rows(t("patch.out.weight")));
         }
         else { auto v = rows_f32(t("patch.out.weight")); f_pout = upload(v.data(), v.size()); }
         // Tensor-core patch projections (K = 2 * patch_size, F32 weights): the weights split into
@@ -539,16 +539,16 @@ struct Engine::Impl {
                     }
                     auto o = rows_f16(t(p + "out.weight"));
                     a.out = reinterpret_cast<__half*>(upload(o.data(), o.size()));
-                    // Q8_0 twins; the norm gain folded into q/k/v/gate must be a no-op for them.
-                    if (q8_type(t(p + "out.weight"))) a.out_q8 = q8_upload(q8_rows(t(p + "out.weight")));
-                    if (q8_type(t(p + "qkv.weight")) && (!a.gate || q8_type(t(p + "gate.weight"))) &&
+                    // Block-quantised twins; the norm gain folded into q/k/v/gate must be a no-op for them.
+                    if (block_type(t(p + "out.weight"))) a.out_blk = block_upload(block_rows(t(p + "out.weight")));
+                    if (block_type(t(p + "qkv.weight")) && (!a.gate || block_type(t(p + "gate.weight"))) &&
                         unit_gains(nw, size_t(D))) {
-                        Q8Host qk = q8_rows(t(p + "qkv.weight"));
-                        Q8Host gt;
-                        if (a.gate) { gt = q8_rows(t(p + "gate.weight")); q8_append(qk, gt); }
-                        a.qkvg_q8 = q8_upload(qk);
+                        BlockHost qk = block_rows(t(p + "qkv.weight"));
+                        BlockHost gt;
+                        if (a.gate) { gt = block_rows(t(p + "gate.weight")); block_append(qk, gt); }
+                        a.qkvg_blk = block_upload(qk);
                         if (!a.time && a.gate)
-                            a.vg_q8 = q8_upload(q8_interleave(q8_slice(qk, size_t(2) * D, size_t(D)), gt, size_t(D)));
+                            a.vg_blk = block_upload(block_interleave(block_slice(qk, size_t(2) * D, size_t(D)), gt, size_t(D)));
                     }
                 } else {
                     auto q = rows_f32(t(p + "qkv.weight"));
@@ -582,11 +582,11 @@ struct Engine::Impl {
                 }
                 auto w3 = rows_f16(t(b + "ffn_w3.weight"));
                 w.w3 = reinterpret_cast<__half*>(upload(w3.data(), w3.size()));
-                if (q8_type(t(b + "ffn_w3.weight"))) w.w3_q8 = q8_upload(q8_rows(t(b + "ffn_w3.weight")));
-                if (q8_type(t(b + "ffn_w12.weight")) &&
+                if (block_type(t(b + "ffn_w3.weight"))) w.w3_blk = block_upload(block_rows(t(b + "ffn_w3.weight")));
+                if (block_type(t(b + "ffn_w12.weight")) &&
                     unit_gains(static_cast<const float*>(t(b + "ffn_norm.weight").data), size_t(D))) {
-                    Q8Host z12 = q8_rows(t(b + "ffn_w12.weight"));
-                    w.w12_q8 = q8_upload(q8_interleave(q8_slice(z12, 0, size_t(F)), q8_slice(z12, size_t(F), size_t(F)), size_t(F)));
+                    BlockHost z12 = block_rows(t(b + "ffn_w12.weight"));
+                    w.w12_blk = block_upload(block_interleave(block_slice(z12, 0, size_t(F)), block_slice(z12, size_t(F), size_t(F)), size_t(F)));
                 }
             } else {
                 auto z = rows_f32(t(b + "ffn_w12.weight"));
@@ -602,9 +602,9 @@ struct Engine::Impl {
             auto a = rows_f16(t("head.hidden.weight")); h_hid = reinterpret_cast<__half*>(upload(a.data(), a.size()));
             auto b = rows_f16(t("head.out.weight")); h_out = reinterpret_cast<__half*>(upload(b.data(), b.size()));
             auto c = rows_f16(t("head.res.weight")); h_res = reinterpret_cast<__half*>(upload(c.data(), c.size()));
-            if (q8_type(t("head.hidden.weight"))) h_hid_q8 = q8_upload(q8_rows(t("head.hidden.weight")));
-            if (q8_type(t("head.out.weight"))) h_out_q8 = q8_upload(q8_rows(t("head.out.weight")));
-            if (q8_type(t("head.res.weight"))) h_res_q8 = q8_upload(q8_rows(t("head.res.weight")));
+            if (block_type(t("head.hidden.weight"))) h_hid_blk = block_upload(block_rows(t("head.hidden.weight")));
+            if (block_type(t("head.out.weight"))) h_out_blk = block_upload(block_rows(t("head.out.weight")));
+            if (block_type(t("head.res.weight"))) h_res_blk = block_upload(block_rows(t("head.res.weight")));
         } else {
             auto a = rows_f32(t("head.hidden.weight")); fh_hid = upload(a.data(), a.size());
             auto b = rows_f32(t("head.out.weight")); fh_out = upload(b.data(), b.size());
@@ -780,7 +780,7 @@ struct Engine::Impl {
             a.A = ph.as<__half>(); a.lda = 4 * D; a.B = p_out; a.ldb = 4 * D; a.M = int(PR); a.N = D; a.K = 4 * D;
             a.epi.out = x.p; a.epi.ldo = D; a.epi.bias = pb_out; a.epi.resid = x.as<float>();
             a.epi.row_group = N; a.epi.row_stride = S;
-            q8(a, p_out_q8);
+            block_b(a, p_out_blk);
             gemm(EPI_RESID, a);
         } else {
             SimtGemm g;
@@ -841,14 +841,14 @@ struct Engine::Impl {
                 GemmArgs a;
                 a.A = a_in; a.lda = D; a.B = w.w12; a.ldb = D; a.M = Mm; a.N = 2 * F; a.K = D;
                 a.epi.out = hb.p; a.epi.ldo = F; a.epi.bias = w.b12;
-                q8(a, w.w12_q8);
+                block_b(a, w.w12_blk);
                 gather_a(a);
                 consume(a.epi);
                 gemm(EPI_SWIGLU, a);
                 GemmArgs o;
                 o.A = hb.as<__half>(); o.lda = F; o.B = w.w3; o.ldb = F; o.M = Mm; o.N = D; o.K = F;
                 o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = w.b3; o.epi.resid = x.as<float>();
-                q8(o, w.w3_q8);
+                block_b(o, w.w3_blk);
                 if (in_tail) scatter_out(o.epi);
                 produce(o.epi);
                 gemm(EPI_RESID, o);
@@ -881,17 +881,17 @@ struct Engine::Impl {
             GemmArgs a;
             a.A = dec.as<__half>(); a.lda = D; a.B = h_hid; a.ldb = D; a.M = DR; a.N = 4 * D; a.K = D;
             a.epi.out = hh.p; a.epi.ldo = 4 * D;
-            q8(a, h_hid_q8);
+            block_b(a, h_hid_blk);
             gemm(EPI_SILU, a);
             GemmArgs b;
             b.A = hh.as<__half>(); b.lda = 4 * D; b.B = h_out; b.ldb = 4 * D; b.M = DR; b.N = NQ; b.K = 4 * D;
             b.epi.out = hraw.p; b.epi.ldo = NQ;
-            q8(b, h_out_q8);
+            block_b(b, h_out_blk);
             gemm(EPI_F32, b);
             GemmArgs c;
             c.A = dec.as<__half>(); c.lda = D; c.B = h_res; c.ldb = D; c.M = DR; c.N = NQ; c.K = D;
             c.epi.out = hraw.p; c.epi.ldo = NQ; c.epi.resid = hraw.as<float>();
-            q8(c, h_res_q8);
+            block_b(c, h_res_blk);
             gemm(EPI_RESID, c);
         } else {
             const int order = round_a ? ORDER_CHAIN : ORDER_F64;
@@ -950,18 +950,18 @@ struct Engine::Impl {
             g.A = a_in; g.lda = D; g.M = M; g.K = D; g.epi.out = att16; g.epi.ldo = D;
             if (tail_stage == 2) gather_a(g);
             consume(g.epi);
-            if (a.gate) { g.B = a.vg; g.ldb = D; g.N = 2 * D; g.epi.bias = a.b_vg; q8(g, a.vg_q8); gemm(EPI_VGATE, g); }
+            if (a.gate) { g.B = a.vg; g.ldb = D; g.N = 2 * D; g.epi.bias = a.b_vg; block_b(g, a.vg_blk); gemm(EPI_VGATE, g); }
             else {
                 g.B = a.qkvg + size_t(2) * D * D; g.ldb = D; g.N = D;
                 g.epi.bias = a.b_qkvg ? a.b_qkvg + 2 * D : nullptr;
-                q8(g, a.qkvg_q8, int64_t(2) * D);
+                block_b(g, a.qkvg_blk, int64_t(2) * D);
                 gemm(EPI_F16, g);
             }
         } else {
             GemmArgs g;
             g.A = a_in; g.lda = D; g.B = a.qkvg; g.ldb = D; g.M = M; g.N = a.n_qkvg; g.K = D;
             g.epi.bias = a.b_qkvg;
-            q8(g, a.qkvg_q8);
+            block_b(g, a.qkvg_blk);
             consume(g.epi);
             g.epi.qkvg[0] = qb.as<__half>(); g.epi.qkvg[1] = kb.as<__half>(); g.epi.qkvg[2] = vb.as<__half>();
             g.epi.qkvg[3] = gb.as<__half>();
@@ -988,7 +988,7 @@ struct Engine::Impl {
         }
         o.A = att16; o.lda = D; o.B = a.out; o.ldb = D; o.N = D; o.K = D;
         o.epi.out = x.p; o.epi.ldo = D; o.epi.bias = a.b_out; o.epi.resid = x.as<float>();
-        q8(o, a.out_q8);
+        block_b(o, a.out_blk);
         if (tail_stage) scatter_out(o.epi);
         produce(o.epi);
         gemm(EPI_RESID, o);
@@ -1236,11 +1236,11 @@ void Engine::attention_kernels(int mode) {
 }
 
 bool Engine::dequant_prologue(bool on) {
-    const bool any = impl_->p_out_q8.q || impl_->h_hid_q8.q || (!impl_->mlp.empty() && impl_->mlp[0].w3_q8.q);
-    impl_->q8_prologue = on && any;
+    const bool any = impl_->p_out_blk.q || impl_->h_hid_blk.q || (!impl_->mlp.empty() && impl_->mlp[0].w3_blk.q);
+    impl_->dq_prologue = on && any;
     impl_->drop_graph();
     impl_->have_last = false;
-    return impl_->q8_prologue == on;
+    return impl_->dq_prologue == on;
 }
 
 void Engine::decoder_tail(bool on) {
