@@ -183,9 +183,29 @@ __device__ __forceinline__ void pack32(const float* v, uint32_t* w) {
 
 // Epilogue of one 128 x BN accumulator for one warp: accumulator rows [mw, mw + 32) (its
 // TMEM lane quarter) and column group `part` of PARTS.
+// RoPE table entries of the q/k/v/gate epilogue for the row this lane reads from TMEM:
+// with rope_half <= 16 and tables whose two halves are equal (cos[d] == cos[d + 32], as for
+// emb = [freqs, freqs]) only dims 0..15 of cos and sin are needed, fetched once for both
+// heads of the column group. Loaded before the accumulator is ready (two dependent global
+// loads: the row's table index, then its entries).
+struct RopeRow {
+    bool on = false;
+    float4 tcs[8];
+};
+__device__ __forceinline__ void load_rope_row(const GemmArgs& g, int m, int first, RopeRow& rr) {
+    const GemmEpilogue& e = g.epi;
+    rr.on = e.rope && e.rope_dup && e.rope_half <= 16 && m < g.M && first / e.D < 2;
+    if (!rr.on) return;
+    const int64_t row = e.rope_row[m];
+    const float4* ct = reinterpret_cast<const float4*>(e.cos_tab + row * 64);
+    const float4* st = reinterpret_cast<const float4*>(e.sin_tab + row * 64);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { rr.tcs[j] = ct[j]; rr.tcs[4 + j] = st[j]; }
+}
+
 template <int KIND, int PARTS>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, int m0, int n0, int quarter, int lane,
-                                              int part, uint8_t* buf, float rsc) {
+                                              int part, uint8_t* buf, float rsc, const RopeRow& rr) {
     const int half = part;
     const GemmEpilogue& e = g.epi;
     const int mw = m0 + quarter * 32;
@@ -376,17 +396,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
             hm[i] = (mi / e.S) * e.H * e.S + mi % e.S;
         }
         // RoPE table entries of this token's position, fetched once for both heads of the
-        // half: with rope_half <= 16 and tables whose two halves are equal (cos[d] == cos[d + 32],
-        // as for emb = [freqs, freqs]) only dims 0..15 of cos and sin are needed.
-        const int first = n0 + half * C * 64;
-        const bool rope16 = e.rope && e.rope_dup && e.rope_half <= 16 && row_ok && first / e.D < 2;
-        float4 tcs[8];
-        if (rope16) {
-            const float4* ct = reinterpret_cast<const float4*>(e.cos_tab + int64_t(e.rope_row[m]) * 64);
-            const float4* st = reinterpret_cast<const float4*>(e.sin_tab + int64_t(e.rope_row[m]) * 64);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) { tcs[j] = ct[j]; tcs[4 + j] = st[j]; }
-        }
+        // half (load_rope_row, done before the accumulator was ready).
+        const bool rope16 = rr.on;
+        const float4* tcs = rr.tcs;
 #pragma unroll 1
         for (int c = 0; c < C; ++c) {
             const int col = n0 + (half * C + c) * 64;
@@ -628,12 +640,15 @@ __global__ void __launch_bounds__(Cfg<KIND, FMT>::THREADS, 1)
             const int b = acc & 1;
             const uint32_t aph = (acc >> 1) & 1;
             const int m0 = (tile / n_tiles) * 2 * BM + int(rank) * BM, n0 = (tile % n_tiles) * BN;
-            // The row's 1/rms (norm carried by the GEMM) is read before the accumulator is ready.
+            // The row's 1/rms (norm carried by the GEMM) and RoPE table entries are read before
+            // the accumulator is ready.
             float rsc = 1.0f;
+            RopeRow rr;
             if constexpr (KIND != EPI_F32 && KIND != EPI_RESID) {
                 const int m = m0 + quarter * 32 + lane;
                 rsc = row_scale(g.epi, a_row(g, m), m < g.M);
             }
+            if constexpr (KIND == EPI_QKVG) load_rope_row(g, m0 + quarter * 32 + lane, n0 + part * 128, rr);
             bool ok = true;
             if (lane == 0) ok = wait_or_abort(&sm->acc_full[b], aph, abort, err, kDevTimeoutAccFull);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -641,7 +656,7 @@ __global__ void __launch_bounds__(Cfg<KIND, FMT>::THREADS, 1)
             __syncwarp();
             tc_fence_after();
             const uint32_t tacc = tmem + (uint32_t(quarter * 32) << 16) + b * BN;
-            epilogue_tile<KIND, PARTS>(g, tacc, m0, n0, quarter, lane, part, stage + (warp - 2) * 32 * 128, rsc);
+            epilogue_tile<KIND, PARTS>(g, tacc, m0, n0, quarter, lane, part, stage + (warp - 2) * 32 * 128, rsc, rr);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster_relaxed(b ? acc_empty1 : acc_empty0);
