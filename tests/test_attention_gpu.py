@@ -184,59 +184,3 @@ def test_attention_time_long(dev, S, N, L, cov, kernel, dense):
     tol = 4e-3 * scale + want.abs() * 2.0 ** -10
     bad = (got - want).abs() > tol
     assert not bad.any(), f"max err {(got - want).abs().max().item():.3e} at {bad.nonzero()[:4].tolist()}"
-
-
-@pytest.mark.parametrize("S,N,L,cov,gated,rows", [(72, 64, 64, 0, True, 37), (72, 64, 64, 0, False, 9), (36, 32, 32, 0, True, 50),
-                                                 (128, 120, 120, 0, True, 11), (1, 1, 1, 0, True, 3), (17, 16, 16, 0, True, 7),
-                                                 (70, 35, 32, 1, True, 13), (96, 90, 90, 0, True, 300)])
-def test_attention_time_ws_equals_tc(dev, S, N, L, cov, gated, rows):
-    """The warp-specialised kernel (one persistent CTA per SM, four problems in flight, TMA
-    producer / MMA thread / two softmax warpgroups / epilogue warpgroup) gives the same bits as
-    the four-CTA tensor-core kernel: same operations in the same order per query. Also the
-    device timing of both on a cfg5-sized launch (printed)."""
-    H, bs = 4, 32
-    g = torch.Generator().manual_seed(S * 11 + rows)
-    q = (torch.randn(rows, H, S, 64, generator=g) * 2).half().to(dev)
-    k = (torch.randn(rows, H, S, 64, generator=g) * 2).half().to(dev)
-    v = torch.randn(rows, H, S, 64, generator=g).half().to(dev)
-    gate = torch.rand(rows, H, S, 64, generator=g).half().to(dev) if gated else None
-    valid = torch.rand(rows, N, generator=g) > 0.2
-    words = (N + 31) // 32
-    bits = np.zeros((rows, words), np.uint32)
-    vn = valid.numpy()
-    for p in range(N):
-        bits[:, p // 32] |= vn[:, p].astype(np.uint32) << np.uint32(p % 32)
-    dbits = torch.from_numpy(bits.view(np.int32)).to(dev)
-    drole = torch.tensor(([0, 1, 2] * rows)[:rows], dtype=torch.int8).to(dev)
-    outs = []
-    for kernel in (1, 4):
-        out = torch.full((rows * S, H * 64), float("nan"), device=dev, dtype=torch.float16)
-        err = C.c_int32(0)
-        rc = tb.lib().tsb_test_attention_time_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), gate.data_ptr() if gated else None,
-                                                 out.data_ptr(), dbits.data_ptr(), drole.data_ptr(), rows, H, S, N, L, cov,
-                                                 bs, kernel, 0, None, C.byref(err))
-        assert rc == 0, (kernel, rc, err.value)
-        outs.append(out.cpu())
-    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
-
-
-def test_attention_time_ws_timing(dev):
-    """Device time of the two S <= 128 kernels on the cfg5 shape at B = 1024 (2,048 rows x 12
-    heads, S = 72), printed; both produce the same bits (test above)."""
-    rows, H, S, N = 2048, 12, 72, 64
-    q = torch.randn(rows, H, S, 64, device=dev).half()
-    k = torch.randn(rows, H, S, 64, device=dev).half()
-    v = torch.randn(rows, H, S, 64, device=dev).half()
-    gate = torch.rand(rows, H, S, 64, device=dev).half()
-    dbits = torch.full((rows, 2), -1, dtype=torch.int32, device=dev)
-    out = torch.empty((rows * S, H * 64), device=dev, dtype=torch.float16)
-    res = {}
-    for kernel in (1, 4, 1, 4):
-        ms = C.c_float(0)
-        err = C.c_int32(0)
-        rc = tb.lib().tsb_test_attention_time_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), gate.data_ptr(), out.data_ptr(),
-                                                 dbits.data_ptr(), None, rows, H, S, N, N, 0, 32, kernel, 20, C.byref(ms),
-                                                 C.byref(err))
-        assert rc == 0, (kernel, rc, err.value)
-        res.setdefault(kernel, []).append(ms.value)
-    print(f"attention S=72, 24,576 problems: four-CTA kernel {res[1]} ms, warp-specialised {res[4]} ms")

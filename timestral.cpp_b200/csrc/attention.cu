@@ -850,326 +850,6 @@ __global__ void __launch_bounds__(AL_THREADS, 2)
     if (warp == 0) tmem_dealloc(tbase, AL_TMEM_COLS);
 }
 
-
-// ---------------------------------------------------------------------------------------
-// Warp-specialised tensor-core time attention (S <= 128): one persistent CTA per SM that keeps
-// up to four (row, head) problems in flight in four 128-column TMEM slots, with each phase of a
-// problem on its own warps, so the phases of different problems overlap inside the SM:
-//   warp 0       TMA producer: q, k, v and sigmoid(gate) tiles of problem i into input buffer
-//                i % WS_NB (a ring), on the buffer's full barrier;
-//   warp 1       TMEM owner (512 columns) and MMA thread: S = Q K^T of problem i into slot
-//                i % 4 once its inputs are in and the slot's previous O has been read; O = P V
-//                once the softmax has written P; polls both without blocking;
-//   warps 4-7    softmax of the even problems, warps 8-11 of the odd ones: the per-query
-//                softmax of the four-CTA kernel (same operations and order), the probabilities
-//                written over the slot's S columns and the row sums into shared memory;
-//   warps 12-15  epilogue: O * (1 / sum) * sigmoid(gate) (the gate tile from the input buffer),
-//                staged row-wise and stored as 128-byte lines; releases the slot and the buffer.
-// The results are those of attn_time_tc_kernel bit for bit.
-constexpr int WS_THREADS = 512;
-constexpr int WS_SLOTS = 4;
-constexpr uint32_t WS_TMEM_COLS = 512;
-
-template <int NK>
-struct WsLayout {
-    __host__ __device__ static constexpr int q_rows(int S) { return (S + 7) / 8 * 8; }
-    // One input buffer: q [QR][64], k [NK][64], v [NK][64], gate [QR][64] (f16, 128-byte rows).
-    __host__ __device__ static constexpr int buf_bytes(int S) { return ((2 * q_rows(S) + 2 * NK) * 128 + 1023) / 1024 * 1024; }
-    static constexpr int STAGE_BYTES = 128 * 128;        // epilogue staging (32 rows x 128 B per warp)
-    static constexpr int SUMS_BYTES = WS_SLOTS * 128 * 4;
-    __host__ __device__ static constexpr int buffers(int S) {
-        const int room = 227 * 1024 - STAGE_BYTES - SUMS_BYTES - 1024 - 512;
-        const int n = room / buf_bytes(S);
-        return n > 5 ? 5 : n;
-    }
-    __host__ __device__ static constexpr int smem(int S) {
-        return buffers(S) * buf_bytes(S) + STAGE_BYTES + SUMS_BYTES + 1024 + 512;
-    }
-};
-
-struct WsBars {
-    uint64_t in_full[5], in_empty[5];
-    uint64_t s_full[WS_SLOTS], p_ready[WS_SLOTS], o_full[WS_SLOTS], tm_free[WS_SLOTS];
-    uint32_t tmem;
-    int abort;
-};
-
-// Bounded poll of one barrier phase without suspending (the MMA thread alternates between
-// several): true when complete; on the cycle limit the kernel's abort flag is raised.
-__device__ __forceinline__ bool ws_ready(uint64_t* bar, uint32_t parity) { return mbar_test_wait(bar, parity); }
-
-template <int NK>
-__global__ void __launch_bounds__(WS_THREADS, 1)
-    attn_time_ws_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                        const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_g,
-                        const int has_gate, __half* __restrict__ out, int rows, int H, const MaskMeta mm, int* err) {
-    using Lay = WsLayout<NK>;
-    extern __shared__ uint8_t smem_raw[];
-    const int S = mm.S, D = H * 64;
-    const int QR = Lay::q_rows(S), NB = Lay::buffers(S), BUF = Lay::buf_bytes(S);
-    uint8_t* bufs = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* obuf = bufs + NB * BUF;
-    float* sums = reinterpret_cast<float*>(obuf + Lay::STAGE_BYTES);
-    WsBars* bars = reinterpret_cast<WsBars*>(obuf + Lay::STAGE_BYTES + Lay::SUMS_BYTES);
-    volatile int* abort = &bars->abort;
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int num = rows * H;
-    // Problems of this CTA: blockIdx.x + i * gridDim.x for i < count.
-    const int count = num > int(blockIdx.x) ? (num - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
-
-    if (threadIdx.x == 0) {
-        for (int b = 0; b < 5; ++b) { mbar_init(&bars->in_full[b], 1); mbar_init(&bars->in_empty[b], 1 + 4); }
-        for (int j = 0; j < WS_SLOTS; ++j) {
-            mbar_init(&bars->s_full[j], 1); mbar_init(&bars->p_ready[j], 4);
-            mbar_init(&bars->o_full[j], 1); mbar_init(&bars->tm_free[j], 4);
-        }
-        bars->abort = 0;
-        mbar_fence_init();
-        fence_proxy_async();
-    }
-    if (warp == 1) { tmem_alloc(&bars->tmem, WS_TMEM_COLS); tmem_relinquish(); }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = bars->tmem;
-    constexpr float kScaleLog2e = 0.125f * 1.4426950408889634f;
-
-    if (warp == 0) {
-        // ---- producer -------------------------------------------------------------------
-        if (lane == 0) {
-            const uint32_t bytes = uint32_t((2 * QR + 2 * NK) * 128) - (has_gate ? 0u : uint32_t(QR * 128));
-            for (int i = 0; i < count; ++i) {
-                const int b = i % NB;
-                if (i >= NB && !at_wait(&bars->in_empty[b], ((i / NB) - 1) & 1, abort, err)) break;
-                uint8_t* base = bufs + b * BUF;
-                const int prob = int(blockIdx.x) + i * int(gridDim.x);
-                mbar_arrive_expect_tx(&bars->in_full[b], bytes);
-                tma_load_3d(base, &map_q, &bars->in_full[b], 0, 0, prob);
-                tma_load_3d(base + QR * 128, &map_k, &bars->in_full[b], 0, 0, prob);
-                tma_load_3d(base + (QR + NK) * 128, &map_v, &bars->in_full[b], 0, 0, prob);
-                if (has_gate) tma_load_3d(base + (QR + 2 * NK) * 128, &map_g, &bars->in_full[b], 0, 0, prob);
-            }
-        }
-    } else if (warp == 1) {
-        // ---- MMA thread: S = Q K^T and O = P V, polled in turn --------------------------
-        if (lane == 0) {
-            const uint32_t id1 = idesc_f16(128, NK), id2 = idesc_f16_bmn(128, 64);
-            int ns = 0, np = 0;                  // next problem for S, for P V
-            long long idle_since = clock64();
-            while (np < count && !*abort) {
-                bool progress = false;
-                if (ns < count && ns - np < WS_SLOTS) {
-                    const int b = ns % NB, slot = ns % WS_SLOTS;
-                    if (ws_ready(&bars->in_full[b], (ns / NB) & 1) &&
-                        (ns < WS_SLOTS || ws_ready(&bars->tm_free[slot], ((ns / WS_SLOTS) - 1) & 1))) {
-                        tc_fence_after();
-                        const uint32_t qa = smem_u32(bufs + b * BUF);
-                        const uint64_t dq = smem_desc_sw128(qa), dk = smem_desc_sw128(qa + QR * 128);
-                        const uint32_t tS = tmem + uint32_t(slot) * 128;
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) mma_f16(tS, dq + uint64_t(2 * k), dk + uint64_t(2 * k), id1, k > 0);
-                        mma_commit(&bars->s_full[slot]);
-                        ++ns;
-                        progress = true;
-                    }
-                }
-                if (np < ns) {
-                    const int b = np % NB, slot = np % WS_SLOTS;
-                    if (ws_ready(&bars->p_ready[slot], (np / WS_SLOTS) & 1)) {
-                        tc_fence_after();
-                        const uint32_t sv = smem_u32(bufs + b * BUF + (QR + NK) * 128);
-                        const uint32_t tS = tmem + uint32_t(slot) * 128;
-#pragma unroll
-                        for (int kk = 0; kk < NK / 16; ++kk)
-                            mma_f16_ts(tS + AT_O_COL, tS + kk * 8, smem_desc_sw128(sv + kk * 16 * 128), id2, kk > 0);
-                        mma_commit(&bars->o_full[slot]);
-                        mma_commit(&bars->in_empty[b]);
-                        ++np;
-                        progress = true;
-                    }
-                }
-                if (progress) {
-                    idle_since = clock64();
-                } else if (clock64() - idle_since > kWaitCycles) {
-                    *abort = 1;
-                    record_error(err, kDevTimeoutAttn);
-                    break;
-                }
-            }
-        }
-    } else if (warp >= 4 && warp < 12) {
-        // ---- softmax: group 0 (warps 4-7) the even problems, group 1 (warps 8-11) the odd --
-        const int grp = (warp - 4) >> 2, quarter = warp & 3;
-        const int t = quarter * 32 + lane;
-        const bool live = t < S;
-        const uint32_t lane_base = uint32_t(quarter * 32) << 16;
-        for (int i = grp; i < count; i += 2) {
-            const int slot = i % WS_SLOTS;
-            const int prob = int(blockIdx.x) + i * int(gridDim.x);
-            const int r = prob / H;
-            uint32_t allowed[4];
-            key_set(mm, r, t, live, allowed);
-            int hi = -1;
-#pragma unroll
-            for (int w = 3; w >= 0; --w)
-                if (hi < 0 && allowed[w]) hi = w * 32 + 31 - __clz(allowed[w]);
-            const int kmax = __reduce_max_sync(0xffffffffu, hi + 1) - 1;
-            if (!warp_wait(&bars->s_full[slot], (i / WS_SLOTS) & 1, abort, err)) break;
-            tc_fence_after();
-            const uint32_t tS = tmem + uint32_t(slot) * 128;
-            float sum = 0.f;
-            if (kmax >= 0) {
-                float mxj[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) mxj[j] = -INFINITY;
-#pragma unroll
-                for (int c = 0; c < NK / 16; ++c) {
-                    if (c * 16 > kmax) break;
-                    uint32_t sc[16];
-                    tmem_ld16(tS + lane_base + c * 16, sc);
-                    tmem_ld_wait();
-                    const uint32_t bits = allowed[(c * 16) >> 5] >> ((c * 16) & 31);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if ((bits >> j) & 1u) mxj[j & 7] = fmaxf(mxj[j & 7], __uint_as_float(sc[j]));
-                }
-                const float mx = fmaxf(fmaxf(fmaxf(mxj[0], mxj[1]), fmaxf(mxj[2], mxj[3])),
-                                       fmaxf(fmaxf(mxj[4], mxj[5]), fmaxf(mxj[6], mxj[7])));
-                const float off = live ? mx * kScaleLog2e : 0.f;
-                float sj[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) sj[j] = 0.f;
-#pragma unroll
-                for (int c = 0; c < NK / 16; ++c) {
-                    uint32_t pk[8];
-                    if (c * 16 <= kmax) {
-                        uint32_t sc[16];
-                        tmem_ld16(tS + lane_base + c * 16, sc);
-                        tmem_ld_wait();
-                        const uint32_t bits = allowed[(c * 16) >> 5] >> ((c * 16) & 31);
-                        float p[16];
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            p[j] = (bits >> j) & 1u ? exp2_ftz(__fmaf_rn(__uint_as_float(sc[j]), kScaleLog2e, -off)) : 0.f;
-                            sj[j & 7] += p[j];
-                        }
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) pk[j] = pack_half2(p[2 * j], p[2 * j + 1]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) pk[j] = 0u;
-                    }
-                    tmem_st8(tS + lane_base + c * 8, pk);
-                }
-                tmem_st_wait();
-                sum = ((sj[0] + sj[1]) + (sj[2] + sj[3])) + ((sj[4] + sj[5]) + (sj[6] + sj[7]));
-            }
-            sums[slot * 128 + t] = sum;
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->p_ready[slot]);
-        }
-    } else if (warp >= 12) {
-        // ---- epilogue ----------------------------------------------------------------------
-        const int quarter = warp & 3;
-        const int t = quarter * 32 + lane;
-        const bool live = t < S, any_live = quarter * 32 < S;
-        const uint32_t lane_base = uint32_t(quarter * 32) << 16;
-        for (int i = 0; i < count; ++i) {
-            const int slot = i % WS_SLOTS, b = i % NB;
-            const int prob = int(blockIdx.x) + i * int(gridDim.x);
-            const int r = prob / H, h = prob % H;
-            // o_full: O is complete; p_ready and in_full (both already complete) make the
-            // softmax's row sums and the TMA-written gate tile visible to these threads.
-            if (!warp_wait(&bars->o_full[slot], (i / WS_SLOTS) & 1, abort, err)) break;
-            if (!warp_wait(&bars->p_ready[slot], (i / WS_SLOTS) & 1, abort, err)) break;
-            if (!warp_wait(&bars->in_full[b], (i / NB) & 1, abort, err)) break;
-            __syncwarp();
-            tc_fence_after();
-            const uint32_t tO = tmem + uint32_t(slot) * 128 + AT_O_COL;
-            const uint8_t* gbase = has_gate ? bufs + b * BUF + (QR + 2 * NK) * 128 : nullptr;
-            const float inv = live ? 1.0f / sums[slot * 128 + t] : 0.f;
-            auto stage = [&](const uint32_t (&o)[32], int half32) {
-#pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
-                    const int c = half32 * 4 + c4;
-                    float y[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) y[j] = __uint_as_float(o[c4 * 8 + j]) * inv;
-                    if (gbase && live) {
-                        const uint4 gu = *reinterpret_cast<const uint4*>(gbase + t * 128 + ((c ^ (t & 7)) << 4));
-                        const __half2* gh = reinterpret_cast<const __half2*>(&gu);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const float2 f = __half22float2(gh[j]);
-                            y[2 * j] = __fmul_rn(y[2 * j], f.x);
-                            y[2 * j + 1] = __fmul_rn(y[2 * j + 1], f.y);
-                        }
-                    }
-                    uint4 u;
-                    u.x = pack_half2(y[0], y[1]); u.y = pack_half2(y[2], y[3]);
-                    u.z = pack_half2(y[4], y[5]); u.w = pack_half2(y[6], y[7]);
-                    *reinterpret_cast<uint4*>(obuf + t * 128 + ((c ^ (t & 7)) << 4)) = u;
-                }
-            };
-            uint32_t o[32];
-            if (any_live) {
-                tmem_ld32(tO + lane_base, o);
-                tmem_ld_wait();
-                stage(o, 0);
-                tmem_ld32(tO + lane_base + 32, o);
-                tmem_ld_wait();
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->tm_free[slot]);     // the slot's next S may start
-            if (any_live) stage(o, 1);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->in_empty[b]);       // gate tile read
-            if (!any_live) continue;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int row = quarter * 32 + j * 4 + (lane >> 3), chunk = lane & 7;
-                if (row < S)
-                    *reinterpret_cast<uint4*>(out + (int64_t(r) * S + row) * D + h * 64 + chunk * 8) =
-                        *reinterpret_cast<const uint4*>(obuf + row * 128 + ((chunk ^ (row & 7)) << 4));
-            }
-            __syncwarp();
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, WS_TMEM_COLS);
-}
-
-template <int NK>
-cudaError_t launch_attn_ws(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out, int rows,
-                           int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
-    using Lay = WsLayout<NK>;
-    const int smem = Lay::smem(mm.S);
-    if (Lay::buffers(mm.S) < 2) return cudaErrorInvalidValue;
-    static bool configured[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(attn_time_ws_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             227 * 1024);
-        if (e != cudaSuccess) return e;
-        configured[dev] = true;
-    }
-    CUtensorMap mq, mk, mv, mg;
-    const int64_t planes = int64_t(rows) * H;
-    const int QR = Lay::q_rows(mm.S);
-    if (!make_map_3d_f16(&mq, q, planes, mm.S, QR) || !make_map_3d_f16(&mk, k, planes, mm.S, NK) ||
-        !make_map_3d_f16(&mv, v, planes, mm.S, NK) || !make_map_3d_f16(&mg, gate ? gate : q, planes, mm.S, QR))
-        return cudaErrorInvalidValue;
-    int grid = device_sm_count();
-    if (int64_t(grid) > planes) grid = int(planes);
-    attn_time_ws_kernel<NK><<<grid, WS_THREADS, smem, stream>>>(mq, mk, mv, mg, gate ? 1 : 0, out, rows, H, mm, err);
-    return cudaGetLastError();
-}
-
 }  // namespace
 
 cudaError_t attention_time_tc_long(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
@@ -1483,23 +1163,6 @@ cudaError_t attention_time_tc(const __half* q, const __half* k, const __half* v,
         case 96: return launch_attn_tc<96>(q, k, v, gate, out, rows, H, mm, stream, err);
         case 112: return launch_attn_tc<112>(q, k, v, gate, out, rows, H, mm, stream, err);
         case 128: return launch_attn_tc<128>(q, k, v, gate, out, rows, H, mm, stream, err);
-    }
-    return cudaErrorInvalidValue;
-}
-
-cudaError_t attention_time_ws(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
-                              int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
-    if (rows <= 0) return cudaSuccess;
-    if (mm.S <= 0 || mm.S > 128) return cudaErrorInvalidValue;
-    switch ((mm.S + 15) / 16 * 16) {
-        case 16: return launch_attn_ws<16>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 32: return launch_attn_ws<32>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 48: return launch_attn_ws<48>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 64: return launch_attn_ws<64>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 80: return launch_attn_ws<80>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 96: return launch_attn_ws<96>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 112: return launch_attn_ws<112>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 128: return launch_attn_ws<128>(q, k, v, gate, out, rows, H, mm, stream, err);
     }
     return cudaErrorInvalidValue;
 }

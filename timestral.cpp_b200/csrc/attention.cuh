@@ -28,12 +28,6 @@ struct MaskMeta {
 cudaError_t attention_time_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
                               int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err);
 
-// The same (S <= 128, same results bit for bit) with one persistent warp-specialised CTA per SM
-// that keeps four problems in flight: TMA producer, MMA thread, two softmax warpgroups,
-// epilogue warpgroup.
-cudaError_t attention_time_ws(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
-                              int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err);
-
 // Same for S > 128 (any S): key/value tiles of 64 tokens, queries in tiles of 128.
 cudaError_t attention_time_tc_long(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
                                    int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err);
