@@ -104,6 +104,28 @@ def test_row_gather_decoder_tokens(dev, group, R):
     assert torch.equal(x[keep], x0[keep])
 
 
+@pytest.mark.parametrize("K", [768, 2048])
+def test_resid_rows_independent_of_tile_schedule(dev, K):
+    """Residual add over many tiles per CTA pair (the epilogue prefetches the residual rows
+    of its next chunks ahead, across tile boundaries, for K <= 1024; longer K loads them
+    into registers): every row equals the same row computed in a launch of 4,096 rows, where
+    the pairs take different tiles, bit for bit, and the float64 reference within the
+    accumulation tolerance. M is ragged (not a multiple of the 256-row tile)."""
+    M, N = 60_001, 768
+    A = torch.randn(M, K, device=dev).half()
+    B = (torch.randn(N, K, device=dev) * 0.05).half()
+    x0 = torch.randn(M, N, device=dev)
+    full = x0.clone()
+    run(2, A, B, M, N, K, out=full, ldo=N, resid=full)
+    sliced = x0.clone()
+    for r0 in range(0, M, 4096):
+        r1 = min(M, r0 + 4096)
+        part = sliced[r0:r1]
+        run(2, A[r0:r1], B, r1 - r0, N, K, out=part, ldo=N, resid=part)
+    assert torch.equal(full, sliced)
+    close(full, x0.double() + ref_mm(A, B), K)
+
+
 def q8_weights(N, K, dev, seed):
     """Random Q8_0 weights: int8 values [N][K], f16 block scales [N][K/32] (d = amax/127 of
     N(0, 0.02) rows, as the converter writes them), and the f16 weights q * d rounded once."""

@@ -60,17 +60,21 @@ constexpr int CONV_WARPS = 2;                 // 384 threads with the 8 epilogue
 // FMT != FMT_F16: the dequantising-prologue variants, which add CONV_WARPS converter warps
 // after the epilogue warps, use two column groups for every epilogue kind (register budget)
 // and four stages.
-template <int KIND, int FMT = FMT_F16>
+template <int KIND, int FMT = FMT_F16, bool RING_OK = true>
 struct Cfg {
     static constexpr bool Q8 = FMT != FMT_F16;
     static constexpr int PARTS = (Q8 || KIND == EPI_QKVG || KIND == EPI_RESID) ? 2 : 4;
     static constexpr int EPI_WARPS = 4 * PARTS;
     static constexpr int THREADS = 64 + 32 * EPI_WARPS + (Q8 ? 32 * CONV_WARPS : 0);
     static constexpr int STAGE = FMT == FMT_Q8 ? Q8_STAGE_BYTES : FMT == FMT_KQ ? KQ_STAGE_BYTES : STAGE_BYTES;
-    static constexpr int STAGES = Q8 ? 4 : PARTS == 2 ? 6 : 5;
-    static constexpr int EPI_STAGE_BYTES = EPI_WARPS * 32 * 128;   // per-warp transposition blocks
+    // The residual add (F16 weights) prefetches its residual rows into a ring of two
+    // transposition blocks per warp (see resid_prefetch), for one operand stage less.
+    static constexpr bool RING = RING_OK && KIND == EPI_RESID && !Q8;
+    static constexpr int STAGES = Q8 ? 4 : RING ? 5 : PARTS == 2 ? 6 : 5;
+    static constexpr int EPI_STAGE_BYTES = EPI_WARPS * 32 * 128 * (RING ? 2 : 1);   // per-warp transposition blocks
     static constexpr int SMEM_BYTES = STAGES * STAGE + EPI_STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+    static_assert(!RING || PARTS == 2, "the residual ring holds two column groups");
 };
 
 template <int STAGES>
@@ -203,6 +207,28 @@ __device__ __forceinline__ void load_rope_row(const GemmArgs& g, int m, int firs
     for (int j = 0; j < 4; ++j) { rr.tcs[j] = ct[j]; rr.tcs[4 + j] = st[j]; }
 }
 
+// Residual-add epilogue, norm carried by the GEMMs: the per-row sums of squares of one
+// 128-column slot (each row's eight column quads are held by the eight lanes sharing
+// lane / 8) into ssq; every |x| <= 2^20 (x / 16 fits f16) whenever a slot's sum of squares
+// is at most 2^40, and a larger sum (rarely a false alarm) sends the forecast to the fallback.
+__device__ __forceinline__ void store_ssq(const GemmEpilogue& e, const int (&orow)[8], const bool (&rok)[8], float (&sq)[8],
+                                          int lane, int slot) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) sq[i] = __fadd_rn(sq[i], __shfl_xor_sync(0xffffffffu, sq[i], o));
+    }
+    bool over = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) over |= !(sq[i] <= 1099511627776.0f);
+    if ((lane & 7) == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (rok[i]) e.ssq[int64_t(orow[i]) * e.ssq_slots + slot] = sq[i];
+    }
+    if (__any_sync(0xffffffffu, over && (lane & 7) == 0) && lane == 0 && e.norm_flag) atomicOr(e.norm_flag, 1);
+}
+
 template <int KIND, int PARTS>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, int m0, int n0, int quarter, int lane,
                                               int part, uint8_t* buf, float rsc, const RopeRow& rr) {
@@ -237,7 +263,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
         float sq[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) sq[i] = 0.f;
-        bool over = false;
 #pragma unroll
         for (int c = 0; c < C; ++c) {
             if constexpr (KIND == EPI_RESID) {
@@ -275,25 +300,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
             __syncwarp();
         }
         if constexpr (KIND == EPI_RESID) {
-            if (e.x16) {
-                // Each row's eight column quads are held by the eight lanes sharing lane / 8.
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-#pragma unroll
-                    for (int o = 1; o < 8; o <<= 1) sq[i] = __fadd_rn(sq[i], __shfl_xor_sync(0xffffffffu, sq[i], o));
-                }
-                const int slot = (n0 + half * C * 32) / 128;
-                // Every |x| <= 2^20 (x / 16 fits f16) whenever a slot's sum of squares is at most
-                // 2^40; a larger sum (rarely a false alarm) sends the forecast to the fallback.
-#pragma unroll
-                for (int i = 0; i < 8; ++i) over |= !(sq[i] <= 1099511627776.0f);
-                if ((lane & 7) == 0) {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        if (rok[i]) e.ssq[int64_t(orow[i]) * e.ssq_slots + slot] = sq[i];
-                }
-                if (__any_sync(0xffffffffu, over && (lane & 7) == 0) && lane == 0 && e.norm_flag) atomicOr(e.norm_flag, 1);
-            }
+            if (e.x16) store_ssq(e, orow, rok, sq, lane, (n0 + half * C * 32) / 128);
         }
     } else if constexpr (KIND == EPI_F16 || KIND == EPI_SILU) {
         // 64 columns (two TMEM reads) per staging pass; the thread stores 8 f16 columns.
@@ -484,12 +491,106 @@ __device__ __forceinline__ void dequant16_scaled(const uint4 q, float2 ab, uint3
     }
 }
 
-template <int KIND, int FMT>
-__global__ void __launch_bounds__(Cfg<KIND, FMT>::THREADS, 1)
+// Residual-add epilogue with its residual rows prefetched (F16 weights). An epilogue warp
+// works through a fixed sequence of 32-column chunks: for its k-th tile (tile pair + k * pairs
+// of the persistent schedule) chunks 4k .. 4k + 3. Chunk q is copied with 16-byte cp.async into
+// slot q % 2 of the warp's two transposition blocks, in the transposed layout the stores use
+// (thread lane holds rows i * 4 + lane / 8, columns (lane % 8) * 4 .. + 3), two chunks before
+// its use and across tile boundaries, so that a chunk's residual latency is covered by the two
+// chunks before it without residual registers held across chunks. Every chunk commits one
+// copy group (empty past the last tile), so a thread's chunk q has landed once at most one
+// younger group is in flight.
+struct ResidRing {
+    int pair, pairs, num_tiles, n_tiles, rank, quarter, part;
+};
+constexpr int RING_CHUNKS = BN / 2 / 32;        // chunks per tile and warp (two column groups)
+constexpr int RING_SLOT = 32 * STAGE_ROW_BYTES;
+// The ring (which costs one of the six operand stages) is used where the epilogue bounds the
+// GEMM: short K (the attention out projection, K = D). Long-K residual adds (the MLP down,
+// K = 2048) keep six stages and the register prefetch of epilogue_tile.
+constexpr int RING_K_MAX = 1024;
+
+__device__ __forceinline__ void resid_prefetch(const GemmArgs& g, const ResidRing& r, int lane, uint32_t q, uint8_t* slot) {
+    const GemmEpilogue& e = g.epi;
+    const int tile = r.pair + int(q / RING_CHUNKS) * r.pairs, c = int(q % RING_CHUNKS);
+    if (tile < r.num_tiles) {
+        const int m0 = (tile / r.n_tiles) * 2 * BM + r.rank * BM, n0 = (tile % r.n_tiles) * BN;
+        const int col = n0 + (r.part * RING_CHUNKS + c) * 32 + (lane & 7) * 4;
+        if (col < g.N) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int row = i * 4 + (lane >> 3), m = m0 + r.quarter * 32 + row;
+                if (m < g.M)
+                    cp_async16(slot + row * STAGE_ROW_BYTES + (((lane & 7) ^ (row & 7)) << 4),
+                               e.resid + out_row(e, m) * e.ldo + col);
+            }
+        }
+    }
+    cp_async_commit();
+}
+
+// The residual-add epilogue of one tile for one warp (two column groups), chunks q0 .. q0 + 3
+// of the warp's sequence; same operations and order as epilogue_tile's.
+__device__ __forceinline__ void epilogue_resid_ring(const GemmArgs& g, uint32_t tacc, int m0, int n0, int lane,
+                                                    const ResidRing& r, uint8_t* ring, uint32_t q0) {
+    const GemmEpilogue& e = g.epi;
+    constexpr int C = RING_CHUNKS;
+    const int mw = m0 + r.quarter * 32;
+    int orow[8];
+    bool rok[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int m = mw + i * 4 + (lane >> 3);
+        rok[i] = m < g.M;
+        orow[i] = rok[i] ? int(out_row(e, m)) : 0;
+    }
+    float sq[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sq[i] = 0.f;
+    uint32_t w[32];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        uint8_t* slot = ring + ((q0 + c) & 1) * RING_SLOT;
+        tmem_ld32(tacc + (r.part * C + c) * 32, w);
+        cp_async_wait<1>();
+        float4 rs[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rs[i] = f4(unstage(slot, i, lane));
+        tmem_ld_wait();
+        __syncwarp();
+        stage_row(slot, lane, w);
+        __syncwarp();
+        const int col = n0 + (r.part * C + c) * 32 + (lane & 7) * 4;
+        if (col < g.N) {
+            const float4 b = e.bias ? *reinterpret_cast<const float4*>(e.bias + col) : make_float4(0, 0, 0, 0);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (!rok[i]) continue;
+                float4 v = f4(unstage(slot, i, lane));
+                if (e.bias) v = add4(v, b);
+                v = add4(rs[i], v);
+                *reinterpret_cast<float4*>(static_cast<float*>(e.out) + int64_t(orow[i]) * e.ldo + col) = v;
+                if (e.x16) {
+                    sq[i] = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, fmaf(v.x, v.x, sq[i]))));
+                    uint2 h;
+                    h.x = pack_half2(v.x * 0.0625f, v.y * 0.0625f);
+                    h.y = pack_half2(v.z * 0.0625f, v.w * 0.0625f);
+                    *reinterpret_cast<uint2*>(e.x16 + int64_t(orow[i]) * e.ldx16 + col) = h;
+                }
+            }
+        }
+        __syncwarp();
+        resid_prefetch(g, r, lane, q0 + c + 2, slot);
+    }
+    if (e.x16) store_ssq(e, orow, rok, sq, lane, (n0 + r.part * C * 32) / 128);
+}
+
+template <int KIND, int FMT, bool RING_OK>
+__global__ void __launch_bounds__(Cfg<KIND, FMT, RING_OK>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_bq, const __grid_constant__ CUtensorMap map_bd,
                    const GemmArgs g, int* err) {
-    using CF = Cfg<KIND, FMT>;
+    using CF = Cfg<KIND, FMT, RING_OK>;
     constexpr bool Q8 = CF::Q8;
     constexpr int STAGES = CF::STAGES, EPI_WARPS = CF::EPI_WARPS, PARTS = CF::PARTS, SB = CF::STAGE;
     extern __shared__ uint8_t smem_raw[];
@@ -636,6 +737,12 @@ __global__ void __launch_bounds__(Cfg<KIND, FMT>::THREADS, 1)
         const uint32_t acc_empty0 = mapa_shared(smem_u32(&sm->acc_empty[0]), 0);
         const uint32_t acc_empty1 = mapa_shared(smem_u32(&sm->acc_empty[1]), 0);
         uint32_t acc = 0;
+        const ResidRing ring{pair, pairs, num_tiles, n_tiles, int(rank), quarter, part};
+        uint8_t* const ring_buf = stage + (warp - 2) * 2 * RING_SLOT;
+        if constexpr (CF::RING) {
+            resid_prefetch(g, ring, lane, 0, ring_buf);
+            resid_prefetch(g, ring, lane, 1, ring_buf + RING_SLOT);
+        }
         for (int tile = pair; tile < num_tiles; tile += pairs, ++acc) {
             const int b = acc & 1;
             const uint32_t aph = (acc >> 1) & 1;
@@ -656,11 +763,15 @@ __global__ void __launch_bounds__(Cfg<KIND, FMT>::THREADS, 1)
             __syncwarp();
             tc_fence_after();
             const uint32_t tacc = tmem + (uint32_t(quarter * 32) << 16) + b * BN;
-            epilogue_tile<KIND, PARTS>(g, tacc, m0, n0, quarter, lane, part, stage + (warp - 2) * 32 * 128, rsc, rr);
+            if constexpr (CF::RING)
+                epilogue_resid_ring(g, tacc, m0, n0, lane, ring, ring_buf, acc * RING_CHUNKS);
+            else
+                epilogue_tile<KIND, PARTS>(g, tacc, m0, n0, quarter, lane, part, stage + (warp - 2) * 32 * 128, rsc, rr);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster_relaxed(b ? acc_empty1 : acc_empty0);
         }
+        if constexpr (CF::RING) cp_async_wait_all();   // the prefetches past the last tile (or an abort)
     }
     tc_fence_before();
     cluster_sync();                                   // no CTA leaves while its pair may touch it
@@ -761,14 +872,15 @@ int device_sm_count() {
     return counts[dev];
 }
 
-template <int KIND, int FMT>
+template <int KIND, int FMT, bool RING_OK = true>
 static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
+    using CF = Cfg<KIND, FMT, RING_OK>;
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<KIND, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg<KIND, FMT>::SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<KIND, FMT, RING_OK>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, CF::SMEM_BYTES);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
@@ -800,8 +912,8 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
     const int pairs = tiles < max_pairs ? tiles : max_pairs;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(Cfg<KIND, FMT>::THREADS);
-    cfg.dynamicSmemBytes = Cfg<KIND, FMT>::SMEM_BYTES;
+    cfg.blockDim = dim3(CF::THREADS);
+    cfg.dynamicSmemBytes = CF::SMEM_BYTES;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -810,13 +922,15 @@ static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<KIND, FMT>, ma, mb, mq, md, a, err);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<KIND, FMT, RING_OK>, ma, mb, mq, md, a, err);
 }
 
 template <int KIND>
 static cudaError_t launch_kind(const GemmArgs& a, cudaStream_t stream, int* err) {
     if (a.Bq && a.Bs) return launch<KIND, FMT_KQ>(a, stream, err);
     if (a.Bq) return launch<KIND, FMT_Q8>(a, stream, err);
+    if constexpr (KIND == EPI_RESID)
+        if (a.K > RING_K_MAX) return launch<KIND, FMT_F16, false>(a, stream, err);
     return launch<KIND, FMT_F16>(a, stream, err);
 }
 
