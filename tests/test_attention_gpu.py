@@ -184,3 +184,50 @@ def test_attention_time_long(dev, S, N, L, cov, kernel, dense):
     tol = 4e-3 * scale + want.abs() * 2.0 ** -10
     bad = (got - want).abs() > tol
     assert not bad.any(), f"max err {(got - want).abs().max().item():.3e} at {bad.nonzero()[:4].tolist()}"
+
+
+@pytest.mark.parametrize("S,N,L,cov,rows,H", [(36, 32, 32, 0, 37, 3), (9, 8, 8, 0, 5, 3), (64, 60, 60, 0, 7, 12),
+                                              (33, 30, 30, 0, 11, 2), (1, 1, 1, 0, 3, 1), (48, 24, 20, 1, 5, 2),
+                                              (16, 16, 16, 0, 1, 1), (64, 32, 32, 1, 5, 3)])
+def test_attention_time_tc_two_problems_per_tile(dev, S, N, L, cov, rows, H):
+    """Rows of S <= 64 tokens run two (row, head) problems per 128-query score tile (their keys
+    side by side, each query's key set moved to its problem's block); the outputs equal the
+    one-problem-per-tile kernel's bit for bit, including an odd problem count (the last tile
+    holds one problem) and the covariate layout, and the float64 restatement within the
+    kernel tolerance."""
+    bs = 4
+    g = torch.Generator().manual_seed(S * 31 + N + cov + rows)
+    q = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
+    k = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
+    v = torch.randn(rows, H, S, 64, generator=g).half()
+    gate = torch.rand(rows, H, S, 64, generator=g).half()
+    valid = torch.rand(rows, N, generator=g) > 0.2
+    valid[:, 0] = True
+    role = torch.tensor([0, 1, 2, 2, 0, 1, 2] * ((rows + 6) // 7), dtype=torch.int8)[:rows]
+    words = (N + 31) // 32
+    bits = np.zeros((rows, words), np.uint32)
+    vn = valid.numpy()
+    for p in range(N):
+        bits[:, p // 32] |= vn[:, p].astype(np.uint32) << np.uint32(p % 32)
+    dq, dk, dv, dg = q.to(dev), k.to(dev), v.to(dev), gate.to(dev)
+    dbits = torch.from_numpy(bits.view(np.int32)).to(dev)
+    drole = role.to(dev)
+    outs = []
+    for kernel in (1, 4):
+        out = torch.full((rows * S, H * 64), float("nan"), device=dev, dtype=torch.float16)
+        err = C.c_int32(0)
+        rc = tb.lib().tsb_test_attention_time_ex(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(),
+                                                 out.data_ptr(), dbits.data_ptr(), drole.data_ptr(), rows, H, S, N, L,
+                                                 cov, bs, kernel, 0, None, C.byref(err))
+        assert rc == 0, (kernel, rc, err.value)
+        outs.append(out.cpu())
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    allowed = time_mask_torch(valid, role, N, L, S, cov, bs)
+    s = torch.einsum("rhqd,rhkd->rhqk", q.double(), k.double()) / 8.0
+    s = s.masked_fill(~allowed[:, None], float("-inf"))
+    want = (torch.einsum("rhqk,rhkd->rhqd", torch.softmax(s, dim=-1), v.double()) * gate.double())
+    want = want.permute(0, 2, 1, 3).reshape(rows * S, H * 64)
+    got = outs[0].double()
+    assert torch.isfinite(got).all()
+    scale = want.abs().reshape(rows, S, H, 64).amax(dim=(1, 3), keepdim=True).expand(rows, S, H, 64).reshape(rows * S, H * 64)
+    assert not ((got - want).abs() > 4e-3 * scale + want.abs() * 2.0 ** -10).any()

@@ -116,13 +116,36 @@ struct AttnBars {
     int abort;
 };
 
-template <int NK>
+template <int NK, int PK>
 struct AttnLayout {
-    static constexpr int KV_BYTES = NK * 128;
+    static constexpr int KV_BYTES = PK * NK * 128;       // the keys (or values) of the tile's problems
     static constexpr int STAGE_BYTES = 128 * 128;
     __host__ __device__ static constexpr int q_rows(int S) { return (S + 7) / 8 * 8; }
-    __host__ __device__ static constexpr int smem(int S) { return q_rows(S) * 128 + 2 * KV_BYTES + STAGE_BYTES + 1024 + 256; }
+    // Problem p's queries at row 64 p (the score MMA reads 128 rows; those past the last
+    // problem's fall in the K region).
+    __host__ __device__ static constexpr int q_bytes(int S) { return ((PK - 1) * 64 + q_rows(S)) * 128; }
+    __host__ __device__ static constexpr int smem(int S) { return q_bytes(S) + 2 * KV_BYTES + STAGE_BYTES + 1024 + 256; }
 };
+
+// Keys of the second problem of a packed tile sit NK positions up: the key set moves up by NK
+// bits (NK a multiple of 16, at most 64).
+template <int NK>
+__device__ __forceinline__ void shift_keys(uint32_t (&m)[4]) {
+    constexpr int WS = NK / 32, BS = NK % 32;
+    uint32_t o[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const uint32_t a = w - WS >= 0 ? m[w - WS] : 0u;
+        if constexpr (BS == 0) {
+            o[w] = a;
+        } else {
+            const uint32_t b = w - WS - 1 >= 0 ? m[w - WS - 1] : 0u;
+            o[w] = (a << BS) | (b >> (32 - BS));
+        }
+    }
+#pragma unroll
+    for (int w = 0; w < 4; ++w) m[w] = o[w];
+}
 
 __device__ __forceinline__ bool at_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -171,24 +194,29 @@ __device__ __forceinline__ float exp2_ftz(float x) {
     return y;
 }
 
-template <int NK>
+template <int NK, int PK>
 __global__ void __launch_bounds__(AT_THREADS, 4)
     attn_time_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const __half* __restrict__ gate,
                         __half* __restrict__ out, int rows, int H, const MaskMeta mm, int* err) {
-    using Lay = AttnLayout<NK>;
+    static_assert(PK == 1 || (PK == 2 && NK <= 64), "two problems per tile need NK <= 64");
+    using Lay = AttnLayout<NK, PK>;
     extern __shared__ uint8_t smem_raw[];
     const int S = mm.S, D = H * 64;
     const int QR = Lay::q_rows(S);
     uint8_t* qbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* kbuf = qbuf + QR * 128;
+    uint8_t* kbuf = qbuf + Lay::q_bytes(S);
     uint8_t* vbuf = kbuf + Lay::KV_BYTES;
     uint8_t* obuf = vbuf + Lay::KV_BYTES;
     AttnBars* bars = reinterpret_cast<AttnBars*>(obuf + Lay::STAGE_BYTES);
     volatile int* abort = &bars->abort;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, t = threadIdx.x;
     const int num = rows * H;
+    const int units = (num + PK - 1) / PK;               // tiles of PK problems
     const bool ctl = threadIdx.x == 0;
+    // This thread's problem of the tile (queries of problem p at TMEM lanes 64 p ..) and query.
+    const int pb = PK == 2 ? t >> 6 : 0;
+    const int qi = t - 64 * pb;
 
     if (ctl) {
         mbar_init(&bars->full_qk, 1); mbar_init(&bars->full_v, 1); mbar_init(&bars->s_full, 1);
@@ -205,24 +233,33 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
     const uint32_t tO = tS + AT_O_COL;
     const uint32_t lane_base = uint32_t(warp * 32) << 16;
 
-    auto issue_qk = [&](int prob) {
-        mbar_arrive_expect_tx(&bars->full_qk, QR * 128 + Lay::KV_BYTES);
-        tma_load_3d(qbuf, &map_q, &bars->full_qk, 0, 0, prob);
-        tma_load_3d(kbuf, &map_k, &bars->full_qk, 0, 0, prob);
+    // A tile's second problem past the last one loads the first one's tiles again (finite
+    // values for the P V product, whose probabilities there are zero); its rows store nothing.
+    auto tile_prob = [&](int unit, int p) { const int pr = unit * PK + p; return pr < num ? pr : unit * PK; };
+    auto issue_qk = [&](int unit) {
+        mbar_arrive_expect_tx(&bars->full_qk, PK * (QR * 128 + NK * 128));
+#pragma unroll
+        for (int p = 0; p < PK; ++p) {
+            tma_load_3d(qbuf + p * 64 * 128, &map_q, &bars->full_qk, 0, 0, tile_prob(unit, p));
+            tma_load_3d(kbuf + p * NK * 128, &map_k, &bars->full_qk, 0, 0, tile_prob(unit, p));
+        }
     };
-    auto issue_v = [&](int prob) {
-        mbar_arrive_expect_tx(&bars->full_v, Lay::KV_BYTES);
-        tma_load_3d(vbuf, &map_v, &bars->full_v, 0, 0, prob);
+    auto issue_v = [&](int unit) {
+        mbar_arrive_expect_tx(&bars->full_v, PK * NK * 128);
+#pragma unroll
+        for (int p = 0; p < PK; ++p) tma_load_3d(vbuf + p * NK * 128, &map_v, &bars->full_v, 0, 0, tile_prob(unit, p));
     };
-    if (ctl && int(blockIdx.x) < num) { issue_qk(blockIdx.x); issue_v(blockIdx.x); }
+    if (ctl && int(blockIdx.x) < units) { issue_qk(blockIdx.x); issue_v(blockIdx.x); }
 
     // logit scale 1/sqrt(64) folded with log2(e) for exp2
     constexpr float kScaleLog2e = 0.125f * 1.4426950408889634f;
     int i = 0;
-    for (int prob = blockIdx.x; prob < num; prob += gridDim.x, ++i) {
+    for (int unit = blockIdx.x; unit < units; unit += gridDim.x, ++i) {
         const uint32_t ph = i & 1;
-        const int next = prob + gridDim.x;
-        const int r = prob / H, h = prob % H;
+        const int next = unit + gridDim.x;
+        const int prob = unit * PK + pb;                // this thread's problem
+        const bool has = prob < num;
+        const int r = has ? prob / H : 0, h = has ? prob % H : 0;
         if (warp == 0) {
             // S = Q K^T once Q and K are resident and every warp has read the previous O.
             int ok = 1;
@@ -232,7 +269,7 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
                 if (ok) {
                     tc_fence_after();
                     const uint64_t dq = smem_desc_sw128(smem_u32(qbuf)), dk = smem_desc_sw128(smem_u32(kbuf));
-                    const uint32_t id1 = idesc_f16(128, NK);
+                    const uint32_t id1 = idesc_f16(128, PK * NK);
 #pragma unroll
                     for (int k = 0; k < 4; ++k) mma_f16(tS, dq + uint64_t(2 * k), dk + uint64_t(2 * k), id1, k > 0);
                     mma_commit(&bars->s_full);
@@ -240,19 +277,31 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
             }
             if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         }
-        const bool live = t < S;
+        const bool live = has && qi < S;
         uint32_t allowed[4];
-        key_set(mm, r, t, live, allowed);
+        key_set(mm, r, qi, live, allowed);
+        if constexpr (PK == 2) {
+            if (pb) shift_keys<NK>(allowed);
+        }
         // Highest key any query of this warp attends: key chunks above it are skipped
-        // (written as zero probabilities), which halves the work of causal rows.
+        // (written as zero probabilities), which halves the work of causal rows. In a packed
+        // tile the chunks below the warp's lowest key (the other problem's) are skipped too.
         int hi = -1;
 #pragma unroll
         for (int w = 3; w >= 0; --w)
             if (hi < 0 && allowed[w]) hi = w * 32 + 31 - __clz(allowed[w]);
         const int kmax = __reduce_max_sync(0xffffffffu, hi + 1) - 1;   // -1: no live query in this warp
+        int kmin = 0;
+        if constexpr (PK == 2) {
+            int lo = 128;
+#pragma unroll
+            for (int w = 0; w < 4; ++w)
+                if (lo == 128 && allowed[w]) lo = w * 32 + __ffs(int(allowed[w])) - 1;
+            kmin = int(__reduce_min_sync(0xffffffffu, unsigned(lo)));
+        }
         if (!warp_wait(&bars->s_full, ph, abort, err)) break;
         tc_fence_after();
-        if (ctl && next < num) issue_qk(next);         // Q and K are free once S is complete
+        if (ctl && next < units) issue_qk(next);       // Q and K are free once S is complete
         float sum = 0.f;
         if (kmax >= 0) {
             // Pass 1: the row maximum over the query's keys (eight partial maxima).
@@ -260,8 +309,9 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
 #pragma unroll
             for (int j = 0; j < 8; ++j) mxj[j] = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < NK / 16; ++c) {
+            for (int c = 0; c < PK * NK / 16; ++c) {
                 if (c * 16 > kmax) break;
+                if (PK == 2 && c * 16 + 15 < kmin) continue;
                 uint32_t sc[16];
                 tmem_ld16(tS + lane_base + c * 16, sc);
                 tmem_ld_wait();
@@ -279,9 +329,9 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
 #pragma unroll
             for (int j = 0; j < 8; ++j) sj[j] = 0.f;
 #pragma unroll
-            for (int c = 0; c < NK / 16; ++c) {
+            for (int c = 0; c < PK * NK / 16; ++c) {
                 uint32_t pk[8];
-                if (c * 16 <= kmax) {
+                if (c * 16 <= kmax && (PK == 1 || c * 16 + 15 >= kmin)) {
                     uint32_t sc[16];
                     tmem_ld16(tS + lane_base + c * 16, sc);
                     tmem_ld_wait();
@@ -316,7 +366,7 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
                     const uint32_t sv = smem_u32(vbuf);
                     const uint32_t id2 = idesc_f16_bmn(128, 64);
 #pragma unroll
-                    for (int kk = 0; kk < NK / 16; ++kk)
+                    for (int kk = 0; kk < PK * NK / 16; ++kk)
                         mma_f16_ts(tO, tS + kk * 8, smem_desc_sw128(sv + kk * 16 * 128), id2, kk > 0);
                     mma_commit(&bars->o_full);
                 }
@@ -325,14 +375,14 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
         }
         // gate row of this query, fetched while O = P V runs
         uint4 gv[8];
-        const __half* g = (gate && live) ? gate + ((int64_t(r) * H + h) * S + t) * 64 : nullptr;
+        const __half* g = (gate && live) ? gate + ((int64_t(r) * H + h) * S + qi) * 64 : nullptr;
         if (g) {
 #pragma unroll
             for (int c = 0; c < 8; ++c) gv[c] = *reinterpret_cast<const uint4*>(g + c * 8);
         }
         if (!warp_wait(&bars->o_full, ph, abort, err)) break;
         tc_fence_after();
-        if (ctl && next < num) issue_v(next);          // V is free once O is complete
+        if (ctl && next < units) issue_v(next);        // V is free once O is complete
         // O * (1/sum) * gate in f16, staged row-wise and stored eight threads per 128-byte
         // output row. The TMEM is released as soon as O's second half is in registers.
         const float inv = live ? 1.0f / sum : 0.f;
@@ -372,11 +422,16 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
         if (kmax < 0) continue;
         stage(o, 1);
         __syncwarp();
+        // A warp's rows all belong to one problem of the tile (64 lanes per problem).
+        const int wpb = PK == 2 ? warp >> 1 : 0;
+        const int wprob = unit * PK + wpb;
+        const int wr = wprob / H, wh = wprob % H;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int row = warp * 32 + j * 4 + (lane >> 3), chunk = lane & 7;
-            if (row < S)
-                *reinterpret_cast<uint4*>(out + (int64_t(r) * S + row) * D + h * 64 + chunk * 8) =
+            const int rq = row - 64 * wpb;
+            if (rq < S && wprob < num)
+                *reinterpret_cast<uint4*>(out + (int64_t(wr) * S + rq) * D + wh * 64 + chunk * 8) =
                     *reinterpret_cast<const uint4*>(obuf + row * 128 + ((chunk ^ (row & 7)) << 4));
         }
         __syncwarp();
@@ -387,17 +442,17 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
     if (warp == 0) tmem_dealloc(bars->tmem, AT_TMEM_COLS);
 }
 
-template <int NK>
+template <int NK, int PK>
 cudaError_t launch_attn_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
                            int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
-    using Lay = AttnLayout<NK>;
+    using Lay = AttnLayout<NK, PK>;
     const int smem = Lay::smem(mm.S);
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
         // The largest request of this key count (S = NK) so later calls need no update.
-        cudaError_t e = cudaFuncSetAttribute(attn_time_tc_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(attn_time_tc_kernel<NK, PK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Lay::smem(NK));
         if (e != cudaSuccess) return e;
         configured[dev] = true;
@@ -412,8 +467,9 @@ cudaError_t launch_attn_tc(const __half* q, const __half* k, const __half* v, co
     if (per_sm > 4) per_sm = 4;
     if (per_sm < 1) per_sm = 1;
     int grid = device_sm_count() * per_sm;
-    if (int64_t(grid) > planes) grid = int(planes);
-    attn_time_tc_kernel<NK><<<grid, AT_THREADS, smem, stream>>>(mq, mk, mv, gate, out, rows, H, mm, err);
+    const int64_t units = (planes + PK - 1) / PK;
+    if (int64_t(grid) > units) grid = int(units);
+    attn_time_tc_kernel<NK, PK><<<grid, AT_THREADS, smem, stream>>>(mq, mk, mv, gate, out, rows, H, mm, err);
     return cudaGetLastError();
 }
 
@@ -1150,19 +1206,24 @@ constexpr size_t simt_smem() { return (SIMT_WARPS * 2 * SIMT_MAX_KEYS + SIMT_WAR
 }  // namespace
 
 cudaError_t attention_time_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
-                              int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
+                              int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err, int pack) {
     if (rows <= 0) return cudaSuccess;
     if (mm.S <= 0 || mm.S > 128) return cudaErrorInvalidValue;
     const int nk = (mm.S + 15) / 16 * 16;
+    const bool two = pack && mm.S <= 64;
     switch (nk) {
-        case 16: return launch_attn_tc<16>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 32: return launch_attn_tc<32>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 48: return launch_attn_tc<48>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 64: return launch_attn_tc<64>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 80: return launch_attn_tc<80>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 96: return launch_attn_tc<96>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 112: return launch_attn_tc<112>(q, k, v, gate, out, rows, H, mm, stream, err);
-        case 128: return launch_attn_tc<128>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 16: return two ? launch_attn_tc<16, 2>(q, k, v, gate, out, rows, H, mm, stream, err)
+                            : launch_attn_tc<16, 1>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 32: return two ? launch_attn_tc<32, 2>(q, k, v, gate, out, rows, H, mm, stream, err)
+                            : launch_attn_tc<32, 1>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 48: return two ? launch_attn_tc<48, 2>(q, k, v, gate, out, rows, H, mm, stream, err)
+                            : launch_attn_tc<48, 1>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 64: return two ? launch_attn_tc<64, 2>(q, k, v, gate, out, rows, H, mm, stream, err)
+                            : launch_attn_tc<64, 1>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 80: return launch_attn_tc<80, 1>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 96: return launch_attn_tc<96, 1>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 112: return launch_attn_tc<112, 1>(q, k, v, gate, out, rows, H, mm, stream, err);
+        case 128: return launch_attn_tc<128, 1>(q, k, v, gate, out, rows, H, mm, stream, err);
     }
     return cudaErrorInvalidValue;
 }

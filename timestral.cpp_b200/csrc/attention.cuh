@@ -24,9 +24,10 @@ struct MaskMeta {
 };
 
 // q/k/v/gate: head-major [rows][H][S][hd]; out: token-major [rows*S][H*hd] (gated).
-// f16 tensor-core kernel, hd = 64, S <= 128.
+// f16 tensor-core kernel, hd = 64, S <= 128. pack != 0: rows of S <= 64 tokens run two
+// (row, head) problems per 128-query tile (same results as one per tile).
 cudaError_t attention_time_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
-                              int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err);
+                              int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err, int pack = 1);
 
 // Same for S > 128 (any S): key/value tiles of 64 tokens, queries in tiles of 128.
 cudaError_t attention_time_tc_long(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
