@@ -196,8 +196,9 @@ TIMESTRAL_API int tsb_test_attention_time(const void* q, const void* k, const vo
  * covariate layout (cov != 0: S = 2N, role [rows] 0 target / 1 past / 2 known, decode blocks
  * of block_size patches). kernel: 0 the engine's choice, 1 the S <= 128 tensor-core kernel
  * (two problems per score tile when S <= 64), 2 the tiled tensor-core kernel (any S), 3 the
- * CUDA-core kernel, 4 the S <= 128 tensor-core kernel with one problem per tile. Same layouts
- * as above.
+ * CUDA-core kernel (the tiled one for S > 128), 4 the S <= 128 tensor-core kernel with one
+ * problem per tile, 5 the CUDA-core kernel with one warp per query, 6 the tiled CUDA-core
+ * kernel (kernels 3, 5 and 6 give the same bits). Same layouts as above.
  * repeat > 0 with ms non-NULL: after the checked launch, *ms = the average device time of
  * `repeat` more launches. */
 TIMESTRAL_API int tsb_test_attention_time_ex(const void* q, const void* k, const void* v, const void* gate, void* out,

@@ -231,3 +231,40 @@ def test_attention_time_tc_two_problems_per_tile(dev, S, N, L, cov, rows, H):
     assert torch.isfinite(got).all()
     scale = want.abs().reshape(rows, S, H, 64).amax(dim=(1, 3), keepdim=True).expand(rows, S, H, 64).reshape(rows * S, H * 64)
     assert not ((got - want).abs() > 4e-3 * scale + want.abs() * 2.0 ** -10).any()
+
+
+@pytest.mark.parametrize("S,N,L,cov,rows,H", [(18, 16, 16, 0, 3, 2), (72, 64, 64, 0, 5, 3), (200, 190, 190, 0, 3, 2),
+                                              (1056, 1024, 1024, 0, 2, 2), (140, 70, 64, 1, 5, 2),
+                                              (2112, 1056, 1024, 1, 2, 1), (33, 33, 33, 0, 4, 1)])
+def test_attention_time_simt_tiled_same_bits(dev, S, N, L, cov, rows, H):
+    """The tiled CUDA-core time attention (key and value tiles in shared memory, 16 queries per
+    block) against the warp-per-query kernel: the reference's operation order in both, so the
+    outputs are the same bits, with and without the covariate layout, up to 2,112 tokens."""
+    bs = 32
+    g = torch.Generator().manual_seed(S * 13 + N + cov)
+    q = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
+    k = (torch.randn(rows, H, S, 64, generator=g) * 2).half()
+    v = torch.randn(rows, H, S, 64, generator=g).half()
+    gate = torch.rand(rows, H, S, 64, generator=g).half()
+    valid = torch.rand(rows, N, generator=g) > 0.2
+    valid[:, 0] = True
+    role = torch.tensor([0, 1, 2, 2, 0][:rows], dtype=torch.int8)
+    words = (N + 31) // 32
+    bits = np.zeros((rows, words), np.uint32)
+    vn = valid.numpy()
+    for p in range(N):
+        bits[:, p // 32] |= vn[:, p].astype(np.uint32) << np.uint32(p % 32)
+    dq, dk, dv, dg = q.to(dev), k.to(dev), v.to(dev), gate.to(dev)
+    dbits = torch.from_numpy(bits.view(np.int32)).to(dev)
+    drole = role.to(dev)
+    outs = []
+    for kernel in (5, 6):
+        out = torch.full((rows * S, H * 64), float("nan"), device=dev, dtype=torch.float16)
+        err = C.c_int32(0)
+        rc = tb.lib().tsb_test_attention_time_ex(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(),
+                                                 out.data_ptr(), dbits.data_ptr(), drole.data_ptr(), rows, H, S, N, L,
+                                                 cov, bs, kernel, 0, None, C.byref(err))
+        assert rc == 0, (kernel, rc, err.value)
+        outs.append(out.cpu())
+    assert torch.isfinite(outs[0].float()).all()
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))

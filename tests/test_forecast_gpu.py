@@ -139,6 +139,16 @@ def test_209m_f32_cfg1():
     check_f32(m.forecast(x, 64), o.forecast(x, 64))
 
 
+def test_209m_f32_published_shape():
+    """The reference's published benchmark shape (the measurement contract of its
+    docs/benchmarks.md): F32 weights, B=1, V=1, context 32768, horizon 1024 (S = 1056, one
+    32-patch block), the dyadic-v1 input, symmetric averaging and clipping on. The CUDA-core
+    F32 path (float64 q.k dots over 1,056 keys) against the oracle at the F32 tolerance."""
+    m, o = models(sy.spec_209m(), "f32")
+    x = sy.series_dyadic(32768)
+    check_f32(m.forecast(x, 1024), o.forecast(x, 1024))
+
+
 # ---- F16 weights: tensor-core path --------------------------------------------------------
 @pytest.mark.parametrize("B,V,T,H", [(3, 1, 256, 64), (2, 3, 200, 40), (2, 1, 256, 1100), (1, 2, 128, 1060)])
 def test_small_f16(B, V, T, H):

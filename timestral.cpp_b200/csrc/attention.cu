@@ -1025,6 +1025,151 @@ __global__ void __launch_bounds__(SIMT_WARPS * 32)
     }
 }
 
+// The same computation for long rows (head_dim 64), tiled through shared memory: block =
+// (row, head, TS_Q consecutive queries), 256 threads. The per-query warp kernel above reads
+// every key row with per-lane strided loads and sums each value column behind a global load
+// per key; here key and value tiles of TS_KT rows are staged once per block (keys as float64,
+// values as float) and shared by its queries, and each thread runs four independent chains.
+// Every operation and its order per query is the reference's, as above: float64 q.k dots over
+// d = 0..63, the logit as float(s) * float(1/8), the maximum over the query's computed keys,
+// ATen exp for keys below the last full eight-key chunk and libm exp after it, eight strided
+// lane sums in key order + the fixed tree + the tail, one reciprocal, and per output column a
+// float FMA chain over the keys in order (masked keys contribute p = 0, as there).
+constexpr int TS_Q = 16;
+constexpr int TS_KT = 64;
+constexpr int TS_THREADS = 256;
+constexpr int TS_KPAD = 65;                // float64 key rows padded: conflict-free column reads
+
+constexpr size_t simt_tiled_smem(int S) {
+    return size_t(TS_Q) * 64 * sizeof(double) + size_t(TS_KT) * TS_KPAD * sizeof(double) +
+           size_t(TS_Q) * S * sizeof(float) + TS_Q * sizeof(float);
+}
+
+template <class T>
+__global__ void __launch_bounds__(TS_THREADS)
+    attn_time_simt_tiled_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                                const T* __restrict__ gate, T* __restrict__ out, int rows, int H, const MaskMeta mm) {
+    extern __shared__ double ts_sh[];
+    constexpr int HD = 64;
+    double* qs = ts_sh;                                   // [TS_Q][64]
+    double* ks = qs + TS_Q * HD;                          // [TS_KT][TS_KPAD]; values as float [TS_KT][64]
+    float* vs = reinterpret_cast<float*>(ks);
+    const int S = mm.S;
+    float* lg = reinterpret_cast<float*>(ks + TS_KT * TS_KPAD);   // [TS_Q][S]: logits, then probabilities
+    float* recip = lg + TS_Q * S;                                 // [TS_Q]
+    const int tid = threadIdx.x;
+    const int qblocks = (S + TS_Q - 1) / TS_Q;
+    const int64_t b = blockIdx.x;
+    const int r = int(b / (int64_t(H) * qblocks)), h = int((b / qblocks) % H), t0 = int(b % qblocks) * TS_Q;
+    if (r >= rows) return;                                        // uniform across the block
+    const int64_t plane = (int64_t(r) * H + h) * S;
+    const int last = min(S, t0 + TS_Q) - 1;
+    const int kend = time_keys(mm, last);                         // keys of the block's last query (the most)
+
+    for (int i = tid; i < TS_Q * HD; i += TS_THREADS) {
+        const int qi = i / HD, d = i % HD;
+        qs[i] = t0 + qi < S ? double(ld(q + (plane + t0 + qi) * HD + d)) : 0.0;
+    }
+    // Logits: thread (kj = tid % 64, queries 4 g .. 4 g + 3 with g = tid / 64).
+    const int kj = tid & (TS_KT - 1), g = tid >> 6;
+    int kq[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) kq[u] = t0 + 4 * g + u < S ? time_keys(mm, t0 + 4 * g + u) : 0;
+    for (int k0 = 0; k0 < kend; k0 += TS_KT) {
+        __syncthreads();                                          // the previous tile is consumed
+        for (int i = tid; i < TS_KT * HD; i += TS_THREADS) {
+            const int jj = i / HD, d = i % HD;
+            ks[jj * TS_KPAD + d] = k0 + jj < S ? double(ld(k + (plane + k0 + jj) * HD + d)) : 0.0;
+        }
+        __syncthreads();
+        const int j = k0 + kj;
+        double acc[4] = {0.0, 0.0, 0.0, 0.0};
+        const double* kr = ks + kj * TS_KPAD;
+        const double* q0 = qs + (4 * g) * HD;
+#pragma unroll 8
+        for (int d = 0; d < HD; ++d) {
+            const double kd = kr[d];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) acc[u] = __fma_rn(q0[u * HD + d], kd, acc[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int t = t0 + 4 * g + u;
+            if (j < kq[u])
+                lg[(4 * g + u) * S + j] = time_allowed(mm, r, t, j) ? __fmul_rn(float(acc[u]), float(1.0 / sqrt(double(HD))))
+                                                                    : -INFINITY;
+        }
+    }
+    __syncthreads();
+    // Softmax of each query: 16 threads per query for the maximum and the exponentials.
+    {
+        const int qi = tid >> 4, sub = tid & 15;
+        const int t = t0 + qi, kt = t < S ? time_keys(mm, t) : 0;
+        float* row = lg + qi * S;
+        float mx = -INFINITY;
+        for (int j = sub; j < kt; j += 16) mx = fmaxf(mx, row[j]);
+#pragma unroll
+        for (int o = 8; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const int end = kt / 8 * 8;
+        for (int j = sub; j < kt; j += 16) {
+            const float x = __fsub_rn(row[j], mx);
+            row[j] = j < end ? attention_exp(x) : float(exp(double(x)));
+        }
+    }
+    __syncthreads();
+    // Sums: eight lane chains per query (keys j = l mod 8 below the last full chunk, in key
+    // order), the fixed tree, then the tail in order.
+    if (tid < TS_Q * 8) {
+        const int qi = tid >> 3, l = tid & 7;
+        const int t = t0 + qi, kt = t < S ? time_keys(mm, t) : 0;
+        const int end = kt / 8 * 8;
+        const float* row = lg + qi * S;
+        float part = 0.f;
+        for (int j = l; j < end; j += 8) part = __fadd_rn(part, row[j]);
+        const int base = (tid & 31) & ~7;
+        float sv[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) sv[m] = __shfl_sync(0xffffffffu, part, base + m);
+        if (l == 0 && t < S) {
+            const float a0 = __fadd_rn(sv[0], sv[4]), a1 = __fadd_rn(sv[1], sv[5]);
+            const float a2 = __fadd_rn(sv[2], sv[6]), a3 = __fadd_rn(sv[3], sv[7]);
+            float sum = __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+            for (int j = end; j < kt; ++j) sum = __fadd_rn(sum, row[j]);
+            recip[qi] = __fdiv_rn(1.0f, sum);
+        }
+    }
+    // Values: thread (column d = tid % 64, queries 4 g .. 4 g + 3): float FMA chains over the
+    // keys in order, value tiles staged as float.
+    const int d = tid & (HD - 1);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < kend; k0 += TS_KT) {
+        __syncthreads();                                          // logits / sums / previous tile done
+        for (int i = tid; i < TS_KT * HD; i += TS_THREADS) {
+            const int jj = i / HD, dd = i % HD;
+            vs[i] = k0 + jj < S ? ld(v + (plane + k0 + jj) * HD + dd) : 0.f;
+        }
+        __syncthreads();
+        const int n = min(TS_KT, kend - k0);
+        const float* pr = lg + (4 * g) * S + k0;
+        for (int jj = 0; jj < n; ++jj) {
+            const float vv = vs[jj * HD + d];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (k0 + jj < kq[u]) acc[u] = __fmaf_rn(pr[u * S + jj], vv, acc[u]);   // uniform per warp
+        }
+    }
+    __syncthreads();
+    const int D = H * HD;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int qi = 4 * g + u, t = t0 + qi;
+        if (t >= S) continue;
+        float val = __fmul_rn(acc[u], recip[qi]);
+        if (gate) val = __fmul_rn(val, ld(gate + (plane + t) * HD + d));
+        st(out + (int64_t(r) * S + t) * D + h * HD + d, val);
+    }
+}
+
 // Variate axis: block = (row, slot, head) with 4 warps over heads; keys are the rows of the
 // query row's series. Sequence index of a key = its row index within the forecast pass.
 template <class T>
@@ -1229,10 +1374,33 @@ cudaError_t attention_time_tc(const __half* q, const __half* k, const __half* v,
 }
 
 template <class T>
+cudaError_t attention_time_simt_tiled(const T* q, const T* k, const T* v, const T* gate, T* out, int rows, int H,
+                                      const MaskMeta& mm, cudaStream_t stream) {
+    const size_t smem = simt_tiled_smem(mm.S);
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        // the largest row this kernel takes, so later calls need no update
+        cudaError_t e = cudaFuncSetAttribute(attn_time_simt_tiled_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(simt_tiled_smem(SIMT_MAX_KEYS)));
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    const int64_t blocks = int64_t(rows) * H * ((mm.S + TS_Q - 1) / TS_Q);
+    attn_time_simt_tiled_kernel<T><<<unsigned(blocks), TS_THREADS, smem, stream>>>(q, k, v, gate, out, rows, H, mm);
+    return cudaGetLastError();
+}
+
+template <class T>
 cudaError_t attention_time_simt(const T* q, const T* k, const T* v, const T* gate, T* out, int rows, int H, int hd,
-                                const MaskMeta& mm, cudaStream_t stream) {
+                                const MaskMeta& mm, cudaStream_t stream, int tiled) {
     if (rows <= 0) return cudaSuccess;
     if (mm.S > SIMT_MAX_KEYS || hd > 256) return cudaErrorInvalidValue;
+    // Long rows of head_dim 64: the tiled kernel (same bits).
+    if (hd == 64 && (tiled > 0 || (tiled < 0 && mm.S > 128)))
+        return attention_time_simt_tiled(q, k, v, gate, out, rows, H, mm, stream);
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1291,9 +1459,9 @@ cudaError_t attention_variate_fast(const __half* q, const __half* k, const __hal
 }
 
 template cudaError_t attention_time_simt<float>(const float*, const float*, const float*, const float*, float*, int, int, int,
-                                                const MaskMeta&, cudaStream_t);
+                                                const MaskMeta&, cudaStream_t, int);
 template cudaError_t attention_time_simt<__half>(const __half*, const __half*, const __half*, const __half*, __half*, int,
-                                                 int, int, const MaskMeta&, cudaStream_t);
+                                                 int, int, const MaskMeta&, cudaStream_t, int);
 template cudaError_t attention_variate_simt<float>(const float*, const float*, const float*, const float*, float*, int, int,
                                                    int, const MaskMeta&, cudaStream_t);
 template cudaError_t attention_variate_simt<__half>(const __half*, const __half*, const __half*, const __half*, __half*,

@@ -39,10 +39,12 @@ constexpr int kSimtMaxKeys = 2176;
 // CUDA-core kernels with the reference's operation order (float64 q.k dots, ATen exp for
 // full eight-lane chunks, libm exp for the tail, eight-lane sums, value FMA chain, one
 // reciprocal multiply). T = float (F32 path) or __half (tensor-core path inputs).
-// gate may be null (no sdpa_sigmoid gate); out is T-typed token-major.
+// gate may be null (no sdpa_sigmoid gate); out is T-typed token-major. tiled: -1 the tiled
+// kernel for rows of more than 128 tokens at head_dim 64, 1 always at head_dim 64, 0 never
+// (the two kernels give the same bits).
 template <class T>
 cudaError_t attention_time_simt(const T* q, const T* k, const T* v, const T* gate, T* out, int rows, int H, int hd,
-                                const MaskMeta& mm, cudaStream_t stream);
+                                const MaskMeta& mm, cudaStream_t stream, int tiled = -1);
 // Variate-axis attention of the tensor-core path: groups of G <= 64 consecutive rows (one
 // series), f16 head-major q/k/v/gate, head_dim 64, out token-major f16.
 cudaError_t attention_variate_fast(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,

@@ -79,7 +79,7 @@ extern "C" TIMESTRAL_API int tsb_test_attention_time_ex(const void* q, const voi
                                                         int32_t repeat, float* ms, int32_t* dev_error) {
     using namespace tsb;
     if (!q || !k || !v || !out || !key_valid || rows <= 0 || H <= 0 || S <= 0 || N <= 0 || N > S || L <= 0 || L > N ||
-        (cov && (!role || block_size <= 0 || S != 2 * N)) || kernel < 0 || kernel > 4 || ((kernel == 1 || kernel == 4) && S > 128))
+        (cov && (!role || block_size <= 0 || S != 2 * N)) || kernel < 0 || kernel > 6 || ((kernel == 1 || kernel == 4) && S > 128))
         return TSB_ERR_ARG;
     MaskMeta mm;
     mm.key_valid = key_valid; mm.kv_words = (N + 31) / 32; mm.N = N; mm.L = L; mm.S = S;
@@ -95,6 +95,8 @@ extern "C" TIMESTRAL_API int tsb_test_attention_time_ex(const void* q, const voi
         return kernel == 1   ? attention_time_tc(hq, hk, hv, hg, ho, rows, H, mm, 0, derr)
                : kernel == 4 ? attention_time_tc(hq, hk, hv, hg, ho, rows, H, mm, 0, derr, 0)
                : kernel == 2 ? attention_time_tc_long(hq, hk, hv, hg, ho, rows, H, mm, 0, derr)
+               : kernel == 5 ? attention_time_simt<__half>(hq, hk, hv, hg, ho, rows, H, 64, mm, 0, 0)
+               : kernel == 6 ? attention_time_simt<__half>(hq, hk, hv, hg, ho, rows, H, 64, mm, 0, 1)
                              : attention_time_simt<__half>(hq, hk, hv, hg, ho, rows, H, 64, mm, 0);
     };
     cudaError_t ce = launch();

@@ -382,6 +382,15 @@ def series_sine(T: int, seed: int = 0):
     return (np.sin(2 * np.pi * t / 24) + 0.1 * rng.standard_normal(T)).astype(np.float32)[None, None, :]
 
 
+def series_dyadic(T: int, V: int = 1):
+    """The reference benchmark's input (named dyadic-v1 there): x[v, t] = (((17 t + 13 v) mod
+    257) - 128) / 64, exact in f32, no missing values; shape [1, V, T]. Its sum is -8.5625 at
+    T = 32768 and -3.234375 at T = 512 (V = 1), the input checksums the reference reports."""
+    t = np.arange(T, dtype=np.int64)[None, :]
+    v = np.arange(V, dtype=np.int64)[:, None]
+    return ((((17 * t + 13 * v) % 257) - 128) / 64.0).astype(np.float32)[None]
+
+
 def series_random_walk(B: int, T: int, nan_frac: float = 0.05, seed0: int = 0):
     """Gaussian random walk (step N(0,1), seed = i) plus a level offset U(-100, 100), with
     a fraction of context steps set to NaN; shape [B,1,T]."""
