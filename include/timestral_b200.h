@@ -225,6 +225,12 @@ TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, vo
 TIMESTRAL_API int tsb_test_attention_variate(const void* q, const void* k, const void* v, const void* gate, void* out,
                                              const uint32_t* key_valid, const int8_t* role, int32_t rows, int32_t H,
                                              int32_t S, int32_t N, int32_t G);
+/* CUDA-core GEMM of the F32 path, out[M][N] f32 = A[M][K] W[N][K]^T (device pointers,
+ * synchronized), with the per-output order `order` (0: 192-wide K panels in K order, 1: one
+ * FMA chain, 2: float64); tiled != 0 lets large panel-order launches run the 64 x 128 tile
+ * kernel (same bits as the 64 x 64 one). */
+TIMESTRAL_API int tsb_test_simt_gemm(const float* A, const float* W, int32_t M, int32_t N, int32_t K, int32_t order,
+                                     int32_t tiled, float* out);
 /* The refine step of one decode block with its float64 scratch from cudaMalloc (as the
  * forecast's workspace provides it), on the current device, synchronized; arguments as
  * tsb_refine_static (patches >= 2, d_role may be NULL). */

@@ -1077,6 +1077,110 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtGemm g) {
     }
 }
 
+// The same per-output order (ORDER_PANEL192) for large unconditional launches: a 64 x 128
+// block tile, 256 threads of 4 x 8 outputs each, 16-byte tile loads, and the 16-deep K steps
+// unrolled (panel boundaries, every 192 = 12 x 16 of K, fall between steps). Each output
+// still accumulates each 192-wide panel in K order with single-rounding FMAs and adds the
+// panel sums in order, so the result is simt_gemm_kernel<ORDER_PANEL192>'s bit for bit.
+// Requires K % 16 == 0 and 16-byte aligned A and W rows.
+constexpr int GB_M = 64, GB_N = 128, GB_K = 16;
+
+__global__ void __launch_bounds__(256, 2) simt_gemm_tiled_kernel(const SimtGemm g) {
+    // Two shared-memory stages: the next K step's tiles are read into registers while the
+    // current one is multiplied, then stored into the other stage (one barrier per step).
+    __shared__ __align__(16) float As[2][GB_K][GB_M + 4];
+    __shared__ __align__(16) float Ws[2][GB_K][GB_N + 4];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const int m0 = int(blockIdx.y) * GB_M, n0 = int(blockIdx.x) * GB_N;
+    const int K = g.K;
+    const bool panels = K >= 192;
+    float sum[4][8], pan[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { sum[i][j] = 0.f; pan[i][j] = 0.f; }
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int ar = threadIdx.x >> 2, kq = (threadIdx.x & 3) * 4;
+    const bool a_ok = m0 + ar < g.M;
+    const float* a_src = g.A + int64_t(m0 + ar) * g.lda + kq;
+    const float* w_src[2];
+    bool w_ok[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int wr = (threadIdx.x + h * 256) >> 2;
+        w_ok[h] = n0 + wr < g.N;
+        w_src[h] = g.W + int64_t(n0 + wr) * K + kq;
+    }
+    float4 ra, rw[2];
+    auto fetch = [&](int k0) {
+        ra = a_ok ? *reinterpret_cast<const float4*>(a_src + k0) : zero;
+        if (g.round_a_f16) {
+            ra.x = __half2float(__float2half_rn(ra.x)); ra.y = __half2float(__float2half_rn(ra.y));
+            ra.z = __half2float(__float2half_rn(ra.z)); ra.w = __half2float(__float2half_rn(ra.w));
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) rw[h] = w_ok[h] ? *reinterpret_cast<const float4*>(w_src[h] + k0) : zero;
+    };
+    auto store = [&](int st) {
+        As[st][kq][ar] = ra.x; As[st][kq + 1][ar] = ra.y; As[st][kq + 2][ar] = ra.z; As[st][kq + 3][ar] = ra.w;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int wr = (threadIdx.x + h * 256) >> 2;
+            Ws[st][kq][wr] = rw[h].x; Ws[st][kq + 1][wr] = rw[h].y; Ws[st][kq + 2][wr] = rw[h].z; Ws[st][kq + 3][wr] = rw[h].w;
+        }
+    };
+    fetch(0);
+    store(0);
+    __syncthreads();
+    int st = 0;
+    for (int k0 = 0; k0 < K; k0 += GB_K) {
+        const bool more = k0 + GB_K < K;
+        if (more) fetch(k0 + GB_K);
+#pragma unroll
+        for (int kk = 0; kk < GB_K; ++kk) {
+            const float4 a4 = *reinterpret_cast<const float4*>(&As[st][kk][ty * 4]);
+            const float4 w0 = *reinterpret_cast<const float4*>(&Ws[st][kk][tx * 8]);
+            const float4 w1 = *reinterpret_cast<const float4*>(&Ws[st][kk][tx * 8 + 4]);
+            const float a[4] = {a4.x, a4.y, a4.z, a4.w};
+            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) pan[i][j] = __fmaf_rn(w[j], a[i], pan[i][j]);
+        }
+        if (panels && ((k0 + GB_K) % 192 == 0 || k0 + GB_K >= K)) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) { sum[i][j] = __fadd_rn(sum[i][j], pan[i][j]); pan[i][j] = 0.f; }
+        }
+        if (more) store(st ^ 1);        // the other stage was last read before the previous barrier
+        __syncthreads();
+        st ^= 1;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + ty * 4 + i;
+        if (m >= g.M) continue;
+        const int64_t orow = g.row_group > 0 ? int64_t(m / g.row_group) * g.row_stride + g.row_offset + m % g.row_group : m;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int n = n0 + tx * 8 + j;
+            if (n >= g.N) continue;
+            float v = panels ? sum[i][j] : pan[i][j];
+            if (g.bias) v = __fadd_rn(v, g.bias[n]);
+            const int64_t o = orow * g.ldo + n;
+            switch (g.epi) {
+                case SEPI_F32: static_cast<float*>(g.out)[o] = v; break;
+                case SEPI_F16: static_cast<__half*>(g.out)[o] = __float2half_rn(v); break;
+                case SEPI_RESID: static_cast<float*>(g.out)[o] = __fadd_rn(static_cast<float*>(g.out)[o], v); break;
+                case SEPI_SILU_F32: static_cast<float*>(g.out)[o] = ref_silu(v); break;
+                case SEPI_SILU_F16: static_cast<__half*>(g.out)[o] = __float2half_rn(ref_silu(v)); break;
+            }
+        }
+    }
+}
+
 }  // namespace
 
 cudaError_t assemble_targets(const float* ctx, const uint8_t* umask, int BV, int T, int kept, int len, int mirrored,
@@ -1424,6 +1528,13 @@ cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s) {
         simt_panel_kernel<<<grid, 256, 0, s>>>(g);
         const int64_t n = int64_t(g.M) * g.N;
         simt_panel_combine_kernel<<<blocks_for(n), TPB, 0, s>>>(g, panels);
+        return cudaGetLastError();
+    }
+    auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (g.order == ORDER_PANEL192 && g.tiled != 0 && !g.only_if && !g.row_mask && g.K % GB_K == 0 && g.lda % 4 == 0 &&
+        aligned(g.A) && aligned(g.W) && g.M >= GB_M && (g.M + GB_M - 1) / GB_M <= 65535) {
+        const dim3 grid((g.N + GB_N - 1) / GB_N, (g.M + GB_M - 1) / GB_M);
+        simt_gemm_tiled_kernel<<<grid, 256, 0, s>>>(g);
         return cudaGetLastError();
     }
     // One tile per block; launches that are conditional on a device flag (only_if) or whose

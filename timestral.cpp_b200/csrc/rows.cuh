@@ -131,6 +131,9 @@ struct SimtGemm {
     // scratch ([panels][M][N] f32) and are summed in order by a second kernel (same result).
     float* panel_scratch = nullptr;
     size_t panel_scratch_bytes = 0;
+    // ORDER_PANEL192 launches of at least 64 rows without only_if / row_mask, K % 16 == 0 and
+    // 16-byte aligned rows run a larger-tile kernel (same bits); 0 keeps the 64 x 64 kernel.
+    int tiled = 1;
 };
 // Bytes of panel scratch that simt_gemm uses for `g` (0: one pass, no scratch).
 size_t simt_panel_scratch_bytes(const SimtGemm& g);

@@ -41,6 +41,17 @@ extern "C" TIMESTRAL_API int tsb_test_gemm(const tsb_gemm_test* t, int32_t* dev_
     return h ? TSB_ERR_DEVICE : TSB_OK;
 }
 
+extern "C" TIMESTRAL_API int tsb_test_simt_gemm(const float* A, const float* W, int32_t M, int32_t N, int32_t K,
+                                                int32_t order, int32_t tiled, float* out) {
+    if (!A || !W || !out || M <= 0 || N <= 0 || K <= 0 || order < 0 || order > 2) return TSB_ERR_ARG;
+    tsb::SimtGemm g;
+    g.A = A; g.lda = K; g.W = W; g.M = M; g.N = N; g.K = K;
+    g.order = order; g.epi = tsb::SEPI_F32; g.out = out; g.ldo = N; g.tiled = tiled;
+    cudaError_t e = tsb::simt_gemm(g, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
+}
+
 extern "C" TIMESTRAL_API int tsb_test_rms(const float* x, const float* w, int32_t tokens, int32_t D, float eps, void* out,
                                           int32_t out_f16) {
     if (!x || !w || !out || tokens < 0 || D <= 0) return TSB_ERR_ARG;
