@@ -67,6 +67,15 @@ CONFIGS = {
                               "one_thread_seconds": 36.392652770,
                               "pytorch_reference_seconds": {"1": 14.379144, "6": 4.443924},
                               "cpu": "AMD Ryzen 5 7430U (6 cores)", "source": "docs/benchmarks.md of the reference"}),
+    "pub512": dict(weights="f32", B=1, V=1, T=512, H=32, cpu_sample=1,
+                   desc="pub512: the reference's published short benchmark shape: 209M f32 random-init, B=1, V=1, "
+                        "T=512, H=32, dyadic-v1 input ((17t+13v) mod 257 - 128)/64, symmetric+clip",
+                   published={"seconds_per_forecast": 0.405898183, "threads": 6,
+                              "what": "timestral.cpp native with the optimized linear kernels, 209M F32, context 512, "
+                                      "horizon 32, B=1",
+                              "one_thread_seconds": 1.541307288,
+                              "pytorch_reference_seconds": {"1": 0.419565},
+                              "cpu": "AMD Ryzen 5 7430U (6 cores)", "source": "docs/m6c-linear.md and docs/benchmarks.md of the reference"}),
     "cfg6": dict(weights="f16", B=64, V=1, T=32768, H=1024, cpu_sample=1,
                  desc="cfg6 long context: 209M f16 random-init, B=64, V=1, T=32768 (the full 1024-patch context), "
                       "H=1024 (one 32-patch decode block, S=1056), seasonal + 1% NaN"),
@@ -220,7 +229,7 @@ def workload(cfg: str, c: dict, lo: int, hi: int):
     if cfg == "cfg4":
         target, past, known, cat = sy.series_covariates(c["B"], V, T, H, seed=0)
         return target[lo:hi], {"past": past[lo:hi], "known": known[lo:hi], "cat_known": cat[lo:hi]}
-    if cfg == "pub32k":
+    if cfg in ("pub32k", "pub512"):
         return np.repeat(sy.series_dyadic(T, V), hi - lo, axis=0), {}
     out = np.empty((hi - lo, 1, T), np.float32)
     for k, i in enumerate(range(lo, hi)):
