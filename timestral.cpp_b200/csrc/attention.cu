@@ -1063,8 +1063,16 @@ __global__ void __launch_bounds__(TS_THREADS)
     const int r = int(b / (int64_t(H) * qblocks)), h = int((b / qblocks) % H), t0 = int(b % qblocks) * TS_Q;
     if (r >= rows) return;                                        // uniform across the block
     const int64_t plane = (int64_t(r) * H + h) * S;
-    const int last = min(S, t0 + TS_Q) - 1;
-    const int kend = time_keys(mm, last);                         // keys of the block's last query (the most)
+    // Keys the block's queries can attend: causal encoder queries (no covariates) see keys up
+    // to themselves, others all their computed keys. Tiles past the block's bound hold only
+    // masked keys, whose probabilities are exactly 0: their logits are written as -inf and
+    // their products are skipped (an FMA with p = 0 leaves the chain unchanged).
+    int kend = 0;
+    for (int qi = 0; qi < TS_Q && t0 + qi < S; ++qi) {
+        const int t = t0 + qi;
+        kend = max(kend, (!mm.cov && t < mm.N) ? t + 1 : time_keys(mm, t));
+    }
+    const int kdone = (kend + TS_KT - 1) / TS_KT * TS_KT;       // keys covered by the tiles
 
     for (int i = tid; i < TS_Q * HD; i += TS_THREADS) {
         const int qi = i / HD, d = i % HD;
@@ -1099,6 +1107,10 @@ __global__ void __launch_bounds__(TS_THREADS)
                 lg[(4 * g + u) * S + j] = time_allowed(mm, r, t, j) ? __fmul_rn(float(acc[u]), float(1.0 / sqrt(double(HD))))
                                                                     : -INFINITY;
         }
+    }
+    for (int i = tid; i < TS_Q * S; i += TS_THREADS) {
+        const int qi = i / S, j = i % S;
+        if (j >= kdone && t0 + qi < S && j < time_keys(mm, t0 + qi)) lg[i] = -INFINITY;
     }
     __syncthreads();
     // Softmax of each query: 16 threads per query for the maximum and the exponentials.
@@ -1138,9 +1150,10 @@ __global__ void __launch_bounds__(TS_THREADS)
             recip[qi] = __fdiv_rn(1.0f, sum);
         }
     }
-    // Values: thread (column d = tid % 64, queries 4 g .. 4 g + 3): float FMA chains over the
+    // Values: thread (query tid / 16, columns 4 (tid % 16) .. + 3): float FMA chains over the
     // keys in order, value tiles staged as float.
-    const int d = tid & (HD - 1);
+    const int vq = tid >> 4, d4 = (tid & 15) * 4;
+    const int vt = t0 + vq, vkeys = vt < S ? min(time_keys(mm, vt), kend) : 0;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int k0 = 0; k0 < kend; k0 += TS_KT) {
         __syncthreads();                                          // logits / sums / previous tile done
@@ -1149,24 +1162,25 @@ __global__ void __launch_bounds__(TS_THREADS)
             vs[i] = k0 + jj < S ? ld(v + (plane + k0 + jj) * HD + dd) : 0.f;
         }
         __syncthreads();
-        const int n = min(TS_KT, kend - k0);
-        const float* pr = lg + (4 * g) * S + k0;
+        const int n = min(TS_KT, vkeys - k0);
+        const float* pr = lg + vq * S + k0;
         for (int jj = 0; jj < n; ++jj) {
-            const float vv = vs[jj * HD + d];
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-                if (k0 + jj < kq[u]) acc[u] = __fmaf_rn(pr[u * S + jj], vv, acc[u]);   // uniform per warp
+            const float p = pr[jj];
+            const float4 vv = *reinterpret_cast<const float4*>(vs + jj * HD + d4);
+            acc[0] = __fmaf_rn(p, vv.x, acc[0]);
+            acc[1] = __fmaf_rn(p, vv.y, acc[1]);
+            acc[2] = __fmaf_rn(p, vv.z, acc[2]);
+            acc[3] = __fmaf_rn(p, vv.w, acc[3]);
         }
     }
-    __syncthreads();
+    if (vt >= S) return;
     const int D = H * HD;
+    const float rc = recip[vq];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const int qi = 4 * g + u, t = t0 + qi;
-        if (t >= S) continue;
-        float val = __fmul_rn(acc[u], recip[qi]);
-        if (gate) val = __fmul_rn(val, ld(gate + (plane + t) * HD + d));
-        st(out + (int64_t(r) * S + t) * D + h * HD + d, val);
+    for (int c = 0; c < 4; ++c) {
+        float val = __fmul_rn(acc[c], rc);
+        if (gate) val = __fmul_rn(val, ld(gate + (plane + vt) * HD + d4 + c));
+        st(out + (int64_t(r) * S + vt) * D + h * HD + d4 + c, val);
     }
 }
 
