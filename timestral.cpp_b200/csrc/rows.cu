@@ -1078,8 +1078,9 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtGemm g) {
 }
 
 // The same per-output order (ORDER_PANEL192) for large unconditional launches: a 64 x 128
-// block tile, 256 threads of 4 x 8 outputs each, 16-byte tile loads, and the 16-deep K steps
-// unrolled (panel boundaries, every 192 = 12 x 16 of K, fall between steps). Each output
+// block tile, 256 threads of 4 x 8 outputs each (columns 4 tx .. + 3 and 64 + 4 tx .. + 3, so
+// that a warp's 16-byte weight reads are conflict-free), 16-byte tile loads, and the 16-deep
+// K steps unrolled (panel boundaries, every 192 = 12 x 16 of K, fall between steps). Each output
 // still accumulates each 192-wide panel in K order with single-rounding FMAs and adds the
 // panel sums in order, so the result is simt_gemm_kernel<ORDER_PANEL192>'s bit for bit.
 // Requires K % 16 == 0 and 16-byte aligned A and W rows.
@@ -1139,8 +1140,8 @@ __global__ void __launch_bounds__(256, 2) simt_gemm_tiled_kernel(const SimtGemm 
 #pragma unroll
         for (int kk = 0; kk < GB_K; ++kk) {
             const float4 a4 = *reinterpret_cast<const float4*>(&As[st][kk][ty * 4]);
-            const float4 w0 = *reinterpret_cast<const float4*>(&Ws[st][kk][tx * 8]);
-            const float4 w1 = *reinterpret_cast<const float4*>(&Ws[st][kk][tx * 8 + 4]);
+            const float4 w0 = *reinterpret_cast<const float4*>(&Ws[st][kk][tx * 4]);
+            const float4 w1 = *reinterpret_cast<const float4*>(&Ws[st][kk][GB_N / 2 + tx * 4]);
             const float a[4] = {a4.x, a4.y, a4.z, a4.w};
             const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
@@ -1165,7 +1166,7 @@ __global__ void __launch_bounds__(256, 2) simt_gemm_tiled_kernel(const SimtGemm 
         const int64_t orow = g.row_group > 0 ? int64_t(m / g.row_group) * g.row_stride + g.row_offset + m % g.row_group : m;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int n = n0 + tx * 8 + j;
+            const int n = n0 + (j < 4 ? tx * 4 + j : GB_N / 2 + tx * 4 + j - 4);
             if (n >= g.N) continue;
             float v = panels ? sum[i][j] : pan[i][j];
             if (g.bias) v = __fadd_rn(v, g.bias[n]);
