@@ -227,8 +227,10 @@ TIMESTRAL_API int tsb_test_attention_variate(const void* q, const void* k, const
                                              int32_t S, int32_t N, int32_t G);
 /* CUDA-core GEMM of the F32 path, out[M][N] f32 = A[M][K] W[N][K]^T (device pointers,
  * synchronized), with the per-output order `order` (0: 192-wide K panels in K order, 1: one
- * FMA chain, 2: float64); tiled != 0 lets large panel-order launches run the 64 x 128 tile
- * kernel (same bits as the 64 x 64 one). */
+ * FMA chain, 2: float64); tiled bit 0 lets large panel-order launches run the 64 x 128 tile
+ * kernel (same bits as the 64 x 64 one); bit 1 gives launches of at most 512 rows with
+ * K >= 384 panel scratch (allocated here), so that they run the panel-split path (one block
+ * per 192-wide panel, the partials summed in panel order; same bits as one pass). */
 TIMESTRAL_API int tsb_test_simt_gemm(const float* A, const float* W, int32_t M, int32_t N, int32_t K, int32_t order,
                                      int32_t tiled, float* out);
 /* The refine step of one decode block with its float64 scratch from cudaMalloc (as the

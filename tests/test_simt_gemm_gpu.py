@@ -1,7 +1,8 @@
 """CUDA-core GEMM of the F32 path (per-output reference order, reference src/layers.cpp:143-177
 linear_f32: f32 FMAs in 192-wide K panels, panel sums added in order): the 64 x 128 tile
-kernel that large launches run equals the 64 x 64 kernel bit for bit, and on small dyadic
-values, where every partial sum is exact whatever the order, it equals the exact product."""
+kernel that large launches run equals the 64 x 64 kernel bit for bit, so does the panel-split
+path of few-row launches, and on small dyadic values, where every partial sum is exact
+whatever the order, the result is the exact product."""
 import ctypes as C
 
 import numpy as np
@@ -39,6 +40,21 @@ def test_tiled_equals_64x64(dev, M, N, K):
     b = run(A, W, 0, 0)
     assert torch.isfinite(a).all()
     assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+
+
+@pytest.mark.parametrize("M,N,K", [(34, 2304, 768), (34, 768, 2048), (64, 4096, 768), (1, 100, 400), (36, 33, 3072),
+                                   (300, 768, 768), (512, 130, 384)])
+def test_panel_split_equals_one_pass(dev, M, N, K):
+    """Launches of at most 512 rows (one decode block of a few series: cfg1 and the reference's
+    short benchmark) split K into 192-wide panels run as separate blocks and sum the partials
+    in panel order in a second kernel; the result equals the one-pass 64 x 64 kernel bit for bit."""
+    g = torch.Generator().manual_seed(M * 3 + N + K)
+    A = torch.randn(M, K, generator=g).to(dev)
+    W = (torch.randn(N, K, generator=g) * 0.05).to(dev)
+    split = run(A, W, 0, 2)
+    one = run(A, W, 0, 0)
+    assert torch.isfinite(split).all()
+    assert torch.equal(split.view(torch.int32), one.view(torch.int32))
 
 
 def test_panel_order_restatement(dev):

@@ -46,9 +46,19 @@ extern "C" TIMESTRAL_API int tsb_test_simt_gemm(const float* A, const float* W, 
     if (!A || !W || !out || M <= 0 || N <= 0 || K <= 0 || order < 0 || order > 2) return TSB_ERR_ARG;
     tsb::SimtGemm g;
     g.A = A; g.lda = K; g.W = W; g.M = M; g.N = N; g.K = K;
-    g.order = order; g.epi = tsb::SEPI_F32; g.out = out; g.ldo = N; g.tiled = tiled;
+    g.order = order; g.epi = tsb::SEPI_F32; g.out = out; g.ldo = N; g.tiled = tiled & 1;
+    // bit 1: give the launch panel scratch, as the engine does, so that few-row launches run
+    // the panel-split path
+    float* scratch = nullptr;
+    const size_t need = (tiled & 2) ? tsb::simt_panel_scratch_bytes(g) : 0;
+    if (need) {
+        if (cudaMalloc(&scratch, need) != cudaSuccess) return TSB_ERR_CUDA;
+        g.panel_scratch = scratch;
+        g.panel_scratch_bytes = need;
+    }
     cudaError_t e = tsb::simt_gemm(g, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (scratch) cudaFree(scratch);
     return e == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
 }
 
