@@ -221,7 +221,14 @@ TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, int32_t K, vo
 /* Variate-axis attention of the tensor-core path over groups of G consecutive rows (one
  * series each): q/k/v/gate f16 head-major [rows][H][S][64] (gate may be NULL), key_valid
  * [rows][ceil(N/32)] bits, role [rows] (0 target, 1 past, 2 known) or NULL without
- * covariates, out f16 token-major [rows * S][H * 64]; synchronized. */
+ * covariates, out f16 token-major [rows * S][H * 64]; synchronized. kernel: 0 the engine's
+ * choice, 1 the CUDA-core kernel (G <= 64), 2 the tensor-core kernel (G <= 32, four
+ * (series, head, slot) problems per score tile). On TSB_ERR_DEVICE *dev_error (may be NULL)
+ * holds the kernel's error word. */
+TIMESTRAL_API int tsb_test_attention_variate_ex(const void* q, const void* k, const void* v, const void* gate, void* out,
+                                                const uint32_t* key_valid, const int8_t* role, int32_t rows, int32_t H,
+                                                int32_t S, int32_t N, int32_t G, int32_t kernel, int32_t* dev_error);
+/* The same with kernel 1. */
 TIMESTRAL_API int tsb_test_attention_variate(const void* q, const void* k, const void* v, const void* gate, void* out,
                                              const uint32_t* key_valid, const int8_t* role, int32_t rows, int32_t H,
                                              int32_t S, int32_t N, int32_t G);

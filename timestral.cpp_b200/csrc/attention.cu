@@ -194,6 +194,65 @@ __device__ __forceinline__ float exp2_ftz(float x) {
     return y;
 }
 
+// logit scale 1/sqrt(64) folded with log2(e) for exp2
+constexpr float kScaleLog2e = 0.125f * 1.4426950408889634f;
+
+// Softmax of the query row in this thread's TMEM lane (`row` = the score tile's address at
+// this warp's lanes) over the keys in `allowed`, which all lie in the 16-key chunks
+// [kmin / 16, kmax / 16] (warp-uniform bounds, kmax >= 0). Pass 1: the maximum (eight
+// partial maxima). Pass 2: the probabilities exp2(s * scale - max * scale) rounded to f16,
+// written two keys per TMEM column over the score columns already read (P columns
+// [8c, 8c + 8) <= S columns [16c, 16c + 16)), zeros in the chunks outside the bounds; returns
+// their sum (eight partial sums). NCH: the tile's 16-key chunks.
+template <int NCH>
+__device__ __forceinline__ float softmax_to_p(uint32_t row, const uint32_t (&allowed)[4], int kmin, int kmax, bool live) {
+    float mxj[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mxj[j] = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        if (c * 16 > kmax) break;
+        if (c * 16 + 15 < kmin) continue;
+        uint32_t sc[16];
+        tmem_ld16(row + c * 16, sc);
+        tmem_ld_wait();
+        const uint32_t bits = allowed[(c * 16) >> 5] >> ((c * 16) & 31);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if ((bits >> j) & 1u) mxj[j & 7] = fmaxf(mxj[j & 7], __uint_as_float(sc[j]));
+    }
+    const float mx = fmaxf(fmaxf(fmaxf(mxj[0], mxj[1]), fmaxf(mxj[2], mxj[3])),
+                           fmaxf(fmaxf(mxj[4], mxj[5]), fmaxf(mxj[6], mxj[7])));
+    const float off = live ? mx * kScaleLog2e : 0.f;
+    float sj[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sj[j] = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        uint32_t pk[8];
+        if (c * 16 <= kmax && c * 16 + 15 >= kmin) {
+            uint32_t sc[16];
+            tmem_ld16(row + c * 16, sc);
+            tmem_ld_wait();
+            const uint32_t bits = allowed[(c * 16) >> 5] >> ((c * 16) & 31);
+            float p[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                p[j] = (bits >> j) & 1u ? exp2_ftz(__fmaf_rn(__uint_as_float(sc[j]), kScaleLog2e, -off)) : 0.f;
+                sj[j & 7] += p[j];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pk[j] = pack_half2(p[2 * j], p[2 * j + 1]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pk[j] = 0u;
+        }
+        tmem_st8(row + c * 8, pk);
+    }
+    tmem_st_wait();
+    return ((sj[0] + sj[1]) + (sj[2] + sj[3])) + ((sj[4] + sj[5]) + (sj[6] + sj[7]));
+}
+
 template <int NK, int PK>
 __global__ void __launch_bounds__(AT_THREADS, 4)
     attn_time_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
@@ -251,8 +310,6 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
     };
     if (ctl && int(blockIdx.x) < units) { issue_qk(blockIdx.x); issue_v(blockIdx.x); }
 
-    // logit scale 1/sqrt(64) folded with log2(e) for exp2
-    constexpr float kScaleLog2e = 0.125f * 1.4426950408889634f;
     int i = 0;
     for (int unit = blockIdx.x; unit < units; unit += gridDim.x, ++i) {
         const uint32_t ph = i & 1;
@@ -302,57 +359,7 @@ __global__ void __launch_bounds__(AT_THREADS, 4)
         if (!warp_wait(&bars->s_full, ph, abort, err)) break;
         tc_fence_after();
         if (ctl && next < units) issue_qk(next);       // Q and K are free once S is complete
-        float sum = 0.f;
-        if (kmax >= 0) {
-            // Pass 1: the row maximum over the query's keys (eight partial maxima).
-            float mxj[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) mxj[j] = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < PK * NK / 16; ++c) {
-                if (c * 16 > kmax) break;
-                if (PK == 2 && c * 16 + 15 < kmin) continue;
-                uint32_t sc[16];
-                tmem_ld16(tS + lane_base + c * 16, sc);
-                tmem_ld_wait();
-                const uint32_t bits = allowed[(c * 16) >> 5] >> ((c * 16) & 31);
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if ((bits >> j) & 1u) mxj[j & 7] = fmaxf(mxj[j & 7], __uint_as_float(sc[j]));
-            }
-            const float mx = fmaxf(fmaxf(fmaxf(mxj[0], mxj[1]), fmaxf(mxj[2], mxj[3])),
-                                   fmaxf(fmaxf(mxj[4], mxj[5]), fmaxf(mxj[6], mxj[7])));
-            const float off = live ? mx * kScaleLog2e : 0.f;
-            // Pass 2: probabilities in f16, two keys per TMEM column over the columns of S
-            // already read (P columns [8c, 8c + 8) <= S columns [16c, 16c + 16)), and their sum.
-            float sj[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) sj[j] = 0.f;
-#pragma unroll
-            for (int c = 0; c < PK * NK / 16; ++c) {
-                uint32_t pk[8];
-                if (c * 16 <= kmax && (PK == 1 || c * 16 + 15 >= kmin)) {
-                    uint32_t sc[16];
-                    tmem_ld16(tS + lane_base + c * 16, sc);
-                    tmem_ld_wait();
-                    const uint32_t bits = allowed[(c * 16) >> 5] >> ((c * 16) & 31);
-                    float p[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        p[j] = (bits >> j) & 1u ? exp2_ftz(__fmaf_rn(__uint_as_float(sc[j]), kScaleLog2e, -off)) : 0.f;
-                        sj[j & 7] += p[j];
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) pk[j] = pack_half2(p[2 * j], p[2 * j + 1]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) pk[j] = 0u;
-                }
-                tmem_st8(tS + lane_base + c * 8, pk);
-            }
-            tmem_st_wait();
-            sum = ((sj[0] + sj[1]) + (sj[2] + sj[3])) + ((sj[4] + sj[5]) + (sj[6] + sj[7]));
-        }
+        const float sum = kmax >= 0 ? softmax_to_p<PK * NK / 16>(tS + lane_base, allowed, kmin, kmax, live) : 0.f;
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->p_ready);
@@ -472,6 +479,227 @@ cudaError_t launch_attn_tc(const __half* q, const __half* k, const __half* v, co
     attn_time_tc_kernel<NK, PK><<<grid, AT_THREADS, smem, stream>>>(mq, mk, mv, gate, out, rows, H, mm, err);
     return cudaGetLastError();
 }
+
+// ---------------------------------------------------------------------------------------
+// Tensor-core variate attention for series of at most 32 rows (reference src/encoder.cpp:80,
+// 86, 88: sdpa over the rows of one series at each patch slot; mask src/masks.cpp:27). A tile
+// holds four problems (series, head, patch slots p0 .. p0 + 3), one per warp: slot p0 + w's
+// query rows at TMEM lanes 32 w .. 32 w + G - 1 and its keys and values at rows 32 w .. of the
+// K and V tiles (one TMA box per slot: that slot of 32 consecutive rows), so the score tile
+// S = Q K^T (M = N = 128) is block-diagonal and each warp's softmax reads its own two 16-key
+// chunks; P in TMEM, O = P V and the epilogue as in the time kernel. Box rows past the series
+// (G < 32) are other series' rows or zero fill, outside every key set. The key set of query
+// row i at slot p: itself, and the series' rows whose patch p is observed (every row at decoder
+// slots), under the covariate role firewall; lane j supplies key j's part through ballots.
+constexpr int AV_SLOTS = 4;
+constexpr int AV_TILE = 128 * 128;                  // one operand tile: 4 slots x 32 rows x 128 B
+constexpr int AV_SMEM = 1024 + 4 * AV_TILE + 256;   // Q, K, V, output staging, barriers
+
+__global__ void __launch_bounds__(AT_THREADS, 3)
+    attn_variate_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                           const __grid_constant__ CUtensorMap map_v, const __half* __restrict__ gate,
+                           __half* __restrict__ out, int rows, int H, int G, const MaskMeta mm, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    const int S = mm.S, D = H * 64;
+    uint8_t* qbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* kbuf = qbuf + AV_TILE;
+    uint8_t* vbuf = kbuf + AV_TILE;
+    uint8_t* obuf = vbuf + AV_TILE;
+    AttnBars* bars = reinterpret_cast<AttnBars*>(obuf + AV_TILE);
+    volatile int* abort = &bars->abort;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, t = threadIdx.x;
+    const int SQ = (S + AV_SLOTS - 1) / AV_SLOTS;
+    const int units = (rows / G) * H * SQ;
+    const bool ctl = threadIdx.x == 0;
+
+    if (ctl) {
+        mbar_init(&bars->full_qk, 1); mbar_init(&bars->full_v, 1); mbar_init(&bars->s_full, 1);
+        mbar_init(&bars->p_ready, 4); mbar_init(&bars->o_full, 1); mbar_init(&bars->tm_free, 4);
+        bars->abort = 0;
+        mbar_fence_init();
+        fence_proxy_async();
+    }
+    if (warp == 0) { tmem_alloc(&bars->tmem, AT_TMEM_COLS); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tS = bars->tmem;                       // S, then P over its first 64 columns
+    const uint32_t tO = tS + AT_O_COL;
+    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+
+    auto issue_qk = [&](int unit) {
+        const int r0 = (unit / (H * SQ)) * G, h = (unit / SQ) % H, p0 = (unit % SQ) * AV_SLOTS;
+        mbar_arrive_expect_tx(&bars->full_qk, 2 * AV_TILE);
+#pragma unroll
+        for (int w = 0; w < AV_SLOTS; ++w) {
+            tma_load_3d(qbuf + w * 32 * 128, &map_q, &bars->full_qk, 0, h * S + p0 + w, r0);
+            tma_load_3d(kbuf + w * 32 * 128, &map_k, &bars->full_qk, 0, h * S + p0 + w, r0);
+        }
+    };
+    auto issue_v = [&](int unit) {
+        const int r0 = (unit / (H * SQ)) * G, h = (unit / SQ) % H, p0 = (unit % SQ) * AV_SLOTS;
+        mbar_arrive_expect_tx(&bars->full_v, AV_TILE);
+#pragma unroll
+        for (int w = 0; w < AV_SLOTS; ++w) tma_load_3d(vbuf + w * 32 * 128, &map_v, &bars->full_v, 0, h * S + p0 + w, r0);
+    };
+    if (ctl && int(blockIdx.x) < units) { issue_qk(blockIdx.x); issue_v(blockIdx.x); }
+
+    int i = 0;
+    for (int unit = blockIdx.x; unit < units; unit += gridDim.x, ++i) {
+        const uint32_t ph = i & 1;
+        const int next = unit + gridDim.x;
+        const int r0 = (unit / (H * SQ)) * G, h = (unit / SQ) % H, p = (unit % SQ) * AV_SLOTS + warp;
+        const int row = r0 + lane;                      // this thread's query row (and key row)
+        const bool in_series = lane < G && p < S;
+        const bool live = in_series;
+        if (warp == 0) {
+            int ok = 1;
+            if (lane == 0) {
+                ok = at_wait(&bars->full_qk, ph, abort, err);
+                if (ok && i > 0) ok = at_wait(&bars->tm_free, ph ^ 1, abort, err);
+                if (ok) {
+                    tc_fence_after();
+                    const uint64_t dq = smem_desc_sw128(smem_u32(qbuf)), dk = smem_desc_sw128(smem_u32(kbuf));
+                    const uint32_t id1 = idesc_f16(128, 128);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) mma_f16(tS, dq + uint64_t(2 * k), dk + uint64_t(2 * k), id1, k > 0);
+                    mma_commit(&bars->s_full);
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        }
+        const bool usable = in_series && (p >= mm.N || kv_bit(mm, row, p));
+        const int role = (mm.cov && in_series) ? mm.role[row] : 0;
+        uint32_t bits = __ballot_sync(0xffffffffu, usable);
+        if (mm.cov) {
+            const uint32_t b0 = __ballot_sync(0xffffffffu, in_series && role == 0);
+            const uint32_t b2 = __ballot_sync(0xffffffffu, in_series && role == 2);
+            if (role != 0) bits &= ~b0;
+            if (role == 2) bits &= b2;
+        }
+        bits = live ? (bits | (1u << lane)) : 0u;
+        uint32_t allowed[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) allowed[w] = w == warp ? bits : 0u;
+        const int hi = bits ? warp * 32 + 31 - __clz(bits) : -1;
+        const int lo = bits ? warp * 32 + __ffs(int(bits)) - 1 : 128;
+        const int kmax = __reduce_max_sync(0xffffffffu, hi + 1) - 1;   // -1: no live query in this warp
+        const int kmin = int(__reduce_min_sync(0xffffffffu, unsigned(lo)));
+        if (!warp_wait(&bars->s_full, ph, abort, err)) break;
+        tc_fence_after();
+        if (ctl && next < units) issue_qk(next);       // Q and K are free once S is complete
+        const float sum = kmax >= 0 ? softmax_to_p<8>(tS + lane_base, allowed, kmin, kmax, live) : 0.f;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_ready);
+        if (warp == 0) {
+            int ok = 1;
+            if (lane == 0) {
+                ok = at_wait(&bars->p_ready, ph, abort, err) && at_wait(&bars->full_v, ph, abort, err);
+                if (ok) {
+                    tc_fence_after();
+                    const uint32_t sv = smem_u32(vbuf);
+                    const uint32_t id2 = idesc_f16_bmn(128, 64);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_f16_ts(tO, tS + kk * 8, smem_desc_sw128(sv + kk * 16 * 128), id2, kk > 0);
+                    mma_commit(&bars->o_full);
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        }
+        uint4 gv[8];
+        const __half* g = (gate && live) ? gate + ((int64_t(row) * H + h) * S + p) * 64 : nullptr;
+        if (g) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) gv[c] = *reinterpret_cast<const uint4*>(g + c * 8);
+        }
+        if (!warp_wait(&bars->o_full, ph, abort, err)) break;
+        tc_fence_after();
+        if (ctl && next < units) issue_v(next);        // V is free once O is complete
+        const float inv = live ? 1.0f / sum : 0.f;
+        auto stage = [&](const uint32_t (&o)[32], int half32) {
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+                const int c = half32 * 4 + c4;
+                float y[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) y[j] = __uint_as_float(o[c4 * 8 + j]) * inv;
+                if (g) {
+                    const __half2* gh = reinterpret_cast<const __half2*>(&gv[c]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __half22float2(gh[j]);
+                        y[2 * j] = __fmul_rn(y[2 * j], f.x);
+                        y[2 * j + 1] = __fmul_rn(y[2 * j + 1], f.y);
+                    }
+                }
+                uint4 u;
+                u.x = pack_half2(y[0], y[1]); u.y = pack_half2(y[2], y[3]);
+                u.z = pack_half2(y[4], y[5]); u.w = pack_half2(y[6], y[7]);
+                *reinterpret_cast<uint4*>(obuf + t * 128 + ((c ^ (t & 7)) << 4)) = u;
+            }
+        };
+        uint32_t o[32];
+        if (kmax >= 0) {
+            tmem_ld32(tO + lane_base, o);
+            tmem_ld_wait();
+            stage(o, 0);
+            tmem_ld32(tO + lane_base + 32, o);
+            tmem_ld_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->tm_free);    // the next S may overwrite P and O
+        if (kmax < 0) continue;
+        stage(o, 1);
+        __syncwarp();
+        // The warp's 32 staged rows: rows r0 + ri of slot p, eight threads per 128-byte row.
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int ri = j * 4 + (lane >> 3), chunk = lane & 7, srow = warp * 32 + ri;
+            if (ri < G)
+                *reinterpret_cast<uint4*>(out + (int64_t(r0 + ri) * S + p) * D + h * 64 + chunk * 8) =
+                    *reinterpret_cast<const uint4*>(obuf + srow * 128 + ((chunk ^ (srow & 7)) << 4));
+        }
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(bars->tmem, AT_TMEM_COLS);
+}
+
+}  // namespace
+
+bool make_map_slot_rows_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t slots, int box_rows);
+
+cudaError_t attention_variate_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
+                                 int rows, int H, int G, const MaskMeta& mm, cudaStream_t stream, int* err) {
+    if (rows <= 0) return cudaSuccess;
+    if (G <= 0 || G > 32 || rows % G || mm.S <= 0 || H <= 0) return cudaErrorInvalidValue;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_variate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AV_SMEM);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    CUtensorMap mq, mk, mv;
+    const int64_t slots = int64_t(H) * mm.S;
+    if (!make_map_slot_rows_f16(&mq, q, rows, slots, 32) || !make_map_slot_rows_f16(&mk, k, rows, slots, 32) ||
+        !make_map_slot_rows_f16(&mv, v, rows, slots, 32))
+        return cudaErrorInvalidValue;
+    const int64_t units = int64_t(rows / G) * H * ((mm.S + AV_SLOTS - 1) / AV_SLOTS);
+    if (units > INT32_MAX) return cudaErrorInvalidValue;
+    int grid = device_sm_count() * 3;                 // shared memory: three CTAs per SM
+    if (int64_t(grid) > units) grid = int(units);
+    attn_variate_tc_kernel<<<grid, AT_THREADS, AV_SMEM, stream>>>(mq, mk, mv, gate, out, rows, H, G, mm, err);
+    return cudaGetLastError();
+}
+
+namespace {
 
 // ---------------------------------------------------------------------------------------
 // Tensor-core time attention for long rows (S > 128: context_length / patch_size up to
@@ -735,7 +963,6 @@ __global__ void __launch_bounds__(AL_THREADS, 2)
         __syncwarp();
     } else {
         // Softmax and epilogue: thread t = query token q0 + t, TMEM lane t.
-        constexpr float kScaleLog2e = 0.125f * 1.4426950408889634f;
         const int t = threadIdx.x;
         const uint32_t lane_base = uint32_t(warp * 32) << 16;
         int i = 0, g = 0;

@@ -45,6 +45,11 @@ constexpr int kSimtMaxKeys = 2176;
 template <class T>
 cudaError_t attention_time_simt(const T* q, const T* k, const T* v, const T* gate, T* out, int rows, int H, int hd,
                                 const MaskMeta& mm, cudaStream_t stream, int tiled = -1);
+// Variate-axis attention on tensor cores for series of G <= 32 consecutive rows (f16
+// head-major q/k/v/gate, head_dim 64, out token-major f16): four (series, head, slot)
+// problems per score tile. err: device error word (expired waits).
+cudaError_t attention_variate_tc(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,
+                                 int rows, int H, int G, const MaskMeta& mm, cudaStream_t stream, int* err);
 // Variate-axis attention of the tensor-core path: groups of G <= 64 consecutive rows (one
 // series), f16 head-major q/k/v/gate, head_dim 64, out token-major f16.
 cudaError_t attention_variate_fast(const __half* q, const __half* k, const __half* v, const __half* gate, __half* out,

@@ -980,7 +980,9 @@ struct Engine::Impl {
                 else
                     run("attention", [&] { return attention_time_tc_long(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, mm, s, err.as<int>()); });
             } else {
-                if (group_rows <= 64)
+                if (group_rows <= 32)
+                    run("attention_variate", [&] { return attention_variate_tc(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, group_rows, mm, s, err.as<int>()); });
+                else if (group_rows <= 64)
                     run("attention_variate", [&] { return attention_variate_fast(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, group_rows, mm, s); });
                 else
                     run("attention_variate", [&] { return attention_variate_simt<__half>(qb.as<__half>(), kb.as<__half>(), vb.as<__half>(), gate, att16, R2, H, hd, mm, s); });

@@ -859,6 +859,21 @@ bool make_map_3d_f16(CUtensorMap* map, const void* base, int64_t planes, int64_t
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3D f16 tensor map over head-major [rows][slots][64] (slots = heads x tokens of a row), box
+// {64, 1 slot, box_rows rows}: the same (head, token) slot of box_rows consecutive rows, laid
+// out in shared memory as box_rows 128-byte rows (the image of a 2D box of box_rows rows).
+bool make_map_slot_rows_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t slots, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {64, cuuint64_t(slots), cuuint64_t(rows)};
+    cuuint64_t strides[2] = {64 * 2, cuuint64_t(slots) * 64 * 2};
+    cuuint32_t box[3] = {64, 1, cuuint32_t(box_rows)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int device_sm_count() {
     static int counts[64] = {0};
     int dev = 0;

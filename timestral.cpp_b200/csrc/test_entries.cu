@@ -168,22 +168,39 @@ extern "C" TIMESTRAL_API int tsb_test_split_f16(const float* a, int64_t rows, in
     return e == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
 }
 
-extern "C" TIMESTRAL_API int tsb_test_attention_variate(const void* q, const void* k, const void* v, const void* gate,
-                                                        void* out, const uint32_t* key_valid, const int8_t* role,
-                                                        int32_t rows, int32_t H, int32_t S, int32_t N, int32_t G) {
+extern "C" TIMESTRAL_API int tsb_test_attention_variate_ex(const void* q, const void* k, const void* v, const void* gate,
+                                                           void* out, const uint32_t* key_valid, const int8_t* role,
+                                                           int32_t rows, int32_t H, int32_t S, int32_t N, int32_t G,
+                                                           int32_t kernel, int32_t* dev_error) {
     using namespace tsb;
     if (!q || !k || !v || !out || !key_valid || rows <= 0 || H <= 0 || S <= 0 || N <= 0 || N > S || G <= 0 ||
-        rows % G)
+        rows % G || kernel < 0 || kernel > 2)
         return TSB_ERR_ARG;
     MaskMeta mm;
     mm.key_valid = key_valid; mm.kv_words = (N + 31) / 32; mm.N = N; mm.L = N; mm.S = S;
     mm.cov = role != nullptr; mm.role = role;
-    cudaError_t ce = attention_variate_fast(static_cast<const __half*>(q), static_cast<const __half*>(k),
-                                            static_cast<const __half*>(v), static_cast<const __half*>(gate),
-                                            static_cast<__half*>(out), rows, H, G, mm, 0);
+    if (kernel == 0) kernel = G <= 32 ? 2 : 1;
+    int* derr = nullptr;
+    if (cudaMalloc(&derr, sizeof(int)) != cudaSuccess) return TSB_ERR_CUDA;
+    cudaMemset(derr, 0, sizeof(int));
+    const __half *hq = static_cast<const __half*>(q), *hk = static_cast<const __half*>(k), *hv = static_cast<const __half*>(v);
+    const __half* hg = static_cast<const __half*>(gate);
+    __half* ho = static_cast<__half*>(out);
+    cudaError_t ce = kernel == 2 ? attention_variate_tc(hq, hk, hv, hg, ho, rows, H, G, mm, 0, derr)
+                                 : attention_variate_fast(hq, hk, hv, hg, ho, rows, H, G, mm, 0);
     if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+    int h = 0;
+    cudaMemcpy(&h, derr, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(derr);
+    if (dev_error) *dev_error = h;
     if (ce != cudaSuccess) return ce == cudaErrorInvalidValue ? TSB_ERR_ARG : TSB_ERR_CUDA;
-    return TSB_OK;
+    return h ? TSB_ERR_DEVICE : TSB_OK;
+}
+
+extern "C" TIMESTRAL_API int tsb_test_attention_variate(const void* q, const void* k, const void* v, const void* gate,
+                                                        void* out, const uint32_t* key_valid, const int8_t* role,
+                                                        int32_t rows, int32_t H, int32_t S, int32_t N, int32_t G) {
+    return tsb_test_attention_variate_ex(q, k, v, gate, out, key_valid, role, rows, H, S, N, G, 1, nullptr);
 }
 
 // The refine kernel as the forecast runs it: float64 scan scratch taken from the allocator

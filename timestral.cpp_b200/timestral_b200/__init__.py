@@ -79,6 +79,7 @@ SIGNATURES = {
     "tsb_test_attention_time_ex": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 9 + [C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
     "tsb_test_split_f16": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p]),
     "tsb_test_attention_variate": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 5),
+    "tsb_test_attention_variate_ex": (C.c_int, [C.c_void_p] * 7 + [C.c_int32] * 6 + [C.POINTER(C.c_int32)]),
     "tsb_test_rms": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_float, C.c_void_p, C.c_int32]),
     "tsb_test_simt_gemm": (C.c_int, [C.c_void_p, C.c_void_p] + [C.c_int32] * 5 + [C.c_void_p]),
     "tsb_test_refine": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 6 + [C.c_double, C.c_void_p]),
