@@ -1496,6 +1496,56 @@ __global__ void __launch_bounds__(256) simt_panel_kernel(const SimtGemm g) {
     }
 }
 
+// The same partials with the whole 192-wide panel staged at once: every thread issues its
+// 16-byte loads of the A and W panel tiles together (one memory latency per block instead of
+// one per 32-deep step), then runs its 2 x 2 K-ordered FMA chains over the panel. Requires
+// K % 4 == 0 and 16-byte aligned A and W rows.
+constexpr int PF_STRIDE = PT + 4;                    // [k][row] tiles, padded
+constexpr size_t panel_full_smem() { return size_t(2) * PANEL * PF_STRIDE * sizeof(float); }
+
+__global__ void __launch_bounds__(256) simt_panel_full_kernel(const SimtGemm g) {
+    extern __shared__ __align__(16) float pf_sh[];
+    float* As = pf_sh;                               // [PANEL][PF_STRIDE]
+    float* Ws = pf_sh + PANEL * PF_STRIDE;
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const int m0 = blockIdx.y * PT, n0 = blockIdx.x * PT, p = blockIdx.z;
+    const int k_lo = p * PANEL, kn = min(g.K, k_lo + PANEL) - k_lo;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int e = threadIdx.x; e < PT * (PANEL / 4); e += 256) {
+        const int rr = e % PT, k4 = (e / PT) * 4;     // a warp stores one k-quad of 32 rows: no conflicts
+        const int m = m0 + rr, n = n0 + rr;
+        float4 a = (m < g.M && k4 < kn) ? *reinterpret_cast<const float4*>(g.A + int64_t(m) * g.lda + k_lo + k4) : zero;
+        if (g.round_a_f16) {
+            a.x = __half2float(__float2half_rn(a.x)); a.y = __half2float(__float2half_rn(a.y));
+            a.z = __half2float(__float2half_rn(a.z)); a.w = __half2float(__float2half_rn(a.w));
+        }
+        const float4 w = (n < g.N && k4 < kn) ? *reinterpret_cast<const float4*>(g.W + int64_t(n) * g.K + k_lo + k4) : zero;
+        As[(k4 + 0) * PF_STRIDE + rr] = a.x; As[(k4 + 1) * PF_STRIDE + rr] = a.y;
+        As[(k4 + 2) * PF_STRIDE + rr] = a.z; As[(k4 + 3) * PF_STRIDE + rr] = a.w;
+        Ws[(k4 + 0) * PF_STRIDE + rr] = w.x; Ws[(k4 + 1) * PF_STRIDE + rr] = w.y;
+        Ws[(k4 + 2) * PF_STRIDE + rr] = w.z; Ws[(k4 + 3) * PF_STRIDE + rr] = w.w;
+    }
+    __syncthreads();
+    float pan[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    for (int kk = 0; kk < kn; ++kk) {
+        const float2 a = *reinterpret_cast<const float2*>(As + kk * PF_STRIDE + ty * 2);
+        const float2 w = *reinterpret_cast<const float2*>(Ws + kk * PF_STRIDE + tx * 2);
+        pan[0][0] = __fmaf_rn(w.x, a.x, pan[0][0]); pan[0][1] = __fmaf_rn(w.y, a.x, pan[0][1]);
+        pan[1][0] = __fmaf_rn(w.x, a.y, pan[1][0]); pan[1][1] = __fmaf_rn(w.y, a.y, pan[1][1]);
+    }
+    float* part = g.panel_scratch + int64_t(p) * g.M * g.N;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int m = m0 + ty * 2 + i;
+        if (m >= g.M) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int n = n0 + tx * 2 + j;
+            if (n < g.N) part[int64_t(m) * g.N + n] = pan[i][j];
+        }
+    }
+}
+
 __global__ void simt_panel_combine_kernel(const SimtGemm g, int panels) {
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= int64_t(g.M) * g.N) return;
@@ -1526,7 +1576,21 @@ cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s) {
     if (need && g.panel_scratch && g.panel_scratch_bytes >= need) {
         const int panels = (g.K + PANEL - 1) / PANEL;
         const dim3 grid((g.N + PT - 1) / PT, (g.M + PT - 1) / PT, panels);
-        simt_panel_kernel<<<grid, 256, 0, s>>>(g);
+        auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+        if (g.tiled != 0 && g.K % 4 == 0 && g.lda % 4 == 0 && aligned16(g.A) && aligned16(g.W)) {
+            static bool configured[64] = {false};
+            int dev = 0;
+            cudaGetDevice(&dev);
+            if (dev >= 0 && dev < 64 && !configured[dev]) {
+                cudaError_t e = cudaFuncSetAttribute(simt_panel_full_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     int(panel_full_smem()));
+                if (e != cudaSuccess) return e;
+                configured[dev] = true;
+            }
+            simt_panel_full_kernel<<<grid, 256, panel_full_smem(), s>>>(g);
+        } else {
+            simt_panel_kernel<<<grid, 256, 0, s>>>(g);
+        }
         const int64_t n = int64_t(g.M) * g.N;
         simt_panel_combine_kernel<<<blocks_for(n), TPB, 0, s>>>(g, panels);
         return cudaGetLastError();
