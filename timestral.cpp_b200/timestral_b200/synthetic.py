@@ -391,6 +391,89 @@ def series_dyadic(T: int, V: int = 1):
     return ((((17 * t + 13 * v) % 257) - 128) / 64.0).astype(np.float32)[None]
 
 
+def reference_case_inputs(case: dict, patch_size: int) -> dict:
+    """Inputs of one case of the reference's forecast tests (its tests/cases.json), built as
+    its generator builds them (reference scripts/gen_reference_baseline.py:675-745): one
+    numpy default_rng(seed); per series b and variate v a Gaussian random walk plus
+    10 sin(2 pi t / (period (1 + v/4)) + 0.3 b), a level and a linear trend (absolute values
+    when `positive`, every step `constant` when given); missing steps: the first `leading`
+    steps and the listed whole patches of the first row, a scattered fraction, and whole rows;
+    numeric covariates 5 sin(2 pi t / (period + 7 + 5 c) + b / 2) + N(0, 1/4) (known ones over
+    T + H), 0/1 indicator rows alternating every 5 + 2 c steps, categorical codes drawn
+    uniformly (a code unseen in the context at step T + H/2 of the known ones when asked).
+    Returns {"context": [B,V,T] float32, "past", "known": float32, "cat_past", "cat_known":
+    float64 (NaN = missing)} with the keys the case uses."""
+    rng = np.random.default_rng(case["seed"])
+    B, V, T, H = case["B"], case["V"], case["T"], case["H"]
+    s = case.get("series", {})
+    period = s.get("period", 24)
+    t = np.arange(T, dtype=np.float64)
+    x = np.empty((B, V, T))
+    for b in range(B):
+        for v in range(V):
+            walk = np.cumsum(rng.normal(0.0, s.get("noise_std", 1.0), T))
+            wave = 10.0 * np.sin(2.0 * np.pi * t / (period * (1.0 + 0.25 * v)) + 0.3 * b)
+            x[b, v] = s.get("level", 0.0) + s.get("trend", 0.0) * t + wave + walk
+    if s.get("positive"):
+        x = np.abs(x)
+    if s.get("constant") is not None:
+        x[:] = s["constant"]
+    x = x.astype(np.float32)
+    rows = x.reshape(B * V, T)
+    miss = case.get("missing", {})
+    if miss.get("leading"):
+        rows[0, :miss["leading"]] = np.nan
+    for p in miss.get("missing_patches", []):
+        rows[0, p * patch_size:(p + 1) * patch_size] = np.nan
+    if miss.get("scattered_frac"):
+        rows[rng.random(rows.shape) < miss["scattered_frac"]] = np.nan
+    for i in miss.get("all_missing_series", []):
+        rows[i, :] = np.nan
+    out = {"context": x}
+
+    def numeric_rows(n, length, nan_frac):
+        tt = np.arange(length, dtype=np.float64)
+        r = np.empty((B, n, length))
+        for b in range(B):
+            for c in range(n):
+                r[b, c] = 5.0 * np.sin(2 * np.pi * tt / (period + 7 + 5 * c) + 0.5 * b) + 0.5 * rng.normal(size=length)
+        r = r.astype(np.float32)
+        if nan_frac:
+            r[rng.random(r.shape) < nan_frac] = np.nan
+        return r
+
+    pc = case.get("past", {})
+    if pc.get("numeric"):
+        out["past"] = numeric_rows(pc["numeric"], T, pc.get("nan_frac", 0.0))
+    kc = case.get("known", {})
+    if kc.get("numeric") or kc.get("indicator"):
+        parts = []
+        if kc.get("numeric"):
+            parts.append(numeric_rows(kc["numeric"], T + H, kc.get("nan_frac", 0.0)))
+        if kc.get("indicator"):
+            tt = np.arange(T + H)
+            ind = np.empty((B, kc["indicator"], T + H), np.float32)
+            for c in range(kc["indicator"]):
+                ind[:, c, :] = ((tt // (5 + 2 * c)) % 2 == 0).astype(np.float32)
+            parts.append(ind)
+        out["known"] = np.concatenate(parts, axis=1)
+    cp = case.get("cat_past", {})
+    if cp.get("rows"):
+        codes = rng.integers(0, cp["n_codes"], size=(B, cp["rows"], T)).astype(np.float64)
+        if cp.get("nan_frac"):
+            codes[rng.random(codes.shape) < cp["nan_frac"]] = np.nan
+        out["cat_past"] = codes
+    ck = case.get("cat_known", {})
+    if ck.get("rows"):
+        codes = rng.integers(0, ck["n_codes"], size=(B, ck["rows"], T + H)).astype(np.float64)
+        if ck.get("unseen_in_horizon"):
+            codes[:, :, T + H // 2] = ck["n_codes"] + 7
+        if ck.get("nan_frac"):
+            codes[rng.random(codes.shape) < ck["nan_frac"]] = np.nan
+        out["cat_known"] = codes
+    return out
+
+
 def series_random_walk(B: int, T: int, nan_frac: float = 0.05, seed0: int = 0):
     """Gaussian random walk (step N(0,1), seed = i) plus a level offset U(-100, 100), with
     a fraction of context steps set to NaN; shape [B,1,T]."""
