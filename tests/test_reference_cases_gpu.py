@@ -7,9 +7,11 @@ categorical covariates with a code unseen in the context, horizons of many decod
 with and without known covariates, leading / scattered / whole-patch gaps, a non-negative
 series far from zero (clipping), a constant series, a series with no observation at all, and
 a context longer than the model's context length. Inputs follow the reference's generator
-(timestral_b200.synthetic.reference_case_inputs). The model is the tiny checkpoint's
+(timestral_b200.synthetic.reference_case_inputs). Two models: the tiny checkpoint's
 architecture in F32 (CUDA-core path), held to the F32 tolerance of tests/test_forecast_gpu.py
-on every value; where the oracle rejects a request, the device must reject it too.
+on every value; and a model with the 209M head and patch geometry in F16 (tensor-core path),
+held to the F16 bounds of that file against the oracle's F16 restatement. Where the oracle
+rejects a request, the device must reject it too.
 """
 import json
 from pathlib import Path
@@ -25,6 +27,7 @@ pytestmark = pytest.mark.gpu
 
 CASES = json.loads((Path(__file__).resolve().parent / "golden" / "reference_cases.json").read_text())
 F32_RTOL, F32_ATOL = 1e-3, 1e-4
+F16_MEAN_ND, F16_ROW_FACTOR, F16_VALUE_FACTOR = 1e-3, 3.0, 30.0   # as tests/test_forecast_gpu.py
 _models = {}
 
 
@@ -35,18 +38,18 @@ def need_gpu():
         pytest.skip("no GPU")
 
 
-def models():
-    if "tiny" not in _models:
-        path = sy.cached_model(sy.spec_tiny(), "f32")
-        _models["tiny"] = (tb.Model(path), op.OracleModel(path))
-    return _models["tiny"]
+def models(spec, weights):
+    key = (spec.name, weights)
+    if key not in _models:
+        path = sy.cached_model(spec, weights)
+        _models[key] = (tb.Model(path), op.OracleModel(path))
+    return _models[key]
 
 
-@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
-def test_reference_case(case):
-    m, o = models()
-    ps = sy.spec_tiny().patch_size
-    inp = sy.reference_case_inputs(case, ps)
+def run_case(case, spec, weights):
+    """(context, device forecast, oracle forecast), or None when both reject the request."""
+    m, o = models(spec, weights)
+    inp = sy.reference_case_inputs(case, spec.patch_size)
     x = inp.pop("context")
     H = case["H"]
     try:
@@ -55,14 +58,37 @@ def test_reference_case(case):
         with pytest.raises(Exception):
             m.forecast(x, H, **inp)
         print(f"{case['name']}: rejected by both ({e})")
-        return
+        return None
     got = m.forecast(x, H, **inp)
     assert got.shape == want.shape == (case["B"], case["V"], H, o.Q)
     assert np.isfinite(got).all()
+    # the reference's invariant: quantiles do not cross
+    assert np.all(np.diff(got, axis=-1) >= 0)
+    return x, got, want
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_reference_case(case):
+    r = run_case(case, sy.spec_tiny(), "f32")
+    if r is None:
+        return
+    _, got, want = r
     err = np.abs(got.astype(np.float64) - want.astype(np.float64))
     tol = F32_ATOL + F32_RTOL * np.abs(want.astype(np.float64))
     print(f"{case['name']}: max|err|={err.max():.3e} worst err/tol={float(np.max(err / tol)):.3e} "
           f"bitwise-equal={np.mean(got == want):.4f}")
     assert np.all(err <= tol), float(np.max(err / tol))
-    # the reference's invariant: quantiles do not cross
-    assert np.all(np.diff(got, axis=-1) >= 0)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_reference_case_f16_tensor_cores(case):
+    spec = sy.spec_small()
+    r = run_case(case, spec, "f16")
+    if r is None:
+        return
+    x, got, want = r
+    loc, sc = op.anchors(x, spec.patch_size)
+    rows_mean, rows_max = op.normalized_deviation_rows(got, want, loc, sc)
+    mean, row, mx = float(np.mean(rows_mean)), float(np.max(rows_mean)), float(np.max(rows_max))
+    print(f"{case['name']}: normalized deviation mean={mean:.3e} worst row={row:.3e} worst value={mx:.3e}")
+    assert mean <= F16_MEAN_ND and row <= F16_ROW_FACTOR * F16_MEAN_ND and mx <= F16_VALUE_FACTOR * F16_MEAN_ND
