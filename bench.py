@@ -1,6 +1,7 @@
 """Forecast throughput benchmark (series/sec) on 1..8 B200s.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg5] [--weights f16|q8_0] [--batch B]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg5] [--weights f16|q8_0|q6_k|q5_k|q4_k]
+                    [--batch B] [--no-cpu] [--no-e2e]
     python bench.py --impl reference ...   # the CPU reference arm (rank 0 only)
 
 Workloads (209M architecture, random init seed 0, synthetic series of each config's shape;
@@ -9,7 +10,10 @@ symmetric averaging and clipping on):
   cfg2  f16  B=64   V=1   T=2048  H=256  random walks + U(-100,100) offset, 5% NaN
   cfg3  f16  B=16   V=32  T=1024  H=128  VAR(1), Sigma_ij = 0.5^|i-j|
   cfg4  f16  B=32   V=4   T=1024  H=96   + 8 past, 4 known, 2 categorical known covariates
-  cfg5  f16 (or --weights q8_0)  B=4096  V=1  T=2048  H=256  seasonal sine + trend, 1% NaN
+  cfg5  f16 (or --weights q8_0 / K-quants)  B=4096  V=1  T=2048  H=256  seasonal sine + trend, 1% NaN
+  cfg6  f16  B=64   V=1   T=32768 H=1024 long context, seasonal + 1% NaN
+  pub32k / pub512  f32  B=1  T=32768 / 512, H=1024 / 32: the reference's published benchmark
+        shapes on its dyadic-v1 input, with the ratio to its published seconds as vs_baseline
 The default is cfg5, the throughput configuration the headline metric is quoted on. The
 batch is sharded across GPUs with no collective on the forecast path; each rank runs its
 slice through its own handle.
@@ -99,7 +103,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS))
-    ap.add_argument("--weights", default="f16", choices=["f16", "q8_0"], help="cfg5 weight type")
+    ap.add_argument("--weights", default="f16", choices=["f16", "q8_0", "q6_k", "q5_k", "q4_k"],
+                    help="cfg5 weight type")
     ap.add_argument("--batch", type=int, default=0, help="override the config's batch")
     ap.add_argument("--cpu-sample", type=int, default=0, help="series timed on the CPU baseline")
     ap.add_argument("--no-e2e", action="store_true")
