@@ -542,6 +542,25 @@ def test_fused_norm_and_its_fallback(V):
         m.fused_norm(1)
 
 
+def test_fused_norm_runs_at_width_128():
+    """A model 128 wide fills half of a 256-column GEMM tile: the residual-add GEMMs keep one
+    128-column sum-of-squares slot per row and must not store the empty second half's (which
+    would clear the next row's slot and, after the last row, write past the buffer). The
+    fused forecast then runs without its fallback (its bits differ from the RMSNorm-kernel
+    forecast's) and stays within the F16 bound."""
+    m, o = models(sy.spec_small(), "f16")
+    x = random_context(3, 1, 256, seed=7)
+    try:
+        m.fused_norm(0)
+        plain = m.forecast(x, 64).copy()
+        m.fused_norm(1)
+        fused = m.forecast(x, 64)
+        assert not np.array_equal(fused.view(np.uint32), plain.view(np.uint32))
+        check_nd(fused, o.forecast(x, 64), x, 32, F16_MEAN_ND)
+    finally:
+        m.fused_norm(1)
+
+
 @pytest.mark.parametrize("mode", [1, 0])
 def test_non_unit_norm_gains(mode):
     """With RMSNorm gains other than 1 (folded into the consuming GEMM weights at load), both

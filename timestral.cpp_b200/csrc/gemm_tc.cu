@@ -300,7 +300,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tacc, 
             __syncwarp();
         }
         if constexpr (KIND == EPI_RESID) {
-            if (e.x16) store_ssq(e, orow, rok, sq, lane, (n0 + half * C * 32) / 128);
+            // a column group past N (N = 128 in a 256-column tile) has no slot of its own
+            if (e.x16 && n0 + half * C * 32 < g.N) store_ssq(e, orow, rok, sq, lane, (n0 + half * C * 32) / 128);
         }
     } else if constexpr (KIND == EPI_F16 || KIND == EPI_SILU) {
         // 64 columns (two TMEM reads) per staging pass; the thread stores 8 f16 columns.
@@ -582,7 +583,7 @@ __device__ __forceinline__ void epilogue_resid_ring(const GemmArgs& g, uint32_t 
         __syncwarp();
         resid_prefetch(g, r, lane, q0 + c + 2, slot);
     }
-    if (e.x16) store_ssq(e, orow, rok, sq, lane, (n0 + r.part * C * 32) / 128);
+    if (e.x16 && n0 + r.part * C * 32 < g.N) store_ssq(e, orow, rok, sq, lane, (n0 + r.part * C * 32) / 128);
 }
 
 template <int KIND, int FMT, bool RING_OK>
