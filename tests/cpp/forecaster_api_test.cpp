@@ -11,10 +11,13 @@
 //    published only when the forecast succeeds;
 //  * decode() of the assembled rows equals the forecast without symmetric averaging, clip and
 //    cap, and its first block equals the forecast trace's first positive block;
+//  * each decode block's context follows from the previous block (the reference's feedback
+//    contract), at the model's cap and at a cap that slides every block;
 //  * the per-request overrides (per-shot patches, cap factor) change the result as requested.
 #include "forecaster.hpp"
 #include "timestral_capi.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -47,6 +50,46 @@ void same_blocks(const std::vector<ts::DecodeBlock>& a, const std::vector<ts::De
         check(same_bytes(a[i].context, b[i].context) && same_bytes(a[i].mask, b[i].mask), "block context bytes");
         check(same_bytes(a[i].future, b[i].future) && same_bytes(a[i].future_mask, b[i].future_mask), "block future bytes");
         check(same_bytes(a[i].predicted, b[i].predicted) && same_bytes(a[i].refined, b[i].refined), "block quantile bytes");
+    }
+}
+
+// Each block's context is the previous block's context followed by that block's refined
+// medians, slid to the cap in whole patches (reference tests/test_forecast.cpp
+// feedback_contract, src/forecaster.cpp decode_impl): a median that is not finite or at
+// least the extreme-value threshold feeds back as 0, past-covariate rows (role 1) feed back
+// 0 unobserved, known-covariate rows (role 2) their known future; bytes and masks exact.
+void feedback_contract(const ts::Config& c, const std::vector<ts::DecodeBlock>& blocks,
+                       const std::vector<int64_t>& roles, size_t R, size_t cap) {
+    const size_t Q = c.num_quantiles(), ps = c.patch_size, med = c.median_index();
+    for (size_t k = 1; k < blocks.size(); ++k) {
+        const ts::DecodeBlock& b = blocks[k - 1];
+        const ts::DecodeBlock& a = blocks[k];
+        const size_t n = b.patches * ps, joined = b.length + n;
+        const size_t keep = joined > cap ? std::max(ps, cap / ps * ps) : joined, start = joined - keep;
+        check(a.offset == b.offset + n && a.length == keep && a.context.size() == R * keep && a.mask.size() == R * keep &&
+                  b.refined.size() == R * n * Q,
+              "feedback: block offsets and context length");
+        bool ok = true;
+        for (size_t row = 0; row < R && ok; ++row)
+            for (size_t t = 0; t < keep && ok; ++t) {
+                const size_t from = start + t;
+                float v;
+                int8_t observed;
+                if (from < b.length) {
+                    v = b.context[row * b.length + from];
+                    observed = b.mask[row * b.length + from];
+                } else {
+                    const size_t j = from - b.length;
+                    v = b.refined[(row * n + j) * Q + med];
+                    observed = 1;
+                    if (!std::isfinite(v) || std::abs(v) >= c.extreme_value_threshold) v = 0;
+                    const int64_t role = roles.empty() ? 0 : roles[row];
+                    if (role == 1) { v = 0; observed = 0; }
+                    if (role == 2) { v = b.future[row * n + j]; observed = b.future_mask[row * n + j]; }
+                }
+                ok = !std::memcmp(&v, &a.context[row * keep + t], sizeof(float)) && observed == a.mask[row * keep + t];
+            }
+        check(ok, "feedback: context values and masks");
     }
 }
 
@@ -158,6 +201,19 @@ void run(const ts::Model& m, ts::Forecaster& fc, timestral_ctx* h, bool covariat
     bool mirrored = neg.context.size() == first.context.size();
     for (size_t i = 0; mirrored && i < neg.context.size(); ++i) mirrored = neg.context[i] == -first.context[i];
     check(mirrored, "the mirrored pass holds the negated rows");
+
+    // Block feedback on the device, both passes: at the model's cap (no slide here) and at a
+    // cap of four patches (every later block slides).
+    feedback_contract(c, captured.positive, a.roles, a.rows_count, c.context_length);
+    feedback_contract(c, captured.negative, a.roles, a.rows_count, c.context_length);
+    ts::ForecastRequest capped = r;
+    capped.max_context = 4 * c.patch_size;
+    ts::ForecastTrace slid;
+    fc.forecast(capped, &slid);
+    const ts::AssembledRows ac = assemble(m, capped);
+    check(slid.positive.size() == 3 && slid.positive[0].length == capped.max_context, "capped blocks");
+    feedback_contract(c, slid.positive, ac.roles, ac.rows_count, capped.max_context);
+    feedback_contract(c, slid.negative, ac.roles, ac.rows_count, capped.max_context);
 
     // Transactional anchors: a failing forecast leaves none.
     only.capture_initial_anchors = false;

@@ -16,6 +16,8 @@ Tolerances:
     oracle's restatement of ggml's Q8_0 path (activations quantised per 32-block). The device
     path dequantises the weights to F16 and keeps F16 activations.
 """
+import dataclasses
+
 import numpy as np
 import pytest
 
@@ -446,6 +448,29 @@ def test_sign_symmetry_bitwise_and_batch_invariance():
     assert np.all(np.isfinite(a)) and np.all(np.diff(a, axis=-1) >= 0), "I6.6"
     one = m.forecast(x[2:3], 96, clip=0)
     assert np.array_equal(one, a[2:3]), "a series' forecast does not depend on the batch it is in"
+    assert np.all(m.forecast(np.abs(x), 96, clip=1) >= 0), "nonnegative clipping"
+
+
+def test_covariates_refused_without_support():
+    """Checkpoints that cannot take covariates refuse them with the reference's errors
+    (src/covariates.cpp:37-38, src/capi_internal.hpp:18-19; tests/test_forecast.cpp
+    invariants), as the oracle does, and still forecast what they support: no covariates
+    at all without covariate training; past but not known-future covariates when no time
+    sublayer is followed by both a time and a variate sublayer."""
+    x = random_context(2, 1, 40, seed=5)
+    known = np.zeros((2, 1, 48), np.float32)
+    past = random_context(2, 1, 40, seed=6, nan_frac=0.0)
+    nocov = dataclasses.replace(sy.spec_tiny(), name="timestral-tiny-nocov", covariate_enabled=False)
+    m = tb.Model(sy.cached_model(nocov, "f32"))
+    for kw in (dict(known=known), dict(past=past)):
+        with pytest.raises(tb.TimestralError, match="this checkpoint was not trained with covariates"):
+            m.forecast(x, 8, **kw)
+    assert np.all(np.isfinite(m.forecast(x, 8)))
+    vt = dataclasses.replace(sy.spec_tiny(), name="timestral-tiny-vt", block_schedule=("variate", "time"))
+    m, o = models(vt, "f32")
+    with pytest.raises(tb.TimestralError, match="this checkpoint cannot condition on known-future covariates"):
+        m.forecast(x, 8, known=known)
+    check_f32(m.forecast(x, 8, past=past), o.forecast(x, 8, past=past))
 
 
 def test_shards_bitwise_equal_to_one_gpu():
@@ -622,6 +647,9 @@ def test_errors_surface_through_the_abi():
         m.forecast(x, 8, mask=np.full(x.shape, 2, np.uint8))
     with pytest.raises(tb.TimestralError, match="max_context exceeds"):
         m.forecast(x, 8, max_context=10 ** 6)
+    # zero horizon (reference src/timestral_capi.cpp:64; tests/test_forecast.cpp invariants)
+    with pytest.raises(tb.TimestralError, match="invalid forecast dimensions"):
+        m.forecast(x, 0)
     # a successful call clears the handle error
     m.forecast(x, 8)
     assert m.last_error == ""
