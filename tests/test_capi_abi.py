@@ -108,6 +108,65 @@ def test_model_loader_rejects_schema_violations(tmp_path):
     assert lib.timestral_capi_last_error(None) == b"missing tensor: out_norm.weight"
 
 
+def _rewrite_gguf(src, dst, drop=(), retype=None):
+    """A copy of the GGUF at src without the tensors in drop and with the tensors in retype
+    ({name: "f16" | "q8_0"}) stored in that type."""
+    import gguf
+    import numpy as np
+    retype = retype or {}
+    r = gguf.GGUFReader(str(src))
+    w = gguf.GGUFWriter(str(dst), "timestral")
+    for f in r.fields.values():
+        if f.name.startswith("GGUF.") or f.name == "general.architecture":
+            continue
+        t = f.types[0]
+        if t == gguf.GGUFValueType.ARRAY:
+            vals = [bytes(f.parts[i]).decode() if f.types[1] == gguf.GGUFValueType.STRING else f.parts[i][0].item()
+                    for i in f.data]
+            w.add_key_value(f.name, vals, t, f.types[1])
+        elif t == gguf.GGUFValueType.STRING:
+            w.add_key_value(f.name, bytes(f.parts[f.data[0]]).decode(), t)
+        else:
+            w.add_key_value(f.name, f.parts[f.data[0]][0].item(), t)
+    for t in r.tensors:
+        if t.name in drop:
+            continue
+        data = np.asarray(t.data)
+        if retype.get(t.name) == "f16":
+            w.add_tensor(t.name, data.astype(np.float16), raw_dtype=gguf.GGMLQuantizationType.F16)
+        elif retype.get(t.name) == "q8_0":
+            q = gguf.quants.quantize(data.astype(np.float32), gguf.GGMLQuantizationType.Q8_0)
+            w.add_tensor(t.name, q, raw_shape=q.shape, raw_dtype=gguf.GGMLQuantizationType.Q8_0)
+        else:
+            w.add_tensor(t.name, data, raw_dtype=t.tensor_type)
+    w.write_header_to_file(); w.write_kv_data_to_file(); w.write_tensors_to_file(); w.close()
+    return dst
+
+
+def test_model_loader_enforces_the_storage_policy(tmp_path):
+    """Reduced types only on the projection weights the reference's policy names, and a
+    Q8_0 row length a multiple of its 32-value block (reference src/model_loader.cpp:275-281,
+    src/weight_policy.hpp:13-30; tests/test_f16.cpp and tests/test_q8.cpp rejections). The
+    loader refuses before any GPU work, with the reference's message (ggml's type names)."""
+    from timestral_b200 import synthetic as sy
+    good = sy.write_gguf(tmp_path / "tiny.gguf", sy.spec_tiny(), "f32")
+    lib = tb.lib()
+    for name, kind in (("out_norm.weight", "f16"), ("rope.cos", "f16"), ("out_norm.weight", "q8_0")):
+        bad = _rewrite_gguf(good, tmp_path / f"bad_{kind}.gguf", retype={name: kind})
+        assert not lib.timestral_capi_load(str(bad).encode(), 1)
+        assert lib.timestral_capi_last_error(None).decode() == \
+            f"tensor {name} has type {kind}, forbidden by the storage policy"
+    # Reduced projection weights pass the loader (on a machine without a GPU the load then
+    # stops at the device).
+    ok = _rewrite_gguf(good, tmp_path / "reduced.gguf",
+                       retype={"blk.0.attn.0.qkv.weight": "q8_0", "head.out.weight": "f16"})
+    h = lib.timestral_capi_load(str(ok).encode(), 1)
+    if h:
+        lib.timestral_capi_free(h)
+    else:
+        assert "storage policy" not in lib.timestral_capi_last_error(None).decode()
+
+
 def test_device_switches_reject_bad_arguments():
     """The device-seam switches refuse a null handle (and tsb_fused_norm an unknown mode)
     without touching a GPU."""
