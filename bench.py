@@ -3,6 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg5] [--weights f16|q8_0|q6_k|q5_k|q4_k]
                     [--batch B] [--no-cpu] [--no-e2e]
     python bench.py --impl reference ...   # the CPU reference arm (rank 0 only)
+    python bench.py --compare-cublas       # the fused GEMMs against cuBLAS at the cfg5 shapes
 
 Workloads (209M architecture, random init seed 0, synthetic series of each config's shape;
 symmetric averaging and clipping on):
@@ -109,6 +110,8 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=0, help="series timed on the CPU baseline")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--compare-cublas", action="store_true",
+                    help="time each fused GEMM kind and cuBLAS (torch.mm, f16 in/out) at the cfg5 token count")
     a = ap.parse_args()
     c = dict(CONFIGS[a.config])
     c.setdefault("cpu_sample_1t", 1)
@@ -330,8 +333,93 @@ def gemm_flops(rows: int, S: int, L: int, V_rows: int, decoder_tokens: int) -> i
     return 2 * rows * (S * per_token + L * patch + decoder_tokens * head)
 
 
+def compare_cublas(seconds: float = 2.0):
+    """The production GEMM kinds of the 209M layer (tsb_test_gemm, one tcgen05 launch each)
+    and cuBLAS (torch.mm, f16 operands, f16 output, no epilogue) on the same operands at the
+    cfg5 token count (M = 4096 series x 2 passes x 72 tokens), each looped for `seconds` so
+    that the power cap settles; one JSON line per op with its SM clock. The test entry
+    synchronizes after each launch (a few microseconds of idle per launch are included)."""
+    import ctypes as C
+    import torch
+    import timestral_b200 as tb
+    M, S, H, D, F = 589_824, 72, 12, 768, 2048
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*shape):
+        return (torch.randn(*shape, device=dev, generator=g) * 0.05).to(torch.float16)
+
+    def ptr(t):
+        return C.c_void_p(t.data_ptr()) if t is not None else None
+
+    def ours(kind, A, B, N, K, out=None, resid=None, qkvg=None, rope=None):
+        t = tb.GemmTest()
+        t.kind, t.A, t.lda, t.B, t.ldb, t.M, t.N, t.K = kind, ptr(A), A.shape[1], ptr(B), B.shape[1], M, N, K
+        t.out, t.ldo, t.resid = ptr(out), (out.shape[1] if out is not None else 0), ptr(resid)
+        if qkvg is not None:
+            for i in range(4):
+                t.qkvg[i] = qkvg[i].data_ptr()
+            t.S, t.H, t.D, t.rope = S, H, D, 1
+            t.cos_tab, t.sin_tab, t.rope_row = ptr(rope[0]), ptr(rope[1]), ptr(rope[2])
+            t.rope_half, t.rope_dup = 16, 1
+        err = C.c_int32(0)
+
+        def call():
+            rc = tb.lib().tsb_test_gemm(C.byref(t), C.byref(err))
+            if rc != 0:
+                raise RuntimeError(f"tsb_test_gemm kind {kind}: {rc} ({err.value})")
+        return call
+
+    A768, A2048 = rnd(M, D), rnd(M, F)
+    Wqkvg, W12, Wout, W3 = rnd(4 * D, D), rnd(2 * F, D), rnd(D, D), rnd(D, F)
+    ang = torch.rand(2113, 16, device=dev, generator=g) * 6.283
+    cos, sin = torch.ones(2113, 64, device=dev), torch.zeros(2113, 64, device=dev)
+    for lo in (0, 32):   # rotated dims 0-15 and 32-47 (the 209M table), equal halves
+        cos[:, lo:lo + 16], sin[:, lo:lo + 16] = torch.cos(ang), torch.sin(ang)
+    rope_row = (torch.arange(M, device=dev, dtype=torch.int32) % S) + 1000
+    qkvg = [torch.empty(M, D, device=dev, dtype=torch.float16) for _ in range(4)]
+    swi = torch.empty(M, F, device=dev, dtype=torch.float16)
+    res = torch.zeros(M, D, device=dev, dtype=torch.float32)
+    o3072 = torch.empty(M, 4 * D, device=dev, dtype=torch.float16)
+    o4096 = torch.empty(M, 2 * F, device=dev, dtype=torch.float16)
+    o768 = torch.empty(M, D, device=dev, dtype=torch.float16)
+    ops = [
+        ("fused q/k/v/gate + RoPE + sigmoid(gate), head-major", ours(6, A768, Wqkvg, 4 * D, D, qkvg=qkvg, rope=(cos, sin, rope_row)), 4 * D, D),
+        ("cuBLAS, same operands, plain f16 output", lambda: torch.mm(A768, Wqkvg.t(), out=o3072), 4 * D, D),
+        ("fused MLP up + SwiGLU", ours(4, A768, W12, 2 * F, D, out=swi), 2 * F, D),
+        ("cuBLAS, same operands, plain f16 output", lambda: torch.mm(A768, W12.t(), out=o4096), 2 * F, D),
+        ("fused out projection + f32 residual add", ours(2, A768, Wout, D, D, out=res, resid=res), D, D),
+        ("cuBLAS, same operands, plain f16 output", lambda: torch.mm(A768, Wout.t(), out=o768), D, D),
+        ("fused MLP down + f32 residual add", ours(2, A2048, W3, D, F, out=res, resid=res), D, F),
+        ("cuBLAS, same operands, plain f16 output", lambda: torch.mm(A2048, W3.t(), out=o768), D, F),
+    ]
+    for name, fn, N, K in ops:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        fn()
+        torch.cuda.synchronize()
+        n = max(5, int(seconds / max(time.perf_counter() - t0, 1e-4)))
+        clk = ClockSampler(0)
+        clk.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        clocks = clk.stop()
+        ms = e0.elapsed_time(e1) / n
+        print(json.dumps({"op": name, "M": M, "N": N, "K": K, "ms": round(ms, 4),
+                          "tflops": round(2.0 * M * N * K / ms / 1e9, 1), "launches": n, "clocks": clocks}), flush=True)
+    return 0
+
+
 def main():
     a, c = parse()
+    if a.compare_cublas:
+        return compare_cublas()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
