@@ -127,8 +127,12 @@ def parse():
 def peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
-        d = json.loads(p.read_text())
-        return d["hbm_gbs"], d["bf16_tflops"], d["bf16_tflops_sustained"], "measured"
+        try:
+            d = json.loads(p.read_text())
+            hbm, burst = float(d["hbm_gbs"]), float(d["bf16_tflops"])
+            return hbm, burst, float(d.get("bf16_tflops_sustained", burst)), "measured"
+        except (ValueError, KeyError, TypeError):
+            pass                  # unreadable: the fallback figures below, labelled as such
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
