@@ -249,6 +249,16 @@ TIMESTRAL_API int tsb_test_refine(const float* d_q, const float* d_rows, const i
                                   float* d_out);
 TIMESTRAL_API int tsb_test_rms(const float* x, const float* w, int32_t tokens, int32_t D, float eps, void* out,
                                int32_t out_f16);
+/* Failure detection without a GPU fault: one CTA whose bounded barrier wait runs out (a
+ * barrier nothing arrives on) while a second role leaves through the abort flag; kernel 0
+ * uses the GEMM roles' wait, 1 the attention kernels'. Takes one wait limit (about 2 s at
+ * full clock), synchronizes, and returns TSB_ERR_DEVICE with the expired wait's error word
+ * in *dev_error (the GEMM's stage-fill or the attention barrier code) and 1 in
+ * *left_by_abort when the second role left through the flag; the context stays usable. */
+TIMESTRAL_API int tsb_test_wait_expiry(int32_t kernel, int32_t* dev_error, int32_t* left_by_abort);
+/* Failure injection on the host: the next n workspace allocations of any forecast in the
+ * process fail as an exhausted device would (cudaErrorMemoryAllocation); 0 clears it. */
+TIMESTRAL_API int tsb_test_fail_workspace_allocations(int32_t n);
 
 #ifdef __cplusplus
 }

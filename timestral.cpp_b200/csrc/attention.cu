@@ -670,7 +670,38 @@ __global__ void __launch_bounds__(AT_THREADS, 3)
     if (warp == 0) tmem_dealloc(bars->tmem, AT_TMEM_COLS);
 }
 
+// The attention kernels' bounded waits (lane 0 waits, its warp follows), made to expire
+// without a fault: warp 0 waits on a barrier that nothing arrives on (kDevTimeoutAttn, abort
+// flag raised); warp 1, waiting on another from half a limit later, leaves through the abort
+// flag (err[1] = 1). The kernel then returns.
+__global__ void attention_wait_expiry_kernel(int* err) {
+    __shared__ uint64_t bars[2];
+    __shared__ int abort_flag;
+    const int warp = threadIdx.x / 32;
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    volatile int* abort = &abort_flag;
+    if (warp == 0) {
+        warp_wait(&bars[0], 0, abort, err);
+    } else if (warp == 1) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < kWaitCycles / 2) __nanosleep(100000);
+        const bool ok = warp_wait(&bars[1], 0, abort, nullptr);
+        if (!ok && (threadIdx.x & 31) == 0 && *abort) err[1] = 1;
+    }
+}
+
 }  // namespace
+
+cudaError_t attention_wait_expiry_selftest(int* err, cudaStream_t stream) {
+    attention_wait_expiry_kernel<<<1, 64, 0, stream>>>(err);
+    return cudaGetLastError();
+}
 
 bool make_map_slot_rows_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t slots, int box_rows);
 

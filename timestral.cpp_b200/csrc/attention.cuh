@@ -58,4 +58,9 @@ template <class T>
 cudaError_t attention_variate_simt(const T* q, const T* k, const T* v, const T* gate, T* out, int rows, int H,
                                    int hd, const MaskMeta& mm, cudaStream_t stream);
 
+// Test of the attention kernels' bounded waits (no fault): one CTA in which one wait expires
+// and records kDevTimeoutAttn in err[0], and a second warp leaves through the abort flag
+// (err[1] = 1). Takes about one wait limit (kWaitCycles SM cycles).
+cudaError_t attention_wait_expiry_selftest(int* err, cudaStream_t stream);
+
 }  // namespace tsb

@@ -65,6 +65,17 @@ void fold_norm(std::vector<uint16_t>& W, size_t K, const float* norm) {
 // workspace addresses of its capture and is replayed only while this count is unchanged.
 std::atomic<uint64_t> g_workspace_generation{0};
 
+// Test hook: the next n workspace allocations in the process fail as an exhausted device
+// would (cudaErrorMemoryAllocation), so that the error path of a forecast can be exercised
+// without a GPU fault.
+std::atomic<int> g_injected_alloc_failures{0};
+bool take_injected_failure() {
+    int n = g_injected_alloc_failures.load();
+    while (n > 0)
+        if (g_injected_alloc_failures.compare_exchange_weak(n, n - 1)) return true;
+    return false;
+}
+
 struct DevBuf {
     void* p = nullptr;
     size_t bytes = 0;
@@ -76,7 +87,8 @@ struct DevBuf {
         if (n <= bytes) return;
         g_workspace_generation.fetch_add(1);
         if (p) { cudaFree(p); p = nullptr; bytes = 0; }
-        check(cudaMalloc(&p, std::max<size_t>(n, 256)), "cudaMalloc workspace");
+        check(take_injected_failure() ? cudaErrorMemoryAllocation : cudaMalloc(&p, std::max<size_t>(n, 256)),
+              "cudaMalloc workspace");
         bytes = std::max<size_t>(n, 256);
     }
     template <class T> T* as() const { return static_cast<T*>(p); }
@@ -1131,8 +1143,10 @@ void Engine::forecast_targets(const float* d_ctx, const uint8_t* d_umask, int B,
             cudaStreamEndCapture(s, &g);
             if (g) cudaGraphDestroy(g);
             cudaGetLastError();
-            im.have_last = false;          // the next identical call runs uncaptured
         }
+        // The next identical call runs uncaptured: a failed call may have left workspace to
+        // allocate, which a capture cannot do.
+        im.have_last = false;
         throw;
     }
     if (capture) {
@@ -1518,5 +1532,7 @@ void Engine::decode_rows(int B, int V, int H, int R, int T, int Hh, bool symmetr
     last_launches_ = im.launches;
     im.check_device_error("forecast");
 }
+
+void inject_workspace_failures(int n) { g_injected_alloc_failures.store(n > 0 ? n : 0); }
 
 }  // namespace tsb

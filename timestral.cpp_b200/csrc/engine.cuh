@@ -186,4 +186,8 @@ private:
     int64_t last_launches_ = 0;
 };
 
+// Test hook: the next n workspace allocations (any engine of the process) fail with
+// cudaErrorMemoryAllocation; 0 clears it.
+void inject_workspace_failures(int n);
+
 }  // namespace tsb

@@ -798,6 +798,33 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// The bounded waits of the GEMM roles, made to expire without a fault: warp 0 waits on a
+// barrier that nothing arrives on, so its wait runs out (it records kDevTimeoutFull and raises
+// the abort flag); warp 1 starts waiting on another such barrier half a limit later and
+// leaves through the abort flag (err[1] = 1), as the other roles of a GEMM leave when one
+// role's wait expires. The kernel then returns; nothing faults and the context stays usable.
+__global__ void wait_expiry_kernel(int* err) {
+    __shared__ uint64_t bars[2];
+    __shared__ int abort_flag;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    volatile int* abort = &abort_flag;
+    if (lane != 0 || warp > 1) return;
+    if (warp == 0) {
+        wait_or_abort(&bars[0], 0, abort, err, kDevTimeoutFull);
+    } else {
+        const long long t0 = clock64();
+        while (clock64() - t0 < kWaitCycles / 2) __nanosleep(100000);
+        if (!wait_or_abort(&bars[1], 0, abort, nullptr, kDevTimeoutEmpty) && *abort) err[1] = 1;
+    }
+}
+
 }  // namespace
 
 // 2D f16 tensor map over a row-major [rows][cols] matrix with row pitch `ld` elements,
@@ -996,6 +1023,11 @@ cudaError_t tc_gemm(EpiKind kind, const GemmArgs& a, cudaStream_t stream, int* e
         case EPI_QKVG: return launch_kind<EPI_QKVG>(a, stream, err);
     }
     return cudaErrorInvalidValue;
+}
+
+cudaError_t gemm_wait_expiry_selftest(int* err, cudaStream_t stream) {
+    wait_expiry_kernel<<<1, 64, 0, stream>>>(err);
+    return cudaGetLastError();
 }
 
 }  // namespace tsb

@@ -82,6 +82,10 @@ struct GemmArgs {
 
 // Launch on `stream`. err: device error word (may be null). Returns a CUDA error code.
 cudaError_t tc_gemm(EpiKind kind, const GemmArgs& args, cudaStream_t stream, int* err);
+// Test of the GEMM roles' bounded waits (no fault): one CTA in which one wait expires and
+// records kDevTimeoutFull in err[0], and a second role leaves through the abort flag
+// (err[1] = 1). Takes about one wait limit (kWaitCycles SM cycles).
+cudaError_t gemm_wait_expiry_selftest(int* err, cudaStream_t stream);
 
 // Number of SMs of the current device (cached per device).
 int device_sm_count();

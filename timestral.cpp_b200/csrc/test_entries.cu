@@ -2,6 +2,7 @@
 // caller-owned device buffers so the GPU tests can compare it with a reference op.
 #include "common.cuh"
 #include "attention.cuh"
+#include "engine.cuh"
 #include "gemm_tc.cuh"
 #include "rows.cuh"
 #include "timestral_b200.h"
@@ -228,4 +229,27 @@ extern "C" TIMESTRAL_API int tsb_test_refine(const float* d_q, const float* d_ro
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     cudaFree(scratch);
     return e == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
+}
+
+extern "C" TIMESTRAL_API int tsb_test_wait_expiry(int32_t kernel, int32_t* dev_error, int32_t* left_by_abort) {
+    using namespace tsb;
+    if (kernel != 0 && kernel != 1) return TSB_ERR_ARG;
+    int* d = nullptr;
+    if (cudaMalloc(&d, 2 * sizeof(int)) != cudaSuccess) return TSB_ERR_CUDA;
+    cudaError_t ce = cudaMemset(d, 0, 2 * sizeof(int));
+    if (ce == cudaSuccess) ce = kernel == 0 ? gemm_wait_expiry_selftest(d, 0) : attention_wait_expiry_selftest(d, 0);
+    if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+    int h[2] = {0, 0};
+    if (ce == cudaSuccess) ce = cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (dev_error) *dev_error = h[0];
+    if (left_by_abort) *left_by_abort = h[1];
+    if (ce != cudaSuccess) return TSB_ERR_CUDA;
+    return h[0] ? TSB_ERR_DEVICE : TSB_OK;
+}
+
+extern "C" TIMESTRAL_API int tsb_test_fail_workspace_allocations(int32_t n) {
+    if (n < 0) return TSB_ERR_ARG;
+    tsb::inject_workspace_failures(n);
+    return TSB_OK;
 }
