@@ -259,6 +259,10 @@ TIMESTRAL_API int tsb_test_wait_expiry(int32_t kernel, int32_t* dev_error, int32
 /* Failure injection on the host: the next n workspace allocations of any forecast in the
  * process fail as an exhausted device would (cudaErrorMemoryAllocation); 0 clears it. */
 TIMESTRAL_API int tsb_test_fail_workspace_allocations(int32_t n);
+/* cudaDeviceReset of the current device (ends this process's context there; every handle
+ * and result buffer of that device must have been freed first). Later handles set their
+ * kernels' launch attributes again and take no pooled result buffer the reset freed. */
+TIMESTRAL_API int tsb_test_device_reset(void);
 
 #ifdef __cplusplus
 }

@@ -91,3 +91,43 @@ def test_failed_shard_fails_the_request_and_the_handle_recovers():
     for _ in range(3):
         got = multi.forecast(x, 64)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+RESET_SCRIPT = r"""
+import gc, sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+import timestral_b200 as tb
+from timestral_b200 import synthetic as sy
+rng = np.random.default_rng(11)
+x = (np.cumsum(rng.standard_normal((3, 1, 300)), axis=-1) + 5).astype(np.float32)
+path = sy.cached_model(sy.spec_small(), "f16")
+m = tb.Model(path)
+out = m.forecast(x, 64)
+want = out.copy()
+del out, m                     # the result buffer goes back to the library's pool
+gc.collect()
+assert tb.lib().tsb_test_device_reset() == tb.TSB_OK
+m = tb.Model(path)             # a new context: launch attributes set again
+for _ in range(3):             # plain launches, graph capture, replay
+    got = m.forecast(x, 64)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), "forecast differs after the reset"
+print("OK after reset")
+"""
+
+
+def test_new_handle_after_a_device_reset(tmp_path):
+    """A process that frees its handles and result buffers, resets the device
+    (cudaDeviceReset) and loads a model again gets the same forecasts: kernels set their
+    launch attributes once per context, and pooled result buffers that the reset freed are
+    not handed out again. Runs in a child process, whose reset does not touch this one's
+    context."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    pkg = Path(tb.__file__).resolve().parents[1]
+    script = tmp_path / "reset.py"
+    script.write_text(RESET_SCRIPT)
+    p = subprocess.run([sys.executable, str(script), str(pkg)], capture_output=True, text=True, timeout=600)
+    print(p.stdout, p.stderr[-2000:])
+    assert p.returncode == 0 and "OK after reset" in p.stdout

@@ -454,15 +454,16 @@ cudaError_t launch_attn_tc(const __half* q, const __half* k, const __half* v, co
                            int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
     using Lay = AttnLayout<NK, PK>;
     const int smem = Lay::smem(mm.S);
-    static bool configured[64] = {false};
+    static KernelSetup configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
+    unsigned long long ctx_key = 0;
+    if (configured.needed(dev, &ctx_key)) {
         // The largest request of this key count (S = NK) so later calls need no update.
         cudaError_t e = cudaFuncSetAttribute(attn_time_tc_kernel<NK, PK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Lay::smem(NK));
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured.done(dev, ctx_key);
     }
     CUtensorMap mq, mk, mv;
     const int64_t planes = int64_t(rows) * H;
@@ -709,13 +710,14 @@ cudaError_t attention_variate_tc(const __half* q, const __half* k, const __half*
                                  int rows, int H, int G, const MaskMeta& mm, cudaStream_t stream, int* err) {
     if (rows <= 0) return cudaSuccess;
     if (G <= 0 || G > 32 || rows % G || mm.S <= 0 || H <= 0) return cudaErrorInvalidValue;
-    static bool configured[64] = {false};
+    static KernelSetup configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
+    unsigned long long ctx_key = 0;
+    if (configured.needed(dev, &ctx_key)) {
         cudaError_t e = cudaFuncSetAttribute(attn_variate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AV_SMEM);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured.done(dev, ctx_key);
     }
     CUtensorMap mq, mk, mv;
     const int64_t slots = int64_t(H) * mm.S;
@@ -1170,13 +1172,14 @@ cudaError_t attention_time_tc_long(const __half* q, const __half* k, const __hal
                                    int rows, int H, const MaskMeta& mm, cudaStream_t stream, int* err) {
     if (rows <= 0) return cudaSuccess;
     if (mm.S <= 0 || H <= 0) return cudaErrorInvalidValue;
-    static bool configured[64] = {false};
+    static KernelSetup configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
+    unsigned long long ctx_key = 0;
+    if (configured.needed(dev, &ctx_key)) {
         cudaError_t e = cudaFuncSetAttribute(attn_time_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AL_SMEM);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured.done(dev, ctx_key);
     }
     CUtensorMap mq, mk, mv;
     const int64_t planes = int64_t(rows) * H;
@@ -1650,15 +1653,16 @@ cudaError_t attention_time_simt_tiled(const T* q, const T* k, const T* v, const 
                                       const MaskMeta& mm, cudaStream_t stream) {
     const size_t smem = simt_tiled_smem(mm.S);
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
-    static bool configured[64] = {false};
+    static KernelSetup configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
+    unsigned long long ctx_key = 0;
+    if (configured.needed(dev, &ctx_key)) {
         // the largest row this kernel takes, so later calls need no update
         cudaError_t e = cudaFuncSetAttribute(attn_time_simt_tiled_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              int(simt_tiled_smem(SIMT_MAX_KEYS)));
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured.done(dev, ctx_key);
     }
     const int64_t blocks = int64_t(rows) * H * ((mm.S + TS_Q - 1) / TS_Q);
     attn_time_simt_tiled_kernel<T><<<unsigned(blocks), TS_THREADS, smem, stream>>>(q, k, v, gate, out, rows, H, mm);
@@ -1673,13 +1677,14 @@ cudaError_t attention_time_simt(const T* q, const T* k, const T* v, const T* gat
     // Long rows of head_dim 64: the tiled kernel (same bits).
     if (hd == 64 && (tiled > 0 || (tiled < 0 && mm.S > 128)))
         return attention_time_simt_tiled(q, k, v, gate, out, rows, H, mm, stream);
-    static bool configured[64] = {false};
+    static KernelSetup configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
+    unsigned long long ctx_key = 0;
+    if (configured.needed(dev, &ctx_key)) {
         cudaError_t e = cudaFuncSetAttribute(attn_time_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(simt_smem()));
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured.done(dev, ctx_key);
     }
     const int64_t blocks = int64_t(rows) * H * ((mm.S + SIMT_WARPS - 1) / SIMT_WARPS);
     attn_time_simt_kernel<T><<<unsigned(blocks), SIMT_WARPS * 32, simt_smem(), stream>>>(q, k, v, gate, out, rows, H, hd, mm);
@@ -1691,13 +1696,14 @@ cudaError_t attention_variate_simt(const T* q, const T* k, const T* v, const T* 
                                    const MaskMeta& mm, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
     if (hd > 256) return cudaErrorInvalidValue;
-    static bool configured[64] = {false};
+    static KernelSetup configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
+    unsigned long long ctx_key = 0;
+    if (configured.needed(dev, &ctx_key)) {
         cudaError_t e = cudaFuncSetAttribute(attn_variate_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(simt_smem()));
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured.done(dev, ctx_key);
     }
     const int64_t blocks = int64_t(rows) * mm.S * ((H + SIMT_WARPS - 1) / SIMT_WARPS);
     attn_variate_simt_kernel<T><<<unsigned(blocks), SIMT_WARPS * 32, simt_smem(), stream>>>(q, k, v, gate, out, rows, H, hd, mm);
@@ -1711,17 +1717,18 @@ cudaError_t attention_variate_fast(const __half* q, const __half* k, const __hal
     const int64_t problems = int64_t(rows / G) * H * mm.S;
     const unsigned blocks = unsigned((problems + VF_WARPS - 1) / VF_WARPS);
     // Both variants use more than the default 48 KB of dynamic shared memory.
-    static bool configured[64] = {false};
+    static KernelSetup configured;
     const size_t smem1 = VF_WARPS * (2 * 32 * 64 + 32) * sizeof(float);
     const size_t smem2 = VF_WARPS * (2 * 64 * 64 + 64) * sizeof(float);
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
+    unsigned long long ctx_key = 0;
+    if (configured.needed(dev, &ctx_key)) {
         cudaError_t e = cudaFuncSetAttribute(attn_variate_fast_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem1));
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(attn_variate_fast_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem2));
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured.done(dev, ctx_key);
     }
     if (G <= 32)
         attn_variate_fast_kernel<1><<<blocks, VF_WARPS * 32, smem1, stream>>>(q, k, v, gate, out, rows, H, G, mm);

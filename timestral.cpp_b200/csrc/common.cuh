@@ -1,12 +1,53 @@
 // Shared device helpers for the sm_100a kernels: error words, bounded mbarrier waits,
 // TMA and tcgen05 PTX wrappers, and the reference's float arithmetic restated for the GPU.
 #pragma once
+#include <atomic>
 #include <cstdint>
+#include <mutex>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace tsb {
+
+// Unique id (for the life of the process) of the calling thread's current CUDA context, or
+// false when the driver does not offer it or no context is current yet.
+inline bool current_context_id(unsigned long long* id) {
+    using GetCurrentFn = CUresult (*)(CUcontext*);
+    using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrentFn get_current = nullptr;
+    static GetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrentFn>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetIdFn>(p);
+    });
+    CUcontext ctx = nullptr;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx) return false;
+    return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Per device, the context in which a kernel's launch attributes (its dynamic shared-memory
+// limit) were last set, so that they are set once per context: again after a device reset
+// (cudaDeviceReset replaces the context and drops them), and on every launch when the
+// context cannot be identified. Safe to use from several host threads.
+struct KernelSetup {
+    std::atomic<unsigned long long> ctx[64] = {};   // context id + 1; 0: not set yet
+    bool needed(int dev, unsigned long long* key) {
+        unsigned long long id = 0;
+        *key = current_context_id(&id) ? id + 1 : 0;
+        return dev < 0 || dev >= 64 || *key == 0 || ctx[dev].load(std::memory_order_acquire) != *key;
+    }
+    void done(int dev, unsigned long long key) {
+        if (dev >= 0 && dev < 64) ctx[dev].store(key, std::memory_order_release);
+    }
+};
 
 // ---------------------------------------------------------------------------------------
 // Device error word. Kernels that wait on barriers never spin forever: a wait that runs

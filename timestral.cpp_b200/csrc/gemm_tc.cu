@@ -918,14 +918,15 @@ int device_sm_count() {
 template <int KIND, int FMT, bool RING_OK = true>
 static cudaError_t launch(const GemmArgs& a, cudaStream_t stream, int* err) {
     using CF = Cfg<KIND, FMT, RING_OK>;
-    static bool configured[64] = {false};
+    static KernelSetup configured;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
+    unsigned long long ctx_key = 0;
+    if (configured.needed(dev, &ctx_key)) {
         cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<KIND, FMT, RING_OK>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, CF::SMEM_BYTES);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured.done(dev, ctx_key);
     }
     CUtensorMap ma, mb, mq, md;
     const bool map_a = a.a_group > 0

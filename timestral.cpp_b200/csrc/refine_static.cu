@@ -36,29 +36,6 @@ double* g_scratch_ptr[kMaxDevices] = {};
 unsigned long long g_scratch_ctx[kMaxDevices] = {};   // context id the address belongs to
 std::mutex g_setup_mutex;
 
-// Unique id (for the life of the process) of the calling thread's current CUDA context, or
-// false when the driver does not offer it or no context is current yet.
-bool current_context_id(unsigned long long* id) {
-    using GetCurrentFn = CUresult (*)(CUcontext*);
-    using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
-    static GetCurrentFn get_current = nullptr;
-    static GetIdFn get_id = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            get_current = reinterpret_cast<GetCurrentFn>(p);
-        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            get_id = reinterpret_cast<GetIdFn>(p);
-    });
-    CUcontext ctx = nullptr;
-    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx) return false;
-    return get_id(ctx, id) == CUDA_SUCCESS;
-}
-
 // Device address of the scratch array on the current device. In host code
 // `g_refine_scratch` names a host-side stand-in, not device memory, so the address is looked
 // up with cudaGetSymbolAddress: on a device's first call (which also loads the library's
@@ -67,13 +44,13 @@ bool current_context_id(unsigned long long* id) {
 cudaError_t scratch_address(int dev, double** out) {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     unsigned long long id = 0;
-    const bool known = current_context_id(&id);
+    const bool known = tsb::current_context_id(&id);
     if (!g_scratch_ptr[dev] || !known || id != g_scratch_ctx[dev]) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_refine_scratch);
         if (e != cudaSuccess) return e;
         g_scratch_ptr[dev] = static_cast<double*>(p);
-        g_scratch_ctx[dev] = current_context_id(&id) ? id : 0;
+        g_scratch_ctx[dev] = tsb::current_context_id(&id) ? id : 0;
     }
     *out = g_scratch_ptr[dev];
     return cudaSuccess;

@@ -1578,14 +1578,15 @@ cudaError_t simt_gemm(const SimtGemm& g, cudaStream_t s) {
         const dim3 grid((g.N + PT - 1) / PT, (g.M + PT - 1) / PT, panels);
         auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
         if (g.tiled != 0 && g.K % 4 == 0 && g.lda % 4 == 0 && aligned16(g.A) && aligned16(g.W)) {
-            static bool configured[64] = {false};
+            static KernelSetup configured;
             int dev = 0;
             cudaGetDevice(&dev);
-            if (dev >= 0 && dev < 64 && !configured[dev]) {
+            unsigned long long ctx_key = 0;
+            if (configured.needed(dev, &ctx_key)) {
                 cudaError_t e = cudaFuncSetAttribute(simt_panel_full_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      int(panel_full_smem()));
                 if (e != cudaSuccess) return e;
-                configured[dev] = true;
+                configured.done(dev, ctx_key);
             }
             simt_panel_full_kernel<<<grid, 256, panel_full_smem(), s>>>(g);
         } else {

@@ -253,3 +253,7 @@ extern "C" TIMESTRAL_API int tsb_test_fail_workspace_allocations(int32_t n) {
     tsb::inject_workspace_failures(n);
     return TSB_OK;
 }
+
+extern "C" TIMESTRAL_API int tsb_test_device_reset(void) {
+    return cudaDeviceReset() == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
+}

@@ -217,25 +217,43 @@ constexpr uint64_t kOutMagic = 0x74736230'6f757462ull;
 constexpr size_t kPoolMaxBuffers = 16;
 constexpr size_t kPoolMaxBytes = size_t(4) << 30;
 
+// A pooled buffer and its capacity, kept beside it: a device reset (cudaDeviceReset) frees
+// the page-locked memory of the context it replaces, so a pooled buffer is checked with the
+// runtime before it is reused and dropped, untouched, when it is no longer page-locked.
+struct PoolEntry {
+    OutHeader* h;
+    size_t capacity;
+};
 std::mutex& pool_mutex() { static std::mutex m; return m; }
-std::vector<OutHeader*>& pool() { static auto* v = new std::vector<OutHeader*>(); return *v; }   // never destroyed
+std::vector<PoolEntry>& pool() { static auto* v = new std::vector<PoolEntry>(); return *v; }   // never destroyed
 size_t pool_bytes = 0;
+
+bool still_page_locked(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
 
 float* out_alloc(size_t bytes, bool* pinned) {
     {
         std::lock_guard<std::mutex> lock(pool_mutex());
         auto& v = pool();
-        size_t best = v.size();
-        for (size_t i = 0; i < v.size(); ++i)
-            if (v[i]->capacity >= bytes && v[i]->capacity <= 2 * bytes + (size_t(1) << 20) &&
-                (best == v.size() || v[i]->capacity < v[best]->capacity))
-                best = i;
-        if (best < v.size()) {
-            OutHeader* h = v[best];
+        while (true) {
+            size_t best = v.size();
+            for (size_t i = 0; i < v.size(); ++i)
+                if (v[i].capacity >= bytes && v[i].capacity <= 2 * bytes + (size_t(1) << 20) &&
+                    (best == v.size() || v[i].capacity < v[best].capacity))
+                    best = i;
+            if (best == v.size()) break;
+            const PoolEntry e = v[best];
             v.erase(v.begin() + std::ptrdiff_t(best));
-            pool_bytes -= h->capacity;
+            pool_bytes -= e.capacity;
+            if (!still_page_locked(e.h)) continue;     // freed by a device reset
             *pinned = true;
-            return reinterpret_cast<float*>(h + 1);
+            return reinterpret_cast<float*>(e.h + 1);
         }
     }
     void* p = nullptr;
@@ -269,7 +287,7 @@ void out_free(void* data) {
         std::lock_guard<std::mutex> lock(pool_mutex());
         auto& v = pool();
         if (v.size() < kPoolMaxBuffers && pool_bytes + h->capacity <= kPoolMaxBytes) {
-            v.push_back(h);
+            v.push_back(PoolEntry{h, size_t(h->capacity)});
             pool_bytes += h->capacity;
             return;
         }

@@ -85,6 +85,7 @@ SIGNATURES = {
     "tsb_test_refine": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 6 + [C.c_double, C.c_void_p]),
     "tsb_test_wait_expiry": (C.c_int, [C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "tsb_test_fail_workspace_allocations": (C.c_int, [C.c_int32]),
+    "tsb_test_device_reset": (C.c_int, []),
     "tsb_refine_static": (C.c_int, [C.c_void_p] * 6 + [C.c_int32] * 6 + [C.c_double, C.c_void_p, C.c_void_p]),
 }
 
